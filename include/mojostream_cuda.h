@@ -1,0 +1,199 @@
+/*
+ * mojostream_cuda.h -- C-ABI of libmojostream_cuda.so, the B200 (sm_100a)
+ * implementation of MojoStream's Gemma-4 token loop.
+ *
+ * A host written in Mojo binds these symbols with DLHandle / external_call,
+ * the mechanism the reference already uses for libc (pread,
+ * src/streaming/stream_runner.mojo:222-224).  Plain pointers and sizes only;
+ * no CUDA, torch or C++ types cross the boundary.  Streams are passed as
+ * `void*` (a cudaStream_t, or NULL for the context's own stream).
+ *
+ * Conventions
+ *   - Every call returns ms_status (0 = MS_OK); ms_last_error() gives the
+ *     message of the last failure on a context.  No exceptions cross the ABI.
+ *   - Shapes, capacities and pointer alignment are validated on the host
+ *     before anything is launched (the reference's kernels check nothing:
+ *     a wrong packed_cols ran out of bounds, README.md:547-563).
+ *   - A context owns all device memory it allocates.  Host buffers passed in
+ *     are borrowed for the duration of the call only.
+ *   - One context per host thread (thread-compatible, not thread-safe).
+ *     Calls are asynchronous on the given stream unless stated otherwise;
+ *     ms_sync() waits.
+ *   - Activations are fp32 row-major, Q4 weights are the reference's layout
+ *     [K][N/2] (low nibble = even column, value (nibble - 8) * scale,
+ *     src/linalg/kernels.mojo:64-70), fp32 lm_head is [D][V].
+ */
+#ifndef MOJOSTREAM_CUDA_H
+#define MOJOSTREAM_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MS_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define MS_API __attribute__((visibility("default")))
+#else
+#define MS_API
+#endif
+
+typedef enum {
+  MS_OK = 0,
+  MS_ERR_INVALID_ARG = 1,  /* null pointer, bad enum, bad layer index            */
+  MS_ERR_SHAPE = 2,        /* unsupported or inconsistent dimensions             */
+  MS_ERR_ALIGN = 3,        /* device pointer not aligned as required             */
+  MS_ERR_CAPACITY = 4,     /* position beyond the KV cache, too many rows        */
+  MS_ERR_CUDA = 5,         /* a CUDA runtime call failed                         */
+  MS_ERR_NCCL = 6,         /* a collective failed                                */
+  MS_ERR_OOM = 7,          /* device allocation failed                           */
+  MS_ERR_STATE = 8,        /* objects from different contexts / wrong order      */
+  MS_ERR_TIMEOUT = 9,      /* a bounded wait ran out                             */
+  MS_ERR_UNSUPPORTED = 10  /* feature not built in this library                  */
+} ms_status;
+
+typedef struct ms_ctx ms_ctx;
+typedef struct ms_model ms_model;
+typedef struct ms_kv ms_kv;
+typedef struct ms_q4_weight ms_q4_weight;
+
+/* ---------------------------------------------------------------- context */
+
+MS_API int ms_abi_version(void);
+MS_API const char *ms_status_string(ms_status s);
+
+/* Bind to CUDA device `device` and create a context with its own stream. */
+MS_API ms_status ms_init(int device, ms_ctx **out);
+MS_API ms_status ms_destroy(ms_ctx *ctx);
+MS_API const char *ms_last_error(const ms_ctx *ctx);
+/* Wait for all work on `stream` (NULL = the context stream). */
+MS_API ms_status ms_sync(ms_ctx *ctx, void *stream);
+
+/* Device memory for hosts without CUDA headers.  kind: 0 host->device,
+ * 1 device->host, 2 device->device.  ms_memcpy is stream-ordered. */
+MS_API ms_status ms_malloc(ms_ctx *ctx, size_t bytes, void **dptr);
+MS_API ms_status ms_free(ms_ctx *ctx, void *dptr);
+MS_API ms_status ms_memcpy(ms_ctx *ctx, void *dst, const void *src, size_t bytes, int kind,
+                    void *stream);
+
+/* ------------------------------------------------- single Q4 projection */
+
+/* Replaces matmul_q4_bpack_raw(C, A, bq_ptr, packed_cols, scale, workers)
+ * (src/linalg/kernels.mojo:201-208).  The weight is repacked once into the
+ * tensor-core tile layout; N is passed explicitly instead of packed_cols so a
+ * wrong column count is rejected (MS_ERR_SHAPE) rather than read out of
+ * bounds.  w_rx may be a host or a device pointer.  K % 64 == 0, N % 16 == 0. */
+MS_API ms_status ms_q4_weight_create(ms_ctx *ctx, const uint8_t *w_rx, int K, int N, float scale,
+                              ms_q4_weight **out);
+MS_API ms_status ms_q4_weight_destroy(ms_ctx *ctx, ms_q4_weight *w);
+/* C[M,N] = A[M,K] . deq(W)   (accumulate = 0)
+ * C[M,N] += A[M,K] . deq(W)  (accumulate = 1, the reference's semantics)
+ * A, C: device pointers, row-major, 8-byte aligned. */
+MS_API ms_status ms_q4_gemm(ms_ctx *ctx, const ms_q4_weight *w, float *C, const float *A, int M,
+                     int accumulate, void *stream);
+
+/* ----------------------------------------------------------------- model */
+
+/* One decoder layer (E4BLayerRef, src/inference/gemma4_e4b.mojo:125-174;
+ * Gemma4LayerWeights, src/main.mojo:305-337).  window = 0 attends to every
+ * cached position (the demo layers and E4B's full-attention layers); window > 0
+ * is a sliding window over a circular cache.  RoPE rotates the leading
+ * rotary_dims of each head, pairs (i, i + rotary_dims / 2), with base
+ * rope_theta (src/linalg/kernels.mojo:553-595).  Matrices in the order
+ * Q, K, V, O, Gate, Up, Down; host or device pointers, reference layout. */
+typedef struct {
+  int head_dim;
+  int n_heads;
+  int n_kv_heads;
+  int window;
+  int rotary_dims;
+  int ffn_dim;
+  float rope_theta;
+  float ple;
+  const uint8_t *w[7];
+  float scale[7];
+} ms_layer_desc;
+
+typedef struct {
+  int hidden;
+  int n_layers;
+  const ms_layer_desc *layers;
+  int vocab;                /* 0 = no lm_head / embedding                    */
+  const float *lm_head;     /* [hidden][vocab] fp32, host or device, or NULL */
+  const float *final_gamma; /* [hidden] final RMSNorm gain, or NULL (= 1)    */
+  int max_rows;             /* largest M of any forward call                 */
+} ms_model_desc;
+
+/* Copies and repacks all weights to the device (the caller's buffers may be
+ * freed afterwards). */
+MS_API ms_status ms_model_create(ms_ctx *ctx, const ms_model_desc *desc, ms_model **out);
+MS_API ms_status ms_model_destroy(ms_ctx *ctx, ms_model *model);
+/* Device bytes held for weights (Q4 tiles + lm_head). */
+MS_API size_t ms_model_weight_bytes(const ms_model *model);
+
+/* -------------------------------------------------------------- KV cache */
+
+/* Paged KV cache for n_seq sequences (KVCache, src/main.mojo:257-301;
+ * HybridKVCache, src/inference/gemma4_e4b.mojo:83-116).  Full-attention
+ * layers hold max_pos positions; sliding layers hold slide_cap slots
+ * (0 = the window, as in the reference; a prefill chunk of L tokens needs
+ * slide_cap >= window + L - 1). */
+MS_API ms_status ms_kv_create(ms_ctx *ctx, const ms_model *model, int n_seq, int max_pos,
+                       int slide_cap, ms_kv **out);
+MS_API ms_status ms_kv_destroy(ms_ctx *ctx, ms_kv *kv);
+MS_API ms_status ms_kv_reset(ms_ctx *ctx, ms_kv *kv);
+MS_API size_t ms_kv_bytes(const ms_kv *kv);
+
+/* ---------------------------------------------------------------- forward */
+
+/* Rows: row r of x belongs to sequence seq_ids[r] at absolute position pos[r]
+ * (host arrays of M ints).  The reference's demo batch (B consecutive
+ * positions of one sequence, src/main.mojo:584-592) is seq_ids = {0,0,0,0},
+ * pos = {p, p+1, p+2, p+3}; independent sequences are seq_ids = {0,1,2,3}.
+ * x is a device pointer [M][hidden], updated in place. */
+
+/* gemma4_forward_layer (src/main.mojo:538-613) / e4b_forward_layer
+ * (src/inference/gemma4_e4b.mojo:459-540) for one layer. */
+MS_API ms_status ms_layer_forward(ms_ctx *ctx, const ms_model *model, int layer, float *x, ms_kv *kv,
+                           const int *seq_ids, const int *pos, int M, void *stream);
+/* All layers in order. */
+MS_API ms_status ms_forward(ms_ctx *ctx, const ms_model *model, float *x, ms_kv *kv,
+                     const int *seq_ids, const int *pos, int M, void *stream);
+/* get_token_embedding (src/inference/lm_head.mojo:171-195): x[r] = column
+ * ids[r] of the lm_head table.  ids: host array. */
+MS_API ms_status ms_embed(ms_ctx *ctx, const ms_model *model, const int *ids, int M, float *x,
+                   void *stream);
+/* apply_final_norm + project_lm_head + greedy temperature_sampling
+ * (src/inference/lm_head.mojo:119-168, 224-230).  x [M][hidden] device (not
+ * modified); logits [M][vocab] device or NULL; argmax_out [M] device or NULL. */
+MS_API ms_status ms_lm_head(ms_ctx *ctx, const ms_model *model, const float *x, int M, float *logits,
+                     int *argmax_out, void *stream);
+
+/* One greedy decode step with host buffers: embed ids, all layers, lm_head,
+ * argmax -> next_ids (host).  Synchronous.  (The token loop of
+ * gemma4_e4b_infer.mojo:163-186, one step.) */
+MS_API ms_status ms_decode_step(ms_ctx *ctx, const ms_model *model, ms_kv *kv, const int *ids,
+                         const int *seq_ids, const int *pos, int M, int *next_ids);
+
+/* `steps` greedy decode steps entirely on the device, replayed from a CUDA
+ * graph: ids (host, M) are the first inputs, pos (host, M) their positions;
+ * token t of step s is written to out_ids[s * M + t] (host).  Synchronous. */
+MS_API ms_status ms_generate(ms_ctx *ctx, const ms_model *model, ms_kv *kv, const int *ids,
+                      const int *seq_ids, const int *pos, int M, int steps, int *out_ids);
+
+/* Prefill (the TTFT pass): n_tokens rows (host arrays ids / seq_ids / pos,
+ * any mix of sequences) run through all layers in chunks of at most max_rows
+ * rows, writing the KV cache.  If first_ids is not NULL, the row with the
+ * highest position of every sequence present goes through the lm_head and
+ * its greedy token is written to first_ids[seq_id] (host, n_seq entries).
+ * Synchronous. */
+MS_API ms_status ms_prefill(ms_ctx *ctx, const ms_model *model, ms_kv *kv, const int *ids,
+                     const int *seq_ids, const int *pos, int n_tokens, int *first_ids);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MOJOSTREAM_CUDA_H */

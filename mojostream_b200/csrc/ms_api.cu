@@ -1,0 +1,1119 @@
+// ms_api.cu -- the C-ABI of libmojostream_cuda.so (include/mojostream_cuda.h):
+// contexts, weight upload + repack, the paged KV cache, layer orchestration,
+// CUDA-graph decode loop.
+//
+// Per layer the token loop runs five kernels (reference order,
+// src/main.mojo:538-613 / src/inference/gemma4_e4b.mojo:459-540):
+//   1. QKV   : PLE + RMSNorm prologue, fused Q|K|V projection, RoPE, KV write
+//   2. attn  : flash-decode GQA over the paged cache
+//   3. O     : projection + residual onto the normalised input + row stats
+//   4. GU    : RMSNorm prologue, fused gate|up projection, SwiGLU
+//   5. Down  : projection + residual + row stats for the next layer's norm
+// launched back to back with programmatic dependent launch, so each kernel's
+// weight stream starts while its predecessor drains.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <set>
+#include <string>
+#include <utility>
+#include <vector>
+
+#include "../../include/mojostream_cuda.h"
+#include "ms_kernels.h"
+
+using namespace ms;
+
+// --------------------------------------------------------------- objects --
+
+struct ms_ctx {
+  int device = 0;
+  int sm_count = 148;
+  cudaStream_t stream = nullptr;
+  std::string err;
+  // scratch shared by the kernels of one stream (consecutive kernels only
+  // touch it after griddepcontrol.wait, so one region serves all of them)
+  float* part = nullptr;
+  size_t part_floats = 0;
+  int* counters = nullptr;
+  size_t n_counters = 0;
+  float* lm_val = nullptr;
+  int* lm_idx = nullptr;
+  int* lm_counter = nullptr;
+  size_t lm_parts = 0;
+};
+
+struct LayerDev {
+  ms_layer_desc d{};
+  int q_dim = 0, kv_dim = 0, qkv_tiles = 0;
+  uint4* wqkv = nullptr;
+  QkvTile* tiles = nullptr;
+  uint4* wo = nullptr;
+  uint4* wgu = nullptr;
+  uint4* wd = nullptr;
+  float* inv_freq = nullptr;
+};
+
+struct ms_model {
+  ms_ctx* ctx = nullptr;
+  int hidden = 0, n_layers = 0, vocab = 0, max_rows = 0;
+  std::vector<LayerDev> layers;
+  float* lm_head = nullptr;
+  float* gamma = nullptr;
+  size_t weight_bytes = 0;
+  int max_q = 0, max_f = 0;
+  int span_hint = 1;  // longest attended span of the call being launched
+  // run buffers (max_rows rows)
+  float* X[2] = {nullptr, nullptr};
+  float* S[2] = {nullptr, nullptr};
+  float* Q = nullptr;
+  float* ATT = nullptr;
+  float* H = nullptr;
+  int* d_seq = nullptr;
+  int* d_pos = nullptr;
+  int* d_ids = nullptr;
+  int* d_next = nullptr;
+  int* d_step = nullptr;
+  int* d_hist = nullptr;
+  int hist_cap = 0;
+  // captured decode step
+  cudaGraphExec_t gexec = nullptr;
+  int g_M = 0;
+  int g_span = 0;
+  const ms_kv* g_kv = nullptr;
+  std::vector<void*> allocs;
+};
+
+struct ms_kv {
+  const ms_model* model = nullptr;
+  int n_seq = 0, max_pos = 0, slide_cap = 0, page = 16;
+  int pages_full = 0, pages_slide = 0;  // per sequence
+  std::vector<float*> k, v;
+  int* bt_full = nullptr;
+  int* bt_slide = nullptr;
+  size_t bytes = 0;
+};
+
+struct ms_q4_weight {
+  int K = 0, N = 0;
+  float scale = 1.f;
+  uint4* w = nullptr;
+};
+
+// ----------------------------------------------------------------- errors --
+
+static ms_status fail(ms_ctx* c, ms_status s, const char* fmt, ...) {
+  if (c) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    c->err = buf;
+  }
+  return s;
+}
+
+#define MS_CUDA(ctx, call)                                                                   \
+  do {                                                                                       \
+    cudaError_t e_ = (call);                                                                 \
+    if (e_ != cudaSuccess)                                                                   \
+      return fail((ctx), e_ == cudaErrorMemoryAllocation ? MS_ERR_OOM : MS_ERR_CUDA, "%s: %s", \
+                  #call, cudaGetErrorString(e_));                                            \
+  } while (0)
+
+#define MS_TRY(expr)               \
+  do {                             \
+    ms_status s_ = (expr);         \
+    if (s_ != MS_OK) return s_;    \
+  } while (0)
+
+static cudaStream_t pick(ms_ctx* c, void* s) { return s ? (cudaStream_t)s : c->stream; }
+
+static ms_status dev_alloc(ms_ctx* c, void** p, size_t bytes) {
+  cudaError_t e = cudaMalloc(p, bytes ? bytes : 16);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(c, MS_ERR_OOM, "cudaMalloc(%zu): %s", bytes, cudaGetErrorString(e));
+  }
+  return MS_OK;
+}
+
+template <typename T>
+static ms_status model_alloc(ms_model* m, T** p, size_t count) {
+  void* q = nullptr;
+  MS_TRY(dev_alloc(m->ctx, &q, count * sizeof(T)));
+  m->allocs.push_back(q);
+  *p = (T*)q;
+  return MS_OK;
+}
+
+static bool is_device_ptr(const void* p) {
+  cudaPointerAttributes a;
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
+}
+
+// ------------------------------------------------------------------ context --
+
+extern "C" int ms_abi_version(void) { return MS_ABI_VERSION; }
+
+extern "C" const char* ms_status_string(ms_status s) {
+  switch (s) {
+    case MS_OK: return "ok";
+    case MS_ERR_INVALID_ARG: return "invalid argument";
+    case MS_ERR_SHAPE: return "unsupported shape";
+    case MS_ERR_ALIGN: return "misaligned pointer";
+    case MS_ERR_CAPACITY: return "capacity exceeded";
+    case MS_ERR_CUDA: return "CUDA error";
+    case MS_ERR_NCCL: return "NCCL error";
+    case MS_ERR_OOM: return "out of device memory";
+    case MS_ERR_STATE: return "invalid state";
+    case MS_ERR_TIMEOUT: return "timeout";
+    case MS_ERR_UNSUPPORTED: return "unsupported";
+  }
+  return "unknown status";
+}
+
+extern "C" ms_status ms_init(int device, ms_ctx** out) {
+  if (!out) return MS_ERR_INVALID_ARG;
+  *out = nullptr;
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || device >= n) {
+    cudaGetLastError();
+    return MS_ERR_CUDA;
+  }
+  ms_ctx* c = new ms_ctx();
+  c->device = device;
+  if (cudaSetDevice(device) != cudaSuccess) {
+    delete c;
+    return MS_ERR_CUDA;
+  }
+  cudaDeviceGetAttribute(&c->sm_count, cudaDevAttrMultiProcessorCount, device);
+  if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) {
+    delete c;
+    return MS_ERR_CUDA;
+  }
+  // split-K / attention partials: 32 MiB; tickets: 1 Mi counters
+  c->part_floats = (size_t)8 << 20;
+  c->n_counters = (size_t)1 << 20;
+  c->lm_parts = (size_t)1 << 20;
+  if (dev_alloc(c, (void**)&c->part, c->part_floats * sizeof(float)) != MS_OK ||
+      dev_alloc(c, (void**)&c->counters, c->n_counters * sizeof(int)) != MS_OK ||
+      dev_alloc(c, (void**)&c->lm_val, c->lm_parts * sizeof(float)) != MS_OK ||
+      dev_alloc(c, (void**)&c->lm_idx, c->lm_parts * sizeof(int)) != MS_OK ||
+      dev_alloc(c, (void**)&c->lm_counter, 64 * sizeof(int)) != MS_OK) {
+    ms_destroy(c);
+    return MS_ERR_OOM;
+  }
+  cudaMemset(c->counters, 0, c->n_counters * sizeof(int));
+  cudaMemset(c->lm_counter, 0, 64 * sizeof(int));
+  if (cudaDeviceSynchronize() != cudaSuccess) {
+    ms_destroy(c);
+    return MS_ERR_CUDA;
+  }
+  *out = c;
+  return MS_OK;
+}
+
+extern "C" ms_status ms_destroy(ms_ctx* c) {
+  if (!c) return MS_ERR_INVALID_ARG;
+  cudaSetDevice(c->device);
+  if (c->stream) cudaStreamSynchronize(c->stream);
+  cudaFree(c->part);
+  cudaFree(c->counters);
+  cudaFree(c->lm_val);
+  cudaFree(c->lm_idx);
+  cudaFree(c->lm_counter);
+  if (c->stream) cudaStreamDestroy(c->stream);
+  delete c;
+  return MS_OK;
+}
+
+extern "C" const char* ms_last_error(const ms_ctx* c) { return c ? c->err.c_str() : "null context"; }
+
+extern "C" ms_status ms_sync(ms_ctx* c, void* stream) {
+  if (!c) return MS_ERR_INVALID_ARG;
+  MS_CUDA(c, cudaStreamSynchronize(pick(c, stream)));
+  return MS_OK;
+}
+
+extern "C" ms_status ms_malloc(ms_ctx* c, size_t bytes, void** dptr) {
+  if (!c || !dptr) return MS_ERR_INVALID_ARG;
+  cudaSetDevice(c->device);
+  return dev_alloc(c, dptr, bytes);
+}
+
+extern "C" ms_status ms_free(ms_ctx* c, void* dptr) {
+  if (!c) return MS_ERR_INVALID_ARG;
+  MS_CUDA(c, cudaFree(dptr));
+  return MS_OK;
+}
+
+extern "C" ms_status ms_memcpy(ms_ctx* c, void* dst, const void* src, size_t bytes, int kind,
+                               void* stream) {
+  if (!c || (!dst && bytes) || (!src && bytes)) return MS_ERR_INVALID_ARG;
+  cudaMemcpyKind k = kind == 0 ? cudaMemcpyHostToDevice
+                               : (kind == 1 ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice);
+  if (kind < 0 || kind > 2) return fail(c, MS_ERR_INVALID_ARG, "ms_memcpy: kind %d", kind);
+  MS_CUDA(c, cudaMemcpyAsync(dst, src, bytes, k, pick(c, stream)));
+  return MS_OK;
+}
+
+// --------------------------------------------------------- repack helpers --
+
+// Stage a reference-layout matrix on the device (copy if it is host memory).
+static ms_status stage_bytes(ms_ctx* c, const uint8_t* src, size_t bytes, const uint8_t** dev,
+                             void** owned) {
+  *owned = nullptr;
+  if (is_device_ptr(src)) {
+    *dev = src;
+    return MS_OK;
+  }
+  void* d = nullptr;
+  MS_TRY(dev_alloc(c, &d, bytes));
+  cudaError_t e = cudaMemcpy(d, src, bytes, cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) {
+    cudaFree(d);
+    return fail(c, MS_ERR_CUDA, "weight upload: %s", cudaGetErrorString(e));
+  }
+  *dev = (const uint8_t*)d;
+  *owned = d;
+  return MS_OK;
+}
+
+// Repack up to three source matrices (columns concatenated by perm) into
+// fragment tiles.
+static ms_status repack(ms_ctx* c, uint4* out, const std::vector<const uint8_t*>& srcs,
+                        const std::vector<int>& src_n, int K, const std::vector<int>& perm) {
+  std::vector<const uint8_t*> dev(srcs.size());
+  std::vector<void*> owned(srcs.size(), nullptr);
+  ms_status st = MS_OK;
+  for (size_t i = 0; i < srcs.size() && st == MS_OK; ++i)
+    st = stage_bytes(c, srcs[i], (size_t)K * (src_n[i] / 2), &dev[i], &owned[i]);
+  int* dperm = nullptr;
+  if (st == MS_OK) st = dev_alloc(c, (void**)&dperm, perm.size() * sizeof(int));
+  if (st == MS_OK) {
+    cudaMemcpy(dperm, perm.data(), perm.size() * sizeof(int), cudaMemcpyHostToDevice);
+    cudaError_t e = launch_repack(out, dev.data(), src_n.data(), (int)srcs.size(), dperm,
+                                  (int)perm.size() / kTileN, K, c->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+    if (e != cudaSuccess) st = fail(c, MS_ERR_CUDA, "repack: %s", cudaGetErrorString(e));
+  }
+  cudaFree(dperm);
+  for (void* o : owned) cudaFree(o);
+  return st;
+}
+
+static std::vector<int> identity_perm(int N, int src = 0) {
+  std::vector<int> p(N);
+  for (int i = 0; i < N; ++i) p[i] = (src << 24) | i;
+  return p;
+}
+
+// ----------------------------------------------------------- Q4 weight API --
+
+extern "C" ms_status ms_q4_weight_create(ms_ctx* c, const uint8_t* w_rx, int K, int N,
+                                         float scale, ms_q4_weight** out) {
+  if (!c || !w_rx || !out) return MS_ERR_INVALID_ARG;
+  *out = nullptr;
+  if (K <= 0 || N <= 0 || K % kChunkK || N % kTileN)
+    return fail(c, MS_ERR_SHAPE, "ms_q4_weight_create: K=%d N=%d (need K%%64==0, N%%16==0)", K, N);
+  cudaSetDevice(c->device);
+  ms_q4_weight* w = new ms_q4_weight();
+  w->K = K;
+  w->N = N;
+  w->scale = scale;
+  if (dev_alloc(c, (void**)&w->w, (size_t)K * N / 2) != MS_OK) {
+    delete w;
+    return MS_ERR_OOM;
+  }
+  ms_status st = repack(c, w->w, {w_rx}, {N}, K, identity_perm(N));
+  if (st != MS_OK) {
+    cudaFree(w->w);
+    delete w;
+    return st;
+  }
+  *out = w;
+  return MS_OK;
+}
+
+extern "C" ms_status ms_q4_weight_destroy(ms_ctx* c, ms_q4_weight* w) {
+  if (!c || !w) return MS_ERR_INVALID_ARG;
+  cudaFree(w->w);
+  delete w;
+  return MS_OK;
+}
+
+// Launch plan of one projection: m-group size, chunks per round, k-segment.
+struct GemvPlan {
+  int mg, ch, kseg, ksplit;
+};
+
+static GemvPlan plan_gemv(const ms_ctx* c, int M, int K, int n_tiles) {
+  GemvPlan pl{};
+  int mg = 1;
+  while (mg < 16 && 4 * mg < M) mg *= 2;
+  pl.mg = mg;
+  const int mb = 4 * mg;
+  const int chunks = K / kChunkK;
+  const int mblocks = (M + mb - 1) / mb;
+  const int nct = (n_tiles + 3) / 4;
+  const long base = (long)mblocks * nct;
+  const long target = 3L * c->sm_count;  // CTAs wanted in flight
+  pl.ch = mg <= 2 ? 8 : (mg == 4 ? 4 : (mg == 8 ? 4 : 2));
+  if (mg <= 2 && base * ((chunks + 7) / 8) < target) pl.ch = 4;  // small matrix: finer split
+  const int rounds = (chunks + pl.ch - 1) / pl.ch;  // rounds if one CTA covered all of K
+  int ksplit = (int)std::min<long>(rounds, std::max<long>(1, (target + base - 1) / base));
+  auto need = [&](int ks) { return ks > 1 ? (size_t)base * ks * 4 * kTileN * mb : (size_t)0; };
+  while (ksplit > 1 && (need(ksplit) > c->part_floats || (size_t)base > c->n_counters)) --ksplit;
+  const int rounds_per = (rounds + ksplit - 1) / ksplit;
+  pl.kseg = rounds_per * pl.ch * kChunkK;
+  pl.ksplit = (K + pl.kseg - 1) / pl.kseg;
+  return pl;
+}
+
+static GemvParams gemv_base(ms_ctx* c, const uint4* w, int n_tiles, int K, int M,
+                            const GemvPlan& pl) {
+  GemvParams p{};
+  p.w = w;
+  p.n_tiles = n_tiles;
+  p.K = K;
+  p.kseg = pl.kseg;
+  p.ksplit = pl.ksplit;
+  p.M = M;
+  p.in_ple = 1.f;
+  p.resid_ple = 1.f;
+  p.scale = 1.f;
+  p.scale2 = 1.f;
+  p.part = c->part;
+  p.counters = c->counters;
+  return p;
+}
+
+extern "C" ms_status ms_q4_gemm(ms_ctx* c, const ms_q4_weight* w, float* C, const float* A, int M,
+                                int accumulate, void* stream) {
+  if (!c || !w || !C || !A) return MS_ERR_INVALID_ARG;
+  if (M <= 0) return fail(c, MS_ERR_SHAPE, "ms_q4_gemm: M=%d", M);
+  if (((uintptr_t)A & 7) || ((uintptr_t)C & 7))
+    return fail(c, MS_ERR_ALIGN, "ms_q4_gemm: A and C must be 8-byte aligned");
+  const int n_tiles = w->N / kTileN;
+  GemvPlan pl = plan_gemv(c, M, w->K, n_tiles);
+  GemvParams p = gemv_base(c, w->w, n_tiles, w->K, M, pl);
+  p.x = A;
+  p.ldx = w->K;
+  p.in_D = w->K;
+  p.epi = accumulate ? kEpiAccum : kEpiStore;
+  p.out = C;
+  p.ldo = w->N;
+  p.scale = w->scale;
+  MS_CUDA(c, launch_gemv(p, pl.mg, pl.ch, pick(c, stream), false));
+  return MS_OK;
+}
+
+// ------------------------------------------------------------------- model --
+
+static ms_status check_layer(ms_ctx* c, const ms_layer_desc& L, int D, int i) {
+  if (L.head_dim <= 0 || L.n_heads <= 0 || L.n_kv_heads <= 0 || L.ffn_dim <= 0)
+    return fail(c, MS_ERR_SHAPE, "layer %d: non-positive dimension", i);
+  if (L.n_heads % L.n_kv_heads)
+    return fail(c, MS_ERR_SHAPE, "layer %d: n_heads %% n_kv_heads != 0", i);
+  const int G = L.n_heads / L.n_kv_heads;
+  const bool hd_ok = L.head_dim == 64 || L.head_dim == 128 || L.head_dim == 256 || L.head_dim == 512;
+  const bool g_ok = G == 1 || G == 2 || G == 4 || G == 5 || G == 8;
+  if (!hd_ok || !g_ok || (L.head_dim == 512 && G > 4))
+    return fail(c, MS_ERR_SHAPE, "layer %d: head_dim %d with %d query heads per KV head not built",
+                i, L.head_dim, G);
+  if (L.rotary_dims < 0 || L.rotary_dims > L.head_dim || L.rotary_dims % 16 ||
+      (L.head_dim - L.rotary_dims) % 16)
+    return fail(c, MS_ERR_SHAPE, "layer %d: rotary_dims %d", i, L.rotary_dims);
+  if (L.window < 0) return fail(c, MS_ERR_SHAPE, "layer %d: window %d", i, L.window);
+  const int q = L.n_heads * L.head_dim, kv = L.n_kv_heads * L.head_dim;
+  if (q % kChunkK || L.ffn_dim % kChunkK || kv % kTileN)
+    return fail(c, MS_ERR_SHAPE, "layer %d: q_dim %d / ffn %d must be multiples of 64", i, q,
+                L.ffn_dim);
+  for (int m = 0; m < 7; ++m)
+    if (!L.w[m]) return fail(c, MS_ERR_INVALID_ARG, "layer %d: weight %d is null", i, m);
+  (void)D;
+  return MS_OK;
+}
+
+// Column order of the fused Q|K|V matrix: per head, RoPE pairs (i, i + R/2)
+// in tiles of 8 + 8, then the unrotated tail in tiles of 16; V plain.
+static void qkv_layout(const ms_layer_desc& L, std::vector<int>& perm, std::vector<QkvTile>& tiles) {
+  const int hd = L.head_dim, R = L.rotary_dims, half = R / 2;
+  auto heads = [&](int src, int nh, bool rope) {
+    for (int h = 0; h < nh; ++h) {
+      const int base = h * hd;
+      int start = 0;
+      if (rope) {
+        for (int i0 = 0; i0 < half; i0 += 8) {
+          QkvTile t{src, base + i0, base + half + i0, i0};
+          tiles.push_back(t);
+          for (int r = 0; r < 8; ++r) perm.push_back((src << 24) | (base + i0 + r));
+          for (int r = 0; r < 8; ++r) perm.push_back((src << 24) | (base + half + i0 + r));
+        }
+        start = R;
+      }
+      for (int c0 = start; c0 < hd; c0 += 16) {
+        QkvTile t{src, base + c0, base + c0 + 8, -1};
+        tiles.push_back(t);
+        for (int r = 0; r < 16; ++r) perm.push_back((src << 24) | (base + c0 + r));
+      }
+    }
+  };
+  heads(0, L.n_heads, R > 0);
+  heads(1, L.n_kv_heads, R > 0);
+  heads(2, L.n_kv_heads, false);
+}
+
+extern "C" ms_status ms_model_create(ms_ctx* c, const ms_model_desc* desc, ms_model** out) {
+  if (!c || !desc || !out || !desc->layers) return MS_ERR_INVALID_ARG;
+  *out = nullptr;
+  const int D = desc->hidden;
+  if (D <= 0 || D % kChunkK || desc->n_layers <= 0 || desc->max_rows <= 0)
+    return fail(c, MS_ERR_SHAPE, "model: hidden %d (multiple of 64), n_layers %d, max_rows %d", D,
+                desc->n_layers, desc->max_rows);
+  if (desc->vocab < 0 || (desc->vocab > 0 && (!desc->lm_head || desc->vocab % 4)))
+    return fail(c, MS_ERR_SHAPE, "model: vocab %d needs an lm_head and vocab %% 4 == 0",
+                desc->vocab);
+  for (int i = 0; i < desc->n_layers; ++i) MS_TRY(check_layer(c, desc->layers[i], D, i));
+  cudaSetDevice(c->device);
+
+  ms_model* m = new ms_model();
+  m->ctx = c;
+  m->hidden = D;
+  m->n_layers = desc->n_layers;
+  m->vocab = desc->vocab;
+  m->max_rows = desc->max_rows;
+  auto bail = [&](ms_status s) {
+    ms_model_destroy(c, m);
+    return s;
+  };
+  for (int i = 0; i < desc->n_layers; ++i) {
+    const ms_layer_desc& L = desc->layers[i];
+    LayerDev ld;
+    ld.d = L;
+    for (int j = 0; j < 7; ++j) ld.d.w[j] = nullptr;
+    ld.q_dim = L.n_heads * L.head_dim;
+    ld.kv_dim = L.n_kv_heads * L.head_dim;
+    m->max_q = std::max(m->max_q, ld.q_dim);
+    m->max_f = std::max(m->max_f, L.ffn_dim);
+    // fused Q|K|V
+    std::vector<int> perm;
+    std::vector<QkvTile> tiles;
+    qkv_layout(L, perm, tiles);
+    ld.qkv_tiles = (int)tiles.size();
+    const int nqkv = ld.q_dim + 2 * ld.kv_dim;
+    ms_status st = model_alloc(m, &ld.wqkv, (size_t)D * nqkv / 2 / sizeof(uint4));
+    if (st == MS_OK) st = repack(c, ld.wqkv, {L.w[0], L.w[1], L.w[2]}, {ld.q_dim, ld.kv_dim, ld.kv_dim}, D, perm);
+    if (st == MS_OK) st = model_alloc(m, &ld.tiles, tiles.size());
+    if (st == MS_OK)
+      cudaMemcpy(ld.tiles, tiles.data(), tiles.size() * sizeof(QkvTile), cudaMemcpyHostToDevice);
+    // O
+    if (st == MS_OK) st = model_alloc(m, &ld.wo, (size_t)ld.q_dim * D / 2 / sizeof(uint4));
+    if (st == MS_OK) st = repack(c, ld.wo, {L.w[3]}, {D}, ld.q_dim, identity_perm(D));
+    // gate | up interleaved by 8 columns
+    if (st == MS_OK) st = model_alloc(m, &ld.wgu, (size_t)D * 2 * L.ffn_dim / 2 / sizeof(uint4));
+    if (st == MS_OK) {
+      std::vector<int> gp;
+      gp.reserve(2 * L.ffn_dim);
+      for (int j = 0; j < L.ffn_dim / 8; ++j) {
+        for (int r = 0; r < 8; ++r) gp.push_back((0 << 24) | (8 * j + r));
+        for (int r = 0; r < 8; ++r) gp.push_back((1 << 24) | (8 * j + r));
+      }
+      st = repack(c, ld.wgu, {L.w[4], L.w[5]}, {L.ffn_dim, L.ffn_dim}, D, gp);
+    }
+    // Down
+    if (st == MS_OK) st = model_alloc(m, &ld.wd, (size_t)L.ffn_dim * D / 2 / sizeof(uint4));
+    if (st == MS_OK) st = repack(c, ld.wd, {L.w[6]}, {D}, L.ffn_dim, identity_perm(D));
+    // RoPE inverse frequencies (src/linalg/kernels.mojo:573-575), fp32 as the
+    // reference computes them
+    if (st == MS_OK && L.rotary_dims > 0) {
+      std::vector<float> inv(L.rotary_dims / 2);
+      const float ln_base = logf(L.rope_theta);
+      for (int j = 0; j < L.rotary_dims / 2; ++j)
+        inv[j] = expf(-(float)(2 * j) / (float)L.rotary_dims * ln_base);
+      st = model_alloc(m, &ld.inv_freq, inv.size());
+      if (st == MS_OK)
+        cudaMemcpy(ld.inv_freq, inv.data(), inv.size() * sizeof(float), cudaMemcpyHostToDevice);
+    }
+    if (st != MS_OK) return bail(st);
+    m->weight_bytes += (size_t)D * nqkv / 2 + (size_t)ld.q_dim * D / 2 +
+                       (size_t)D * L.ffn_dim + (size_t)L.ffn_dim * D / 2;
+    m->layers.push_back(ld);
+  }
+  if (desc->vocab > 0) {
+    const size_t n = (size_t)D * desc->vocab;
+    if (model_alloc(m, &m->lm_head, n) != MS_OK) return bail(MS_ERR_OOM);
+    if (cudaMemcpy(m->lm_head, desc->lm_head, n * sizeof(float), cudaMemcpyDefault) != cudaSuccess)
+      return bail(fail(c, MS_ERR_CUDA, "lm_head upload failed"));
+    m->weight_bytes += n * sizeof(float);
+    if (desc->final_gamma) {
+      if (model_alloc(m, &m->gamma, D) != MS_OK) return bail(MS_ERR_OOM);
+      cudaMemcpy(m->gamma, desc->final_gamma, D * sizeof(float), cudaMemcpyDefault);
+    }
+  }
+  const int R = desc->max_rows;
+  ms_status st = MS_OK;
+  for (int i = 0; i < 2 && st == MS_OK; ++i) {
+    st = model_alloc(m, &m->X[i], (size_t)R * D);
+    if (st == MS_OK) st = model_alloc(m, &m->S[i], (size_t)R * (D / kTileN));
+  }
+  if (st == MS_OK) st = model_alloc(m, &m->Q, (size_t)R * m->max_q);
+  if (st == MS_OK) st = model_alloc(m, &m->ATT, (size_t)R * m->max_q);
+  if (st == MS_OK) st = model_alloc(m, &m->H, (size_t)R * m->max_f);
+  if (st == MS_OK) st = model_alloc(m, &m->d_seq, R);
+  if (st == MS_OK) st = model_alloc(m, &m->d_pos, R);
+  if (st == MS_OK) st = model_alloc(m, &m->d_ids, R);
+  if (st == MS_OK) st = model_alloc(m, &m->d_next, R);
+  if (st == MS_OK) st = model_alloc(m, &m->d_step, 1);
+  if (st != MS_OK) return bail(st);
+  if (cudaDeviceSynchronize() != cudaSuccess) return bail(fail(c, MS_ERR_CUDA, "model upload"));
+  *out = m;
+  return MS_OK;
+}
+
+extern "C" ms_status ms_model_destroy(ms_ctx* c, ms_model* m) {
+  if (!c || !m) return MS_ERR_INVALID_ARG;
+  cudaSetDevice(c->device);
+  cudaStreamSynchronize(c->stream);
+  if (m->gexec) cudaGraphExecDestroy(m->gexec);
+  for (void* p : m->allocs) cudaFree(p);
+  if (m->d_hist) cudaFree(m->d_hist);
+  delete m;
+  return MS_OK;
+}
+
+extern "C" size_t ms_model_weight_bytes(const ms_model* m) { return m ? m->weight_bytes : 0; }
+
+// ---------------------------------------------------------------- KV cache --
+
+extern "C" ms_status ms_kv_create(ms_ctx* c, const ms_model* m, int n_seq, int max_pos,
+                                  int slide_cap, ms_kv** out) {
+  if (!c || !m || !out) return MS_ERR_INVALID_ARG;
+  *out = nullptr;
+  if (m->ctx != c) return fail(c, MS_ERR_STATE, "model belongs to another context");
+  if (n_seq <= 0 || max_pos <= 0 || slide_cap < 0)
+    return fail(c, MS_ERR_SHAPE, "kv: n_seq %d max_pos %d slide_cap %d", n_seq, max_pos, slide_cap);
+  cudaSetDevice(c->device);
+  ms_kv* kv = new ms_kv();
+  kv->model = m;
+  kv->n_seq = n_seq;
+  kv->max_pos = max_pos;
+  int win = 0;
+  for (const LayerDev& L : m->layers) win = std::max(win, L.d.window);
+  if (win > 0) {
+    int cap = slide_cap ? slide_cap : win;
+    if (cap < win) {
+      delete kv;
+      return fail(c, MS_ERR_SHAPE, "kv: slide_cap %d below the window %d", cap, win);
+    }
+    if (cap % kv->page) {
+      delete kv;
+      return fail(c, MS_ERR_SHAPE, "kv: slide_cap %d must be a multiple of %d", cap, kv->page);
+    }
+    kv->slide_cap = cap;
+    kv->pages_slide = cap / kv->page;
+  }
+  kv->pages_full = (max_pos + kv->page - 1) / kv->page;
+  auto cleanup = [&](ms_status s) {
+    ms_kv_destroy(c, kv);
+    return s;
+  };
+  // block tables: sequence s owns pages [s * P, (s + 1) * P) of every pool
+  std::vector<int> bt((size_t)n_seq * std::max(kv->pages_full, kv->pages_slide));
+  for (int pass = 0; pass < 2; ++pass) {
+    const int P = pass == 0 ? kv->pages_full : kv->pages_slide;
+    if (P == 0) continue;
+    for (int s = 0; s < n_seq; ++s)
+      for (int j = 0; j < P; ++j) bt[(size_t)s * P + j] = s * P + j;
+    int** dst = pass == 0 ? &kv->bt_full : &kv->bt_slide;
+    if (dev_alloc(c, (void**)dst, (size_t)n_seq * P * sizeof(int)) != MS_OK) return cleanup(MS_ERR_OOM);
+    cudaMemcpy(*dst, bt.data(), (size_t)n_seq * P * sizeof(int), cudaMemcpyHostToDevice);
+  }
+  for (const LayerDev& L : m->layers) {
+    const int P = L.d.window > 0 ? kv->pages_slide : kv->pages_full;
+    const size_t n = (size_t)n_seq * P * kv->page * L.kv_dim;
+    float *k = nullptr, *v = nullptr;
+    if (dev_alloc(c, (void**)&k, n * sizeof(float)) != MS_OK) return cleanup(MS_ERR_OOM);
+    kv->k.push_back(k);
+    if (dev_alloc(c, (void**)&v, n * sizeof(float)) != MS_OK) return cleanup(MS_ERR_OOM);
+    kv->v.push_back(v);
+    cudaMemset(k, 0, n * sizeof(float));
+    cudaMemset(v, 0, n * sizeof(float));
+    kv->bytes += 2 * n * sizeof(float);
+  }
+  if (cudaDeviceSynchronize() != cudaSuccess) return cleanup(fail(c, MS_ERR_CUDA, "kv create"));
+  *out = kv;
+  return MS_OK;
+}
+
+extern "C" ms_status ms_kv_destroy(ms_ctx* c, ms_kv* kv) {
+  if (!c || !kv) return MS_ERR_INVALID_ARG;
+  cudaSetDevice(c->device);
+  cudaStreamSynchronize(c->stream);
+  for (float* p : kv->k) cudaFree(p);
+  for (float* p : kv->v) cudaFree(p);
+  cudaFree(kv->bt_full);
+  cudaFree(kv->bt_slide);
+  delete kv;
+  return MS_OK;
+}
+
+extern "C" ms_status ms_kv_reset(ms_ctx* c, ms_kv* kv) {
+  if (!c || !kv) return MS_ERR_INVALID_ARG;
+  // positions are explicit per call; the contents need no clearing, but do it
+  // so a reset cache is indistinguishable from a new one
+  for (size_t i = 0; i < kv->k.size(); ++i) {
+    const LayerDev& L = kv->model->layers[i];
+    const int P = L.d.window > 0 ? kv->pages_slide : kv->pages_full;
+    const size_t n = (size_t)kv->n_seq * P * kv->page * L.kv_dim * sizeof(float);
+    MS_CUDA(c, cudaMemsetAsync(kv->k[i], 0, n, c->stream));
+    MS_CUDA(c, cudaMemsetAsync(kv->v[i], 0, n, c->stream));
+  }
+  return MS_OK;
+}
+
+extern "C" size_t ms_kv_bytes(const ms_kv* kv) { return kv ? kv->bytes : 0; }
+
+// ----------------------------------------------------------------- forward --
+
+// Host-side validation of one call's rows against the cache.
+static ms_status check_rows(ms_ctx* c, const ms_model* m, const ms_kv* kv, const int* seq,
+                            const int* pos, int M) {
+  if (!seq || !pos) return fail(c, MS_ERR_INVALID_ARG, "seq_ids / pos are null");
+  if (M <= 0 || M > m->max_rows)
+    return fail(c, MS_ERR_CAPACITY, "M=%d outside 1..max_rows=%d", M, m->max_rows);
+  if (kv->model != m) return fail(c, MS_ERR_STATE, "KV cache was made for another model");
+  std::set<std::pair<int, int>> seen;
+  std::vector<int> pmin(kv->n_seq, 1 << 30), pmax(kv->n_seq, -1);
+  for (int r = 0; r < M; ++r) {
+    if (seq[r] < 0 || seq[r] >= kv->n_seq)
+      return fail(c, MS_ERR_INVALID_ARG, "row %d: sequence %d outside 0..%d", r, seq[r], kv->n_seq - 1);
+    if (pos[r] < 0 || pos[r] >= kv->max_pos)
+      return fail(c, MS_ERR_CAPACITY, "row %d: position %d outside the cache (max_pos %d)", r,
+                  pos[r], kv->max_pos);
+    if (!seen.insert({seq[r], pos[r]}).second)
+      return fail(c, MS_ERR_INVALID_ARG, "row %d: (sequence %d, position %d) given twice", r,
+                  seq[r], pos[r]);
+    pmin[seq[r]] = std::min(pmin[seq[r]], pos[r]);
+    pmax[seq[r]] = std::max(pmax[seq[r]], pos[r]);
+  }
+  if (kv->slide_cap > 0) {
+    int win = 0;
+    for (const LayerDev& L : m->layers) win = std::max(win, L.d.window);
+    for (int s = 0; s < kv->n_seq; ++s)
+      if (pmax[s] >= 0 && pmax[s] - pmin[s] + win > kv->slide_cap)
+        return fail(c, MS_ERR_CAPACITY,
+                    "sequence %d: positions %d..%d in one call overwrite sliding slots still in "
+                    "the window (slide_cap %d)", s, pmin[s], pmax[s], kv->slide_cap);
+  }
+  return MS_OK;
+}
+
+static void set_span(ms_model* m, const int* pos, int M, int extra) {
+  int mx = 0;
+  for (int r = 0; r < M; ++r) mx = std::max(mx, pos[r] + 1 + extra);
+  m->span_hint = std::max(1, mx);
+}
+
+static ms_status upload_rows(ms_ctx* c, ms_model* m, const int* seq, const int* pos, int M,
+                             cudaStream_t s) {
+  set_span(m, pos, M, 0);
+  MS_CUDA(c, cudaMemcpyAsync(m->d_seq, seq, M * sizeof(int), cudaMemcpyHostToDevice, s));
+  MS_CUDA(c, cudaMemcpyAsync(m->d_pos, pos, M * sizeof(int), cudaMemcpyHostToDevice, s));
+  return MS_OK;
+}
+
+static KvView kv_view(const ms_kv* kv, int layer) {
+  const LayerDev& L = kv->model->layers[layer];
+  KvView v{};
+  v.k = kv->k[layer];
+  v.v = kv->v[layer];
+  const bool slide = L.d.window > 0;
+  v.block_table = slide ? kv->bt_slide : kv->bt_full;
+  v.bt_stride = slide ? kv->pages_slide : kv->pages_full;
+  v.page = kv->page;
+  v.cap = slide ? kv->slide_cap : kv->pages_full * kv->page;
+  v.circular = slide ? 1 : 0;
+  v.kv_dim = L.kv_dim;
+  return v;
+}
+
+// The five kernels of one layer.  x/xs: input rows and their stats (in
+// place: the layer output lands in x, its stats in xs); y/ys: the second
+// residual buffer.
+static ms_status run_layer(ms_ctx* c, ms_model* m, const ms_kv* kv, int li, int M, float* x,
+                           float* xs, float* y, float* ys, cudaStream_t s, bool pdl) {
+  const LayerDev& L = m->layers[li];
+  const int D = m->hidden, F = L.d.ffn_dim, nstat = D / kTileN;
+  // 1. QKV + RoPE + KV write
+  {
+    GemvPlan pl = plan_gemv(c, M, D, L.qkv_tiles);
+    GemvParams p = gemv_base(c, L.wqkv, L.qkv_tiles, D, M, pl);
+    p.x = x;
+    p.ldx = D;
+    p.in_stats = xs;
+    p.in_nstat = nstat;
+    p.in_ple = L.d.ple;
+    p.in_D = D;
+    p.epi = kEpiQKV;
+    p.tiles = L.tiles;
+    p.sq = L.d.scale[0];
+    p.sk = L.d.scale[1];
+    p.sv = L.d.scale[2];
+    p.q_out = m->Q;
+    p.ldq = L.q_dim;
+    p.inv_freq = L.inv_freq;
+    p.pos = m->d_pos;
+    p.seq = m->d_seq;
+    p.kv = kv_view(kv, li);
+    MS_CUDA(c, launch_gemv(p, pl.mg, pl.ch, s, pdl));
+  }
+  // 2. attention
+  {
+    AttnParams a{};
+    a.q = m->Q;
+    a.ldq = L.q_dim;
+    a.out = m->ATT;
+    a.ldo = L.q_dim;
+    a.kv = kv_view(kv, li);
+    a.seq = m->d_seq;
+    a.pos = m->d_pos;
+    a.hd = L.d.head_dim;
+    a.n_heads = L.d.n_heads;
+    a.n_kv = L.d.n_kv_heads;
+    a.window = L.d.window;
+    a.M = M;
+    a.scale = 1.0f / sqrtf((float)L.d.head_dim);
+    // splits: enough CTAs to fill the GPU at the longest span of this call;
+    // the kernel sizes each row's chunks itself, so any position is covered
+    const int span = L.d.window > 0 ? std::min(L.d.window, m->span_hint) : m->span_hint;
+    const long ctas_per_split = (long)M * L.d.n_kv_heads;
+    const int min_chunk = 32;
+    int splits = (int)std::max<long>(1, (2L * c->sm_count + ctas_per_split - 1) / ctas_per_split);
+    splits = std::min(splits, std::max(1, (span + min_chunk - 1) / min_chunk));
+    splits = std::min(splits, 64);
+    const int G = L.d.n_heads / L.d.n_kv_heads;
+    while (splits > 1 &&
+           (size_t)M * L.d.n_kv_heads * splits * G * (L.d.head_dim + 2) > c->part_floats)
+      splits = (splits + 1) / 2;
+    if ((size_t)M * L.d.n_kv_heads * G * (L.d.head_dim + 2) > c->part_floats && splits > 1)
+      return fail(c, MS_ERR_CAPACITY, "attention scratch too small");
+    if ((size_t)M * L.d.n_kv_heads > c->n_counters)
+      return fail(c, MS_ERR_CAPACITY, "attention: too many rows for the ticket counters");
+    a.chunk = min_chunk;
+    a.n_splits = splits;
+    a.part = c->part;
+    a.counters = c->counters;
+    MS_CUDA(c, launch_attention(a, s, pdl));
+  }
+  // 3. O projection + residual onto the normalised input
+  {
+    GemvPlan pl = plan_gemv(c, M, L.q_dim, D / kTileN);
+    GemvParams p = gemv_base(c, L.wo, D / kTileN, L.q_dim, M, pl);
+    p.x = m->ATT;
+    p.ldx = L.q_dim;
+    p.in_D = D;
+    p.epi = kEpiResid;
+    p.out = y;
+    p.ldo = D;
+    p.scale = L.d.scale[3];
+    p.resid = x;
+    p.ldr = D;
+    p.resid_stats = xs;
+    p.resid_nstat = nstat;
+    p.resid_ple = L.d.ple;
+    p.out_stats = ys;
+    MS_CUDA(c, launch_gemv(p, pl.mg, pl.ch, s, pdl));
+  }
+  // 4. gate | up + SwiGLU
+  {
+    const int nt = 2 * F / kTileN;
+    GemvPlan pl = plan_gemv(c, M, D, nt);
+    GemvParams p = gemv_base(c, L.wgu, nt, D, M, pl);
+    p.x = y;
+    p.ldx = D;
+    p.in_stats = ys;
+    p.in_nstat = nstat;
+    p.in_D = D;
+    p.epi = kEpiSwiGLU;
+    p.out = m->H;
+    p.ldo = F;
+    p.scale = L.d.scale[4];
+    p.scale2 = L.d.scale[5];
+    MS_CUDA(c, launch_gemv(p, pl.mg, pl.ch, s, pdl));
+  }
+  // 5. Down + residual
+  {
+    GemvPlan pl = plan_gemv(c, M, F, D / kTileN);
+    GemvParams p = gemv_base(c, L.wd, D / kTileN, F, M, pl);
+    p.x = m->H;
+    p.ldx = F;
+    p.in_D = D;
+    p.epi = kEpiResid;
+    p.out = x;
+    p.ldo = D;
+    p.scale = L.d.scale[6];
+    p.resid = y;
+    p.ldr = D;
+    p.resid_stats = ys;
+    p.resid_nstat = nstat;
+    p.resid_ple = 1.f;
+    p.out_stats = xs;
+    MS_CUDA(c, launch_gemv(p, pl.mg, pl.ch, s, pdl));
+  }
+  return MS_OK;
+}
+
+static ms_status check_x(ms_ctx* c, const float* x) {
+  if (!x) return fail(c, MS_ERR_INVALID_ARG, "x is null");
+  if ((uintptr_t)x & 15) return fail(c, MS_ERR_ALIGN, "x must be 16-byte aligned");
+  return MS_OK;
+}
+
+extern "C" ms_status ms_layer_forward(ms_ctx* c, const ms_model* mc, int layer, float* x,
+                                      ms_kv* kv, const int* seq, const int* pos, int M,
+                                      void* stream) {
+  if (!c || !mc || !kv) return MS_ERR_INVALID_ARG;
+  ms_model* m = const_cast<ms_model*>(mc);
+  if (layer < 0 || layer >= m->n_layers) return fail(c, MS_ERR_INVALID_ARG, "layer %d", layer);
+  MS_TRY(check_x(c, x));
+  MS_TRY(check_rows(c, m, kv, seq, pos, M));
+  cudaStream_t s = pick(c, stream);
+  MS_TRY(upload_rows(c, m, seq, pos, M, s));
+  MS_CUDA(c, launch_rowstats(m->S[0], x, m->hidden, M, m->hidden, s, false));
+  return run_layer(c, m, kv, layer, M, x, m->S[0], m->X[1], m->S[1], s, true);
+}
+
+extern "C" ms_status ms_forward(ms_ctx* c, const ms_model* mc, float* x, ms_kv* kv,
+                                const int* seq, const int* pos, int M, void* stream) {
+  if (!c || !mc || !kv) return MS_ERR_INVALID_ARG;
+  ms_model* m = const_cast<ms_model*>(mc);
+  MS_TRY(check_x(c, x));
+  MS_TRY(check_rows(c, m, kv, seq, pos, M));
+  cudaStream_t s = pick(c, stream);
+  MS_TRY(upload_rows(c, m, seq, pos, M, s));
+  MS_CUDA(c, launch_rowstats(m->S[0], x, m->hidden, M, m->hidden, s, false));
+  for (int l = 0; l < m->n_layers; ++l)
+    MS_TRY(run_layer(c, m, kv, l, M, x, m->S[0], m->X[1], m->S[1], s, true));
+  return MS_OK;
+}
+
+static ms_status lm_head_launch(ms_ctx* c, ms_model* m, const float* x, const float* stats, int M,
+                                float* logits, int* argmax, cudaStream_t s, bool pdl) {
+  LmHeadParams p{};
+  p.x = x;
+  p.stats = stats;
+  p.nstat = m->hidden / kTileN;
+  p.gamma = m->gamma;
+  p.W = m->lm_head;
+  p.D = m->hidden;
+  p.V = m->vocab;
+  p.M = M;
+  p.logits = logits;
+  p.part_val = c->lm_val;
+  p.part_idx = c->lm_idx;
+  p.counter = c->lm_counter;
+  p.argmax = argmax;
+  const size_t ctas = (m->vocab + 511) / 512;
+  if (ctas * M > c->lm_parts) return fail(c, MS_ERR_CAPACITY, "lm_head: too many rows");
+  MS_CUDA(c, launch_lm_head(p, s, pdl));
+  return MS_OK;
+}
+
+extern "C" ms_status ms_embed(ms_ctx* c, const ms_model* mc, const int* ids, int M, float* x,
+                              void* stream) {
+  if (!c || !mc || !ids) return MS_ERR_INVALID_ARG;
+  ms_model* m = const_cast<ms_model*>(mc);
+  MS_TRY(check_x(c, x));
+  if (m->vocab <= 0) return fail(c, MS_ERR_STATE, "model has no embedding table");
+  if (M <= 0 || M > m->max_rows) return fail(c, MS_ERR_CAPACITY, "M=%d", M);
+  for (int r = 0; r < M; ++r)
+    if (ids[r] < 0 || ids[r] >= m->vocab)
+      return fail(c, MS_ERR_INVALID_ARG, "token id %d outside 0..%d", ids[r], m->vocab - 1);
+  cudaStream_t s = pick(c, stream);
+  MS_CUDA(c, cudaMemcpyAsync(m->d_ids, ids, M * sizeof(int), cudaMemcpyHostToDevice, s));
+  MS_CUDA(c, launch_embed_stats(x, m->S[0], m->lm_head, m->d_ids, M, m->hidden, m->vocab, s, false));
+  return MS_OK;
+}
+
+extern "C" ms_status ms_lm_head(ms_ctx* c, const ms_model* mc, const float* x, int M,
+                                float* logits, int* argmax_out, void* stream) {
+  if (!c || !mc) return MS_ERR_INVALID_ARG;
+  ms_model* m = const_cast<ms_model*>(mc);
+  MS_TRY(check_x(c, x));
+  if (m->vocab <= 0) return fail(c, MS_ERR_STATE, "model has no lm_head");
+  if (M <= 0 || M > m->max_rows) return fail(c, MS_ERR_CAPACITY, "M=%d", M);
+  if (logits && ((uintptr_t)logits & 15)) return fail(c, MS_ERR_ALIGN, "logits must be 16-byte aligned");
+  cudaStream_t s = pick(c, stream);
+  MS_CUDA(c, launch_rowstats(m->S[1], x, m->hidden, M, m->hidden, s, false));
+  return lm_head_launch(c, m, x, m->S[1], M, logits, argmax_out, s, true);
+}
+
+// One decode step on the device: d_ids/d_pos/d_seq -> d_next (and advance).
+static ms_status decode_body(ms_ctx* c, ms_model* m, const ms_kv* kv, int M, cudaStream_t s,
+                             bool advance) {
+  MS_CUDA(c, launch_embed_stats(m->X[0], m->S[0], m->lm_head, m->d_ids, M, m->hidden, m->vocab, s, true));
+  for (int l = 0; l < m->n_layers; ++l)
+    MS_TRY(run_layer(c, m, kv, l, M, m->X[0], m->S[0], m->X[1], m->S[1], s, true));
+  MS_TRY(lm_head_launch(c, m, m->X[0], m->S[0], M, nullptr, m->d_next, s, true));
+  if (advance)
+    MS_CUDA(c, launch_advance_step(m->d_ids, m->d_next, m->d_pos, m->d_hist, m->d_step, M, s, true));
+  return MS_OK;
+}
+
+extern "C" ms_status ms_decode_step(ms_ctx* c, const ms_model* mc, ms_kv* kv, const int* ids,
+                                    const int* seq, const int* pos, int M, int* next_ids) {
+  if (!c || !mc || !kv || !ids || !next_ids) return MS_ERR_INVALID_ARG;
+  ms_model* m = const_cast<ms_model*>(mc);
+  if (m->vocab <= 0) return fail(c, MS_ERR_STATE, "model has no lm_head");
+  MS_TRY(check_rows(c, m, kv, seq, pos, M));
+  for (int r = 0; r < M; ++r)
+    if (ids[r] < 0 || ids[r] >= m->vocab)
+      return fail(c, MS_ERR_INVALID_ARG, "token id %d outside 0..%d", ids[r], m->vocab - 1);
+  cudaStream_t s = c->stream;
+  MS_TRY(upload_rows(c, m, seq, pos, M, s));
+  MS_CUDA(c, cudaMemcpyAsync(m->d_ids, ids, M * sizeof(int), cudaMemcpyHostToDevice, s));
+  MS_TRY(decode_body(c, m, kv, M, s, false));
+  MS_CUDA(c, cudaMemcpyAsync(next_ids, m->d_next, M * sizeof(int), cudaMemcpyDeviceToHost, s));
+  MS_CUDA(c, cudaStreamSynchronize(s));
+  return MS_OK;
+}
+
+// Capture one decode step (with feedback) into a CUDA graph.
+static ms_status ensure_graph(ms_ctx* c, ms_model* m, const ms_kv* kv, int M) {
+  if (m->gexec && m->g_M == M && m->g_kv == kv) return MS_OK;
+  if (m->gexec) {
+    cudaGraphExecDestroy(m->gexec);
+    m->gexec = nullptr;
+  }
+  cudaStream_t s = c->stream;
+  cudaGraph_t g = nullptr;
+  MS_CUDA(c, cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+  ms_status st = decode_body(c, m, kv, M, s, true);
+  cudaError_t e = cudaStreamEndCapture(s, &g);
+  if (st != MS_OK) {
+    if (g) cudaGraphDestroy(g);
+    return st;
+  }
+  if (e != cudaSuccess) return fail(c, MS_ERR_CUDA, "graph capture: %s", cudaGetErrorString(e));
+  e = cudaGraphInstantiate(&m->gexec, g, 0);
+  cudaGraphDestroy(g);
+  if (e != cudaSuccess) return fail(c, MS_ERR_CUDA, "graph instantiate: %s", cudaGetErrorString(e));
+  m->g_M = M;
+  m->g_kv = kv;
+  m->g_span = m->span_hint;
+  return MS_OK;
+}
+
+extern "C" ms_status ms_generate(ms_ctx* c, const ms_model* mc, ms_kv* kv, const int* ids,
+                                 const int* seq, const int* pos, int M, int steps, int* out_ids) {
+  if (!c || !mc || !kv || !ids || !out_ids) return MS_ERR_INVALID_ARG;
+  ms_model* m = const_cast<ms_model*>(mc);
+  if (m->vocab <= 0) return fail(c, MS_ERR_STATE, "model has no lm_head");
+  if (steps <= 0) return fail(c, MS_ERR_INVALID_ARG, "steps=%d", steps);
+  MS_TRY(check_rows(c, m, kv, seq, pos, M));
+  // every position the loop will reach must fit the cache
+  std::vector<int> last(pos, pos + M);
+  for (int& p : last) p += steps - 1;
+  MS_TRY(check_rows(c, m, kv, seq, last.data(), M));
+  for (int r = 0; r < M; ++r)
+    if (ids[r] < 0 || ids[r] >= m->vocab)
+      return fail(c, MS_ERR_INVALID_ARG, "token id %d outside 0..%d", ids[r], m->vocab - 1);
+  cudaStream_t s = c->stream;
+  if (m->hist_cap < steps * M) {
+    if (m->d_hist) cudaFree(m->d_hist);
+    m->d_hist = nullptr;
+    m->hist_cap = 0;
+    MS_TRY(dev_alloc(c, (void**)&m->d_hist, (size_t)steps * M * sizeof(int)));
+    m->hist_cap = steps * M;
+    if (m->gexec) {  // the graph bakes the history pointer
+      cudaGraphExecDestroy(m->gexec);
+      m->gexec = nullptr;
+    }
+  }
+  MS_TRY(upload_rows(c, m, seq, pos, M, s));
+  set_span(m, pos, M, steps - 1);
+  if (m->gexec && m->g_span < m->span_hint) {  // re-plan splits for longer spans
+    cudaGraphExecDestroy(m->gexec);
+    m->gexec = nullptr;
+  }
+  MS_TRY(ensure_graph(c, m, kv, M));
+  MS_CUDA(c, cudaMemcpyAsync(m->d_ids, ids, M * sizeof(int), cudaMemcpyHostToDevice, s));
+  MS_CUDA(c, cudaMemsetAsync(m->d_step, 0, sizeof(int), s));
+  for (int i = 0; i < steps; ++i) MS_CUDA(c, cudaGraphLaunch(m->gexec, s));
+  MS_CUDA(c, cudaMemcpyAsync(out_ids, m->d_hist, (size_t)steps * M * sizeof(int),
+                             cudaMemcpyDeviceToHost, s));
+  MS_CUDA(c, cudaStreamSynchronize(s));
+  return MS_OK;
+}
+
+extern "C" ms_status ms_prefill(ms_ctx* c, const ms_model* mc, ms_kv* kv, const int* ids,
+                                const int* seq, const int* pos, int n_tokens, int* first_ids) {
+  if (!c || !mc || !kv || !ids || !seq || !pos) return MS_ERR_INVALID_ARG;
+  ms_model* m = const_cast<ms_model*>(mc);
+  if (m->vocab <= 0) return fail(c, MS_ERR_STATE, "model has no embedding table");
+  if (n_tokens <= 0) return fail(c, MS_ERR_INVALID_ARG, "n_tokens=%d", n_tokens);
+  cudaStream_t s = c->stream;
+  // last row of every sequence (its logits give the first generated token)
+  std::vector<int> last_row(kv->n_seq, -1);
+  for (int r = 0; r < n_tokens; ++r) {
+    if (seq[r] < 0 || seq[r] >= kv->n_seq) return fail(c, MS_ERR_INVALID_ARG, "row %d: sequence %d", r, seq[r]);
+    if (last_row[seq[r]] < 0 || pos[r] > pos[last_row[seq[r]]]) last_row[seq[r]] = r;
+  }
+  std::vector<int> keep_rows;  // rows (global index) whose hidden state feeds the lm_head
+  float* keep = nullptr;
+  int n_keep = 0;
+  for (int s2 = 0; s2 < kv->n_seq; ++s2)
+    if (last_row[s2] >= 0) ++n_keep;
+  if (n_keep > m->max_rows)
+    return fail(c, MS_ERR_CAPACITY, "prefill: %d sequences exceed max_rows %d", n_keep, m->max_rows);
+  if (first_ids && n_keep) MS_TRY(dev_alloc(c, (void**)&keep, (size_t)n_keep * m->hidden * sizeof(float)));
+  ms_status st = MS_OK;
+  int kept = 0;
+  std::vector<int> kept_seq;
+  for (int r0 = 0; r0 < n_tokens && st == MS_OK; r0 += m->max_rows) {
+    const int M = std::min(m->max_rows, n_tokens - r0);
+    st = check_rows(c, m, kv, seq + r0, pos + r0, M);
+    if (st != MS_OK) break;
+    st = ms_embed(c, m, ids + r0, M, m->X[0], s);
+    if (st != MS_OK) break;
+    st = upload_rows(c, m, seq + r0, pos + r0, M, s);
+    for (int l = 0; l < m->n_layers && st == MS_OK; ++l)
+      st = run_layer(c, m, kv, l, M, m->X[0], m->S[0], m->X[1], m->S[1], s, true);
+    if (st != MS_OK || !first_ids) continue;
+    for (int r = r0; r < r0 + M; ++r)
+      if (last_row[seq[r]] == r) {
+        cudaMemcpyAsync(keep + (size_t)kept * m->hidden, m->X[0] + (size_t)(r - r0) * m->hidden,
+                        m->hidden * sizeof(float), cudaMemcpyDeviceToDevice, s);
+        kept_seq.push_back(seq[r]);
+        ++kept;
+      }
+  }
+  if (st == MS_OK && first_ids && n_keep) {
+    MS_CUDA(c, launch_rowstats(m->S[1], keep, m->hidden, n_keep, m->hidden, s, false));
+    st = lm_head_launch(c, m, keep, m->S[1], n_keep, nullptr, m->d_next, s, true);
+    std::vector<int> nxt(n_keep);
+    if (st == MS_OK) {
+      cudaMemcpyAsync(nxt.data(), m->d_next, n_keep * sizeof(int), cudaMemcpyDeviceToHost, s);
+      if (cudaStreamSynchronize(s) != cudaSuccess) st = fail(c, MS_ERR_CUDA, "prefill sync");
+    }
+    if (st == MS_OK)
+      for (int i = 0; i < n_keep; ++i) first_ids[kept_seq[i]] = nxt[i];
+  }
+  if (keep) {
+    cudaStreamSynchronize(s);
+    cudaFree(keep);
+  }
+  if (st == MS_OK) MS_CUDA(c, cudaStreamSynchronize(s));
+  return st;
+}

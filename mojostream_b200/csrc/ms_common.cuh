@@ -1,0 +1,103 @@
+// ms_common.cuh -- device helpers shared by the sm_100a kernels.
+//
+// Numeric scheme of the Q4 projections (all of them run on tensor cores):
+//   * a weight (nibble - 8) is an integer in [-8, 7]: exact in bf16;
+//   * an fp32 activation v is split as hi = bf16(v), lo = bf16(v - hi);
+//     |v - hi - lo| <= 2^-18 |v|, so one bf16 MMA pass over [hi | lo] keeps
+//     fp32-class accuracy (the per-tensor scale is applied in fp32 after the
+//     k-sum, as the reference's dequant (nibble - 8) * scale factors out).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+namespace ms {
+
+constexpr int kWarp = 32;
+
+// ---------------------------------------------------------------- PDL --
+// Programmatic dependent launch: a kernel may start while its predecessor in
+// the stream drains.  Everything before pdl_wait() may only read data that no
+// earlier kernel writes (the weights); pdl_trigger() lets the next kernel be
+// scheduled.  Both are no-ops when the launch carries no PDL attribute.
+__device__ __forceinline__ void pdl_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// ------------------------------------------------------- global loads --
+// Weights are streamed once per step: keep them out of L1.
+__device__ __forceinline__ uint4 ld_stream_u4(const uint4* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+__device__ __forceinline__ float4 ld_stream_f4(const float4* p) {
+  float4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.f32 {%0,%1,%2,%3}, [%4];"
+               : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w)
+               : "l"(p));
+  return r;
+}
+
+// --------------------------------------------------------- bf16 packs --
+__device__ __forceinline__ uint32_t bf16_bits(__nv_bfloat16 h) {
+  return (uint32_t)__bfloat16_as_ushort(h);
+}
+// Split v into hi + lo (both bf16).
+__device__ __forceinline__ void split_bf16(float v, uint32_t& hi, uint32_t& lo) {
+  __nv_bfloat16 h = __float2bfloat16_rn(v);
+  __nv_bfloat16 l = __float2bfloat16_rn(v - __bfloat162float(h));
+  hi = bf16_bits(h);
+  lo = bf16_bits(l);
+}
+
+// Four bf16x2 A-fragment registers from one packed word of eight nibbles.
+// (0x4300 | n) is the bf16 of 128 + n; subtracting 136 gives n - 8 exactly.
+__device__ __forceinline__ void dequant_word(uint32_t q, uint32_t (&a)[4]) {
+  const uint32_t kMask = 0x000F000Fu, kMagic = 0x43004300u, kBias = 0x43084308u;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    uint32_t t = ((q >> (4 * j)) & kMask) | kMagic;
+    uint32_t r;
+    asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(t), "r"(kBias));
+    a[j] = r;
+  }
+}
+
+// D += A(16x16 bf16) * B(16x8 bf16), fp32 accumulate.
+__device__ __forceinline__ void mma_bf16_16816(float (&c)[4], const uint32_t (&a)[4],
+                                               uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Slot of absolute position p in a sequence's KV ring (circular: p % cap).
+__device__ __forceinline__ size_t kv_row_offset(const int* __restrict__ block_table,
+                                                int bt_stride, int page, int cap,
+                                                int circular, int seq, int p, int kv_dim) {
+  const int slot = circular ? (p % cap) : p;
+  const int phys = block_table[seq * bt_stride + slot / page];
+  return ((size_t)phys * (size_t)page + (size_t)(slot % page)) * (size_t)kv_dim;
+}
+
+}  // namespace ms

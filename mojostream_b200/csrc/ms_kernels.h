@@ -1,0 +1,128 @@
+// ms_kernels.h -- parameter blocks and launchers of the sm_100a kernels.
+// Internal to libmojostream_cuda.so (the public C-ABI is include/mojostream_cuda.h).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace ms {
+
+// ------------------------------------------------------------------------
+// Tiled Q4 weight layout ("fragment tiles").
+//
+// A matrix W[K][N] (reference layout: bytes [K][N/2], low nibble = even
+// column) is stored as N/16 column tiles x K/64 k-chunks x 32 lanes x uint4.
+// Word s (0..3) of lane (g = lane/4, t = lane%4) in chunk c of tile j holds the
+// eight nibbles that lane needs as the A operand (W^T, 16 x 16) of one
+// mma.m16n8k16 for k-subtile 4c+s:
+//   bits  0- 3 / 16-19 : rows g   , k 2t   / 2t+1
+//   bits  4- 7 / 20-23 : rows g+8 , k 2t   / 2t+1
+//   bits  8-11 / 24-27 : rows g   , k 2t+8 / 2t+9
+//   bits 12-15 / 28-31 : rows g+8 , k 2t+8 / 2t+9
+// Tile row r maps to a logical output column through a permutation chosen
+// at repack time, so that the two rows a thread owns (g, g+8) are the pair an
+// epilogue needs: RoPE partners (i, i + R/2), or gate/up of the same column.
+// ------------------------------------------------------------------------
+constexpr int kTileN = 16;
+constexpr int kChunkK = 64;
+
+// Epilogues of the projection kernel.
+enum Epilogue : int {
+  kEpiStore = 0,   // out = s * acc
+  kEpiAccum = 1,   // out += s * acc
+  kEpiResid = 2,   // out = ple * resid * inv_rms(resid) + s * acc ; + row stats
+  kEpiSwiGLU = 3,  // rows 0-7 gate, rows 8-15 up: h = up * g * sigmoid(g)
+  kEpiQKV = 4,     // RoPE (rows g / g+8 partners) then Q store / K,V cache write
+};
+
+// Tile descriptor of a fused Q|K|V matrix: dst 0=Q 1=K 2=V, logical column of
+// tile rows 0..7 (col_lo + g) and 8..15 (col_hi + g), RoPE frequency index of
+// row 0 (or -1).
+struct QkvTile {
+  int dst, col_lo, col_hi, rope_i0;
+};
+
+struct KvView {
+  float* k;                  // layer pool [n_pages][page][kv_dim]
+  float* v;
+  const int* block_table;    // [n_seq][bt_stride] physical page ids
+  int bt_stride, page, cap, circular, kv_dim;
+};
+
+struct GemvParams {
+  const uint4* w;    // fragment tiles
+  int n_tiles, K, kseg, ksplit, M;  // kseg: k per CTA (multiple of 64), ksplit = ceil(K / kseg)
+  // input rows x[M][K] (row stride ldx); optional RMSNorm in the prologue
+  const float* x;
+  int ldx;
+  const float* in_stats;  // [in_nstat][M] partial sums of squares, or null
+  int in_nstat;
+  float in_ple;           // x is multiplied by ple before the norm
+  int in_D;
+  // epilogue
+  int epi;
+  float* out;
+  int ldo;
+  float scale, scale2;
+  const float* resid;
+  int ldr;
+  const float* resid_stats;
+  int resid_nstat;
+  float resid_ple;
+  float* out_stats;       // [n_tiles][M]
+  // QKV epilogue
+  const QkvTile* tiles;
+  float sq, sk, sv;
+  float* q_out;
+  int ldq;
+  const float* inv_freq;  // per RoPE frequency index
+  const int* pos;
+  const int* seq;
+  KvView kv;
+  // split-K scratch
+  float* part;            // [mblocks][n_ctas][ksplit][4 tiles][16][MB]
+  int* counters;          // [mblocks][n_ctas]
+};
+
+struct AttnParams {
+  const float* q;
+  int ldq;
+  float* out;
+  int ldo;
+  KvView kv;
+  const int* seq;
+  const int* pos;
+  int hd, n_heads, n_kv, window, chunk /* minimum positions per split */, n_splits, M;
+  float scale;
+  float* part;    // [M][n_kv][n_splits][G][hd + 2]
+  int* counters;  // [M][n_kv]
+};
+
+struct LmHeadParams {
+  const float* x;         // [M][D] raw residual rows
+  const float* stats;     // [nstat][M]
+  int nstat;
+  const float* gamma;     // [D] or null
+  const float* W;         // [D][V] fp32 (reference layout)
+  int D, V, M;
+  float* logits;          // [M][V] or null
+  float* part_val;        // [M][n_ctas]
+  int* part_idx;
+  int* counter;
+  int* argmax;            // [M] or null
+};
+
+// Launchers (return cudaGetLastError of the launch).
+cudaError_t launch_gemv(const GemvParams& p, int mg, int ch, cudaStream_t s, bool pdl);
+cudaError_t launch_attention(const AttnParams& p, cudaStream_t s, bool pdl);
+cudaError_t launch_lm_head(const LmHeadParams& p, cudaStream_t s, bool pdl);
+cudaError_t launch_repack(uint4* out, const uint8_t* const* src, const int* src_n, int n_src,
+                          const int* perm, int n_tiles, int K, cudaStream_t s);
+cudaError_t launch_embed_stats(float* x, float* stats, const float* W, const int* ids, int M,
+                               int D, int V, cudaStream_t s, bool pdl);
+cudaError_t launch_rowstats(float* stats, const float* x, int ldx, int M, int D,
+                            cudaStream_t s, bool pdl);
+cudaError_t launch_advance_step(int* ids, const int* next, int* pos, int* hist, int* step, int M,
+                                cudaStream_t s, bool pdl);
+
+}  // namespace ms

@@ -1,0 +1,359 @@
+// ms_misc.cu -- lm_head, embedding gather, row statistics, weight repack and
+// the on-device greedy feedback of the decode loop.
+#include "ms_common.cuh"
+#include "ms_kernels.h"
+
+namespace ms {
+
+// =========================================================================
+// lm_head: final weighted RMSNorm + fp32 projection + greedy argmax.
+// Reference: apply_final_norm (src/inference/lm_head.mojo:119-130 ->
+// rmsnorm_weighted_inplace, src/linalg/kernels.mojo:598-613), project_lm_head
+// (lm_head.mojo:146-168 -> matmul_fp32_raw, kernels.mojo:616-671) and the
+// greedy branch of temperature_sampling (lm_head.mojo:224-230: strict '>', so
+// the first maximum wins = smallest index among equal maxima).
+//
+// W is the reference's fp32 [D][V] table.  At decode batch sizes it is the
+// largest tensor of the model and is read exactly once: each thread owns 4
+// consecutive vocab columns (one float4 per k row, coalesced along V) for all
+// rows of the pass; the normalised rows live in shared memory.  Each CTA
+// reduces its (max, index) per row; the last CTA (atomic ticket) reduces the
+// CTAs in order.
+// =========================================================================
+constexpr int kLmThreads = 128;
+constexpr int kLmCols = kLmThreads * 4;
+constexpr int kLmUnroll = 8;
+
+__device__ __forceinline__ void argmax_merge(float& v, int& i, float v2, int i2) {
+  if (v2 > v || (v2 == v && i2 < i)) {
+    v = v2;
+    i = i2;
+  }
+}
+
+template <int MR>
+__global__ void __launch_bounds__(kLmThreads) lm_head_kernel(const LmHeadParams p, int row0) {
+  extern __shared__ float xs[];  // [MR][D]
+  __shared__ float s_inv[MR];
+  __shared__ float s_rv[kLmThreads / kWarp][MR];
+  __shared__ int s_ri[kLmThreads / kWarp][MR];
+  __shared__ int s_last;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int col = blockIdx.x * kLmCols + tid * 4;
+  const bool col_ok = col + 3 < p.V;
+  const int rows = min(MR, p.M - row0);
+
+  // first k rows of W: independent of earlier kernels
+  float4 pre[kLmUnroll];
+  if (col_ok) {
+#pragma unroll
+    for (int u = 0; u < kLmUnroll; ++u)
+      if (u < p.D) pre[u] = ld_stream_f4(reinterpret_cast<const float4*>(p.W + (size_t)u * p.V + col));
+  }
+  pdl_trigger();
+  pdl_wait();
+
+  for (int r = warp; r < MR; r += kLmThreads / kWarp) {
+    float inv = 1.f;
+    if (r < rows && p.stats) {
+      float s = 0.f;
+      for (int i = lane; i < p.nstat; i += kWarp) s += p.stats[(size_t)i * p.M + row0 + r];
+      s = warp_sum(s);
+      inv = 1.0f / sqrtf(s / (float)p.D + 1e-6f);
+    }
+    if (lane == 0) s_inv[r] = inv;
+  }
+  __syncthreads();
+  for (int idx = tid; idx < MR * p.D; idx += kLmThreads) {
+    const int r = idx / p.D, k = idx % p.D;
+    float v = 0.f;
+    if (r < rows) {
+      v = p.x[(size_t)(row0 + r) * p.D + k] * s_inv[r];
+      if (p.gamma) v = v * p.gamma[k];
+    }
+    xs[idx] = v;
+  }
+  __syncthreads();
+
+  float acc[MR][4];
+#pragma unroll
+  for (int r = 0; r < MR; ++r) acc[r][0] = acc[r][1] = acc[r][2] = acc[r][3] = 0.f;
+  if (col_ok) {
+    int k0 = 0;
+    for (; k0 + kLmUnroll <= p.D; k0 += kLmUnroll) {
+      float4 w[kLmUnroll];
+#pragma unroll
+      for (int u = 0; u < kLmUnroll; ++u) w[u] = pre[u];
+      const int kn = k0 + kLmUnroll;
+#pragma unroll
+      for (int u = 0; u < kLmUnroll; ++u)
+        if (kn + u < p.D)
+          pre[u] = ld_stream_f4(reinterpret_cast<const float4*>(p.W + (size_t)(kn + u) * p.V + col));
+#pragma unroll
+      for (int u = 0; u < kLmUnroll; ++u) {
+#pragma unroll
+        for (int r = 0; r < MR; ++r) {
+          const float a = xs[r * p.D + k0 + u];
+          acc[r][0] = fmaf(a, w[u].x, acc[r][0]);
+          acc[r][1] = fmaf(a, w[u].y, acc[r][1]);
+          acc[r][2] = fmaf(a, w[u].z, acc[r][2]);
+          acc[r][3] = fmaf(a, w[u].w, acc[r][3]);
+        }
+      }
+    }
+    for (int u = 0; k0 + u < p.D; ++u) {  // D not a multiple of the unroll
+      const float4 w = pre[u];
+#pragma unroll
+      for (int r = 0; r < MR; ++r) {
+        const float a = xs[r * p.D + k0 + u];
+        acc[r][0] = fmaf(a, w.x, acc[r][0]);
+        acc[r][1] = fmaf(a, w.y, acc[r][1]);
+        acc[r][2] = fmaf(a, w.z, acc[r][2]);
+        acc[r][3] = fmaf(a, w.w, acc[r][3]);
+      }
+    }
+  }
+
+  // logits (optional) and the per-CTA argmax of every row
+#pragma unroll
+  for (int r = 0; r < MR; ++r) {
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    if (r < rows && col_ok) {
+      if (p.logits)
+        *reinterpret_cast<float4*>(p.logits + (size_t)(row0 + r) * p.V + col) =
+            make_float4(acc[r][0], acc[r][1], acc[r][2], acc[r][3]);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) argmax_merge(bv, bi, acc[r][j], col + j);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      argmax_merge(bv, bi, ov, oi);
+    }
+    if (lane == 0) {
+      s_rv[warp][r] = bv;
+      s_ri[warp][r] = bi;
+    }
+  }
+  __syncthreads();
+  if (!p.argmax) return;
+  if (tid < rows) {
+    float bv = s_rv[0][tid];
+    int bi = s_ri[0][tid];
+    for (int w = 1; w < kLmThreads / kWarp; ++w) argmax_merge(bv, bi, s_rv[w][tid], s_ri[w][tid]);
+    p.part_val[(size_t)(row0 + tid) * gridDim.x + blockIdx.x] = bv;
+    p.part_idx[(size_t)(row0 + tid) * gridDim.x + blockIdx.x] = bi;
+  }
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) s_last = (atomicAdd(p.counter, 1) == (int)gridDim.x - 1);
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  for (int r = warp; r < rows; r += kLmThreads / kWarp) {
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int c = lane; c < (int)gridDim.x; c += kWarp)
+      argmax_merge(bv, bi, __ldcg(p.part_val + (size_t)(row0 + r) * gridDim.x + c),
+                   __ldcg(p.part_idx + (size_t)(row0 + r) * gridDim.x + c));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      argmax_merge(bv, bi, ov, oi);
+    }
+    if (lane == 0) p.argmax[row0 + r] = bi;
+  }
+  if (tid == 0) *p.counter = 0;
+}
+
+cudaError_t launch_lm_head(const LmHeadParams& p, cudaStream_t s, bool pdl) {
+  constexpr int MR = 4;
+  const size_t smem = (size_t)MR * p.D * sizeof(float);
+  auto kern = lm_head_kernel<MR>;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  for (int row0 = 0; row0 < p.M; row0 += MR) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((p.V + kLmCols - 1) / kLmCols);
+    cfg.blockDim = dim3(kLmThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p, row0);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+// =========================================================================
+// Embedding gather (get_token_embedding, lm_head.mojo:171-195): x[m] = column
+// ids[m] of the tied fp32 [D][V] table.  Also writes the per-16-column sums of
+// squares that the first layer's RMSNorm prologue consumes.
+// =========================================================================
+__global__ void embed_kernel(float* x, float* stats, const float* __restrict__ W,
+                             const int* __restrict__ ids, int M, int D, int V) {
+  pdl_trigger();
+  pdl_wait();
+  const int m = blockIdx.x;
+  const int id = ids[m];
+  for (int t = threadIdx.x; t < D / kTileN; t += blockDim.x) {
+    float sq = 0.f;
+#pragma unroll
+    for (int j = 0; j < kTileN; ++j) {
+      const int d = t * kTileN + j;
+      const float v = W[(size_t)d * V + id];
+      x[(size_t)m * D + d] = v;
+      sq += v * v;
+    }
+    stats[(size_t)t * M + m] = sq;
+  }
+}
+
+// Row statistics of caller-provided rows: stats[t][m] = sum of squares of the
+// 16 columns of tile t.
+__global__ void rowstats_kernel(float* stats, const float* __restrict__ x, int ldx, int M, int D) {
+  pdl_trigger();
+  pdl_wait();
+  const int m = blockIdx.x;
+  for (int t = threadIdx.x; t < D / kTileN; t += blockDim.x) {
+    float sq = 0.f;
+#pragma unroll
+    for (int j = 0; j < kTileN; ++j) {
+      const float v = x[(size_t)m * ldx + t * kTileN + j];
+      sq += v * v;
+    }
+    stats[(size_t)t * M + m] = sq;
+  }
+}
+
+cudaError_t launch_rowstats(float* stats, const float* x, int ldx, int M, int D, cudaStream_t s,
+                            bool pdl) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(M);
+  cfg.blockDim = dim3(128);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, rowstats_kernel, stats, x, ldx, M, D);
+}
+
+// =========================================================================
+// Repack: reference Q4 bytes [K][N/2] (one or more source matrices whose
+// columns are concatenated) -> fragment tiles (layout in ms_kernels.h).
+// perm[16 j + r] = (source << 24) | column gives the logical column of tile
+// row r.  One thread per output word.
+// =========================================================================
+struct RepackSrc {
+  const uint8_t* p[3];
+  int n[3];
+};
+
+__global__ void repack_kernel(uint32_t* __restrict__ out, RepackSrc src,
+                              const int* __restrict__ perm, int n_tiles, int K) {
+  const int nchunks = K / kChunkK;
+  const size_t total = (size_t)n_tiles * nchunks * kWarp * 4;
+  for (size_t w = (size_t)blockIdx.x * blockDim.x + threadIdx.x; w < total;
+       w += (size_t)gridDim.x * blockDim.x) {
+    const int s = (int)(w & 3);
+    const int lane = (int)((w >> 2) & 31);
+    const size_t tc = w >> 7;  // tile * nchunks + chunk
+    const int c = (int)(tc % nchunks);
+    const int j = (int)(tc / nchunks);
+    const int g = lane >> 2, t = lane & 3;
+    uint32_t word = 0;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      // e -> (row, k within subtile), nibble position
+      const int jj = e & 3;              // register j of the fragment
+      const int hi = e >> 2;             // element in the upper 16 bits
+      const int row = g + ((jj & 1) ? 8 : 0);
+      const int kk = 2 * t + hi + ((jj & 2) ? 8 : 0);
+      const int k = c * kChunkK + s * 16 + kk;
+      const int pe = perm[j * kTileN + row];
+      const int si = pe >> 24, col = pe & 0xFFFFFF;
+      const uint8_t b = src.p[si][(size_t)k * (src.n[si] / 2) + (col >> 1)];
+      const uint32_t nib = (col & 1) ? (b >> 4) : (b & 15);
+      word |= nib << (4 * jj + 16 * hi);
+    }
+    out[w] = word;
+  }
+}
+
+cudaError_t launch_repack(uint4* out, const uint8_t* const* src, const int* src_n, int n_src,
+                          const int* perm, int n_tiles, int K, cudaStream_t s) {
+  RepackSrc rs = {};
+  for (int i = 0; i < n_src && i < 3; ++i) {
+    rs.p[i] = src[i];
+    rs.n[i] = src_n[i];
+  }
+  const size_t total = (size_t)n_tiles * (K / kChunkK) * kWarp * 4;
+  const int threads = 256;
+  const size_t want = (total + threads - 1) / threads;
+  const int blocks = (int)(want < 148 * 64 ? want : 148 * 64);
+  repack_kernel<<<blocks, threads, 0, s>>>(reinterpret_cast<uint32_t*>(out), rs, perm, n_tiles, K);
+  return cudaGetLastError();
+}
+
+// =========================================================================
+// Greedy feedback of the on-device decode loop: next ids become the inputs
+// of the following step, positions advance, ids are appended to a history.
+// =========================================================================
+__global__ void advance_kernel(int* ids, const int* next, int* pos, int* hist, int* step, int M) {
+  pdl_trigger();
+  pdl_wait();
+  const int m = threadIdx.x;
+  const int st = *step;
+  __syncthreads();
+  if (m < M) {
+    const int v = next[m];
+    ids[m] = v;
+    pos[m] += 1;
+    if (hist) hist[(size_t)st * M + m] = v;
+  }
+  __syncthreads();
+  if (m == 0) *step = st + 1;
+}
+
+// Launchers with the extra buffers the C-ABI layer owns.
+cudaError_t launch_embed_stats(float* x, float* stats, const float* W, const int* ids, int M,
+                               int D, int V, cudaStream_t s, bool pdl) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(M);
+  cfg.blockDim = dim3(128);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, embed_kernel, x, stats, W, ids, M, D, V);
+}
+
+cudaError_t launch_advance_step(int* ids, const int* next, int* pos, int* hist, int* step, int M,
+                                cudaStream_t s, bool pdl) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1);
+  cfg.blockDim = dim3(((M + 31) / 32) * 32);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, advance_kernel, ids, next, pos, hist, step, M);
+}
+
+}  // namespace ms

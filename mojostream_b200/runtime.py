@@ -1,0 +1,214 @@
+"""Python host of libmojostream_cuda.so: contexts, models, KV caches, calls.
+
+Device memory for activations is handled with torch tensors (plumbing only);
+every computation runs in the CUDA library through its C-ABI.
+"""
+import ctypes
+
+import numpy as np
+
+from . import _lib
+from ._lib import check, int_array, lib
+
+
+def _ptr(t):
+    """Data pointer of a torch tensor or NumPy array (kept alive by the caller)."""
+    if hasattr(t, "data_ptr"):
+        return ctypes.c_void_p(t.data_ptr())
+    return ctypes.c_void_p(t.ctypes.data)
+
+
+def _stream():
+    import torch
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+class Context:
+    """ms_ctx: one CUDA device, its stream and scratch memory."""
+
+    def __init__(self, device=0):
+        h = ctypes.c_void_p()
+        st = lib().ms_init(device, ctypes.byref(h))
+        if st != 0:
+            raise _lib.MsError(st, f"ms_init({device}) failed")
+        self.h = h
+        self.device = device
+
+    def check(self, status):
+        check(status, self.h)
+
+    def sync(self):
+        self.check(lib().ms_sync(self.h, None))
+
+    def close(self):
+        if self.h:
+            lib().ms_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class Q4Weight:
+    """ms_q4_weight: one Q4 matrix repacked for the tensor-core projection."""
+
+    def __init__(self, ctx, w_rx, K, N, scale):
+        self.ctx, self.K, self.N = ctx, K, N
+        h = ctypes.c_void_p()
+        ctx.check(lib().ms_q4_weight_create(ctx.h, _ptr(w_rx), K, N, float(scale),
+                                            ctypes.byref(h)))
+        self.h = h
+
+    def gemm(self, A, C, accumulate=False):
+        M = A.shape[0]
+        self.ctx.check(lib().ms_q4_gemm(self.ctx.h, self.h, _ptr(C), _ptr(A), M,
+                                        1 if accumulate else 0, _stream()))
+        return C
+
+    def close(self):
+        if self.h:
+            lib().ms_q4_weight_destroy(self.ctx.h, self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class Model:
+    """ms_model built from a ModelSpec and ModelWeights (NumPy or torch)."""
+
+    def __init__(self, ctx, spec, weights, max_rows=4):
+        self.ctx, self.spec, self.max_rows = ctx, spec, max_rows
+        n = spec.n_layers
+        descs = (_lib.LayerDesc * n)()
+        keep = []
+        for i, (ls, lw) in enumerate(zip(spec.layers, weights.layers)):
+            d = descs[i]
+            d.head_dim, d.n_heads, d.n_kv_heads = ls.head_dim, ls.n_heads, ls.n_kv_heads
+            d.window, d.rotary_dims, d.ffn_dim = ls.window, ls.rotary_dims, ls.ffn_dim
+            d.rope_theta, d.ple = ls.rope_theta, lw.ple
+            for m in range(7):
+                arr = lw.mats[m]
+                if isinstance(arr, np.ndarray):
+                    arr = np.ascontiguousarray(arr, dtype=np.uint8)
+                else:
+                    arr = arr.contiguous()
+                keep.append(arr)
+                d.w[m] = _ptr(arr).value
+                d.scale[m] = lw.scales[m]
+        md = _lib.ModelDesc()
+        md.hidden, md.n_layers = spec.hidden, n
+        md.layers = descs
+        md.vocab = spec.vocab
+        md.max_rows = max_rows
+        if spec.vocab:
+            lm = weights.lm_head
+            lm = np.ascontiguousarray(lm, np.float32) if isinstance(lm, np.ndarray) else lm.contiguous()
+            g = weights.final_gamma
+            if g is not None:
+                g = np.ascontiguousarray(g, np.float32) if isinstance(g, np.ndarray) else g.contiguous()
+            keep += [lm, g]
+            md.lm_head = _ptr(lm).value
+            md.final_gamma = _ptr(g).value if g is not None else None
+        h = ctypes.c_void_p()
+        ctx.check(lib().ms_model_create(ctx.h, ctypes.byref(md), ctypes.byref(h)))
+        self.h = h
+
+    @property
+    def weight_bytes(self):
+        return lib().ms_model_weight_bytes(self.h)
+
+    def close(self):
+        if self.h:
+            lib().ms_model_destroy(self.ctx.h, self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # ---- calls -------------------------------------------------------------
+    def layer_forward(self, layer, x, kv, seq, pos):
+        """x: CUDA float32 tensor [M][hidden], updated in place."""
+        M = x.shape[0]
+        self.ctx.check(lib().ms_layer_forward(self.ctx.h, self.h, layer, _ptr(x), kv.h,
+                                              int_array(seq), int_array(pos), M, _stream()))
+        return x
+
+    def forward(self, x, kv, seq, pos):
+        M = x.shape[0]
+        self.ctx.check(lib().ms_forward(self.ctx.h, self.h, _ptr(x), kv.h, int_array(seq),
+                                        int_array(pos), M, _stream()))
+        return x
+
+    def embed(self, ids):
+        import torch
+        x = torch.empty((len(ids), self.spec.hidden), dtype=torch.float32, device="cuda")
+        self.ctx.check(lib().ms_embed(self.ctx.h, self.h, int_array(ids), len(ids), _ptr(x),
+                                      _stream()))
+        return x
+
+    def lm_head(self, x, logits=True):
+        import torch
+        M = x.shape[0]
+        lg = torch.empty((M, self.spec.vocab), dtype=torch.float32, device="cuda") if logits else None
+        am = torch.empty(M, dtype=torch.int32, device="cuda")
+        self.ctx.check(lib().ms_lm_head(self.ctx.h, self.h, _ptr(x), M,
+                                        _ptr(lg) if lg is not None else None, _ptr(am), _stream()))
+        return lg, am
+
+    def decode_step(self, kv, ids, seq, pos):
+        M = len(ids)
+        out = (ctypes.c_int * M)()
+        self.ctx.check(lib().ms_decode_step(self.ctx.h, self.h, kv.h, int_array(ids),
+                                            int_array(seq), int_array(pos), M, out))
+        return list(out)
+
+    def generate(self, kv, ids, seq, pos, steps):
+        M = len(ids)
+        out = (ctypes.c_int * (M * steps))()
+        self.ctx.check(lib().ms_generate(self.ctx.h, self.h, kv.h, int_array(ids),
+                                         int_array(seq), int_array(pos), M, steps, out))
+        return np.array(list(out), dtype=np.int64).reshape(steps, M)
+
+    def prefill(self, kv, ids, seq, pos):
+        first = (ctypes.c_int * kv.n_seq)(*([-1] * kv.n_seq))
+        self.ctx.check(lib().ms_prefill(self.ctx.h, self.h, kv.h, int_array(ids),
+                                        int_array(seq), int_array(pos), len(ids), first))
+        return list(first)
+
+
+class KVCache:
+    """ms_kv: paged cache for n_seq sequences."""
+
+    def __init__(self, ctx, model, n_seq, max_pos, slide_cap=0):
+        self.ctx, self.n_seq, self.max_pos = ctx, n_seq, max_pos
+        h = ctypes.c_void_p()
+        ctx.check(lib().ms_kv_create(ctx.h, model.h, n_seq, max_pos, slide_cap, ctypes.byref(h)))
+        self.h = h
+
+    @property
+    def nbytes(self):
+        return lib().ms_kv_bytes(self.h)
+
+    def reset(self):
+        self.ctx.check(lib().ms_kv_reset(self.ctx.h, self.h))
+
+    def close(self):
+        if self.h:
+            lib().ms_kv_destroy(self.ctx.h, self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
