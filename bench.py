@@ -1,0 +1,371 @@
+#!/usr/bin/env python3
+"""Benchmark of the Gemma-4 token loop on B200 (one JSON line on rank 0).
+
+Workload (default): Gemma-4-E4B-shaped random Q4 model
+(D 2560, 42 layers = 35 sliding (hd 256, window 512) + 7 full (hd 512, 128
+rotary dims, theta 1e6), 8 q / 2 KV heads, FFN 10240, fp32 lm_head over a
+262144 vocab), 4 independent sequences, 512-token seeded prompts (TTFT), then
+greedy decode at batch 4.  A step = one decode step of the 4 sequences
+(4 tokens).  Weights (4.66 GB) and KV are far larger than L2 (126 MB), so no L2
+flush is needed between steps.
+
+value : decode tokens/s, device-resident loop (CUDA-graph replays on the
+        library stream, CUDA events), max over ranks
+e2e   : the same through ms_decode_step with host buffers (per step: ids / seq /
+        pos host->device from pinned memory, next ids device->host)
+--gpus N: N independent replicas (one process per GPU, no collective on the
+        data path: the sequences are independent), weak scaling.
+--impl reference: the reference's CPU algorithm (the C port in oracle/, since
+        the Mojo reference cannot be built here) on the host cores.
+"""
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+PROMPT = 512
+BATCH = 4
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--layers", type=int, default=42, help="(debug) fewer layers")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def dist_setup(args):
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+# ------------------------------------------------------------------ clocks --
+class ClockSampler:
+    """nvidia-smi samples (200 ms) of SM clock and throttle reasons."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu):
+        self.gpu, self.rows, self.proc = gpu, [], None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([x.strip() for x in line.split(",")])
+
+    def stop(self):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+        out = {"sm_mhz": None, "sm_max_mhz": None, "reasons": []}
+        rows = [r for r in self.rows if len(r) >= 9]
+        if not rows:
+            return out
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        out["sm_mhz"] = float(np.median(sm)) if sm else None
+        out["sm_max_mhz"] = float(rows[0][2]) if rows[0][2].replace(".", "").isdigit() else None
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = set()
+        for r in rows:
+            for i, n in enumerate(names):
+                if r[5 + i].lower().startswith("active"):
+                    reasons.add(n)
+        out["reasons"] = sorted(reasons)
+        out["samples"] = len(rows)
+        return out
+
+
+# --------------------------------------------------------------- helpers --
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+def profile_traffic(kernel):
+    """DRAM bytes per launch of `kernel` from the committed ncu summary, if any."""
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d.get(kernel)
+    return None
+
+
+def prompts(seed=7):
+    rng = np.random.default_rng(seed)
+    return rng.integers(0, 262144, size=(BATCH, PROMPT)).tolist()
+
+
+# ---------------------------------------------------------------- our arm --
+def run_ours(args, ws, rank, local):
+    import torch
+    import torch.distributed as dist
+
+    from mojostream_b200.model import e4b_spec, synth_weights_device
+    from mojostream_b200.runtime import Context, KVCache, Model
+
+    torch.cuda.set_device(local)
+    if ws > 1:
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local),
+                                timeout=__import__("datetime").timedelta(seconds=600))
+    spec = e4b_spec(n_layers=args.layers)
+    w = synth_weights_device(spec, seed=1234)
+    ctx = Context(local)
+    model = Model(ctx, spec, w, max_rows=BATCH * PROMPT)
+    del w
+    torch.cuda.empty_cache()
+    max_pos = ((PROMPT + args.warmup + 2 * args.steps + 8 + 63) // 64) * 64
+    kv = KVCache(ctx, model, BATCH, max_pos, slide_cap=1024)
+    lib_stream = torch.cuda.ExternalStream(ctx.stream_ptr)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if ws > 1:
+            dist.barrier()
+
+    def max_over_ranks(v):
+        if ws == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- TTFT: 4 x 512-token prefill + first token -------------------------
+    P = prompts()
+    ids = sum(P, [])
+    seq = sum([[s] * PROMPT for s in range(BATCH)], [])
+    pos = sum([list(range(PROMPT)) for _ in range(BATCH)], [])
+    model.prefill(kv, ids, seq, pos)  # warm (kernel attributes, allocations)
+    kv.reset()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(lib_stream)
+    first = model.prefill(kv, ids, seq, pos)
+    e1.record(lib_stream)
+    e1.synchronize()
+    ttft_ms = max_over_ranks(e0.elapsed_time(e1))
+
+    # ---- decode: warm-up then the timed device-resident loop ---------------
+    seqs = list(range(BATCH))
+    p0 = [PROMPT] * BATCH
+    gen = model.generate(kv, first, seqs, p0, args.warmup)
+    cur = [int(t) for t in gen[-1]]
+    p1 = [PROMPT + args.warmup] * BATCH
+    barrier()
+    clocks = ClockSampler(local)
+    clocks.start()
+    gen2, dev_ms = model.generate(kv, cur, seqs, p1, args.steps, timing=True)
+    barrier()
+    dev_ms = max_over_ranks(dev_ms)
+    # ---- e2e through host buffers, one ms_decode_step per step -------------
+    cur = [int(t) for t in gen2[-1]]
+    p2 = [PROMPT + args.warmup + args.steps] * BATCH
+    barrier()
+    e0.record(lib_stream)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        cur = model.decode_step(kv, cur, seqs, [p + i for p in p2])
+    e1.record(lib_stream)
+    e1.synchronize()
+    wall_e2e = time.perf_counter() - t0
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1))
+    barrier()
+    clk = clocks.stop()
+
+    # ---- dominant kernels timed alone (CUDA events on their stream) --------
+    hbm, tf, peak_kind = measured_peaks()
+    x = torch.randn((BATCH, spec.hidden), device="cuda")
+    for _ in range(3):
+        model.lm_head(x, logits=False)
+    torch.cuda.synchronize()
+    n_rep = 10
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s0.record()
+    for _ in range(n_rep):
+        model.lm_head(x, logits=False)
+    s1.record()
+    s1.synchronize()
+    lm_ms = s0.elapsed_time(s1) / n_rep
+    lm_bytes = 4 * spec.hidden * spec.vocab + 4 * BATCH * spec.hidden
+
+    q4 = spec.q4_bytes()
+    kv_read = BATCH * spec.kv_bytes_per_seq(PROMPT + args.warmup + args.steps // 2)
+    step_bytes = q4 + spec.lm_head_bytes() + kv_read
+    step_ms = dev_ms / args.steps
+    tokens = BATCH * args.steps * ws
+    value = tokens / (dev_ms / 1000.0)
+    e2e_val = tokens / (e2e_ms / 1000.0)
+    launches_per_step = 1 + 5 * spec.n_layers + (BATCH + 3) // 4 + 1
+
+    result = {
+        "metric": "decode tokens/s (batch 4), Gemma-4-E4B-shaped Q4 model",
+        "value": round(value, 2),
+        "unit": "tokens/s",
+        "n_gpus": ws,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(step_ms, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "int4 weights x fp32 activations (bf16x2 split on tensor cores), fp32 lm_head",
+        "data": "synthetic (seeded random Q4 weights, N(0,0.02) fp32 lm_head, seeded token ids)",
+        "config": {
+            "workload": "gemma4-e4b decode, batch 4 independent sequences, 512-token prompts",
+            "layers": spec.n_layers, "hidden": spec.hidden, "vocab": spec.vocab,
+            "batch": BATCH, "prompt": PROMPT, "positions": [PROMPT + args.warmup,
+                                                            PROMPT + args.warmup + args.steps],
+            "parallelism": f"replicas x{ws}" if ws > 1 else "single GPU",
+            "l2": "weights + lm_head 4.66 GB >> 126 MB L2 (no flush needed)",
+        },
+        "ttft_ms": round(ttft_ms, 3),
+        "e2e": {"value": round(e2e_val, 2), "unit": "tokens/s",
+                "h2d_bytes_per_step": 3 * 4 * BATCH, "d2h_bytes_per_step": 4 * BATCH,
+                "wall_s": round(wall_e2e, 4)},
+        "gpu_launches": launches_per_step * args.steps,
+        "roofline": {
+            "kernel": "lm_head_kernel (fp32 [2560 x 262144], argmax fused)",
+            "bound": "hbm", "achieved": round(lm_bytes / (lm_ms / 1e3) / 1e9, 1),
+            "peak": hbm, "unit": "GB/s",
+            "frac": round(lm_bytes / (lm_ms / 1e3) / 1e9 / hbm, 4),
+            "traffic": profile_traffic("lm_head_kernel"),
+            "peak_source": peak_kind,
+            "launch_ms": round(lm_ms, 4),
+        },
+        "step_roofline": {
+            "bytes_per_step": step_bytes, "achieved_gbs": round(step_bytes / (step_ms / 1e3) / 1e9, 1),
+            "peak": hbm, "frac": round(step_bytes / (step_ms / 1e3) / 1e9 / hbm, 4),
+            "note": "Q4 weights + fp32 lm_head + KV read per decode step / step time",
+        },
+        "clocks": clk,
+        "first_ids": first[:BATCH],
+    }
+    if rank == 0 and not args.no_cpu_baseline:
+        result["cpu_baseline"] = cpu_baseline(spec, model, ctx)
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+    if ws > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+# ---------------------------------------------------------- CPU baseline --
+def oracle_e4b(spec, weights_np, positions, seed=5):
+    """Oracle model with KV caches filled with seeded values for positions
+    below `positions` (the sample times decode steps, not the prefill)."""
+    from oracle import oracle
+    om = oracle.OracleModel(spec, weights_np, BATCH, positions + 256, slide_cap=1024)
+    rng = np.random.default_rng(seed)
+    for li in range(spec.n_layers):
+        k, v = om.kv_arrays(li)
+        n = min(positions, k.shape[1])
+        k[:, :n] = rng.standard_normal((BATCH, n, k.shape[2]), dtype=np.float32)
+        v[:, :n] = rng.standard_normal((BATCH, n, k.shape[2]), dtype=np.float32)
+    return om
+
+
+def host_weights(spec, w_dev):
+    from mojostream_b200.model import LayerWeights, ModelWeights
+    layers = [LayerWeights(l.ple, l.scales, [m.cpu().numpy() for m in l.mats]) for l in w_dev.layers]
+    return ModelWeights(layers, w_dev.lm_head.cpu().numpy(), w_dev.final_gamma.cpu().numpy())
+
+
+def time_oracle_steps(om, n_steps, start_pos, budget_s=None):
+    rng = np.random.default_rng(1)
+    ids = rng.integers(0, 262144, size=BATCH).tolist()
+    t0 = time.perf_counter()
+    done = 0
+    for i in range(n_steps):
+        x = om.embed(ids)
+        x = om.forward(x, list(range(BATCH)), [start_pos + i] * BATCH)
+        ids = om.argmax(om.lm_head(x))
+        done += 1
+        if budget_s and time.perf_counter() - t0 > budget_s:
+            break
+    return done, time.perf_counter() - t0
+
+
+def cpu_baseline(spec, model, ctx, budget_s=20.0):
+    import torch
+    from mojostream_b200.model import synth_weights_device
+    w = synth_weights_device(spec, seed=1234)
+    wn = host_weights(spec, w)
+    del w
+    torch.cuda.empty_cache()
+    om = oracle_e4b(spec, wn, PROMPT)
+    done, dt = time_oracle_steps(om, 1000, PROMPT, budget_s=budget_s)
+    return {"value": round(BATCH * done / dt, 3), "unit": "tokens/s", "cores": 1,
+            "kind": "port",
+            "sample": f"{done} decode steps x {BATCH} sequences at positions {PROMPT}+ "
+                      f"(KV pre-filled with seeded values), {dt:.1f} s; the reference's "
+                      "algorithm threads over 64-row blocks, so batch 4 runs on 1 thread"}
+
+
+def run_reference(args, ws, rank, local):
+    """The reference's CPU path (C port) on the host cores, rank 0 only."""
+    if rank != 0:
+        return
+    from mojostream_b200.model import e4b_spec, synth_weights
+    spec = e4b_spec(n_layers=args.layers)
+    wn = synth_weights(spec, seed=1234)
+    om = oracle_e4b(spec, wn, PROMPT)
+    time_oracle_steps(om, args.warmup, PROMPT)
+    done, dt = time_oracle_steps(om, args.steps, PROMPT + args.warmup)
+    v = BATCH * done / dt
+    print(json.dumps({
+        "impl": "reference",
+        "metric": "decode tokens/s (batch 4), Gemma-4-E4B-shaped Q4 model",
+        "value": round(v, 3), "unit": "tokens/s", "n_gpus": ws, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(1e3 * dt / done, 2),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "fp32", "data": "synthetic (seeded)",
+        "config": {"workload": "gemma4-e4b decode, batch 4 independent sequences, 512-token prompts",
+                   "layers": spec.n_layers, "batch": BATCH},
+        "cpu_baseline": {"value": round(v, 3), "unit": "tokens/s", "cores": 1, "kind": "port",
+                         "sample": f"{done} decode steps x {BATCH} sequences (KV pre-filled)"},
+        "e2e": {"value": round(v, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main():
+    args = parse()
+    ws, rank, local = dist_setup(args)
+    if args.impl == "reference":
+        run_reference(args, ws, rank, local)
+    else:
+        run_ours(args, ws, rank, local)
+
+
+if __name__ == "__main__":
+    main()

@@ -178,11 +178,19 @@ MS_API ms_status ms_lm_head(ms_ctx *ctx, const ms_model *model, const float *x, 
 MS_API ms_status ms_decode_step(ms_ctx *ctx, const ms_model *model, ms_kv *kv, const int *ids,
                          const int *seq_ids, const int *pos, int M, int *next_ids);
 
-/* `steps` greedy decode steps entirely on the device, replayed from a CUDA
- * graph: ids (host, M) are the first inputs, pos (host, M) their positions;
- * token t of step s is written to out_ids[s * M + t] (host).  Synchronous. */
+/* `steps` greedy decode steps entirely on the device, each a replay of the
+ * captured decode-step graph followed by the on-device feedback (next ids
+ * become inputs, positions advance): ids (host, M) are the first inputs, pos
+ * (host, M) their positions; token t of step s is written to
+ * out_ids[s * M + t] (host).  device_ms (nullable) receives the device time of
+ * the replays (CUDA events on the context stream).  Synchronous. */
 MS_API ms_status ms_generate(ms_ctx *ctx, const ms_model *model, ms_kv *kv, const int *ids,
-                      const int *seq_ids, const int *pos, int M, int steps, int *out_ids);
+                             const int *seq_ids, const int *pos, int M, int steps, int *out_ids,
+                             float *device_ms);
+
+/* The context's CUDA stream (a cudaStream_t), for callers that order their
+ * own work or timing events with the library's. */
+MS_API void *ms_ctx_stream(ms_ctx *ctx);
 
 /* Prefill (the TTFT pass): n_tokens rows (host arrays ids / seq_ids / pos,
  * any mix of sequences) run through all layers in chunks of at most max_rows

@@ -69,7 +69,8 @@ SIGNATURES = {
     "ms_lm_head": (ctypes.c_int, [_vp, _vp, _vp, ctypes.c_int, _vp, _vp, _vp]),
     "ms_decode_step": (ctypes.c_int, [_vp, _vp, _vp, _ip, _ip, _ip, ctypes.c_int, _ip]),
     "ms_generate": (ctypes.c_int, [_vp, _vp, _vp, _ip, _ip, _ip, ctypes.c_int, ctypes.c_int,
-                                   _ip]),
+                                   _ip, _fp]),
+    "ms_ctx_stream": (_vp, [_vp]),
     "ms_prefill": (ctypes.c_int, [_vp, _vp, _vp, _ip, _ip, _ip, ctypes.c_int, _ip]),
 }
 

@@ -45,6 +45,7 @@ struct ms_ctx {
   int* lm_idx = nullptr;
   int* lm_counter = nullptr;
   size_t lm_parts = 0;
+  cudaEvent_t ev[2] = {nullptr, nullptr};
 };
 
 struct LayerDev {
@@ -66,7 +67,6 @@ struct ms_model {
   float* gamma = nullptr;
   size_t weight_bytes = 0;
   int max_q = 0, max_f = 0;
-  int span_hint = 1;  // longest attended span of the call being launched
   // run buffers (max_rows rows)
   float* X[2] = {nullptr, nullptr};
   float* S[2] = {nullptr, nullptr};
@@ -80,10 +80,10 @@ struct ms_model {
   int* d_step = nullptr;
   int* d_hist = nullptr;
   int hist_cap = 0;
+  int* h_stage = nullptr;  // pinned: ids | seq | pos | next, max_rows each
   // captured decode step
   cudaGraphExec_t gexec = nullptr;
   int g_M = 0;
-  int g_span = 0;
   const ms_kv* g_kv = nullptr;
   std::vector<void*> allocs;
 };
@@ -215,6 +215,8 @@ extern "C" ms_status ms_init(int device, ms_ctx** out) {
   }
   cudaMemset(c->counters, 0, c->n_counters * sizeof(int));
   cudaMemset(c->lm_counter, 0, 64 * sizeof(int));
+  cudaEventCreate(&c->ev[0]);
+  cudaEventCreate(&c->ev[1]);
   if (cudaDeviceSynchronize() != cudaSuccess) {
     ms_destroy(c);
     return MS_ERR_CUDA;
@@ -232,6 +234,8 @@ extern "C" ms_status ms_destroy(ms_ctx* c) {
   cudaFree(c->lm_val);
   cudaFree(c->lm_idx);
   cudaFree(c->lm_counter);
+  if (c->ev[0]) cudaEventDestroy(c->ev[0]);
+  if (c->ev[1]) cudaEventDestroy(c->ev[1]);
   if (c->stream) cudaStreamDestroy(c->stream);
   delete c;
   return MS_OK;
@@ -575,6 +579,8 @@ extern "C" ms_status ms_model_create(ms_ctx* c, const ms_model_desc* desc, ms_mo
   if (st == MS_OK) st = model_alloc(m, &m->d_ids, R);
   if (st == MS_OK) st = model_alloc(m, &m->d_next, R);
   if (st == MS_OK) st = model_alloc(m, &m->d_step, 1);
+  if (st == MS_OK && cudaMallocHost((void**)&m->h_stage, 4 * (size_t)R * sizeof(int)) != cudaSuccess)
+    st = fail(c, MS_ERR_OOM, "pinned staging");
   if (st != MS_OK) return bail(st);
   if (cudaDeviceSynchronize() != cudaSuccess) return bail(fail(c, MS_ERR_CUDA, "model upload"));
   *out = m;
@@ -588,6 +594,7 @@ extern "C" ms_status ms_model_destroy(ms_ctx* c, ms_model* m) {
   if (m->gexec) cudaGraphExecDestroy(m->gexec);
   for (void* p : m->allocs) cudaFree(p);
   if (m->d_hist) cudaFree(m->d_hist);
+  if (m->h_stage) cudaFreeHost(m->h_stage);
   delete m;
   return MS_OK;
 }
@@ -719,15 +726,8 @@ static ms_status check_rows(ms_ctx* c, const ms_model* m, const ms_kv* kv, const
   return MS_OK;
 }
 
-static void set_span(ms_model* m, const int* pos, int M, int extra) {
-  int mx = 0;
-  for (int r = 0; r < M; ++r) mx = std::max(mx, pos[r] + 1 + extra);
-  m->span_hint = std::max(1, mx);
-}
-
 static ms_status upload_rows(ms_ctx* c, ms_model* m, const int* seq, const int* pos, int M,
                              cudaStream_t s) {
-  set_span(m, pos, M, 0);
   MS_CUDA(c, cudaMemcpyAsync(m->d_seq, seq, M * sizeof(int), cudaMemcpyHostToDevice, s));
   MS_CUDA(c, cudaMemcpyAsync(m->d_pos, pos, M * sizeof(int), cudaMemcpyHostToDevice, s));
   return MS_OK;
@@ -794,9 +794,11 @@ static ms_status run_layer(ms_ctx* c, ms_model* m, const ms_kv* kv, int li, int 
     a.window = L.d.window;
     a.M = M;
     a.scale = 1.0f / sqrtf((float)L.d.head_dim);
-    // splits: enough CTAs to fill the GPU at the longest span of this call;
-    // the kernel sizes each row's chunks itself, so any position is covered
-    const int span = L.d.window > 0 ? std::min(L.d.window, m->span_hint) : m->span_hint;
+    // splits: enough CTAs to fill the GPU at the longest span the cache can
+    // hold; the kernel sizes each row's chunks itself (short rows leave splits
+    // idle), so one launch shape -- and one captured graph -- serves every
+    // position
+    const int span = L.d.window > 0 ? std::min(L.d.window, kv->max_pos) : kv->max_pos;
     const long ctas_per_split = (long)M * L.d.n_kv_heads;
     const int min_chunk = 32;
     int splits = (int)std::max<long>(1, (2L * c->sm_count + ctas_per_split - 1) / ctas_per_split);
@@ -959,37 +961,18 @@ extern "C" ms_status ms_lm_head(ms_ctx* c, const ms_model* mc, const float* x, i
   return lm_head_launch(c, m, x, m->S[1], M, logits, argmax_out, s, true);
 }
 
-// One decode step on the device: d_ids/d_pos/d_seq -> d_next (and advance).
-static ms_status decode_body(ms_ctx* c, ms_model* m, const ms_kv* kv, int M, cudaStream_t s,
-                             bool advance) {
+// One decode step on the device: d_ids / d_seq / d_pos -> d_next.
+static ms_status decode_body(ms_ctx* c, ms_model* m, const ms_kv* kv, int M, cudaStream_t s) {
   MS_CUDA(c, launch_embed_stats(m->X[0], m->S[0], m->lm_head, m->d_ids, M, m->hidden, m->vocab, s, true));
   for (int l = 0; l < m->n_layers; ++l)
     MS_TRY(run_layer(c, m, kv, l, M, m->X[0], m->S[0], m->X[1], m->S[1], s, true));
   MS_TRY(lm_head_launch(c, m, m->X[0], m->S[0], M, nullptr, m->d_next, s, true));
-  if (advance)
-    MS_CUDA(c, launch_advance_step(m->d_ids, m->d_next, m->d_pos, m->d_hist, m->d_step, M, s, true));
   return MS_OK;
 }
 
-extern "C" ms_status ms_decode_step(ms_ctx* c, const ms_model* mc, ms_kv* kv, const int* ids,
-                                    const int* seq, const int* pos, int M, int* next_ids) {
-  if (!c || !mc || !kv || !ids || !next_ids) return MS_ERR_INVALID_ARG;
-  ms_model* m = const_cast<ms_model*>(mc);
-  if (m->vocab <= 0) return fail(c, MS_ERR_STATE, "model has no lm_head");
-  MS_TRY(check_rows(c, m, kv, seq, pos, M));
-  for (int r = 0; r < M; ++r)
-    if (ids[r] < 0 || ids[r] >= m->vocab)
-      return fail(c, MS_ERR_INVALID_ARG, "token id %d outside 0..%d", ids[r], m->vocab - 1);
-  cudaStream_t s = c->stream;
-  MS_TRY(upload_rows(c, m, seq, pos, M, s));
-  MS_CUDA(c, cudaMemcpyAsync(m->d_ids, ids, M * sizeof(int), cudaMemcpyHostToDevice, s));
-  MS_TRY(decode_body(c, m, kv, M, s, false));
-  MS_CUDA(c, cudaMemcpyAsync(next_ids, m->d_next, M * sizeof(int), cudaMemcpyDeviceToHost, s));
-  MS_CUDA(c, cudaStreamSynchronize(s));
-  return MS_OK;
-}
-
-// Capture one decode step (with feedback) into a CUDA graph.
+// The decode step captured as a CUDA graph.  No launch shape depends on the
+// positions (they are read from d_pos on the device), so one graph serves a
+// whole generation.
 static ms_status ensure_graph(ms_ctx* c, ms_model* m, const ms_kv* kv, int M) {
   if (m->gexec && m->g_M == M && m->g_kv == kv) return MS_OK;
   if (m->gexec) {
@@ -999,7 +982,7 @@ static ms_status ensure_graph(ms_ctx* c, ms_model* m, const ms_kv* kv, int M) {
   cudaStream_t s = c->stream;
   cudaGraph_t g = nullptr;
   MS_CUDA(c, cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
-  ms_status st = decode_body(c, m, kv, M, s, true);
+  ms_status st = decode_body(c, m, kv, M, s);
   cudaError_t e = cudaStreamEndCapture(s, &g);
   if (st != MS_OK) {
     if (g) cudaGraphDestroy(g);
@@ -1011,51 +994,80 @@ static ms_status ensure_graph(ms_ctx* c, ms_model* m, const ms_kv* kv, int M) {
   if (e != cudaSuccess) return fail(c, MS_ERR_CUDA, "graph instantiate: %s", cudaGetErrorString(e));
   m->g_M = M;
   m->g_kv = kv;
-  m->g_span = m->span_hint;
+  return MS_OK;
+}
+
+// Validate a decode call and stage its rows (ids / seq / pos) through pinned
+// host memory into the device row buffers.
+static ms_status stage_rows(ms_ctx* c, ms_model* m, const ms_kv* kv, const int* ids,
+                            const int* seq, const int* pos, int M, int steps, cudaStream_t s) {
+  if (m->vocab <= 0) return fail(c, MS_ERR_STATE, "model has no lm_head");
+  MS_TRY(check_rows(c, m, kv, seq, pos, M));
+  if (steps > 1) {  // every position the loop reaches must fit the cache
+    std::vector<int> last(pos, pos + M);
+    for (int& p : last) p += steps - 1;
+    MS_TRY(check_rows(c, m, kv, seq, last.data(), M));
+  }
+  for (int r = 0; r < M; ++r)
+    if (ids[r] < 0 || ids[r] >= m->vocab)
+      return fail(c, MS_ERR_INVALID_ARG, "token id %d outside 0..%d", ids[r], m->vocab - 1);
+  int* h = m->h_stage;
+  memcpy(h, ids, M * sizeof(int));
+  memcpy(h + m->max_rows, seq, M * sizeof(int));
+  memcpy(h + 2 * m->max_rows, pos, M * sizeof(int));
+  MS_CUDA(c, cudaMemcpyAsync(m->d_ids, h, M * sizeof(int), cudaMemcpyHostToDevice, s));
+  MS_CUDA(c, cudaMemcpyAsync(m->d_seq, h + m->max_rows, M * sizeof(int), cudaMemcpyHostToDevice, s));
+  MS_CUDA(c, cudaMemcpyAsync(m->d_pos, h + 2 * m->max_rows, M * sizeof(int), cudaMemcpyHostToDevice, s));
+  return MS_OK;
+}
+
+extern "C" ms_status ms_decode_step(ms_ctx* c, const ms_model* mc, ms_kv* kv, const int* ids,
+                                    const int* seq, const int* pos, int M, int* next_ids) {
+  if (!c || !mc || !kv || !ids || !next_ids) return MS_ERR_INVALID_ARG;
+  ms_model* m = const_cast<ms_model*>(mc);
+  cudaStream_t s = c->stream;
+  MS_TRY(stage_rows(c, m, kv, ids, seq, pos, M, 1, s));
+  MS_TRY(ensure_graph(c, m, kv, M));
+  MS_CUDA(c, cudaGraphLaunch(m->gexec, s));
+  MS_CUDA(c, cudaMemcpyAsync(m->h_stage + 3 * m->max_rows, m->d_next, M * sizeof(int),
+                             cudaMemcpyDeviceToHost, s));
+  MS_CUDA(c, cudaStreamSynchronize(s));
+  memcpy(next_ids, m->h_stage + 3 * m->max_rows, M * sizeof(int));
   return MS_OK;
 }
 
 extern "C" ms_status ms_generate(ms_ctx* c, const ms_model* mc, ms_kv* kv, const int* ids,
-                                 const int* seq, const int* pos, int M, int steps, int* out_ids) {
+                                 const int* seq, const int* pos, int M, int steps, int* out_ids,
+                                 float* device_ms) {
   if (!c || !mc || !kv || !ids || !out_ids) return MS_ERR_INVALID_ARG;
   ms_model* m = const_cast<ms_model*>(mc);
-  if (m->vocab <= 0) return fail(c, MS_ERR_STATE, "model has no lm_head");
   if (steps <= 0) return fail(c, MS_ERR_INVALID_ARG, "steps=%d", steps);
-  MS_TRY(check_rows(c, m, kv, seq, pos, M));
-  // every position the loop will reach must fit the cache
-  std::vector<int> last(pos, pos + M);
-  for (int& p : last) p += steps - 1;
-  MS_TRY(check_rows(c, m, kv, seq, last.data(), M));
-  for (int r = 0; r < M; ++r)
-    if (ids[r] < 0 || ids[r] >= m->vocab)
-      return fail(c, MS_ERR_INVALID_ARG, "token id %d outside 0..%d", ids[r], m->vocab - 1);
   cudaStream_t s = c->stream;
   if (m->hist_cap < steps * M) {
+    cudaStreamSynchronize(s);
     if (m->d_hist) cudaFree(m->d_hist);
     m->d_hist = nullptr;
     m->hist_cap = 0;
     MS_TRY(dev_alloc(c, (void**)&m->d_hist, (size_t)steps * M * sizeof(int)));
     m->hist_cap = steps * M;
-    if (m->gexec) {  // the graph bakes the history pointer
-      cudaGraphExecDestroy(m->gexec);
-      m->gexec = nullptr;
-    }
   }
-  MS_TRY(upload_rows(c, m, seq, pos, M, s));
-  set_span(m, pos, M, steps - 1);
-  if (m->gexec && m->g_span < m->span_hint) {  // re-plan splits for longer spans
-    cudaGraphExecDestroy(m->gexec);
-    m->gexec = nullptr;
-  }
+  MS_TRY(stage_rows(c, m, kv, ids, seq, pos, M, steps, s));
   MS_TRY(ensure_graph(c, m, kv, M));
-  MS_CUDA(c, cudaMemcpyAsync(m->d_ids, ids, M * sizeof(int), cudaMemcpyHostToDevice, s));
   MS_CUDA(c, cudaMemsetAsync(m->d_step, 0, sizeof(int), s));
-  for (int i = 0; i < steps; ++i) MS_CUDA(c, cudaGraphLaunch(m->gexec, s));
+  MS_CUDA(c, cudaEventRecord(c->ev[0], s));
+  for (int i = 0; i < steps; ++i) {
+    MS_CUDA(c, cudaGraphLaunch(m->gexec, s));
+    MS_CUDA(c, launch_advance_step(m->d_ids, m->d_next, m->d_pos, m->d_hist, m->d_step, M, s, false));
+  }
+  MS_CUDA(c, cudaEventRecord(c->ev[1], s));
   MS_CUDA(c, cudaMemcpyAsync(out_ids, m->d_hist, (size_t)steps * M * sizeof(int),
                              cudaMemcpyDeviceToHost, s));
   MS_CUDA(c, cudaStreamSynchronize(s));
+  if (device_ms) MS_CUDA(c, cudaEventElapsedTime(device_ms, c->ev[0], c->ev[1]));
   return MS_OK;
 }
+
+extern "C" void* ms_ctx_stream(ms_ctx* c) { return c ? (void*)c->stream : nullptr; }
 
 extern "C" ms_status ms_prefill(ms_ctx* c, const ms_model* mc, ms_kv* kv, const int* ids,
                                 const int* seq, const int* pos, int n_tokens, int* first_ids) {

@@ -40,6 +40,11 @@ class Context:
     def sync(self):
         self.check(lib().ms_sync(self.h, None))
 
+    @property
+    def stream_ptr(self):
+        """The context's cudaStream_t (as an int)."""
+        return lib().ms_ctx_stream(self.h)
+
     def close(self):
         if self.h:
             lib().ms_destroy(self.h)
@@ -172,12 +177,16 @@ class Model:
                                             int_array(seq), int_array(pos), M, out))
         return list(out)
 
-    def generate(self, kv, ids, seq, pos, steps):
+    def generate(self, kv, ids, seq, pos, steps, timing=False):
+        """Greedy tokens [steps][M]; with timing=True also the device ms of the loop."""
         M = len(ids)
         out = (ctypes.c_int * (M * steps))()
+        ms = ctypes.c_float(0.0)
         self.ctx.check(lib().ms_generate(self.ctx.h, self.h, kv.h, int_array(ids),
-                                         int_array(seq), int_array(pos), M, steps, out))
-        return np.array(list(out), dtype=np.int64).reshape(steps, M)
+                                         int_array(seq), int_array(pos), M, steps, out,
+                                         ctypes.byref(ms)))
+        ids_out = np.array(list(out), dtype=np.int64).reshape(steps, M)
+        return (ids_out, float(ms.value)) if timing else ids_out
 
     def prefill(self, kv, ids, seq, pos):
         first = (ctypes.c_int * kv.n_seq)(*([-1] * kv.n_seq))

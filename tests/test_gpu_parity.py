@@ -1,0 +1,345 @@
+"""Parity of the CUDA library (through its C-ABI) with the CPU oracle.
+
+Tolerances: per-layer relative RMSE <= 1e-4 (the reference's own validation
+threshold, src/tests/validate_layer.mojo:31), final logits <= 1e-3, greedy ids
+identical; the Q4 dequant is bit-exact.  Each teacher-forced check feeds the
+same input rows to both sides so errors do not compound.
+"""
+import os
+
+import numpy as np
+import pytest
+
+from golden_io import DEMO_CFG, demo_layer0_weights
+from mojostream_b200.model import (LayerSpec, LayerWeights, ModelSpec, ModelWeights, e4b_spec,
+                                   small_spec, synth_weights)
+
+pytestmark = pytest.mark.gpu
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+def rel_rmse(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.sqrt(((a - b) ** 2).mean()) / (np.sqrt((b ** 2).mean()) + 1e-12))
+
+
+@pytest.fixture(scope="module")
+def torch_cuda():
+    import torch
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    return torch
+
+
+@pytest.fixture(scope="module")
+def ctx(torch_cuda):
+    from mojostream_b200.runtime import Context
+    c = Context(0)
+    yield c
+    c.close()
+
+
+def to_dev(torch, a):
+    return torch.from_numpy(np.ascontiguousarray(a, np.float32)).cuda()
+
+
+# ---------------------------------------------------------------- Q4 GEMM --
+
+@pytest.mark.parametrize("M", [1, 3, 4, 16, 64, 70])
+@pytest.mark.parametrize("K,N", [(1024, 1024), (2560, 512), (512, 2560), (10240, 256)])
+def test_q4_gemm_matches_oracle(ctx, torch_cuda, oracle_lib, M, K, N):
+    from mojostream_b200.runtime import Q4Weight
+    torch = torch_cuda
+    rng = np.random.default_rng(M * 7919 + K + N)
+    W = rng.integers(0, 256, size=(K, N // 2), dtype=np.uint8)
+    A = rng.standard_normal((M, K)).astype(np.float32)
+    scale = float(rng.uniform(0.005, 0.02))
+    w = Q4Weight(ctx, W, K, N, scale)
+    C = torch.zeros((M, N), dtype=torch.float32, device="cuda")
+    w.gemm(to_dev(torch, A), C)
+    torch.cuda.synchronize()
+    ref = oracle_lib.q4_matmul(A, W, N, scale)
+    assert rel_rmse(C.cpu().numpy(), ref) < 2e-5
+    w.close()
+
+
+def test_q4_gemm_accumulates_like_the_reference(ctx, torch_cuda, oracle_lib):
+    from mojostream_b200.runtime import Q4Weight
+    torch = torch_cuda
+    rng = np.random.default_rng(1)
+    K, N, M = 2560, 2048, 4
+    W = rng.integers(0, 256, size=(K, N // 2), dtype=np.uint8)
+    A = rng.standard_normal((M, K)).astype(np.float32)
+    C0 = rng.standard_normal((M, N)).astype(np.float32)
+    w = Q4Weight(ctx, W, K, N, 0.01)
+    C = to_dev(torch, C0)
+    w.gemm(to_dev(torch, A), C, accumulate=True)
+    torch.cuda.synchronize()
+    ref = oracle_lib.q4_matmul(A, W, N, 0.01, C=C0)
+    assert rel_rmse(C.cpu().numpy(), ref) < 2e-5
+
+
+def test_q4_dequant_bit_exact(ctx, torch_cuda, oracle_lib):
+    """One-hot rows read the dequantised weights back: (nibble - 8) * scale
+    must be bit-identical to the reference's dequant_vec."""
+    from mojostream_b200.runtime import Q4Weight
+    torch = torch_cuda
+    rng = np.random.default_rng(2)
+    K, N = 128, 256
+    W = rng.integers(0, 256, size=(K, N // 2), dtype=np.uint8)
+    scale = 0.0137
+    w = Q4Weight(ctx, W, K, N, scale)
+    for k0 in (0, 64):
+        A = np.zeros((64, K), np.float32)
+        A[np.arange(64), k0 + np.arange(64)] = 1.0
+        C = torch.zeros((64, N), dtype=torch.float32, device="cuda")
+        w.gemm(to_dev(torch, A), C)
+        torch.cuda.synchronize()
+        ref = oracle_lib.dequant(W[k0:k0 + 64], N, scale)
+        assert np.array_equal(C.cpu().numpy(), ref)
+
+
+def test_q4_gemm_rejects_bad_shapes(ctx, torch_cuda):
+    from mojostream_b200._lib import MsError
+    from mojostream_b200.runtime import Q4Weight
+    W = np.zeros((100, 32), np.uint8)
+    with pytest.raises(MsError) as e:
+        Q4Weight(ctx, W, 100, 64, 1.0)  # K not a multiple of 64
+    assert e.value.name == "MS_ERR_SHAPE"
+    with pytest.raises(MsError):
+        Q4Weight(ctx, np.zeros((64, 4), np.uint8), 64, 8, 1.0)  # N not a multiple of 16
+
+
+# ------------------------------------------------------------ layer parity --
+
+def uniform_spec(cfg):
+    hd = cfg["hidden"] // cfg["n_heads"]
+    l = LayerSpec(hd, cfg["n_heads"], cfg["n_kv_heads"], 0, hd, cfg["ffn_dim"], 1e4)
+    return ModelSpec("uniform", cfg["hidden"], [l], 0)
+
+
+def test_reference_validation_case_layer0(ctx, torch_cuda):
+    """The reference's own numeric test (validate_layer.mojo): layer 0 of the
+    seed-42 demo model vs its NumPy oracle output, rel-RMSE < 1e-4."""
+    from mojostream_b200 import reference_api as ra
+    from mojostream_b200.runtime import Model
+    torch = torch_cuda
+    d = np.load(os.path.join(GOLDEN, "demo_layer0.npz"))
+    w = demo_layer0_weights()
+    spec = uniform_spec(DEMO_CFG)
+    model = Model(ctx, spec, ModelWeights([LayerWeights(w["ple"], w["scales"], w["mats"])]),
+                  max_rows=4)
+    kv = ra.KVCache(ctx, model, 8)
+    x = to_dev(torch, d["x_in"])
+    cfg = ra.Gemma4Config(1024, 256, 2048, 1, 16, 4)
+    ra.gemma4_forward_layer(x, 0, model, kv, cfg, 0)
+    torch.cuda.synchronize()
+    err = rel_rmse(x.cpu().numpy(), d["x_out"])
+    assert err < 1e-4, err
+
+
+def run_teacher_forced(ctx, torch, oracle_lib, spec, weights, n_seq, max_pos, calls,
+                       slide_cap=0, tol=1e-4):
+    """calls: list of (seq list, pos list).  Every call runs every layer on both
+    sides with identical input rows; returns the worst per-layer rel-RMSE."""
+    from mojostream_b200.runtime import KVCache, Model
+    M = max(len(s) for s, _ in calls)
+    model = Model(ctx, spec, weights, max_rows=M)
+    kv = KVCache(ctx, model, n_seq, max_pos, slide_cap)
+    om = oracle_lib.OracleModel(spec, weights, n_seq, max_pos, slide_cap=slide_cap or None)
+    rng = np.random.default_rng(11)
+    worst = 0.0
+    for seq, pos in calls:
+        x = (rng.standard_normal((len(seq), spec.hidden)) * 2.0).astype(np.float32)
+        for l in range(spec.n_layers):
+            xg = to_dev(torch, x)
+            model.layer_forward(l, xg, kv, seq, pos)
+            y_ref = om.layer_forward(l, x, seq, pos)
+            torch.cuda.synchronize()
+            err = rel_rmse(xg.cpu().numpy(), y_ref)
+            worst = max(worst, err)
+            assert err < tol, (l, seq, pos, err)
+            x = y_ref
+    return worst
+
+
+def test_small_hybrid_decode_window_wrap(ctx, torch_cuda, oracle_lib):
+    """Sliding (window 64, circular cache) and full layers with partial RoPE;
+    3 independent sequences decoded past two window wraps."""
+    spec = small_spec(vocab=0, n_layers=6, window=64)
+    w = synth_weights(spec, seed=21)
+    calls = [([0, 1, 2], [p, p + 5, p + 17]) for p in range(0, 150)]
+    run_teacher_forced(ctx, torch_cuda, oracle_lib, spec, w, 3, 256, calls)
+
+
+def test_rx_demo_batch_is_positions_of_one_sequence(ctx, torch_cuda, oracle_lib):
+    """The reference's batch semantics (src/main.mojo:584-592): B rows are the
+    consecutive positions base..base+B-1 of one sequence, causal inside the
+    batch; RX demo dims (16 x 64 heads, 4 KV heads, FFN 2048)."""
+    l = LayerSpec(64, 16, 4, 0, 64, 2048, 1e4)
+    spec = ModelSpec("demo-rx-2", 1024, [l, l], 0, (0.04, 0.15))
+    w = synth_weights(spec, seed=42)
+    calls = [([0] * 4, [b + 4 * s for b in range(4)]) for s in range(12)]
+    run_teacher_forced(ctx, torch_cuda, oracle_lib, spec, w, 1, 64, calls)
+
+
+def test_ragged_rows_and_mixed_sequences(ctx, torch_cuda, oracle_lib):
+    spec = small_spec(vocab=0, n_layers=6, window=32)
+    w = synth_weights(spec, seed=5)
+    calls = [([0], [0]), ([1, 1, 1], [0, 1, 2]), ([0, 1, 2, 0, 2], [1, 3, 0, 2, 1]),
+             ([2] * 7, list(range(2, 9)))]
+    # sequence 2 writes 7 positions in one call: the sliding ring needs 32 + 7 - 1 slots
+    run_teacher_forced(ctx, torch_cuda, oracle_lib, spec, w, 3, 64, calls, slide_cap=48)
+
+
+def test_large_row_block(ctx, torch_cuda, oracle_lib):
+    """M = 70 rows: two m-blocks of the projection kernel (64 + 6)."""
+    spec = small_spec(vocab=0, n_layers=2, window=96)
+    w = synth_weights(spec, seed=9)
+    calls = [([0] * 70, list(range(70)))]
+    run_teacher_forced(ctx, torch_cuda, oracle_lib, spec, w, 1, 128, calls, slide_cap=176)
+
+
+def test_e4b_dims_sliding_and_full_layers(ctx, torch_cuda, oracle_lib):
+    """Real E4B layer shapes (hd 256 sliding window 512 / hd 512 full with
+    128 rotary dims, theta 1e6): a 640-token prompt in 64-row chunks (the
+    sliding ring wraps), then single-row decode steps."""
+    spec = e4b_spec(n_layers=6, vocab=0)
+    w = synth_weights(spec, seed=4)
+    calls = [([0] * 64, list(range(p, p + 64))) for p in range(0, 640, 64)]
+    calls += [([0], [640 + i]) for i in range(3)]
+    run_teacher_forced(ctx, torch_cuda, oracle_lib, spec, w, 1, 1024, calls, slide_cap=576)
+
+
+# ------------------------------------------------------------- lm_head --
+
+def test_lm_head_logits_and_argmax(ctx, torch_cuda, oracle_lib):
+    from mojostream_b200.runtime import Model
+    torch = torch_cuda
+    spec = small_spec(vocab=32768, n_layers=1)
+    spec.hidden = 256
+    w = synth_weights(spec, seed=8)
+    model = Model(ctx, spec, w, max_rows=6)
+    om = oracle_lib.OracleModel(spec, w, 1, 16)
+    rng = np.random.default_rng(3)
+    x = (rng.standard_normal((6, spec.hidden)) * 3).astype(np.float32)
+    logits, am = model.lm_head(to_dev(torch, x))
+    torch.cuda.synchronize()
+    ref = om.lm_head(x)
+    assert rel_rmse(logits.cpu().numpy(), ref) < 1e-5
+    assert am.cpu().tolist() == om.argmax(ref)
+
+
+def test_argmax_ties_pick_the_first(ctx, torch_cuda):
+    """temperature_sampling's strict '>' (lm_head.mojo:226-229): among equal
+    maxima the smallest index wins, also across CTAs of the kernel."""
+    from mojostream_b200.runtime import Model
+    torch = torch_cuda
+    spec = small_spec(vocab=8192, n_layers=1)
+    w = synth_weights(spec, seed=1)
+    w.lm_head[:] = 0.0
+    w.lm_head[:, [700, 5000, 7000]] = 1.0  # three equal maxima in different CTAs
+    w.final_gamma[:] = 1.0
+    model = Model(ctx, spec, w, max_rows=2)
+    x = np.ones((2, spec.hidden), np.float32)
+    _, am = model.lm_head(to_dev(torch, x), logits=False)
+    torch.cuda.synchronize()
+    assert am.cpu().tolist() == [700, 700]
+
+
+# ---------------------------------------------------------- end to end --
+
+def oracle_generate(om, prompts, steps):
+    """Greedy loop on the oracle: prefill every prompt, then `steps` tokens."""
+    n = len(prompts)
+    last = []
+    for s, p in enumerate(prompts):
+        x = om.embed(p)
+        x = om.forward(x, [s] * len(p), list(range(len(p))))
+        last.append(x[-1])
+    ids = om.argmax(om.lm_head(np.stack(last)))
+    pos = [len(p) for p in prompts]
+    out = [ids]
+    for _ in range(steps - 1):
+        x = om.embed(ids)
+        x = om.forward(x, list(range(n)), pos)
+        ids = om.argmax(om.lm_head(x))
+        pos = [q + 1 for q in pos]
+        out.append(ids)
+    return np.array(out)
+
+
+def test_prefill_and_greedy_generate_match_oracle(ctx, torch_cuda, oracle_lib):
+    """Identical greedy ids over 32 steps (the north-star gate) for 3
+    sequences with different prompt lengths."""
+    from mojostream_b200.runtime import KVCache, Model
+    spec = small_spec(vocab=4096, n_layers=6, window=32)
+    w = synth_weights(spec, seed=77)
+    rng = np.random.default_rng(99)
+    prompts = [list(rng.integers(0, 4096, size=n)) for n in (9, 20, 3)]
+    steps = 32
+    om = oracle_lib.OracleModel(spec, w, 3, 128, slide_cap=64)
+    ref = oracle_generate(om, prompts, steps)
+
+    model = Model(ctx, spec, w, max_rows=32)
+    kv = KVCache(ctx, model, 3, 128, slide_cap=64)
+    ids = sum(prompts, [])
+    seq = sum([[s] * len(p) for s, p in enumerate(prompts)], [])
+    pos = sum([list(range(len(p))) for p in prompts], [])
+    first = model.prefill(kv, ids, seq, pos)
+    assert first == list(ref[0])
+    gen = model.generate(kv, first, [0, 1, 2], [len(p) for p in prompts], steps - 1)
+    assert np.array_equal(gen, ref[1:]), (gen, ref[1:])
+
+
+def test_decode_step_host_buffers_match_generate(ctx, torch_cuda):
+    from mojostream_b200.runtime import KVCache, Model
+    spec = small_spec(vocab=4096, n_layers=6, window=32)
+    w = synth_weights(spec, seed=78)
+    model = Model(ctx, spec, w, max_rows=4)
+    kv1 = KVCache(ctx, model, 2, 64)
+    kv2 = KVCache(ctx, model, 2, 64)
+    ids, pos = [5, 17], [0, 0]
+    steps = []
+    for _ in range(10):
+        ids = model.decode_step(kv1, ids, [0, 1], pos)
+        pos = [p + 1 for p in pos]
+        steps.append(ids)
+    gen = model.generate(kv2, [5, 17], [0, 1], [0, 0], 10)
+    assert np.array_equal(gen, np.array(steps))
+
+
+# ------------------------------------------------------------ host errors --
+
+def test_capacity_and_argument_errors_before_launch(ctx, torch_cuda):
+    from mojostream_b200._lib import MsError
+    from mojostream_b200.runtime import KVCache, Model
+    torch = torch_cuda
+    spec = small_spec(vocab=0, n_layers=2, window=16)
+    w = synth_weights(spec, seed=2)
+    model = Model(ctx, spec, w, max_rows=4)
+    kv = KVCache(ctx, model, 2, 32)
+    x = torch.zeros((2, spec.hidden), dtype=torch.float32, device="cuda")
+    with pytest.raises(MsError) as e:
+        model.forward(x, kv, [0, 1], [5, 32])  # position beyond max_pos
+    assert e.value.name == "MS_ERR_CAPACITY"
+    with pytest.raises(MsError) as e:
+        model.forward(x, kv, [0, 2], [0, 0])  # no such sequence
+    assert e.value.name == "MS_ERR_INVALID_ARG"
+    with pytest.raises(MsError) as e:
+        model.forward(x, kv, [1, 1], [3, 3])  # same slot twice
+    assert e.value.name == "MS_ERR_INVALID_ARG"
+    x5 = torch.zeros((5, spec.hidden), dtype=torch.float32, device="cuda")
+    with pytest.raises(MsError) as e:
+        model.forward(x5, kv, [0] * 5, list(range(5)))  # more rows than max_rows
+    assert e.value.name == "MS_ERR_CAPACITY"
+    with pytest.raises(MsError) as e:  # 20 positions of one sequence overrun the 16-slot ring
+        big = Model(ctx, spec, w, max_rows=20)
+        kvb = KVCache(ctx, big, 1, 64)
+        big.forward(torch.zeros((20, spec.hidden), device="cuda"), kvb, [0] * 20, list(range(20)))
+    assert e.value.name == "MS_ERR_CAPACITY"
+    xu = torch.zeros((3 * spec.hidden + 1,), dtype=torch.float32, device="cuda")[1:]
+    with pytest.raises(MsError) as e:
+        model.forward(xu.view(3, spec.hidden), kv, [0, 1, 0], [0, 0, 1])
+    assert e.value.name == "MS_ERR_ALIGN"
