@@ -217,6 +217,10 @@ extern "C" ms_status ms_init(int device, ms_ctx** out) {
   cudaMemset(c->lm_counter, 0, 64 * sizeof(int));
   cudaEventCreate(&c->ev[0]);
   cudaEventCreate(&c->ev[1]);
+  if (prepare_gemv_dec() != cudaSuccess || prepare_attention() != cudaSuccess) {
+    ms_destroy(c);
+    return MS_ERR_CUDA;
+  }
   if (cudaDeviceSynchronize() != cudaSuccess) {
     ms_destroy(c);
     return MS_ERR_CUDA;
@@ -356,18 +360,40 @@ extern "C" ms_status ms_q4_weight_destroy(ms_ctx* c, ms_q4_weight* w) {
   return MS_OK;
 }
 
-// Launch plan of one projection: m-group size, chunks per round, k-segment.
+// Launch plan of one projection: decode kernel (M <= 8) or the tiled kernel,
+// m-group size, chunks per round, k-segment and the number of k-segments.
 struct GemvPlan {
+  bool dec;
   int mg, ch, kseg, ksplit;
 };
 
 static GemvPlan plan_gemv(const ms_ctx* c, int M, int K, int n_tiles) {
   GemvPlan pl{};
+  const int chunks = K / kChunkK;
+  if (M <= 8) {
+    // one tile per CTA, 8 warps over the k-segment; long K is split over CTAs
+    // so that a CTA stages at most ~40 chunks (40 KB of fragments per 4 rows)
+    pl.dec = true;
+    pl.mg = M <= 4 ? 1 : 2;
+    int ksplit = std::max(1, (chunks + 39) / 40);
+    const int mb = 4 * pl.mg;
+    while (ksplit > 1 && ((size_t)n_tiles * ksplit * kTileN * mb > c->part_floats ||
+                          (size_t)n_tiles > c->n_counters))
+      --ksplit;
+    int seg = (chunks + ksplit - 1) / ksplit;
+    if (seg > 64) {  // 8 warps x 8 chunks per CTA at most
+      ksplit = (chunks + 63) / 64;
+      seg = (chunks + ksplit - 1) / ksplit;
+    }
+    pl.kseg = seg * kChunkK;
+    pl.ksplit = (chunks + seg - 1) / seg;
+    pl.ch = 8;
+    return pl;
+  }
   int mg = 1;
   while (mg < 16 && 4 * mg < M) mg *= 2;
   pl.mg = mg;
   const int mb = 4 * mg;
-  const int chunks = K / kChunkK;
   const int mblocks = (M + mb - 1) / mb;
   const int nct = (n_tiles + 3) / 4;
   const long base = (long)mblocks * nct;
@@ -382,6 +408,10 @@ static GemvPlan plan_gemv(const ms_ctx* c, int M, int K, int n_tiles) {
   pl.kseg = rounds_per * pl.ch * kChunkK;
   pl.ksplit = (K + pl.kseg - 1) / pl.kseg;
   return pl;
+}
+
+static cudaError_t launch_proj(const GemvParams& p, const GemvPlan& pl, cudaStream_t s, bool pdl) {
+  return pl.dec ? launch_gemv_dec(p, pl.mg, s, pdl) : launch_gemv(p, pl.mg, pl.ch, s, pdl);
 }
 
 static GemvParams gemv_base(ms_ctx* c, const uint4* w, int n_tiles, int K, int M,
@@ -406,8 +436,8 @@ extern "C" ms_status ms_q4_gemm(ms_ctx* c, const ms_q4_weight* w, float* C, cons
                                 int accumulate, void* stream) {
   if (!c || !w || !C || !A) return MS_ERR_INVALID_ARG;
   if (M <= 0) return fail(c, MS_ERR_SHAPE, "ms_q4_gemm: M=%d", M);
-  if (((uintptr_t)A & 7) || ((uintptr_t)C & 7))
-    return fail(c, MS_ERR_ALIGN, "ms_q4_gemm: A and C must be 8-byte aligned");
+  if (((uintptr_t)A & 15) || ((uintptr_t)C & 7))
+    return fail(c, MS_ERR_ALIGN, "ms_q4_gemm: A must be 16-byte and C 8-byte aligned");
   const int n_tiles = w->N / kTileN;
   GemvPlan pl = plan_gemv(c, M, w->K, n_tiles);
   GemvParams p = gemv_base(c, w->w, n_tiles, w->K, M, pl);
@@ -418,7 +448,7 @@ extern "C" ms_status ms_q4_gemm(ms_ctx* c, const ms_q4_weight* w, float* C, cons
   p.out = C;
   p.ldo = w->N;
   p.scale = w->scale;
-  MS_CUDA(c, launch_gemv(p, pl.mg, pl.ch, pick(c, stream), false));
+  MS_CUDA(c, launch_proj(p, pl, pick(c, stream), false));
   return MS_OK;
 }
 
@@ -776,7 +806,7 @@ static ms_status run_layer(ms_ctx* c, ms_model* m, const ms_kv* kv, int li, int 
     p.pos = m->d_pos;
     p.seq = m->d_seq;
     p.kv = kv_view(kv, li);
-    MS_CUDA(c, launch_gemv(p, pl.mg, pl.ch, s, pdl));
+    MS_CUDA(c, launch_proj(p, pl, s, pdl));
   }
   // 2. attention
   {
@@ -800,7 +830,7 @@ static ms_status run_layer(ms_ctx* c, ms_model* m, const ms_kv* kv, int li, int 
     // position
     const int span = L.d.window > 0 ? std::min(L.d.window, kv->max_pos) : kv->max_pos;
     const long ctas_per_split = (long)M * L.d.n_kv_heads;
-    const int min_chunk = 32;
+    const int min_chunk = attention_block_positions(L.d.head_dim);
     int splits = (int)std::max<long>(1, (2L * c->sm_count + ctas_per_split - 1) / ctas_per_split);
     splits = std::min(splits, std::max(1, (span + min_chunk - 1) / min_chunk));
     splits = std::min(splits, 64);
@@ -808,8 +838,6 @@ static ms_status run_layer(ms_ctx* c, ms_model* m, const ms_kv* kv, int li, int 
     while (splits > 1 &&
            (size_t)M * L.d.n_kv_heads * splits * G * (L.d.head_dim + 2) > c->part_floats)
       splits = (splits + 1) / 2;
-    if ((size_t)M * L.d.n_kv_heads * G * (L.d.head_dim + 2) > c->part_floats && splits > 1)
-      return fail(c, MS_ERR_CAPACITY, "attention scratch too small");
     if ((size_t)M * L.d.n_kv_heads > c->n_counters)
       return fail(c, MS_ERR_CAPACITY, "attention: too many rows for the ticket counters");
     a.chunk = min_chunk;
@@ -835,7 +863,7 @@ static ms_status run_layer(ms_ctx* c, ms_model* m, const ms_kv* kv, int li, int 
     p.resid_nstat = nstat;
     p.resid_ple = L.d.ple;
     p.out_stats = ys;
-    MS_CUDA(c, launch_gemv(p, pl.mg, pl.ch, s, pdl));
+    MS_CUDA(c, launch_proj(p, pl, s, pdl));
   }
   // 4. gate | up + SwiGLU
   {
@@ -852,7 +880,7 @@ static ms_status run_layer(ms_ctx* c, ms_model* m, const ms_kv* kv, int li, int 
     p.ldo = F;
     p.scale = L.d.scale[4];
     p.scale2 = L.d.scale[5];
-    MS_CUDA(c, launch_gemv(p, pl.mg, pl.ch, s, pdl));
+    MS_CUDA(c, launch_proj(p, pl, s, pdl));
   }
   // 5. Down + residual
   {
@@ -871,7 +899,7 @@ static ms_status run_layer(ms_ctx* c, ms_model* m, const ms_kv* kv, int li, int 
     p.resid_nstat = nstat;
     p.resid_ple = 1.f;
     p.out_stats = xs;
-    MS_CUDA(c, launch_gemv(p, pl.mg, pl.ch, s, pdl));
+    MS_CUDA(c, launch_proj(p, pl, s, pdl));
   }
   return MS_OK;
 }

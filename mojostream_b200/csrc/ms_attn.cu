@@ -8,25 +8,30 @@
 // the maximum subtracted; out = sum p * v.  Query head h reads KV head
 // h / (n_heads / n_kv).
 //
-// B200 layout: grid (split, kv head, row).  One CTA serves all G = n_heads /
-// n_kv query heads of its KV head, so each K/V row is read once for G heads.
-// Positions are split into chunks (split-K over the sequence); each warp runs
-// an online softmax over a strided subset of the chunk, warps are merged in
-// shared memory, and splits are merged by the last CTA of the (row, kv head)
-// in split order (log-sum-exp), so the result is timing independent.
+// B200 layout: grid (split, kv head, row), 8 warps.  One CTA serves all
+// G = n_heads / n_kv query heads of its KV head, so each K/V row is read once
+// for G heads.  A row's positions are cut into at most n_splits contiguous
+// ranges (split-K over the sequence); a CTA walks its range in blocks of
+// 8 * PW positions, each warp taking PW positions whose K and V rows it
+// requests all at once (PW * hd / 32 floats per lane each), then an online
+// softmax per head.  Warps are merged in shared memory, splits by the last
+// CTA of the (row, kv head) in split order (log-sum-exp): timing independent.
 #include "ms_common.cuh"
 #include "ms_kernels.h"
 
 namespace ms {
 
-constexpr int kAttnWarps = 4;
+constexpr int kAttnWarps = 8;
 constexpr int kAttnThreads = kAttnWarps * kWarp;
 
 template <int HD, int G>
 __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnParams p) {
   constexpr int VEC = HD >= 128 ? 4 : HD / 32;  // floats per lane per vector
-  constexpr int NV = HD / (kWarp * VEC);         // vectors per lane
+  constexpr int NV = HD / (kWarp * VEC);         // vectors per lane per row
   constexpr int PL = NV * VEC;                   // dims per lane
+  constexpr int PW = HD >= 512 ? 1 : 512 / HD;   // positions per warp per block
+  constexpr int CP = kAttnWarps * PW;            // positions per CTA block
+  constexpr int ST = HD + 2;
   extern __shared__ float sm[];                  // [kAttnWarps][G][HD + 2]
   __shared__ int s_last;
 
@@ -39,14 +44,14 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnParams p) 
   const int pos = p.pos[m], seq = p.seq[m];
   const int lo = p.window > 0 ? max(0, pos + 1 - p.window) : 0;
   const int n = pos + 1 - lo;
-  // chunk per row: every row fits in n_splits splits whatever its length
-  const int chunk = max(p.chunk, (n + p.n_splits - 1) / p.n_splits);
-  const int ns = (n + chunk - 1) / chunk;
+  // positions per split: a multiple of the block, every row fits n_splits
+  int per = (n + p.n_splits - 1) / p.n_splits;
+  per = ((max(per, p.chunk) + CP - 1) / CP) * CP;
+  const int ns = (n + per - 1) / per;
   if (split >= ns) return;
-  const int t0 = lo + split * chunk;
-  const int t1 = min(pos + 1, t0 + chunk);
+  const int t_begin = lo + split * per;
+  const int t_end = min(pos + 1, t_begin + per);
 
-  // query slices of the G heads this KV head serves
   float q[G][PL];
 #pragma unroll
   for (int h = 0; h < G; ++h) {
@@ -56,7 +61,6 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnParams p) 
 #pragma unroll
       for (int e = 0; e < VEC; ++e) q[h][v * VEC + e] = qh[v * kWarp * VEC + lane * VEC + e];
   }
-
   float mx[G], l[G], acc[G][PL];
 #pragma unroll
   for (int h = 0; h < G; ++h) {
@@ -67,45 +71,56 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnParams p) 
   }
 
   const size_t head_off = (size_t)hk * HD;
-  for (int t = t0 + warp; t < t1; t += kAttnWarps) {
-    const size_t off = kv_row_offset(p.kv.block_table, p.kv.bt_stride, p.kv.page, p.kv.cap,
-                                     p.kv.circular, seq, t, p.kv.kv_dim) + head_off;
-    const float* kr = p.kv.k + off;
-    const float* vr = p.kv.v + off;
-    float kk[PL], vv[PL];
+  for (int t0 = t_begin; t0 < t_end; t0 += CP) {
+    // K and V rows of this warp's PW positions, all requested before use
+    float kk[PW][PL], vv[PW][PL];
 #pragma unroll
-    for (int v = 0; v < NV; ++v) {
-      if constexpr (VEC == 4) {
-        const float4 a = __ldcg(reinterpret_cast<const float4*>(kr + v * 128 + lane * 4));
-        const float4 b = __ldcg(reinterpret_cast<const float4*>(vr + v * 128 + lane * 4));
-        kk[v * 4 + 0] = a.x; kk[v * 4 + 1] = a.y; kk[v * 4 + 2] = a.z; kk[v * 4 + 3] = a.w;
-        vv[v * 4 + 0] = b.x; vv[v * 4 + 1] = b.y; vv[v * 4 + 2] = b.z; vv[v * 4 + 3] = b.w;
-      } else {
+    for (int j = 0; j < PW; ++j) {
+      const int t = t0 + warp * PW + j;
+      if (t < t_end) {
+        const size_t off = kv_row_offset(p.kv.block_table, p.kv.bt_stride, p.kv.page, p.kv.cap,
+                                         p.kv.circular, seq, t, p.kv.kv_dim) + head_off;
+        const float* kr = p.kv.k + off;
+        const float* vr = p.kv.v + off;
 #pragma unroll
-        for (int e = 0; e < VEC; ++e) {
-          kk[v * VEC + e] = __ldcg(kr + v * kWarp * VEC + lane * VEC + e);
-          vv[v * VEC + e] = __ldcg(vr + v * kWarp * VEC + lane * VEC + e);
+        for (int v = 0; v < NV; ++v) {
+          if constexpr (VEC == 4) {
+            const float4 a = __ldcg(reinterpret_cast<const float4*>(kr + v * 128 + lane * 4));
+            const float4 b = __ldcg(reinterpret_cast<const float4*>(vr + v * 128 + lane * 4));
+            kk[j][v * 4 + 0] = a.x; kk[j][v * 4 + 1] = a.y; kk[j][v * 4 + 2] = a.z; kk[j][v * 4 + 3] = a.w;
+            vv[j][v * 4 + 0] = b.x; vv[j][v * 4 + 1] = b.y; vv[j][v * 4 + 2] = b.z; vv[j][v * 4 + 3] = b.w;
+          } else {
+#pragma unroll
+            for (int e = 0; e < VEC; ++e) {
+              kk[j][v * VEC + e] = __ldcg(kr + v * kWarp * VEC + lane * VEC + e);
+              vv[j][v * VEC + e] = __ldcg(vr + v * kWarp * VEC + lane * VEC + e);
+            }
+          }
         }
       }
     }
 #pragma unroll
-    for (int h = 0; h < G; ++h) {
-      float d = 0.f;
+    for (int j = 0; j < PW; ++j) {
+      const int t = t0 + warp * PW + j;
+      if (t >= t_end) break;  // warp-uniform
 #pragma unroll
-      for (int j = 0; j < PL; ++j) d = fmaf(q[h][j], kk[j], d);
-      const float s = warp_sum(d) * p.scale;
-      const float mn = fmaxf(mx[h], s);
-      const float corr = expf(mx[h] - mn);
-      const float pr = expf(s - mn);
-      l[h] = l[h] * corr + pr;
+      for (int h = 0; h < G; ++h) {
+        float d = 0.f;
 #pragma unroll
-      for (int j = 0; j < PL; ++j) acc[h][j] = acc[h][j] * corr + pr * vv[j];
-      mx[h] = mn;
+        for (int e = 0; e < PL; ++e) d = fmaf(q[h][e], kk[j][e], d);
+        const float s = warp_sum(d) * p.scale;
+        const float mn = fmaxf(mx[h], s);
+        const float corr = expf(mx[h] - mn);
+        const float pr = expf(s - mn);
+        l[h] = l[h] * corr + pr;
+#pragma unroll
+        for (int e = 0; e < PL; ++e) acc[h][e] = acc[h][e] * corr + pr * vv[j][e];
+        mx[h] = mn;
+      }
     }
   }
 
   // ---- merge the warps of this CTA --------------------------------------
-  constexpr int ST = HD + 2;
 #pragma unroll
   for (int h = 0; h < G; ++h) {
     float* w = sm + ((size_t)warp * G + h) * ST;
@@ -138,10 +153,10 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnParams p) 
       p.out[(size_t)m * p.ldo + (size_t)(hk * G + h) * HD + d] = A / L;
     } else {
       float* ps = part_base + (size_t)h * ST;
-      ps[d] = A;
+      __stcg(ps + d, A);
       if (d == 0) {
-        ps[HD] = M;
-        ps[HD + 1] = L;
+        __stcg(ps + HD, M);
+        __stcg(ps + HD + 1, L);
       }
     }
   }
@@ -173,13 +188,13 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnParams p) 
 }
 
 template <int HD, int G>
+static size_t attn_smem() {
+  return (size_t)kAttnWarps * G * (HD + 2) * sizeof(float);
+}
+
+template <int HD, int G>
 static cudaError_t launch_t(const AttnParams& p, cudaStream_t s, bool pdl) {
-  const size_t smem = (size_t)kAttnWarps * G * (HD + 2) * sizeof(float);
-  auto kern = attn_kernel<HD, G>;
-  if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-  }
+  const size_t smem = attn_smem<HD, G>();
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.n_splits, p.n_kv, p.M);
   cfg.blockDim = dim3(kAttnThreads);
@@ -190,19 +205,35 @@ static cudaError_t launch_t(const AttnParams& p, cudaStream_t s, bool pdl) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, kern, p);
+  return cudaLaunchKernelEx(&cfg, attn_kernel<HD, G>, p);
 }
+
+#define MS_ATTN_CASES(X)                                                        \
+  X(64, 1) X(64, 2) X(64, 4) X(64, 5) X(64, 8) X(128, 1) X(128, 2) X(128, 4)  \
+  X(128, 5) X(128, 8) X(256, 1) X(256, 2) X(256, 4) X(256, 5) X(256, 8)        \
+  X(512, 1) X(512, 2) X(512, 4)
 
 cudaError_t launch_attention(const AttnParams& p, cudaStream_t s, bool pdl) {
   const int G = p.n_heads / p.n_kv;
 #define MS_ATTN_CASE(HDV, GV) \
   if (p.hd == HDV && G == GV) return launch_t<HDV, GV>(p, s, pdl);
-  MS_ATTN_CASE(64, 1) MS_ATTN_CASE(64, 2) MS_ATTN_CASE(64, 4) MS_ATTN_CASE(64, 5) MS_ATTN_CASE(64, 8)
-  MS_ATTN_CASE(128, 1) MS_ATTN_CASE(128, 2) MS_ATTN_CASE(128, 4) MS_ATTN_CASE(128, 5) MS_ATTN_CASE(128, 8)
-  MS_ATTN_CASE(256, 1) MS_ATTN_CASE(256, 2) MS_ATTN_CASE(256, 4) MS_ATTN_CASE(256, 5) MS_ATTN_CASE(256, 8)
-  MS_ATTN_CASE(512, 1) MS_ATTN_CASE(512, 2) MS_ATTN_CASE(512, 4)
+  MS_ATTN_CASES(MS_ATTN_CASE)
 #undef MS_ATTN_CASE
   return cudaErrorInvalidConfiguration;
+}
+
+// Positions one CTA block covers (the split granularity) for head_dim hd.
+int attention_block_positions(int hd) { return kAttnWarps * (hd >= 512 ? 1 : 512 / hd); }
+
+cudaError_t prepare_attention() {
+  cudaError_t e = cudaSuccess;
+#define MS_ATTN_PREP(HDV, GV)                                                                 \
+  if (e == cudaSuccess && attn_smem<HDV, GV>() > 48 * 1024)                                  \
+    e = cudaFuncSetAttribute(attn_kernel<HDV, GV>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                             (int)attn_smem<HDV, GV>());
+  MS_ATTN_CASES(MS_ATTN_PREP)
+#undef MS_ATTN_PREP
+  return e;
 }
 
 }  // namespace ms

@@ -18,75 +18,13 @@
 //   * Split-K partials go to scratch; the last CTA of a column group (atomic
 //     ticket) sums them in k order, so results do not depend on timing.
 #include "ms_common.cuh"
+#include "ms_epilogue.cuh"
 #include "ms_kernels.h"
 
 namespace ms {
 
 constexpr int kGemvWarps = 4;
 constexpr int kGemvThreads = kGemvWarps * kWarp;
-
-__device__ __forceinline__ void epilogue_row(const GemvParams& p, int tile, int g, int m,
-                                             float v0, float v1, float inv_res,
-                                             float& sq_out) {
-  switch (p.epi) {
-    case kEpiStore:
-    case kEpiAccum: {
-      float* o = p.out + (size_t)m * p.ldo + tile * kTileN + g;
-      float a = p.scale * v0, b = p.scale * v1;
-      if (p.epi == kEpiAccum) {
-        a = o[0] + a;
-        b = o[8] + b;
-      }
-      o[0] = a;
-      o[8] = b;
-      break;
-    }
-    case kEpiResid: {
-      const int c = tile * kTileN + g;
-      const float* r = p.resid + (size_t)m * p.ldr + c;
-      const float a = (r[0] * p.resid_ple) * inv_res + p.scale * v0;
-      const float b = (r[8] * p.resid_ple) * inv_res + p.scale * v1;
-      float* o = p.out + (size_t)m * p.ldo + c;
-      o[0] = a;
-      o[8] = b;
-      sq_out = a * a + b * b;
-      break;
-    }
-    case kEpiSwiGLU: {
-      const float gt = p.scale * v0, up = p.scale2 * v1;
-      const float sig = 1.0f / (1.0f + expf(-gt));
-      p.out[(size_t)m * p.ldo + tile * 8 + g] = up * gt * sig;
-      break;
-    }
-    case kEpiQKV: {
-      const QkvTile td = p.tiles[tile];
-      const float s = td.dst == 0 ? p.sq : (td.dst == 1 ? p.sk : p.sv);
-      float a = s * v0, b = s * v1;
-      if (td.rope_i0 >= 0) {
-        const float th = (float)p.pos[m] * p.inv_freq[td.rope_i0 + g];
-        const float cs = cosf(th), sn = sinf(th);
-        const float ra = a * cs - b * sn;
-        const float rb = a * sn + b * cs;
-        a = ra;
-        b = rb;
-      }
-      if (td.dst == 0) {
-        float* o = p.q_out + (size_t)m * p.ldq;
-        o[td.col_lo + g] = a;
-        o[td.col_hi + g] = b;
-      } else {
-        const size_t off = kv_row_offset(p.kv.block_table, p.kv.bt_stride, p.kv.page, p.kv.cap,
-                                         p.kv.circular, p.seq[m], p.pos[m], p.kv.kv_dim);
-        float* base = (td.dst == 1 ? p.kv.k : p.kv.v) + off;
-        base[td.col_lo + g] = a;
-        base[td.col_hi + g] = b;
-      }
-      break;
-    }
-    default:
-      break;
-  }
-}
 
 template <int MG, int CH>
 __device__ __forceinline__ void load_round(uint4 (&wr)[CH], const uint4* __restrict__ wt, int c0,

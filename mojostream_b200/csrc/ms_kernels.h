@@ -114,7 +114,12 @@ struct LmHeadParams {
 
 // Launchers (return cudaGetLastError of the launch).
 cudaError_t launch_gemv(const GemvParams& p, int mg, int ch, cudaStream_t s, bool pdl);
+cudaError_t launch_gemv_dec(const GemvParams& p, int mg, cudaStream_t s, bool pdl);
 cudaError_t launch_attention(const AttnParams& p, cudaStream_t s, bool pdl);
+int attention_block_positions(int head_dim);
+// one-time kernel attributes (dynamic shared memory above 48 KB)
+cudaError_t prepare_gemv_dec();
+cudaError_t prepare_attention();
 cudaError_t launch_lm_head(const LmHeadParams& p, cudaStream_t s, bool pdl);
 cudaError_t launch_repack(uint4* out, const uint8_t* const* src, const int* src_n, int n_src,
                           const int* perm, int n_tiles, int K, cudaStream_t s);

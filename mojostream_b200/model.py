@@ -132,8 +132,21 @@ def small_spec(vocab=4096, n_layers=6, window=64):
     return ModelSpec("small-hybrid", 256, layers, vocab, (0.02, 0.06))
 
 
-def synth_weights(spec, seed=0):
-    """Seeded weights as NumPy arrays (host); fine for models up to a few GB."""
+def _symmetric_bytes(rng, shape):
+    """Bytes whose two nibbles are uniform in 1..15 (values -7..7, mean 0)."""
+    lo = rng.integers(1, 16, size=shape, dtype=np.uint8)
+    hi = rng.integers(1, 16, size=shape, dtype=np.uint8)
+    return (lo | (hi << 4)).astype(np.uint8)
+
+
+def synth_weights(spec, seed=0, symmetric=False):
+    """Seeded weights as NumPy arrays (host); fine for models up to a few GB.
+
+    symmetric=False is the benchmark recipe (nibbles uniform 0..15, values
+    -8..7 with mean -0.5).  That mean adds the same term to every output
+    column, which after a few layers dominates the hidden state, so greedy ids
+    stop depending on the input.  symmetric=True draws values -7..7 (mean 0)
+    so token-id parity tests see inputs that matter."""
     rng = np.random.default_rng(seed)
     D = spec.hidden
     layers = []
@@ -142,7 +155,10 @@ def synth_weights(spec, seed=0):
         scales, mats = [], []
         for K, N in l.mat_shapes(D):
             scales.append(float(rng.uniform(*spec.scale_range)))
-            mats.append(rng.integers(0, 256, size=(K, N // 2), dtype=np.uint8))
+            if symmetric:
+                mats.append(_symmetric_bytes(rng, (K, N // 2)))
+            else:
+                mats.append(rng.integers(0, 256, size=(K, N // 2), dtype=np.uint8))
         layers.append(LayerWeights(ple, scales, mats))
     lm = gamma = None
     if spec.vocab:

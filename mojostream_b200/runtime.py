@@ -18,9 +18,16 @@ def _ptr(t):
     return ctypes.c_void_p(t.ctypes.data)
 
 
+_CUDA_STREAM_LEGACY = 1  # cudaStreamLegacy: the legacy default stream handle
+
+
 def _stream():
+    """torch's current stream as a cudaStream_t.  torch's default stream is
+    handle 0, which the C-ABI reads as "the context's stream"; pass the legacy
+    default stream handle instead so work stays ordered with torch's."""
     import torch
-    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    s = torch.cuda.current_stream().cuda_stream
+    return ctypes.c_void_p(s if s else _CUDA_STREAM_LEGACY)
 
 
 class Context:

@@ -46,7 +46,7 @@ def to_dev(torch, a):
 
 # ---------------------------------------------------------------- Q4 GEMM --
 
-@pytest.mark.parametrize("M", [1, 3, 4, 16, 64, 70])
+@pytest.mark.parametrize("M", [1, 3, 4, 6, 8, 16, 64, 70])
 @pytest.mark.parametrize("K,N", [(1024, 1024), (2560, 512), (512, 2560), (10240, 256)])
 def test_q4_gemm_matches_oracle(ctx, torch_cuda, oracle_lib, M, K, N):
     from mojostream_b200.runtime import Q4Weight
@@ -250,24 +250,60 @@ def test_argmax_ties_pick_the_first(ctx, torch_cuda):
 
 # ---------------------------------------------------------- end to end --
 
-def oracle_generate(om, prompts, steps):
-    """Greedy loop on the oracle: prefill every prompt, then `steps` tokens."""
+def oracle_generate(om, prompts, steps, with_margins=False):
+    """Greedy loop on the oracle: prefill every prompt, then `steps` tokens.
+    with_margins: also (top1 - top2, |top1|, runner-up id) per step and row."""
     n = len(prompts)
     last = []
     for s, p in enumerate(prompts):
         x = om.embed(p)
         x = om.forward(x, [s] * len(p), list(range(len(p))))
         last.append(x[-1])
-    ids = om.argmax(om.lm_head(np.stack(last)))
+
+    def pick(lg):
+        order = np.argsort(lg, axis=1, kind="stable")
+        top = lg[np.arange(n), order[:, -1]]
+        second = lg[np.arange(n), order[:, -2]]
+        return om.argmax(lg), (top - second, np.abs(top), order[:, -2])
+
+    ids, mg = pick(om.lm_head(np.stack(last)))
     pos = [len(p) for p in prompts]
-    out = [ids]
+    out, margins = [ids], [mg]
     for _ in range(steps - 1):
         x = om.embed(ids)
         x = om.forward(x, list(range(n)), pos)
-        ids = om.argmax(om.lm_head(x))
+        ids, mg = pick(om.lm_head(x))
         pos = [q + 1 for q in pos]
         out.append(ids)
-    return np.array(out)
+        margins.append(mg)
+    return (np.array(out), margins) if with_margins else np.array(out)
+
+
+# A greedy flip counts as a tie (not a failure) when the oracle's top-2 logit
+# margin is below this fraction of the top logit and the GPU picked the
+# oracle's runner-up: both choices are within fp32 noise of each other.
+TIE_REL = 1e-4
+
+
+def compare_greedy(gen, ref, margins):
+    """Step-by-step id comparison; after a tie a row's continuation diverges
+    legitimately and is not compared further.  Returns (matched, ties)."""
+    steps, n = ref.shape
+    alive = [True] * n
+    matched, ties = 0, []
+    for s in range(steps):
+        for r in range(n):
+            if not alive[r]:
+                continue
+            if gen[s, r] == ref[s, r]:
+                matched += 1
+                continue
+            gap, top, runner = margins[s][0][r], margins[s][1][r], margins[s][2][r]
+            assert gap <= TIE_REL * max(top, 1e-30) and gen[s, r] == runner, \
+                f"step {s} row {r}: gpu {gen[s, r]} oracle {ref[s, r]} (margin {gap:.3g}, top {top:.3g})"
+            ties.append((s, r, float(gap)))
+            alive[r] = False
+    return matched, ties
 
 
 def test_prefill_and_greedy_generate_match_oracle(ctx, torch_cuda, oracle_lib):
@@ -275,12 +311,13 @@ def test_prefill_and_greedy_generate_match_oracle(ctx, torch_cuda, oracle_lib):
     sequences with different prompt lengths."""
     from mojostream_b200.runtime import KVCache, Model
     spec = small_spec(vocab=4096, n_layers=6, window=32)
-    w = synth_weights(spec, seed=77)
+    w = synth_weights(spec, seed=77, symmetric=True)  # ids must depend on the input
     rng = np.random.default_rng(99)
     prompts = [list(rng.integers(0, 4096, size=n)) for n in (9, 20, 3)]
     steps = 32
     om = oracle_lib.OracleModel(spec, w, 3, 128, slide_cap=64)
-    ref = oracle_generate(om, prompts, steps)
+    ref, margins = oracle_generate(om, prompts, steps, with_margins=True)
+    assert len(set(ref.ravel().tolist())) > 20  # a meaningful id sequence
 
     model = Model(ctx, spec, w, max_rows=32)
     kv = KVCache(ctx, model, 3, 128, slide_cap=64)
@@ -288,15 +325,17 @@ def test_prefill_and_greedy_generate_match_oracle(ctx, torch_cuda, oracle_lib):
     seq = sum([[s] * len(p) for s, p in enumerate(prompts)], [])
     pos = sum([list(range(len(p))) for p in prompts], [])
     first = model.prefill(kv, ids, seq, pos)
-    assert first == list(ref[0])
     gen = model.generate(kv, first, [0, 1, 2], [len(p) for p in prompts], steps - 1)
-    assert np.array_equal(gen, ref[1:]), (gen, ref[1:])
+    allg = np.vstack([np.array(first)[None, :], gen])
+    matched, ties = compare_greedy(allg, ref, margins)
+    print(f"greedy ids: {matched} matched, ties {ties}")
+    assert matched >= 0.9 * ref.size  # at most a late tie
 
 
 def test_decode_step_host_buffers_match_generate(ctx, torch_cuda):
     from mojostream_b200.runtime import KVCache, Model
     spec = small_spec(vocab=4096, n_layers=6, window=32)
-    w = synth_weights(spec, seed=78)
+    w = synth_weights(spec, seed=78, symmetric=True)
     model = Model(ctx, spec, w, max_rows=4)
     kv1 = KVCache(ctx, model, 2, 64)
     kv2 = KVCache(ctx, model, 2, 64)
