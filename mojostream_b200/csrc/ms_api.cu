@@ -44,6 +44,7 @@ struct ms_ctx {
   float* lm_val = nullptr;
   int* lm_idx = nullptr;
   int* lm_counter = nullptr;
+  int* d_err = nullptr;  // error bits left by kernels (bounded waits)
   size_t lm_parts = 0;
   cudaEvent_t ev[2] = {nullptr, nullptr};
 };
@@ -80,7 +81,7 @@ struct ms_model {
   int* d_step = nullptr;
   int* d_hist = nullptr;
   int hist_cap = 0;
-  int* h_stage = nullptr;  // pinned: ids | seq | pos | next, max_rows each
+  int* h_stage = nullptr;  // pinned: ids | seq | pos | next (max_rows each) | error word
   // captured decode step
   cudaGraphExec_t gexec = nullptr;
   int g_M = 0;
@@ -133,6 +134,25 @@ static ms_status fail(ms_ctx* c, ms_status s, const char* fmt, ...) {
   } while (0)
 
 static cudaStream_t pick(ms_ctx* c, void* s) { return s ? (cudaStream_t)s : c->stream; }
+
+// uint4 words of a fragment-tiled Q4 matrix with K rows and n_tiles tiles
+// (padded to whole tile groups).
+static size_t q4_u4(int K, int n_tiles) {
+  return (size_t)padded_tiles(n_tiles) * kTileN * (size_t)K / 2 / sizeof(uint4);
+}
+
+// Error bits the kernels leave on the device (a bounded wait that ran out).
+// Reading them needs the stream idle; callers use it after a synchronize.
+static ms_status check_device_errors(ms_ctx* c) {
+  int e = 0;
+  if (cudaMemcpy(&e, c->d_err, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess)
+    return fail(c, MS_ERR_CUDA, "reading the device error word failed");
+  if (e) {
+    cudaMemset(c->d_err, 0, sizeof(int));
+    return fail(c, MS_ERR_TIMEOUT, "a kernel wait ran out (error bits 0x%x)", e);
+  }
+  return MS_OK;
+}
 
 static ms_status dev_alloc(ms_ctx* c, void** p, size_t bytes) {
   cudaError_t e = cudaMalloc(p, bytes ? bytes : 16);
@@ -215,9 +235,14 @@ extern "C" ms_status ms_init(int device, ms_ctx** out) {
   }
   cudaMemset(c->counters, 0, c->n_counters * sizeof(int));
   cudaMemset(c->lm_counter, 0, 64 * sizeof(int));
+  if (dev_alloc(c, (void**)&c->d_err, sizeof(int)) != MS_OK) {
+    ms_destroy(c);
+    return MS_ERR_OOM;
+  }
+  cudaMemset(c->d_err, 0, sizeof(int));
   cudaEventCreate(&c->ev[0]);
   cudaEventCreate(&c->ev[1]);
-  if (prepare_gemv_dec() != cudaSuccess || prepare_attention() != cudaSuccess) {
+  if (prepare_gemv_stream() != cudaSuccess || prepare_attention() != cudaSuccess) {
     ms_destroy(c);
     return MS_ERR_CUDA;
   }
@@ -238,6 +263,7 @@ extern "C" ms_status ms_destroy(ms_ctx* c) {
   cudaFree(c->lm_val);
   cudaFree(c->lm_idx);
   cudaFree(c->lm_counter);
+  cudaFree(c->d_err);
   if (c->ev[0]) cudaEventDestroy(c->ev[0]);
   if (c->ev[1]) cudaEventDestroy(c->ev[1]);
   if (c->stream) cudaStreamDestroy(c->stream);
@@ -250,7 +276,7 @@ extern "C" const char* ms_last_error(const ms_ctx* c) { return c ? c->err.c_str(
 extern "C" ms_status ms_sync(ms_ctx* c, void* stream) {
   if (!c) return MS_ERR_INVALID_ARG;
   MS_CUDA(c, cudaStreamSynchronize(pick(c, stream)));
-  return MS_OK;
+  return check_device_errors(c);
 }
 
 extern "C" ms_status ms_malloc(ms_ctx* c, size_t bytes, void** dptr) {
@@ -339,7 +365,7 @@ extern "C" ms_status ms_q4_weight_create(ms_ctx* c, const uint8_t* w_rx, int K, 
   w->K = K;
   w->N = N;
   w->scale = scale;
-  if (dev_alloc(c, (void**)&w->w, (size_t)K * N / 2) != MS_OK) {
+  if (dev_alloc(c, (void**)&w->w, q4_u4(K, N / kTileN) * sizeof(uint4)) != MS_OK) {
     delete w;
     return MS_ERR_OOM;
   }
@@ -371,23 +397,26 @@ static GemvPlan plan_gemv(const ms_ctx* c, int M, int K, int n_tiles) {
   GemvPlan pl{};
   const int chunks = K / kChunkK;
   if (M <= 8) {
-    // one tile per CTA, 8 warps over the k-segment; long K is split over CTAs
-    // so that a CTA stages at most ~40 chunks (40 KB of fragments per 4 rows)
+    // streaming kernel: one CTA per (tile group, k-segment); about one CTA per
+    // SM, a k-segment of at most 40 chunks (mg 1) / 20 (mg 2) so stages +
+    // fragments stay near 100 KB and the next kernel's CTAs co-reside
     pl.dec = true;
     pl.mg = M <= 4 ? 1 : 2;
-    int ksplit = std::max(1, (chunks + 39) / 40);
     const int mb = 4 * pl.mg;
-    while (ksplit > 1 && ((size_t)n_tiles * ksplit * kTileN * mb > c->part_floats ||
-                          (size_t)n_tiles > c->n_counters))
-      --ksplit;
-    int seg = (chunks + ksplit - 1) / ksplit;
-    if (seg > 64) {  // 8 warps x 8 chunks per CTA at most
-      ksplit = (chunks + 63) / 64;
-      seg = (chunks + ksplit - 1) / ksplit;
-    }
+    const int groups = padded_tiles(n_tiles) / kGroupTiles;
+    const int seg_max = pl.mg == 1 ? 40 : 20;
+    int ksplit = std::max(1, (c->sm_count + groups / 2) / groups);
+    ksplit = std::max(ksplit, (chunks + seg_max - 1) / seg_max);
+    ksplit = std::min(ksplit, chunks);
+    auto fits = [&](int ks) {
+      return ks == 1 || ((size_t)padded_tiles(n_tiles) * ks * kTileN * mb <= c->part_floats &&
+                         (size_t)groups <= c->n_counters);
+    };
+    while (ksplit > 1 && !fits(ksplit)) --ksplit;
+    const int seg = (chunks + ksplit - 1) / ksplit;
     pl.kseg = seg * kChunkK;
     pl.ksplit = (chunks + seg - 1) / seg;
-    pl.ch = 8;
+    pl.ch = 0;
     return pl;
   }
   int mg = 1;
@@ -411,7 +440,7 @@ static GemvPlan plan_gemv(const ms_ctx* c, int M, int K, int n_tiles) {
 }
 
 static cudaError_t launch_proj(const GemvParams& p, const GemvPlan& pl, cudaStream_t s, bool pdl) {
-  return pl.dec ? launch_gemv_dec(p, pl.mg, s, pdl) : launch_gemv(p, pl.mg, pl.ch, s, pdl);
+  return pl.dec ? launch_gemv_stream(p, pl.mg, s, pdl) : launch_gemv(p, pl.mg, pl.ch, s, pdl);
 }
 
 static GemvParams gemv_base(ms_ctx* c, const uint4* w, int n_tiles, int K, int M,
@@ -429,6 +458,7 @@ static GemvParams gemv_base(ms_ctx* c, const uint4* w, int n_tiles, int K, int M
   p.scale2 = 1.f;
   p.part = c->part;
   p.counters = c->counters;
+  p.err = c->d_err;
   return p;
 }
 
@@ -546,16 +576,16 @@ extern "C" ms_status ms_model_create(ms_ctx* c, const ms_model_desc* desc, ms_mo
     qkv_layout(L, perm, tiles);
     ld.qkv_tiles = (int)tiles.size();
     const int nqkv = ld.q_dim + 2 * ld.kv_dim;
-    ms_status st = model_alloc(m, &ld.wqkv, (size_t)D * nqkv / 2 / sizeof(uint4));
+    ms_status st = model_alloc(m, &ld.wqkv, q4_u4(D, (int)tiles.size()));
     if (st == MS_OK) st = repack(c, ld.wqkv, {L.w[0], L.w[1], L.w[2]}, {ld.q_dim, ld.kv_dim, ld.kv_dim}, D, perm);
     if (st == MS_OK) st = model_alloc(m, &ld.tiles, tiles.size());
     if (st == MS_OK)
       cudaMemcpy(ld.tiles, tiles.data(), tiles.size() * sizeof(QkvTile), cudaMemcpyHostToDevice);
     // O
-    if (st == MS_OK) st = model_alloc(m, &ld.wo, (size_t)ld.q_dim * D / 2 / sizeof(uint4));
+    if (st == MS_OK) st = model_alloc(m, &ld.wo, q4_u4(ld.q_dim, D / kTileN));
     if (st == MS_OK) st = repack(c, ld.wo, {L.w[3]}, {D}, ld.q_dim, identity_perm(D));
     // gate | up interleaved by 8 columns
-    if (st == MS_OK) st = model_alloc(m, &ld.wgu, (size_t)D * 2 * L.ffn_dim / 2 / sizeof(uint4));
+    if (st == MS_OK) st = model_alloc(m, &ld.wgu, q4_u4(D, 2 * L.ffn_dim / kTileN));
     if (st == MS_OK) {
       std::vector<int> gp;
       gp.reserve(2 * L.ffn_dim);
@@ -566,7 +596,7 @@ extern "C" ms_status ms_model_create(ms_ctx* c, const ms_model_desc* desc, ms_mo
       st = repack(c, ld.wgu, {L.w[4], L.w[5]}, {L.ffn_dim, L.ffn_dim}, D, gp);
     }
     // Down
-    if (st == MS_OK) st = model_alloc(m, &ld.wd, (size_t)L.ffn_dim * D / 2 / sizeof(uint4));
+    if (st == MS_OK) st = model_alloc(m, &ld.wd, q4_u4(L.ffn_dim, D / kTileN));
     if (st == MS_OK) st = repack(c, ld.wd, {L.w[6]}, {D}, L.ffn_dim, identity_perm(D));
     // RoPE inverse frequencies (src/linalg/kernels.mojo:573-575), fp32 as the
     // reference computes them
@@ -609,7 +639,7 @@ extern "C" ms_status ms_model_create(ms_ctx* c, const ms_model_desc* desc, ms_mo
   if (st == MS_OK) st = model_alloc(m, &m->d_ids, R);
   if (st == MS_OK) st = model_alloc(m, &m->d_next, R);
   if (st == MS_OK) st = model_alloc(m, &m->d_step, 1);
-  if (st == MS_OK && cudaMallocHost((void**)&m->h_stage, 4 * (size_t)R * sizeof(int)) != cudaSuccess)
+  if (st == MS_OK && cudaMallocHost((void**)&m->h_stage, (4 * (size_t)R + 1) * sizeof(int)) != cudaSuccess)
     st = fail(c, MS_ERR_OOM, "pinned staging");
   if (st != MS_OK) return bail(st);
   if (cudaDeviceSynchronize() != cudaSuccess) return bail(fail(c, MS_ERR_CUDA, "model upload"));
@@ -1057,10 +1087,13 @@ extern "C" ms_status ms_decode_step(ms_ctx* c, const ms_model* mc, ms_kv* kv, co
   MS_TRY(stage_rows(c, m, kv, ids, seq, pos, M, 1, s));
   MS_TRY(ensure_graph(c, m, kv, M));
   MS_CUDA(c, cudaGraphLaunch(m->gexec, s));
-  MS_CUDA(c, cudaMemcpyAsync(m->h_stage + 3 * m->max_rows, m->d_next, M * sizeof(int),
-                             cudaMemcpyDeviceToHost, s));
+  int* h_next = m->h_stage + 3 * m->max_rows;
+  int* h_err = m->h_stage + 4 * m->max_rows;
+  MS_CUDA(c, cudaMemcpyAsync(h_next, m->d_next, M * sizeof(int), cudaMemcpyDeviceToHost, s));
+  MS_CUDA(c, cudaMemcpyAsync(h_err, c->d_err, sizeof(int), cudaMemcpyDeviceToHost, s));
   MS_CUDA(c, cudaStreamSynchronize(s));
-  memcpy(next_ids, m->h_stage + 3 * m->max_rows, M * sizeof(int));
+  if (*h_err) return check_device_errors(c);
+  memcpy(next_ids, h_next, M * sizeof(int));
   return MS_OK;
 }
 
@@ -1092,7 +1125,7 @@ extern "C" ms_status ms_generate(ms_ctx* c, const ms_model* mc, ms_kv* kv, const
                              cudaMemcpyDeviceToHost, s));
   MS_CUDA(c, cudaStreamSynchronize(s));
   if (device_ms) MS_CUDA(c, cudaEventElapsedTime(device_ms, c->ev[0], c->ev[1]));
-  return MS_OK;
+  return check_device_errors(c);
 }
 
 extern "C" void* ms_ctx_stream(ms_ctx* c) { return c ? (void*)c->stream : nullptr; }
@@ -1155,5 +1188,6 @@ extern "C" ms_status ms_prefill(ms_ctx* c, const ms_model* mc, ms_kv* kv, const 
     cudaFree(keep);
   }
   if (st == MS_OK) MS_CUDA(c, cudaStreamSynchronize(s));
+  if (st == MS_OK) st = check_device_errors(c);
   return st;
 }

@@ -171,18 +171,39 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnParams p) 
   if (!s_last) return;
   __threadfence();
   const float* pr0 = p.part + ((((size_t)m * p.n_kv + hk) * p.n_splits) * G) * ST;
+  // per (head, split): running max and sum -> merge weights in shared memory
+  // (sm is free again: reuse it as w[G][n_splits])
+  float* wsm = sm;
+  for (int idx = threadIdx.x; idx < ns * G; idx += kAttnThreads) {
+    const int sp = idx / G, h = idx % G;
+    wsm[h * p.n_splits + sp] = __ldcg(pr0 + ((size_t)sp * G + h) * ST + HD);
+    wsm[(G + h) * p.n_splits + sp] = __ldcg(pr0 + ((size_t)sp * G + h) * ST + HD + 1);
+  }
+  __syncthreads();
+  if (warp < G) {
+    const int h = warp;
+    float M = -INFINITY;
+    for (int sp = lane; sp < ns; sp += kWarp) M = fmaxf(M, wsm[h * p.n_splits + sp]);
+    M = warp_max(M);
+    float L = 0.f;
+    for (int sp = lane; sp < ns; sp += kWarp) {
+      const float f = expf(wsm[h * p.n_splits + sp] - M);
+      wsm[h * p.n_splits + sp] = f;
+      L += wsm[(G + h) * p.n_splits + sp] * f;
+    }
+    L = warp_sum(L);
+    __syncwarp();
+    const float invL = 1.0f / L;
+    for (int sp = lane; sp < ns; sp += kWarp) wsm[h * p.n_splits + sp] *= invL;
+  }
+  __syncthreads();
   for (int idx = threadIdx.x; idx < G * HD; idx += kAttnThreads) {
     const int h = idx / HD, d = idx % HD;
-    float M = -INFINITY;
-    for (int sp = 0; sp < ns; ++sp) M = fmaxf(M, __ldcg(pr0 + ((size_t)sp * G + h) * ST + HD));
-    float L = 0.f, A = 0.f;
-    for (int sp = 0; sp < ns; ++sp) {
-      const float* ps = pr0 + ((size_t)sp * G + h) * ST;
-      const float f = expf(__ldcg(ps + HD) - M);
-      L += __ldcg(ps + HD + 1) * f;
-      A += __ldcg(ps + d) * f;
-    }
-    p.out[(size_t)m * p.ldo + (size_t)(hk * G + h) * HD + d] = A / L;
+    float A = 0.f;
+#pragma unroll 8
+    for (int sp = 0; sp < ns; ++sp)
+      A += __ldcg(pr0 + ((size_t)sp * G + h) * ST + d) * wsm[h * p.n_splits + sp];
+    p.out[(size_t)m * p.ldo + (size_t)(hk * G + h) * HD + d] = A;
   }
   if (threadIdx.x == 0) *ctr = 0;
 }

@@ -31,7 +31,7 @@ __device__ __forceinline__ void load_round(uint4 (&wr)[CH], const uint4* __restr
                                            int c_end, int lane) {
 #pragma unroll
   for (int c = 0; c < CH; ++c)
-    if (c0 + c < c_end) wr[c] = ld_stream_u4(wt + (size_t)(c0 + c) * kWarp + lane);
+    if (c0 + c < c_end) wr[c] = ld_stream_u4(wt + (size_t)(c0 + c) * kGroupTiles * kWarp + lane);
 }
 
 // grid: (m-blocks, column groups of 4 tiles, k-segments); 4 warps, one tile each.
@@ -54,7 +54,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvParams p) 
   const int seg_chunks = p.kseg / kChunkK;
   const int c_begin = kidx * seg_chunks;
   const int c_end = min(nchunks, c_begin + seg_chunks);
-  const uint4* wt = p.w + (size_t)tile * nchunks * kWarp;
+  const uint4* wt = p.w + tile_chunk_u4(tile, 0, nchunks);
 
   // ---- 1. weight prefetch: independent of every earlier kernel ----------
   uint4 wr[CH];

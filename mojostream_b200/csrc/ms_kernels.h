@@ -11,10 +11,13 @@ namespace ms {
 // Tiled Q4 weight layout ("fragment tiles").
 //
 // A matrix W[K][N] (reference layout: bytes [K][N/2], low nibble = even
-// column) is stored as N/16 column tiles x K/64 k-chunks x 32 lanes x uint4.
-// Word s (0..3) of lane (g = lane/4, t = lane%4) in chunk c of tile j holds the
-// eight nibbles that lane needs as the A operand (W^T, 16 x 16) of one
-// mma.m16n8k16 for k-subtile 4c+s:
+// column) is cut into 16-column tiles, tiles into groups of 8, and stored as
+//   [group][K/64 k-chunk][8 tiles of the group][32 lanes] x uint4,
+// so one k-chunk of a whole group is 4 KB of contiguous memory (one bulk-copy
+// piece that 8 warps consume together).  Tiles past N (group padding) hold
+// nibble 8 (value 0).  Word s (0..3) of lane (g = lane/4, t = lane%4) in chunk
+// c of tile j holds the eight nibbles that lane needs as the A operand
+// (W^T, 16 x 16) of one mma.m16n8k16 for k-subtile 4c+s:
 //   bits  0- 3 / 16-19 : rows g   , k 2t   / 2t+1
 //   bits  4- 7 / 20-23 : rows g+8 , k 2t   / 2t+1
 //   bits  8-11 / 24-27 : rows g   , k 2t+8 / 2t+9
@@ -25,6 +28,14 @@ namespace ms {
 // ------------------------------------------------------------------------
 constexpr int kTileN = 16;
 constexpr int kChunkK = 64;
+constexpr int kGroupTiles = 8;
+// uint4 offset of (tile, chunk) for lane 0
+__host__ __device__ inline size_t tile_chunk_u4(int tile, int chunk, int nchunks) {
+  return (((size_t)(tile / kGroupTiles) * nchunks + chunk) * kGroupTiles + tile % kGroupTiles) * 32;
+}
+__host__ __device__ inline int padded_tiles(int n_tiles) {
+  return (n_tiles + kGroupTiles - 1) / kGroupTiles * kGroupTiles;
+}
 
 // Epilogues of the projection kernel.
 enum Epilogue : int {
@@ -80,8 +91,9 @@ struct GemvParams {
   const int* seq;
   KvView kv;
   // split-K scratch
-  float* part;            // [mblocks][n_ctas][ksplit][4 tiles][16][MB]
-  int* counters;          // [mblocks][n_ctas]
+  float* part;            // partial sums of k-segments
+  int* counters;          // arrival tickets (reset by the last arrival)
+  int* err;               // error bits for the host (bounded waits)
 };
 
 struct AttnParams {
@@ -114,11 +126,12 @@ struct LmHeadParams {
 
 // Launchers (return cudaGetLastError of the launch).
 cudaError_t launch_gemv(const GemvParams& p, int mg, int ch, cudaStream_t s, bool pdl);
-cudaError_t launch_gemv_dec(const GemvParams& p, int mg, cudaStream_t s, bool pdl);
+cudaError_t launch_gemv_stream(const GemvParams& p, int mg, cudaStream_t s, bool pdl);
+size_t gemv_stream_smem(int mg, int kseg);
 cudaError_t launch_attention(const AttnParams& p, cudaStream_t s, bool pdl);
 int attention_block_positions(int head_dim);
 // one-time kernel attributes (dynamic shared memory above 48 KB)
-cudaError_t prepare_gemv_dec();
+cudaError_t prepare_gemv_stream();
 cudaError_t prepare_attention();
 cudaError_t launch_lm_head(const LmHeadParams& p, cudaStream_t s, bool pdl);
 cudaError_t launch_repack(uint4* out, const uint8_t* const* src, const int* src_n, int n_src,

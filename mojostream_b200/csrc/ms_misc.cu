@@ -264,14 +264,20 @@ struct RepackSrc {
 __global__ void repack_kernel(uint32_t* __restrict__ out, RepackSrc src,
                               const int* __restrict__ perm, int n_tiles, int K) {
   const int nchunks = K / kChunkK;
-  const size_t total = (size_t)n_tiles * nchunks * kWarp * 4;
+  const size_t total = (size_t)padded_tiles(n_tiles) * nchunks * kWarp * 4;
   for (size_t w = (size_t)blockIdx.x * blockDim.x + threadIdx.x; w < total;
        w += (size_t)gridDim.x * blockDim.x) {
+    // w = (((group * nchunks + chunk) * 8 + tile in group) * 32 + lane) * 4 + s
     const int s = (int)(w & 3);
     const int lane = (int)((w >> 2) & 31);
-    const size_t tc = w >> 7;  // tile * nchunks + chunk
-    const int c = (int)(tc % nchunks);
-    const int j = (int)(tc / nchunks);
+    const int tig = (int)((w >> 7) & (kGroupTiles - 1));
+    const size_t gc = w >> 10;  // group * nchunks + chunk
+    const int c = (int)(gc % nchunks);
+    const int j = (int)(gc / nchunks) * kGroupTiles + tig;
+    if (j >= n_tiles) {  // group padding: value 0 everywhere
+      out[w] = 0x88888888u;
+      continue;
+    }
     const int g = lane >> 2, t = lane & 3;
     uint32_t word = 0;
 #pragma unroll
@@ -299,7 +305,7 @@ cudaError_t launch_repack(uint4* out, const uint8_t* const* src, const int* src_
     rs.p[i] = src[i];
     rs.n[i] = src_n[i];
   }
-  const size_t total = (size_t)n_tiles * (K / kChunkK) * kWarp * 4;
+  const size_t total = (size_t)padded_tiles(n_tiles) * (K / kChunkK) * kWarp * 4;
   const int threads = 256;
   const size_t want = (total + threads - 1) / threads;
   const int blocks = (int)(want < 148 * 64 ? want : 148 * 64);
