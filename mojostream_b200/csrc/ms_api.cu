@@ -74,6 +74,10 @@ struct ms_model {
   float* Q = nullptr;
   float* ATT = nullptr;
   float* H = nullptr;
+  // the same rows as MMA fragments for decode batches (M <= 8): X[0], X[1], ATT, H
+  uint16_t* FX[2] = {nullptr, nullptr};
+  uint16_t* FATT = nullptr;
+  uint16_t* FH = nullptr;
   int* d_seq = nullptr;
   int* d_pos = nullptr;
   int* d_ids = nullptr;
@@ -103,6 +107,7 @@ struct ms_q4_weight {
   int K = 0, N = 0;
   float scale = 1.f;
   uint4* w = nullptr;
+  uint16_t* frag = nullptr;  // the input rows as MMA fragments (decode path)
 };
 
 // ----------------------------------------------------------------- errors --
@@ -140,6 +145,9 @@ static cudaStream_t pick(ms_ctx* c, void* s) { return s ? (cudaStream_t)s : c->s
 static size_t q4_u4(int K, int n_tiles) {
   return (size_t)padded_tiles(n_tiles) * kTileN * (size_t)K / 2 / sizeof(uint4);
 }
+
+// Fragment rows of buffer X[i] when the call takes the decode path (M <= 8).
+static uint16_t* frag_in(ms_model* m, int i, int M) { return M <= 8 ? m->FX[i] : nullptr; }
 
 // Error bits the kernels leave on the device (a bounded wait that ran out).
 // Reading them needs the stream idle; callers use it after a synchronize.
@@ -365,13 +373,16 @@ extern "C" ms_status ms_q4_weight_create(ms_ctx* c, const uint8_t* w_rx, int K, 
   w->K = K;
   w->N = N;
   w->scale = scale;
-  if (dev_alloc(c, (void**)&w->w, q4_u4(K, N / kTileN) * sizeof(uint4)) != MS_OK) {
+  if (dev_alloc(c, (void**)&w->w, q4_u4(K, N / kTileN) * sizeof(uint4)) != MS_OK ||
+      dev_alloc(c, (void**)&w->frag, (size_t)2 * K * 16) != MS_OK) {
+    cudaFree(w->w);
     delete w;
     return MS_ERR_OOM;
   }
   ms_status st = repack(c, w->w, {w_rx}, {N}, K, identity_perm(N));
   if (st != MS_OK) {
     cudaFree(w->w);
+    cudaFree(w->frag);
     delete w;
     return st;
   }
@@ -381,7 +392,9 @@ extern "C" ms_status ms_q4_weight_create(ms_ctx* c, const uint8_t* w_rx, int K, 
 
 extern "C" ms_status ms_q4_weight_destroy(ms_ctx* c, ms_q4_weight* w) {
   if (!c || !w) return MS_ERR_INVALID_ARG;
+  cudaStreamSynchronize(c->stream);
   cudaFree(w->w);
+  cudaFree(w->frag);
   delete w;
   return MS_OK;
 }
@@ -478,7 +491,12 @@ extern "C" ms_status ms_q4_gemm(ms_ctx* c, const ms_q4_weight* w, float* C, cons
   p.out = C;
   p.ldo = w->N;
   p.scale = w->scale;
-  MS_CUDA(c, launch_proj(p, pl, pick(c, stream), false));
+  cudaStream_t s = pick(c, stream);
+  if (pl.dec) {  // the streaming kernel reads its rows as MMA fragments
+    MS_CUDA(c, launch_rowstats(nullptr, w->frag, A, w->K, M, w->K, s, false));
+    p.xfrag = reinterpret_cast<const uint2*>(w->frag);
+  }
+  MS_CUDA(c, launch_proj(p, pl, s, false));
   return MS_OK;
 }
 
@@ -634,6 +652,10 @@ extern "C" ms_status ms_model_create(ms_ctx* c, const ms_model_desc* desc, ms_mo
   if (st == MS_OK) st = model_alloc(m, &m->Q, (size_t)R * m->max_q);
   if (st == MS_OK) st = model_alloc(m, &m->ATT, (size_t)R * m->max_q);
   if (st == MS_OK) st = model_alloc(m, &m->H, (size_t)R * m->max_f);
+  // fragment rows: 2 row blocks x width / 16 subtiles x 32 lanes x 4 halves
+  for (int i = 0; i < 2 && st == MS_OK; ++i) st = model_alloc(m, &m->FX[i], (size_t)2 * D * 16);
+  if (st == MS_OK) st = model_alloc(m, &m->FATT, (size_t)2 * m->max_q * 16);
+  if (st == MS_OK) st = model_alloc(m, &m->FH, (size_t)2 * m->max_f * 16);
   if (st == MS_OK) st = model_alloc(m, &m->d_seq, R);
   if (st == MS_OK) st = model_alloc(m, &m->d_pos, R);
   if (st == MS_OK) st = model_alloc(m, &m->d_ids, R);
@@ -836,6 +858,7 @@ static ms_status run_layer(ms_ctx* c, ms_model* m, const ms_kv* kv, int li, int 
     p.pos = m->d_pos;
     p.seq = m->d_seq;
     p.kv = kv_view(kv, li);
+    p.xfrag = reinterpret_cast<const uint2*>(frag_in(m, 0, M));
     MS_CUDA(c, launch_proj(p, pl, s, pdl));
   }
   // 2. attention
@@ -874,6 +897,7 @@ static ms_status run_layer(ms_ctx* c, ms_model* m, const ms_kv* kv, int li, int 
     a.n_splits = splits;
     a.part = c->part;
     a.counters = c->counters;
+    a.out_frag = M <= 8 ? m->FATT : nullptr;
     MS_CUDA(c, launch_attention(a, s, pdl));
   }
   // 3. O projection + residual onto the normalised input
@@ -893,6 +917,8 @@ static ms_status run_layer(ms_ctx* c, ms_model* m, const ms_kv* kv, int li, int 
     p.resid_nstat = nstat;
     p.resid_ple = L.d.ple;
     p.out_stats = ys;
+    p.xfrag = M <= 8 ? reinterpret_cast<const uint2*>(m->FATT) : nullptr;
+    p.out_frag = frag_in(m, 1, M);
     MS_CUDA(c, launch_proj(p, pl, s, pdl));
   }
   // 4. gate | up + SwiGLU
@@ -910,6 +936,8 @@ static ms_status run_layer(ms_ctx* c, ms_model* m, const ms_kv* kv, int li, int 
     p.ldo = F;
     p.scale = L.d.scale[4];
     p.scale2 = L.d.scale[5];
+    p.xfrag = reinterpret_cast<const uint2*>(frag_in(m, 1, M));
+    p.out_frag = M <= 8 ? m->FH : nullptr;
     MS_CUDA(c, launch_proj(p, pl, s, pdl));
   }
   // 5. Down + residual
@@ -929,6 +957,8 @@ static ms_status run_layer(ms_ctx* c, ms_model* m, const ms_kv* kv, int li, int 
     p.resid_nstat = nstat;
     p.resid_ple = 1.f;
     p.out_stats = xs;
+    p.xfrag = M <= 8 ? reinterpret_cast<const uint2*>(m->FH) : nullptr;
+    p.out_frag = frag_in(m, 0, M);
     MS_CUDA(c, launch_proj(p, pl, s, pdl));
   }
   return MS_OK;
@@ -950,7 +980,7 @@ extern "C" ms_status ms_layer_forward(ms_ctx* c, const ms_model* mc, int layer, 
   MS_TRY(check_rows(c, m, kv, seq, pos, M));
   cudaStream_t s = pick(c, stream);
   MS_TRY(upload_rows(c, m, seq, pos, M, s));
-  MS_CUDA(c, launch_rowstats(m->S[0], x, m->hidden, M, m->hidden, s, false));
+  MS_CUDA(c, launch_rowstats(m->S[0], frag_in(m, 0, M), x, m->hidden, M, m->hidden, s, false));
   return run_layer(c, m, kv, layer, M, x, m->S[0], m->X[1], m->S[1], s, true);
 }
 
@@ -962,7 +992,7 @@ extern "C" ms_status ms_forward(ms_ctx* c, const ms_model* mc, float* x, ms_kv* 
   MS_TRY(check_rows(c, m, kv, seq, pos, M));
   cudaStream_t s = pick(c, stream);
   MS_TRY(upload_rows(c, m, seq, pos, M, s));
-  MS_CUDA(c, launch_rowstats(m->S[0], x, m->hidden, M, m->hidden, s, false));
+  MS_CUDA(c, launch_rowstats(m->S[0], frag_in(m, 0, M), x, m->hidden, M, m->hidden, s, false));
   for (int l = 0; l < m->n_layers; ++l)
     MS_TRY(run_layer(c, m, kv, l, M, x, m->S[0], m->X[1], m->S[1], s, true));
   return MS_OK;
@@ -1002,7 +1032,8 @@ extern "C" ms_status ms_embed(ms_ctx* c, const ms_model* mc, const int* ids, int
       return fail(c, MS_ERR_INVALID_ARG, "token id %d outside 0..%d", ids[r], m->vocab - 1);
   cudaStream_t s = pick(c, stream);
   MS_CUDA(c, cudaMemcpyAsync(m->d_ids, ids, M * sizeof(int), cudaMemcpyHostToDevice, s));
-  MS_CUDA(c, launch_embed_stats(x, m->S[0], m->lm_head, m->d_ids, M, m->hidden, m->vocab, s, false));
+  MS_CUDA(c, launch_embed_stats(x, m->S[0], frag_in(m, 0, M), m->lm_head, m->d_ids, M, m->hidden,
+                                m->vocab, s, false));
   return MS_OK;
 }
 
@@ -1015,13 +1046,14 @@ extern "C" ms_status ms_lm_head(ms_ctx* c, const ms_model* mc, const float* x, i
   if (M <= 0 || M > m->max_rows) return fail(c, MS_ERR_CAPACITY, "M=%d", M);
   if (logits && ((uintptr_t)logits & 15)) return fail(c, MS_ERR_ALIGN, "logits must be 16-byte aligned");
   cudaStream_t s = pick(c, stream);
-  MS_CUDA(c, launch_rowstats(m->S[1], x, m->hidden, M, m->hidden, s, false));
+  MS_CUDA(c, launch_rowstats(m->S[1], nullptr, x, m->hidden, M, m->hidden, s, false));
   return lm_head_launch(c, m, x, m->S[1], M, logits, argmax_out, s, true);
 }
 
 // One decode step on the device: d_ids / d_seq / d_pos -> d_next.
 static ms_status decode_body(ms_ctx* c, ms_model* m, const ms_kv* kv, int M, cudaStream_t s) {
-  MS_CUDA(c, launch_embed_stats(m->X[0], m->S[0], m->lm_head, m->d_ids, M, m->hidden, m->vocab, s, true));
+  MS_CUDA(c, launch_embed_stats(m->X[0], m->S[0], frag_in(m, 0, M), m->lm_head, m->d_ids, M,
+                                m->hidden, m->vocab, s, true));
   for (int l = 0; l < m->n_layers; ++l)
     MS_TRY(run_layer(c, m, kv, l, M, m->X[0], m->S[0], m->X[1], m->S[1], s, true));
   MS_TRY(lm_head_launch(c, m, m->X[0], m->S[0], M, nullptr, m->d_next, s, true));
@@ -1173,7 +1205,7 @@ extern "C" ms_status ms_prefill(ms_ctx* c, const ms_model* mc, ms_kv* kv, const 
       }
   }
   if (st == MS_OK && first_ids && n_keep) {
-    MS_CUDA(c, launch_rowstats(m->S[1], keep, m->hidden, n_keep, m->hidden, s, false));
+    MS_CUDA(c, launch_rowstats(m->S[1], nullptr, keep, m->hidden, n_keep, m->hidden, s, false));
     st = lm_head_launch(c, m, keep, m->S[1], n_keep, nullptr, m->d_next, s, true);
     std::vector<int> nxt(n_keep);
     if (st == MS_OK) {

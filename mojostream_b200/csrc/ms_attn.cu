@@ -150,7 +150,9 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnParams p) 
       A += ws[d] * f;
     }
     if (ns == 1) {
-      p.out[(size_t)m * p.ldo + (size_t)(hk * G + h) * HD + d] = A / L;
+      const int c = (hk * G + h) * HD + d;
+      p.out[(size_t)m * p.ldo + c] = A / L;
+      if (p.out_frag) frag_store(p.out_frag, p.ldo / 16, m, c, A / L);
     } else {
       float* ps = part_base + (size_t)h * ST;
       __stcg(ps + d, A);
@@ -203,7 +205,9 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnParams p) 
 #pragma unroll 8
     for (int sp = 0; sp < ns; ++sp)
       A += __ldcg(pr0 + ((size_t)sp * G + h) * ST + d) * wsm[h * p.n_splits + sp];
-    p.out[(size_t)m * p.ldo + (size_t)(hk * G + h) * HD + d] = A;
+    const int c = (hk * G + h) * HD + d;
+    p.out[(size_t)m * p.ldo + c] = A;
+    if (p.out_frag) frag_store(p.out_frag, p.ldo / 16, m, c, A);
   }
   if (threadIdx.x == 0) *ctr = 0;
 }

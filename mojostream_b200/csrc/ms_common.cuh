@@ -57,6 +57,22 @@ __device__ __forceinline__ void split_bf16(float v, uint32_t& hi, uint32_t& lo) 
   lo = bf16_bits(l);
 }
 
+// Activation rows in MMA-fragment layout ("fragment rows"): for a row block
+// of 4 rows (G = m / 4) and a 16-wide k-subtile ks, lane (g, t) of the B
+// operand holds {k 2t, 2t+1} and {k 2t+8, 2t+9} of row g (g < 4, bf16 hi
+// part) or row g - 4 (g >= 4, bf16 lo part).  Layout [G][ks][lane] x uint2,
+// i.e. 256 bytes per (G, ks): a projection's producer thread copies a whole
+// k-segment of it with one bulk copy.  Writers store 16-bit halves.
+__device__ __forceinline__ void frag_store(uint16_t* f, int ks_total, int m, int k, float v) {
+  uint32_t h, l;
+  split_bf16(v, h, l);
+  const int G = m >> 2, mm = m & 3, ks = k >> 4, kk = k & 15;
+  const int kp = kk >> 1, half = kk & 1, tq = kp & 3, reg = kp >> 2;
+  const size_t base = ((size_t)G * ks_total + ks) * 32;
+  f[((base + mm * 4 + tq) * 2 + reg) * 2 + half] = (uint16_t)h;
+  f[((base + (mm + 4) * 4 + tq) * 2 + reg) * 2 + half] = (uint16_t)l;
+}
+
 // Four bf16x2 A-fragment registers from one packed word of eight nibbles.
 // (0x4300 | n) is the bf16 of 128 + n; subtracting 136 gives n - 8 exactly.
 __device__ __forceinline__ void dequant_word(uint32_t q, uint32_t (&a)[4]) {

@@ -11,10 +11,12 @@
 //     through a 4-stage mbarrier ring.  The first stages are issued before
 //     griddepcontrol.wait: weights do not depend on the previous kernel, so
 //     under programmatic dependent launch their fetch overlaps its tail;
-//   * after the wait the consumers split the activations of the k-segment
-//     into bf16 hi | lo MMA fragments once (shared by the 8 tiles);
+//   * the activations arrive already in MMA-fragment layout (bf16 hi | lo,
+//     written by the kernel that produced them) with one more bulk copy
+//     right after the wait: no conversion pass on the critical path;
 //   * each warp dequantises its tile in registers (int4 -> bf16, exact) and
-//     runs mma.m16n8k16 with the 4 rows x {hi, lo} as the 8 B columns;
+//     runs mma.m16n8k16 with the 4 rows x {hi, lo} as the 8 B columns, over
+//     4 independent accumulator chains (one per 16-k subtile of a chunk);
 //   * RMSNorm and PLE are per-row scalars applied to the finished sums;
 //   * k-segments of one group (long K, or to fill the GPU) are summed by the
 //     last CTA of the group in k order: deterministic results.
@@ -42,8 +44,8 @@ __global__ void __launch_bounds__(kSThreads) gemv_stream_kernel(const GemvParams
   constexpr int MB = 4 * MG;
   extern __shared__ __align__(128) uint8_t dsm[];
   uint4* stages = reinterpret_cast<uint4*>(dsm);
-  uint2* sB = reinterpret_cast<uint2*>(dsm + kStages * kStageBytes);
-  __shared__ __align__(8) uint64_t full[kStages], empty[kStages];
+  uint2* sB = reinterpret_cast<uint2*>(dsm + kStages * kStageBytes);  // [G][ks][32]
+  __shared__ __align__(8) uint64_t full[kStages], empty[kStages], bready;
   __shared__ float s_fin[MB], s_fres[MB];
   __shared__ int s_last;
 
@@ -55,6 +57,7 @@ __global__ void __launch_bounds__(kSThreads) gemv_stream_kernel(const GemvParams
   const int c_end = min(nchunks, c_begin + seg);
   const int n_cta = c_end - c_begin;
   const int n_st = (n_cta + kStageChunks - 1) / kStageChunks;
+  const int ks_cta = n_cta * 4;  // 16-k subtiles of the segment
   const uint4* wg = p.w + (size_t)group * nchunks * kGroupTiles * kWarp;
 
   if (threadIdx.x == 0) {
@@ -62,6 +65,7 @@ __global__ void __launch_bounds__(kSThreads) gemv_stream_kernel(const GemvParams
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kSWarps);
     }
+    mbar_init(&bready, 1);
     mbar_fence_init();
   }
   __syncthreads();
@@ -70,18 +74,31 @@ __global__ void __launch_bounds__(kSThreads) gemv_stream_kernel(const GemvParams
   // ------------------------------------------------------------ producer --
   if (warp == kSWarps) {
     if (lane == 0) {
-      for (int j = 0; j < n_st; ++j) {
+      auto issue = [&](int j) {
         const int slot = j % kStages;
-        if (j >= kStages && !mbar_wait(&empty[slot], ((j / kStages) - 1) & 1)) {
-          atomicOr(p.err, kErrWaitTimeout);
-          break;  // consumers time out on the stages never issued
-        }
         const int c0 = c_begin + j * kStageChunks;
         const int nc = min(kStageChunks, c_end - c0);
         const uint32_t bytes = (uint32_t)nc * kGroupTiles * kWarp * 16;
         mbar_expect_tx(&full[slot], bytes);
         bulk_g2s(stages + (size_t)slot * kStageU4, wg + (size_t)c0 * kGroupTiles * kWarp, bytes,
                  &full[slot]);
+      };
+      const int first = min(n_st, kStages);
+      for (int j = 0; j < first; ++j) issue(j);  // weights: before the wait
+      pdl_wait();
+      // the k-segment's activation fragments, one copy per 4-row block
+      const int KS = p.K / 16;
+      const uint32_t gbytes = (uint32_t)ks_cta * kWarp * sizeof(uint2);
+      mbar_expect_tx(&bready, gbytes * MG);
+      for (int G = 0; G < MG; ++G)
+        bulk_g2s(sB + (size_t)G * ks_cta * kWarp, p.xfrag + ((size_t)G * KS + c_begin * 4) * kWarp,
+                 gbytes, &bready);
+      for (int j = first; j < n_st; ++j) {
+        if (!mbar_wait(&empty[j % kStages], ((j / kStages) - 1) & 1)) {
+          atomicOr(p.err, kErrWaitTimeout);
+          break;  // consumers time out on the stages never issued
+        }
+        issue(j);
       }
     }
     return;
@@ -115,50 +132,18 @@ __global__ void __launch_bounds__(kSThreads) gemv_stream_kernel(const GemvParams
       s_fres[m] = fres;
     }
   }
-  // activations of the k-segment -> bf16 hi | lo fragments [subtile][G][lane]
-  {
-    uint32_t* sBw = reinterpret_cast<uint32_t*>(sB);
-    const int k_base = c_begin * kChunkK;
-    const int items = n_cta * 4 * MB * 4;  // (subtile, row, quad of 4 k)
-#pragma unroll 4
-    for (int it = threadIdx.x; it < items; it += kSConsumers) {
-      const int q = it & 3;
-      const int ml = (it >> 2) % MB;
-      const int ks = (it >> 2) / MB;
-      uint32_t hi0 = 0, lo0 = 0, hi1 = 0, lo1 = 0;
-      if (ml < p.M) {
-        const float4 xv = *reinterpret_cast<const float4*>(p.x + (size_t)ml * p.ldx + k_base +
-                                                          ks * 16 + 4 * q);
-        uint32_t h0, l0, h1, l1, h2, l2, h3, l3;
-        split_bf16(xv.x, h0, l0);
-        split_bf16(xv.y, h1, l1);
-        split_bf16(xv.z, h2, l2);
-        split_bf16(xv.w, h3, l3);
-        hi0 = h0 | (h1 << 16);
-        lo0 = l0 | (l1 << 16);
-        hi1 = h2 | (h3 << 16);
-        lo1 = l2 | (l3 << 16);
-      }
-      // k pairs 2q (k 4q, 4q+1) and 2q+1 (k 4q+2, 4q+3) of the subtile
-      const int G = ml >> 2, mm = ml & 3;
-      const int row = (ks * MG + G) * kWarp;
-      const int kp0 = 2 * q, kp1 = 2 * q + 1;
-      sBw[(row + mm * 4 + (kp0 & 3)) * 2 + (kp0 >> 2)] = hi0;
-      sBw[(row + (mm + 4) * 4 + (kp0 & 3)) * 2 + (kp0 >> 2)] = lo0;
-      sBw[(row + mm * 4 + (kp1 & 3)) * 2 + (kp1 >> 2)] = hi1;
-      sBw[(row + (mm + 4) * 4 + (kp1 & 3)) * 2 + (kp1 >> 2)] = lo1;
-    }
-  }
-  bar_sync_n(1, kSConsumers);
 
-  float acc[MG][4];
+  // 4 accumulator chains x MG row blocks
+  float acc[4][MG][4];
 #pragma unroll
-  for (int G = 0; G < MG; ++G)
+  for (int s = 0; s < 4; ++s)
 #pragma unroll
-    for (int i = 0; i < 4; ++i) acc[G][i] = 0.f;
-  bool ok = true;
+    for (int G = 0; G < MG; ++G)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[s][G][i] = 0.f;
+  bool ok = mbar_wait(&bready, 0);
   int j = 0;
-  for (; j < n_st; ++j) {
+  for (; ok && j < n_st; ++j) {
     const int slot = j % kStages;
     if (!mbar_wait(&full[slot], (j / kStages) & 1)) {
       ok = false;
@@ -178,8 +163,8 @@ __global__ void __launch_bounds__(kSThreads) gemv_stream_kernel(const GemvParams
           dequant_word(words[s], a);
 #pragma unroll
           for (int G = 0; G < MG; ++G) {
-            const uint2 b = sB[((ks0 + s) * MG + G) * kWarp + lane];
-            mma_bf16_16816(acc[G], a, b.x, b.y);
+            const uint2 b = sB[((size_t)G * ks_cta + ks0 + s) * kWarp + lane];
+            mma_bf16_16816(acc[s][G], a, b.x, b.y);
           }
         }
       }
@@ -188,16 +173,21 @@ __global__ void __launch_bounds__(kSThreads) gemv_stream_kernel(const GemvParams
     if (lane == 0) mbar_arrive(&empty[slot]);
   }
   if (!ok) {
-    // a stage never arrived: report, let issued copies land, skip the output
+    // a copy never arrived: report, let issued copies land, skip the output
     if (lane == 0) atomicOr(p.err, kErrWaitTimeout);
-    for (int jj = j + 1; jj < n_st && jj < j + kStages; ++jj)
+    mbar_wait(&bready, 0);
+    for (int jj = j; jj < n_st && jj < j + kStages; ++jj)
       if (!mbar_wait(&full[jj % kStages], (jj / kStages) & 1)) break;
     return;
   }
+  float r[MG][4];
 #pragma unroll
   for (int G = 0; G < MG; ++G)
 #pragma unroll
-    for (int i = 0; i < 4; ++i) acc[G][i] += __shfl_xor_sync(0xffffffffu, acc[G][i], 2);
+    for (int i = 0; i < 4; ++i) {
+      const float v = (acc[0][G][i] + acc[1][G][i]) + (acc[2][G][i] + acc[3][G][i]);
+      r[G][i] = v + __shfl_xor_sync(0xffffffffu, v, 2);  // fold lo (cols 4-7) onto hi
+    }
   const int g = lane >> 2, tq = lane & 3;
   const bool tile_ok = tile < p.n_tiles;
 
@@ -208,8 +198,8 @@ __global__ void __launch_bounds__(kSThreads) gemv_stream_kernel(const GemvParams
 #pragma unroll
       for (int G = 0; G < MG; ++G) {
         const int mc = 4 * G + 2 * tq;
-        __stcg(reinterpret_cast<float2*>(my + g * MB + mc), make_float2(acc[G][0], acc[G][1]));
-        __stcg(reinterpret_cast<float2*>(my + (g + 8) * MB + mc), make_float2(acc[G][2], acc[G][3]));
+        __stcg(reinterpret_cast<float2*>(my + g * MB + mc), make_float2(r[G][0], r[G][1]));
+        __stcg(reinterpret_cast<float2*>(my + (g + 8) * MB + mc), make_float2(r[G][2], r[G][3]));
       }
     }
     __threadfence();
@@ -222,7 +212,7 @@ __global__ void __launch_bounds__(kSThreads) gemv_stream_kernel(const GemvParams
 #pragma unroll
       for (int G = 0; G < MG; ++G)
 #pragma unroll
-        for (int i = 0; i < 4; ++i) acc[G][i] = 0.f;
+        for (int i = 0; i < 4; ++i) r[G][i] = 0.f;
       for (int kk = 0; kk < p.ksplit; ++kk) {
         const float* pp = p.part + ((size_t)tile * p.ksplit + kk) * (kTileN * MB);
 #pragma unroll
@@ -230,10 +220,10 @@ __global__ void __launch_bounds__(kSThreads) gemv_stream_kernel(const GemvParams
           const int mc = 4 * G + 2 * tq;
           const float2 a = __ldcg(reinterpret_cast<const float2*>(pp + g * MB + mc));
           const float2 b = __ldcg(reinterpret_cast<const float2*>(pp + (g + 8) * MB + mc));
-          acc[G][0] += a.x;
-          acc[G][1] += a.y;
-          acc[G][2] += b.x;
-          acc[G][3] += b.y;
+          r[G][0] += a.x;
+          r[G][1] += a.y;
+          r[G][2] += b.x;
+          r[G][3] += b.y;
         }
       }
     }
@@ -250,7 +240,7 @@ __global__ void __launch_bounds__(kSThreads) gemv_stream_kernel(const GemvParams
       float sq = 0.f;
       if (tq < 2 && m < p.M) {
         const float f = s_fin[m];
-        epilogue_row(p, tile, g, m, acc[G][b] * f, acc[G][2 + b] * f, s_fres[m], sq);
+        epilogue_row(p, tile, g, m, r[G][b] * f, r[G][2 + b] * f, s_fres[m], sq);
       }
       if (p.epi == kEpiResid && p.out_stats) {
         sq += __shfl_xor_sync(0xffffffffu, sq, 4);
@@ -277,10 +267,10 @@ static cudaError_t launch_stream_t(const GemvParams& p, cudaStream_t s, bool pdl
   return cudaLaunchKernelEx(&cfg, gemv_stream_kernel<MG>, p);
 }
 
-// M <= 4 (MG 1) or M <= 8 (MG 2); the k-segment's fragments must fit in
-// shared memory next to the stage ring (kseg <= 64 chunks for MG 1).
+// M <= 4 (MG 1) or M <= 8 (MG 2); p.xfrag holds the input rows as fragments;
+// the k-segment's fragments must fit in shared memory next to the stage ring.
 cudaError_t launch_gemv_stream(const GemvParams& p, int mg, cudaStream_t s, bool pdl) {
-  if (p.M > 4 * mg || gemv_stream_smem(mg, p.kseg) > 200 * 1024 || p.kseg % kChunkK)
+  if (p.M > 4 * mg || !p.xfrag || gemv_stream_smem(mg, p.kseg) > 200 * 1024 || p.kseg % kChunkK)
     return cudaErrorInvalidConfiguration;
   if (mg == 1) return launch_stream_t<1>(p, s, pdl);
   if (mg == 2) return launch_stream_t<2>(p, s, pdl);

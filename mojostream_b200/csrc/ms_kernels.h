@@ -90,6 +90,11 @@ struct GemvParams {
   const int* pos;
   const int* seq;
   KvView kv;
+  // fragment rows (decode path, M <= 8): the input as MMA fragments
+  // [G][K/16][32] uint2, and an optional fragment copy of the output rows
+  // (width N; [G][N/16][32] uint2) for the next projection
+  const uint2* xfrag;
+  uint16_t* out_frag;
   // split-K scratch
   float* part;            // partial sums of k-segments
   int* counters;          // arrival tickets (reset by the last arrival)
@@ -106,6 +111,7 @@ struct AttnParams {
   const int* pos;
   int hd, n_heads, n_kv, window, chunk /* minimum positions per split */, n_splits, M;
   float scale;
+  uint16_t* out_frag;  // fragment rows of the output ([G][q_dim/16][32] uint2) or null
   float* part;    // [M][n_kv][n_splits][G][hd + 2]
   int* counters;  // [M][n_kv]
 };
@@ -136,9 +142,9 @@ cudaError_t prepare_attention();
 cudaError_t launch_lm_head(const LmHeadParams& p, cudaStream_t s, bool pdl);
 cudaError_t launch_repack(uint4* out, const uint8_t* const* src, const int* src_n, int n_src,
                           const int* perm, int n_tiles, int K, cudaStream_t s);
-cudaError_t launch_embed_stats(float* x, float* stats, const float* W, const int* ids, int M,
-                               int D, int V, cudaStream_t s, bool pdl);
-cudaError_t launch_rowstats(float* stats, const float* x, int ldx, int M, int D,
+cudaError_t launch_embed_stats(float* x, float* stats, uint16_t* frag, const float* W,
+                               const int* ids, int M, int D, int V, cudaStream_t s, bool pdl);
+cudaError_t launch_rowstats(float* stats, uint16_t* frag, const float* x, int ldx, int M, int D,
                             cudaStream_t s, bool pdl);
 cudaError_t launch_advance_step(int* ids, const int* next, int* pos, int* hist, int* step, int M,
                                 cudaStream_t s, bool pdl);
