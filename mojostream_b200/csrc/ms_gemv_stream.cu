@@ -26,9 +26,15 @@
 
 namespace ms {
 
-constexpr int kSWarps = kGroupTiles;                   // consumer warps = tiles per group
-constexpr int kSConsumers = kSWarps * kWarp;          // 256
+// Two consumer warps per tile (16 per CTA): warp w computes tile w % 8 over
+// chunks {2h, 2h+1} of every stage, h = w / 8.  Two warps per tile double the
+// instruction streams a scheduler can interleave (the dequant -> MMA chain
+// is latency-bound with one warp per tile).
+constexpr int kSHalves = 2;
+constexpr int kSWarps = kGroupTiles * kSHalves;       // consumer warps
+constexpr int kSConsumers = kSWarps * kWarp;          // 512
 constexpr int kSThreads = kSConsumers + kWarp;        // + producer warp
+constexpr int kSTileThreads = kGroupTiles * kWarp;    // one warp per tile (after the halves merge)
 constexpr int kStageChunks = 4;
 constexpr int kStages = 4;
 constexpr int kStageU4 = kStageChunks * kGroupTiles * kWarp;  // 1024 uint4 = 16 KB
@@ -40,17 +46,18 @@ size_t gemv_stream_smem(int mg, int kseg) {
 }
 
 template <int MG>
-__global__ void __launch_bounds__(kSThreads) gemv_stream_kernel(const GemvParams p) {
+__global__ void __launch_bounds__(kSThreads, 2) gemv_stream_kernel(const GemvParams p) {
   constexpr int MB = 4 * MG;
   extern __shared__ __align__(128) uint8_t dsm[];
   uint4* stages = reinterpret_cast<uint4*>(dsm);
   uint2* sB = reinterpret_cast<uint2*>(dsm + kStages * kStageBytes);  // [G][ks][32]
   __shared__ __align__(8) uint64_t full[kStages], empty[kStages], bready;
   __shared__ float s_fin[MB], s_fres[MB];
-  __shared__ int s_last;
+  __shared__ int s_last, s_bad;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int group = blockIdx.x, kidx = blockIdx.y;
+  if (threadIdx.x == 0) s_bad = 0;
   const int nchunks = p.K / kChunkK;
   const int seg = p.kseg / kChunkK;
   const int c_begin = kidx * seg;
@@ -106,7 +113,8 @@ __global__ void __launch_bounds__(kSThreads) gemv_stream_kernel(const GemvParams
 
   // ----------------------------------------------------------- consumers --
   pdl_wait();
-  const int tile = group * kGroupTiles + warp;
+  const int tl = warp & (kGroupTiles - 1), half = warp / kGroupTiles;
+  const int tile = group * kGroupTiles + tl;
   // per-row factors, used by the epilogue only
   if (warp < MB) {
     const int m = warp;
@@ -150,9 +158,10 @@ __global__ void __launch_bounds__(kSThreads) gemv_stream_kernel(const GemvParams
       break;
     }
     const int nc = min(kStageChunks, n_cta - j * kStageChunks);
-    const uint4* st = stages + (size_t)slot * kStageU4 + warp * kWarp + lane;
+    const uint4* st = stages + (size_t)slot * kStageU4 + tl * kWarp + lane;
 #pragma unroll
-    for (int cc = 0; cc < kStageChunks; ++cc) {
+    for (int c2 = 0; c2 < kStageChunks / kSHalves; ++c2) {
+      const int cc = half * (kStageChunks / kSHalves) + c2;
       if (cc < nc) {
         const uint4 wv = lds_u4(st + cc * kGroupTiles * kWarp);
         const uint32_t words[4] = {wv.x, wv.y, wv.z, wv.w};
@@ -173,12 +182,15 @@ __global__ void __launch_bounds__(kSThreads) gemv_stream_kernel(const GemvParams
     if (lane == 0) mbar_arrive(&empty[slot]);
   }
   if (!ok) {
-    // a copy never arrived: report, let issued copies land, skip the output
-    if (lane == 0) atomicOr(p.err, kErrWaitTimeout);
+    // a copy never arrived: report, let issued copies land (bounded), and
+    // make the whole CTA skip its output after the barriers below
+    if (lane == 0) {
+      atomicOr(p.err, kErrWaitTimeout);
+      s_bad = 1;
+    }
     mbar_wait(&bready, 0);
     for (int jj = j; jj < n_st && jj < j + kStages; ++jj)
       if (!mbar_wait(&full[jj % kStages], (jj / kStages) & 1)) break;
-    return;
   }
   float r[MG][4];
 #pragma unroll
@@ -190,6 +202,26 @@ __global__ void __launch_bounds__(kSThreads) gemv_stream_kernel(const GemvParams
     }
   const int g = lane >> 2, tq = lane & 3;
   const bool tile_ok = tile < p.n_tiles;
+
+  // ---- merge the two halves of each tile (half 0 + half 1, fixed order) ------
+  {
+    float* red = reinterpret_cast<float*>(stages);  // the stage ring is drained
+    bar_sync_n(1, kSConsumers);                     // every warp is past its last stage
+    if (half == 1 && tq < 2) {
+#pragma unroll
+      for (int G = 0; G < MG; ++G)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) red[((tl * MG + G) * 4 + i) * 64 + lane] = r[G][i];
+    }
+    bar_sync_n(1, kSConsumers);
+    if (half == 1 || s_bad) return;  // CTA-uniform after the barrier (s_bad)
+    if (tq < 2) {
+#pragma unroll
+      for (int G = 0; G < MG; ++G)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) r[G][i] += red[((tl * MG + G) * 4 + i) * 64 + lane];
+    }
+  }
 
   // ---- k-segments of the group: the last CTA sums the partials in k order --
   if (p.ksplit > 1) {
@@ -203,9 +235,9 @@ __global__ void __launch_bounds__(kSThreads) gemv_stream_kernel(const GemvParams
       }
     }
     __threadfence();
-    bar_sync_n(1, kSConsumers);
+    bar_sync_n(1, kSTileThreads);
     if (threadIdx.x == 0) s_last = (atomicAdd(p.counters + group, 1) == p.ksplit - 1);
-    bar_sync_n(1, kSConsumers);
+    bar_sync_n(1, kSTileThreads);
     if (!s_last) return;
     __threadfence();
     if (tq < 2) {
