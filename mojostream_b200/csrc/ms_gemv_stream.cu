@@ -178,11 +178,26 @@ __global__ void __launch_bounds__(kSThreads, 2) gemv_stream_kernel(const GemvPar
 #pragma unroll
       for (int i = 0; i < 4; ++i) acc[s][G][i] = 0.f;
   bool ok = true;
-  long g_first_unit = u_begin;  // first unit of the current group in this CTA
+  // group / stage index of the current unit, stepped without divisions (a
+  // 64-bit division per unit cost more than the unit's math)
+  int g = (int)(u_begin / S), s_idx = (int)(u_begin % S);
+  int g_first_s = s_idx;  // stage index at which this CTA entered group g
+  auto mma_chunk = [&](const uint4* st, const uint2* bs, int cc) {
+    const uint4 wv = lds_u4(st + cc * kGroupTiles * kWarp);
+    const uint32_t words[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+    for (int s = 0; s < 4; ++s) {
+      uint32_t a[4];
+      dequant_word(words[s], a);
+#pragma unroll
+      for (int G = 0; G < MG; ++G) {
+        const uint2 b = bs[(G * kUnitKs + cc * 4 + s) * kWarp];
+        mma_bf16_16816(acc[s][G], a, b.x, b.y);
+      }
+    }
+  };
   for (int j = 0; j < n_units; ++j) {
-    const long u = u_begin + j;
-    const int g = (int)(u / S), s_idx = (int)(u % S);
-    const int slot = j % kStages;
+    const int slot = j & (kStages - 1);
     if (ok && *reinterpret_cast<volatile int*>(&s_bad)) ok = false;  // another warp gave up
     if (ok && !mbar_wait(&full[slot], (j / kStages) & 1)) {
       ok = false;
@@ -192,33 +207,33 @@ __global__ void __launch_bounds__(kSThreads, 2) gemv_stream_kernel(const GemvPar
       }
     }
     if (ok) {
-      const int nc = min(kStageChunks, nchunks - s_idx * kStageChunks);
-      const uint4* st = stages + (size_t)slot * kStageU4 + tl * kWarp + lane;
-      const uint2* bs = sB + (size_t)slot * kBU2 + lane;
+      const uint4* st = stages + slot * kStageU4 + tl * kWarp + lane;
+      const uint2* bs = sB + slot * kBU2 + lane;
+      constexpr int kHalf = kStageChunks / kSHalves;
+      const int nc = nchunks - s_idx * kStageChunks;  // chunks left in the group
+      if (nc >= kStageChunks) {                        // full stage: no branches
 #pragma unroll
-      for (int c2 = 0; c2 < kStageChunks / kSHalves; ++c2) {
-        const int cc = half * (kStageChunks / kSHalves) + c2;
-        if (cc < nc) {
-          const uint4 wv = lds_u4(st + cc * kGroupTiles * kWarp);
-          const uint32_t words[4] = {wv.x, wv.y, wv.z, wv.w};
-#pragma unroll
-          for (int s = 0; s < 4; ++s) {
-            uint32_t a[4];
-            dequant_word(words[s], a);
-#pragma unroll
-            for (int G = 0; G < MG; ++G) {
-              const uint2 b = bs[((size_t)G * kUnitKs + cc * 4 + s) * kWarp];
-              mma_bf16_16816(acc[s][G], a, b.x, b.y);
-            }
-          }
-        }
+        for (int c2 = 0; c2 < kHalf; ++c2) mma_chunk(st, bs, half * kHalf + c2);
+      } else {
+        for (int c2 = 0; c2 < kHalf; ++c2)
+          if (half * kHalf + c2 < nc) mma_chunk(st, bs, half * kHalf + c2);
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[slot]);
     }
 
     // ---- leaving group g: flush it ------------------------------------------
-    const bool group_end = (j + 1 == n_units) || ((u + 1) % S == 0);
+    const bool last_of_group = (s_idx + 1 == S);
+    const bool group_end = (j + 1 == n_units) || last_of_group;
+    const bool whole = (g_first_s == 0) && last_of_group;
+    const int g_cur = g;
+    if (last_of_group) {
+      ++g;
+      s_idx = 0;
+      g_first_s = 0;
+    } else {
+      ++s_idx;
+    }
     if (!group_end) continue;
     float r[MG][4];
 #pragma unroll
@@ -238,9 +253,7 @@ __global__ void __launch_bounds__(kSThreads, 2) gemv_stream_kernel(const GemvPar
         for (int i = 0; i < 4; ++i) red[((tl * MG + G) * 4 + i) * kWarp + lane] = r[G][i];
     }
     bar_sync_n(1, kSConsumers);
-    const bool whole = (g_first_unit % S == 0) && ((u + 1) % S == 0);
-    const long next_first = u + 1;
-    const int tile = g * kGroupTiles + tl;
+    const int tile = g_cur * kGroupTiles + tl;
     // (after a timeout the sums are garbage but every warp still takes the
     // same barriers; the host sees the error word)
     if (half == 0) {
@@ -253,10 +266,10 @@ __global__ void __launch_bounds__(kSThreads, 2) gemv_stream_kernel(const GemvPar
       bool finish = whole;
       if (!whole) {
         // group shared with neighbouring CTAs: partial, ticket, last one sums
-        const int c_first = unit_owner((long)g * S, T, C);
-        const int c_last = unit_owner((long)(g + 1) * S - 1, T, C);
-        float* my = p.part + (((size_t)g * p.ksplit + (cta - c_first)) * kGroupTiles + tl) *
-                                 (kTileN * MB);
+        const int c_first = unit_owner((long)g_cur * S, T, C);
+        const int c_last = unit_owner((long)(g_cur + 1) * S - 1, T, C);
+        float* my = p.part +
+                    (((size_t)g_cur * p.ksplit + (cta - c_first)) * kGroupTiles + tl) * (kTileN * MB);
         if (tq < 2) {
 #pragma unroll
           for (int G = 0; G < MG; ++G) {
@@ -266,14 +279,17 @@ __global__ void __launch_bounds__(kSThreads, 2) gemv_stream_kernel(const GemvPar
                    make_float2(r[G][2], r[G][3]));
           }
         }
-        __threadfence();
+        // the barrier orders the warps' stores before thread 0's release fence
+        // and ticket; the last CTA's acquire fence orders its reads after
         bar_sync_n(2, kSTileThreads);
-        if (threadIdx.x == 0)
-          s_last = (atomicAdd(p.counters + g, 1) == c_last - c_first);
+        if (threadIdx.x == 0) {
+          asm volatile("fence.acq_rel.gpu;" ::: "memory");
+          s_last = (atomicAdd(p.counters + g_cur, 1) == c_last - c_first);
+          if (s_last) asm volatile("fence.acq_rel.gpu;" ::: "memory");
+        }
         bar_sync_n(2, kSTileThreads);
         finish = s_last;
         if (finish) {
-          __threadfence();
           if (tq < 2) {
 #pragma unroll
             for (int G = 0; G < MG; ++G)
@@ -281,7 +297,7 @@ __global__ void __launch_bounds__(kSThreads, 2) gemv_stream_kernel(const GemvPar
               for (int i = 0; i < 4; ++i) r[G][i] = 0.f;
             for (int c = 0; c <= c_last - c_first; ++c) {
               const float* pp =
-                  p.part + (((size_t)g * p.ksplit + c) * kGroupTiles + tl) * (kTileN * MB);
+                  p.part + (((size_t)g_cur * p.ksplit + c) * kGroupTiles + tl) * (kTileN * MB);
 #pragma unroll
               for (int G = 0; G < MG; ++G) {
                 const int mc = 4 * G + 2 * tq;
@@ -294,7 +310,7 @@ __global__ void __launch_bounds__(kSThreads, 2) gemv_stream_kernel(const GemvPar
               }
             }
           }
-          if (threadIdx.x == 0) p.counters[g] = 0;
+          if (threadIdx.x == 0) p.counters[g_cur] = 0;
         }
       }
       if (finish && tile < p.n_tiles) {
@@ -318,7 +334,6 @@ __global__ void __launch_bounds__(kSThreads, 2) gemv_stream_kernel(const GemvPar
         }
       }
     }
-    g_first_unit = next_first;
   }
   // fault path: let every copy the producer issued land before the CTA (and
   // its shared memory) goes away; bounded waits
