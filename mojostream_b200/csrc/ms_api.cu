@@ -404,31 +404,31 @@ extern "C" ms_status ms_q4_weight_destroy(ms_ctx* c, ms_q4_weight* w) {
 struct GemvPlan {
   bool dec;
   int mg, ch, kseg, ksplit;
-  int ctas;  // decode path: CTAs sharing the weight stream
 };
 
 static GemvPlan plan_gemv(const ms_ctx* c, int M, int K, int n_tiles) {
   GemvPlan pl{};
   const int chunks = K / kChunkK;
   if (M <= 8) {
-    // streaming kernel: one CTA per SM, each an equal slice of the stage
-    // units (tile group x 4 k-chunks); ksplit carries the partial slots a
-    // group shared by several CTAs needs
+    // streaming kernel: one CTA per (tile group, k-segment); about one CTA per
+    // SM, a k-segment of at most 40 chunks (mg 1) / 20 (mg 2) so stages +
+    // fragments stay near 100 KB and the next kernel's CTAs co-reside
     pl.dec = true;
     pl.mg = M <= 4 ? 1 : 2;
     const int mb = 4 * pl.mg;
     const int groups = padded_tiles(n_tiles) / kGroupTiles;
-    const long units = (long)groups * ((chunks + 3) / 4);
-    int ctas = (int)std::min<long>(c->sm_count, units);
-    int slots = gemv_stream_max_share(n_tiles, K, ctas);
-    while (ctas > 1 && ((size_t)groups * slots * kGroupTiles * kTileN * mb > c->part_floats ||
-                        (size_t)groups > c->n_counters)) {
-      ctas = (ctas + 1) / 2;
-      slots = gemv_stream_max_share(n_tiles, K, ctas);
-    }
-    pl.ctas = ctas;
-    pl.ksplit = slots;
-    pl.kseg = K;
+    const int seg_max = pl.mg == 1 ? 40 : 20;
+    int ksplit = std::max(1, (c->sm_count + groups / 2) / groups);
+    ksplit = std::max(ksplit, (chunks + seg_max - 1) / seg_max);
+    ksplit = std::min(ksplit, chunks);
+    auto fits = [&](int ks) {
+      return ks == 1 || ((size_t)padded_tiles(n_tiles) * ks * kTileN * mb <= c->part_floats &&
+                         (size_t)groups <= c->n_counters);
+    };
+    while (ksplit > 1 && !fits(ksplit)) --ksplit;
+    const int seg = (chunks + ksplit - 1) / ksplit;
+    pl.kseg = seg * kChunkK;
+    pl.ksplit = (chunks + seg - 1) / seg;
     pl.ch = 0;
     return pl;
   }
@@ -453,8 +453,7 @@ static GemvPlan plan_gemv(const ms_ctx* c, int M, int K, int n_tiles) {
 }
 
 static cudaError_t launch_proj(const GemvParams& p, const GemvPlan& pl, cudaStream_t s, bool pdl) {
-  return pl.dec ? launch_gemv_stream(p, pl.mg, pl.ctas, s, pdl)
-                : launch_gemv(p, pl.mg, pl.ch, s, pdl);
+  return pl.dec ? launch_gemv_stream(p, pl.mg, s, pdl) : launch_gemv(p, pl.mg, pl.ch, s, pdl);
 }
 
 static GemvParams gemv_base(ms_ctx* c, const uint4* w, int n_tiles, int K, int M,

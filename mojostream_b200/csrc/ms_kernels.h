@@ -132,11 +132,8 @@ struct LmHeadParams {
 
 // Launchers (return cudaGetLastError of the launch).
 cudaError_t launch_gemv(const GemvParams& p, int mg, int ch, cudaStream_t s, bool pdl);
-// Decode projection (M <= 8): `ctas` CTAs share the weight stream evenly;
-// p.ksplit = partial slots per tile group (gemv_stream_max_share).
-cudaError_t launch_gemv_stream(const GemvParams& p, int mg, int ctas, cudaStream_t s, bool pdl);
-int gemv_stream_max_share(int n_tiles, int K, int ctas);
-size_t gemv_stream_smem(int mg);
+cudaError_t launch_gemv_stream(const GemvParams& p, int mg, cudaStream_t s, bool pdl);
+size_t gemv_stream_smem(int mg, int kseg);
 cudaError_t launch_attention(const AttnParams& p, cudaStream_t s, bool pdl);
 int attention_block_positions(int head_dim);
 // one-time kernel attributes (dynamic shared memory above 48 KB)
