@@ -33,6 +33,8 @@ sys.path.insert(0, ROOT)
 
 PROMPT = 512
 BATCH = 4
+METRIC = "decode tokens/s (batch 4), Gemma-4-E4B-shaped Q4 model"
+WORKLOAD = "gemma4-e4b decode, batch 4 independent sequences, 512-token prompts"
 
 
 def parse():
@@ -43,6 +45,13 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--layers", type=int, default=42, help="(debug) fewer layers")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--case", default="decode", choices=["decode", "q4"],
+                    help="q4: the isolated Q4 projection (BASELINE configs[1] shapes), "
+                         "a small case for profiling")
+    ap.add_argument("--m", type=int, default=4)
+    ap.add_argument("--k", type=int, default=2560)
+    ap.add_argument("--n", type=int, default=20480)
+    ap.add_argument("--copies", type=int, default=8)
     return ap.parse_args()
 
 
@@ -217,6 +226,8 @@ def run_ours(args, ws, rank, local):
     s1.synchronize()
     lm_ms = s0.elapsed_time(s1) / n_rep
     lm_bytes = 4 * spec.hidden * spec.vocab + 4 * BATCH * spec.hidden
+    proj_ms, proj_bytes = time_q4(ctx, PROJ["M"], PROJ["K"], PROJ["N"], PROJ_COPIES, 3, 10)
+    proj_gbs = proj_bytes / (proj_ms / 1e3) / 1e9
 
     q4 = spec.q4_bytes()
     kv_read = BATCH * spec.kv_bytes_per_seq(PROMPT + args.warmup + args.steps // 2)
@@ -228,7 +239,7 @@ def run_ours(args, ws, rank, local):
     launches_per_step = 1 + 5 * spec.n_layers + (BATCH + 3) // 4 + 1
 
     result = {
-        "metric": "decode tokens/s (batch 4), Gemma-4-E4B-shaped Q4 model",
+        "metric": METRIC,
         "value": round(value, 2),
         "unit": "tokens/s",
         "n_gpus": ws,
@@ -241,7 +252,7 @@ def run_ours(args, ws, rank, local):
         "dtype": "int4 weights x fp32 activations (bf16x2 split on tensor cores), fp32 lm_head",
         "data": "synthetic (seeded random Q4 weights, N(0,0.02) fp32 lm_head, seeded token ids)",
         "config": {
-            "workload": "gemma4-e4b decode, batch 4 independent sequences, 512-token prompts",
+            "workload": WORKLOAD,
             "layers": spec.n_layers, "hidden": spec.hidden, "vocab": spec.vocab,
             "batch": BATCH, "prompt": PROMPT, "positions": [PROMPT + args.warmup,
                                                             PROMPT + args.warmup + args.steps],
@@ -254,12 +265,20 @@ def run_ours(args, ws, rank, local):
                 "wall_s": round(wall_e2e, 4)},
         "gpu_launches": launches_per_step * args.steps,
         "roofline": {
+            "kernel": "gemv_stream_kernel (Q4 projection, M 4, gate|up K 2560 x N 20480)",
+            "bound": "hbm", "achieved": round(proj_gbs, 1), "peak": hbm, "unit": "GB/s",
+            "frac": round(proj_gbs / hbm, 4),
+            "traffic": profile_traffic("gemv_stream_kernel"),
+            "algorithmic_bytes": proj_bytes, "peak_source": peak_kind,
+            "launch_ms": round(proj_ms, 5),
+        },
+        "roofline_lm_head": {
             "kernel": "lm_head_kernel (fp32 [2560 x 262144], argmax fused)",
             "bound": "hbm", "achieved": round(lm_bytes / (lm_ms / 1e3) / 1e9, 1),
             "peak": hbm, "unit": "GB/s",
             "frac": round(lm_bytes / (lm_ms / 1e3) / 1e9 / hbm, 4),
             "traffic": profile_traffic("lm_head_kernel"),
-            "peak_source": peak_kind,
+            "algorithmic_bytes": lm_bytes, "peak_source": peak_kind,
             "launch_ms": round(lm_ms, 4),
         },
         "step_roofline": {
@@ -271,7 +290,7 @@ def run_ours(args, ws, rank, local):
         "first_ids": first[:BATCH],
     }
     if rank == 0 and not args.no_cpu_baseline:
-        result["cpu_baseline"] = cpu_baseline(spec, model, ctx)
+        result["cpu_baseline"] = cpu_baseline(spec)
     if rank == 0:
         print(json.dumps(result), flush=True)
     if ws > 1:
@@ -280,11 +299,27 @@ def run_ours(args, ws, rank, local):
 
 
 # ---------------------------------------------------------- CPU baseline --
-def oracle_e4b(spec, weights_np, positions, seed=5):
-    """Oracle model with KV caches filled with seeded values for positions
-    below `positions` (the sample times decode steps, not the prefill)."""
+# The reference's CPU path is timed on a proportional sample of a decode step:
+# 6 of the 42 layers (5 sliding + 1 full, the model's own 5:1 pattern) and
+# 1/7 of the lm_head columns, i.e. 1/7 of every kind of work in a step; the
+# step time is 7 x the sample time.  A full E4B step is ~3 s on one core, so
+# the sample keeps the reference arm's K + W steps within a couple of minutes.
+SAMPLE_FRAC = 7
+
+
+def sample_spec(spec):
+    from mojostream_b200.model import e4b_spec
+    return e4b_spec(n_layers=spec.n_layers // SAMPLE_FRAC, vocab=spec.vocab // SAMPLE_FRAC)
+
+
+def oracle_sample(spec, positions, seed=5):
+    """Oracle model of the sample spec (seeded weights) with KV caches filled
+    with seeded values below `positions` (the sample times decode steps, not
+    the prefill)."""
+    from mojostream_b200.model import synth_weights
     from oracle import oracle
-    om = oracle.OracleModel(spec, weights_np, BATCH, positions + 256, slide_cap=1024)
+    wn = synth_weights(spec, seed=1234)
+    om = oracle.OracleModel(spec, wn, BATCH, positions + 1024, slide_cap=1024)
     rng = np.random.default_rng(seed)
     for li in range(spec.n_layers):
         k, v = om.kv_arrays(li)
@@ -294,15 +329,10 @@ def oracle_e4b(spec, weights_np, positions, seed=5):
     return om
 
 
-def host_weights(spec, w_dev):
-    from mojostream_b200.model import LayerWeights, ModelWeights
-    layers = [LayerWeights(l.ple, l.scales, [m.cpu().numpy() for m in l.mats]) for l in w_dev.layers]
-    return ModelWeights(layers, w_dev.lm_head.cpu().numpy(), w_dev.final_gamma.cpu().numpy())
-
-
 def time_oracle_steps(om, n_steps, start_pos, budget_s=None):
+    """Times n_steps sampled decode steps; returns (steps done, seconds)."""
     rng = np.random.default_rng(1)
-    ids = rng.integers(0, 262144, size=BATCH).tolist()
+    ids = rng.integers(0, om.spec.vocab, size=BATCH).tolist()
     t0 = time.perf_counter()
     done = 0
     for i in range(n_steps):
@@ -315,53 +345,107 @@ def time_oracle_steps(om, n_steps, start_pos, budget_s=None):
     return done, time.perf_counter() - t0
 
 
-def cpu_baseline(spec, model, ctx, budget_s=20.0):
-    import torch
-    from mojostream_b200.model import synth_weights_device
-    w = synth_weights_device(spec, seed=1234)
-    wn = host_weights(spec, w)
-    del w
-    torch.cuda.empty_cache()
-    om = oracle_e4b(spec, wn, PROMPT)
-    done, dt = time_oracle_steps(om, 1000, PROMPT, budget_s=budget_s)
-    return {"value": round(BATCH * done / dt, 3), "unit": "tokens/s", "cores": 1,
+SAMPLE_NOTE = ("each step: 6 of 42 layers (5 sliding + 1 full) and 1/7 of the lm_head "
+               "columns at batch 4, step time = 7 x sample time; the reference's Q4 "
+               "matmul threads over 64-row blocks, so batch 4 runs on 1 thread")
+
+
+def cpu_baseline(spec, budget_s=20.0):
+    sspec = sample_spec(spec)
+    om = oracle_sample(sspec, PROMPT)
+    time_oracle_steps(om, 1, PROMPT)
+    done, dt = time_oracle_steps(om, 1000, PROMPT + 1, budget_s=budget_s)
+    step_s = SAMPLE_FRAC * dt / done
+    return {"value": round(BATCH / step_s, 4), "unit": "tokens/s", "cores": 1,
             "kind": "port",
-            "sample": f"{done} decode steps x {BATCH} sequences at positions {PROMPT}+ "
-                      f"(KV pre-filled with seeded values), {dt:.1f} s; the reference's "
-                      "algorithm threads over 64-row blocks, so batch 4 runs on 1 thread"}
+            "sample": f"{done} sampled decode steps at positions {PROMPT + 1}+ (KV pre-filled "
+                      f"with seeded values), {dt:.1f} s; " + SAMPLE_NOTE}
 
 
 def run_reference(args, ws, rank, local):
-    """The reference's CPU path (C port) on the host cores, rank 0 only."""
+    """The reference's CPU path (C restatement) on the host cores, rank 0 only."""
     if rank != 0:
         return
-    from mojostream_b200.model import e4b_spec, synth_weights
+    from mojostream_b200.model import e4b_spec
     spec = e4b_spec(n_layers=args.layers)
-    wn = synth_weights(spec, seed=1234)
-    om = oracle_e4b(spec, wn, PROMPT)
+    sspec = sample_spec(spec)
+    om = oracle_sample(sspec, PROMPT)
     time_oracle_steps(om, args.warmup, PROMPT)
     done, dt = time_oracle_steps(om, args.steps, PROMPT + args.warmup)
-    v = BATCH * done / dt
+    step_s = SAMPLE_FRAC * dt / done
+    v = BATCH / step_s
     print(json.dumps({
         "impl": "reference",
-        "metric": "decode tokens/s (batch 4), Gemma-4-E4B-shaped Q4 model",
-        "value": round(v, 3), "unit": "tokens/s", "n_gpus": ws, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(1e3 * dt / done, 2),
+        "metric": METRIC,
+        "value": round(v, 4), "unit": "tokens/s", "n_gpus": ws, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(1e3 * step_s, 2),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "fp32", "data": "synthetic (seeded)",
-        "config": {"workload": "gemma4-e4b decode, batch 4 independent sequences, 512-token prompts",
-                   "layers": spec.n_layers, "batch": BATCH},
-        "cpu_baseline": {"value": round(v, 3), "unit": "tokens/s", "cores": 1, "kind": "port",
-                         "sample": f"{done} decode steps x {BATCH} sequences (KV pre-filled)"},
-        "e2e": {"value": round(v, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+        "config": {"workload": WORKLOAD, "layers": spec.n_layers, "batch": BATCH},
+        "cpu_baseline": {"value": round(v, 4), "unit": "tokens/s", "cores": 1, "kind": "port",
+                         "sample": f"{done} sampled decode steps; " + SAMPLE_NOTE},
+        "e2e": {"value": round(v, 4), "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }), flush=True)
+
+
+def time_q4(ctx, M, K, N, copies, warmup, reps):
+    """Average time of one ms_q4_gemm launch (CUDA events on the launching
+    stream) cycling over `copies` distinct weights, so that the weights
+    streamed between two uses of the same one exceed L2.  Returns (ms, bytes
+    per launch: packed weights + fp32 input and output rows)."""
+    import torch
+    from mojostream_b200.runtime import Q4Weight
+    g = torch.Generator(device="cuda").manual_seed(3)
+    ws = []
+    for _ in range(copies):
+        w = torch.randint(0, 256, (K, N // 2), dtype=torch.uint8, device="cuda", generator=g)
+        ws.append(Q4Weight(ctx, w, K, N, 0.01))
+        del w
+    x = torch.randn((M, K), device="cuda", generator=g)
+    y = torch.empty((M, N), device="cuda")
+    for _ in range(warmup):
+        for q in ws:
+            q.gemm(x, y)  # launched on torch's current stream
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        for q in ws:
+            q.gemm(x, y)
+    e1.record()
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / (reps * copies)
+    for q in ws:
+        q.close()
+    return ms, K * N // 2 + 4 * M * (K + N)
+
+
+# The projection shape the bench's roofline line is quoted on: the fused
+# gate|up matrix of an E4B layer (the largest of a decode step).
+PROJ = dict(M=BATCH, K=2560, N=2 * 10240)
+PROJ_COPIES = 8   # 8 x 26 MB > L2
+
+
+def run_q4_case(args):
+    """The isolated Q4 projection (a small case, e.g. for ncu captures)."""
+    import torch
+    from mojostream_b200.runtime import Context
+    torch.cuda.set_device(0)
+    ctx = Context(0)
+    ms, nbytes = time_q4(ctx, args.m, args.k, args.n, args.copies, args.warmup, args.steps)
+    hbm, _, kind = measured_peaks()
+    print(json.dumps({"case": "q4", "M": args.m, "K": args.k, "N": args.n, "copies": args.copies,
+                      "ms": round(ms, 5), "gbs": round(nbytes / ms / 1e6, 1), "peak": hbm,
+                      "peak_source": kind, "frac": round(nbytes / ms / 1e6 / hbm, 4)}), flush=True)
 
 
 def main():
     args = parse()
     ws, rank, local = dist_setup(args)
-    if args.impl == "reference":
+    if args.case == "q4":
+        run_q4_case(args)
+    elif args.impl == "reference":
         run_reference(args, ws, rank, local)
     else:
         run_ours(args, ws, rank, local)
