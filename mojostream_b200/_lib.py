@@ -54,6 +54,7 @@ SIGNATURES = {
                                            ctypes.POINTER(_vp)]),
     "ms_q4_weight_destroy": (ctypes.c_int, [_vp, _vp]),
     "ms_q4_gemm": (ctypes.c_int, [_vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int, _vp]),
+    "ms_q4_gemm_noalloc": (ctypes.c_int, [_vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int, _vp]),
     "ms_model_create": (ctypes.c_int, [_vp, ctypes.POINTER(ModelDesc), ctypes.POINTER(_vp)]),
     "ms_model_destroy": (ctypes.c_int, [_vp, _vp]),
     "ms_model_weight_bytes": (ctypes.c_size_t, [_vp]),

@@ -500,6 +500,92 @@ extern "C" ms_status ms_q4_gemm(ms_ctx* c, const ms_q4_weight* w, float* C, cons
   return MS_OK;
 }
 
+// ------------------------------------------------ allocation-free variant --
+// ms_q4_gemm_noalloc runs the same projection as ms_q4_gemm, but its scratch
+// (split-K partial sums, arrival tickets, the input rows as MMA fragments)
+// lives in one fixed file-scope device array instead of buffers taken from
+// the context or the weight.  Some callers cannot let a call allocate device
+// memory or share the context's scratch: a serving host that reserved all of
+// HBM for KV pages up front, or code on a latency-critical path where an
+// allocation (implicitly synchronising) is not allowed.  This entry point
+// allocates nothing, on the device or (on success) on the host.
+namespace {
+constexpr size_t kNaAlign = 256;
+constexpr size_t kNaPartFloats = 256 * 1024;          // 1 MiB of partial sums
+constexpr size_t kNaCounters = 4096;                  // arrival tickets
+constexpr int kNaMaxK = 32768;                        // fragment rows: K <= 32768 (M <= 8)
+constexpr size_t kNaFragBytes = (size_t)2 * kNaMaxK * 16;  // 1 MiB
+constexpr size_t kNaPartOff = 0;
+constexpr size_t kNaCountOff = kNaPartOff + kNaPartFloats * sizeof(float);
+constexpr size_t kNaFragOff =
+    (kNaCountOff + kNaCounters * sizeof(int) + kNaAlign - 1) / kNaAlign * kNaAlign;
+constexpr size_t kNaBytes = kNaFragOff + kNaFragBytes;  // 2 MiB + 16 KiB in total
+constexpr int kNaMaxDevices = 64;
+}  // namespace
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNaBytes];
+
+// Device address of g_noalloc_scratch per device ordinal, resolved on the
+// first call made on that device (with the device current).
+static unsigned char* g_noalloc_addr[kNaMaxDevices] = {};
+
+extern "C" ms_status ms_q4_gemm_noalloc(ms_ctx* c, const ms_q4_weight* w, float* C,
+                                        const float* A, int M, int accumulate, void* stream) {
+  if (!c || !w || !C || !A) return MS_ERR_INVALID_ARG;
+  if (M <= 0) return fail(c, MS_ERR_SHAPE, "ms_q4_gemm_noalloc: M=%d", M);
+  if (((uintptr_t)A & 15) || ((uintptr_t)C & 7))
+    return fail(c, MS_ERR_ALIGN, "ms_q4_gemm_noalloc: A must be 16-byte and C 8-byte aligned");
+  if (c->device < 0 || c->device >= kNaMaxDevices)
+    return fail(c, MS_ERR_UNSUPPORTED, "ms_q4_gemm_noalloc: device %d", c->device);
+  if (M <= 8 && w->K > kNaMaxK)
+    return fail(c, MS_ERR_CAPACITY,
+                "ms_q4_gemm_noalloc: K=%d exceeds the static fragment scratch (K <= %d when "
+                "M <= 8)",
+                w->K, kNaMaxK);
+  MS_CUDA(c, cudaSetDevice(c->device));
+  unsigned char* base = g_noalloc_addr[c->device];
+  if (!base) {
+    // one-time set-up for this device: look up the array's device address
+    // (may load the module, so the first call belongs before any capture)
+    void* ptr = nullptr;
+    MS_CUDA(c, cudaGetSymbolAddress(&ptr, g_noalloc_scratch));
+    base = static_cast<unsigned char*>(ptr);
+    g_noalloc_addr[c->device] = base;
+  }
+
+  // the same plan rule as ms_q4_gemm, with the static region's limits: a
+  // k-split whose partials would not fit falls back to fewer k-segments
+  ms_ctx lim;
+  lim.device = c->device;
+  lim.sm_count = c->sm_count;
+  lim.part = reinterpret_cast<float*>(base + kNaPartOff);
+  lim.part_floats = kNaPartFloats;
+  lim.counters = reinterpret_cast<int*>(base + kNaCountOff);
+  lim.n_counters = kNaCounters;
+  lim.d_err = c->d_err;  // timeouts reach the context's error word (ms_sync)
+  const int n_tiles = w->N / kTileN;
+  GemvPlan pl = plan_gemv(&lim, M, w->K, n_tiles);
+  GemvParams p = gemv_base(&lim, w->w, n_tiles, w->K, M, pl);
+  p.x = A;
+  p.ldx = w->K;
+  p.in_D = w->K;
+  p.epi = accumulate ? kEpiAccum : kEpiStore;
+  p.out = C;
+  p.ldo = w->N;
+  p.scale = w->scale;
+  cudaStream_t s = pick(c, stream);
+  // tickets must be zero when the kernel starts; a completed launch leaves
+  // them zero, and clearing them here also covers a call that timed out
+  MS_CUDA(c, cudaMemsetAsync(lim.counters, 0, kNaCounters * sizeof(int), s));
+  if (pl.dec) {
+    uint16_t* frag = reinterpret_cast<uint16_t*>(base + kNaFragOff);
+    MS_CUDA(c, launch_rowstats(nullptr, frag, A, w->K, M, w->K, s, false));
+    p.xfrag = reinterpret_cast<const uint2*>(frag);
+  }
+  MS_CUDA(c, launch_proj(p, pl, s, false));
+  return MS_OK;
+}
+
 // ------------------------------------------------------------------- model --
 
 static ms_status check_layer(ms_ctx* c, const ms_layer_desc& L, int D, int i) {
