@@ -94,21 +94,21 @@ MS_API ms_status ms_q4_weight_destroy(ms_ctx *ctx, ms_q4_weight *w);
  * A, C: device pointers, row-major, 8-byte aligned. */
 MS_API ms_status ms_q4_gemm(ms_ctx *ctx, const ms_q4_weight *w, float *C, const float *A, int M,
                      int accumulate, void *stream);
-/* No counterpart in the reference.  The same projection as ms_q4_gemm for
- * callers that cannot have a call allocate device memory or use the
- * context's scratch (for example a host that reserved all of HBM for its KV
- * pages, or a path where an implicitly synchronising allocation is not
- * allowed).  It allocates nothing: its scratch is one fixed device array of
- * 2 MiB + 16 KiB inside the library (split-K partials, arrival tickets, and
- * the input rows as MMA fragments).
- *   - Limit: K <= 32768 when M <= 8 (fragment rows), else MS_ERR_CAPACITY.
- *     Larger k-splits than the partials region holds fall back to fewer
- *     k-segments, as in ms_q4_gemm.
+/* No counterpart in the reference.  The same projection as ms_q4_gemm (same
+ * plan, same results) for callers that cannot have a call allocate device
+ * memory or use the context's scratch (for example a host that reserved all
+ * of HBM for its KV pages, or a path where an implicitly synchronising
+ * allocation is not allowed).  It allocates nothing: its scratch is one fixed
+ * device array of 1 MiB + 16 KiB inside the library (split-K partial sums and
+ * arrival tickets).
+ *   - Limit: the plan's partial sums and tickets must fit (262144 floats,
+ *     4096 tickets), else MS_ERR_CAPACITY with both sizes in the message;
+ *     e.g. every projection of the E4B model (K <= 10240) at M <= 4 fits.
  *   - The first call on each device looks up the array's device address
  *     (cudaGetSymbolAddress, which may load the module): make that first
  *     call before any stream capture.
- *   - The arrival tickets must be zero at launch; the call clears them on
- *     `stream` before its kernel.
+ *   - The arrival tickets must be zero at launch; the call clears the ones
+ *     it uses on `stream` before its kernel.
  *   - The scratch is shared by every call on the device: calls that overlap
  *     in time (other streams, other threads, other contexts) race; order
  *     them on one stream.

@@ -74,10 +74,6 @@ struct ms_model {
   float* Q = nullptr;
   float* ATT = nullptr;
   float* H = nullptr;
-  // the same rows as MMA fragments for decode batches (M <= 8): X[0], X[1], ATT, H
-  uint16_t* FX[2] = {nullptr, nullptr};
-  uint16_t* FATT = nullptr;
-  uint16_t* FH = nullptr;
   int* d_seq = nullptr;
   int* d_pos = nullptr;
   int* d_ids = nullptr;
@@ -107,7 +103,6 @@ struct ms_q4_weight {
   int K = 0, N = 0;
   float scale = 1.f;
   uint4* w = nullptr;
-  uint16_t* frag = nullptr;  // the input rows as MMA fragments (decode path)
 };
 
 // ----------------------------------------------------------------- errors --
@@ -147,7 +142,6 @@ static size_t q4_u4(int K, int n_tiles) {
 }
 
 // Fragment rows of buffer X[i] when the call takes the decode path (M <= 8).
-static uint16_t* frag_in(ms_model* m, int i, int M) { return M <= 8 ? m->FX[i] : nullptr; }
 
 // Error bits the kernels leave on the device (a bounded wait that ran out).
 // Reading them needs the stream idle; callers use it after a synchronize.
@@ -373,8 +367,7 @@ extern "C" ms_status ms_q4_weight_create(ms_ctx* c, const uint8_t* w_rx, int K, 
   w->K = K;
   w->N = N;
   w->scale = scale;
-  if (dev_alloc(c, (void**)&w->w, q4_u4(K, N / kTileN) * sizeof(uint4)) != MS_OK ||
-      dev_alloc(c, (void**)&w->frag, (size_t)2 * K * 16) != MS_OK) {
+  if (dev_alloc(c, (void**)&w->w, q4_u4(K, N / kTileN) * sizeof(uint4)) != MS_OK) {
     cudaFree(w->w);
     delete w;
     return MS_ERR_OOM;
@@ -382,7 +375,6 @@ extern "C" ms_status ms_q4_weight_create(ms_ctx* c, const uint8_t* w_rx, int K, 
   ms_status st = repack(c, w->w, {w_rx}, {N}, K, identity_perm(N));
   if (st != MS_OK) {
     cudaFree(w->w);
-    cudaFree(w->frag);
     delete w;
     return st;
   }
@@ -394,7 +386,6 @@ extern "C" ms_status ms_q4_weight_destroy(ms_ctx* c, ms_q4_weight* w) {
   if (!c || !w) return MS_ERR_INVALID_ARG;
   cudaStreamSynchronize(c->stream);
   cudaFree(w->w);
-  cudaFree(w->frag);
   delete w;
   return MS_OK;
 }
@@ -492,34 +483,24 @@ extern "C" ms_status ms_q4_gemm(ms_ctx* c, const ms_q4_weight* w, float* C, cons
   p.ldo = w->N;
   p.scale = w->scale;
   cudaStream_t s = pick(c, stream);
-  if (pl.dec) {  // the streaming kernel reads its rows as MMA fragments
-    MS_CUDA(c, launch_rowstats(nullptr, w->frag, A, w->K, M, w->K, s, false));
-    p.xfrag = reinterpret_cast<const uint2*>(w->frag);
-  }
   MS_CUDA(c, launch_proj(p, pl, s, false));
   return MS_OK;
 }
 
 // ------------------------------------------------ allocation-free variant --
-// ms_q4_gemm_noalloc runs the same projection as ms_q4_gemm, but its scratch
-// (split-K partial sums, arrival tickets, the input rows as MMA fragments)
-// lives in one fixed file-scope device array instead of buffers taken from
-// the context or the weight.  Some callers cannot let a call allocate device
-// memory or share the context's scratch: a serving host that reserved all of
-// HBM for KV pages up front, or code on a latency-critical path where an
-// allocation (implicitly synchronising) is not allowed.  This entry point
-// allocates nothing, on the device or (on success) on the host.
+// ms_q4_gemm_noalloc runs the same projection as ms_q4_gemm (same plan, same
+// kernels, the same results), but its scratch (split-K partial sums and
+// arrival tickets) lives in one fixed file-scope device array instead of the
+// context's buffers.  Some callers cannot let a call allocate device memory
+// or share the context's scratch: a serving host that reserved all of HBM for
+// KV pages up front, or code on a latency-critical path where an allocation
+// (implicitly synchronising) is not allowed.  This entry point allocates
+// nothing, on the device or (on success) on the host.
 namespace {
-constexpr size_t kNaAlign = 256;
-constexpr size_t kNaPartFloats = 256 * 1024;          // 1 MiB of partial sums
-constexpr size_t kNaCounters = 4096;                  // arrival tickets
-constexpr int kNaMaxK = 32768;                        // fragment rows: K <= 32768 (M <= 8)
-constexpr size_t kNaFragBytes = (size_t)2 * kNaMaxK * 16;  // 1 MiB
-constexpr size_t kNaPartOff = 0;
-constexpr size_t kNaCountOff = kNaPartOff + kNaPartFloats * sizeof(float);
-constexpr size_t kNaFragOff =
-    (kNaCountOff + kNaCounters * sizeof(int) + kNaAlign - 1) / kNaAlign * kNaAlign;
-constexpr size_t kNaBytes = kNaFragOff + kNaFragBytes;  // 2 MiB + 16 KiB in total
+constexpr size_t kNaPartFloats = 256 * 1024;  // 1 MiB of partial sums
+constexpr size_t kNaCounters = 4096;          // arrival tickets
+constexpr size_t kNaCountOff = kNaPartFloats * sizeof(float);
+constexpr size_t kNaBytes = kNaCountOff + kNaCounters * sizeof(int);  // 1 MiB + 16 KiB
 constexpr int kNaMaxDevices = 64;
 }  // namespace
 
@@ -529,6 +510,23 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kNaBytes];
 // first call made on that device (with the device current).
 static unsigned char* g_noalloc_addr[kNaMaxDevices] = {};
 
+// Partial-sum floats and tickets a projection plan uses (0 without a k-split).
+static void plan_scratch(const GemvPlan& pl, int M, int n_tiles, size_t* floats,
+                         size_t* tickets) {
+  *floats = 0;
+  *tickets = 0;
+  if (pl.ksplit <= 1) return;
+  const int mb = 4 * pl.mg;
+  if (pl.dec) {
+    *floats = (size_t)padded_tiles(n_tiles) * pl.ksplit * kTileN * mb;
+    *tickets = (size_t)padded_tiles(n_tiles) / kGroupTiles;
+  } else {
+    const size_t base = (size_t)((M + mb - 1) / mb) * ((n_tiles + 3) / 4);
+    *floats = base * pl.ksplit * 4 * kTileN * mb;
+    *tickets = base;
+  }
+}
+
 extern "C" ms_status ms_q4_gemm_noalloc(ms_ctx* c, const ms_q4_weight* w, float* C,
                                         const float* A, int M, int accumulate, void* stream) {
   if (!c || !w || !C || !A) return MS_ERR_INVALID_ARG;
@@ -537,11 +535,15 @@ extern "C" ms_status ms_q4_gemm_noalloc(ms_ctx* c, const ms_q4_weight* w, float*
     return fail(c, MS_ERR_ALIGN, "ms_q4_gemm_noalloc: A must be 16-byte and C 8-byte aligned");
   if (c->device < 0 || c->device >= kNaMaxDevices)
     return fail(c, MS_ERR_UNSUPPORTED, "ms_q4_gemm_noalloc: device %d", c->device);
-  if (M <= 8 && w->K > kNaMaxK)
+  const int n_tiles = w->N / kTileN;
+  const GemvPlan pl = plan_gemv(c, M, w->K, n_tiles);  // the plan ms_q4_gemm uses
+  size_t need_floats = 0, need_tickets = 0;
+  plan_scratch(pl, M, n_tiles, &need_floats, &need_tickets);
+  if (need_floats > kNaPartFloats || need_tickets > kNaCounters)
     return fail(c, MS_ERR_CAPACITY,
-                "ms_q4_gemm_noalloc: K=%d exceeds the static fragment scratch (K <= %d when "
-                "M <= 8)",
-                w->K, kNaMaxK);
+                "ms_q4_gemm_noalloc: M=%d K=%d N=%d needs %zu partial floats and %zu tickets; "
+                "the static scratch holds %zu and %zu",
+                M, w->K, w->N, need_floats, need_tickets, kNaPartFloats, kNaCounters);
   MS_CUDA(c, cudaSetDevice(c->device));
   unsigned char* base = g_noalloc_addr[c->device];
   if (!base) {
@@ -552,20 +554,9 @@ extern "C" ms_status ms_q4_gemm_noalloc(ms_ctx* c, const ms_q4_weight* w, float*
     base = static_cast<unsigned char*>(ptr);
     g_noalloc_addr[c->device] = base;
   }
-
-  // the same plan rule as ms_q4_gemm, with the static region's limits: a
-  // k-split whose partials would not fit falls back to fewer k-segments
-  ms_ctx lim;
-  lim.device = c->device;
-  lim.sm_count = c->sm_count;
-  lim.part = reinterpret_cast<float*>(base + kNaPartOff);
-  lim.part_floats = kNaPartFloats;
-  lim.counters = reinterpret_cast<int*>(base + kNaCountOff);
-  lim.n_counters = kNaCounters;
-  lim.d_err = c->d_err;  // timeouts reach the context's error word (ms_sync)
-  const int n_tiles = w->N / kTileN;
-  GemvPlan pl = plan_gemv(&lim, M, w->K, n_tiles);
-  GemvParams p = gemv_base(&lim, w->w, n_tiles, w->K, M, pl);
+  GemvParams p = gemv_base(c, w->w, n_tiles, w->K, M, pl);
+  p.part = reinterpret_cast<float*>(base);
+  p.counters = reinterpret_cast<int*>(base + kNaCountOff);  // d_err: the context's (ms_sync)
   p.x = A;
   p.ldx = w->K;
   p.in_D = w->K;
@@ -576,12 +567,7 @@ extern "C" ms_status ms_q4_gemm_noalloc(ms_ctx* c, const ms_q4_weight* w, float*
   cudaStream_t s = pick(c, stream);
   // tickets must be zero when the kernel starts; a completed launch leaves
   // them zero, and clearing them here also covers a call that timed out
-  MS_CUDA(c, cudaMemsetAsync(lim.counters, 0, kNaCounters * sizeof(int), s));
-  if (pl.dec) {
-    uint16_t* frag = reinterpret_cast<uint16_t*>(base + kNaFragOff);
-    MS_CUDA(c, launch_rowstats(nullptr, frag, A, w->K, M, w->K, s, false));
-    p.xfrag = reinterpret_cast<const uint2*>(frag);
-  }
+  if (need_tickets) MS_CUDA(c, cudaMemsetAsync(p.counters, 0, need_tickets * sizeof(int), s));
   MS_CUDA(c, launch_proj(p, pl, s, false));
   return MS_OK;
 }
@@ -738,10 +724,6 @@ extern "C" ms_status ms_model_create(ms_ctx* c, const ms_model_desc* desc, ms_mo
   if (st == MS_OK) st = model_alloc(m, &m->Q, (size_t)R * m->max_q);
   if (st == MS_OK) st = model_alloc(m, &m->ATT, (size_t)R * m->max_q);
   if (st == MS_OK) st = model_alloc(m, &m->H, (size_t)R * m->max_f);
-  // fragment rows: 2 row blocks x width / 16 subtiles x 32 lanes x 4 halves
-  for (int i = 0; i < 2 && st == MS_OK; ++i) st = model_alloc(m, &m->FX[i], (size_t)2 * D * 16);
-  if (st == MS_OK) st = model_alloc(m, &m->FATT, (size_t)2 * m->max_q * 16);
-  if (st == MS_OK) st = model_alloc(m, &m->FH, (size_t)2 * m->max_f * 16);
   if (st == MS_OK) st = model_alloc(m, &m->d_seq, R);
   if (st == MS_OK) st = model_alloc(m, &m->d_pos, R);
   if (st == MS_OK) st = model_alloc(m, &m->d_ids, R);
@@ -944,7 +926,6 @@ static ms_status run_layer(ms_ctx* c, ms_model* m, const ms_kv* kv, int li, int 
     p.pos = m->d_pos;
     p.seq = m->d_seq;
     p.kv = kv_view(kv, li);
-    p.xfrag = reinterpret_cast<const uint2*>(frag_in(m, 0, M));
     MS_CUDA(c, launch_proj(p, pl, s, pdl));
   }
   // 2. attention
@@ -963,27 +944,27 @@ static ms_status run_layer(ms_ctx* c, ms_model* m, const ms_kv* kv, int li, int 
     a.window = L.d.window;
     a.M = M;
     a.scale = 1.0f / sqrtf((float)L.d.head_dim);
-    // splits: enough CTAs to fill the GPU at the longest span the cache can
-    // hold; the kernel sizes each row's chunks itself (short rows leave splits
+    // splits: about one CTA per SM at the longest span the cache can hold;
+    // the kernel sizes each row's ranges itself (short rows leave splits
     // idle), so one launch shape -- and one captured graph -- serves every
     // position
     const int span = L.d.window > 0 ? std::min(L.d.window, kv->max_pos) : kv->max_pos;
     const long ctas_per_split = (long)M * L.d.n_kv_heads;
-    const int min_chunk = attention_block_positions(L.d.head_dim);
-    int splits = (int)std::max<long>(1, (2L * c->sm_count + ctas_per_split - 1) / ctas_per_split);
-    splits = std::min(splits, std::max(1, (span + min_chunk - 1) / min_chunk));
-    splits = std::min(splits, 64);
+    const int min_per = 8;  // positions per split at least
+    int splits = (int)std::max<long>(1, (c->sm_count + ctas_per_split - 1) / ctas_per_split);
+    splits = std::min(splits, std::max(1, (span + min_per - 1) / min_per));
+    splits = std::min(splits, attention_max_splits());
     const int G = L.d.n_heads / L.d.n_kv_heads;
     while (splits > 1 &&
-           (size_t)M * L.d.n_kv_heads * splits * G * (L.d.head_dim + 2) > c->part_floats)
+           (size_t)M * L.d.n_kv_heads * splits * G * (L.d.head_dim + 4) > c->part_floats)
       splits = (splits + 1) / 2;
     if ((size_t)M * L.d.n_kv_heads > c->n_counters)
       return fail(c, MS_ERR_CAPACITY, "attention: too many rows for the ticket counters");
-    a.chunk = min_chunk;
+    a.chunk = min_per;
     a.n_splits = splits;
     a.part = c->part;
     a.counters = c->counters;
-    a.out_frag = M <= 8 ? m->FATT : nullptr;
+    a.err = c->d_err;
     MS_CUDA(c, launch_attention(a, s, pdl));
   }
   // 3. O projection + residual onto the normalised input
@@ -1003,8 +984,6 @@ static ms_status run_layer(ms_ctx* c, ms_model* m, const ms_kv* kv, int li, int 
     p.resid_nstat = nstat;
     p.resid_ple = L.d.ple;
     p.out_stats = ys;
-    p.xfrag = M <= 8 ? reinterpret_cast<const uint2*>(m->FATT) : nullptr;
-    p.out_frag = frag_in(m, 1, M);
     MS_CUDA(c, launch_proj(p, pl, s, pdl));
   }
   // 4. gate | up + SwiGLU
@@ -1022,8 +1001,6 @@ static ms_status run_layer(ms_ctx* c, ms_model* m, const ms_kv* kv, int li, int 
     p.ldo = F;
     p.scale = L.d.scale[4];
     p.scale2 = L.d.scale[5];
-    p.xfrag = reinterpret_cast<const uint2*>(frag_in(m, 1, M));
-    p.out_frag = M <= 8 ? m->FH : nullptr;
     MS_CUDA(c, launch_proj(p, pl, s, pdl));
   }
   // 5. Down + residual
@@ -1043,8 +1020,6 @@ static ms_status run_layer(ms_ctx* c, ms_model* m, const ms_kv* kv, int li, int 
     p.resid_nstat = nstat;
     p.resid_ple = 1.f;
     p.out_stats = xs;
-    p.xfrag = M <= 8 ? reinterpret_cast<const uint2*>(m->FH) : nullptr;
-    p.out_frag = frag_in(m, 0, M);
     MS_CUDA(c, launch_proj(p, pl, s, pdl));
   }
   return MS_OK;
@@ -1066,7 +1041,7 @@ extern "C" ms_status ms_layer_forward(ms_ctx* c, const ms_model* mc, int layer, 
   MS_TRY(check_rows(c, m, kv, seq, pos, M));
   cudaStream_t s = pick(c, stream);
   MS_TRY(upload_rows(c, m, seq, pos, M, s));
-  MS_CUDA(c, launch_rowstats(m->S[0], frag_in(m, 0, M), x, m->hidden, M, m->hidden, s, false));
+  MS_CUDA(c, launch_rowstats(m->S[0], x, m->hidden, M, m->hidden, s, false));
   return run_layer(c, m, kv, layer, M, x, m->S[0], m->X[1], m->S[1], s, true);
 }
 
@@ -1078,7 +1053,7 @@ extern "C" ms_status ms_forward(ms_ctx* c, const ms_model* mc, float* x, ms_kv* 
   MS_TRY(check_rows(c, m, kv, seq, pos, M));
   cudaStream_t s = pick(c, stream);
   MS_TRY(upload_rows(c, m, seq, pos, M, s));
-  MS_CUDA(c, launch_rowstats(m->S[0], frag_in(m, 0, M), x, m->hidden, M, m->hidden, s, false));
+  MS_CUDA(c, launch_rowstats(m->S[0], x, m->hidden, M, m->hidden, s, false));
   for (int l = 0; l < m->n_layers; ++l)
     MS_TRY(run_layer(c, m, kv, l, M, x, m->S[0], m->X[1], m->S[1], s, true));
   return MS_OK;
@@ -1118,7 +1093,7 @@ extern "C" ms_status ms_embed(ms_ctx* c, const ms_model* mc, const int* ids, int
       return fail(c, MS_ERR_INVALID_ARG, "token id %d outside 0..%d", ids[r], m->vocab - 1);
   cudaStream_t s = pick(c, stream);
   MS_CUDA(c, cudaMemcpyAsync(m->d_ids, ids, M * sizeof(int), cudaMemcpyHostToDevice, s));
-  MS_CUDA(c, launch_embed_stats(x, m->S[0], frag_in(m, 0, M), m->lm_head, m->d_ids, M, m->hidden,
+  MS_CUDA(c, launch_embed_stats(x, m->S[0], m->lm_head, m->d_ids, M, m->hidden,
                                 m->vocab, s, false));
   return MS_OK;
 }
@@ -1132,13 +1107,13 @@ extern "C" ms_status ms_lm_head(ms_ctx* c, const ms_model* mc, const float* x, i
   if (M <= 0 || M > m->max_rows) return fail(c, MS_ERR_CAPACITY, "M=%d", M);
   if (logits && ((uintptr_t)logits & 15)) return fail(c, MS_ERR_ALIGN, "logits must be 16-byte aligned");
   cudaStream_t s = pick(c, stream);
-  MS_CUDA(c, launch_rowstats(m->S[1], nullptr, x, m->hidden, M, m->hidden, s, false));
+  MS_CUDA(c, launch_rowstats(m->S[1], x, m->hidden, M, m->hidden, s, false));
   return lm_head_launch(c, m, x, m->S[1], M, logits, argmax_out, s, true);
 }
 
 // One decode step on the device: d_ids / d_seq / d_pos -> d_next.
 static ms_status decode_body(ms_ctx* c, ms_model* m, const ms_kv* kv, int M, cudaStream_t s) {
-  MS_CUDA(c, launch_embed_stats(m->X[0], m->S[0], frag_in(m, 0, M), m->lm_head, m->d_ids, M,
+  MS_CUDA(c, launch_embed_stats(m->X[0], m->S[0], m->lm_head, m->d_ids, M,
                                 m->hidden, m->vocab, s, true));
   for (int l = 0; l < m->n_layers; ++l)
     MS_TRY(run_layer(c, m, kv, l, M, m->X[0], m->S[0], m->X[1], m->S[1], s, true));
@@ -1291,7 +1266,7 @@ extern "C" ms_status ms_prefill(ms_ctx* c, const ms_model* mc, ms_kv* kv, const 
       }
   }
   if (st == MS_OK && first_ids && n_keep) {
-    MS_CUDA(c, launch_rowstats(m->S[1], nullptr, keep, m->hidden, n_keep, m->hidden, s, false));
+    MS_CUDA(c, launch_rowstats(m->S[1], keep, m->hidden, n_keep, m->hidden, s, false));
     st = lm_head_launch(c, m, keep, m->S[1], n_keep, nullptr, m->d_next, s, true);
     std::vector<int> nxt(n_keep);
     if (st == MS_OK) {

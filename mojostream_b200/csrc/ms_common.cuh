@@ -1,6 +1,7 @@
 // ms_common.cuh -- device helpers shared by the sm_100a kernels.
 //
-// Numeric scheme of the Q4 projections (all of them run on tensor cores):
+// Numeric scheme of the prefill Q4 projection (tensor cores, bf16; the decode
+// projection uses exact integer MMA instead, see ms_gemv_stream.cu):
 //   * a weight (nibble - 8) is an integer in [-8, 7]: exact in bf16;
 //   * an fp32 activation v is split as hi = bf16(v), lo = bf16(v - hi);
 //     |v - hi - lo| <= 2^-18 |v|, so one bf16 MMA pass over [hi | lo] keeps
@@ -55,22 +56,6 @@ __device__ __forceinline__ void split_bf16(float v, uint32_t& hi, uint32_t& lo) 
   __nv_bfloat16 l = __float2bfloat16_rn(v - __bfloat162float(h));
   hi = bf16_bits(h);
   lo = bf16_bits(l);
-}
-
-// Activation rows in MMA-fragment layout ("fragment rows"): for a row block
-// of 4 rows (G = m / 4) and a 16-wide k-subtile ks, lane (g, t) of the B
-// operand holds {k 2t, 2t+1} and {k 2t+8, 2t+9} of row g (g < 4, bf16 hi
-// part) or row g - 4 (g >= 4, bf16 lo part).  Layout [G][ks][lane] x uint2,
-// i.e. 256 bytes per (G, ks): a projection's producer thread copies a whole
-// k-segment of it with one bulk copy.  Writers store 16-bit halves.
-__device__ __forceinline__ void frag_store(uint16_t* f, int ks_total, int m, int k, float v) {
-  uint32_t h, l;
-  split_bf16(v, h, l);
-  const int G = m >> 2, mm = m & 3, ks = k >> 4, kk = k & 15;
-  const int kp = kk >> 1, half = kk & 1, tq = kp & 3, reg = kp >> 2;
-  const size_t base = ((size_t)G * ks_total + ks) * 32;
-  f[((base + mm * 4 + tq) * 2 + reg) * 2 + half] = (uint16_t)h;
-  f[((base + (mm + 4) * 4 + tq) * 2 + reg) * 2 + half] = (uint16_t)l;
 }
 
 // Four bf16x2 A-fragment registers from one packed word of eight nibbles.

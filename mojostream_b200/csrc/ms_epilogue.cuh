@@ -42,10 +42,6 @@ __device__ __forceinline__ void epilogue_row(const GemvParams& p, int tile, int 
       float* o = p.out + (size_t)m * p.ldo + c;
       o[0] = a;
       o[8] = b;
-      if (p.out_frag) {
-        frag_store(p.out_frag, p.ldo / 16, m, c, a);
-        frag_store(p.out_frag, p.ldo / 16, m, c + 8, b);
-      }
       sq_out = a * a + b * b;
       break;
     }
@@ -54,7 +50,6 @@ __device__ __forceinline__ void epilogue_row(const GemvParams& p, int tile, int 
       const float sig = 1.0f / (1.0f + expf(-gt));
       const float h = up * gt * sig;
       p.out[(size_t)m * p.ldo + tile * 8 + g] = h;
-      if (p.out_frag) frag_store(p.out_frag, p.ldo / 16, m, tile * 8 + g, h);
       break;
     }
     case kEpiQKV: {

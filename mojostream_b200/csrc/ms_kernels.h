@@ -90,11 +90,6 @@ struct GemvParams {
   const int* pos;
   const int* seq;
   KvView kv;
-  // fragment rows (decode path, M <= 8): the input as MMA fragments
-  // [G][K/16][32] uint2, and an optional fragment copy of the output rows
-  // (width N; [G][N/16][32] uint2) for the next projection
-  const uint2* xfrag;
-  uint16_t* out_frag;
   // split-K scratch
   float* part;            // partial sums of k-segments
   int* counters;          // arrival tickets (reset by the last arrival)
@@ -111,9 +106,9 @@ struct AttnParams {
   const int* pos;
   int hd, n_heads, n_kv, window, chunk /* minimum positions per split */, n_splits, M;
   float scale;
-  uint16_t* out_frag;  // fragment rows of the output ([G][q_dim/16][32] uint2) or null
-  float* part;    // [M][n_kv][n_splits][G][hd + 2]
+  float* part;    // [M][n_kv][n_splits][G][hd + 4]
   int* counters;  // [M][n_kv]
+  int* err;       // error bits for the host (bounded waits)
 };
 
 struct LmHeadParams {
@@ -136,15 +131,16 @@ cudaError_t launch_gemv_stream(const GemvParams& p, int mg, cudaStream_t s, bool
 size_t gemv_stream_smem(int mg, int kseg);
 cudaError_t launch_attention(const AttnParams& p, cudaStream_t s, bool pdl);
 int attention_block_positions(int head_dim);
+int attention_max_splits();
 // one-time kernel attributes (dynamic shared memory above 48 KB)
 cudaError_t prepare_gemv_stream();
 cudaError_t prepare_attention();
 cudaError_t launch_lm_head(const LmHeadParams& p, cudaStream_t s, bool pdl);
 cudaError_t launch_repack(uint4* out, const uint8_t* const* src, const int* src_n, int n_src,
                           const int* perm, int n_tiles, int K, cudaStream_t s);
-cudaError_t launch_embed_stats(float* x, float* stats, uint16_t* frag, const float* W,
+cudaError_t launch_embed_stats(float* x, float* stats, const float* W,
                                const int* ids, int M, int D, int V, cudaStream_t s, bool pdl);
-cudaError_t launch_rowstats(float* stats, uint16_t* frag, const float* x, int ldx, int M, int D,
+cudaError_t launch_rowstats(float* stats, const float* x, int ldx, int M, int D,
                             cudaStream_t s, bool pdl);
 cudaError_t launch_advance_step(int* ids, const int* next, int* pos, int* hist, int* step, int M,
                                 cudaStream_t s, bool pdl);

@@ -198,10 +198,9 @@ cudaError_t launch_lm_head(const LmHeadParams& p, cudaStream_t s, bool pdl) {
 // =========================================================================
 // Embedding gather (get_token_embedding, lm_head.mojo:171-195): x[m] = column
 // ids[m] of the tied fp32 [D][V] table.  Also writes the per-16-column sums of
-// squares that the first layer's RMSNorm consumes, and (decode batches) the
-// rows in MMA-fragment layout for the first projection.
+// squares that the first layer's RMSNorm consumes.
 // =========================================================================
-__global__ void embed_kernel(float* x, float* stats, uint16_t* frag, const float* __restrict__ W,
+__global__ void embed_kernel(float* x, float* stats, const float* __restrict__ W,
                              const int* __restrict__ ids, int M, int D, int V) {
   pdl_trigger();
   pdl_wait();
@@ -214,7 +213,6 @@ __global__ void embed_kernel(float* x, float* stats, uint16_t* frag, const float
       const int d = t * kTileN + j;
       const float v = W[(size_t)d * V + id];
       x[(size_t)m * D + d] = v;
-      if (frag) frag_store(frag, D / 16, m, d, v);
       sq += v * v;
     }
     stats[(size_t)t * M + m] = sq;
@@ -222,8 +220,8 @@ __global__ void embed_kernel(float* x, float* stats, uint16_t* frag, const float
 }
 
 // Row statistics of caller-provided rows: stats[t][m] = sum of squares of the
-// 16 columns of tile t; optionally the rows as fragments.
-__global__ void rowstats_kernel(float* stats, uint16_t* frag, const float* __restrict__ x, int ldx,
+// 16 columns of tile t.
+__global__ void rowstats_kernel(float* stats, const float* __restrict__ x, int ldx,
                                 int M, int D) {
   pdl_trigger();
   pdl_wait();
@@ -233,14 +231,13 @@ __global__ void rowstats_kernel(float* stats, uint16_t* frag, const float* __res
 #pragma unroll
     for (int j = 0; j < kTileN; ++j) {
       const float v = x[(size_t)m * ldx + t * kTileN + j];
-      if (frag) frag_store(frag, D / 16, m, t * kTileN + j, v);
       sq += v * v;
     }
-    if (stats) stats[(size_t)t * M + m] = sq;
+    stats[(size_t)t * M + m] = sq;
   }
 }
 
-cudaError_t launch_rowstats(float* stats, uint16_t* frag, const float* x, int ldx, int M, int D,
+cudaError_t launch_rowstats(float* stats, const float* x, int ldx, int M, int D,
                             cudaStream_t s, bool pdl) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(M);
@@ -251,7 +248,7 @@ cudaError_t launch_rowstats(float* stats, uint16_t* frag, const float* x, int ld
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, rowstats_kernel, stats, frag, x, ldx, M, D);
+  return cudaLaunchKernelEx(&cfg, rowstats_kernel, stats, x, ldx, M, D);
 }
 
 // =========================================================================
@@ -338,7 +335,7 @@ __global__ void advance_kernel(int* ids, const int* next, int* pos, int* hist, i
 }
 
 // Launchers with the extra buffers the C-ABI layer owns.
-cudaError_t launch_embed_stats(float* x, float* stats, uint16_t* frag, const float* W,
+cudaError_t launch_embed_stats(float* x, float* stats, const float* W,
                                const int* ids, int M, int D, int V, cudaStream_t s, bool pdl) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(M);
@@ -349,7 +346,7 @@ cudaError_t launch_embed_stats(float* x, float* stats, uint16_t* frag, const flo
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, embed_kernel, x, stats, frag, W, ids, M, D, V);
+  return cudaLaunchKernelEx(&cfg, embed_kernel, x, stats, W, ids, M, D, V);
 }
 
 cudaError_t launch_advance_step(int* ids, const int* next, int* pos, int* hist, int* step, int M,

@@ -85,10 +85,12 @@ def test_noalloc_accumulates(ctx, torch_cuda):
     w.close()
 
 
-def test_noalloc_rejects_k_beyond_the_static_scratch(ctx, torch_cuda):
+def test_noalloc_rejects_plans_beyond_the_static_scratch(ctx, torch_cuda):
+    # M 8, K 65536, N 2048: 52 k-segments x 128 tiles x 16 x 8 partial floats
+    # (851968) exceed the 262144 of the static array
     from mojostream_b200.runtime import Q4Weight, _stream
     torch = torch_cuda
-    K, N, M = 32768 + 64, 16, 4
+    K, N, M = 65536, 2048, 8
     W = np.full((K, N // 2), 0x88, dtype=np.uint8)
     w = Q4Weight(ctx, W, K, N, 0.01)
     A = torch.zeros((M, K), dtype=torch.float32, device="cuda")
