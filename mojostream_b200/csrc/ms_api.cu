@@ -46,6 +46,12 @@ struct ms_ctx {
   int* lm_counter = nullptr;
   int* d_err = nullptr;  // error bits left by kernels (bounded waits)
   size_t lm_parts = 0;
+  // tensor-core projections: activation limb planes and per-row factors
+  // (grown on demand outside graph capture; sized up front by ms_model_create)
+  uint8_t* lq = nullptr;
+  size_t lq_bytes = 0;
+  float2* rowf = nullptr;
+  size_t rowf_n = 0;
   cudaEvent_t ev[2] = {nullptr, nullptr};
 };
 
@@ -74,6 +80,8 @@ struct ms_model {
   float* Q = nullptr;
   float* ATT = nullptr;
   float* H = nullptr;
+  uint8_t* lq = nullptr;    // tensor-core scratch: limb planes (max_rows x widest K)
+  float2* rowf = nullptr;   // and per-row factors
   int* d_seq = nullptr;
   int* d_pos = nullptr;
   int* d_ids = nullptr;
@@ -244,7 +252,8 @@ extern "C" ms_status ms_init(int device, ms_ctx** out) {
   cudaMemset(c->d_err, 0, sizeof(int));
   cudaEventCreate(&c->ev[0]);
   cudaEventCreate(&c->ev[1]);
-  if (prepare_gemv_stream() != cudaSuccess || prepare_attention() != cudaSuccess) {
+  if (prepare_gemv_stream() != cudaSuccess || prepare_attention() != cudaSuccess ||
+      prepare_gemm_tc() != cudaSuccess) {
     ms_destroy(c);
     return MS_ERR_CUDA;
   }
@@ -266,6 +275,8 @@ extern "C" ms_status ms_destroy(ms_ctx* c) {
   cudaFree(c->lm_idx);
   cudaFree(c->lm_counter);
   cudaFree(c->d_err);
+  cudaFree(c->lq);
+  cudaFree(c->rowf);
   if (c->ev[0]) cudaEventDestroy(c->ev[0]);
   if (c->ev[1]) cudaEventDestroy(c->ev[1]);
   if (c->stream) cudaStreamDestroy(c->stream);
@@ -393,13 +404,47 @@ extern "C" ms_status ms_q4_weight_destroy(ms_ctx* c, ms_q4_weight* w) {
 // Launch plan of one projection: decode kernel (M <= 8) or the tiled kernel,
 // m-group size, chunks per round, k-segment and the number of k-segments.
 struct GemvPlan {
-  bool dec;
+  bool dec, tc;
   int mg, ch, kseg, ksplit;
 };
 
-static GemvPlan plan_gemv(const ms_ctx* c, int M, int K, int n_tiles) {
+// Rows above which projections run on the tensor cores (tcgen05 GEMM).
+constexpr int kTcMinRows = 9;
+
+// Grow the tensor-core scratch (limb planes, row factors) to M rows x K.
+// Synchronises the context's stream when it allocates; never called while a
+// graph is being captured (the model sizes it for max_rows up front).
+static ms_status ensure_tc_scratch(ms_ctx* c, int M, int K) {
+  const size_t need = tc_limb_bytes(M, K);
+  const size_t rows = (size_t)tc_rows_pad(M);
+  if (need <= c->lq_bytes && rows <= c->rowf_n) return MS_OK;
+  cudaStreamSynchronize(c->stream);
+  if (need > c->lq_bytes) {
+    cudaFree(c->lq);
+    c->lq = nullptr;
+    c->lq_bytes = 0;
+    MS_TRY(dev_alloc(c, (void**)&c->lq, need));
+    c->lq_bytes = need;
+  }
+  if (rows > c->rowf_n) {
+    cudaFree(c->rowf);
+    c->rowf = nullptr;
+    c->rowf_n = 0;
+    MS_TRY(dev_alloc(c, (void**)&c->rowf, rows * sizeof(float2)));
+    c->rowf_n = rows;
+  }
+  return MS_OK;
+}
+
+static GemvPlan plan_gemv(const ms_ctx* c, int M, int K, int n_tiles, bool allow_tc = true) {
   GemvPlan pl{};
   const int chunks = K / kChunkK;
+  if (allow_tc && M >= kTcMinRows) {
+    pl.tc = true;  // one CTA per (tile group, 128-row tile), all of K
+    pl.ksplit = 1;
+    pl.kseg = K;
+    return pl;
+  }
   if (M <= 8) {
     // streaming kernel: one CTA per (tile group, k-segment); about one CTA per
     // SM, a k-segment of at most 40 chunks (mg 1) / 20 (mg 2) so stages +
@@ -444,6 +489,7 @@ static GemvPlan plan_gemv(const ms_ctx* c, int M, int K, int n_tiles) {
 }
 
 static cudaError_t launch_proj(const GemvParams& p, const GemvPlan& pl, cudaStream_t s, bool pdl) {
+  if (pl.tc) return launch_gemm_tc(p, s, pdl);
   return pl.dec ? launch_gemv_stream(p, pl.mg, s, pdl) : launch_gemv(p, pl.mg, pl.ch, s, pdl);
 }
 
@@ -463,6 +509,8 @@ static GemvParams gemv_base(ms_ctx* c, const uint4* w, int n_tiles, int K, int M
   p.part = c->part;
   p.counters = c->counters;
   p.err = c->d_err;
+  p.lq = c->lq;
+  p.rowf = c->rowf;
   return p;
 }
 
@@ -474,6 +522,7 @@ extern "C" ms_status ms_q4_gemm(ms_ctx* c, const ms_q4_weight* w, float* C, cons
     return fail(c, MS_ERR_ALIGN, "ms_q4_gemm: A must be 16-byte and C 8-byte aligned");
   const int n_tiles = w->N / kTileN;
   GemvPlan pl = plan_gemv(c, M, w->K, n_tiles);
+  if (pl.tc) MS_TRY(ensure_tc_scratch(c, M, w->K));
   GemvParams p = gemv_base(c, w->w, n_tiles, w->K, M, pl);
   p.x = A;
   p.ldx = w->K;
@@ -536,7 +585,9 @@ extern "C" ms_status ms_q4_gemm_noalloc(ms_ctx* c, const ms_q4_weight* w, float*
   if (c->device < 0 || c->device >= kNaMaxDevices)
     return fail(c, MS_ERR_UNSUPPORTED, "ms_q4_gemm_noalloc: device %d", c->device);
   const int n_tiles = w->N / kTileN;
-  const GemvPlan pl = plan_gemv(c, M, w->K, n_tiles);  // the plan ms_q4_gemm uses
+  // the plan ms_q4_gemm uses, minus the tensor-core path (whose limb
+  // buffer grows with M x K): rows above 8 take the CUDA-core tiled kernel
+  const GemvPlan pl = plan_gemv(c, M, w->K, n_tiles, false);
   size_t need_floats = 0, need_tickets = 0;
   plan_scratch(pl, M, n_tiles, &need_floats, &need_tickets);
   if (need_floats > kNaPartFloats || need_tickets > kNaCounters)
@@ -717,6 +768,14 @@ extern "C" ms_status ms_model_create(ms_ctx* c, const ms_model_desc* desc, ms_mo
   }
   const int R = desc->max_rows;
   ms_status st = MS_OK;
+  if (R >= kTcMinRows) {
+    // the model's own tensor-core scratch (its captured graphs keep these
+    // pointers, so it is never shared with ms_q4_gemm's growable buffer)
+    int kmax = std::max(D, m->max_f);
+    kmax = std::max(kmax, m->max_q);
+    st = model_alloc(m, &m->lq, tc_limb_bytes(R, kmax));
+    if (st == MS_OK) st = model_alloc(m, &m->rowf, (size_t)tc_rows_pad(R));
+  }
   for (int i = 0; i < 2 && st == MS_OK; ++i) {
     st = model_alloc(m, &m->X[i], (size_t)R * D);
     if (st == MS_OK) st = model_alloc(m, &m->S[i], (size_t)R * (D / kTileN));
@@ -909,6 +968,8 @@ static ms_status run_layer(ms_ctx* c, ms_model* m, const ms_kv* kv, int li, int 
   {
     GemvPlan pl = plan_gemv(c, M, D, L.qkv_tiles);
     GemvParams p = gemv_base(c, L.wqkv, L.qkv_tiles, D, M, pl);
+    p.lq = m->lq;
+    p.rowf = m->rowf;
     p.x = x;
     p.ldx = D;
     p.in_stats = xs;
@@ -971,6 +1032,8 @@ static ms_status run_layer(ms_ctx* c, ms_model* m, const ms_kv* kv, int li, int 
   {
     GemvPlan pl = plan_gemv(c, M, L.q_dim, D / kTileN);
     GemvParams p = gemv_base(c, L.wo, D / kTileN, L.q_dim, M, pl);
+    p.lq = m->lq;
+    p.rowf = m->rowf;
     p.x = m->ATT;
     p.ldx = L.q_dim;
     p.in_D = D;
@@ -991,6 +1054,8 @@ static ms_status run_layer(ms_ctx* c, ms_model* m, const ms_kv* kv, int li, int 
     const int nt = 2 * F / kTileN;
     GemvPlan pl = plan_gemv(c, M, D, nt);
     GemvParams p = gemv_base(c, L.wgu, nt, D, M, pl);
+    p.lq = m->lq;
+    p.rowf = m->rowf;
     p.x = y;
     p.ldx = D;
     p.in_stats = ys;
@@ -1007,6 +1072,8 @@ static ms_status run_layer(ms_ctx* c, ms_model* m, const ms_kv* kv, int li, int 
   {
     GemvPlan pl = plan_gemv(c, M, F, D / kTileN);
     GemvParams p = gemv_base(c, L.wd, D / kTileN, F, M, pl);
+    p.lq = m->lq;
+    p.rowf = m->rowf;
     p.x = m->H;
     p.ldx = F;
     p.in_D = D;

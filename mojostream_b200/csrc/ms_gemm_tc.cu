@@ -1,0 +1,349 @@
+// ms_gemm_tc.cu -- Q4 projection for prefill and large batches on the
+// 5th-generation tensor cores (tcgen05, accumulators in tensor memory).
+// Reference: matmul_q4_bpack_raw (src/linalg/kernels.mojo:201-267) with the
+// steps fused around its call sites (src/main.mojo:538-613,
+// src/inference/gemma4_e4b.mojo:459-540) in the epilogue.
+//
+// Arithmetic (exact integer products, like the decode kernel's):
+//   * each input row x (K values) is quantised once per projection by
+//     quant_rows_kernel: a = max |x|, q = rint(x 2^22 / a), |q| <= 2^22, split
+//     into three signed 8-bit limbs q = d0 + 2^8 d1 + 2^16 d2 (balanced
+//     digits, |d2| <= 64).  The error is 2^-23 a per value, far below the
+//     fp32 rounding of the sums.
+//   * weights are the reference's nibbles u (0..15); the kernel unpacks them
+//     in shared memory to s8 values u - 8 (the reference's dequant without
+//     the per-tensor scale, which is applied once in fp32 at the end).
+//   * per limb one s8 x s8 -> s32 MMA chain over all of K; |sum| <= K * 8 *
+//     128 < 2^31 for K <= 2^21.  The epilogue combines the limbs in int64 and
+//     scales by (a / 2^22) * (RMSNorm factor) * (weight scale).
+//
+// CTA tile: 128 rows x 128 columns (one tile group of 8 x 16 columns), the
+// whole K.  Warp roles: warp 0 streams stages with cp.async.bulk (24 KB of
+// limbs + 4 KB of packed nibbles per 64-k chunk, 5-stage mbarrier ring);
+// warp 1 allocates 512 tensor-memory columns and one thread issues the
+// MMAs (3 limbs x 2 k32 steps per chunk; M 128, N 128, K 32); warps 2-9
+// unpack the nibbles into the B operand; warps 2-5 run the epilogue (tensor
+// memory lane = row).  Every wait is bounded (error word + drain on timeout).
+#include "ms_common.cuh"
+#include "ms_epilogue.cuh"
+#include "ms_kernels.h"
+#include "ms_tc.cuh"
+
+namespace ms {
+
+constexpr int kTcBM = 128;
+constexpr int kTcBN = kGroupTiles * kTileN;              // 128
+constexpr int kTcLimbs = 3;
+constexpr int kTcStages = 5;
+constexpr int kTcPlane = kTcBM * kChunkK;                // 8 KB: one limb of 128 rows x 64 k
+constexpr int kTcAStage = kTcLimbs * kTcPlane;           // 24 KB
+constexpr int kTcBPacked = kGroupTiles * kWarp * 16;     // 4 KB
+constexpr int kTcBConv = kTcBN * kChunkK;                // 8 KB
+constexpr int kTcStageBytes = kTcAStage + kTcBPacked + kTcBConv;
+constexpr int kTcConvWarps = 8;
+constexpr int kTcThreads = (2 + kTcConvWarps) * kWarp;   // 320
+constexpr uint32_t kTcCols = 512;                        // 3 x 128 used
+constexpr float kTcQuantOne = 4194304.0f;                // 2^22
+constexpr size_t kTcSmem = (size_t)kTcStages * kTcStageBytes;
+// Core matrices: K-adjacent 128 bytes apart, row groups 512 bytes apart.
+constexpr uint32_t kTcLbo = 128, kTcSbo = 512;
+
+static_assert(kTcStageBytes % 1024 == 0, "stage alignment");
+
+int tc_rows_pad(int M) { return (M + kTcBM - 1) / kTcBM * kTcBM; }
+size_t tc_limb_bytes(int M, int K) { return (size_t)tc_rows_pad(M) * K * kTcLimbs; }
+
+// ------------------------------------------------------------- quantiser --
+// Rows of x -> limb planes in the MMA's A layout:
+//   lq[(m_tile * nchunks + chunk) * 3 + limb][row group][k16][row % 8][16 B]
+// Byte j of a 16-byte core row holds k = 2t + 8 (e & 1) + (e >> 1) of its
+// 16-k subtile (t = j / 4, e = j % 4): the order of the weight words.
+// rowf[m] = {(a / 2^22) * fin, fres}: the factors the epilogue applies.
+// CTA: 8 rows (one row group), 256 threads; thread (row tid % 8, subtile
+// tid / 8 + 32 j).  Rows >= M are written as zeros.
+constexpr int kQThreads = 256;
+__global__ void __launch_bounds__(kQThreads) quant_rows_kernel(const GemvParams p) {
+  __shared__ float s_max[kQThreads / kWarp][8];
+  const int r8 = threadIdx.x & 7, sub0 = threadIdx.x >> 3;
+  const int m = blockIdx.x * 8 + r8;
+  const int mt = m / kTcBM, r = m % kTcBM;
+  const int nchunks = p.K / kChunkK, nsub = p.K / 16;
+  const bool live = m < p.M;
+  pdl_wait();
+  pdl_trigger();
+  const float* x = p.x + (size_t)(live ? m : 0) * p.ldx;
+  float a = 0.f;
+  if (live)
+    for (int i = sub0; i < nsub; i += kQThreads / 8) {
+      const float4* v4 = reinterpret_cast<const float4*>(x + 16 * i);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float4 v = __ldg(v4 + q);
+        a = fmaxf(a, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+      }
+    }
+  // lanes with equal lane % 8 share a row
+  a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 8));
+  a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 16));
+  if ((threadIdx.x & 31) < 8) s_max[threadIdx.x >> 5][r8] = a;
+  __syncthreads();
+#pragma unroll
+  for (int w = 0; w < kQThreads / kWarp; ++w) a = fmaxf(a, s_max[w][r8]);
+  const float inv = a > 0.f ? kTcQuantOne / a : 0.f;
+
+  if (sub0 == 0) {
+    float fin = p.in_ple, fres = 1.f;
+    if (live && p.in_stats) {
+      float s = 0.f;
+      for (int i = 0; i < p.in_nstat; ++i) s += p.in_stats[(size_t)i * p.M + m];
+      fin = p.in_ple / sqrtf(p.in_ple * p.in_ple * s / (float)p.in_D + 1e-6f);
+    }
+    if (live && p.epi == kEpiResid && p.resid_stats) {
+      float s = 0.f;
+      for (int i = 0; i < p.resid_nstat; ++i) s += p.resid_stats[(size_t)i * p.M + m];
+      fres = 1.0f / sqrtf(p.resid_ple * p.resid_ple * s / (float)p.in_D + 1e-6f);
+    }
+    p.rowf[m] = live ? make_float2(a / kTcQuantOne * fin, fres) : make_float2(0.f, 0.f);
+  }
+
+  for (int i = sub0; i < nsub; i += kQThreads / 8) {
+    float v[16];
+    if (live) {
+      const float4* v4 = reinterpret_cast<const float4*>(x + 16 * i);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float4 t4 = __ldg(v4 + q);
+        v[4 * q] = t4.x;
+        v[4 * q + 1] = t4.y;
+        v[4 * q + 2] = t4.z;
+        v[4 * q + 3] = t4.w;
+      }
+    } else {
+#pragma unroll
+      for (int q = 0; q < 16; ++q) v[q] = 0.f;
+    }
+    uint32_t wl[kTcLimbs][4];
+#pragma unroll
+    for (int l = 0; l < kTcLimbs; ++l)
+#pragma unroll
+      for (int t = 0; t < 4; ++t) wl[l][t] = 0u;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int t = j >> 2, e = j & 3;
+      const int k = 2 * t + (e & 1) * 8 + (e >> 1);
+      int q = __float2int_rn(v[k] * inv);
+      const int d0 = (int)(int8_t)(q & 0xFF);
+      q = (q - d0) >> 8;  // exact: a multiple of 256
+      const int d1 = (int)(int8_t)(q & 0xFF);
+      q = (q - d1) >> 8;  // |q| <= 64
+      wl[0][t] |= ((uint32_t)d0 & 0xFFu) << (8 * e);
+      wl[1][t] |= ((uint32_t)d1 & 0xFFu) << (8 * e);
+      wl[2][t] |= ((uint32_t)q & 0xFFu) << (8 * e);
+    }
+    const int c = i >> 2, s = i & 3;
+    uint8_t* dst = p.lq + (size_t)(mt * nchunks + c) * kTcAStage + ((r >> 3) * 4 + s) * 128 +
+                   (r & 7) * 16;
+#pragma unroll
+    for (int l = 0; l < kTcLimbs; ++l)
+      *reinterpret_cast<uint4*>(dst + l * kTcPlane) = make_uint4(wl[l][0], wl[l][1], wl[l][2], wl[l][3]);
+  }
+}
+
+// --------------------------------------------------------------- GEMM --
+__global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const GemvParams p) {
+  extern __shared__ __align__(1024) uint8_t dsm[];
+  __shared__ __align__(8) uint64_t full[kTcStages], conv[kTcStages], empty[kTcStages], done;
+  __shared__ uint32_t s_tmem;
+  __shared__ volatile int s_bad;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int group = blockIdx.x, mt = blockIdx.y;
+  const int nchunks = p.K / kChunkK;
+
+  if (threadIdx.x == 0) {
+    s_bad = 0;
+    for (int s = 0; s < kTcStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&conv[s], kTcConvWarps);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(&done, 1);
+    mbar_fence_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&s_tmem, kTcCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s_tmem;
+  pdl_trigger();
+
+  if (warp == 0) {
+    // ------------------------------------------------------- producer --
+    if (lane == 0) {
+      pdl_wait();  // the limbs are the previous kernel's output
+      const uint8_t* a_src = p.lq + (size_t)mt * nchunks * kTcAStage;
+      const uint4* b_src = p.w + (size_t)group * nchunks * kGroupTiles * kWarp;
+      int c = 0;
+      for (; c < nchunks; ++c) {
+        const int s = c % kTcStages;
+        if (c >= kTcStages && !mbar_wait(&empty[s], ((c / kTcStages) - 1) & 1)) {
+          atomicOr(p.err, kErrWaitTimeout);
+          s_bad = 1;
+          break;
+        }
+        uint8_t* st = dsm + (size_t)s * kTcStageBytes;
+        mbar_expect_tx(&full[s], kTcAStage + kTcBPacked);
+        bulk_g2s(st, a_src + (size_t)c * kTcAStage, kTcAStage, &full[s]);
+        bulk_g2s(st + kTcAStage, b_src + (size_t)c * kGroupTiles * kWarp, kTcBPacked, &full[s]);
+      }
+      if (s_bad) {
+        // let the copies already issued land before the CTA can exit
+        for (int j = c - 1; j >= 0 && j >= c - kTcStages; --j)
+          if (!mbar_wait(&full[j % kTcStages], (j / kTcStages) & 1)) break;
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------ MMA issuer --
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_i8(kTcBM, kTcBN);
+      for (int c = 0; c < nchunks; ++c) {
+        const int s = c % kTcStages;
+        const uint32_t ph = (c / kTcStages) & 1;
+        if (!mbar_wait(&full[s], ph) || !mbar_wait(&conv[s], ph)) {
+          atomicOr(p.err, kErrWaitTimeout);
+          s_bad = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t a0 = smem_u32(dsm + (size_t)s * kTcStageBytes);
+        const uint32_t b0 = a0 + kTcAStage + kTcBPacked;
+#pragma unroll
+        for (int kk = 0; kk < 2; ++kk) {
+          const uint64_t db = umma_desc(b0 + kk * 256, kTcLbo, kTcSbo);
+#pragma unroll
+          for (int l = 0; l < kTcLimbs; ++l)
+            umma_i8(tmem + l * kTcBN, umma_desc(a0 + l * kTcPlane + kk * 256, kTcLbo, kTcSbo), db,
+                    idesc, (c | kk) != 0);
+        }
+        umma_commit(&empty[s]);
+      }
+      umma_commit(&done);  // arrives when every MMA issued above has finished
+    }
+  } else {
+    // ---------------------------------------------- nibble unpacking --
+    // thread ci: tile ci / 32 of the group, fragment lane (g, t) = ci % 32;
+    // word w of its uint4 is k-subtile w of the chunk: low nibbles are tile
+    // row g, high nibbles row g + 8, k order {2t, 2t+8, 2t+1, 2t+9}.
+    const int ci = threadIdx.x - 2 * kWarp;
+    const int tl = ci >> 5, g = (ci & 31) >> 2, t = ci & 3;
+    for (int c = 0; c < nchunks; ++c) {
+      const int s = c % kTcStages;
+      if (!mbar_wait(&full[s], (c / kTcStages) & 1)) {
+        atomicOr(p.err, kErrWaitTimeout);
+        s_bad = 1;
+        break;
+      }
+      uint8_t* st = dsm + (size_t)s * kTcStageBytes;
+      const uint4 wv = lds_u4(reinterpret_cast<const uint4*>(st + kTcAStage) + ci);
+      uint8_t* bc = st + kTcAStage + kTcBPacked + g * 16 + 4 * t;
+      const uint32_t wd[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+        // (u + 0x78) ^ 0x80 per byte = two's complement of u - 8 (no carries)
+        const uint32_t lo = ((wd[w] & 0x0F0F0F0Fu) + 0x78787878u) ^ 0x80808080u;
+        const uint32_t hi = (((wd[w] >> 4) & 0x0F0F0F0Fu) + 0x78787878u) ^ 0x80808080u;
+        sts_u32(bc + ((2 * tl) * 4 + w) * 128, lo);
+        sts_u32(bc + ((2 * tl + 1) * 4 + w) * 128, hi);
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&conv[s]);
+    }
+
+    // ------------------------------------------------------- epilogue --
+    if (warp < 2 + 4) {
+      pdl_wait();
+      const int quad = warp & 3;  // tensor-memory lanes 32 quad .. +31
+      const int row = quad * kWarp + lane;
+      const int m = mt * kTcBM + row;
+      const bool ok = mbar_wait(&done, 0);
+      tc_fence_after();
+      if (!ok) atomicOr(p.err, kErrWaitTimeout);
+      if (ok && !s_bad) {
+        const float2 rf = m < p.M ? p.rowf[m] : make_float2(0.f, 0.f);
+        const uint32_t tl_addr = tmem + ((uint32_t)(quad * kWarp) << 16);
+        for (int j = 0; j < kGroupTiles; ++j) {
+          const int tile = group * kGroupTiles + j;
+          uint32_t a0[16], a1[16], a2[16];
+          tmem_ld16(tl_addr + 0 * kTcBN + 16 * j, a0);
+          tmem_ld16(tl_addr + 1 * kTcBN + 16 * j, a1);
+          tmem_ld16(tl_addr + 2 * kTcBN + 16 * j, a2);
+          tmem_wait_ld();
+          if (tile >= p.n_tiles || m >= p.M) continue;
+          float v[16];
+#pragma unroll
+          for (int q = 0; q < 16; ++q) {
+            const long long iv = (long long)(int)a0[q] + 256LL * (long long)(int)a1[q] +
+                                 65536LL * (long long)(int)a2[q];
+            v[q] = (float)iv * rf.x;
+          }
+          float sq = 0.f;
+#pragma unroll
+          for (int gg = 0; gg < 8; ++gg) {
+            float sqr = 0.f;
+            epilogue_row(p, tile, gg, m, v[gg], v[gg + 8], rf.y, sqr);
+            sq += sqr;
+          }
+          if (p.epi == kEpiResid && p.out_stats) p.out_stats[(size_t)tile * p.M + m] = sq;
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    // no MMA may still write the columns being freed (bounded, as every wait)
+    mbar_wait(&done, 0);
+    tc_fence_after();
+    tmem_dealloc(tmem, kTcCols);
+  }
+}
+
+cudaError_t launch_gemm_tc(const GemvParams& p, cudaStream_t s, bool pdl) {
+  if (p.K % kChunkK || !p.lq || !p.rowf || !p.x || (p.ldx & 3) || ((uintptr_t)p.x & 15) ||
+      ((uintptr_t)p.lq & 15) || ((uintptr_t)p.rowf & 7) || p.M <= 0)
+    return cudaErrorInvalidConfiguration;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  const int m_pad = tc_rows_pad(p.M);
+  {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(m_pad / 8);
+    cfg.blockDim = dim3(kQThreads);
+    cfg.stream = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, quant_rows_kernel, p);
+    if (e != cudaSuccess) return e;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(padded_tiles(p.n_tiles) / kGroupTiles, m_pad / kTcBM);
+  cfg.blockDim = dim3(kTcThreads);
+  cfg.dynamicSmemBytes = kTcSmem;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;  // the quantiser just before it is always a PDL-aware kernel
+  return cudaLaunchKernelEx(&cfg, gemm_tc_kernel, p);
+}
+
+cudaError_t prepare_gemm_tc() {
+  return cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              (int)kTcSmem);
+}
+
+}  // namespace ms

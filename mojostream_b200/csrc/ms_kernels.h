@@ -94,6 +94,9 @@ struct GemvParams {
   float* part;            // partial sums of k-segments
   int* counters;          // arrival tickets (reset by the last arrival)
   int* err;               // error bits for the host (bounded waits)
+  // tensor-core path: activation limbs and per-row factors (quant_rows_kernel)
+  uint8_t* lq;
+  float2* rowf;
 };
 
 struct AttnParams {
@@ -129,12 +132,17 @@ struct LmHeadParams {
 cudaError_t launch_gemv(const GemvParams& p, int mg, int ch, cudaStream_t s, bool pdl);
 cudaError_t launch_gemv_stream(const GemvParams& p, int mg, cudaStream_t s, bool pdl);
 size_t gemv_stream_smem(int mg, int kseg);
+// tcgen05 path (prefill / large batches): quantiser + GEMM, two launches
+cudaError_t launch_gemm_tc(const GemvParams& p, cudaStream_t s, bool pdl);
+int tc_rows_pad(int M);
+size_t tc_limb_bytes(int M, int K);
 cudaError_t launch_attention(const AttnParams& p, cudaStream_t s, bool pdl);
 int attention_block_positions(int head_dim);
 int attention_max_splits();
 // one-time kernel attributes (dynamic shared memory above 48 KB)
 cudaError_t prepare_gemv_stream();
 cudaError_t prepare_attention();
+cudaError_t prepare_gemm_tc();
 cudaError_t launch_lm_head(const LmHeadParams& p, cudaStream_t s, bool pdl);
 cudaError_t launch_repack(uint4* out, const uint8_t* const* src, const int* src_n, int n_src,
                           const int* perm, int n_tiles, int K, cudaStream_t s);
