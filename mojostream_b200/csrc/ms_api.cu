@@ -17,6 +17,7 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <set>
 #include <string>
@@ -52,6 +53,7 @@ struct ms_ctx {
   size_t lq_bytes = 0;
   float2* rowf = nullptr;
   size_t rowf_n = 0;
+  bool mk_ok = false;  // the persistent decode kernel can be co-resident on every SM
   cudaEvent_t ev[2] = {nullptr, nullptr};
 };
 
@@ -82,6 +84,25 @@ struct ms_model {
   float* H = nullptr;
   uint8_t* lq = nullptr;    // tensor-core scratch: limb planes (max_rows x widest K)
   float2* rowf = nullptr;   // and per-row factors
+  // prefill attention: query blocks (runs of consecutive positions of one
+  // sequence, at most `bq` rows each) of the rows last uploaded, per distinct
+  // bq among the layers
+  struct QBlocks {
+    int bq = 0, n = 0;
+    int4* d = nullptr;
+  };
+  std::vector<QBlocks> qblocks;
+  // op lists of the persistent decode kernel: the captured decode step's and
+  // the eager calls' (ms_forward / ms_layer_forward), kept apart so a graph
+  // never sees a list rewritten by a later call
+  struct MkBuf {
+    MkOp* ops = nullptr;
+    GemvParams* gp = nullptr;
+    AttnParams* ap = nullptr;
+    int* done = nullptr;  // [n_ops] counters + abort word
+    int n_ops = 0, mg = 0;
+  };
+  MkBuf mk_graph, mk_eager;
   int* d_seq = nullptr;
   int* d_pos = nullptr;
   int* d_ids = nullptr;
@@ -253,9 +274,18 @@ extern "C" ms_status ms_init(int device, ms_ctx** out) {
   cudaEventCreate(&c->ev[0]);
   cudaEventCreate(&c->ev[1]);
   if (prepare_gemv_stream() != cudaSuccess || prepare_attention() != cudaSuccess ||
-      prepare_gemm_tc() != cudaSuccess) {
+      prepare_gemm_tc() != cudaSuccess || prepare_attention_prefill() != cudaSuccess) {
     ms_destroy(c);
     return MS_ERR_CUDA;
+  }
+  {
+    int coop = 0;
+    cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, device);
+    // the persistent decode kernel is opt-in (MS_PERSISTENT_DECODE=1) until it
+    // is faster than the per-op kernels on every measured shape
+    const char* pe = getenv("MS_PERSISTENT_DECODE");
+    c->mk_ok = coop && pe && pe[0] == '1' && prepare_decode_step() == cudaSuccess;
+    cudaGetLastError();
   }
   if (cudaDeviceSynchronize() != cudaSuccess) {
     ms_destroy(c);
@@ -776,6 +806,16 @@ extern "C" ms_status ms_model_create(ms_ctx* c, const ms_model_desc* desc, ms_mo
     st = model_alloc(m, &m->lq, tc_limb_bytes(R, kmax));
     if (st == MS_OK) st = model_alloc(m, &m->rowf, (size_t)tc_rows_pad(R));
   }
+  for (const LayerDev& ld : m->layers) {
+    const int bq = attention_prefill_tokens(ld.d.head_dim, ld.d.n_heads / ld.d.n_kv_heads);
+    bool have = bq <= 0;
+    for (const auto& q : m->qblocks) have = have || q.bq == bq;
+    if (have || st != MS_OK) continue;
+    ms_model::QBlocks q;
+    q.bq = bq;
+    st = model_alloc(m, &q.d, (size_t)R);
+    m->qblocks.push_back(q);
+  }
   for (int i = 0; i < 2 && st == MS_OK; ++i) {
     st = model_alloc(m, &m->X[i], (size_t)R * D);
     if (st == MS_OK) st = model_alloc(m, &m->S[i], (size_t)R * (D / kTileN));
@@ -939,6 +979,21 @@ static ms_status upload_rows(ms_ctx* c, ms_model* m, const int* seq, const int* 
                              cudaStream_t s) {
   MS_CUDA(c, cudaMemcpyAsync(m->d_seq, seq, M * sizeof(int), cudaMemcpyHostToDevice, s));
   MS_CUDA(c, cudaMemcpyAsync(m->d_pos, pos, M * sizeof(int), cudaMemcpyHostToDevice, s));
+  // query blocks for the prefill attention kernel: a block continues while the
+  // next row is the same sequence at the next position and it has room
+  for (auto& q : m->qblocks) {
+    std::vector<int4> b;
+    for (int r = 0; r < M; ++r) {
+      if (!b.empty() && seq[r] == b.back().z && pos[r] == b.back().w + b.back().y &&
+          b.back().y < q.bq)
+        ++b.back().y;
+      else
+        b.push_back(make_int4(r, 1, seq[r], pos[r]));
+    }
+    q.n = (int)b.size();
+    // pageable source: the copy has taken the data when the call returns
+    MS_CUDA(c, cudaMemcpyAsync(q.d, b.data(), b.size() * sizeof(int4), cudaMemcpyHostToDevice, s));
+  }
   return MS_OK;
 }
 
@@ -954,14 +1009,39 @@ static KvView kv_view(const ms_kv* kv, int layer) {
   v.cap = slide ? kv->slide_cap : kv->pages_full * kv->page;
   v.circular = slide ? 1 : 0;
   v.kv_dim = L.kv_dim;
+  v.off32 = (size_t)kv->n_seq * v.bt_stride * v.page * v.kv_dim < ((size_t)1 << 32);
   return v;
+}
+
+// Op list of the persistent decode kernel, filled by run_layer instead of
+// launching the per-op kernels.
+struct MkCollect {
+  std::vector<MkOp> ops;
+  std::vector<GemvParams> gp;
+  std::vector<AttnParams> ap;
+};
+
+static ms_status emit_proj(ms_ctx* c, MkCollect* mk, const GemvParams& p, const GemvPlan& pl,
+                           cudaStream_t s, bool pdl) {
+  if (!mk) {
+    MS_CUDA(c, launch_proj(p, pl, s, pdl));
+    return MS_OK;
+  }
+  // the kernel's fragment region holds a k-segment of 2560 / mg values per row
+  if (!pl.dec || pl.kseg > 2560 / pl.mg)
+    return fail(c, MS_ERR_STATE, "persistent kernel: projection plan outside its limits");
+  const int groups = padded_tiles(p.n_tiles) / kGroupTiles;
+  mk->ops.push_back(MkOp{kMkProj, (int)mk->gp.size(), groups * pl.ksplit, groups, 0});
+  mk->gp.push_back(p);
+  return MS_OK;
 }
 
 // The five kernels of one layer.  x/xs: input rows and their stats (in
 // place: the layer output lands in x, its stats in xs); y/ys: the second
 // residual buffer.
 static ms_status run_layer(ms_ctx* c, ms_model* m, const ms_kv* kv, int li, int M, float* x,
-                           float* xs, float* y, float* ys, cudaStream_t s, bool pdl) {
+                           float* xs, float* y, float* ys, cudaStream_t s, bool pdl,
+                           bool blocks_valid, MkCollect* mk = nullptr) {
   const LayerDev& L = m->layers[li];
   const int D = m->hidden, F = L.d.ffn_dim, nstat = D / kTileN;
   // 1. QKV + RoPE + KV write
@@ -987,7 +1067,7 @@ static ms_status run_layer(ms_ctx* c, ms_model* m, const ms_kv* kv, int li, int 
     p.pos = m->d_pos;
     p.seq = m->d_seq;
     p.kv = kv_view(kv, li);
-    MS_CUDA(c, launch_proj(p, pl, s, pdl));
+    MS_TRY(emit_proj(c, mk, p, pl, s, pdl));
   }
   // 2. attention
   {
@@ -1013,6 +1093,7 @@ static ms_status run_layer(ms_ctx* c, ms_model* m, const ms_kv* kv, int li, int 
     const long ctas_per_split = (long)M * L.d.n_kv_heads;
     const int min_per = 8;  // positions per split at least
     int splits = (int)std::max<long>(1, (c->sm_count + ctas_per_split - 1) / ctas_per_split);
+    if (mk) splits = mk_attn_splits(c->sm_count, M, L.d.n_kv_heads);  // one unit per CTA
     splits = std::min(splits, std::max(1, (span + min_per - 1) / min_per));
     splits = std::min(splits, attention_max_splits());
     const int G = L.d.n_heads / L.d.n_kv_heads;
@@ -1026,7 +1107,29 @@ static ms_status run_layer(ms_ctx* c, ms_model* m, const ms_kv* kv, int li, int 
     a.part = c->part;
     a.counters = c->counters;
     a.err = c->d_err;
-    MS_CUDA(c, launch_attention(a, s, pdl));
+    // prefill chunks (query blocks of 4+ rows on average) take the tiled
+    // kernel; decode rows and scattered rows the flash-decode kernel
+    if (mk) {
+      const int variant = mk_attn_variant(L.d.head_dim, G);
+      if (variant < 0) return fail(c, MS_ERR_UNSUPPORTED, "persistent kernel: attention shape");
+      mk->ops.push_back(MkOp{kMkAttn, (int)mk->ap.size(), splits * L.d.n_kv_heads * M,
+                             L.d.n_kv_heads * M, variant});
+      mk->ap.push_back(a);
+    }
+    const ms_model::QBlocks* qb = nullptr;
+    const int bq = attention_prefill_tokens(L.d.head_dim, G);
+    if (blocks_valid && M > 8 && bq > 0)
+      for (const auto& q : m->qblocks)
+        if (q.bq == bq && q.n > 0 && M >= 4 * q.n) qb = &q;
+    if (mk) {
+      // collected above
+    } else if (qb) {
+      a.blocks = qb->d;
+      a.n_blocks = qb->n;
+      MS_CUDA(c, launch_attention_prefill(a, s, pdl));
+    } else {
+      MS_CUDA(c, launch_attention(a, s, pdl));
+    }
   }
   // 3. O projection + residual onto the normalised input
   {
@@ -1047,7 +1150,7 @@ static ms_status run_layer(ms_ctx* c, ms_model* m, const ms_kv* kv, int li, int 
     p.resid_nstat = nstat;
     p.resid_ple = L.d.ple;
     p.out_stats = ys;
-    MS_CUDA(c, launch_proj(p, pl, s, pdl));
+    MS_TRY(emit_proj(c, mk, p, pl, s, pdl));
   }
   // 4. gate | up + SwiGLU
   {
@@ -1066,7 +1169,7 @@ static ms_status run_layer(ms_ctx* c, ms_model* m, const ms_kv* kv, int li, int 
     p.ldo = F;
     p.scale = L.d.scale[4];
     p.scale2 = L.d.scale[5];
-    MS_CUDA(c, launch_proj(p, pl, s, pdl));
+    MS_TRY(emit_proj(c, mk, p, pl, s, pdl));
   }
   // 5. Down + residual
   {
@@ -1087,8 +1190,54 @@ static ms_status run_layer(ms_ctx* c, ms_model* m, const ms_kv* kv, int li, int 
     p.resid_nstat = nstat;
     p.resid_ple = 1.f;
     p.out_stats = xs;
-    MS_CUDA(c, launch_proj(p, pl, s, pdl));
+    MS_TRY(emit_proj(c, mk, p, pl, s, pdl));
   }
+  return MS_OK;
+}
+
+// The persistent decode kernel serves M <= 8 rows when every layer's
+// attention shape is one it carries.
+static bool mk_usable(const ms_ctx* c, const ms_model* m, int M) {
+  if (!c->mk_ok || M < 1 || M > 8) return false;
+  for (const LayerDev& L : m->layers)
+    if (mk_attn_variant(L.d.head_dim, L.d.n_heads / L.d.n_kv_heads) < 0) return false;
+  return true;
+}
+
+// Build the op list of layers [l0, l1) and upload it into b (stream-ordered;
+// never called while capturing: the pageable source needs a staged copy).
+static ms_status mk_build(ms_ctx* c, ms_model* m, const ms_kv* kv, int l0, int l1, int M,
+                          float* x, float* xs, float* y, float* ys, ms_model::MkBuf& b,
+                          cudaStream_t s) {
+  MkCollect mk;
+  for (int l = l0; l < l1; ++l) MS_TRY(run_layer(c, m, kv, l, M, x, xs, y, ys, s, false, false, &mk));
+  const int cap = 5 * m->n_layers;
+  if (!b.ops) {
+    MS_TRY(model_alloc(m, &b.ops, (size_t)cap));
+    MS_TRY(model_alloc(m, &b.gp, (size_t)4 * m->n_layers));
+    MS_TRY(model_alloc(m, &b.ap, (size_t)m->n_layers));
+    MS_TRY(model_alloc(m, &b.done, (size_t)cap + 1));
+  }
+  if ((int)mk.ops.size() > cap || mk.gp.size() > (size_t)4 * m->n_layers ||
+      mk.ap.size() > (size_t)m->n_layers)
+    return fail(c, MS_ERR_STATE, "persistent kernel: op list larger than its buffer");
+  MS_CUDA(c, cudaMemcpyAsync(b.ops, mk.ops.data(), mk.ops.size() * sizeof(MkOp),
+                             cudaMemcpyHostToDevice, s));
+  MS_CUDA(c, cudaMemcpyAsync(b.gp, mk.gp.data(), mk.gp.size() * sizeof(GemvParams),
+                             cudaMemcpyHostToDevice, s));
+  if (!mk.ap.empty())
+    MS_CUDA(c, cudaMemcpyAsync(b.ap, mk.ap.data(), mk.ap.size() * sizeof(AttnParams),
+                               cudaMemcpyHostToDevice, s));
+  b.n_ops = (int)mk.ops.size();
+  b.mg = M <= 4 ? 1 : 2;
+  return MS_OK;
+}
+
+// Zero the counters and launch the persistent kernel over b's op list.
+static ms_status mk_launch(ms_ctx* c, const ms_model::MkBuf& b, cudaStream_t s) {
+  MS_CUDA(c, cudaMemsetAsync(b.done, 0, (size_t)(b.n_ops + 1) * sizeof(int), s));
+  MkParams P{b.ops, b.n_ops, b.gp, b.ap, b.done, b.done + b.n_ops, c->d_err};
+  MS_CUDA(c, launch_decode_step(P, b.mg, c->sm_count, s));
   return MS_OK;
 }
 
@@ -1109,7 +1258,11 @@ extern "C" ms_status ms_layer_forward(ms_ctx* c, const ms_model* mc, int layer, 
   cudaStream_t s = pick(c, stream);
   MS_TRY(upload_rows(c, m, seq, pos, M, s));
   MS_CUDA(c, launch_rowstats(m->S[0], x, m->hidden, M, m->hidden, s, false));
-  return run_layer(c, m, kv, layer, M, x, m->S[0], m->X[1], m->S[1], s, true);
+  if (mk_usable(c, m, M)) {
+    MS_TRY(mk_build(c, m, kv, layer, layer + 1, M, x, m->S[0], m->X[1], m->S[1], m->mk_eager, s));
+    return mk_launch(c, m->mk_eager, s);
+  }
+  return run_layer(c, m, kv, layer, M, x, m->S[0], m->X[1], m->S[1], s, true, true);
 }
 
 extern "C" ms_status ms_forward(ms_ctx* c, const ms_model* mc, float* x, ms_kv* kv,
@@ -1121,8 +1274,12 @@ extern "C" ms_status ms_forward(ms_ctx* c, const ms_model* mc, float* x, ms_kv* 
   cudaStream_t s = pick(c, stream);
   MS_TRY(upload_rows(c, m, seq, pos, M, s));
   MS_CUDA(c, launch_rowstats(m->S[0], x, m->hidden, M, m->hidden, s, false));
+  if (mk_usable(c, m, M)) {
+    MS_TRY(mk_build(c, m, kv, 0, m->n_layers, M, x, m->S[0], m->X[1], m->S[1], m->mk_eager, s));
+    return mk_launch(c, m->mk_eager, s);
+  }
   for (int l = 0; l < m->n_layers; ++l)
-    MS_TRY(run_layer(c, m, kv, l, M, x, m->S[0], m->X[1], m->S[1], s, true));
+    MS_TRY(run_layer(c, m, kv, l, M, x, m->S[0], m->X[1], m->S[1], s, true, true));
   return MS_OK;
 }
 
@@ -1182,8 +1339,12 @@ extern "C" ms_status ms_lm_head(ms_ctx* c, const ms_model* mc, const float* x, i
 static ms_status decode_body(ms_ctx* c, ms_model* m, const ms_kv* kv, int M, cudaStream_t s) {
   MS_CUDA(c, launch_embed_stats(m->X[0], m->S[0], m->lm_head, m->d_ids, M,
                                 m->hidden, m->vocab, s, true));
-  for (int l = 0; l < m->n_layers; ++l)
-    MS_TRY(run_layer(c, m, kv, l, M, m->X[0], m->S[0], m->X[1], m->S[1], s, true));
+  if (mk_usable(c, m, M)) {
+    MS_TRY(mk_launch(c, m->mk_graph, s));  // op list built before the capture
+  } else {
+    for (int l = 0; l < m->n_layers; ++l)
+      MS_TRY(run_layer(c, m, kv, l, M, m->X[0], m->S[0], m->X[1], m->S[1], s, true, false));
+  }
   MS_TRY(lm_head_launch(c, m, m->X[0], m->S[0], M, nullptr, m->d_next, s, true));
   return MS_OK;
 }
@@ -1199,6 +1360,9 @@ static ms_status ensure_graph(ms_ctx* c, ms_model* m, const ms_kv* kv, int M) {
   }
   cudaStream_t s = c->stream;
   cudaGraph_t g = nullptr;
+  if (mk_usable(c, m, M))
+    MS_TRY(mk_build(c, m, kv, 0, m->n_layers, M, m->X[0], m->S[0], m->X[1], m->S[1],
+                    m->mk_graph, s));
   MS_CUDA(c, cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
   ms_status st = decode_body(c, m, kv, M, s);
   cudaError_t e = cudaStreamEndCapture(s, &g);
@@ -1322,7 +1486,7 @@ extern "C" ms_status ms_prefill(ms_ctx* c, const ms_model* mc, ms_kv* kv, const 
     if (st != MS_OK) break;
     st = upload_rows(c, m, seq + r0, pos + r0, M, s);
     for (int l = 0; l < m->n_layers && st == MS_OK; ++l)
-      st = run_layer(c, m, kv, l, M, m->X[0], m->S[0], m->X[1], m->S[1], s, true);
+      st = run_layer(c, m, kv, l, M, m->X[0], m->S[0], m->X[1], m->S[1], s, true, true);
     if (st != MS_OK || !first_ids) continue;
     for (int r = r0; r < r0 + M; ++r)
       if (last_row[seq[r]] == r) {

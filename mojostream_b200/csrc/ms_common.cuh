@@ -152,6 +152,25 @@ __device__ __forceinline__ void bar_sync_n(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
+// ------------------------------------------------ cross-CTA handshakes --
+// Writers publish with: all threads write -> CTA barrier -> ONE thread runs
+// fence.acq_rel.gpu and a relaxed atomic (the fence is cumulative over the
+// writes the barrier ordered before it).  Readers: one thread observes the
+// counter with acquire semantics -> CTA barrier -> everyone reads (through
+// L2).  One fence per CTA instead of one per thread.
+__device__ __forceinline__ void fence_acq_rel_gpu() {
+  asm volatile("fence.acq_rel.gpu;" ::: "memory");
+}
+// Ticket: returns the old value; release for this CTA's prior writes,
+// acquire for the tickets taken before it.  Call from one thread after a
+// CTA barrier.
+__device__ __forceinline__ int ticket_acq_rel(int* ctr) {
+  fence_acq_rel_gpu();
+  const int old = atomicAdd(ctr, 1);
+  fence_acq_rel_gpu();
+  return old;
+}
+
 // Error bits a kernel can leave for the host (ms_sync reports them).
 constexpr int kErrWaitTimeout = 1;
 

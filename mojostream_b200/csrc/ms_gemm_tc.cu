@@ -91,19 +91,32 @@ __global__ void __launch_bounds__(kQThreads) quant_rows_kernel(const GemvParams 
   for (int w = 0; w < kQThreads / kWarp; ++w) a = fmaxf(a, s_max[w][r8]);
   const float inv = a > 0.f ? kTcQuantOne / a : 0.f;
 
-  if (sub0 == 0) {
-    float fin = p.in_ple, fres = 1.f;
-    if (live && p.in_stats) {
-      float s = 0.f;
-      for (int i = 0; i < p.in_nstat; ++i) s += p.in_stats[(size_t)i * p.M + m];
-      fin = p.in_ple / sqrtf(p.in_ple * p.in_ple * s / (float)p.in_D + 1e-6f);
+  // RMSNorm factors from the per-tile sums of squares: the 32 threads of a
+  // row each sum a strided share, then one fixed-order tree (deterministic)
+  {
+    __shared__ float s_part[2][kQThreads / 8][8];
+    float si = 0.f, sr = 0.f;
+    if (live && p.in_stats)
+      for (int i = sub0; i < p.in_nstat; i += kQThreads / 8) si += p.in_stats[(size_t)i * p.M + m];
+    if (live && p.epi == kEpiResid && p.resid_stats)
+      for (int i = sub0; i < p.resid_nstat; i += kQThreads / 8)
+        sr += p.resid_stats[(size_t)i * p.M + m];
+    s_part[0][sub0][r8] = si;
+    s_part[1][sub0][r8] = sr;
+    __syncthreads();
+    if (sub0 == 0) {
+      si = 0.f;
+      sr = 0.f;
+      for (int i = 0; i < kQThreads / 8; ++i) {
+        si += s_part[0][i][r8];
+        sr += s_part[1][i][r8];
+      }
+      float fin = p.in_ple, fres = 1.f;
+      if (live && p.in_stats) fin = p.in_ple / sqrtf(p.in_ple * p.in_ple * si / (float)p.in_D + 1e-6f);
+      if (live && p.epi == kEpiResid && p.resid_stats)
+        fres = 1.0f / sqrtf(p.resid_ple * p.resid_ple * sr / (float)p.in_D + 1e-6f);
+      p.rowf[m] = live ? make_float2(a / kTcQuantOne * fin, fres) : make_float2(0.f, 0.f);
     }
-    if (live && p.epi == kEpiResid && p.resid_stats) {
-      float s = 0.f;
-      for (int i = 0; i < p.resid_nstat; ++i) s += p.resid_stats[(size_t)i * p.M + m];
-      fres = 1.0f / sqrtf(p.resid_ple * p.resid_ple * s / (float)p.in_D + 1e-6f);
-    }
-    p.rowf[m] = live ? make_float2(a / kTcQuantOne * fin, fres) : make_float2(0.f, 0.f);
   }
 
   for (int i = sub0; i < nsub; i += kQThreads / 8) {

@@ -168,15 +168,10 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvParams p) 
         *reinterpret_cast<float2*>(my + (g + 8) * MB + mc) = make_float2(acc[G][2], acc[G][3]);
       }
     }
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      const int old = atomicAdd(p.counters + grp, 1);
-      s_last = (old == p.ksplit - 1);
-    }
+    __syncthreads();  // partials written
+    if (threadIdx.x == 0) s_last = (ticket_acq_rel(p.counters + grp) == p.ksplit - 1);
     __syncthreads();
     if (!s_last) return;
-    __threadfence();
     if (tile_ok && tq < 2) {
 #pragma unroll
       for (int G = 0; G < MG; ++G)

@@ -58,6 +58,7 @@ struct KvView {
   float* v;
   const int* block_table;    // [n_seq][bt_stride] physical page ids
   int bt_stride, page, cap, circular, kv_dim;
+  int off32;                 // every row offset of the pool fits 32 bits
 };
 
 struct GemvParams {
@@ -112,6 +113,10 @@ struct AttnParams {
   float* part;    // [M][n_kv][n_splits][G][hd + 4]
   int* counters;  // [M][n_kv]
   int* err;       // error bits for the host (bounded waits)
+  // prefill kernel: query blocks {row0, n_rows, seq, pos0} of consecutive
+  // positions of one sequence (rows row0 .. row0 + n_rows - 1)
+  const int4* blocks;
+  int n_blocks;
 };
 
 struct LmHeadParams {
@@ -128,6 +133,25 @@ struct LmHeadParams {
   int* argmax;            // [M] or null
 };
 
+// Persistent decode-step kernel: the op list of a layer range.
+enum MkKind : int { kMkProj = 0, kMkAttn = 1 };
+struct MkOp {
+  int kind;     // kMkProj / kMkAttn
+  int index;    // into MkParams::gp / ::ap
+  int n_units;  // projection: groups x ksplit; attention: n_splits x n_kv x M
+  int target;   // completions that publish the op (groups / M x n_kv)
+  int variant;  // attention shape id (mk_attn_variant)
+};
+struct MkParams {
+  const MkOp* ops;
+  int n_ops;
+  const GemvParams* gp;
+  const AttnParams* ap;
+  int* done;   // [n_ops] completion counters, zero at launch
+  int* abort;  // zero at launch
+  int* err;
+};
+
 // Launchers (return cudaGetLastError of the launch).
 cudaError_t launch_gemv(const GemvParams& p, int mg, int ch, cudaStream_t s, bool pdl);
 cudaError_t launch_gemv_stream(const GemvParams& p, int mg, cudaStream_t s, bool pdl);
@@ -138,11 +162,19 @@ int tc_rows_pad(int M);
 size_t tc_limb_bytes(int M, int K);
 cudaError_t launch_attention(const AttnParams& p, cudaStream_t s, bool pdl);
 int attention_block_positions(int head_dim);
+// tiled attention for prefill: one CTA per (query block, KV head)
+cudaError_t launch_attention_prefill(const AttnParams& p, cudaStream_t s, bool pdl);
+int attention_prefill_tokens(int head_dim, int group);  // tokens per query block
 int attention_max_splits();
 // one-time kernel attributes (dynamic shared memory above 48 KB)
 cudaError_t prepare_gemv_stream();
 cudaError_t prepare_attention();
 cudaError_t prepare_gemm_tc();
+cudaError_t prepare_attention_prefill();
+cudaError_t launch_decode_step(const MkParams& p, int mg, int n_cta, cudaStream_t s);
+cudaError_t prepare_decode_step();
+int mk_attn_variant(int hd, int g);       // -1: shape not carried by the persistent kernel
+int mk_attn_splits(int n_cta, int M, int n_kv);
 cudaError_t launch_lm_head(const LmHeadParams& p, cudaStream_t s, bool pdl);
 cudaError_t launch_repack(uint4* out, const uint8_t* const* src, const int* src_n, int n_src,
                           const int* perm, int n_tiles, int K, cudaStream_t s);

@@ -147,12 +147,10 @@ __global__ void __launch_bounds__(kLmThreads) lm_head_kernel(const LmHeadParams 
     p.part_val[(size_t)(row0 + tid) * gridDim.x + blockIdx.x] = bv;
     p.part_idx[(size_t)(row0 + tid) * gridDim.x + blockIdx.x] = bi;
   }
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) s_last = (atomicAdd(p.counter, 1) == (int)gridDim.x - 1);
+  __syncthreads();  // partials written
+  if (tid == 0) s_last = (ticket_acq_rel(p.counter) == (int)gridDim.x - 1);
   __syncthreads();
   if (!s_last) return;
-  __threadfence();
   for (int r = warp; r < rows; r += kLmThreads / kWarp) {
     float bv = -INFINITY;
     int bi = 0x7fffffff;
