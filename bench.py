@@ -45,9 +45,12 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--layers", type=int, default=42, help="(debug) fewer layers")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--case", default="decode", choices=["decode", "q4"],
+    ap.add_argument("--case", default="decode", choices=["decode", "q4", "tp"],
                     help="q4: the isolated Q4 projection (BASELINE configs[1] shapes), "
-                         "a small case for profiling")
+                         "a small case for profiling; tp: the 14B-class model (configs[4]) "
+                         "tensor-parallel over the torchrun ranks")
+    ap.add_argument("--batch", type=int, default=64, help="(tp) sequences")
+    ap.add_argument("--prompt", type=int, default=1024, help="(tp) prompt tokens per sequence")
     ap.add_argument("--m", type=int, default=4)
     ap.add_argument("--k", type=int, default=2560)
     ap.add_argument("--n", type=int, default=20480)
@@ -440,11 +443,129 @@ def run_q4_case(args):
                       "peak_source": kind, "frac": round(nbytes / ms / 1e6 / hbm, 4)}), flush=True)
 
 
+def run_tp(args, ws, rank, local):
+    """14B-class random Q4 model, heads / FFN columns /
+    vocabulary sharded over the ranks (one all-reduce after O and after down
+    per layer, NCCL inside the library), batch-B prefill of P-token prompts
+    then greedy decode.  value = decode tokens/s of the whole job (every rank
+    serves the same tokens: strong scaling)."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from mojostream_b200.model import b14_spec, synth_weights_device
+    from mojostream_b200.runtime import Context, KVCache, Model
+    from mojostream_b200.tp import tp_setup
+
+    torch.cuda.set_device(local)
+    if ws > 1:
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local),
+                                timeout=datetime.timedelta(seconds=600))
+    B, P = args.batch, args.prompt
+    spec = b14_spec(n_layers=args.layers if args.layers != 42 else 48)
+    ctx = Context(local)
+    if ws > 1:
+        tp_setup(ctx)
+    w = synth_weights_device(spec, seed=1414)
+    model = Model(ctx, spec, w, max_rows=2048)
+    del w
+    torch.cuda.empty_cache()
+    window = max(l.window for l in spec.layers)
+    max_pos = ((P + args.warmup + 2 * args.steps + 8 + 63) // 64) * 64
+    kv = KVCache(ctx, model, B, max_pos, slide_cap=window + P)
+    lib_stream = torch.cuda.ExternalStream(ctx.stream_ptr)
+
+    def barrier():
+        if ws > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v):
+        if ws == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    rng = np.random.default_rng(77)
+    prompts_ = [[int(t) for t in rng.integers(0, spec.vocab, P)] for _ in range(B)]
+    ids = sum(prompts_, [])
+    seq = sum([[s_] * P for s_ in range(B)], [])
+    pos = sum([list(range(P)) for _ in range(B)], [])
+    # warm prefill (kernel attributes, NCCL connections), then the timed one
+    model.prefill(kv, ids[:P], seq[:P], pos[:P])
+    kv.reset()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(lib_stream)
+    first = model.prefill(kv, ids, seq, pos)
+    e1.record(lib_stream)
+    e1.synchronize()
+    ttft_ms = max_over_ranks(e0.elapsed_time(e1))
+
+    seqs = list(range(B))
+    gen = model.generate(kv, first, seqs, [P] * B, args.warmup)
+    cur = [int(t) for t in gen[-1]]
+    barrier()
+    clocks = ClockSampler(local)
+    clocks.start()
+    gen2, dev_ms = model.generate(kv, cur, seqs, [P + args.warmup] * B, args.steps, timing=True)
+    barrier()
+    dev_ms = max_over_ranks(dev_ms)
+    cur = [int(t) for t in gen2[-1]]
+    p2 = P + args.warmup + args.steps
+    barrier()
+    e0.record(lib_stream)
+    for i in range(args.steps):
+        cur = model.decode_step(kv, cur, seqs, [p2 + i] * B)
+    e1.record(lib_stream)
+    e1.synchronize()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1))
+    barrier()
+    clk = clocks.stop()
+    hbm, _, peak_kind = measured_peaks()
+    tokens = B * args.steps
+    step_ms = dev_ms / args.steps
+    kv_read = B * spec.kv_bytes_per_seq(P + args.warmup + args.steps // 2)
+    step_bytes = (spec.q4_bytes() + spec.lm_head_bytes() + kv_read) / ws  # per GPU
+    result = {
+        "metric": "decode tokens/s (batch %d), 14B-class Q4 model, tensor parallel" % B,
+        "value": round(tokens / (dev_ms / 1e3), 2), "unit": "tokens/s", "n_gpus": ws,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_ms, 4),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "int4 weights x fp32 activations (exact int8-limb tensor-core products), fp32 lm_head",
+        "data": "synthetic (seeded random Q4 weights and token ids)",
+        "config": {"workload": "14b-class tensor-parallel decode (BASELINE configs[4])",
+                   "layers": spec.n_layers, "hidden": spec.hidden, "vocab": spec.vocab,
+                   "batch": B, "prompt": P, "parallelism": f"tp{ws}",
+                   "l2": "weights + KV >> 126 MB L2 (no flush needed)"},
+        "ttft_ms": round(ttft_ms, 3),
+        "e2e": {"value": round(tokens / (e2e_ms / 1e3), 2), "unit": "tokens/s",
+                "h2d_bytes_per_step": 12 * B, "d2h_bytes_per_step": 4 * B},
+        "step_roofline": {"bytes_per_step_per_gpu": int(step_bytes),
+                          "achieved_gbs": round(step_bytes / (step_ms / 1e3) / 1e9, 1),
+                          "peak": hbm, "peak_source": peak_kind,
+                          "frac": round(step_bytes / (step_ms / 1e3) / 1e9 / hbm, 4)},
+        "clocks": clk,
+        "first_ids": first[:4],
+    }
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+    kv.close()
+    model.close()
+    ctx.close()
+    if ws > 1:
+        dist.destroy_process_group()
+
+
 def main():
     args = parse()
     ws, rank, local = dist_setup(args)
     if args.case == "q4":
         run_q4_case(args)
+    elif args.case == "tp" and args.impl != "reference":
+        run_tp(args, ws, rank, local)
     elif args.impl == "reference":
         run_reference(args, ws, rank, local)
     else:

@@ -213,6 +213,29 @@ MS_API ms_status ms_generate(ms_ctx *ctx, const ms_model *model, ms_kv *kv, cons
  * own work or timing events with the library's. */
 MS_API void *ms_ctx_stream(ms_ctx *ctx);
 
+/* ------------------------------------------------------ tensor parallelism */
+
+/* No counterpart in the reference (which runs one CPU process): the larger
+ * configurations split every layer's heads and FFN columns over W GPUs of one
+ * node, one process (and one ms_ctx) per GPU.  Rank 0 creates an id
+ * (ms_tp_unique_id, ms_tp_unique_id_bytes() bytes) and the host hands it to
+ * every rank by its own means; each rank then calls ms_tp_init before
+ * ms_model_create.  ms_model_create takes the FULL reference-layout weights
+ * on every rank and keeps this rank's slices: Q/K/V and gate/up columns of
+ * its heads / FFN columns, O and down rows, lm_head vocabulary columns
+ * [rank V/W, (rank+1) V/W).  Per layer one all-reduce (NCCL) follows O and one
+ * follows down; the embedding and the greedy argmax are combined over ranks,
+ * so ms_embed / ms_decode_step / ms_generate / ms_prefill return the same
+ * ids on every rank.  ms_lm_head's logits hold this rank's vocabulary slice
+ * only.  Every rank must make the same calls in the same order.
+ * Shapes: n_heads, n_kv_heads divisible by W, ffn_dim by 64 W, the local
+ * q width by 64, vocab by 4 W (else MS_ERR_SHAPE).  W = 1: no-op. */
+MS_API size_t ms_tp_unique_id_bytes(void);
+MS_API ms_status ms_tp_unique_id(void *id_out, size_t bytes);
+MS_API ms_status ms_tp_init(ms_ctx *ctx, int world, int rank, const void *unique_id);
+/* Ranks of the context's tensor-parallel group (1 before / without ms_tp_init). */
+MS_API int ms_tp_world(const ms_ctx *ctx);
+
 /* Prefill (the TTFT pass): n_tokens rows (host arrays ids / seq_ids / pos,
  * any mix of sequences) run through all layers in chunks of at most max_rows
  * rows, writing the KV cache.  If first_ids is not NULL, the row with the

@@ -12,6 +12,7 @@
 // launched back to back with programmatic dependent launch, so each kernel's
 // weight stream starts while its predecessor drains.
 #include <cuda_runtime.h>
+#include <nccl.h>
 
 #include <algorithm>
 #include <cmath>
@@ -54,6 +55,9 @@ struct ms_ctx {
   float2* rowf = nullptr;
   size_t rowf_n = 0;
   bool mk_ok = false;  // the persistent decode kernel can be co-resident on every SM
+  // tensor parallelism (ms_tp_init): heads and FFN columns sharded over ranks
+  ncclComm_t comm = nullptr;
+  int tp_world = 1, tp_rank = 0;
   cudaEvent_t ev[2] = {nullptr, nullptr};
 };
 
@@ -71,6 +75,11 @@ struct LayerDev {
 struct ms_model {
   ms_ctx* ctx = nullptr;
   int hidden = 0, n_layers = 0, vocab = 0, max_rows = 0;
+  int vocab_local = 0, vocab0 = 0;  // this rank's lm_head columns (all of them without TP)
+  float* P = nullptr;               // TP: partial sums of the row-parallel projections
+  int* d_lidx = nullptr;            // TP: local argmax, its value and the packed keys
+  float* d_maxv = nullptr;
+  unsigned long long* d_key = nullptr;
   std::vector<LayerDev> layers;
   float* lm_head = nullptr;
   float* gamma = nullptr;
@@ -307,6 +316,7 @@ extern "C" ms_status ms_destroy(ms_ctx* c) {
   cudaFree(c->d_err);
   cudaFree(c->lq);
   cudaFree(c->rowf);
+  if (c->comm) ncclCommDestroy(c->comm);
   if (c->ev[0]) cudaEventDestroy(c->ev[0]);
   if (c->ev[1]) cudaEventDestroy(c->ev[1]);
   if (c->stream) cudaStreamDestroy(c->stream);
@@ -343,6 +353,43 @@ extern "C" ms_status ms_memcpy(ms_ctx* c, void* dst, const void* src, size_t byt
   MS_CUDA(c, cudaMemcpyAsync(dst, src, bytes, k, pick(c, stream)));
   return MS_OK;
 }
+
+// ------------------------------------------------------ tensor parallelism --
+
+extern "C" size_t ms_tp_unique_id_bytes(void) { return sizeof(ncclUniqueId); }
+
+extern "C" ms_status ms_tp_unique_id(void* out, size_t bytes) {
+  if (!out || bytes < sizeof(ncclUniqueId)) return MS_ERR_INVALID_ARG;
+  ncclUniqueId id;
+  if (ncclGetUniqueId(&id) != ncclSuccess) return MS_ERR_NCCL;
+  memcpy(out, &id, sizeof(id));
+  return MS_OK;
+}
+
+extern "C" ms_status ms_tp_init(ms_ctx* c, int world, int rank, const void* unique_id) {
+  if (!c || !unique_id || world < 1 || rank < 0 || rank >= world) return MS_ERR_INVALID_ARG;
+  if (c->comm || c->tp_world > 1) return fail(c, MS_ERR_STATE, "tensor parallelism already set up");
+  if (world == 1) return MS_OK;
+  MS_CUDA(c, cudaSetDevice(c->device));
+  ncclUniqueId id;
+  memcpy(&id, unique_id, sizeof(id));
+  const ncclResult_t r = ncclCommInitRank(&c->comm, world, id, rank);
+  if (r != ncclSuccess) {
+    c->comm = nullptr;
+    return fail(c, MS_ERR_NCCL, "ncclCommInitRank: %s", ncclGetErrorString(r));
+  }
+  c->tp_world = world;
+  c->tp_rank = rank;
+  return MS_OK;
+}
+
+extern "C" int ms_tp_world(const ms_ctx* c) { return c ? c->tp_world : 0; }
+
+#define MS_NCCL(c, call)                                                             \
+  do {                                                                               \
+    const ncclResult_t r_ = (call);                                                  \
+    if (r_ != ncclSuccess) return fail(c, MS_ERR_NCCL, "%s: %s", #call, ncclGetErrorString(r_)); \
+  } while (0)
 
 // --------------------------------------------------------- repack helpers --
 
@@ -682,9 +729,14 @@ static ms_status check_layer(ms_ctx* c, const ms_layer_desc& L, int D, int i) {
 
 // Column order of the fused Q|K|V matrix: per head, RoPE pairs (i, i + R/2)
 // in tiles of 8 + 8, then the unrotated tail in tiles of 16; V plain.
-static void qkv_layout(const ms_layer_desc& L, std::vector<int>& perm, std::vector<QkvTile>& tiles) {
+// Tiles of the fused Q|K|V matrix of the local heads (L: the local view);
+// source columns are those of heads q_head0.. / kv_head0.. of the full
+// matrices, destination columns are local.
+static void qkv_layout(const ms_layer_desc& L, std::vector<int>& perm, std::vector<QkvTile>& tiles,
+                       int q_head0 = 0, int kv_head0 = 0) {
   const int hd = L.head_dim, R = L.rotary_dims, half = R / 2;
   auto heads = [&](int src, int nh, bool rope) {
+    const int sh = (src == 0 ? q_head0 : kv_head0) * hd;  // source column shift
     for (int h = 0; h < nh; ++h) {
       const int base = h * hd;
       int start = 0;
@@ -692,15 +744,15 @@ static void qkv_layout(const ms_layer_desc& L, std::vector<int>& perm, std::vect
         for (int i0 = 0; i0 < half; i0 += 8) {
           QkvTile t{src, base + i0, base + half + i0, i0};
           tiles.push_back(t);
-          for (int r = 0; r < 8; ++r) perm.push_back((src << 24) | (base + i0 + r));
-          for (int r = 0; r < 8; ++r) perm.push_back((src << 24) | (base + half + i0 + r));
+          for (int r = 0; r < 8; ++r) perm.push_back((src << 24) | (sh + base + i0 + r));
+          for (int r = 0; r < 8; ++r) perm.push_back((src << 24) | (sh + base + half + i0 + r));
         }
         start = R;
       }
       for (int c0 = start; c0 < hd; c0 += 16) {
         QkvTile t{src, base + c0, base + c0 + 8, -1};
         tiles.push_back(t);
-        for (int r = 0; r < 16; ++r) perm.push_back((src << 24) | (base + c0 + r));
+        for (int r = 0; r < 16; ++r) perm.push_back((src << 24) | (sh + base + c0 + r));
       }
     }
   };
@@ -720,6 +772,19 @@ extern "C" ms_status ms_model_create(ms_ctx* c, const ms_model_desc* desc, ms_mo
     return fail(c, MS_ERR_SHAPE, "model: vocab %d needs an lm_head and vocab %% 4 == 0",
                 desc->vocab);
   for (int i = 0; i < desc->n_layers; ++i) MS_TRY(check_layer(c, desc->layers[i], D, i));
+  // tensor parallelism: every layer's heads and FFN columns split evenly,
+  // local widths on whole 64-k chunks, the vocabulary split evenly
+  const int TW = c->tp_world, TR = c->tp_rank;
+  for (int i = 0; i < desc->n_layers && TW > 1; ++i) {
+    const ms_layer_desc& L = desc->layers[i];
+    if (L.n_heads % TW || L.n_kv_heads % TW || L.ffn_dim % (kChunkK * TW) ||
+        (L.n_heads / TW * L.head_dim) % kChunkK)
+      return fail(c, MS_ERR_SHAPE,
+                  "layer %d: %d q heads, %d kv heads, ffn %d do not split over %d ranks", i,
+                  L.n_heads, L.n_kv_heads, L.ffn_dim, TW);
+  }
+  if (TW > 1 && desc->vocab > 0 && (desc->vocab % TW || (desc->vocab / TW) % 4))
+    return fail(c, MS_ERR_SHAPE, "vocab %d does not split over %d ranks", desc->vocab, TW);
   cudaSetDevice(c->device);
 
   ms_model* m = new ms_model();
@@ -733,42 +798,50 @@ extern "C" ms_status ms_model_create(ms_ctx* c, const ms_model_desc* desc, ms_mo
     return s;
   };
   for (int i = 0; i < desc->n_layers; ++i) {
-    const ms_layer_desc& L = desc->layers[i];
+    const ms_layer_desc& L = desc->layers[i];  // full shapes
     LayerDev ld;
-    ld.d = L;
+    ld.d = L;  // the local view: this rank's heads and FFN columns
+    ld.d.n_heads = L.n_heads / TW;
+    ld.d.n_kv_heads = L.n_kv_heads / TW;
+    ld.d.ffn_dim = L.ffn_dim / TW;
     for (int j = 0; j < 7; ++j) ld.d.w[j] = nullptr;
-    ld.q_dim = L.n_heads * L.head_dim;
-    ld.kv_dim = L.n_kv_heads * L.head_dim;
+    ld.q_dim = ld.d.n_heads * L.head_dim;
+    ld.kv_dim = ld.d.n_kv_heads * L.head_dim;
+    const int q_full = L.n_heads * L.head_dim, kv_full = L.n_kv_heads * L.head_dim;
+    const int F = ld.d.ffn_dim;
     m->max_q = std::max(m->max_q, ld.q_dim);
-    m->max_f = std::max(m->max_f, L.ffn_dim);
-    // fused Q|K|V
+    m->max_f = std::max(m->max_f, F);
+    // fused Q|K|V of the local heads (column slices of the full matrices)
     std::vector<int> perm;
     std::vector<QkvTile> tiles;
-    qkv_layout(L, perm, tiles);
+    qkv_layout(ld.d, perm, tiles, TR * ld.d.n_heads, TR * ld.d.n_kv_heads);
     ld.qkv_tiles = (int)tiles.size();
     const int nqkv = ld.q_dim + 2 * ld.kv_dim;
     ms_status st = model_alloc(m, &ld.wqkv, q4_u4(D, (int)tiles.size()));
-    if (st == MS_OK) st = repack(c, ld.wqkv, {L.w[0], L.w[1], L.w[2]}, {ld.q_dim, ld.kv_dim, ld.kv_dim}, D, perm);
+    if (st == MS_OK) st = repack(c, ld.wqkv, {L.w[0], L.w[1], L.w[2]}, {q_full, kv_full, kv_full}, D, perm);
     if (st == MS_OK) st = model_alloc(m, &ld.tiles, tiles.size());
     if (st == MS_OK)
       cudaMemcpy(ld.tiles, tiles.data(), tiles.size() * sizeof(QkvTile), cudaMemcpyHostToDevice);
-    // O
+    // O: the rows of the local heads (a row slice of [q_full][D/2])
     if (st == MS_OK) st = model_alloc(m, &ld.wo, q4_u4(ld.q_dim, D / kTileN));
-    if (st == MS_OK) st = repack(c, ld.wo, {L.w[3]}, {D}, ld.q_dim, identity_perm(D));
-    // gate | up interleaved by 8 columns
-    if (st == MS_OK) st = model_alloc(m, &ld.wgu, q4_u4(D, 2 * L.ffn_dim / kTileN));
+    if (st == MS_OK)
+      st = repack(c, ld.wo, {L.w[3] + (size_t)TR * ld.q_dim * (D / 2)}, {D}, ld.q_dim,
+                  identity_perm(D));
+    // gate | up of the local FFN columns, interleaved by 8 columns
+    if (st == MS_OK) st = model_alloc(m, &ld.wgu, q4_u4(D, 2 * F / kTileN));
     if (st == MS_OK) {
       std::vector<int> gp;
-      gp.reserve(2 * L.ffn_dim);
-      for (int j = 0; j < L.ffn_dim / 8; ++j) {
-        for (int r = 0; r < 8; ++r) gp.push_back((0 << 24) | (8 * j + r));
-        for (int r = 0; r < 8; ++r) gp.push_back((1 << 24) | (8 * j + r));
+      gp.reserve(2 * F);
+      for (int j = 0; j < F / 8; ++j) {
+        for (int r = 0; r < 8; ++r) gp.push_back((0 << 24) | (TR * F + 8 * j + r));
+        for (int r = 0; r < 8; ++r) gp.push_back((1 << 24) | (TR * F + 8 * j + r));
       }
       st = repack(c, ld.wgu, {L.w[4], L.w[5]}, {L.ffn_dim, L.ffn_dim}, D, gp);
     }
-    // Down
-    if (st == MS_OK) st = model_alloc(m, &ld.wd, q4_u4(L.ffn_dim, D / kTileN));
-    if (st == MS_OK) st = repack(c, ld.wd, {L.w[6]}, {D}, L.ffn_dim, identity_perm(D));
+    // Down: the rows of the local FFN columns
+    if (st == MS_OK) st = model_alloc(m, &ld.wd, q4_u4(F, D / kTileN));
+    if (st == MS_OK)
+      st = repack(c, ld.wd, {L.w[6] + (size_t)TR * F * (D / 2)}, {D}, F, identity_perm(D));
     // RoPE inverse frequencies (src/linalg/kernels.mojo:573-575), fp32 as the
     // reference computes them
     if (st == MS_OK && L.rotary_dims > 0) {
@@ -781,14 +854,19 @@ extern "C" ms_status ms_model_create(ms_ctx* c, const ms_model_desc* desc, ms_mo
         cudaMemcpy(ld.inv_freq, inv.data(), inv.size() * sizeof(float), cudaMemcpyHostToDevice);
     }
     if (st != MS_OK) return bail(st);
-    m->weight_bytes += (size_t)D * nqkv / 2 + (size_t)ld.q_dim * D / 2 +
-                       (size_t)D * L.ffn_dim + (size_t)L.ffn_dim * D / 2;
+    m->weight_bytes += (size_t)D * nqkv / 2 + (size_t)ld.q_dim * D / 2 + (size_t)D * F +
+                       (size_t)F * D / 2;
     m->layers.push_back(ld);
   }
+  m->vocab_local = desc->vocab / TW;
+  m->vocab0 = TR * m->vocab_local;
   if (desc->vocab > 0) {
-    const size_t n = (size_t)D * desc->vocab;
+    // this rank's columns v0 .. v0 + V/TW of the [D][V] table
+    const size_t n = (size_t)D * m->vocab_local;
     if (model_alloc(m, &m->lm_head, n) != MS_OK) return bail(MS_ERR_OOM);
-    if (cudaMemcpy(m->lm_head, desc->lm_head, n * sizeof(float), cudaMemcpyDefault) != cudaSuccess)
+    if (cudaMemcpy2D(m->lm_head, (size_t)m->vocab_local * sizeof(float), desc->lm_head + m->vocab0,
+                     (size_t)desc->vocab * sizeof(float), (size_t)m->vocab_local * sizeof(float), D,
+                     cudaMemcpyDefault) != cudaSuccess)
       return bail(fail(c, MS_ERR_CUDA, "lm_head upload failed"));
     m->weight_bytes += n * sizeof(float);
     if (desc->final_gamma) {
@@ -828,6 +906,12 @@ extern "C" ms_status ms_model_create(ms_ctx* c, const ms_model_desc* desc, ms_mo
   if (st == MS_OK) st = model_alloc(m, &m->d_ids, R);
   if (st == MS_OK) st = model_alloc(m, &m->d_next, R);
   if (st == MS_OK) st = model_alloc(m, &m->d_step, 1);
+  if (st == MS_OK && TW > 1) {
+    st = model_alloc(m, &m->P, (size_t)R * D);
+    if (st == MS_OK) st = model_alloc(m, &m->d_lidx, R);
+    if (st == MS_OK) st = model_alloc(m, &m->d_maxv, R);
+    if (st == MS_OK) st = model_alloc(m, &m->d_key, R);
+  }
   if (st == MS_OK && cudaMallocHost((void**)&m->h_stage, (4 * (size_t)R + 1) * sizeof(int)) != cudaSuccess)
     st = fail(c, MS_ERR_OOM, "pinned staging");
   if (st != MS_OK) return bail(st);
@@ -1131,7 +1215,9 @@ static ms_status run_layer(ms_ctx* c, ms_model* m, const ms_kv* kv, int li, int 
       MS_CUDA(c, launch_attention(a, s, pdl));
     }
   }
-  // 3. O projection + residual onto the normalised input
+  // 3. O projection + residual onto the normalised input (tensor parallel:
+  //    partial sums, all-reduce, then the residual)
+  const bool tp = c->tp_world > 1;
   {
     GemvPlan pl = plan_gemv(c, M, L.q_dim, D / kTileN);
     GemvParams p = gemv_base(c, L.wo, D / kTileN, L.q_dim, M, pl);
@@ -1150,7 +1236,15 @@ static ms_status run_layer(ms_ctx* c, ms_model* m, const ms_kv* kv, int li, int 
     p.resid_nstat = nstat;
     p.resid_ple = L.d.ple;
     p.out_stats = ys;
+    if (tp) {
+      p.epi = kEpiStore;
+      p.out = m->P;
+    }
     MS_TRY(emit_proj(c, mk, p, pl, s, pdl));
+    if (tp) {
+      MS_NCCL(c, ncclAllReduce(m->P, m->P, (size_t)M * D, ncclFloat, ncclSum, c->comm, s));
+      MS_CUDA(c, launch_resid_add(y, ys, m->P, x, xs, L.d.ple, M, D, s));
+    }
   }
   // 4. gate | up + SwiGLU
   {
@@ -1190,7 +1284,15 @@ static ms_status run_layer(ms_ctx* c, ms_model* m, const ms_kv* kv, int li, int 
     p.resid_nstat = nstat;
     p.resid_ple = 1.f;
     p.out_stats = xs;
+    if (tp) {
+      p.epi = kEpiStore;
+      p.out = m->P;
+    }
     MS_TRY(emit_proj(c, mk, p, pl, s, pdl));
+    if (tp) {
+      MS_NCCL(c, ncclAllReduce(m->P, m->P, (size_t)M * D, ncclFloat, ncclSum, c->comm, s));
+      MS_CUDA(c, launch_resid_add(x, xs, m->P, y, ys, 1.f, M, D, s));
+    }
   }
   return MS_OK;
 }
@@ -1198,7 +1300,7 @@ static ms_status run_layer(ms_ctx* c, ms_model* m, const ms_kv* kv, int li, int 
 // The persistent decode kernel serves M <= 8 rows when every layer's
 // attention shape is one it carries.
 static bool mk_usable(const ms_ctx* c, const ms_model* m, int M) {
-  if (!c->mk_ok || M < 1 || M > 8) return false;
+  if (!c->mk_ok || c->tp_world > 1 || M < 1 || M > 8) return false;
   for (const LayerDev& L : m->layers)
     if (mk_attn_variant(L.d.head_dim, L.d.n_heads / L.d.n_kv_heads) < 0) return false;
   return true;
@@ -1292,16 +1394,38 @@ static ms_status lm_head_launch(ms_ctx* c, ms_model* m, const float* x, const fl
   p.gamma = m->gamma;
   p.W = m->lm_head;
   p.D = m->hidden;
-  p.V = m->vocab;
+  p.V = m->vocab_local;  // this rank's columns (all of them without TP)
   p.M = M;
   p.logits = logits;
   p.part_val = c->lm_val;
   p.part_idx = c->lm_idx;
   p.counter = c->lm_counter;
   p.argmax = argmax;
-  const size_t ctas = (m->vocab + 511) / 512;
+  const bool tp = c->tp_world > 1 && argmax;
+  if (tp) {  // local argmax and its value, then the combine over ranks
+    p.argmax = m->d_lidx;
+    p.maxval = m->d_maxv;
+  }
+  const size_t ctas = (m->vocab_local + 511) / 512;
   if (ctas * M > c->lm_parts) return fail(c, MS_ERR_CAPACITY, "lm_head: too many rows");
   MS_CUDA(c, launch_lm_head(p, s, pdl));
+  if (tp) {
+    MS_CUDA(c, launch_argmax_pack(m->d_key, m->d_maxv, m->d_lidx, M, m->vocab0, s));
+    MS_NCCL(c, ncclAllReduce(m->d_key, m->d_key, M, ncclUint64, ncclMax, c->comm, s));
+    MS_CUDA(c, launch_argmax_unpack(argmax, m->d_key, M, s));
+  }
+  return MS_OK;
+}
+
+// Embedding rows of d_ids into x (+ stats in S[0]).  Tensor parallel: every
+// rank gathers the ids in its vocabulary slice, an all-reduce sums the rows.
+static ms_status embed_rows(ms_ctx* c, ms_model* m, float* x, int M, cudaStream_t s, bool pdl) {
+  MS_CUDA(c, launch_embed_stats(x, m->S[0], m->lm_head, m->d_ids, M, m->hidden, m->vocab_local, s,
+                                pdl, m->vocab0));
+  if (c->tp_world > 1) {
+    MS_NCCL(c, ncclAllReduce(x, x, (size_t)M * m->hidden, ncclFloat, ncclSum, c->comm, s));
+    MS_CUDA(c, launch_rowstats(m->S[0], x, m->hidden, M, m->hidden, s, false));
+  }
   return MS_OK;
 }
 
@@ -1317,9 +1441,7 @@ extern "C" ms_status ms_embed(ms_ctx* c, const ms_model* mc, const int* ids, int
       return fail(c, MS_ERR_INVALID_ARG, "token id %d outside 0..%d", ids[r], m->vocab - 1);
   cudaStream_t s = pick(c, stream);
   MS_CUDA(c, cudaMemcpyAsync(m->d_ids, ids, M * sizeof(int), cudaMemcpyHostToDevice, s));
-  MS_CUDA(c, launch_embed_stats(x, m->S[0], m->lm_head, m->d_ids, M, m->hidden,
-                                m->vocab, s, false));
-  return MS_OK;
+  return embed_rows(c, m, x, M, s, false);
 }
 
 extern "C" ms_status ms_lm_head(ms_ctx* c, const ms_model* mc, const float* x, int M,
@@ -1337,8 +1459,7 @@ extern "C" ms_status ms_lm_head(ms_ctx* c, const ms_model* mc, const float* x, i
 
 // One decode step on the device: d_ids / d_seq / d_pos -> d_next.
 static ms_status decode_body(ms_ctx* c, ms_model* m, const ms_kv* kv, int M, cudaStream_t s) {
-  MS_CUDA(c, launch_embed_stats(m->X[0], m->S[0], m->lm_head, m->d_ids, M,
-                                m->hidden, m->vocab, s, true));
+  MS_TRY(embed_rows(c, m, m->X[0], M, s, true));
   if (mk_usable(c, m, M)) {
     MS_TRY(mk_launch(c, m->mk_graph, s));  // op list built before the capture
   } else {

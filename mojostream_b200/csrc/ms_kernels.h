@@ -131,6 +131,7 @@ struct LmHeadParams {
   int* part_idx;
   int* counter;
   int* argmax;            // [M] or null
+  float* maxval;          // [M] the maximum itself (tensor-parallel combine), or null
 };
 
 // Persistent decode-step kernel: the op list of a layer range.
@@ -178,8 +179,23 @@ int mk_attn_splits(int n_cta, int M, int n_kv);
 cudaError_t launch_lm_head(const LmHeadParams& p, cudaStream_t s, bool pdl);
 cudaError_t launch_repack(uint4* out, const uint8_t* const* src, const int* src_n, int n_src,
                           const int* perm, int n_tiles, int K, cudaStream_t s);
+// x[m] = column ids[m] - v0 of the [D][V] table (zeros when that column is
+// outside 0..V-1: another rank's vocabulary slice); stats per 16 columns.
 cudaError_t launch_embed_stats(float* x, float* stats, const float* W,
-                               const int* ids, int M, int D, int V, cudaStream_t s, bool pdl);
+                               const int* ids, int M, int D, int V, cudaStream_t s, bool pdl,
+                               int v0 = 0);
+// Tensor-parallel epilogue of the row-parallel projections (O, down):
+// out = resid * ple * inv_rms(resid * ple) + partial (already all-reduced),
+// plus the per-16-column sums of squares of out.
+cudaError_t launch_resid_add(float* out, float* out_stats, const float* partial,
+                             const float* resid, const float* resid_stats, float resid_ple,
+                             int M, int D, cudaStream_t s);
+// Greedy argmax across vocabulary shards: pack (value, v0 + index) into keys
+// whose unsigned maximum is the largest value, ties to the smallest index;
+// then unpack the winning index.
+cudaError_t launch_argmax_pack(unsigned long long* key, const float* val, const int* idx, int M,
+                               int v0, cudaStream_t s);
+cudaError_t launch_argmax_unpack(int* ids, const unsigned long long* key, int M, cudaStream_t s);
 cudaError_t launch_rowstats(float* stats, const float* x, int ldx, int M, int D,
                             cudaStream_t s, bool pdl);
 cudaError_t launch_advance_step(int* ids, const int* next, int* pos, int* hist, int* step, int M,

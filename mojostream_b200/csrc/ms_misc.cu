@@ -163,7 +163,10 @@ __global__ void __launch_bounds__(kLmThreads) lm_head_kernel(const LmHeadParams 
       const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
       argmax_merge(bv, bi, ov, oi);
     }
-    if (lane == 0) p.argmax[row0 + r] = bi;
+    if (lane == 0) {
+      p.argmax[row0 + r] = bi;
+      if (p.maxval) p.maxval[row0 + r] = bv;
+    }
   }
   if (tid == 0) *p.counter = 0;
 }
@@ -199,17 +202,18 @@ cudaError_t launch_lm_head(const LmHeadParams& p, cudaStream_t s, bool pdl) {
 // squares that the first layer's RMSNorm consumes.
 // =========================================================================
 __global__ void embed_kernel(float* x, float* stats, const float* __restrict__ W,
-                             const int* __restrict__ ids, int M, int D, int V) {
+                             const int* __restrict__ ids, int M, int D, int V, int v0) {
   pdl_trigger();
   pdl_wait();
   const int m = blockIdx.x;
-  const int id = ids[m];
+  const int id = ids[m] - v0;
+  const bool mine = id >= 0 && id < V;
   for (int t = threadIdx.x; t < D / kTileN; t += blockDim.x) {
     float sq = 0.f;
 #pragma unroll
     for (int j = 0; j < kTileN; ++j) {
       const int d = t * kTileN + j;
-      const float v = W[(size_t)d * V + id];
+      const float v = mine ? W[(size_t)d * V + id] : 0.f;
       x[(size_t)m * D + d] = v;
       sq += v * v;
     }
@@ -334,7 +338,8 @@ __global__ void advance_kernel(int* ids, const int* next, int* pos, int* hist, i
 
 // Launchers with the extra buffers the C-ABI layer owns.
 cudaError_t launch_embed_stats(float* x, float* stats, const float* W,
-                               const int* ids, int M, int D, int V, cudaStream_t s, bool pdl) {
+                               const int* ids, int M, int D, int V, cudaStream_t s, bool pdl,
+                               int v0) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(M);
   cfg.blockDim = dim3(128);
@@ -344,7 +349,91 @@ cudaError_t launch_embed_stats(float* x, float* stats, const float* W,
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, embed_kernel, x, stats, W, ids, M, D, V);
+  return cudaLaunchKernelEx(&cfg, embed_kernel, x, stats, W, ids, M, D, V, v0);
+}
+
+// =========================================================================
+// Tensor-parallel helpers (heads / FFN columns sharded over ranks).
+// =========================================================================
+
+// One CTA per row.  The residual branch matches kEpiResid of the projection
+// epilogue (src/main.mojo:598-600, 610-613): the row's RMSNorm factor from its
+// per-tile sums of squares, then out = resid * ple * inv + partial.
+__global__ void resid_add_kernel(float* out, float* out_stats, const float* __restrict__ partial,
+                                 const float* __restrict__ resid,
+                                 const float* __restrict__ resid_stats, float ple, int M, int D) {
+  __shared__ float s_red[32];
+  __shared__ float s_inv;
+  const int m = blockIdx.x, nstat = D / kTileN;
+  float s = 0.f;
+  for (int i = threadIdx.x; i < nstat; i += blockDim.x) s += resid_stats[(size_t)i * M + m];
+  s = warp_sum(s);
+  if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += s_red[w];
+    s_inv = 1.0f / sqrtf(ple * ple * t / (float)D + 1e-6f);
+  }
+  __syncthreads();
+  const float inv = s_inv;
+  for (int t = threadIdx.x; t < nstat; t += blockDim.x) {
+    const float4* r4 = reinterpret_cast<const float4*>(resid + (size_t)m * D + t * kTileN);
+    const float4* p4 = reinterpret_cast<const float4*>(partial + (size_t)m * D + t * kTileN);
+    float4* o4 = reinterpret_cast<float4*>(out + (size_t)m * D + t * kTileN);
+    float sq = 0.f;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float4 r = r4[q], pp = p4[q];
+      float4 o;
+      o.x = (r.x * ple) * inv + pp.x;
+      o.y = (r.y * ple) * inv + pp.y;
+      o.z = (r.z * ple) * inv + pp.z;
+      o.w = (r.w * ple) * inv + pp.w;
+      o4[q] = o;
+      sq += o.x * o.x + o.y * o.y + o.z * o.z + o.w * o.w;
+    }
+    out_stats[(size_t)t * M + m] = sq;
+  }
+}
+
+cudaError_t launch_resid_add(float* out, float* out_stats, const float* partial,
+                             const float* resid, const float* resid_stats, float resid_ple,
+                             int M, int D, cudaStream_t s) {
+  if (D % kTileN || ((uintptr_t)out | (uintptr_t)partial | (uintptr_t)resid) & 15)
+    return cudaErrorInvalidConfiguration;
+  resid_add_kernel<<<M, 256, 0, s>>>(out, out_stats, partial, resid, resid_stats, resid_ple, M, D);
+  return cudaGetLastError();
+}
+
+// Order-preserving map of a float onto an unsigned integer.
+__device__ __forceinline__ unsigned int ordered_bits(float f) {
+  const unsigned int u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+__global__ void argmax_pack_kernel(unsigned long long* key, const float* __restrict__ val,
+                                   const int* __restrict__ idx, int M, int v0) {
+  const int m = blockIdx.x * blockDim.x + threadIdx.x;
+  if (m >= M) return;
+  const unsigned int gi = (unsigned int)(idx[m] + v0);
+  key[m] = ((unsigned long long)ordered_bits(val[m]) << 32) | (unsigned long long)(0xFFFFFFFFu - gi);
+}
+
+__global__ void argmax_unpack_kernel(int* ids, const unsigned long long* __restrict__ key, int M) {
+  const int m = blockIdx.x * blockDim.x + threadIdx.x;
+  if (m >= M) return;
+  ids[m] = (int)(0xFFFFFFFFu - (unsigned int)(key[m] & 0xFFFFFFFFull));
+}
+
+cudaError_t launch_argmax_pack(unsigned long long* key, const float* val, const int* idx, int M,
+                               int v0, cudaStream_t s) {
+  argmax_pack_kernel<<<(M + 127) / 128, 128, 0, s>>>(key, val, idx, M, v0);
+  return cudaGetLastError();
+}
+cudaError_t launch_argmax_unpack(int* ids, const unsigned long long* key, int M, cudaStream_t s) {
+  argmax_unpack_kernel<<<(M + 127) / 128, 128, 0, s>>>(ids, key, M);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_advance_step(int* ids, const int* next, int* pos, int* hist, int* step, int M,

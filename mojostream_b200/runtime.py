@@ -30,6 +30,14 @@ def _stream():
     return ctypes.c_void_p(s if s else _CUDA_STREAM_LEGACY)
 
 
+def tp_unique_id():
+    """A fresh tensor-parallel group id (ms_tp_unique_id), made by rank 0."""
+    n = lib().ms_tp_unique_id_bytes()
+    buf = ctypes.create_string_buffer(n)
+    check(lib().ms_tp_unique_id(buf, n))
+    return buf.raw
+
+
 class Context:
     """ms_ctx: one CUDA device, its stream and scratch memory."""
 
@@ -51,6 +59,17 @@ class Context:
     def stream_ptr(self):
         """The context's cudaStream_t (as an int)."""
         return lib().ms_ctx_stream(self.h)
+
+    def tp_init(self, world, rank, unique_id):
+        """Join a tensor-parallel group of `world` ranks (ms_tp_init); call
+        before creating models.  unique_id: the bytes of tp_unique_id() made
+        by rank 0."""
+        buf = ctypes.create_string_buffer(bytes(unique_id), len(unique_id))
+        self.check(lib().ms_tp_init(self.h, int(world), int(rank), buf))
+
+    @property
+    def tp_world(self):
+        return lib().ms_tp_world(self.h)
 
     def close(self):
         if self.h:

@@ -1,0 +1,61 @@
+"""One rank of the tensor-parallel GPU test (tests/test_tp.py launches it).
+
+Env: RANK, WORLD_SIZE, MASTER_PORT.  argv[1]: output path prefix.  Builds the
+small hybrid model sharded over WORLD_SIZE GPUs, prefills two prompts,
+decodes four greedy steps and runs one teacher-forced layer; writes the ids
+and the layer output as JSON (rank 0 and 1 must agree with the oracle).
+"""
+import datetime
+import json
+import os
+import sys
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, ROOT)
+
+
+def main(prefix):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{os.environ['MASTER_PORT']}",
+                            rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120))
+    from mojostream_b200.model import small_spec, synth_weights
+    from mojostream_b200.runtime import Context, KVCache, Model
+    from mojostream_b200.tp import tp_setup
+
+    spec = small_spec(vocab=4096, n_layers=6, window=32)
+    w = synth_weights(spec, seed=1234, symmetric=True)
+    ctx = Context(rank)
+    tp_setup(ctx)
+    model = Model(ctx, spec, w, max_rows=16)
+    kv = KVCache(ctx, model, 2, 64, slide_cap=48)
+    prompts = [[11, 402, 7, 3999, 58], [1, 2, 3]]
+    ids = sum(prompts, [])
+    seq = [0] * 5 + [1] * 3
+    pos = list(range(5)) + list(range(3))
+    first = model.prefill(kv, ids, seq, pos)
+    gen = model.generate(kv, first, [0, 1], [5, 3], 4)
+
+    kv2 = KVCache(ctx, model, 2, 64, slide_cap=48)
+    x = np.random.default_rng(0).standard_normal((2, spec.hidden)).astype(np.float32)
+    xg = torch.from_numpy(x).cuda()
+    model.layer_forward(5, xg, kv2, [0, 1], [0, 0])
+    torch.cuda.synchronize()
+    out = {"first": [int(v) for v in first], "gen": np.asarray(gen).tolist(),
+           "layer5": xg.cpu().numpy().astype(np.float64).tolist()}
+    with open(f"{prefix}.{rank}.json", "w") as f:
+        json.dump(out, f)
+    kv2.close()
+    kv.close()
+    model.close()
+    ctx.close()
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main(sys.argv[1])
