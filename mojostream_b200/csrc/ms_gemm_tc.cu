@@ -44,11 +44,13 @@ constexpr int kTcConvWarps = 8;
 constexpr int kTcThreads = (2 + kTcConvWarps) * kWarp;   // 320
 constexpr uint32_t kTcCols = 512;                        // 3 x 128 used
 constexpr float kTcQuantOne = 4194304.0f;                // 2^22
+constexpr int kTcRowS = kTcBN + 4;  // staged output row (floats): 16-byte aligned, 4-way banks
 constexpr size_t kTcSmem = (size_t)kTcStages * kTcStageBytes;
 // Core matrices: K-adjacent 128 bytes apart, row groups 512 bytes apart.
 constexpr uint32_t kTcLbo = 128, kTcSbo = 512;
 
 static_assert(kTcStageBytes % 1024 == 0, "stage alignment");
+static_assert((size_t)kTcBM * kTcRowS * 4 <= (size_t)kTcStages * kTcStageBytes, "staged tile");
 
 int tc_rows_pad(int M) { return (M + kTcBM - 1) / kTcBM * kTcBM; }
 size_t tc_limb_bytes(int M, int K) { return (size_t)tc_rows_pad(M) * K * kTcLimbs; }
@@ -277,40 +279,122 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const GemvParams
     }
 
     // ------------------------------------------------------- epilogue --
+    // Phase 1 (warps 2-5, tensor-memory lane = row): combine the limbs of
+    // the 128 x 128 tile and stage it in shared memory (the stage ring is
+    // idle: every copy landed and every MMA completed before `done`).
+    // Phase 2 (warps 2-9): write the tile row by row, lanes along the
+    // columns, so every store instruction covers contiguous bytes.
+    pdl_wait();
+    const bool ok = mbar_wait(&done, 0);
+    tc_fence_after();
+    if (!ok && threadIdx.x == 2 * kWarp) atomicOr(p.err, kErrWaitTimeout);
+    float* S = reinterpret_cast<float*>(dsm);  // [kTcBM][kTcRowS]
     if (warp < 2 + 4) {
-      pdl_wait();
       const int quad = warp & 3;  // tensor-memory lanes 32 quad .. +31
       const int row = quad * kWarp + lane;
       const int m = mt * kTcBM + row;
-      const bool ok = mbar_wait(&done, 0);
-      tc_fence_after();
-      if (!ok) atomicOr(p.err, kErrWaitTimeout);
-      if (ok && !s_bad) {
-        const float2 rf = m < p.M ? p.rowf[m] : make_float2(0.f, 0.f);
-        const uint32_t tl_addr = tmem + ((uint32_t)(quad * kWarp) << 16);
-        for (int j = 0; j < kGroupTiles; ++j) {
-          const int tile = group * kGroupTiles + j;
-          uint32_t a0[16], a1[16], a2[16];
-          tmem_ld16(tl_addr + 0 * kTcBN + 16 * j, a0);
-          tmem_ld16(tl_addr + 1 * kTcBN + 16 * j, a1);
-          tmem_ld16(tl_addr + 2 * kTcBN + 16 * j, a2);
-          tmem_wait_ld();
-          if (tile >= p.n_tiles || m >= p.M) continue;
-          float v[16];
+      const float dq = (ok && m < p.M) ? p.rowf[m].x : 0.f;
+      const uint32_t tl_addr = tmem + ((uint32_t)(quad * kWarp) << 16);
+      for (int j = 0; j < kGroupTiles && ok; ++j) {
+        uint32_t a0[16], a1[16], a2[16];
+        tmem_ld16(tl_addr + 0 * kTcBN + 16 * j, a0);
+        tmem_ld16(tl_addr + 1 * kTcBN + 16 * j, a1);
+        tmem_ld16(tl_addr + 2 * kTcBN + 16 * j, a2);
+        tmem_wait_ld();
+        float v[16];
 #pragma unroll
-          for (int q = 0; q < 16; ++q) {
-            const long long iv = (long long)(int)a0[q] + 256LL * (long long)(int)a1[q] +
-                                 65536LL * (long long)(int)a2[q];
-            v[q] = (float)iv * rf.x;
-          }
+        for (int q = 0; q < 16; ++q) {
+          const long long iv = (long long)(int)a0[q] + 256LL * (long long)(int)a1[q] +
+                               65536LL * (long long)(int)a2[q];
+          v[q] = (float)iv * dq;
+        }
+        float4* dst = reinterpret_cast<float4*>(S + row * kTcRowS + 16 * j);
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          dst[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+      }
+    }
+    bar_sync_n(2, kTcConvWarps * kWarp);
+    if (ok && !s_bad) {
+      const int w8 = warp - 2;
+      const int jt = lane >> 2;                  // tile of the group this lane covers
+      const int tile = group * kGroupTiles + jt;
+      const bool tile_ok = tile < p.n_tiles;
+      for (int r = w8; r < kTcBM; r += kTcConvWarps) {
+        const int m = mt * kTcBM + r;
+        if (m >= p.M) break;  // warp-uniform
+        const float* Sr = S + r * kTcRowS;
+        if (p.epi == kEpiStore || p.epi == kEpiAccum || p.epi == kEpiResid) {
+          const int c = group * kTcBN + 4 * lane;
+          float4 v = *reinterpret_cast<const float4*>(Sr + 4 * lane);
+          float4 o;
           float sq = 0.f;
-#pragma unroll
-          for (int gg = 0; gg < 8; ++gg) {
-            float sqr = 0.f;
-            epilogue_row(p, tile, gg, m, v[gg], v[gg + 8], rf.y, sqr);
-            sq += sqr;
+          if (p.epi == kEpiResid) {
+            const float fres = p.rowf[m].y;
+            const float4 rr = __ldcg(reinterpret_cast<const float4*>(p.resid + (size_t)m * p.ldr + c));
+            o.x = (rr.x * p.resid_ple) * fres + p.scale * v.x;
+            o.y = (rr.y * p.resid_ple) * fres + p.scale * v.y;
+            o.z = (rr.z * p.resid_ple) * fres + p.scale * v.z;
+            o.w = (rr.w * p.resid_ple) * fres + p.scale * v.w;
+            sq = o.x * o.x + o.y * o.y + o.z * o.z + o.w * o.w;
+          } else {
+            o = make_float4(p.scale * v.x, p.scale * v.y, p.scale * v.z, p.scale * v.w);
+            if (p.epi == kEpiAccum && tile_ok) {
+              const float4 cur = __ldcg(reinterpret_cast<const float4*>(p.out + (size_t)m * p.ldo + c));
+              o.x = cur.x + o.x; o.y = cur.y + o.y; o.z = cur.z + o.z; o.w = cur.w + o.w;
+            }
           }
-          if (p.epi == kEpiResid && p.out_stats) p.out_stats[(size_t)tile * p.M + m] = sq;
+          if (tile_ok) *reinterpret_cast<float4*>(p.out + (size_t)m * p.ldo + c) = o;
+          if (p.epi == kEpiResid && p.out_stats) {
+            sq += __shfl_xor_sync(0xffffffffu, sq, 1);
+            sq += __shfl_xor_sync(0xffffffffu, sq, 2);
+            if (tile_ok && (lane & 3) == 0) p.out_stats[(size_t)tile * p.M + m] = sq;
+          }
+        } else if (p.epi == kEpiSwiGLU) {
+          // tile rows 0-7 gate, 8-15 up of the same output column
+          const int g0 = 2 * (lane & 3);
+          const float2 gv = *reinterpret_cast<const float2*>(Sr + 16 * jt + g0);
+          const float2 uv = *reinterpret_cast<const float2*>(Sr + 16 * jt + 8 + g0);
+          float h[2];
+          const float gs[2] = {gv.x, gv.y}, us[2] = {uv.x, uv.y};
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const float gt = p.scale * gs[e], up = p.scale2 * us[e];
+            const float sig = 1.0f / (1.0f + expf(-gt));
+            h[e] = up * gt * sig;
+          }
+          if (tile_ok)
+            *reinterpret_cast<float2*>(p.out + (size_t)m * p.ldo + group * (kTcBN / 2) + 2 * lane) =
+                make_float2(h[0], h[1]);
+        } else if (p.epi == kEpiQKV && tile_ok) {
+          const int g0 = 2 * (lane & 3);
+          const QkvTile td = p.tiles[tile];
+          const float sc = td.dst == 0 ? p.sq : (td.dst == 1 ? p.sk : p.sv);
+          const float2 lv = *reinterpret_cast<const float2*>(Sr + 16 * jt + g0);
+          const float2 hv = *reinterpret_cast<const float2*>(Sr + 16 * jt + 8 + g0);
+          float lo[2] = {sc * lv.x, sc * lv.y}, hi[2] = {sc * hv.x, sc * hv.y};
+          const int pos = p.pos[m];
+          if (td.rope_i0 >= 0) {
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const float th = (float)pos * p.inv_freq[td.rope_i0 + g0 + e];
+              const float cs = cosf(th), sn = sinf(th);
+              const float ra = lo[e] * cs - hi[e] * sn;
+              const float rb = lo[e] * sn + hi[e] * cs;
+              lo[e] = ra;
+              hi[e] = rb;
+            }
+          }
+          float* base;
+          if (td.dst == 0) {
+            base = p.q_out + (size_t)m * p.ldq;
+          } else {
+            const size_t off = kv_row_offset(p.kv.block_table, p.kv.bt_stride, p.kv.page, p.kv.cap,
+                                             p.kv.circular, p.seq[m], pos, p.kv.kv_dim);
+            base = (td.dst == 1 ? p.kv.k : p.kv.v) + off;
+          }
+          *reinterpret_cast<float2*>(base + td.col_lo + g0) = make_float2(lo[0], lo[1]);
+          *reinterpret_cast<float2*>(base + td.col_hi + g0) = make_float2(hi[0], hi[1]);
         }
       }
     }

@@ -171,26 +171,39 @@ __global__ void __launch_bounds__(kLmThreads) lm_head_kernel(const LmHeadParams 
   if (tid == 0) *p.counter = 0;
 }
 
-cudaError_t launch_lm_head(const LmHeadParams& p, cudaStream_t s, bool pdl) {
-  constexpr int MR = 4;
+template <int MR>
+static cudaError_t launch_lm_head_t(const LmHeadParams& p, int row0, cudaStream_t s, bool pdl) {
   const size_t smem = (size_t)MR * p.D * sizeof(float);
   auto kern = lm_head_kernel<MR>;
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
   }
-  for (int row0 = 0; row0 < p.M; row0 += MR) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((p.V + kLmCols - 1) / kLmCols);
-    cfg.blockDim = dim3(kLmThreads);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = pdl ? 1 : 0;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p, row0);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((p.V + kLmCols - 1) / kLmCols);
+  cfg.blockDim = dim3(kLmThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, p, row0);
+}
+
+// Rows per pass: every pass streams the whole table, so a batch takes as few
+// passes as the normalised rows in shared memory allow (<= 200 KB): 4 rows
+// for decode batches, up to 16 for larger ones.
+cudaError_t launch_lm_head(const LmHeadParams& p, cudaStream_t s, bool pdl) {
+  const size_t row_bytes = (size_t)p.D * sizeof(float);
+  int mr = 4;
+  if (p.M > 4 && 8 * row_bytes <= 200 * 1024) mr = 8;
+  if (p.M > 8 && 16 * row_bytes <= 200 * 1024) mr = 16;
+  for (int row0 = 0; row0 < p.M; row0 += mr) {
+    cudaError_t e = mr == 16 ? launch_lm_head_t<16>(p, row0, s, pdl && row0 == 0)
+                  : mr == 8  ? launch_lm_head_t<8>(p, row0, s, pdl && row0 == 0)
+                             : launch_lm_head_t<4>(p, row0, s, pdl && row0 == 0);
     if (e != cudaSuccess) return e;
   }
   return cudaSuccess;
