@@ -31,8 +31,9 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-PROMPT = 512
+PROMPT = 512     # set from --prompt / --batch in main()
 BATCH = 4
+MAX_ROWS = 2048  # rows per prefill call (the model's activation buffers)
 METRIC = "decode tokens/s (batch 4), Gemma-4-E4B-shaped Q4 model"
 WORKLOAD = "gemma4-e4b decode, batch 4 independent sequences, 512-token prompts"
 
@@ -49,8 +50,10 @@ def parse():
                     help="q4: the isolated Q4 projection (BASELINE configs[1] shapes), "
                          "a small case for profiling; tp: the 14B-class model (configs[4]) "
                          "tensor-parallel over the torchrun ranks")
-    ap.add_argument("--batch", type=int, default=64, help="(tp) sequences")
-    ap.add_argument("--prompt", type=int, default=1024, help="(tp) prompt tokens per sequence")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="sequences (decode: 4 = configs[2], 64 = configs[3]; tp: 64)")
+    ap.add_argument("--prompt", type=int, default=None,
+                    help="prompt tokens per sequence (decode: 512, configs[3]: 4096; tp: 1024)")
     ap.add_argument("--m", type=int, default=4)
     ap.add_argument("--k", type=int, default=2560)
     ap.add_argument("--n", type=int, default=20480)
@@ -153,11 +156,13 @@ def run_ours(args, ws, rank, local):
     spec = e4b_spec(n_layers=args.layers)
     w = synth_weights_device(spec, seed=1234)
     ctx = Context(local)
-    model = Model(ctx, spec, w, max_rows=BATCH * PROMPT)
+    model = Model(ctx, spec, w, max_rows=min(BATCH * PROMPT, MAX_ROWS))
     del w
     torch.cuda.empty_cache()
     max_pos = ((PROMPT + args.warmup + 2 * args.steps + 8 + 63) // 64) * 64
-    kv = KVCache(ctx, model, BATCH, max_pos, slide_cap=1024)
+    # sliding ring: the window plus the rows of one sequence in one prefill call
+    window = max(l.window for l in spec.layers)
+    kv = KVCache(ctx, model, BATCH, max_pos, slide_cap=window + min(PROMPT, MAX_ROWS))
     lib_stream = torch.cuda.ExternalStream(ctx.stream_ptr)
 
     def barrier():
@@ -229,7 +234,7 @@ def run_ours(args, ws, rank, local):
     s1.synchronize()
     lm_ms = s0.elapsed_time(s1) / n_rep
     lm_bytes = 4 * spec.hidden * spec.vocab + 4 * BATCH * spec.hidden
-    proj_ms, proj_bytes = time_q4(ctx, PROJ["M"], PROJ["K"], PROJ["N"], PROJ_COPIES, 3, 10)
+    proj_ms, proj_bytes = time_q4(ctx, BATCH, PROJ["K"], PROJ["N"], PROJ_COPIES, 3, 10)
     proj_gbs = proj_bytes / (proj_ms / 1e3) / 1e9
 
     q4 = spec.q4_bytes()
@@ -268,10 +273,11 @@ def run_ours(args, ws, rank, local):
                 "wall_s": round(wall_e2e, 4)},
         "gpu_launches": launches_per_step * args.steps,
         "roofline": {
-            "kernel": "gemv_stream_kernel (Q4 projection, M 4, gate|up K 2560 x N 20480)",
+            "kernel": (f"{'gemv_stream_kernel' if BATCH <= 8 else 'gemm_tc_kernel'} "
+                       f"(Q4 projection, M {BATCH}, gate|up K 2560 x N 20480)"),
             "bound": "hbm", "achieved": round(proj_gbs, 1), "peak": hbm, "unit": "GB/s",
             "frac": round(proj_gbs / hbm, 4),
-            "traffic": profile_traffic("gemv_stream_kernel"),
+            "traffic": profile_traffic("gemv_stream_kernel") if BATCH <= 8 else None,
             "algorithmic_bytes": proj_bytes, "peak_source": peak_kind,
             "launch_ms": round(proj_ms, 5),
         },
@@ -290,7 +296,7 @@ def run_ours(args, ws, rank, local):
             "note": "Q4 weights + fp32 lm_head + KV read per decode step / step time",
         },
         "clocks": clk,
-        "first_ids": first[:BATCH],
+        "first_ids": first[:8],
     }
     if rank == 0 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(spec)
@@ -560,11 +566,21 @@ def run_tp(args, ws, rank, local):
 
 
 def main():
+    global BATCH, PROMPT, METRIC, WORKLOAD
     args = parse()
     ws, rank, local = dist_setup(args)
+    if args.case == "decode":
+        BATCH = args.batch or BATCH
+        PROMPT = args.prompt or PROMPT
+        if (BATCH, PROMPT) != (4, 512):
+            METRIC = f"decode tokens/s (batch {BATCH}), Gemma-4-E4B-shaped Q4 model"
+            WORKLOAD = (f"gemma4-e4b decode, batch {BATCH} independent sequences, "
+                        f"{PROMPT}-token prompts")
     if args.case == "q4":
         run_q4_case(args)
     elif args.case == "tp" and args.impl != "reference":
+        args.batch = args.batch or 64
+        args.prompt = args.prompt or 1024
         run_tp(args, ws, rank, local)
     elif args.impl == "reference":
         run_reference(args, ws, rank, local)

@@ -517,9 +517,19 @@ static GemvPlan plan_gemv(const ms_ctx* c, int M, int K, int n_tiles, bool allow
   GemvPlan pl{};
   const int chunks = K / kChunkK;
   if (allow_tc && M >= kTcMinRows) {
-    pl.tc = true;  // one CTA per (tile group, 128-row tile), all of K
-    pl.ksplit = 1;
-    pl.kseg = K;
+    // one CTA per (tile group, 128-row tile), all of K -- or k slices when
+    // that grid cannot fill the GPU (small batches of narrow projections);
+    // the slices' fp32 tiles are summed in k order by the last one
+    pl.tc = true;
+    const long tiles = (long)(padded_tiles(n_tiles) / kGroupTiles) * ((M + 127) / 128);
+    int ks = 1;
+    if (tiles < c->sm_count) ks = (int)std::min<long>((c->sm_count + tiles - 1) / tiles, 16);
+    ks = std::max(1, std::min(ks, chunks / 4));
+    while (ks > 1 && ((size_t)tiles * ks * 128 * 128 > c->part_floats || (size_t)tiles > c->n_counters))
+      --ks;
+    const int seg = (chunks + ks - 1) / ks;
+    pl.kseg = seg * kChunkK;
+    pl.ksplit = (chunks + seg - 1) / seg;
     return pl;
   }
   if (M <= 8) {

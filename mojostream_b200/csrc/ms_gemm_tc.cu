@@ -61,8 +61,11 @@ size_t tc_limb_bytes(int M, int K) { return (size_t)tc_rows_pad(M) * K * kTcLimb
 // Byte j of a 16-byte core row holds k = 2t + 8 (e & 1) + (e >> 1) of its
 // 16-k subtile (t = j / 4, e = j % 4): the order of the weight words.
 // rowf[m] = {(a / 2^22) * fin, fres}: the factors the epilogue applies.
-// CTA: 8 rows (one row group), 256 threads; thread (row tid % 8, subtile
-// tid / 8 + 32 j).  Rows >= M are written as zeros.
+// CTA (row group, k slice): 8 rows, 256 threads; thread (row tid % 8,
+// subtile tid / 8 + 32 j).  Every CTA of a row group takes the maximum over
+// the whole row (so small batches still spread over many CTAs) and
+// quantises its slice of the subtiles; slice 0 writes the row factors.
+// Rows >= M are written as zeros.
 constexpr int kQThreads = 256;
 __global__ void __launch_bounds__(kQThreads) quant_rows_kernel(const GemvParams p) {
   __shared__ float s_max[kQThreads / kWarp][8];
@@ -70,6 +73,8 @@ __global__ void __launch_bounds__(kQThreads) quant_rows_kernel(const GemvParams 
   const int m = blockIdx.x * 8 + r8;
   const int mt = m / kTcBM, r = m % kTcBM;
   const int nchunks = p.K / kChunkK, nsub = p.K / 16;
+  const int s_begin = (int)((long long)nsub * blockIdx.y / gridDim.y);
+  const int s_end = (int)((long long)nsub * (blockIdx.y + 1) / gridDim.y);
   const bool live = m < p.M;
   pdl_wait();
   pdl_trigger();
@@ -95,7 +100,7 @@ __global__ void __launch_bounds__(kQThreads) quant_rows_kernel(const GemvParams 
 
   // RMSNorm factors from the per-tile sums of squares: the 32 threads of a
   // row each sum a strided share, then one fixed-order tree (deterministic)
-  {
+  if (blockIdx.y == 0) {
     __shared__ float s_part[2][kQThreads / 8][8];
     float si = 0.f, sr = 0.f;
     if (live && p.in_stats)
@@ -121,7 +126,7 @@ __global__ void __launch_bounds__(kQThreads) quant_rows_kernel(const GemvParams 
     }
   }
 
-  for (int i = sub0; i < nsub; i += kQThreads / 8) {
+  for (int i = s_begin + sub0; i < s_end; i += kQThreads / 8) {
     float v[16];
     if (live) {
       const float4* v4 = reinterpret_cast<const float4*>(x + 16 * i);
@@ -170,10 +175,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const GemvParams
   __shared__ __align__(8) uint64_t full[kTcStages], conv[kTcStages], empty[kTcStages], done;
   __shared__ uint32_t s_tmem;
   __shared__ volatile int s_bad;
+  __shared__ int s_last;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int group = blockIdx.x, mt = blockIdx.y;
   const int nchunks = p.K / kChunkK;
+  // k slice of this CTA (split-K when the tile grid alone cannot fill the GPU)
+  const int kidx = blockIdx.z, seg = p.kseg / kChunkK;
+  const int c_begin = kidx * seg;
+  const int n_loc = min(nchunks, c_begin + seg) - c_begin;
 
   if (threadIdx.x == 0) {
     s_bad = 0;
@@ -199,10 +209,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const GemvParams
     // ------------------------------------------------------- producer --
     if (lane == 0) {
       pdl_wait();  // the limbs are the previous kernel's output
-      const uint8_t* a_src = p.lq + (size_t)mt * nchunks * kTcAStage;
-      const uint4* b_src = p.w + (size_t)group * nchunks * kGroupTiles * kWarp;
+      const uint8_t* a_src = p.lq + ((size_t)mt * nchunks + c_begin) * kTcAStage;
+      const uint4* b_src = p.w + ((size_t)group * nchunks + c_begin) * kGroupTiles * kWarp;
       int c = 0;
-      for (; c < nchunks; ++c) {
+      for (; c < n_loc; ++c) {
         const int s = c % kTcStages;
         if (c >= kTcStages && !mbar_wait(&empty[s], ((c / kTcStages) - 1) & 1)) {
           atomicOr(p.err, kErrWaitTimeout);
@@ -224,7 +234,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const GemvParams
     // ------------------------------------------------------ MMA issuer --
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_i8(kTcBM, kTcBN);
-      for (int c = 0; c < nchunks; ++c) {
+      for (int c = 0; c < n_loc; ++c) {
         const int s = c % kTcStages;
         const uint32_t ph = (c / kTcStages) & 1;
         if (!mbar_wait(&full[s], ph) || !mbar_wait(&conv[s], ph)) {
@@ -254,7 +264,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const GemvParams
     // row g, high nibbles row g + 8, k order {2t, 2t+8, 2t+1, 2t+9}.
     const int ci = threadIdx.x - 2 * kWarp;
     const int tl = ci >> 5, g = (ci & 31) >> 2, t = ci & 3;
-    for (int c = 0; c < nchunks; ++c) {
+    for (int c = 0; c < n_loc; ++c) {
       const int s = c % kTcStages;
       if (!mbar_wait(&full[s], (c / kTcStages) & 1)) {
         atomicOr(p.err, kErrWaitTimeout);
@@ -315,7 +325,39 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const GemvParams
       }
     }
     bar_sync_n(2, kTcConvWarps * kWarp);
-    if (ok && !s_bad) {
+    bool finish = ok && !s_bad;
+    if (finish && p.ksplit > 1) {
+      // every k slice stores its rows < M; the last one (ticket) sums the
+      // slices in k order into S and finishes the tile
+      const int t8 = threadIdx.x - 2 * kWarp;  // 0 .. 255
+      const int rows = min(kTcBM, p.M - mt * kTcBM);
+      const size_t tile_id = (size_t)mt * gridDim.x + group;
+      float* part = p.part + tile_id * p.ksplit * (kTcBM * kTcBN);
+      for (int i = t8; i < rows * (kTcBN / 4); i += kTcConvWarps * kWarp) {
+        const int r = i / (kTcBN / 4), c4 = i % (kTcBN / 4);
+        __stcg(reinterpret_cast<float4*>(part + (size_t)kidx * kTcBM * kTcBN + r * kTcBN) + c4,
+               *reinterpret_cast<const float4*>(S + r * kTcRowS + 4 * c4));
+      }
+      bar_sync_n(2, kTcConvWarps * kWarp);
+      if (t8 == 0) s_last = ticket_acq_rel(p.counters + tile_id) == p.ksplit - 1;
+      bar_sync_n(2, kTcConvWarps * kWarp);
+      finish = s_last != 0;
+      if (finish) {
+        for (int i = t8; i < rows * (kTcBN / 4); i += kTcConvWarps * kWarp) {
+          const int r = i / (kTcBN / 4), c4 = i % (kTcBN / 4);
+          float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+          for (int kk = 0; kk < p.ksplit; ++kk) {
+            const float4 v = __ldcg(reinterpret_cast<const float4*>(
+                part + (size_t)kk * kTcBM * kTcBN + r * kTcBN) + c4);
+            a.x += v.x; a.y += v.y; a.z += v.z; a.w += v.w;
+          }
+          *reinterpret_cast<float4*>(S + r * kTcRowS + 4 * c4) = a;
+        }
+        if (t8 == 0) p.counters[tile_id] = 0;
+        bar_sync_n(2, kTcConvWarps * kWarp);
+      }
+    }
+    if (finish) {
       const int w8 = warp - 2;
       const int jt = lane >> 2;                  // tile of the group this lane covers
       const int tile = group * kGroupTiles + jt;
@@ -411,6 +453,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const GemvParams
 }
 
 cudaError_t launch_gemm_tc(const GemvParams& p, cudaStream_t s, bool pdl) {
+  if (p.ksplit < 1 || p.kseg % kChunkK || p.kseg <= 0 || (p.ksplit > 1 && (!p.part || !p.counters)) ||
+      (long long)p.kseg * (p.ksplit - 1) >= p.K)
+    return cudaErrorInvalidConfiguration;
   if (p.K % kChunkK || !p.lq || !p.rowf || !p.x || (p.ldx & 3) || ((uintptr_t)p.x & 15) ||
       ((uintptr_t)p.lq & 15) || ((uintptr_t)p.rowf & 7) || p.M <= 0)
     return cudaErrorInvalidConfiguration;
@@ -419,8 +464,12 @@ cudaError_t launch_gemm_tc(const GemvParams& p, cudaStream_t s, bool pdl) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   const int m_pad = tc_rows_pad(p.M);
   {
+    // k slices so that a small batch still fills the GPU (>= ~2 CTAs per SM)
+    const int groups = m_pad / 8, nsub = p.K / 16;
+    int ks = (2 * 148 + groups - 1) / groups;
+    ks = ks < 1 ? 1 : (ks > nsub / 32 ? (nsub / 32 > 0 ? nsub / 32 : 1) : ks);
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(m_pad / 8);
+    cfg.gridDim = dim3(groups, ks);
     cfg.blockDim = dim3(kQThreads);
     cfg.stream = s;
     cfg.attrs = attr;
@@ -429,7 +478,7 @@ cudaError_t launch_gemm_tc(const GemvParams& p, cudaStream_t s, bool pdl) {
     if (e != cudaSuccess) return e;
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(padded_tiles(p.n_tiles) / kGroupTiles, m_pad / kTcBM);
+  cfg.gridDim = dim3(padded_tiles(p.n_tiles) / kGroupTiles, m_pad / kTcBM, p.ksplit);
   cfg.blockDim = dim3(kTcThreads);
   cfg.dynamicSmemBytes = kTcSmem;
   cfg.stream = s;

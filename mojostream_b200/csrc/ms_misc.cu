@@ -20,8 +20,7 @@ namespace ms {
 // reduces its (max, index) per row; the last CTA (atomic ticket) reduces the
 // CTAs in order.
 // =========================================================================
-constexpr int kLmThreads = 128;
-constexpr int kLmCols = kLmThreads * 4;
+constexpr int kLmThreads = 128;  // CTA size of the 4-row pass (decode batches)
 constexpr int kLmUnroll = 8;
 
 __device__ __forceinline__ void argmax_merge(float& v, int& i, float v2, int i2) {
@@ -31,30 +30,31 @@ __device__ __forceinline__ void argmax_merge(float& v, int& i, float v2, int i2)
   }
 }
 
-template <int MR>
-__global__ void __launch_bounds__(kLmThreads) lm_head_kernel(const LmHeadParams p, int row0) {
+template <int MR, int NT>
+__global__ void __launch_bounds__(NT) lm_head_kernel(const LmHeadParams p, int row0) {
+  constexpr int LU = MR >= 16 ? 4 : kLmUnroll;  // W rows in flight (registers)
   extern __shared__ float xs[];  // [MR][D]
   __shared__ float s_inv[MR];
-  __shared__ float s_rv[kLmThreads / kWarp][MR];
-  __shared__ int s_ri[kLmThreads / kWarp][MR];
+  __shared__ float s_rv[NT / kWarp][MR];
+  __shared__ int s_ri[NT / kWarp][MR];
   __shared__ int s_last;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int col = blockIdx.x * kLmCols + tid * 4;
+  const int col = blockIdx.x * (NT * 4) + tid * 4;
   const bool col_ok = col + 3 < p.V;
   const int rows = min(MR, p.M - row0);
 
   // first k rows of W: independent of earlier kernels
-  float4 pre[kLmUnroll];
+  float4 pre[LU];
   if (col_ok) {
 #pragma unroll
-    for (int u = 0; u < kLmUnroll; ++u)
+    for (int u = 0; u < LU; ++u)
       if (u < p.D) pre[u] = ld_stream_f4(reinterpret_cast<const float4*>(p.W + (size_t)u * p.V + col));
   }
   pdl_trigger();
   pdl_wait();
 
-  for (int r = warp; r < MR; r += kLmThreads / kWarp) {
+  for (int r = warp; r < MR; r += NT / kWarp) {
     float inv = 1.f;
     if (r < rows && p.stats) {
       float s = 0.f;
@@ -65,7 +65,7 @@ __global__ void __launch_bounds__(kLmThreads) lm_head_kernel(const LmHeadParams 
     if (lane == 0) s_inv[r] = inv;
   }
   __syncthreads();
-  for (int idx = tid; idx < MR * p.D; idx += kLmThreads) {
+  for (int idx = tid; idx < MR * p.D; idx += NT) {
     const int r = idx / p.D, k = idx % p.D;
     float v = 0.f;
     if (r < rows) {
@@ -81,17 +81,17 @@ __global__ void __launch_bounds__(kLmThreads) lm_head_kernel(const LmHeadParams 
   for (int r = 0; r < MR; ++r) acc[r][0] = acc[r][1] = acc[r][2] = acc[r][3] = 0.f;
   if (col_ok) {
     int k0 = 0;
-    for (; k0 + kLmUnroll <= p.D; k0 += kLmUnroll) {
-      float4 w[kLmUnroll];
+    for (; k0 + LU <= p.D; k0 += LU) {
+      float4 w[LU];
 #pragma unroll
-      for (int u = 0; u < kLmUnroll; ++u) w[u] = pre[u];
-      const int kn = k0 + kLmUnroll;
+      for (int u = 0; u < LU; ++u) w[u] = pre[u];
+      const int kn = k0 + LU;
 #pragma unroll
-      for (int u = 0; u < kLmUnroll; ++u)
+      for (int u = 0; u < LU; ++u)
         if (kn + u < p.D)
           pre[u] = ld_stream_f4(reinterpret_cast<const float4*>(p.W + (size_t)(kn + u) * p.V + col));
 #pragma unroll
-      for (int u = 0; u < kLmUnroll; ++u) {
+      for (int u = 0; u < LU; ++u) {
 #pragma unroll
         for (int r = 0; r < MR; ++r) {
           const float a = xs[r * p.D + k0 + u];
@@ -143,7 +143,7 @@ __global__ void __launch_bounds__(kLmThreads) lm_head_kernel(const LmHeadParams 
   if (tid < rows) {
     float bv = s_rv[0][tid];
     int bi = s_ri[0][tid];
-    for (int w = 1; w < kLmThreads / kWarp; ++w) argmax_merge(bv, bi, s_rv[w][tid], s_ri[w][tid]);
+    for (int w = 1; w < NT / kWarp; ++w) argmax_merge(bv, bi, s_rv[w][tid], s_ri[w][tid]);
     p.part_val[(size_t)(row0 + tid) * gridDim.x + blockIdx.x] = bv;
     p.part_idx[(size_t)(row0 + tid) * gridDim.x + blockIdx.x] = bi;
   }
@@ -151,7 +151,7 @@ __global__ void __launch_bounds__(kLmThreads) lm_head_kernel(const LmHeadParams 
   if (tid == 0) s_last = (ticket_acq_rel(p.counter) == (int)gridDim.x - 1);
   __syncthreads();
   if (!s_last) return;
-  for (int r = warp; r < rows; r += kLmThreads / kWarp) {
+  for (int r = warp; r < rows; r += NT / kWarp) {
     float bv = -INFINITY;
     int bi = 0x7fffffff;
     for (int c = lane; c < (int)gridDim.x; c += kWarp)
@@ -171,17 +171,20 @@ __global__ void __launch_bounds__(kLmThreads) lm_head_kernel(const LmHeadParams 
   if (tid == 0) *p.counter = 0;
 }
 
-template <int MR>
+// NT threads per CTA, 4 vocab columns each: more rows per pass hold more
+// normalised rows in shared memory, so the CTA grows with them to keep
+// enough warps per SM.
+template <int MR, int NT>
 static cudaError_t launch_lm_head_t(const LmHeadParams& p, int row0, cudaStream_t s, bool pdl) {
   const size_t smem = (size_t)MR * p.D * sizeof(float);
-  auto kern = lm_head_kernel<MR>;
+  auto kern = lm_head_kernel<MR, NT>;
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((p.V + kLmCols - 1) / kLmCols);
-  cfg.blockDim = dim3(kLmThreads);
+  cfg.gridDim = dim3((p.V + NT * 4 - 1) / (NT * 4));
+  cfg.blockDim = dim3(NT);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
@@ -201,9 +204,9 @@ cudaError_t launch_lm_head(const LmHeadParams& p, cudaStream_t s, bool pdl) {
   if (p.M > 4 && 8 * row_bytes <= 200 * 1024) mr = 8;
   if (p.M > 8 && 16 * row_bytes <= 200 * 1024) mr = 16;
   for (int row0 = 0; row0 < p.M; row0 += mr) {
-    cudaError_t e = mr == 16 ? launch_lm_head_t<16>(p, row0, s, pdl && row0 == 0)
-                  : mr == 8  ? launch_lm_head_t<8>(p, row0, s, pdl && row0 == 0)
-                             : launch_lm_head_t<4>(p, row0, s, pdl && row0 == 0);
+    cudaError_t e = mr == 16 ? launch_lm_head_t<16, 512>(p, row0, s, pdl && row0 == 0)
+                  : mr == 8  ? launch_lm_head_t<8, 256>(p, row0, s, pdl && row0 == 0)
+                             : launch_lm_head_t<4, kLmThreads>(p, row0, s, pdl && row0 == 0);
     if (e != cudaSuccess) return e;
   }
   return cudaSuccess;
