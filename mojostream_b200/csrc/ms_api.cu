@@ -1187,6 +1187,9 @@ static ms_status run_layer(ms_ctx* c, ms_model* m, const ms_kv* kv, int li, int 
     const long ctas_per_split = (long)M * L.d.n_kv_heads;
     const int min_per = 8;  // positions per split at least
     int splits = (int)std::max<long>(1, (c->sm_count + ctas_per_split - 1) / ctas_per_split);
+    // long spans: at most ~256 positions per split, so a large batch at long
+    // context still has enough CTAs to keep every SM streaming
+    splits = std::max(splits, (span + 255) / 256);
     if (mk) splits = mk_attn_splits(c->sm_count, M, L.d.n_kv_heads);  // one unit per CTA
     splits = std::min(splits, std::max(1, (span + min_per - 1) / min_per));
     splits = std::min(splits, attention_max_splits());

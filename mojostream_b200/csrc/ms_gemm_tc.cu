@@ -464,9 +464,10 @@ cudaError_t launch_gemm_tc(const GemvParams& p, cudaStream_t s, bool pdl) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   const int m_pad = tc_rows_pad(p.M);
   {
-    // k slices so that a small batch still fills the GPU (>= ~2 CTAs per SM)
+    // k slices so that a small batch still has about one CTA per SM (each
+    // slice re-reads the rows for their maximum, so large batches keep one)
     const int groups = m_pad / 8, nsub = p.K / 16;
-    int ks = (2 * 148 + groups - 1) / groups;
+    int ks = (148 + groups - 1) / groups;
     ks = ks < 1 ? 1 : (ks > nsub / 32 ? (nsub / 32 > 0 ? nsub / 32 : 1) : ks);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(groups, ks);
