@@ -12,7 +12,8 @@
 // launched back to back with programmatic dependent launch, so each kernel's
 // weight stream starts while its predecessor drains.
 #include <cuda_runtime.h>
-#include <nccl.h>
+#include <dlfcn.h>
+#include <nccl.h>  // types only: the functions are resolved at ms_tp_init (nccl_api)
 
 #include <algorithm>
 #include <cmath>
@@ -221,6 +222,36 @@ static bool is_device_ptr(const void* p) {
   return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
 }
 
+// NCCL is resolved on first use instead of linked: a single-GPU host never
+// needs it, and in a process that already loaded an NCCL (torch does), the
+// same soname resolves to that copy rather than binding it to another one.
+struct NcclApi {
+  bool ok = false;
+  ncclResult_t (*get_unique_id)(ncclUniqueId*) = nullptr;
+  ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*all_reduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                             cudaStream_t) = nullptr;
+  ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+  const char* (*error_string)(ncclResult_t) = nullptr;
+};
+
+static const NcclApi& nccl_api() {
+  static NcclApi api = [] {
+    NcclApi a;
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) return a;
+    a.get_unique_id = (decltype(a.get_unique_id))dlsym(h, "ncclGetUniqueId");
+    a.comm_init_rank = (decltype(a.comm_init_rank))dlsym(h, "ncclCommInitRank");
+    a.all_reduce = (decltype(a.all_reduce))dlsym(h, "ncclAllReduce");
+    a.comm_destroy = (decltype(a.comm_destroy))dlsym(h, "ncclCommDestroy");
+    a.error_string = (decltype(a.error_string))dlsym(h, "ncclGetErrorString");
+    a.ok = a.get_unique_id && a.comm_init_rank && a.all_reduce && a.comm_destroy && a.error_string;
+    return a;
+  }();
+  return api;
+}
+
 // ------------------------------------------------------------------ context --
 
 extern "C" int ms_abi_version(void) { return MS_ABI_VERSION; }
@@ -316,7 +347,7 @@ extern "C" ms_status ms_destroy(ms_ctx* c) {
   cudaFree(c->d_err);
   cudaFree(c->lq);
   cudaFree(c->rowf);
-  if (c->comm) ncclCommDestroy(c->comm);
+  if (c->comm) nccl_api().comm_destroy(c->comm);
   if (c->ev[0]) cudaEventDestroy(c->ev[0]);
   if (c->ev[1]) cudaEventDestroy(c->ev[1]);
   if (c->stream) cudaStreamDestroy(c->stream);
@@ -356,12 +387,13 @@ extern "C" ms_status ms_memcpy(ms_ctx* c, void* dst, const void* src, size_t byt
 
 // ------------------------------------------------------ tensor parallelism --
 
+
 extern "C" size_t ms_tp_unique_id_bytes(void) { return sizeof(ncclUniqueId); }
 
 extern "C" ms_status ms_tp_unique_id(void* out, size_t bytes) {
   if (!out || bytes < sizeof(ncclUniqueId)) return MS_ERR_INVALID_ARG;
   ncclUniqueId id;
-  if (ncclGetUniqueId(&id) != ncclSuccess) return MS_ERR_NCCL;
+  if (!nccl_api().ok || nccl_api().get_unique_id(&id) != ncclSuccess) return MS_ERR_NCCL;
   memcpy(out, &id, sizeof(id));
   return MS_OK;
 }
@@ -371,12 +403,13 @@ extern "C" ms_status ms_tp_init(ms_ctx* c, int world, int rank, const void* uniq
   if (c->comm || c->tp_world > 1) return fail(c, MS_ERR_STATE, "tensor parallelism already set up");
   if (world == 1) return MS_OK;
   MS_CUDA(c, cudaSetDevice(c->device));
+  if (!nccl_api().ok) return fail(c, MS_ERR_NCCL, "libnccl.so.2 could not be loaded");
   ncclUniqueId id;
   memcpy(&id, unique_id, sizeof(id));
-  const ncclResult_t r = ncclCommInitRank(&c->comm, world, id, rank);
+  const ncclResult_t r = nccl_api().comm_init_rank(&c->comm, world, id, rank);
   if (r != ncclSuccess) {
     c->comm = nullptr;
-    return fail(c, MS_ERR_NCCL, "ncclCommInitRank: %s", ncclGetErrorString(r));
+    return fail(c, MS_ERR_NCCL, "ncclCommInitRank: %s", nccl_api().error_string(r));
   }
   c->tp_world = world;
   c->tp_rank = rank;
@@ -388,7 +421,8 @@ extern "C" int ms_tp_world(const ms_ctx* c) { return c ? c->tp_world : 0; }
 #define MS_NCCL(c, call)                                                             \
   do {                                                                               \
     const ncclResult_t r_ = (call);                                                  \
-    if (r_ != ncclSuccess) return fail(c, MS_ERR_NCCL, "%s: %s", #call, ncclGetErrorString(r_)); \
+    if (r_ != ncclSuccess)                                                           \
+      return fail(c, MS_ERR_NCCL, "%s: %s", #call, nccl_api().error_string(r_));    \
   } while (0)
 
 // --------------------------------------------------------- repack helpers --
@@ -1255,7 +1289,7 @@ static ms_status run_layer(ms_ctx* c, ms_model* m, const ms_kv* kv, int li, int 
     }
     MS_TRY(emit_proj(c, mk, p, pl, s, pdl));
     if (tp) {
-      MS_NCCL(c, ncclAllReduce(m->P, m->P, (size_t)M * D, ncclFloat, ncclSum, c->comm, s));
+      MS_NCCL(c, nccl_api().all_reduce(m->P, m->P, (size_t)M * D, ncclFloat, ncclSum, c->comm, s));
       MS_CUDA(c, launch_resid_add(y, ys, m->P, x, xs, L.d.ple, M, D, s));
     }
   }
@@ -1303,7 +1337,7 @@ static ms_status run_layer(ms_ctx* c, ms_model* m, const ms_kv* kv, int li, int 
     }
     MS_TRY(emit_proj(c, mk, p, pl, s, pdl));
     if (tp) {
-      MS_NCCL(c, ncclAllReduce(m->P, m->P, (size_t)M * D, ncclFloat, ncclSum, c->comm, s));
+      MS_NCCL(c, nccl_api().all_reduce(m->P, m->P, (size_t)M * D, ncclFloat, ncclSum, c->comm, s));
       MS_CUDA(c, launch_resid_add(x, xs, m->P, y, ys, 1.f, M, D, s));
     }
   }
@@ -1424,7 +1458,7 @@ static ms_status lm_head_launch(ms_ctx* c, ms_model* m, const float* x, const fl
   MS_CUDA(c, launch_lm_head(p, s, pdl));
   if (tp) {
     MS_CUDA(c, launch_argmax_pack(m->d_key, m->d_maxv, m->d_lidx, M, m->vocab0, s));
-    MS_NCCL(c, ncclAllReduce(m->d_key, m->d_key, M, ncclUint64, ncclMax, c->comm, s));
+    MS_NCCL(c, nccl_api().all_reduce(m->d_key, m->d_key, M, ncclUint64, ncclMax, c->comm, s));
     MS_CUDA(c, launch_argmax_unpack(argmax, m->d_key, M, s));
   }
   return MS_OK;
@@ -1436,7 +1470,7 @@ static ms_status embed_rows(ms_ctx* c, ms_model* m, float* x, int M, cudaStream_
   MS_CUDA(c, launch_embed_stats(x, m->S[0], m->lm_head, m->d_ids, M, m->hidden, m->vocab_local, s,
                                 pdl, m->vocab0));
   if (c->tp_world > 1) {
-    MS_NCCL(c, ncclAllReduce(x, x, (size_t)M * m->hidden, ncclFloat, ncclSum, c->comm, s));
+    MS_NCCL(c, nccl_api().all_reduce(x, x, (size_t)M * m->hidden, ncclFloat, ncclSum, c->comm, s));
     MS_CUDA(c, launch_rowstats(m->S[0], x, m->hidden, M, m->hidden, s, false));
   }
   return MS_OK;
