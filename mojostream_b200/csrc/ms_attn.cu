@@ -1,47 +1,277 @@
 // ms_attn.cu -- flash-decode GQA attention over the paged KV cache, one
-// launch per layer: grid (split, kv head, row), 8 warps, about one CTA per SM
-// in decode.  Each CTA runs one unit of ms_attn_unit.cuh, which documents the
-// reference semantics and the algorithm.
+// launch per layer: grid (split, KV head, row).
+//
+// Reference semantics: gqa_attention_decode (src/main.mojo:445-519),
+// compute_sliding_attention / compute_full_attention
+// (src/inference/gemma4_e4b.mojo:259-411): row m (sequence seq[m] at absolute
+// position pos[m]) attends positions lo..pos, lo = max(0, pos + 1 - window)
+// on sliding layers and 0 otherwise; score = (q . k) / sqrt(hd); softmax with
+// the maximum subtracted; out = sum p * v.  Query head h reads KV head
+// h / (n_heads / n_kv); a CTA serves all G query heads of its KV head, so each
+// K / V row is read once for G heads.
+//
+// Per-warp streams (no CTA barrier in the main loop): the CTA's positions go
+// to its NW warps round-robin; every warp brings its next positions' K and V
+// rows into a private ring of P slots with cp.async.bulk (its own mbarriers),
+// so up to NW * P rows are in flight per CTA.  A warp holds its lanes' slices
+// of the G query vectors and of the G running outputs in registers; per
+// position it forms the G scores (lane partial dot products, one warp
+// all-reduce each), updates its running maximum / sum / output (online
+// softmax, expf), and moves on.  At the end the warps are combined through
+// shared memory (log-sum-exp weights), and the row's splits are merged by the
+// last CTA of the (row, KV head) in split order: results do not depend on
+// timing.  (The persistent decode kernel keeps the chunked unit of
+// ms_attn_unit.cuh, whose shared memory fits next to its weight ring.)
 #include "ms_attn_unit.cuh"
 
 namespace ms {
 
-constexpr int kAttnWarps = 8;
-constexpr int kAttnThreads = kAttnWarps * kWarp;
-// one chunk buffer: 44 KB of K and V rows (two buffers + the unit's static
-// shared state leave room for 2 CTAs per SM)
-constexpr int kAttnBufFloats = 11264;
+template <int HD, int G>
+struct WarpAttn {
+  static constexpr int NW = (G * HD >= 2048) ? 4 : 8;  // warps (registers: q + out slices)
+  static constexpr int NT = NW * kWarp;
+  static constexpr int VEC = HD >= 128 ? 4 : 2;        // floats per lane load
+  static constexpr int NV = HD / (kWarp * VEC);        // loads per lane per row
+  static constexpr int PL = NV * VEC;                  // dims per lane
+  static constexpr int SLOT = 2 * HD;                  // floats: K row then V row
+  // slots per warp: about 64 KB of rows in flight per CTA, and at least enough
+  // for the end-of-unit combine (NW x G x (HD + 2) floats) to reuse the rings
+  static constexpr int P0 = 65536 / (NW * SLOT * 4);
+  static constexpr int PMIN = (G * (HD + 2) + SLOT - 1) / SLOT;
+  static constexpr int P1 = P0 > 8 ? 8 : (P0 < 2 ? 2 : P0);
+  static constexpr int P = P1 < PMIN ? PMIN : P1;
+  static constexpr size_t smem = (size_t)NW * P * SLOT * sizeof(float);
+  static constexpr int ST = HD + 4;                    // partial row stride (16 B)
+  static_assert(NW * G * (HD + 2) <= NW * P * SLOT, "combine buffer");
+};
+
+template <int VEC>
+__device__ __forceinline__ void ld_vec(float* dst, const float* src) {
+  if constexpr (VEC == 4) {
+    const float4 v = *reinterpret_cast<const float4*>(src);
+    dst[0] = v.x; dst[1] = v.y; dst[2] = v.z; dst[3] = v.w;
+  } else {
+    const float2 v = *reinterpret_cast<const float2*>(src);
+    dst[0] = v.x; dst[1] = v.y;
+  }
+}
 
 template <int HD, int G>
-__global__ void __launch_bounds__(kAttnThreads) attn_kernel(const AttnParams p) {
-  extern __shared__ __align__(128) float sm[];  // [2][PC][2][HD]
-  __shared__ __align__(8) uint64_t full[2];
-  __shared__ AttnShared sh;
-  if (threadIdx.x == 0) {
-    mbar_init(&full[0], 1);
-    mbar_init(&full[1], 1);
+__global__ void __launch_bounds__(WarpAttn<HD, G>::NT) attn_kernel(const AttnParams p) {
+  using S = WarpAttn<HD, G>;
+  constexpr int NW = S::NW, NT = S::NT, P = S::P, PL = S::PL, VEC = S::VEC, ST = S::ST;
+  extern __shared__ __align__(128) float sm[];  // [NW][P][K row | V row]
+  __shared__ __align__(8) uint64_t bar[NW][P];
+  __shared__ float s_w[G][kAttnMaxSplits];
+  __shared__ int s_last, s_bad;
+
+  const int split = blockIdx.x, hk = blockIdx.y, m = blockIdx.z;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (tid == 0) {
+    for (int w = 0; w < NW; ++w)
+      for (int s = 0; s < P; ++s) mbar_init(&bar[w][s], 1);
     mbar_fence_init();
+    s_bad = 0;
   }
   __syncthreads();
   pdl_wait();
   pdl_trigger();
-  uint32_t ac = 0;
-  attn_unit<HD, G, kAttnThreads, kAttnBufFloats>(p, blockIdx.x, blockIdx.y, blockIdx.z, sm, full,
-                                                 ac, sh, 1);
-}
 
-template <int HD, int G>
-static size_t attn_smem() {
-  return (size_t)2 * AttnShape<HD, kAttnBufFloats>::PC * 2 * HD * sizeof(float);
+  const int pos = p.pos[m], seq = p.seq[m];
+  const int lo = p.window > 0 ? max(0, pos + 1 - p.window) : 0;
+  const int n = pos + 1 - lo;
+  const int per = max((n + p.n_splits - 1) / p.n_splits, p.chunk);
+  const int ns = (n + per - 1) / per;
+  if (split >= ns) return;  // CTA-uniform
+  const int t_begin = lo + split * per;
+  const int t_end = min(pos + 1, t_begin + per);
+  const int n_pos = t_end - t_begin;
+  const int cnt = n_pos > warp ? (n_pos - warp + NW - 1) / NW : 0;  // this warp's positions
+  const size_t head_off = (size_t)hk * HD;
+  float* ring = sm + (size_t)warp * P * S::SLOT;
+
+  // lane 0 streams position i of this warp (t_begin + warp + NW i) into slot i % P
+  auto issue = [&](int i) {
+    const int t = t_begin + warp + NW * i;
+    const int slot = i % P;
+    const size_t off = kv_row_offset(p.kv.block_table, p.kv.bt_stride, p.kv.page, p.kv.cap,
+                                     p.kv.circular, seq, t, p.kv.kv_dim) + head_off;
+    mbar_expect_tx(&bar[warp][slot], (uint32_t)(S::SLOT * sizeof(float)));
+    bulk_g2s(ring + slot * S::SLOT, p.kv.k + off, HD * sizeof(float), &bar[warp][slot]);
+    bulk_g2s(ring + slot * S::SLOT + HD, p.kv.v + off, HD * sizeof(float), &bar[warp][slot]);
+  };
+  if (lane == 0)
+    for (int i = 0; i < cnt && i < P; ++i) issue(i);
+
+  // this lane's slices: dims (v * 32 + lane) * VEC + e
+  float q[G][PL], acc[G][PL], mrun[G], lrun[G];
+#pragma unroll
+  for (int h = 0; h < G; ++h) {
+    const float* qh = p.q + (size_t)m * p.ldq + (size_t)(hk * G + h) * HD;
+#pragma unroll
+    for (int v = 0; v < S::NV; ++v) {
+      if constexpr (VEC == 4) {
+        const float4 t = __ldcg(reinterpret_cast<const float4*>(qh + (v * kWarp + lane) * VEC));
+        q[h][v * 4] = t.x; q[h][v * 4 + 1] = t.y; q[h][v * 4 + 2] = t.z; q[h][v * 4 + 3] = t.w;
+      } else {
+        const float2 t = __ldcg(reinterpret_cast<const float2*>(qh + (v * kWarp + lane) * VEC));
+        q[h][v * 2] = t.x; q[h][v * 2 + 1] = t.y;
+      }
+    }
+#pragma unroll
+    for (int e = 0; e < PL; ++e) acc[h][e] = 0.f;
+    mrun[h] = -INFINITY;
+    lrun[h] = 0.f;
+  }
+
+  int i = 0;
+  for (; i < cnt; ++i) {
+    const int slot = i % P;
+    if (!mbar_wait(&bar[warp][slot], (i / P) & 1)) {
+      if (lane == 0) {
+        atomicOr(p.err, kErrWaitTimeout);
+        s_bad = 1;
+      }
+      break;
+    }
+    float kk[PL], vv[PL];
+    const float* kr = ring + slot * S::SLOT;
+#pragma unroll
+    for (int v = 0; v < S::NV; ++v) {
+      ld_vec<VEC>(&kk[v * VEC], kr + (v * kWarp + lane) * VEC);
+      ld_vec<VEC>(&vv[v * VEC], kr + HD + (v * kWarp + lane) * VEC);
+    }
+    __syncwarp();  // every lane holds its slice: the slot can be refilled
+    if (lane == 0 && i + P < cnt) issue(i + P);
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+      float d = 0.f;
+#pragma unroll
+      for (int e = 0; e < PL; ++e) d = fmaf(q[h][e], kk[e], d);
+      const float s = warp_sum(d) * p.scale;
+      const float m_new = fmaxf(mrun[h], s);
+      const float corr = expf(mrun[h] - m_new);  // 0 on the first position
+      const float ew = expf(s - m_new);
+      lrun[h] = lrun[h] * corr + ew;
+#pragma unroll
+      for (int e = 0; e < PL; ++e) acc[h][e] = fmaf(ew, vv[e], acc[h][e] * corr);
+      mrun[h] = m_new;
+    }
+  }
+  if (i < cnt && lane == 0) {
+    // a copy never arrived: let this warp's issued copies land (bounded)
+    for (int j = i; j < cnt && j < i + P; ++j) mbar_wait(&bar[warp][j % P], (j / P) & 1);
+  }
+  __syncthreads();  // every warp is past its ring: it becomes the combine buffer
+  if (s_bad) return;
+
+  // ---- combine the warps: comb[w][h][0..HD) outputs, [HD] max, [HD+1] sum ----
+  float* comb = sm;
+#pragma unroll
+  for (int h = 0; h < G; ++h) {
+    float* c = comb + ((size_t)warp * G + h) * (HD + 2);
+#pragma unroll
+    for (int v = 0; v < S::NV; ++v)
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) c[(v * kWarp + lane) * VEC + e] = acc[h][v * VEC + e];
+    if (lane == 0) {
+      c[HD] = mrun[h];
+      c[HD + 1] = lrun[h];
+    }
+  }
+  __syncthreads();
+  float* part_base = p.part + (((size_t)m * p.n_kv + hk) * p.n_splits + split) * G * ST;
+  for (int idx = tid; idx < G * HD; idx += NT) {
+    const int h = idx / HD, d = idx % HD;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) M = fmaxf(M, comb[((size_t)w * G + h) * (HD + 2) + HD]);
+    float a = 0.f, L = 0.f;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) {
+      const float* c = comb + ((size_t)w * G + h) * (HD + 2);
+      const float f = expf(c[HD] - M);  // 0 for warps without positions
+      a = fmaf(c[d], f, a);
+      L = fmaf(c[HD + 1], f, L);
+    }
+    if (ns == 1) {
+      p.out[(size_t)m * p.ldo + (hk * G + h) * HD + d] = a / L;
+    } else {
+      __stcg(part_base + (size_t)h * ST + d, a);
+      if (d == 0) {
+        __stcg(part_base + (size_t)h * ST + HD, M);
+        __stcg(part_base + (size_t)h * ST + HD + 1, L);
+      }
+    }
+  }
+  if (ns == 1) return;
+
+  // ---- merge the splits: the last CTA of (row, KV head) does it in order ---
+  __syncthreads();  // partials written
+  int* ctr = p.counters + (size_t)m * p.n_kv + hk;
+  if (tid == 0) s_last = (ticket_acq_rel(ctr) == ns - 1);
+  __syncthreads();
+  if (!s_last) return;
+  for (int h = warp; h < G; h += NW) {
+    const float* pr0 = p.part + ((size_t)m * p.n_kv + hk) * p.n_splits * G * ST;
+    float Ms[kAttnMaxSplits / kWarp], Ls[kAttnMaxSplits / kWarp];
+    float Mx = -INFINITY;
+#pragma unroll
+    for (int qq = 0; qq < kAttnMaxSplits / kWarp; ++qq) {
+      const int sp = lane + qq * kWarp;
+      const float* pp = pr0 + ((size_t)sp * G + h) * ST;
+      Ms[qq] = sp < ns ? __ldcg(pp + HD) : -INFINITY;
+      Ls[qq] = sp < ns ? __ldcg(pp + HD + 1) : 0.f;
+    }
+#pragma unroll
+    for (int qq = 0; qq < kAttnMaxSplits / kWarp; ++qq) Mx = fmaxf(Mx, Ms[qq]);
+    Mx = warp_max(Mx);
+    float L = 0.f;
+#pragma unroll
+    for (int qq = 0; qq < kAttnMaxSplits / kWarp; ++qq) {
+      const int sp = lane + qq * kWarp;
+      if (sp < ns) {
+        const float f = expf(Ms[qq] - Mx);
+        s_w[h][sp] = f;
+        L += Ls[qq] * f;
+      }
+    }
+    L = warp_sum(L);
+    __syncwarp();
+    const float invL = 1.0f / L;
+    for (int sp = lane; sp < ns; sp += kWarp) s_w[h][sp] *= invL;
+  }
+  __syncthreads();
+  const float* pr0 = p.part + ((size_t)m * p.n_kv + hk) * p.n_splits * G * ST;
+  for (int idx = tid; idx < G * HD / 4; idx += NT) {
+    const int h = idx / (HD / 4), d4 = idx % (HD / 4);
+    float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int sp0 = 0; sp0 < ns; sp0 += kAttnMergeBatch) {
+      float4 v[kAttnMergeBatch];
+#pragma unroll
+      for (int b = 0; b < kAttnMergeBatch; ++b)
+        if (sp0 + b < ns)
+          v[b] = __ldcg(reinterpret_cast<const float4*>(pr0 + ((size_t)(sp0 + b) * G + h) * ST + d4 * 4));
+#pragma unroll
+      for (int b = 0; b < kAttnMergeBatch; ++b)
+        if (sp0 + b < ns) {
+          const float w = s_w[h][sp0 + b];
+          a.x = fmaf(w, v[b].x, a.x); a.y = fmaf(w, v[b].y, a.y);
+          a.z = fmaf(w, v[b].z, a.z); a.w = fmaf(w, v[b].w, a.w);
+        }
+    }
+    *reinterpret_cast<float4*>(p.out + (size_t)m * p.ldo + (hk * G + h) * HD + d4 * 4) = a;
+  }
+  if (tid == 0) *ctr = 0;
 }
 
 template <int HD, int G>
 static cudaError_t launch_t(const AttnParams& p, cudaStream_t s, bool pdl) {
-  const size_t smem = attn_smem<HD, G>();
+  using S = WarpAttn<HD, G>;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.n_splits, p.n_kv, p.M);
-  cfg.blockDim = dim3(kAttnThreads);
-  cfg.dynamicSmemBytes = smem;
+  cfg.blockDim = dim3(S::NT);
+  cfg.dynamicSmemBytes = S::smem;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -70,16 +300,14 @@ cudaError_t launch_attention(const AttnParams& p, cudaStream_t s, bool pdl) {
   return cudaErrorInvalidConfiguration;
 }
 
-// Positions of one chunk buffer for head_dim hd.
-int attention_block_positions(int hd) { return kAttnBufFloats / (2 * hd); }
 int attention_max_splits() { return kAttnMaxSplits; }
 
 cudaError_t prepare_attention() {
   cudaError_t e = cudaSuccess;
-#define MS_ATTN_PREP(HDV, GV)                                                                 \
-  if (e == cudaSuccess && attn_smem<HDV, GV>() > 48 * 1024)                                  \
+#define MS_ATTN_PREP(HDV, GV)                                                                  \
+  if (e == cudaSuccess && WarpAttn<HDV, GV>::smem > 48 * 1024)                                \
     e = cudaFuncSetAttribute(attn_kernel<HDV, GV>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
-                             (int)attn_smem<HDV, GV>());
+                             (int)WarpAttn<HDV, GV>::smem);
   MS_ATTN_CASES(MS_ATTN_PREP)
 #undef MS_ATTN_PREP
   return e;

@@ -162,7 +162,6 @@ cudaError_t launch_gemm_tc(const GemvParams& p, cudaStream_t s, bool pdl);
 int tc_rows_pad(int M);
 size_t tc_limb_bytes(int M, int K);
 cudaError_t launch_attention(const AttnParams& p, cudaStream_t s, bool pdl);
-int attention_block_positions(int head_dim);
 // tiled attention for prefill: one CTA per (query block, KV head)
 cudaError_t launch_attention_prefill(const AttnParams& p, cudaStream_t s, bool pdl);
 int attention_prefill_tokens(int head_dim, int group);  // tokens per query block
