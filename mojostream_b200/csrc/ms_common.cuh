@@ -171,6 +171,39 @@ __device__ __forceinline__ int ticket_acq_rel(int* ctr) {
   return old;
 }
 
+// Cross-GPU (peer memory over NVLink) variants: system scope.
+__device__ __forceinline__ void fence_acq_rel_sys() {
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
+}
+__device__ __forceinline__ int ld_acquire_sys(const int* p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ float4 ld_sys_f4(const float4* p) {
+  float4 r;
+  asm volatile("ld.relaxed.sys.global.v4.f32 {%0,%1,%2,%3}, [%4];"
+               : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w)
+               : "l"(p)
+               : "memory");
+  return r;
+}
+// One thread: wait until *ctr >= target (a peer's counter), about one second
+// at most; false on timeout.
+__device__ __forceinline__ bool wait_counter_sys(const int* ctr, int target) {
+  unsigned long long t0;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+  for (unsigned int i = 0;; ++i) {
+    if (ld_acquire_sys(ctr) >= target) return true;
+    if ((i & 255) == 255) {
+      unsigned long long t;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+      if (t - t0 > 1000000000ull) return false;
+    }
+    __nanosleep(100);
+  }
+}
+
 // Error bits a kernel can leave for the host (ms_sync reports them).
 constexpr int kErrWaitTimeout = 1;
 

@@ -357,6 +357,49 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const GemvParams
         bar_sync_n(2, kTcConvWarps * kWarp);
       }
     }
+    if (finish && p.peer_tiles) {
+      // tensor parallel: this rank's share of the tile -> its peer-visible
+      // buffer, one release per tile (use counter), wait until every rank's
+      // counter for the tile reached the same use, then sum the ranks' tiles
+      // in rank order (the same bits on every rank) into S
+      const int t8 = threadIdx.x - 2 * kWarp;
+      const int rows = min(kTcBM, p.M - mt * kTcBM);
+      const size_t tile_id = (size_t)mt * gridDim.x + group;
+      float* mine = p.peer_tiles[p.tp_rank] + tile_id * (kTcBM * kTcBN);
+      for (int i = t8; i < rows * (kTcBN / 4); i += kTcConvWarps * kWarp) {
+        const int r = i / (kTcBN / 4), c4 = i % (kTcBN / 4);
+        __stcg(reinterpret_cast<float4*>(mine + r * kTcBN) + c4,
+               *reinterpret_cast<const float4*>(S + r * kTcRowS + 4 * c4));
+      }
+      bar_sync_n(2, kTcConvWarps * kWarp);
+      if (t8 == 0) {
+        fence_acq_rel_sys();
+        const int use = atomicAdd_system(p.peer_flags[p.tp_rank] + tile_id, 1) + 1;
+        int ok_all = 1;
+        for (int r = 0; r < p.tp_world && ok_all; ++r)
+          if (r != p.tp_rank) ok_all = wait_counter_sys(p.peer_flags[r] + tile_id, use);
+        if (!ok_all) {
+          atomicOr(p.err, kErrWaitTimeout);
+          s_bad = 1;
+        }
+        fence_acq_rel_sys();
+      }
+      bar_sync_n(2, kTcConvWarps * kWarp);
+      finish = !s_bad;
+      if (finish) {
+        for (int i = t8; i < rows * (kTcBN / 4); i += kTcConvWarps * kWarp) {
+          const int r = i / (kTcBN / 4), c4 = i % (kTcBN / 4);
+          float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+          for (int rk = 0; rk < p.tp_world; ++rk) {
+            const float4 v = ld_sys_f4(reinterpret_cast<const float4*>(
+                p.peer_tiles[rk] + tile_id * (kTcBM * kTcBN) + r * kTcBN) + c4);
+            a.x += v.x; a.y += v.y; a.z += v.z; a.w += v.w;
+          }
+          *reinterpret_cast<float4*>(S + r * kTcRowS + 4 * c4) = a;
+        }
+        bar_sync_n(2, kTcConvWarps * kWarp);
+      }
+    }
     if (finish) {
       const int w8 = warp - 2;
       const int jt = lane >> 2;                  // tile of the group this lane covers

@@ -98,6 +98,13 @@ struct GemvParams {
   // tensor-core path: activation limbs and per-row factors (quant_rows_kernel)
   uint8_t* lq;
   float2* rowf;
+  // tensor parallel (tensor-core path): the finished output tile is summed
+  // over the ranks inside the epilogue.  peer_tiles[r] / peer_flags[r]: rank
+  // r's tile buffer ([tile][128 x 128] floats) and per-tile use counters, as
+  // mapped in this process (CUDA IPC); null = no cross-rank sum.
+  float* const* peer_tiles;
+  int* const* peer_flags;
+  int tp_world, tp_rank;
 };
 
 struct AttnParams {

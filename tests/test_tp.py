@@ -95,6 +95,29 @@ def test_two_gpu_tensor_parallel_matches_oracle(tmp_path, oracle_lib):
     om2 = oracle_lib.OracleModel(spec, w, 2, 64, slide_cap=48)
     x = np.random.default_rng(0).standard_normal((2, spec.hidden)).astype(np.float32)
     ref = om2.layer_forward(5, x, [0, 1], [0, 0]).astype(np.float64)
+    # rows > 8 (tensor-core projections, all-reduce fused into their epilogue)
+    om3 = oracle_lib.OracleModel(spec, w, 2, 64, slide_cap=48)
+    long_prompts = [[(37 * i + 11) % 4096 for i in range(12)], [(91 * i + 5) % 4096 for i in range(9)]]
+    last3 = []
+    for s_, p_ in enumerate(long_prompts):
+        x3 = om3.forward(om3.embed(p_), [s_] * len(p_), list(range(len(p_))))
+        last3.append(x3[-1])
+    ref_first3 = [int(v) for v in om3.argmax(om3.lm_head(np.stack(last3)))]
+    cur3, p3, ref_gen3 = list(ref_first3), [12, 9], []
+    for _ in range(3):
+        x3 = om3.forward(om3.embed(cur3), [0, 1], p3)
+        cur3 = om3.argmax(om3.lm_head(x3))
+        ref_gen3.append([int(v) for v in cur3])
+        p3 = [q + 1 for q in p3]
+    om4 = oracle_lib.OracleModel(spec, w, 2, 64, slide_cap=48)
+    x12 = np.random.default_rng(1).standard_normal((12, spec.hidden)).astype(np.float32)
+    ref12 = om4.layer_forward(3, x12, [0] * 12, list(range(12))).astype(np.float64)
+    for r in range(2):
+        assert res[r]["first3"] == ref_first3
+        assert [list(map(int, g)) for g in res[r]["gen3"]] == ref_gen3
+        got12 = np.asarray(res[r]["layer3_12"])
+        err12 = np.sqrt(((got12 - ref12) ** 2).mean() / (ref12 ** 2).mean())
+        assert err12 < 1e-4, (r, err12)
     for r in range(2):
         assert res[r]["first"] == ref_first
         assert [list(map(int, g)) for g in res[r]["gen"]] == [list(map(int, g)) for g in ref_gen]

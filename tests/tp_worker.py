@@ -46,8 +46,26 @@ def main(prefix):
     xg = torch.from_numpy(x).cuda()
     model.layer_forward(5, xg, kv2, [0, 1], [0, 0])
     torch.cuda.synchronize()
+    # rows > 8: the tensor-core projections with the all-reduce inside their
+    # epilogue (a 16-row prefill chunk, then 5 rows; a 12-row layer)
+    kv3 = KVCache(ctx, model, 2, 64, slide_cap=48)
+    long_prompts = [[(37 * i + 11) % 4096 for i in range(12)], [(91 * i + 5) % 4096 for i in range(9)]]
+    ids3 = sum(long_prompts, [])
+    seq3 = [0] * 12 + [1] * 9
+    pos3 = list(range(12)) + list(range(9))
+    first3 = model.prefill(kv3, ids3, seq3, pos3)
+    gen3 = model.generate(kv3, first3, [0, 1], [12, 9], 3)
+    kv4 = KVCache(ctx, model, 2, 64, slide_cap=48)
+    x12 = np.random.default_rng(1).standard_normal((12, spec.hidden)).astype(np.float32)
+    xg12 = torch.from_numpy(x12).cuda()
+    model.layer_forward(3, xg12, kv4, [0] * 12, list(range(12)))
+    torch.cuda.synchronize()
     out = {"first": [int(v) for v in first], "gen": np.asarray(gen).tolist(),
-           "layer5": xg.cpu().numpy().astype(np.float64).tolist()}
+           "layer5": xg.cpu().numpy().astype(np.float64).tolist(),
+           "first3": [int(v) for v in first3], "gen3": np.asarray(gen3).tolist(),
+           "layer3_12": xg12.cpu().numpy().astype(np.float64).tolist()}
+    kv4.close()
+    kv3.close()
     with open(f"{prefix}.{rank}.json", "w") as f:
         json.dump(out, f)
     kv2.close()
