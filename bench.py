@@ -54,6 +54,11 @@ def parse():
                     help="sequences (decode: 4 = configs[2], 64 = configs[3]; tp: 64)")
     ap.add_argument("--prompt", type=int, default=None,
                     help="prompt tokens per sequence (decode: 512, configs[3]: 4096; tp: 1024)")
+    ap.add_argument("--temperature", type=float, default=0.0,
+                    help="token-loop sampling (default greedy, the north-star mode; the "
+                         "reference's e4b loop uses 0.7)")
+    ap.add_argument("--penalty", type=float, default=1.0,
+                    help="repetition penalty (the reference's e4b loop uses 1.2)")
     ap.add_argument("--m", type=int, default=4)
     ap.add_argument("--k", type=int, default=2560)
     ap.add_argument("--n", type=int, default=20480)
@@ -157,6 +162,8 @@ def run_ours(args, ws, rank, local):
     w = synth_weights_device(spec, seed=1234)
     ctx = Context(local)
     model = Model(ctx, spec, w, max_rows=min(BATCH * PROMPT, MAX_ROWS))
+    if args.temperature > 0.01 or args.penalty > 1.0:
+        model.set_sampling(args.temperature, args.penalty, 1234)
     del w
     torch.cuda.empty_cache()
     max_pos = ((PROMPT + args.warmup + 2 * args.steps + 8 + 63) // 64) * 64
@@ -245,6 +252,8 @@ def run_ours(args, ws, rank, local):
     value = tokens / (dev_ms / 1000.0)
     e2e_val = tokens / (e2e_ms / 1000.0)
     launches_per_step = 1 + 5 * spec.n_layers + (BATCH + 3) // 4 + 1
+    if args.temperature > 0.01 or args.penalty > 1.0:
+        launches_per_step += 1  # the sampler after the lm_head
 
     result = {
         "metric": METRIC,
@@ -266,6 +275,8 @@ def run_ours(args, ws, rank, local):
                                                             PROMPT + args.warmup + args.steps],
             "parallelism": f"replicas x{ws}" if ws > 1 else "single GPU",
             "l2": "weights + lm_head 4.66 GB >> 126 MB L2 (no flush needed)",
+            "sampling": ({"temperature": args.temperature, "penalty": args.penalty}
+                         if args.temperature > 0.01 or args.penalty > 1.0 else "greedy"),
         },
         "ttft_ms": round(ttft_ms, 3),
         "e2e": {"value": round(e2e_val, 2), "unit": "tokens/s",

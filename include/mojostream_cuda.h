@@ -213,6 +213,36 @@ MS_API ms_status ms_generate(ms_ctx *ctx, const ms_model *model, ms_kv *kv, cons
  * own work or timing events with the library's. */
 MS_API void *ms_ctx_stream(ms_ctx *ctx);
 
+/* ---------------------------------------------------------------- sampling */
+
+/* temperature_sampling (src/inference/lm_head.mojo:198-254) on M rows at once.
+ * logits [M][V] fp32 device (read only: the reference rewrites its row in
+ * place).  Row r's "generated" list is hist[hist_off[r] .. hist_off[r+1])
+ * (device int arrays, hist_off with M + 1 entries; both NULL = empty).
+ * penalty > 1: every occurrence of an id in the list divides its logit if
+ * positive, multiplies it otherwise.  temperature <= 0.01: the first maximum.
+ * Otherwise softmax(logits / temperature) and the first id whose running sum
+ * reaches target = ((seed * 6364136223846793005 + 1442695040888963407) &
+ * 0x7FFFFFFF) / 2^31 with seed = seeds[r] (device uint64 array; the reference
+ * draws it from perf_counter_ns).  Where rounding leaves the running sum
+ * short of the target, the last id with a nonzero weight (the reference
+ * returns V - 1).  out_ids [M] device.  M <= 65535, V <= 8388608.
+ * Asynchronous. */
+MS_API ms_status ms_sample(ms_ctx *ctx, const float *logits, int M, int V, const int *hist,
+                           const int *hist_off, float temperature, float penalty,
+                           const uint64_t *seeds, int *out_ids, void *stream);
+
+/* Sampling of the token loop (ms_decode_step, ms_generate and ms_prefill's
+ * first ids; the reference's loop calls temperature_sampling with T = 0.7,
+ * penalty 1.2, gemma4_e4b_infer.mojo:38-39, 139, 179).  Default: temperature
+ * 0, penalty 1 (the plain greedy argmax).  A row's "generated" list is every
+ * token the cache has been fed for its sequence up to and including the row's
+ * position (prompt + generated ids; ms_kv_reset clears it), its seed
+ * splitmix64(seed ^ (seq << 32 | pos)), so a generation repeats for a seed.
+ * Under tensor parallelism every rank makes the same call. */
+MS_API ms_status ms_set_sampling(ms_ctx *ctx, const ms_model *model, float temperature,
+                                 float penalty, uint64_t seed);
+
 /* ------------------------------------------------------ tensor parallelism */
 
 /* No counterpart in the reference (which runs one CPU process): the larger

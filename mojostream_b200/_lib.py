@@ -73,6 +73,10 @@ SIGNATURES = {
                                    _ip, _fp]),
     "ms_ctx_stream": (_vp, [_vp]),
     "ms_prefill": (ctypes.c_int, [_vp, _vp, _vp, _ip, _ip, _ip, ctypes.c_int, _ip]),
+    "ms_sample": (ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int, _vp, _vp, ctypes.c_float,
+                                 ctypes.c_float, _vp, _vp, _vp]),
+    "ms_set_sampling": (ctypes.c_int, [_vp, _vp, ctypes.c_float, ctypes.c_float,
+                                       ctypes.c_uint64]),
     "ms_tp_unique_id_bytes": (ctypes.c_size_t, []),
     "ms_tp_unique_id": (ctypes.c_int, [_vp, ctypes.c_size_t]),
     "ms_tp_init": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, _vp]),

@@ -56,6 +56,11 @@ struct ms_ctx {
   float2* rowf = nullptr;
   size_t rowf_n = 0;
   bool mk_ok = false;  // the persistent decode kernel can be co-resident on every SM
+  // ms_sample: chunk partials and per-row arrival tickets (grown on demand)
+  float2* samp_part = nullptr;
+  size_t samp_part_n = 0;
+  int* samp_cnt = nullptr;
+  size_t samp_cnt_n = 0;
   // tensor parallelism (ms_tp_init): heads and FFN columns sharded over ranks
   ncclComm_t comm = nullptr;
   int tp_world = 1, tp_rank = 0;
@@ -128,9 +133,20 @@ struct ms_model {
   int* d_hist = nullptr;
   int hist_cap = 0;
   int* h_stage = nullptr;  // pinned: ids | seq | pos | next (max_rows each) | error word
+  // token-loop sampling (ms_set_sampling): greedy without penalty when off
+  float samp_t = 0.f, samp_pen = 1.f;
+  unsigned long long samp_seed = 0;
+  int samp_ver = 0;
+  float* d_logits = nullptr;    // [logits_rows][vocab_local], read by the sampler
+  int logits_rows = 0;
+  float2* d_spart = nullptr;    // [max_rows][chunks] sampler partials
+  int* d_scnt = nullptr;        // [max_rows] sampler tickets
+  float2* d_rowsum = nullptr;   // TP: this rank's (max, sum) per row
+  float2* d_rowsum_all = nullptr;  // TP: [W][max_rows]
+  bool sampling() const { return samp_t > 0.01f || samp_pen > 1.f; }
   // captured decode step
   cudaGraphExec_t gexec = nullptr;
-  int g_M = 0;
+  int g_M = 0, g_samp = -1;
   const ms_kv* g_kv = nullptr;
   std::vector<void*> allocs;
 };
@@ -142,6 +158,7 @@ struct ms_kv {
   std::vector<float*> k, v;
   int* bt_full = nullptr;
   int* bt_slide = nullptr;
+  int* tok = nullptr;  // [n_seq][max_pos] token fed at each position (-1: none)
   size_t bytes = 0;
 };
 
@@ -358,6 +375,8 @@ extern "C" ms_status ms_destroy(ms_ctx* c) {
   cudaFree(c->d_err);
   cudaFree(c->lq);
   cudaFree(c->rowf);
+  cudaFree(c->samp_part);
+  cudaFree(c->samp_cnt);
   if (c->comm) nccl_api().comm_destroy(c->comm);
   if (c->ev[0]) cudaEventDestroy(c->ev[0]);
   if (c->ev[1]) cudaEventDestroy(c->ev[1]);
@@ -1041,6 +1060,7 @@ extern "C" ms_status ms_model_destroy(ms_ctx* c, ms_model* m) {
   for (void* p : m->peer_maps) cudaIpcCloseMemHandle(p);
   for (void* p : m->allocs) cudaFree(p);
   if (m->d_hist) cudaFree(m->d_hist);
+  if (m->d_logits) cudaFree(m->d_logits);
   if (m->h_stage) cudaFreeHost(m->h_stage);
   delete m;
   return MS_OK;
@@ -1105,6 +1125,10 @@ extern "C" ms_status ms_kv_create(ms_ctx* c, const ms_model* m, int n_seq, int m
     cudaMemset(v, 0, n * sizeof(float));
     kv->bytes += 2 * n * sizeof(float);
   }
+  // the repetition-penalty history of every sequence
+  if (dev_alloc(c, (void**)&kv->tok, (size_t)n_seq * max_pos * sizeof(int)) != MS_OK)
+    return cleanup(MS_ERR_OOM);
+  cudaMemset(kv->tok, 0xFF, (size_t)n_seq * max_pos * sizeof(int));
   if (cudaDeviceSynchronize() != cudaSuccess) return cleanup(fail(c, MS_ERR_CUDA, "kv create"));
   *out = kv;
   return MS_OK;
@@ -1118,6 +1142,7 @@ extern "C" ms_status ms_kv_destroy(ms_ctx* c, ms_kv* kv) {
   for (float* p : kv->v) cudaFree(p);
   cudaFree(kv->bt_full);
   cudaFree(kv->bt_slide);
+  cudaFree(kv->tok);
   delete kv;
   return MS_OK;
 }
@@ -1133,6 +1158,7 @@ extern "C" ms_status ms_kv_reset(ms_ctx* c, ms_kv* kv) {
     MS_CUDA(c, cudaMemsetAsync(kv->k[i], 0, n, c->stream));
     MS_CUDA(c, cudaMemsetAsync(kv->v[i], 0, n, c->stream));
   }
+  MS_CUDA(c, cudaMemsetAsync(kv->tok, 0xFF, (size_t)kv->n_seq * kv->max_pos * sizeof(int), c->stream));
   return MS_OK;
 }
 
@@ -1548,11 +1574,96 @@ static ms_status lm_head_launch(ms_ctx* c, ms_model* m, const float* x, const fl
   return MS_OK;
 }
 
+// Buffers of the token-loop sampler; the logits block grows to `rows` rows
+// (outside graph capture; a captured decode step holding the old block is
+// dropped).
+static ms_status ensure_sampler(ms_ctx* c, ms_model* m, int rows) {
+  if (!m->d_spart) {
+    const size_t nch = (m->vocab_local + kSampChunk - 1) / kSampChunk;
+    MS_TRY(model_alloc(m, &m->d_spart, (size_t)m->max_rows * nch));
+    MS_TRY(model_alloc(m, &m->d_scnt, (size_t)m->max_rows));
+    MS_CUDA(c, cudaMemset(m->d_scnt, 0, m->max_rows * sizeof(int)));
+    if (c->tp_world > 1) {
+      MS_TRY(model_alloc(m, &m->d_rowsum, (size_t)m->max_rows));
+      MS_TRY(model_alloc(m, &m->d_rowsum_all, (size_t)c->tp_world * m->max_rows));
+    }
+  }
+  if (m->logits_rows < rows) {
+    MS_CUDA(c, cudaStreamSynchronize(c->stream));
+    if (m->gexec) {
+      cudaGraphExecDestroy(m->gexec);
+      m->gexec = nullptr;
+    }
+    cudaFree(m->d_logits);
+    m->d_logits = nullptr;
+    m->logits_rows = 0;
+    MS_TRY(dev_alloc(c, (void**)&m->d_logits, (size_t)rows * m->vocab_local * sizeof(float)));
+    m->logits_rows = rows;
+  }
+  return MS_OK;
+}
+
+// temperature_sampling (lm_head.mojo:198-254) of the M rows in d_logits into
+// out (device ids).  History: the cache's token table up to each row's
+// position; seed of a row: splitmix64(seed ^ (seq << 32 | pos)).  Tensor
+// parallel: greedy combines (value, index) keys like the plain argmax; with a
+// temperature the ranks all-gather their (max, sum) per row and the rank that
+// holds the target picks (an all-reduce max leaves its id everywhere).
+static ms_status sample_rows(ms_ctx* c, ms_model* m, const ms_kv* kv, int M, const int* seq,
+                             const int* pos, int* out, cudaStream_t s) {
+  SampleParams p{};
+  p.logits = m->d_logits;
+  p.ld = m->vocab_local;
+  p.M = M;
+  p.V = m->vocab_local;
+  p.v0 = m->vocab0;
+  p.nchunk = (m->vocab_local + kSampChunk - 1) / kSampChunk;
+  p.tok = kv ? kv->tok : nullptr;
+  p.seq = seq;
+  p.pos = pos;
+  p.tok_ld = kv ? kv->max_pos : 0;
+  p.temperature = m->samp_t;
+  p.penalty = m->samp_pen;
+  p.seed = m->samp_seed;
+  p.part = m->d_spart;
+  p.counter = m->d_scnt;
+  p.tp_world = c->tp_world;
+  p.tp_rank = c->tp_rank;
+  if (c->tp_world == 1) {
+    p.out = out;
+    MS_CUDA(c, launch_sample(p, s));
+    return MS_OK;
+  }
+  if (m->samp_t <= 0.01f) {
+    p.out = m->d_lidx;
+    p.maxval = m->d_maxv;
+    MS_CUDA(c, launch_sample(p, s));
+    MS_CUDA(c, launch_argmax_pack(m->d_key, m->d_maxv, m->d_lidx, M, m->vocab0, s));
+    MS_NCCL(c, nccl_api().all_reduce(m->d_key, m->d_key, M, ncclUint64, ncclMax, c->comm, s));
+    MS_CUDA(c, launch_argmax_unpack(out, m->d_key, M, s));
+    return MS_OK;
+  }
+  p.rowsum = m->d_rowsum;
+  MS_CUDA(c, launch_sample(p, s));
+  MS_NCCL(c, nccl_api().all_gather(m->d_rowsum, m->d_rowsum_all, 2 * (size_t)M, ncclFloat,
+                                   c->comm, s));
+  p.rowsum = nullptr;
+  p.rowsum_all = m->d_rowsum_all;
+  p.out = out;
+  MS_CUDA(c, launch_sample_pick(p, s));
+  MS_NCCL(c, nccl_api().all_reduce(out, out, M, ncclInt32, ncclMax, c->comm, s));
+  return MS_OK;
+}
+
 // Embedding rows of d_ids into x (+ stats in S[0]).  Tensor parallel: every
 // rank gathers the ids in its vocabulary slice, an all-reduce sums the rows.
-static ms_status embed_rows(ms_ctx* c, ms_model* m, float* x, int M, cudaStream_t s, bool pdl) {
+// With a cache, the ids are also recorded at (d_seq, d_pos) in its token
+// table (the repetition-penalty history).
+static ms_status embed_rows(ms_ctx* c, ms_model* m, float* x, int M, cudaStream_t s, bool pdl,
+                            const ms_kv* kv = nullptr) {
+  const TokenLog log{kv ? kv->tok : nullptr, kv ? kv->max_pos : 0, m->d_seq, m->d_pos};
   MS_CUDA(c, launch_embed_stats(x, m->S[0], m->lm_head, m->d_ids, M, m->hidden, m->vocab_local, s,
-                                pdl, m->vocab0));
+                                pdl, m->vocab0, log));
   if (c->tp_world > 1) {
     MS_NCCL(c, nccl_api().all_reduce(x, x, (size_t)M * m->hidden, ncclFloat, ncclSum, c->comm, s));
     MS_CUDA(c, launch_rowstats(m->S[0], x, m->hidden, M, m->hidden, s, false));
@@ -1560,19 +1671,22 @@ static ms_status embed_rows(ms_ctx* c, ms_model* m, float* x, int M, cudaStream_
   return MS_OK;
 }
 
-extern "C" ms_status ms_embed(ms_ctx* c, const ms_model* mc, const int* ids, int M, float* x,
-                              void* stream) {
-  if (!c || !mc || !ids) return MS_ERR_INVALID_ARG;
-  ms_model* m = const_cast<ms_model*>(mc);
-  MS_TRY(check_x(c, x));
+static ms_status embed_ids(ms_ctx* c, ms_model* m, const int* ids, int M, float* x,
+                           cudaStream_t s, const ms_kv* kv) {
   if (m->vocab <= 0) return fail(c, MS_ERR_STATE, "model has no embedding table");
   if (M <= 0 || M > m->max_rows) return fail(c, MS_ERR_CAPACITY, "M=%d", M);
   for (int r = 0; r < M; ++r)
     if (ids[r] < 0 || ids[r] >= m->vocab)
       return fail(c, MS_ERR_INVALID_ARG, "token id %d outside 0..%d", ids[r], m->vocab - 1);
-  cudaStream_t s = pick(c, stream);
   MS_CUDA(c, cudaMemcpyAsync(m->d_ids, ids, M * sizeof(int), cudaMemcpyHostToDevice, s));
-  return embed_rows(c, m, x, M, s, false);
+  return embed_rows(c, m, x, M, s, false, kv);
+}
+
+extern "C" ms_status ms_embed(ms_ctx* c, const ms_model* mc, const int* ids, int M, float* x,
+                              void* stream) {
+  if (!c || !mc || !ids) return MS_ERR_INVALID_ARG;
+  MS_TRY(check_x(c, x));
+  return embed_ids(c, const_cast<ms_model*>(mc), ids, M, x, pick(c, stream), nullptr);
 }
 
 extern "C" ms_status ms_lm_head(ms_ctx* c, const ms_model* mc, const float* x, int M,
@@ -1590,14 +1704,19 @@ extern "C" ms_status ms_lm_head(ms_ctx* c, const ms_model* mc, const float* x, i
 
 // One decode step on the device: d_ids / d_seq / d_pos -> d_next.
 static ms_status decode_body(ms_ctx* c, ms_model* m, const ms_kv* kv, int M, cudaStream_t s) {
-  MS_TRY(embed_rows(c, m, m->X[0], M, s, true));
+  MS_TRY(embed_rows(c, m, m->X[0], M, s, true, kv));
   if (mk_usable(c, m, M)) {
     MS_TRY(mk_launch(c, m->mk_graph, s));  // op list built before the capture
   } else {
     for (int l = 0; l < m->n_layers; ++l)
       MS_TRY(run_layer(c, m, kv, l, M, m->X[0], m->S[0], m->X[1], m->S[1], s, true, false));
   }
-  MS_TRY(lm_head_launch(c, m, m->X[0], m->S[0], M, nullptr, m->d_next, s, true));
+  if (m->sampling()) {
+    MS_TRY(lm_head_launch(c, m, m->X[0], m->S[0], M, m->d_logits, nullptr, s, true));
+    MS_TRY(sample_rows(c, m, kv, M, m->d_seq, m->d_pos, m->d_next, s));
+  } else {
+    MS_TRY(lm_head_launch(c, m, m->X[0], m->S[0], M, nullptr, m->d_next, s, true));
+  }
   return MS_OK;
 }
 
@@ -1605,11 +1724,12 @@ static ms_status decode_body(ms_ctx* c, ms_model* m, const ms_kv* kv, int M, cud
 // positions (they are read from d_pos on the device), so one graph serves a
 // whole generation.
 static ms_status ensure_graph(ms_ctx* c, ms_model* m, const ms_kv* kv, int M) {
-  if (m->gexec && m->g_M == M && m->g_kv == kv) return MS_OK;
+  if (m->gexec && m->g_M == M && m->g_kv == kv && m->g_samp == m->samp_ver) return MS_OK;
   if (m->gexec) {
     cudaGraphExecDestroy(m->gexec);
     m->gexec = nullptr;
   }
+  if (m->sampling()) MS_TRY(ensure_sampler(c, m, M));
   cudaStream_t s = c->stream;
   cudaGraph_t g = nullptr;
   if (mk_usable(c, m, M))
@@ -1628,6 +1748,7 @@ static ms_status ensure_graph(ms_ctx* c, ms_model* m, const ms_kv* kv, int M) {
   if (e != cudaSuccess) return fail(c, MS_ERR_CUDA, "graph instantiate: %s", cudaGetErrorString(e));
   m->g_M = M;
   m->g_kv = kv;
+  m->g_samp = m->samp_ver;
   return MS_OK;
 }
 
@@ -1706,6 +1827,70 @@ extern "C" ms_status ms_generate(ms_ctx* c, const ms_model* mc, ms_kv* kv, const
 
 extern "C" void* ms_ctx_stream(ms_ctx* c) { return c ? (void*)c->stream : nullptr; }
 
+// ---------------------------------------------------------------- sampling --
+
+extern "C" ms_status ms_set_sampling(ms_ctx* c, const ms_model* mc, float temperature, float penalty,
+                                     uint64_t seed) {
+  if (!c || !mc) return MS_ERR_INVALID_ARG;
+  ms_model* m = const_cast<ms_model*>(mc);
+  if (m->vocab <= 0) return fail(c, MS_ERR_STATE, "model has no lm_head");
+  if (!std::isfinite(temperature) || !std::isfinite(penalty))
+    return fail(c, MS_ERR_INVALID_ARG, "temperature %g / penalty %g", temperature, penalty);
+  m->samp_t = temperature;
+  m->samp_pen = penalty;
+  m->samp_seed = seed;
+  ++m->samp_ver;  // the captured decode step is rebuilt on its next use
+  if (m->sampling()) MS_TRY(ensure_sampler(c, m, 0));
+  return MS_OK;
+}
+
+extern "C" ms_status ms_sample(ms_ctx* c, const float* logits, int M, int V, const int* hist,
+                               const int* hist_off, float temperature, float penalty,
+                               const uint64_t* seeds, int* out_ids, void* stream) {
+  if (!c || !logits || !out_ids) return MS_ERR_INVALID_ARG;
+  if (M <= 0 || M > 65535 || V <= 0) return fail(c, MS_ERR_SHAPE, "sample: M=%d V=%d", M, V);
+  const size_t nch = ((size_t)V + kSampChunk - 1) / kSampChunk;
+  if (nch > 1024) return fail(c, MS_ERR_SHAPE, "sample: V=%d above %d", V, 1024 * kSampChunk);
+  if (!hist != !hist_off) return fail(c, MS_ERR_INVALID_ARG, "sample: hist and hist_off go together");
+  if (!std::isfinite(temperature) || !std::isfinite(penalty))
+    return fail(c, MS_ERR_INVALID_ARG, "temperature %g / penalty %g", temperature, penalty);
+  if (temperature > 0.01f && !seeds) return fail(c, MS_ERR_INVALID_ARG, "sample: seeds needed");
+  if (!is_device_ptr(logits) || !is_device_ptr(out_ids) || (hist && !is_device_ptr(hist_off)) ||
+      (seeds && temperature > 0.01f && !is_device_ptr(seeds)))
+    return fail(c, MS_ERR_INVALID_ARG, "sample: logits, history, seeds and ids must be device memory");
+  cudaStream_t s = pick(c, stream);
+  if (c->samp_part_n < (size_t)M * nch || c->samp_cnt_n < (size_t)M) {
+    MS_CUDA(c, cudaDeviceSynchronize());
+    cudaFree(c->samp_part);
+    cudaFree(c->samp_cnt);
+    c->samp_part = nullptr;
+    c->samp_cnt = nullptr;
+    c->samp_part_n = c->samp_cnt_n = 0;
+    MS_TRY(dev_alloc(c, (void**)&c->samp_part, (size_t)M * nch * sizeof(float2)));
+    MS_TRY(dev_alloc(c, (void**)&c->samp_cnt, (size_t)M * sizeof(int)));
+    MS_CUDA(c, cudaMemset(c->samp_cnt, 0, (size_t)M * sizeof(int)));
+    c->samp_part_n = (size_t)M * nch;
+    c->samp_cnt_n = M;
+  }
+  SampleParams p{};
+  p.logits = logits;
+  p.ld = V;
+  p.M = M;
+  p.V = V;
+  p.nchunk = (int)nch;
+  p.hist = hist;
+  p.hist_off = hist_off;
+  p.temperature = temperature;
+  p.penalty = penalty;
+  p.seeds = temperature > 0.01f ? reinterpret_cast<const unsigned long long*>(seeds) : nullptr;
+  p.part = c->samp_part;
+  p.counter = c->samp_cnt;
+  p.tp_world = 1;
+  p.out = out_ids;
+  MS_CUDA(c, launch_sample(p, s));
+  return MS_OK;
+}
+
 extern "C" ms_status ms_prefill(ms_ctx* c, const ms_model* mc, ms_kv* kv, const int* ids,
                                 const int* seq, const int* pos, int n_tokens, int* first_ids) {
   if (!c || !mc || !kv || !ids || !seq || !pos) return MS_ERR_INVALID_ARG;
@@ -1734,9 +1919,9 @@ extern "C" ms_status ms_prefill(ms_ctx* c, const ms_model* mc, ms_kv* kv, const 
     const int M = std::min(m->max_rows, n_tokens - r0);
     st = check_rows(c, m, kv, seq + r0, pos + r0, M);
     if (st != MS_OK) break;
-    st = ms_embed(c, m, ids + r0, M, m->X[0], s);
-    if (st != MS_OK) break;
     st = upload_rows(c, m, seq + r0, pos + r0, M, s);
+    if (st != MS_OK) break;
+    st = embed_ids(c, m, ids + r0, M, m->X[0], s, kv);
     for (int l = 0; l < m->n_layers && st == MS_OK; ++l)
       st = run_layer(c, m, kv, l, M, m->X[0], m->S[0], m->X[1], m->S[1], s, true, true);
     if (st != MS_OK || !first_ids) continue;
@@ -1750,7 +1935,19 @@ extern "C" ms_status ms_prefill(ms_ctx* c, const ms_model* mc, ms_kv* kv, const 
   }
   if (st == MS_OK && first_ids && n_keep) {
     MS_CUDA(c, launch_rowstats(m->S[1], keep, m->hidden, n_keep, m->hidden, s, false));
-    st = lm_head_launch(c, m, keep, m->S[1], n_keep, nullptr, m->d_next, s, true);
+    if (m->sampling()) {  // each sequence's last row: its sequence and position
+      std::vector<int> ks(kept_seq), kp(n_keep);
+      for (int i = 0; i < n_keep; ++i) kp[i] = pos[last_row[kept_seq[i]]];
+      st = ensure_sampler(c, m, n_keep);
+      if (st == MS_OK) {
+        cudaMemcpyAsync(m->d_seq, ks.data(), n_keep * sizeof(int), cudaMemcpyHostToDevice, s);
+        cudaMemcpyAsync(m->d_pos, kp.data(), n_keep * sizeof(int), cudaMemcpyHostToDevice, s);
+        st = lm_head_launch(c, m, keep, m->S[1], n_keep, m->d_logits, nullptr, s, true);
+      }
+      if (st == MS_OK) st = sample_rows(c, m, kv, n_keep, m->d_seq, m->d_pos, m->d_next, s);
+    } else {
+      st = lm_head_launch(c, m, keep, m->S[1], n_keep, nullptr, m->d_next, s, true);
+    }
     std::vector<int> nxt(n_keep);
     if (st == MS_OK) {
       cudaMemcpyAsync(nxt.data(), m->d_next, n_keep * sizeof(int), cudaMemcpyDeviceToHost, s);

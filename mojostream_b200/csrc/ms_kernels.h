@@ -185,11 +185,20 @@ int mk_attn_splits(int n_cta, int M, int n_kv);
 cudaError_t launch_lm_head(const LmHeadParams& p, cudaStream_t s, bool pdl);
 cudaError_t launch_repack(uint4* out, const uint8_t* const* src, const int* src_n, int n_src,
                           const int* perm, int n_tiles, int K, cudaStream_t s);
+// Per-sequence token table (the repetition-penalty history):
+// tok[seq[m] * ld + pos[m]] = ids[m]; tok == null records nothing.
+struct TokenLog {
+  int* tok;
+  int ld;
+  const int* seq;
+  const int* pos;
+};
 // x[m] = column ids[m] - v0 of the [D][V] table (zeros when that column is
-// outside 0..V-1: another rank's vocabulary slice); stats per 16 columns.
+// outside 0..V-1: another rank's vocabulary slice); stats per 16 columns;
+// each id also goes to the token table.
 cudaError_t launch_embed_stats(float* x, float* stats, const float* W,
                                const int* ids, int M, int D, int V, cudaStream_t s, bool pdl,
-                               int v0 = 0);
+                               int v0 = 0, TokenLog log = TokenLog{nullptr, 0, nullptr, nullptr});
 // Tensor-parallel epilogue of the row-parallel projections (O, down):
 // out = resid * ple * inv_rms(resid * ple) + partial (already all-reduced),
 // plus the per-16-column sums of squares of out.
@@ -206,5 +215,39 @@ cudaError_t launch_rowstats(float* stats, const float* x, int ldx, int M, int D,
                             cudaStream_t s, bool pdl);
 cudaError_t launch_advance_step(int* ids, const int* next, int* pos, int* hist, int* step, int M,
                                 cudaStream_t s, bool pdl);
+
+// Repetition penalty + temperature sampling (temperature_sampling,
+// src/inference/lm_head.mojo:198-254) over rows of fp32 logits.
+constexpr int kSampChunk = 8192;   // logits columns per CTA
+constexpr int kSampThreads = 256;
+struct SampleParams {
+  const float* logits;  // [M][ld]: this rank's V columns (global ids v0 ..)
+  long long ld;
+  int M, V, v0;
+  int nchunk;           // ceil(V / kSampChunk)
+  // history of row r ("generated"): CSR (hist + hist_off[r] .. hist_off[r+1])
+  // when hist_off is set, else the token table tok[seq[r] * tok_ld + 0 .. pos[r]]
+  const int* hist;
+  const int* hist_off;
+  const int* tok;
+  const int* seq;
+  const int* pos;
+  int tok_ld;
+  float temperature, penalty;
+  const unsigned long long* seeds;  // per-row seeds (CSR mode) ...
+  unsigned long long seed;          // ... else one seed mixed with (seq, pos)
+  float2* part;        // [M][nchunk] chunk partials
+  int* counter;        // [M] arrival tickets (zero between launches)
+  float2* rowsum;      // tensor parallel: this rank's (max, sum) per row, or null
+  const float2* rowsum_all;  // [W][M] all ranks' (max, sum), pick launch
+  int tp_world, tp_rank;
+  int* out;            // [M] global ids (greedy TP: this rank's local index)
+  float* maxval;       // greedy TP: this rank's penalised maximum, or null
+};
+// Chunk pass (+ the pick for a single rank, by the last CTA of each row).
+cudaError_t launch_sample(const SampleParams& p, cudaStream_t s);
+// Tensor parallel, temperature mode: the pick after the all-gather of the
+// ranks' (max, sum); the owning rank writes the id, the others -1.
+cudaError_t launch_sample_pick(const SampleParams& p, cudaStream_t s);
 
 }  // namespace ms

@@ -218,10 +218,12 @@ cudaError_t launch_lm_head(const LmHeadParams& p, cudaStream_t s, bool pdl) {
 // squares that the first layer's RMSNorm consumes.
 // =========================================================================
 __global__ void embed_kernel(float* x, float* stats, const float* __restrict__ W,
-                             const int* __restrict__ ids, int M, int D, int V, int v0) {
+                             const int* __restrict__ ids, int M, int D, int V, int v0,
+                             TokenLog log) {
   pdl_trigger();
   pdl_wait();
   const int m = blockIdx.x;
+  if (log.tok && threadIdx.x == 0) log.tok[(size_t)log.seq[m] * log.ld + log.pos[m]] = ids[m];
   const int id = ids[m] - v0;
   const bool mine = id >= 0 && id < V;
   for (int t = threadIdx.x; t < D / kTileN; t += blockDim.x) {
@@ -355,7 +357,7 @@ __global__ void advance_kernel(int* ids, const int* next, int* pos, int* hist, i
 // Launchers with the extra buffers the C-ABI layer owns.
 cudaError_t launch_embed_stats(float* x, float* stats, const float* W,
                                const int* ids, int M, int D, int V, cudaStream_t s, bool pdl,
-                               int v0) {
+                               int v0, TokenLog log) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(M);
   cfg.blockDim = dim3(128);
@@ -365,7 +367,7 @@ cudaError_t launch_embed_stats(float* x, float* stats, const float* W,
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, embed_kernel, x, stats, W, ids, M, D, V, v0);
+  return cudaLaunchKernelEx(&cfg, embed_kernel, x, stats, W, ids, M, D, V, v0, log);
 }
 
 // =========================================================================

@@ -60,6 +60,27 @@ class Context:
         """The context's cudaStream_t (as an int)."""
         return lib().ms_ctx_stream(self.h)
 
+    def sample(self, logits, generated, temperature, penalty, seeds):
+        """temperature_sampling (lm_head.mojo:198-254) of every row of a CUDA
+        fp32 logits tensor [M][V] (ms_sample).  generated: one id list per row
+        (the repetition-penalty history); seeds: one uint64 per row (the
+        reference draws it from perf_counter_ns).  Returns int32 ids on the
+        device."""
+        import torch
+        M, V = logits.shape
+        hist = [int(t) for g in generated for t in g]
+        off = np.zeros(M + 1, np.int32)
+        off[1:] = np.cumsum([len(g) for g in generated])
+        h = torch.tensor(hist + [0], dtype=torch.int32, device=logits.device)
+        o = torch.tensor(off, dtype=torch.int32, device=logits.device)
+        sd = torch.tensor(np.asarray(seeds, np.uint64).view(np.int64), dtype=torch.int64,
+                          device=logits.device)
+        out = torch.empty(M, dtype=torch.int32, device=logits.device)
+        self.check(lib().ms_sample(self.h, _ptr(logits), M, V, _ptr(h), _ptr(o),
+                                   float(temperature), float(penalty), _ptr(sd), _ptr(out),
+                                   _stream()))
+        return out
+
     def tp_init(self, world, rank, unique_id):
         """Join a tensor-parallel group of `world` ranks (ms_tp_init); call
         before creating models.  unique_id: the bytes of tp_unique_id() made
@@ -196,6 +217,12 @@ class Model:
                                         _ptr(lg) if lg is not None else None, _ptr(am), _stream()))
         return lg, am
 
+    def set_sampling(self, temperature=0.0, penalty=1.0, seed=0):
+        """Sampling of decode_step / generate / prefill (ms_set_sampling);
+        the defaults are the greedy argmax."""
+        self.ctx.check(lib().ms_set_sampling(self.ctx.h, self.h, float(temperature),
+                                             float(penalty), int(seed) & 0xFFFFFFFFFFFFFFFF))
+
     def decode_step(self, kv, ids, seq, pos):
         M = len(ids)
         out = (ctypes.c_int * M)()
@@ -204,7 +231,8 @@ class Model:
         return list(out)
 
     def generate(self, kv, ids, seq, pos, steps, timing=False):
-        """Greedy tokens [steps][M]; with timing=True also the device ms of the loop."""
+        """Tokens [steps][M] (greedy unless set_sampling chose otherwise); with
+        timing=True also the device ms of the loop."""
         M = len(ids)
         out = (ctypes.c_int * (M * steps))()
         ms = ctypes.c_float(0.0)

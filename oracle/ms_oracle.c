@@ -410,6 +410,52 @@ int orc_argmax(const float *row, int n)
     return best;
 }
 
+float orc_sample_target(uint64_t seed)
+{
+    /* lm_head.mojo:246-247: one LCG step, low 31 bits, divided by
+     * Float32(0x7FFFFFFF), which rounds to 2^31. */
+    uint64_t lcg = (seed * 6364136223846793005ull + 1442695040888963407ull) & 0x7FFFFFFFull;
+    return (float)lcg / (float)0x7FFFFFFF;
+}
+
+int orc_temperature_sampling(float *row, int n, float temperature, const int *generated,
+                             int n_generated, float penalty, uint64_t seed)
+{
+    /* lm_head.mojo:213-221 */
+    if (penalty > 1.0f) {
+        for (int i = 0; i < n_generated; ++i) {
+            int tid = generated[i];
+            if (tid >= 0 && tid < n) {
+                float v = row[tid];
+                row[tid] = v > 0.0f ? v / penalty : v * penalty;
+            }
+        }
+    }
+    /* :223-230 */
+    if (temperature <= 0.01f) return orc_argmax(row, n);
+    /* :232-243 */
+    float inv_t = 1.0f / temperature;
+    float max_v = row[0];
+    for (int j = 1; j < n; ++j)
+        if (row[j] > max_v) max_v = row[j];
+    float sum_e = 0.0f;
+    for (int j = 0; j < n; ++j) {
+        float e = expf((row[j] - max_v) * inv_t);
+        row[j] = e;
+        sum_e += e;
+    }
+    float inv_s = 1.0f / sum_e;
+    for (int j = 0; j < n; ++j) row[j] = row[j] * inv_s;
+    /* :245-254 */
+    float target = orc_sample_target(seed);
+    float cdf = 0.0f;
+    for (int j = 0; j < n; ++j) {
+        cdf += row[j];
+        if (cdf >= target) return j;
+    }
+    return n - 1;
+}
+
 void orc_embed(float *x, const float *W, int D, int V, int id)
 {
     for (int r = 0; r < D; ++r) x[r] = W[(size_t)r * V + id];

@@ -92,6 +92,18 @@ void orc_lm_head(float *logits, float *x, const float *gamma, const float *W,
 /* lm_head.mojo:224-230: greedy pick, strict '>' so the first maximum wins. */
 int orc_argmax(const float *row, int n);
 
+/* lm_head.mojo:198-254 (temperature_sampling), one logits row, modified in
+ * place as there: repetition penalty once per entry of `generated` (divide
+ * positive, multiply non-positive logits) when penalty > 1; temperature <=
+ * 0.01 -> first maximum; else softmax(logits / T), normalised, and the first
+ * id whose running sum reaches target = ((seed * 6364136223846793005 +
+ * 1442695040888963407) & 0x7FFFFFFF) / 2^31 (the reference takes the seed
+ * from perf_counter_ns), n - 1 if the sum never reaches it. */
+int orc_temperature_sampling(float *row, int n, float temperature, const int *generated,
+                             int n_generated, float penalty, uint64_t seed);
+/* The target above, for a seed. */
+float orc_sample_target(uint64_t seed);
+
 /* lm_head.mojo:171-195: x = column `id` of the fp32 [D][V] table. */
 void orc_embed(float *x, const float *W, int D, int V, int id);
 

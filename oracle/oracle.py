@@ -71,6 +71,11 @@ def lib():
         L.orc_argmax.argtypes = [_f32p, ctypes.c_int]
         L.orc_argmax.restype = ctypes.c_int
         L.orc_embed.argtypes = [_f32p, _f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int]
+        L.orc_temperature_sampling.argtypes = [_f32p, ctypes.c_int, ctypes.c_float, _i32p,
+                                               ctypes.c_int, ctypes.c_float, ctypes.c_uint64]
+        L.orc_temperature_sampling.restype = ctypes.c_int
+        L.orc_sample_target.argtypes = [ctypes.c_uint64]
+        L.orc_sample_target.restype = ctypes.c_float
         _lib = L
     return _lib
 
@@ -220,3 +225,32 @@ class OracleModel:
         logits = _f32(logits)
         return [lib().orc_argmax(_p(np.ascontiguousarray(logits[r]), _f32p), logits.shape[1])
                 for r in range(logits.shape[0])]
+
+
+def temperature_sampling(row, temperature, generated, penalty, seed):
+    """lm_head.mojo:198-254 on one logits row (a copy; the reference writes
+    its row in place).  Returns the sampled id."""
+    r = np.ascontiguousarray(_f32(row)).copy()
+    g = np.ascontiguousarray(np.asarray(generated, np.int32))
+    return lib().orc_temperature_sampling(_p(r, _f32p), r.size, float(temperature),
+                                          _p(g, _i32p), g.size, float(penalty),
+                                          int(seed) & 0xFFFFFFFFFFFFFFFF)
+
+
+def sample_target(seed):
+    """The uniform draw of temperature_sampling for a seed (lm_head.mojo:246-247)."""
+    return float(lib().orc_sample_target(int(seed) & 0xFFFFFFFFFFFFFFFF))
+
+
+def splitmix64(z):
+    """SplitMix64 (Steele, Lea, Flood 2014): the token loop's per-row seed is
+    splitmix64(seed ^ (seq << 32 | pos))."""
+    M = 0xFFFFFFFFFFFFFFFF
+    z = (z + 0x9E3779B97F4A7C15) & M
+    z = ((z ^ (z >> 30)) * 0xBF58476D1CE4E5B9) & M
+    z = ((z ^ (z >> 27)) * 0x94D049BB133111EB) & M
+    return z ^ (z >> 31)
+
+
+def row_seed(seed, seq, pos):
+    return splitmix64((int(seed) ^ ((int(seq) << 32) | int(pos))) & 0xFFFFFFFFFFFFFFFF)

@@ -124,4 +124,11 @@ def test_two_gpu_tensor_parallel_matches_oracle(tmp_path, oracle_lib):
         got = np.asarray(res[r]["layer5"])
         err = np.sqrt(((got - ref) ** 2).mean() / (ref ** 2).mean())
         assert err < 1e-4, (r, err)
+    # sampled generations, checked teacher-forced against the oracle
+    from sampling_check import check_sampled_ids
+    for key, (T, pen) in {"samp": (0.7, 1.2), "samp_greedy": (0.0, 1.3)}.items():
+        om5 = oracle_lib.OracleModel(spec, w, 2, 64, slide_cap=48)
+        exact, near = check_sampled_ids(oracle_lib, om5, prompts, np.asarray(res[0][key]), T, pen,
+                                        2024)
+        assert exact >= 0.9 * 14, (key, exact, near)
     assert res[0] == res[1]

@@ -2,8 +2,9 @@
 
 Env: RANK, WORLD_SIZE, MASTER_PORT.  argv[1]: output path prefix.  Builds the
 small hybrid model sharded over WORLD_SIZE GPUs, prefills two prompts,
-decodes four greedy steps and runs one teacher-forced layer; writes the ids
-and the layer output as JSON (rank 0 and 1 must agree with the oracle).
+decodes four greedy steps and runs one teacher-forced layer, then a sampled
+generation; writes the ids and the layer output as JSON (rank 0 and 1 must
+agree with the oracle).
 """
 import datetime
 import json
@@ -60,7 +61,18 @@ def main(prefix):
     xg12 = torch.from_numpy(x12).cuda()
     model.layer_forward(3, xg12, kv4, [0] * 12, list(range(12)))
     torch.cuda.synchronize()
-    out = {"first": [int(v) for v in first], "gen": np.asarray(gen).tolist(),
+    # sampled token loop (temperature + repetition penalty, then greedy +
+    # penalty): the vocabulary shards combine through the sampler's collectives
+    sampled = {}
+    for key, (T, pen) in {"samp": (0.7, 1.2), "samp_greedy": (0.0, 1.3)}.items():
+        model.set_sampling(T, pen, 2024)
+        kv5 = KVCache(ctx, model, 2, 64, slide_cap=48)
+        f5 = model.prefill(kv5, ids, seq, pos)
+        g5 = model.generate(kv5, f5, [0, 1], [5, 3], 6)
+        sampled[key] = [[int(v) for v in f5]] + np.asarray(g5).tolist()
+        kv5.close()
+    model.set_sampling()
+    out = {"first": [int(v) for v in first], "gen": np.asarray(gen).tolist(), **sampled,
            "layer5": xg.cpu().numpy().astype(np.float64).tolist(),
            "first3": [int(v) for v in first3], "gen3": np.asarray(gen3).tolist(),
            "layer3_12": xg12.cpu().numpy().astype(np.float64).tolist()}
