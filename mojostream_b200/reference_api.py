@@ -8,15 +8,19 @@ replace, so host code and parity tests read like the reference's own:
   base_pos .. base_pos + B - 1 of one sequence, causal inside the batch)
 * ``e4b_forward_layer``    -- src/inference/gemma4_e4b.mojo:459-540 (same rows)
 * ``apply_final_norm`` + ``project_lm_head`` -- src/inference/lm_head.mojo:119-168
-* greedy ``temperature_sampling`` (lm_head.mojo:224-230) is the argmax that
-  ``apply_final_norm_and_project`` returns, computed on the device
+* ``temperature_sampling`` -- src/inference/lm_head.mojo:198-254 (row 0 of
+  the logits, repetition penalty over ``generated``, greedy at T <= 0.01);
+  greedy without a penalty is also the argmax ``apply_final_norm_and_project``
+  returns
 
 Differences (by design): the reference's kernels check nothing; here shapes and
 cache capacity are checked before launch and raise ``MsError``.  Weights are
 uploaded and repacked once (``Gemma4Weights`` wraps an ``ms_model``) instead of
-being passed per call.  Sampling with temperature > 0.01 and the repetition
-penalty are not provided yet.
+being passed per call.  ``temperature_sampling`` leaves the logits unchanged
+(the reference rewrites its row in place) and takes the seed of its draw as an
+argument (the reference reads perf_counter_ns, which stays the default).
 """
+import time
 from dataclasses import dataclass
 
 from . import runtime
@@ -96,3 +100,20 @@ def apply_final_norm_and_project(x, weights):
 
 
 Gemma4Weights = runtime.Model
+
+
+def temperature_sampling(logits, temperature, generated, penalty=1.0, seed=None, ctx=None):
+    """lm_head.mojo:198-254 on row 0 of a CUDA float32 logits tensor: returns
+    the sampled id (int).  seed: the draw's seed (default perf_counter_ns, as
+    the reference)."""
+    own = ctx is None
+    ctx = ctx or runtime.Context(logits.device.index or 0)
+    try:
+        if seed is None:
+            seed = time.perf_counter_ns()
+        out = ctx.sample(logits[:1].contiguous(), [list(generated)], temperature, penalty,
+                         [seed & 0xFFFFFFFFFFFFFFFF])
+        return int(out.cpu()[0])
+    finally:
+        if own:
+            ctx.close()

@@ -186,3 +186,17 @@ def test_decode_step_samples_like_generate(ctx, torch_cuda):
     model.set_sampling(0.0, 1.0, 5)
     g2 = model.generate(kv2, [5, 17], [0, 1], [0, 0], 4)
     assert np.array_equal(g1, g2)
+
+
+def test_reference_named_temperature_sampling(ctx, torch_cuda, oracle_lib):
+    """reference_api.temperature_sampling: row 0, as lm_head.mojo:198-254."""
+    from mojostream_b200 import reference_api as ra
+    torch = torch_cuda
+    rng = np.random.default_rng(3)
+    lg = (rng.standard_normal((4, 5000)) * 3).astype(np.float32)
+    gen = [int(lg[0].argmax())] * 2 + [7, 9]
+    t = torch.from_numpy(lg).cuda()
+    for T, pen, seed in [(0.0, 1.2, 0), (0.7, 1.2, 987654321), (1.5, 1.0, 42)]:
+        got = ra.temperature_sampling(t, T, gen, pen, seed=seed, ctx=ctx)
+        assert got == oracle_lib.temperature_sampling(lg[0], T, gen, pen, seed), (T, pen, seed)
+    assert np.array_equal(t.cpu().numpy(), lg)  # the logits are left as they were
