@@ -155,6 +155,62 @@ MS_API ms_status ms_model_destroy(ms_ctx *ctx, ms_model *model);
 /* Device bytes held for weights (Q4 tiles + lm_head). */
 MS_API size_t ms_model_weight_bytes(const ms_model *model);
 
+/* ------------------------------------------------------ .mojostream files */
+
+/* Header of a .mojostream file (src/streaming/mojostream.mojo:95-160; written
+ * by scripts/create_fake_model.py:194-281, format 1, and scripts/convert.py:
+ * 359-414, format 2 with the Engram extension in header bytes 64-127). */
+typedef struct {
+  int format_tag;        /* 1: uniform demo stack, 2: layer-typed (sliding / full) */
+  int n_layers, hidden, kv_dim, ffn_dim, n_heads, n_kv_heads;
+  uint64_t n_tensors, data_start, data_end, file_size;
+  /* format 2 (Engram extension; 0 when absent) */
+  int kv_shared_layers, sliding_kv_dim, full_kv_dim, ple_dim, sliding_window;
+} ms_file_info;
+
+/* Open a .mojostream file, read its header and tensor directory and run the
+ * reference's ShapeGuard and TensorGuard (src/streaming/stream_runner.mojo:
+ * 288-400): head / KV-head divisibility, n_tensors = 8 n_layers, per entry the
+ * (layer, type) sequence, its dims, scale > 0, 4096-aligned offset, inside the
+ * file.  Format 2 accepts layer-typed dims (Q / K / V / O of a layer follow
+ * its head_dim, one of sliding_kv_dim / n_kv and full_kv_dim / n_kv), which
+ * the reference's StreamingRunner guard rejects for Gemma-4-E4B.  info may be
+ * NULL.  On failure err (may be NULL) receives the message; MS_ERR_SHAPE for a
+ * failed guard, MS_ERR_INVALID_ARG for an unreadable file.  No device use. */
+MS_API ms_status ms_file_check(const char *path, ms_file_info *info, char *err, size_t err_bytes);
+
+/* What the file does not say, per attention kind.  Zero fields take the
+ * defaults in brackets. */
+typedef struct {
+  int full_every;         /* full attention iff (layer + 1) % full_every == 0
+                             [format 1: every layer; format 2: 6, E4B's
+                             rule, src/inference/gemma4_e4b.mojo:60-63]    */
+  int window;             /* sliding window [the file's sliding_window]   */
+  float slide_theta;      /* [1e4]                                          */
+  float full_theta;       /* [1e6; format 1: slide_theta]                   */
+  int full_rotary;        /* rotary dims of full layers [128, capped at
+                             head_dim; format 1: head_dim]; sliding layers
+                             rotate the whole head                          */
+  int max_rows;           /* as ms_model_desc.max_rows [64]                 */
+  size_t staging_bytes;   /* pinned host staging per buffer [64 MiB]        */
+} ms_load_opts;
+
+/* A model from a .mojostream file (and optionally an lm_head_proto.bin,
+ * load_lm_head, src/inference/lm_head.mojo:61-116: v2 = fp32 weights, final
+ * gamma and BOS embedding; v1 = Q4 weights, expanded to fp32 on the device,
+ * gamma 1).  The file is checked as ms_file_check does, then its tensor data
+ * streams to the device through two pinned host buffers in turn (a pread into
+ * one overlaps the cudaMemcpyAsync of the other, the reference's double buffer
+ * of sparse_pin.mojo:136-330 aimed at HBM) and is repacked as ms_model_create
+ * does.  With an lm_head file, token id 2 (BOS) embeds as the file's BOS
+ * vector (apply_bos_embedding, lm_head.mojo:133-143).  Tensor parallel: each
+ * rank loads the file and keeps its slices.  opts may be NULL. */
+MS_API ms_status ms_model_load(ms_ctx *ctx, const char *path, const char *lm_head_path,
+                               const ms_load_opts *opts, ms_model **out);
+/* Seconds and bytes of the last ms_model_load on this context (file reads +
+ * host-to-device copies, before the repack). */
+MS_API ms_status ms_load_stats(const ms_ctx *ctx, double *seconds, uint64_t *bytes);
+
 /* -------------------------------------------------------------- KV cache */
 
 /* Paged KV cache for n_seq sequences (KVCache, src/main.mojo:257-301;

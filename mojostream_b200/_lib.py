@@ -39,6 +39,26 @@ class ModelDesc(ctypes.Structure):
                 ("lm_head", _vp), ("final_gamma", _vp), ("max_rows", ctypes.c_int)]
 
 
+class FileInfo(ctypes.Structure):
+    """ms_file_info."""
+    _fields_ = [("format_tag", ctypes.c_int), ("n_layers", ctypes.c_int),
+                ("hidden", ctypes.c_int), ("kv_dim", ctypes.c_int), ("ffn_dim", ctypes.c_int),
+                ("n_heads", ctypes.c_int), ("n_kv_heads", ctypes.c_int),
+                ("n_tensors", ctypes.c_uint64), ("data_start", ctypes.c_uint64),
+                ("data_end", ctypes.c_uint64), ("file_size", ctypes.c_uint64),
+                ("kv_shared_layers", ctypes.c_int), ("sliding_kv_dim", ctypes.c_int),
+                ("full_kv_dim", ctypes.c_int), ("ple_dim", ctypes.c_int),
+                ("sliding_window", ctypes.c_int)]
+
+
+class LoadOpts(ctypes.Structure):
+    """ms_load_opts."""
+    _fields_ = [("full_every", ctypes.c_int), ("window", ctypes.c_int),
+                ("slide_theta", ctypes.c_float), ("full_theta", ctypes.c_float),
+                ("full_rotary", ctypes.c_int), ("max_rows", ctypes.c_int),
+                ("staging_bytes", ctypes.c_size_t)]
+
+
 # name -> (restype, argtypes); every symbol include/mojostream_cuda.h declares
 SIGNATURES = {
     "ms_abi_version": (ctypes.c_int, []),
@@ -58,6 +78,12 @@ SIGNATURES = {
     "ms_model_create": (ctypes.c_int, [_vp, ctypes.POINTER(ModelDesc), ctypes.POINTER(_vp)]),
     "ms_model_destroy": (ctypes.c_int, [_vp, _vp]),
     "ms_model_weight_bytes": (ctypes.c_size_t, [_vp]),
+    "ms_file_check": (ctypes.c_int, [ctypes.c_char_p, ctypes.POINTER(FileInfo), ctypes.c_char_p,
+                                     ctypes.c_size_t]),
+    "ms_model_load": (ctypes.c_int, [_vp, ctypes.c_char_p, ctypes.c_char_p,
+                                     ctypes.POINTER(LoadOpts), ctypes.POINTER(_vp)]),
+    "ms_load_stats": (ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_double),
+                                     ctypes.POINTER(ctypes.c_uint64)]),
     "ms_kv_create": (ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                     ctypes.POINTER(_vp)]),
     "ms_kv_destroy": (ctypes.c_int, [_vp, _vp]),

@@ -27,6 +27,7 @@
 #include <vector>
 
 #include "../../include/mojostream_cuda.h"
+#include "ms_internal.h"
 #include "ms_kernels.h"
 
 using namespace ms;
@@ -59,6 +60,8 @@ struct ms_ctx {
   // ms_sample: chunk partials and per-row arrival tickets (grown on demand)
   float2* samp_part = nullptr;
   size_t samp_part_n = 0;
+  double load_secs = 0.0;  // last ms_model_load: reads + host-to-device copies
+  uint64_t load_bytes = 0;
   int* samp_cnt = nullptr;
   size_t samp_cnt_n = 0;
   // tensor parallelism (ms_tp_init): heads and FFN columns sharded over ranks
@@ -96,6 +99,8 @@ struct ms_model {
   std::vector<LayerDev> layers;
   float* lm_head = nullptr;
   float* gamma = nullptr;
+  float* bos = nullptr;  // a loaded lm_head file's BOS embedding (token bos_id)
+  int bos_id = -1;
   size_t weight_bytes = 0;
   int max_q = 0, max_f = 0;
   // run buffers (max_rows rows)
@@ -386,6 +391,23 @@ extern "C" ms_status ms_destroy(ms_ctx* c) {
 }
 
 extern "C" const char* ms_last_error(const ms_ctx* c) { return c ? c->err.c_str() : "null context"; }
+
+// ------------------------------------------------- internal (ms_loader.cu) --
+
+ms_status ms_fail_(ms_ctx* c, ms_status s, const char* msg) { return fail(c, s, "%s", msg); }
+cudaStream_t ms_stream_(ms_ctx* c) { return c->stream; }
+int ms_device_(const ms_ctx* c) { return c->device; }
+void ms_set_load_stats_(ms_ctx* c, double seconds, uint64_t bytes) {
+  c->load_secs = seconds;
+  c->load_bytes = bytes;
+}
+
+extern "C" ms_status ms_load_stats(const ms_ctx* c, double* seconds, uint64_t* bytes) {
+  if (!c) return MS_ERR_INVALID_ARG;
+  if (seconds) *seconds = c->load_secs;
+  if (bytes) *bytes = c->load_bytes;
+  return MS_OK;
+}
 
 extern "C" ms_status ms_sync(ms_ctx* c, void* stream) {
   if (!c) return MS_ERR_INVALID_ARG;
@@ -1068,6 +1090,17 @@ extern "C" ms_status ms_model_destroy(ms_ctx* c, ms_model* m) {
 
 extern "C" size_t ms_model_weight_bytes(const ms_model* m) { return m ? m->weight_bytes : 0; }
 
+ms_status ms_model_set_bos_(ms_ctx* c, ms_model* m, const float* bos, int bos_id) {
+  if (!m->bos) MS_TRY(model_alloc(m, &m->bos, (size_t)m->hidden));
+  MS_CUDA(c, cudaMemcpy(m->bos, bos, m->hidden * sizeof(float), cudaMemcpyDefault));
+  m->bos_id = bos_id;
+  if (m->gexec) {  // a captured decode step holds the embedding's arguments
+    cudaGraphExecDestroy(m->gexec);
+    m->gexec = nullptr;
+  }
+  return MS_OK;
+}
+
 // ---------------------------------------------------------------- KV cache --
 
 extern "C" ms_status ms_kv_create(ms_ctx* c, const ms_model* m, int n_seq, int max_pos,
@@ -1663,7 +1696,7 @@ static ms_status embed_rows(ms_ctx* c, ms_model* m, float* x, int M, cudaStream_
                             const ms_kv* kv = nullptr) {
   const TokenLog log{kv ? kv->tok : nullptr, kv ? kv->max_pos : 0, m->d_seq, m->d_pos};
   MS_CUDA(c, launch_embed_stats(x, m->S[0], m->lm_head, m->d_ids, M, m->hidden, m->vocab_local, s,
-                                pdl, m->vocab0, log));
+                                pdl, m->vocab0, log, m->bos, m->bos_id));
   if (c->tp_world > 1) {
     MS_NCCL(c, nccl_api().all_reduce(x, x, (size_t)M * m->hidden, ncclFloat, ncclSum, c->comm, s));
     MS_CUDA(c, launch_rowstats(m->S[0], x, m->hidden, M, m->hidden, s, false));

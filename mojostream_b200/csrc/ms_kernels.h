@@ -196,9 +196,16 @@ struct TokenLog {
 // x[m] = column ids[m] - v0 of the [D][V] table (zeros when that column is
 // outside 0..V-1: another rank's vocabulary slice); stats per 16 columns;
 // each id also goes to the token table.
+// bos (may be null): token id bos_id embeds as bos[D] (rank 0's share under
+// tensor parallelism) instead of its column.
 cudaError_t launch_embed_stats(float* x, float* stats, const float* W,
                                const int* ids, int M, int D, int V, cudaStream_t s, bool pdl,
-                               int v0 = 0, TokenLog log = TokenLog{nullptr, 0, nullptr, nullptr});
+                               int v0 = 0, TokenLog log = TokenLog{nullptr, 0, nullptr, nullptr},
+                               const float* bos = nullptr, int bos_id = -1);
+// out[2 i + h] = ((q[i] >> 4 h) & 15) - 8) * scale: a Q4 [K][N/2] matrix as
+// fp32 [K][N] (the reference's dequant, src/linalg/kernels.mojo:100-108).
+cudaError_t launch_dequant_q4_f32(float* out, const uint8_t* q, size_t n_bytes, float scale,
+                                  cudaStream_t s);
 // Tensor-parallel epilogue of the row-parallel projections (O, down):
 // out = resid * ple * inv_rms(resid * ple) + partial (already all-reduced),
 // plus the per-16-column sums of squares of out.

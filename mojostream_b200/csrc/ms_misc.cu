@@ -219,19 +219,20 @@ cudaError_t launch_lm_head(const LmHeadParams& p, cudaStream_t s, bool pdl) {
 // =========================================================================
 __global__ void embed_kernel(float* x, float* stats, const float* __restrict__ W,
                              const int* __restrict__ ids, int M, int D, int V, int v0,
-                             TokenLog log) {
+                             TokenLog log, const float* __restrict__ bos, int bos_id) {
   pdl_trigger();
   pdl_wait();
   const int m = blockIdx.x;
   if (log.tok && threadIdx.x == 0) log.tok[(size_t)log.seq[m] * log.ld + log.pos[m]] = ids[m];
+  const bool is_bos = bos && ids[m] == bos_id;
   const int id = ids[m] - v0;
-  const bool mine = id >= 0 && id < V;
+  const bool mine = is_bos ? v0 == 0 : (id >= 0 && id < V);
   for (int t = threadIdx.x; t < D / kTileN; t += blockDim.x) {
     float sq = 0.f;
 #pragma unroll
     for (int j = 0; j < kTileN; ++j) {
       const int d = t * kTileN + j;
-      const float v = mine ? W[(size_t)d * V + id] : 0.f;
+      const float v = mine ? (is_bos ? bos[d] : W[(size_t)d * V + id]) : 0.f;
       x[(size_t)m * D + d] = v;
       sq += v * v;
     }
@@ -357,7 +358,7 @@ __global__ void advance_kernel(int* ids, const int* next, int* pos, int* hist, i
 // Launchers with the extra buffers the C-ABI layer owns.
 cudaError_t launch_embed_stats(float* x, float* stats, const float* W,
                                const int* ids, int M, int D, int V, cudaStream_t s, bool pdl,
-                               int v0, TokenLog log) {
+                               int v0, TokenLog log, const float* bos, int bos_id) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(M);
   cfg.blockDim = dim3(128);
@@ -367,7 +368,22 @@ cudaError_t launch_embed_stats(float* x, float* stats, const float* W,
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, embed_kernel, x, stats, W, ids, M, D, V, v0, log);
+  return cudaLaunchKernelEx(&cfg, embed_kernel, x, stats, W, ids, M, D, V, v0, log, bos, bos_id);
+}
+
+__global__ void dequant_q4_f32_kernel(float2* __restrict__ out, const uint8_t* __restrict__ q,
+                                      size_t n, float scale) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const int b = q[i];
+    out[i] = make_float2((float)((b & 15) - 8) * scale, (float)((b >> 4) - 8) * scale);
+  }
+}
+
+cudaError_t launch_dequant_q4_f32(float* out, const uint8_t* q, size_t n_bytes, float scale,
+                                  cudaStream_t s) {
+  dequant_q4_f32_kernel<<<148 * 8, 256, 0, s>>>(reinterpret_cast<float2*>(out), q, n_bytes, scale);
+  return cudaGetLastError();
 }
 
 // =========================================================================

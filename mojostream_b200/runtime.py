@@ -172,6 +172,28 @@ class Model:
         ctx.check(lib().ms_model_create(ctx.h, ctypes.byref(md), ctypes.byref(h)))
         self.h = h
 
+    @classmethod
+    def load(cls, ctx, path, lm_head_path=None, max_rows=64, full_every=0, window=0,
+             slide_theta=0.0, full_theta=0.0, full_rotary=0, staging_bytes=0):
+        """ms_model_load: a model from a .mojostream file (and an
+        lm_head_proto.bin).  The options cover what the file does not say;
+        zeros take the loader's defaults."""
+        from . import fileformat
+        o = _lib.LoadOpts(full_every, window, slide_theta, full_theta, full_rotary, max_rows,
+                          staging_bytes)
+        h = ctypes.c_void_p()
+        ctx.check(lib().ms_model_load(ctx.h, str(path).encode(),
+                                      str(lm_head_path).encode() if lm_head_path else None,
+                                      ctypes.byref(o), ctypes.byref(h)))
+        self = cls.__new__(cls)
+        self.ctx, self.max_rows, self.h = ctx, max_rows, h
+        self.spec = fileformat.spec_from_file(path, lm_head_path, full_every, window, slide_theta,
+                                              full_theta, full_rotary)
+        secs, nbytes = ctypes.c_double(), ctypes.c_uint64()
+        lib().ms_load_stats(ctx.h, ctypes.byref(secs), ctypes.byref(nbytes))
+        self.load_seconds, self.load_bytes = secs.value, nbytes.value
+        return self
+
     @property
     def weight_bytes(self):
         return lib().ms_model_weight_bytes(self.h)
