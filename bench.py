@@ -46,7 +46,7 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--layers", type=int, default=42, help="(debug) fewer layers")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--case", default="decode", choices=["decode", "q4", "tp"],
+    ap.add_argument("--case", default="decode", choices=["decode", "q4", "tp", "load"],
                     help="q4: the isolated Q4 projection (BASELINE configs[1] shapes), "
                          "a small case for profiling; tp: the 14B-class model (configs[4]) "
                          "tensor-parallel over the torchrun ranks")
@@ -460,6 +460,61 @@ def run_q4_case(args):
                       "peak_source": kind, "frac": round(nbytes / ms / 1e6 / hbm, 4)}), flush=True)
 
 
+def run_load(args):
+    """The model-file path (.mojostream + lm_head_proto.bin -> HBM): the E4B
+    files written to a temporary directory (so they sit in the page cache),
+    then ms_model_load timed; beside it the reference's way of reading a
+    .mojostream file, one whole-file read into host memory
+    (src/streaming/mojostream.mojo:112-116), timed on the same files."""
+    import shutil
+    import tempfile
+
+    import torch
+    from mojostream_b200 import fileformat as ff
+    from mojostream_b200.model import e4b_spec, synth_weights
+    from mojostream_b200.runtime import Context, Model
+    torch.cuda.set_device(0)
+    spec = e4b_spec(n_layers=args.layers)
+    tmp = tempfile.mkdtemp(prefix="ms_load_")
+    try:
+        path, lmp = os.path.join(tmp, "e4b.mojostream"), os.path.join(tmp, "lm_head_proto.bin")
+        w = synth_weights(spec, seed=1234)
+        ff.write_mojostream(path, spec, w)
+        ff.write_lm_head(lmp, w.lm_head, w.final_gamma)
+        del w
+        file_bytes = os.path.getsize(path) + os.path.getsize(lmp)
+        t0 = time.perf_counter()
+        for p in (path, lmp):
+            with open(p, "rb") as f:
+                blob = f.read()
+            del blob
+        ref_s = time.perf_counter() - t0
+        ctx = Context(0)
+        runs = []
+        for _ in range(max(1, args.steps)):
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            m = Model.load(ctx, path, lmp, max_rows=64)
+            torch.cuda.synchronize()
+            runs.append((time.perf_counter() - t0, m.load_seconds, m.load_bytes))
+            m.close()
+        wall, stream_s, nbytes = min(runs)
+        print(json.dumps({
+            "case": "load", "metric": "model file -> HBM GB/s (E4B .mojostream + fp32 lm_head)",
+            "value": round(nbytes / stream_s / 1e9, 2), "unit": "GB/s",
+            "bytes": nbytes, "stream_s": round(stream_s, 4),
+            "e2e": {"value": round(nbytes / wall / 1e9, 2), "unit": "GB/s",
+                    "wall_s": round(wall, 4), "note": "Model.load incl. repack"},
+            "runs": len(runs), "files": "page cache (written just before)",
+            "cpu_baseline": {"value": round(file_bytes / ref_s / 1e9, 2), "unit": "GB/s",
+                             "kind": "reference-style whole-file read into host RAM",
+                             "cores": 1, "seconds": round(ref_s, 4)},
+        }), flush=True)
+        ctx.close()
+    finally:
+        shutil.rmtree(tmp, ignore_errors=True)
+
+
 def run_tp(args, ws, rank, local):
     """14B-class random Q4 model, heads / FFN columns /
     vocabulary sharded over the ranks (one all-reduce after O and after down
@@ -589,6 +644,8 @@ def main():
                         f"{PROMPT}-token prompts")
     if args.case == "q4":
         run_q4_case(args)
+    elif args.case == "load":
+        run_load(args)
     elif args.case == "tp" and args.impl != "reference":
         args.batch = args.batch or 64
         args.prompt = args.prompt or 1024

@@ -192,17 +192,17 @@ typedef struct {
                              head_dim; format 1: head_dim]; sliding layers
                              rotate the whole head                          */
   int max_rows;           /* as ms_model_desc.max_rows [64]                 */
-  size_t staging_bytes;   /* pinned host staging per buffer [64 MiB]        */
+  size_t staging_bytes;   /* pinned host staging per reader thread [32 MiB] */
 } ms_load_opts;
 
 /* A model from a .mojostream file (and optionally an lm_head_proto.bin,
  * load_lm_head, src/inference/lm_head.mojo:61-116: v2 = fp32 weights, final
  * gamma and BOS embedding; v1 = Q4 weights, expanded to fp32 on the device,
  * gamma 1).  The file is checked as ms_file_check does, then its tensor data
- * streams to the device through two pinned host buffers in turn (a pread into
- * one overlaps the cudaMemcpyAsync of the other, the reference's double buffer
- * of sparse_pin.mojo:136-330 aimed at HBM) and is repacked as ms_model_create
- * does.  With an lm_head file, token id 2 (BOS) embeds as the file's BOS
+ * streams to the device through pinned host buffers, one per reader thread
+ * (up to 8 preads in parallel, each overlapping the others' cudaMemcpyAsync:
+ * the reference's double buffer of sparse_pin.mojo:136-330, widened and aimed
+ * at HBM) and is repacked as ms_model_create does.  With an lm_head file, token id 2 (BOS) embeds as the file's BOS
  * vector (apply_bos_embedding, lm_head.mojo:133-143).  Tensor parallel: each
  * rank loads the file and keeps its slices.  opts may be NULL. */
 MS_API ms_status ms_model_load(ms_ctx *ctx, const char *path, const char *lm_head_path,

@@ -11,21 +11,25 @@
 //   data     per tensor rows x cols/2 bytes of Q4, on 4096-byte boundaries
 // The checks are the reference's ShapeGuard / TensorGuard
 // (src/streaming/stream_runner.mojo:288-400), with layer-typed dims accepted
-// for format 2.  Loading streams the data region through two pinned host
-// buffers (pread into one while the other's cudaMemcpyAsync runs, the double
-// buffer of src/streaming/sparse_pin.mojo:136-330, aimed at HBM once since
-// the models fit) and hands device pointers to ms_model_create.
+// for format 2.  Loading streams the data region through pinned host buffers,
+// one per reader thread (preads in parallel, each overlapping the others'
+// cudaMemcpyAsync: the double buffer of src/streaming/sparse_pin.mojo:136-330
+// widened, and aimed at HBM once since the models fit), and hands device
+// pointers to ms_model_create.
 #include <fcntl.h>
 #include <sys/stat.h>
 #include <unistd.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cerrno>
 #include <chrono>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "ms_internal.h"
@@ -229,22 +233,26 @@ bool read_and_check(const char* path, FileView& f) {
   return true;
 }
 
-// Two pinned buffers in turn: the pread into one overlaps the host-to-device
-// copy out of the other.
+// Reader threads, each with its own pinned buffer: a thread preads its next
+// chunk while the copies of the others' (and its own previous one, until its
+// event completes) run on the stream, so disk / page-cache reads proceed in
+// parallel and overlap the host-to-device DMA.
 struct Staging {
-  uint8_t* pin[2] = {nullptr, nullptr};
-  cudaEvent_t ev[2] = {nullptr, nullptr};
+  std::vector<uint8_t*> pin;
+  std::vector<cudaEvent_t> ev;
   size_t bytes = 0;
-  bool init(size_t n) {
-    bytes = n;
-    for (int i = 0; i < 2; ++i) {
-      if (cudaHostAlloc((void**)&pin[i], n, cudaHostAllocDefault) != cudaSuccess) return false;
+  bool init(int n, size_t b) {
+    bytes = b;
+    pin.assign(n, nullptr);
+    ev.assign(n, nullptr);
+    for (int i = 0; i < n; ++i) {
+      if (cudaHostAlloc((void**)&pin[i], b, cudaHostAllocDefault) != cudaSuccess) return false;
       if (cudaEventCreateWithFlags(&ev[i], cudaEventDisableTiming) != cudaSuccess) return false;
     }
     return true;
   }
   ~Staging() {
-    for (int i = 0; i < 2; ++i) {
+    for (size_t i = 0; i < pin.size(); ++i) {
       if (ev[i]) cudaEventSynchronize(ev[i]), cudaEventDestroy(ev[i]);
       if (pin[i]) cudaFreeHost(pin[i]);
     }
@@ -252,30 +260,40 @@ struct Staging {
 };
 
 bool stream_to_device(int fd, uint64_t off, uint64_t n, uint8_t* dev, Staging& S, cudaStream_t s,
-                      std::string& err) {
-  uint64_t done = 0;
-  for (int k = 0; done < n; ++k) {
-    const int slot = k & 1;
-    cudaEventSynchronize(S.ev[slot]);  // the copy out of this buffer has finished
-    const size_t len = (size_t)std::min<uint64_t>(S.bytes, n - done);
-    if (!pread_all(fd, S.pin[slot], len, off + done)) {
-      cudaStreamSynchronize(s);
-      err = "read failed at offset " + std::to_string(off + done);
-      return false;
+                      int device, std::string& err) {
+  const int T = (int)S.pin.size();
+  const uint64_t chunks = (n + S.bytes - 1) / S.bytes;
+  std::atomic<bool> bad{false};
+  std::mutex mu;
+  auto worker = [&](int t) {
+    cudaSetDevice(device);
+    for (uint64_t k = t; k < chunks && !bad.load(); k += T) {
+      cudaEventSynchronize(S.ev[t]);  // this thread's previous copy has finished
+      const uint64_t at = k * S.bytes;
+      const size_t len = (size_t)std::min<uint64_t>(S.bytes, n - at);
+      std::string e;
+      if (!pread_all(fd, S.pin[t], len, off + at))
+        e = "read failed at offset " + std::to_string(off + at);
+      else if (cudaMemcpyAsync(dev + at, S.pin[t], len, cudaMemcpyHostToDevice, s) != cudaSuccess ||
+               cudaEventRecord(S.ev[t], s) != cudaSuccess)
+        e = std::string("host-to-device copy: ") + cudaGetErrorString(cudaGetLastError());
+      if (!e.empty()) {
+        std::lock_guard<std::mutex> g(mu);
+        if (!bad.exchange(true)) err = e;
+        return;
+      }
     }
-    if (cudaMemcpyAsync(dev + done, S.pin[slot], len, cudaMemcpyHostToDevice, s) != cudaSuccess ||
-        cudaEventRecord(S.ev[slot], s) != cudaSuccess) {
-      cudaStreamSynchronize(s);
-      err = std::string("host-to-device copy: ") + cudaGetErrorString(cudaGetLastError());
-      return false;
-    }
-    done += len;
-  }
-  if (cudaStreamSynchronize(s) != cudaSuccess) {
-    err = std::string("host-to-device copy: ") + cudaGetErrorString(cudaGetLastError());
+  };
+  std::vector<std::thread> pool;
+  for (int t = 1; t < T && (uint64_t)t < chunks; ++t) pool.emplace_back(worker, t);
+  worker(0);
+  for (auto& th : pool) th.join();
+  const cudaError_t e = cudaStreamSynchronize(s);
+  if (!bad.load() && e != cudaSuccess) {
+    err = std::string("host-to-device copy: ") + cudaGetErrorString(e);
     return false;
   }
-  return true;
+  return !bad.load();
 }
 
 struct DevBuf {
@@ -312,7 +330,8 @@ extern "C" ms_status ms_model_load(ms_ctx* c, const char* path, const char* lm_h
   const float slide_theta = o.slide_theta > 0.f ? o.slide_theta : 1e4f;
   const float full_theta = o.full_theta > 0.f ? o.full_theta : (typed ? 1e6f : slide_theta);
   const int max_rows = o.max_rows > 0 ? o.max_rows : 64;
-  const size_t staging = o.staging_bytes ? o.staging_bytes : ((size_t)64 << 20);
+  const size_t staging = o.staging_bytes ? o.staging_bytes : ((size_t)32 << 20);
+  const int readers = (int)std::max(1u, std::min(8u, std::thread::hardware_concurrency() / 2));
   char msg[512];
 
   // layer table (what the file does not say comes from the options)
@@ -349,7 +368,7 @@ extern "C" ms_status ms_model_load(ms_ctx* c, const char* path, const char* lm_h
   cudaSetDevice(ms_device_(c));
   cudaStream_t s = ms_stream_(c);
   Staging S;
-  if (!S.init(staging)) return ms_fail_(c, MS_ERR_OOM, "pinned staging buffers");
+  if (!S.init(readers, staging)) return ms_fail_(c, MS_ERR_OOM, "pinned staging buffers");
   const auto t0 = std::chrono::steady_clock::now();
   uint64_t moved = 0;
   std::string err;
@@ -361,7 +380,7 @@ extern "C" ms_status ms_model_load(ms_ctx* c, const char* path, const char* lm_h
     cudaGetLastError();
     return ms_fail_(c, MS_ERR_OOM, "device buffer for the layer data");
   }
-  if (!stream_to_device(f.fd, I.data_start, span, (uint8_t*)raw.p, S, s, err))
+  if (!stream_to_device(f.fd, I.data_start, span, (uint8_t*)raw.p, S, s, ms_device_(c), err))
     return ms_fail_(c, MS_ERR_CUDA, err.c_str());
   moved += span;
   for (int l = 0; l < I.n_layers; ++l)
@@ -412,7 +431,7 @@ extern "C" ms_status ms_model_load(ms_ctx* c, const char* path, const char* lm_h
       return ms_fail_(c, MS_ERR_OOM, "device buffer for the lm_head");
     }
     if (v2) {
-      if (!stream_to_device(g.fd, 12 + 8 * D, D * V * 4, (uint8_t*)lm.p, S, s, err))
+      if (!stream_to_device(g.fd, 12 + 8 * D, D * V * 4, (uint8_t*)lm.p, S, s, ms_device_(c), err))
         return ms_fail_(c, MS_ERR_CUDA, err.c_str());
       moved += D * V * 4;
     } else {  // Q4 [D][V/2]: expanded to the fp32 values (nibble - 8) * scale
@@ -420,7 +439,7 @@ extern "C" ms_status ms_model_load(ms_ctx* c, const char* path, const char* lm_h
         cudaGetLastError();
         return ms_fail_(c, MS_ERR_OOM, "device buffer for the Q4 lm_head");
       }
-      if (!stream_to_device(g.fd, 8 + 4 * D, D * V / 2, (uint8_t*)lmq.p, S, s, err))
+      if (!stream_to_device(g.fd, 8 + 4 * D, D * V / 2, (uint8_t*)lmq.p, S, s, ms_device_(c), err))
         return ms_fail_(c, MS_ERR_CUDA, err.c_str());
       moved += D * V / 2;
       if (ms::launch_dequant_q4_f32((float*)lm.p, (const uint8_t*)lmq.p, D * V / 2, q_scale, s) !=
