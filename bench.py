@@ -59,6 +59,9 @@ def parse():
                          "reference's e4b loop uses 0.7)")
     ap.add_argument("--penalty", type=float, default=1.0,
                     help="repetition penalty (the reference's e4b loop uses 1.2)")
+    ap.add_argument("--kv", default="f32", choices=["f32", "bf16"],
+                    help="KV cache element type (f32: the parity mode; bf16: configs[3]'s "
+                         "reduced-precision cache)")
     ap.add_argument("--m", type=int, default=4)
     ap.add_argument("--k", type=int, default=2560)
     ap.add_argument("--n", type=int, default=20480)
@@ -169,7 +172,8 @@ def run_ours(args, ws, rank, local):
     max_pos = ((PROMPT + args.warmup + 2 * args.steps + 8 + 63) // 64) * 64
     # sliding ring: the window plus the rows of one sequence in one prefill call
     window = max(l.window for l in spec.layers)
-    kv = KVCache(ctx, model, BATCH, max_pos, slide_cap=window + min(PROMPT, MAX_ROWS))
+    kv = KVCache(ctx, model, BATCH, max_pos, slide_cap=window + min(PROMPT, MAX_ROWS),
+                 dtype=args.kv)
     lib_stream = torch.cuda.ExternalStream(ctx.stream_ptr)
 
     def barrier():
@@ -246,6 +250,8 @@ def run_ours(args, ws, rank, local):
 
     q4 = spec.q4_bytes()
     kv_read = BATCH * spec.kv_bytes_per_seq(PROMPT + args.warmup + args.steps // 2)
+    if args.kv == "bf16":
+        kv_read //= 2
     step_bytes = q4 + spec.lm_head_bytes() + kv_read
     step_ms = dev_ms / args.steps
     tokens = BATCH * args.steps * ws
@@ -275,6 +281,7 @@ def run_ours(args, ws, rank, local):
                                                             PROMPT + args.warmup + args.steps],
             "parallelism": f"replicas x{ws}" if ws > 1 else "single GPU",
             "l2": "weights + lm_head 4.66 GB >> 126 MB L2 (no flush needed)",
+            "kv_dtype": args.kv,
             "sampling": ({"temperature": args.temperature, "penalty": args.penalty}
                          if args.temperature > 0.01 or args.penalty > 1.0 else "greedy"),
         },
@@ -545,7 +552,7 @@ def run_tp(args, ws, rank, local):
     torch.cuda.empty_cache()
     window = max(l.window for l in spec.layers)
     max_pos = ((P + args.warmup + 2 * args.steps + 8 + 63) // 64) * 64
-    kv = KVCache(ctx, model, B, max_pos, slide_cap=window + P)
+    kv = KVCache(ctx, model, B, max_pos, slide_cap=window + P, dtype=args.kv)
     lib_stream = torch.cuda.ExternalStream(ctx.stream_ptr)
 
     def barrier():
@@ -600,6 +607,8 @@ def run_tp(args, ws, rank, local):
     tokens = B * args.steps
     step_ms = dev_ms / args.steps
     kv_read = B * spec.kv_bytes_per_seq(P + args.warmup + args.steps // 2)
+    if args.kv == "bf16":
+        kv_read //= 2
     step_bytes = (spec.q4_bytes() + spec.lm_head_bytes() + kv_read) / ws  # per GPU
     result = {
         "metric": "decode tokens/s (batch %d), 14B-class Q4 model, tensor parallel" % B,
@@ -610,7 +619,7 @@ def run_tp(args, ws, rank, local):
         "data": "synthetic (seeded random Q4 weights and token ids)",
         "config": {"workload": "14b-class tensor-parallel decode (BASELINE configs[4])",
                    "layers": spec.n_layers, "hidden": spec.hidden, "vocab": spec.vocab,
-                   "batch": B, "prompt": P, "parallelism": f"tp{ws}",
+                   "batch": B, "prompt": P, "parallelism": f"tp{ws}", "kv_dtype": args.kv,
                    "l2": "weights + KV >> 126 MB L2 (no flush needed)"},
         "ttft_ms": round(ttft_ms, 3),
         "e2e": {"value": round(tokens / (e2e_ms / 1e3), 2), "unit": "tokens/s",

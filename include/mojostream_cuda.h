@@ -220,6 +220,14 @@ MS_API ms_status ms_load_stats(const ms_ctx *ctx, double *seconds, uint64_t *byt
  * slide_cap >= window + L - 1). */
 MS_API ms_status ms_kv_create(ms_ctx *ctx, const ms_model *model, int n_seq, int max_pos,
                        int slide_cap, ms_kv **out);
+/* Element type of the cached K / V values. */
+enum { MS_KV_F32 = 0, MS_KV_BF16 = 1 };
+/* ms_kv_create with an element type: MS_KV_F32 (the parity mode: the
+ * reference's fp32 cache) or MS_KV_BF16 (half the cache bytes; K / V rounded
+ * to nearest bfloat16 when written, widened to fp32 when read; attention,
+ * softmax and accumulation stay fp32; needs every kv_dim % 8 == 0). */
+MS_API ms_status ms_kv_create_typed(ms_ctx *ctx, const ms_model *model, int n_seq, int max_pos,
+                                    int slide_cap, int dtype, ms_kv **out);
 MS_API ms_status ms_kv_destroy(ms_ctx *ctx, ms_kv *kv);
 MS_API ms_status ms_kv_reset(ms_ctx *ctx, ms_kv *kv);
 MS_API size_t ms_kv_bytes(const ms_kv *kv);

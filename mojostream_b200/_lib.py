@@ -86,6 +86,8 @@ SIGNATURES = {
                                      ctypes.POINTER(ctypes.c_uint64)]),
     "ms_kv_create": (ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                     ctypes.POINTER(_vp)]),
+    "ms_kv_create_typed": (ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                          ctypes.c_int, ctypes.POINTER(_vp)]),
     "ms_kv_destroy": (ctypes.c_int, [_vp, _vp]),
     "ms_kv_reset": (ctypes.c_int, [_vp, _vp]),
     "ms_kv_bytes": (ctypes.c_size_t, [_vp]),

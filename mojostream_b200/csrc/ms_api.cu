@@ -164,6 +164,7 @@ struct ms_kv {
   int* bt_full = nullptr;
   int* bt_slide = nullptr;
   int* tok = nullptr;  // [n_seq][max_pos] token fed at each position (-1: none)
+  int bf16 = 0;        // K / V pools hold bfloat16
   size_t bytes = 0;
 };
 
@@ -1105,14 +1106,27 @@ ms_status ms_model_set_bos_(ms_ctx* c, ms_model* m, const float* bos, int bos_id
 
 extern "C" ms_status ms_kv_create(ms_ctx* c, const ms_model* m, int n_seq, int max_pos,
                                   int slide_cap, ms_kv** out) {
+  return ms_kv_create_typed(c, m, n_seq, max_pos, slide_cap, MS_KV_F32, out);
+}
+
+extern "C" ms_status ms_kv_create_typed(ms_ctx* c, const ms_model* m, int n_seq, int max_pos,
+                                        int slide_cap, int dtype, ms_kv** out) {
   if (!c || !m || !out) return MS_ERR_INVALID_ARG;
   *out = nullptr;
   if (m->ctx != c) return fail(c, MS_ERR_STATE, "model belongs to another context");
   if (n_seq <= 0 || max_pos <= 0 || slide_cap < 0)
     return fail(c, MS_ERR_SHAPE, "kv: n_seq %d max_pos %d slide_cap %d", n_seq, max_pos, slide_cap);
+  if (dtype != MS_KV_F32 && dtype != MS_KV_BF16)
+    return fail(c, MS_ERR_INVALID_ARG, "kv: dtype %d", dtype);
+  if (dtype == MS_KV_BF16)
+    for (const LayerDev& L : m->layers)
+      if (L.kv_dim % 8)
+        return fail(c, MS_ERR_SHAPE, "kv: a bf16 cache needs kv_dim %% 8 == 0 (%d)", L.kv_dim);
   cudaSetDevice(c->device);
   ms_kv* kv = new ms_kv();
   kv->model = m;
+  kv->bf16 = dtype == MS_KV_BF16;
+  const size_t eb = kv->bf16 ? 2 : 4;  // bytes per cached value
   kv->n_seq = n_seq;
   kv->max_pos = max_pos;
   int win = 0;
@@ -1150,13 +1164,13 @@ extern "C" ms_status ms_kv_create(ms_ctx* c, const ms_model* m, int n_seq, int m
     const int P = L.d.window > 0 ? kv->pages_slide : kv->pages_full;
     const size_t n = (size_t)n_seq * P * kv->page * L.kv_dim;
     float *k = nullptr, *v = nullptr;
-    if (dev_alloc(c, (void**)&k, n * sizeof(float)) != MS_OK) return cleanup(MS_ERR_OOM);
+    if (dev_alloc(c, (void**)&k, n * eb) != MS_OK) return cleanup(MS_ERR_OOM);
     kv->k.push_back(k);
-    if (dev_alloc(c, (void**)&v, n * sizeof(float)) != MS_OK) return cleanup(MS_ERR_OOM);
+    if (dev_alloc(c, (void**)&v, n * eb) != MS_OK) return cleanup(MS_ERR_OOM);
     kv->v.push_back(v);
-    cudaMemset(k, 0, n * sizeof(float));
-    cudaMemset(v, 0, n * sizeof(float));
-    kv->bytes += 2 * n * sizeof(float);
+    cudaMemset(k, 0, n * eb);
+    cudaMemset(v, 0, n * eb);
+    kv->bytes += 2 * n * eb;
   }
   // the repetition-penalty history of every sequence
   if (dev_alloc(c, (void**)&kv->tok, (size_t)n_seq * max_pos * sizeof(int)) != MS_OK)
@@ -1187,7 +1201,7 @@ extern "C" ms_status ms_kv_reset(ms_ctx* c, ms_kv* kv) {
   for (size_t i = 0; i < kv->k.size(); ++i) {
     const LayerDev& L = kv->model->layers[i];
     const int P = L.d.window > 0 ? kv->pages_slide : kv->pages_full;
-    const size_t n = (size_t)kv->n_seq * P * kv->page * L.kv_dim * sizeof(float);
+    const size_t n = (size_t)kv->n_seq * P * kv->page * L.kv_dim * (kv->bf16 ? 2 : 4);
     MS_CUDA(c, cudaMemsetAsync(kv->k[i], 0, n, c->stream));
     MS_CUDA(c, cudaMemsetAsync(kv->v[i], 0, n, c->stream));
   }
@@ -1267,6 +1281,7 @@ static KvView kv_view(const ms_kv* kv, int layer) {
   v.circular = slide ? 1 : 0;
   v.kv_dim = L.kv_dim;
   v.off32 = (size_t)kv->n_seq * v.bt_stride * v.page * v.kv_dim < ((size_t)1 << 32);
+  v.bf16 = kv->bf16;
   return v;
 }
 
@@ -1489,8 +1504,9 @@ static ms_status run_layer(ms_ctx* c, ms_model* m, const ms_kv* kv, int li, int 
 
 // The persistent decode kernel serves M <= 8 rows when every layer's
 // attention shape is one it carries.
-static bool mk_usable(const ms_ctx* c, const ms_model* m, int M) {
-  if (!c->mk_ok || c->tp_world > 1 || M < 1 || M > 8) return false;
+static bool mk_usable(const ms_ctx* c, const ms_model* m, const ms_kv* kv, int M) {
+  // (its attention unit reads fp32 caches only)
+  if (!c->mk_ok || c->tp_world > 1 || M < 1 || M > 8 || kv->bf16) return false;
   for (const LayerDev& L : m->layers)
     if (mk_attn_variant(L.d.head_dim, L.d.n_heads / L.d.n_kv_heads) < 0) return false;
   return true;
@@ -1550,7 +1566,7 @@ extern "C" ms_status ms_layer_forward(ms_ctx* c, const ms_model* mc, int layer, 
   cudaStream_t s = pick(c, stream);
   MS_TRY(upload_rows(c, m, seq, pos, M, s));
   MS_CUDA(c, launch_rowstats(m->S[0], x, m->hidden, M, m->hidden, s, false));
-  if (mk_usable(c, m, M)) {
+  if (mk_usable(c, m, kv, M)) {
     MS_TRY(mk_build(c, m, kv, layer, layer + 1, M, x, m->S[0], m->X[1], m->S[1], m->mk_eager, s));
     return mk_launch(c, m->mk_eager, s);
   }
@@ -1566,7 +1582,7 @@ extern "C" ms_status ms_forward(ms_ctx* c, const ms_model* mc, float* x, ms_kv* 
   cudaStream_t s = pick(c, stream);
   MS_TRY(upload_rows(c, m, seq, pos, M, s));
   MS_CUDA(c, launch_rowstats(m->S[0], x, m->hidden, M, m->hidden, s, false));
-  if (mk_usable(c, m, M)) {
+  if (mk_usable(c, m, kv, M)) {
     MS_TRY(mk_build(c, m, kv, 0, m->n_layers, M, x, m->S[0], m->X[1], m->S[1], m->mk_eager, s));
     return mk_launch(c, m->mk_eager, s);
   }
@@ -1738,7 +1754,7 @@ extern "C" ms_status ms_lm_head(ms_ctx* c, const ms_model* mc, const float* x, i
 // One decode step on the device: d_ids / d_seq / d_pos -> d_next.
 static ms_status decode_body(ms_ctx* c, ms_model* m, const ms_kv* kv, int M, cudaStream_t s) {
   MS_TRY(embed_rows(c, m, m->X[0], M, s, true, kv));
-  if (mk_usable(c, m, M)) {
+  if (mk_usable(c, m, kv, M)) {
     MS_TRY(mk_launch(c, m->mk_graph, s));  // op list built before the capture
   } else {
     for (int l = 0; l < m->n_layers; ++l)
@@ -1765,7 +1781,7 @@ static ms_status ensure_graph(ms_ctx* c, ms_model* m, const ms_kv* kv, int M) {
   if (m->sampling()) MS_TRY(ensure_sampler(c, m, M));
   cudaStream_t s = c->stream;
   cudaGraph_t g = nullptr;
-  if (mk_usable(c, m, M))
+  if (mk_usable(c, m, kv, M))
     MS_TRY(mk_build(c, m, kv, 0, m->n_layers, M, m->X[0], m->S[0], m->X[1], m->S[1],
                     m->mk_graph, s));
   MS_CUDA(c, cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));

@@ -12,8 +12,10 @@
 //
 // Per-warp streams (no CTA barrier in the main loop): the CTA's positions go
 // to its NW warps round-robin; every warp brings its next positions' K and V
-// rows into a private ring of P slots with cp.async.bulk (its own mbarriers),
-// so up to NW * P rows are in flight per CTA.  A warp holds its lanes' slices
+// rows into a private ring of P slots, all 32 lanes issuing 16-byte cp.async
+// copies (one commit group per position), so up to NW * P rows are in flight
+// per CTA.  (One bulk copy per row, issued by one lane, was bounded by the
+// per-SM rate of copy requests: the same time for half the bytes.)  A warp holds its lanes' slices
 // of the G query vectors and of the G running outputs in registers; per
 // position it forms the G scores (lane partial dot products, one warp
 // all-reduce each), updates its running maximum / sum / output (online
@@ -26,28 +28,42 @@
 
 namespace ms {
 
-template <int HD, int G>
+// BF: the cache holds bfloat16 K / V (rows half the bytes, widened to fp32
+// as they are read out of the ring).
+template <int HD, int G, bool BF>
 struct WarpAttn {
   static constexpr int NW = (G * HD >= 2048) ? 4 : 8;  // warps (registers: q + out slices)
   static constexpr int NT = NW * kWarp;
-  static constexpr int VEC = HD >= 128 ? 4 : 2;        // floats per lane load
+  static constexpr int VEC = HD >= 128 ? 4 : 2;        // values per lane load
   static constexpr int NV = HD / (kWarp * VEC);        // loads per lane per row
   static constexpr int PL = NV * VEC;                  // dims per lane
-  static constexpr int SLOT = 2 * HD;                  // floats: K row then V row
+  static constexpr int EB = BF ? 2 : 4;                // bytes per cached value
+  static constexpr int SLOTB = 2 * HD * EB;            // bytes: K row then V row
   // slots per warp: about 64 KB of rows in flight per CTA, and at least enough
   // for the end-of-unit combine (NW x G x (HD + 2) floats) to reuse the rings
-  static constexpr int P0 = 65536 / (NW * SLOT * 4);
-  static constexpr int PMIN = (G * (HD + 2) + SLOT - 1) / SLOT;
+  static constexpr int P0 = 65536 / (NW * SLOTB);
+  static constexpr int PMIN = (G * (HD + 2) * 4 + SLOTB - 1) / SLOTB;
   static constexpr int P1 = P0 > 8 ? 8 : (P0 < 2 ? 2 : P0);
   static constexpr int P = P1 < PMIN ? PMIN : P1;
-  static constexpr size_t smem = (size_t)NW * P * SLOT * sizeof(float);
+  static constexpr size_t smem = (size_t)NW * P * SLOTB;
   static constexpr int ST = HD + 4;                    // partial row stride (16 B)
-  static_assert(NW * G * (HD + 2) <= NW * P * SLOT, "combine buffer");
+  static_assert(NW * G * (HD + 2) * 4 <= NW * P * SLOTB, "combine buffer");
+  static_assert(P <= 32, "row offsets are fetched 32 positions at a time");
 };
 
-template <int VEC>
-__device__ __forceinline__ void ld_vec(float* dst, const float* src) {
-  if constexpr (VEC == 4) {
+// VEC cached values at src (shared memory) as floats.
+template <int VEC, bool BF>
+__device__ __forceinline__ void ld_vec(float* dst, const unsigned char* src) {
+  if constexpr (BF) {
+    if constexpr (VEC == 4) {
+      const uint2 u = *reinterpret_cast<const uint2*>(src);
+      dst[0] = __uint_as_float(u.x << 16); dst[1] = __uint_as_float(u.x & 0xffff0000u);
+      dst[2] = __uint_as_float(u.y << 16); dst[3] = __uint_as_float(u.y & 0xffff0000u);
+    } else {
+      const uint32_t u = *reinterpret_cast<const uint32_t*>(src);
+      dst[0] = __uint_as_float(u << 16); dst[1] = __uint_as_float(u & 0xffff0000u);
+    }
+  } else if constexpr (VEC == 4) {
     const float4 v = *reinterpret_cast<const float4*>(src);
     dst[0] = v.x; dst[1] = v.y; dst[2] = v.z; dst[3] = v.w;
   } else {
@@ -56,24 +72,17 @@ __device__ __forceinline__ void ld_vec(float* dst, const float* src) {
   }
 }
 
-template <int HD, int G>
-__global__ void __launch_bounds__(WarpAttn<HD, G>::NT) attn_kernel(const AttnParams p) {
-  using S = WarpAttn<HD, G>;
+template <int HD, int G, bool BF>
+__global__ void __launch_bounds__(WarpAttn<HD, G, BF>::NT) attn_kernel(const AttnParams p) {
+  using S = WarpAttn<HD, G, BF>;
   constexpr int NW = S::NW, NT = S::NT, P = S::P, PL = S::PL, VEC = S::VEC, ST = S::ST;
-  extern __shared__ __align__(128) float sm[];  // [NW][P][K row | V row]
-  __shared__ __align__(8) uint64_t bar[NW][P];
+  constexpr int EB = S::EB;
+  extern __shared__ __align__(128) unsigned char smb[];  // [NW][P][K row | V row]
   __shared__ float s_w[G][kAttnMaxSplits];
-  __shared__ int s_last, s_bad;
+  __shared__ int s_last;
 
   const int split = blockIdx.x, hk = blockIdx.y, m = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  if (tid == 0) {
-    for (int w = 0; w < NW; ++w)
-      for (int s = 0; s < P; ++s) mbar_init(&bar[w][s], 1);
-    mbar_fence_init();
-    s_bad = 0;
-  }
-  __syncthreads();
   pdl_wait();
   pdl_trigger();
 
@@ -88,20 +97,39 @@ __global__ void __launch_bounds__(WarpAttn<HD, G>::NT) attn_kernel(const AttnPar
   const int n_pos = t_end - t_begin;
   const int cnt = n_pos > warp ? (n_pos - warp + NW - 1) / NW : 0;  // this warp's positions
   const size_t head_off = (size_t)hk * HD;
-  float* ring = sm + (size_t)warp * P * S::SLOT;
+  unsigned char* ring = smb + (size_t)warp * P * S::SLOTB;
+  const unsigned char* kpool = reinterpret_cast<const unsigned char*>(p.kv.k);
+  const unsigned char* vpool = reinterpret_cast<const unsigned char*>(p.kv.v);
 
-  // lane 0 streams position i of this warp (t_begin + warp + NW i) into slot i % P
-  auto issue = [&](int i) {
-    const int t = t_begin + warp + NW * i;
-    const int slot = i % P;
-    const size_t off = kv_row_offset(p.kv.block_table, p.kv.bt_stride, p.kv.page, p.kv.cap,
-                                     p.kv.circular, seq, t, p.kv.kv_dim) + head_off;
-    mbar_expect_tx(&bar[warp][slot], (uint32_t)(S::SLOT * sizeof(float)));
-    bulk_g2s(ring + slot * S::SLOT, p.kv.k + off, HD * sizeof(float), &bar[warp][slot]);
-    bulk_g2s(ring + slot * S::SLOT + HD, p.kv.v + off, HD * sizeof(float), &bar[warp][slot]);
+  // Row offsets of this warp's positions, 32 at a time: lane j holds that of
+  // position base + j (one batch of independent block-table loads instead of
+  // a dependent load before every copy).
+  auto row_offsets = [&](int base) -> unsigned long long {
+    const int i = base + lane;
+    if (i >= cnt) return 0ull;
+    return kv_row_offset(p.kv.block_table, p.kv.bt_stride, p.kv.page, p.kv.cap, p.kv.circular,
+                         seq, t_begin + warp + NW * i, p.kv.kv_dim) + head_off;
   };
-  if (lane == 0)
-    for (int i = 0; i < cnt && i < P; ++i) issue(i);
+  // the warp streams position i (t_begin + warp + NW i), whose row offset is
+  // `off`, into slot i % P, then closes the position's commit group (always,
+  // so that group j is position j's)
+  auto issue = [&](int i, unsigned long long off) {
+    if (i < cnt) {
+      unsigned char* dst = ring + (i % P) * S::SLOTB;
+      const unsigned char* ks = kpool + off * EB;
+      const unsigned char* vs = vpool + off * EB;
+      constexpr int CH = HD * EB / 16;  // 16-byte chunks per row
+#pragma unroll
+      for (int c = lane; c < CH; c += kWarp) {
+        cp_async16(dst + c * 16, ks + c * 16);
+        cp_async16(dst + HD * EB + c * 16, vs + c * 16);
+      }
+    }
+    cp_async_commit();
+  };
+  unsigned long long offs = row_offsets(0);  // positions 0..31 (P <= 32)
+#pragma unroll
+  for (int i = 0; i < P; ++i) issue(i, __shfl_sync(0xffffffffu, offs, i));
 
   // this lane's slices: dims (v * 32 + lane) * VEC + e
   float q[G][PL], acc[G][PL], mrun[G], lrun[G];
@@ -124,49 +152,54 @@ __global__ void __launch_bounds__(WarpAttn<HD, G>::NT) attn_kernel(const AttnPar
     lrun[h] = 0.f;
   }
 
-  int i = 0;
-  for (; i < cnt; ++i) {
+  for (int i = 0; i < cnt; ++i) {
     const int slot = i % P;
-    if (!mbar_wait(&bar[warp][slot], (i / P) & 1)) {
-      if (lane == 0) {
-        atomicOr(p.err, kErrWaitTimeout);
-        s_bad = 1;
-      }
-      break;
-    }
+    cp_async_wait<P - 1>();  // this lane's copies of position i have landed
+    __syncwarp();            // ... and every other lane's
     float kk[PL], vv[PL];
-    const float* kr = ring + slot * S::SLOT;
+    const unsigned char* kr = ring + slot * S::SLOTB;
 #pragma unroll
     for (int v = 0; v < S::NV; ++v) {
-      ld_vec<VEC>(&kk[v * VEC], kr + (v * kWarp + lane) * VEC);
-      ld_vec<VEC>(&vv[v * VEC], kr + HD + (v * kWarp + lane) * VEC);
+      ld_vec<VEC, BF>(&kk[v * VEC], kr + (v * kWarp + lane) * VEC * EB);
+      ld_vec<VEC, BF>(&vv[v * VEC], kr + (HD + (v * kWarp + lane) * VEC) * EB);
     }
     __syncwarp();  // every lane holds its slice: the slot can be refilled
-    if (lane == 0 && i + P < cnt) issue(i + P);
+    if (((i + P) & 31) == 0) offs = row_offsets(i + P);  // warp-uniform
+    issue(i + P, __shfl_sync(0xffffffffu, offs, (i + P) & 31));
+    float sc[G];
 #pragma unroll
     for (int h = 0; h < G; ++h) {
       float d = 0.f;
 #pragma unroll
       for (int e = 0; e < PL; ++e) d = fmaf(q[h][e], kk[e], d);
-      const float s = warp_sum(d) * p.scale;
-      const float m_new = fmaxf(mrun[h], s);
-      const float corr = expf(mrun[h] - m_new);  // 0 on the first position
-      const float ew = expf(s - m_new);
-      lrun[h] = lrun[h] * corr + ew;
+      sc[h] = d;
+    }
 #pragma unroll
-      for (int e = 0; e < PL; ++e) acc[h][e] = fmaf(ew, vv[e], acc[h][e] * corr);
-      mrun[h] = m_new;
+    for (int h = 0; h < G; ++h) sc[h] = warp_sum(sc[h]) * p.scale;  // G independent chains
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+      const float s = sc[h];
+      // the running maximum only moves up: rescale when it does (s is the
+      // same in every lane, so the branch is warp-uniform); otherwise the
+      // factor is exactly 1 and the products are unchanged
+      if (s > mrun[h]) {
+        const float corr = expf(mrun[h] - s);  // 0 on the first position
+        lrun[h] *= corr;
+#pragma unroll
+        for (int e = 0; e < PL; ++e) acc[h][e] *= corr;
+        mrun[h] = s;
+      }
+      const float ew = expf(s - mrun[h]);
+      lrun[h] += ew;
+#pragma unroll
+      for (int e = 0; e < PL; ++e) acc[h][e] = fmaf(ew, vv[e], acc[h][e]);
     }
   }
-  if (i < cnt && lane == 0) {
-    // a copy never arrived: let this warp's issued copies land (bounded)
-    for (int j = i; j < cnt && j < i + P; ++j) mbar_wait(&bar[warp][j % P], (j / P) & 1);
-  }
-  __syncthreads();  // every warp is past its ring: it becomes the combine buffer
-  if (s_bad) return;
+  cp_async_wait<0>();  // (only empty groups remain)
+  __syncthreads();     // every warp is past its ring: it becomes the combine buffer
 
   // ---- combine the warps: comb[w][h][0..HD) outputs, [HD] max, [HD+1] sum ----
-  float* comb = sm;
+  float* comb = reinterpret_cast<float*>(smb);
 #pragma unroll
   for (int h = 0; h < G; ++h) {
     float* c = comb + ((size_t)warp * G + h) * (HD + 2);
@@ -265,9 +298,9 @@ __global__ void __launch_bounds__(WarpAttn<HD, G>::NT) attn_kernel(const AttnPar
   if (tid == 0) *ctr = 0;
 }
 
-template <int HD, int G>
+template <int HD, int G, bool BF>
 static cudaError_t launch_t(const AttnParams& p, cudaStream_t s, bool pdl) {
-  using S = WarpAttn<HD, G>;
+  using S = WarpAttn<HD, G, BF>;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.n_splits, p.n_kv, p.M);
   cfg.blockDim = dim3(S::NT);
@@ -278,7 +311,7 @@ static cudaError_t launch_t(const AttnParams& p, cudaStream_t s, bool pdl) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, attn_kernel<HD, G>, p);
+  return cudaLaunchKernelEx(&cfg, attn_kernel<HD, G, BF>, p);
 }
 
 #define MS_ATTN_CASES(X)                                                        \
@@ -287,14 +320,16 @@ static cudaError_t launch_t(const AttnParams& p, cudaStream_t s, bool pdl) {
   X(512, 1) X(512, 2) X(512, 4)
 
 // q, out: 16-byte aligned rows (ldq, ldo multiples of 4); the KV pools 16-byte
-// aligned; n_splits <= 64.
+// aligned, rows on 16-byte boundaries (kv_dim a multiple of 4, of 8 for bf16);
+// n_splits <= 64.
 cudaError_t launch_attention(const AttnParams& p, cudaStream_t s, bool pdl) {
   if (p.n_splits < 1 || p.n_splits > kAttnMaxSplits || p.chunk < 1 || (p.ldq & 3) ||
-      (p.ldo & 3) || (p.kv.kv_dim & 3))
+      (p.ldo & 3) || (p.kv.kv_dim & 3) || (p.kv.bf16 && (p.kv.kv_dim & 7)))
     return cudaErrorInvalidConfiguration;
   const int G = p.n_heads / p.n_kv;
-#define MS_ATTN_CASE(HDV, GV) \
-  if (p.hd == HDV && G == GV) return launch_t<HDV, GV>(p, s, pdl);
+#define MS_ATTN_CASE(HDV, GV)                                                   \
+  if (p.hd == HDV && G == GV)                                                   \
+    return p.kv.bf16 ? launch_t<HDV, GV, true>(p, s, pdl) : launch_t<HDV, GV, false>(p, s, pdl);
   MS_ATTN_CASES(MS_ATTN_CASE)
 #undef MS_ATTN_CASE
   return cudaErrorInvalidConfiguration;
@@ -304,12 +339,15 @@ int attention_max_splits() { return kAttnMaxSplits; }
 
 cudaError_t prepare_attention() {
   cudaError_t e = cudaSuccess;
-#define MS_ATTN_PREP(HDV, GV)                                                                  \
-  if (e == cudaSuccess && WarpAttn<HDV, GV>::smem > 48 * 1024)                                \
-    e = cudaFuncSetAttribute(attn_kernel<HDV, GV>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
-                             (int)WarpAttn<HDV, GV>::smem);
+#define MS_ATTN_PREP1(HDV, GV, BFV)                                                        \
+  if (e == cudaSuccess && WarpAttn<HDV, GV, BFV>::smem > 48 * 1024)                       \
+    e = cudaFuncSetAttribute(attn_kernel<HDV, GV, BFV>,                                   \
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,                 \
+                             (int)WarpAttn<HDV, GV, BFV>::smem);
+#define MS_ATTN_PREP(HDV, GV) MS_ATTN_PREP1(HDV, GV, false) MS_ATTN_PREP1(HDV, GV, true)
   MS_ATTN_CASES(MS_ATTN_PREP)
 #undef MS_ATTN_PREP
+#undef MS_ATTN_PREP1
   return e;
 }
 

@@ -18,7 +18,8 @@
 //   2. mask (causal + window), online softmax per row (one warp per row,
 //      expf; running max / sum / rescale factor);
 //   3. O[R][hd] += P V: thread tile of rows x float4 slices of hd.
-// fp32 throughout (CUDA cores): the per-layer parity bound is 1e-4.
+// fp32 throughout (CUDA cores): the per-layer parity bound is 1e-4.  A bf16
+// cache is widened to fp32 as the rows are staged.
 #include "ms_common.cuh"
 #include "ms_kernels.h"
 
@@ -102,8 +103,8 @@ __global__ void __launch_bounds__(kPfThreads, 1) attn_prefill_kernel(const AttnP
       if (t <= t_last) {
         const size_t off = kv_row_offset(p.kv.block_table, p.kv.bt_stride, p.kv.page, p.kv.cap,
                                          p.kv.circular, seq, t, p.kv.kv_dim) + head_off + 4 * d4;
-        kv4 = *reinterpret_cast<const float4*>(p.kv.k + off);
-        vv4 = *reinterpret_cast<const float4*>(p.kv.v + off);
+        kv4 = kv_get4(p.kv.k, p.kv.bf16, off);
+        vv4 = kv_get4(p.kv.v, p.kv.bf16, off);
       }
       *reinterpret_cast<float4*>(sK + j * QS + 4 * d4) = kv4;
       *reinterpret_cast<float4*>(sV + j * QS + 4 * d4) = vv4;
@@ -254,7 +255,8 @@ int attention_prefill_tokens(int hd, int group) {
 // q, out: 16-byte aligned rows (ldq, ldo multiples of 4); the KV pools
 // 16-byte aligned; every block has at most attention_prefill_tokens() rows.
 cudaError_t launch_attention_prefill(const AttnParams& p, cudaStream_t s, bool pdl) {
-  if (p.n_blocks < 1 || !p.blocks || (p.ldq & 3) || (p.ldo & 3) || (p.kv.kv_dim & 3))
+  if (p.n_blocks < 1 || !p.blocks || (p.ldq & 3) || (p.ldo & 3) || (p.kv.kv_dim & 3) ||
+      (p.kv.bf16 && (p.kv.kv_dim & 7)))
     return cudaErrorInvalidConfiguration;
   const int G = p.n_heads / p.n_kv;
 #define MS_PF_CASE(HDV, GV) \

@@ -140,6 +140,19 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       "l"(src), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
 }
+// Per-thread asynchronous 16-byte copies global -> shared (through L2 only),
+// completed in commit groups: wait<N> returns once at most N of this
+// thread's groups are still in flight.
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 __device__ __forceinline__ uint4 lds_u4(const uint4* p) {
   uint4 r;
   asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
@@ -208,6 +221,30 @@ __device__ __forceinline__ bool wait_counter_sys(const int* ctr, int target) {
 constexpr int kErrWaitTimeout = 1;
 
 // Slot of absolute position p in a sequence's KV ring (circular: p % cap).
+// Store one value into a K / V pool at element index idx: fp32, or bfloat16
+// rounded to nearest (ties to even) when the cache is bf16.
+__device__ __forceinline__ void kv_put(float* pool, int bf16, size_t idx, float v) {
+  if (bf16)
+    reinterpret_cast<__nv_bfloat16*>(pool)[idx] = __float2bfloat16_rn(v);
+  else
+    pool[idx] = v;
+}
+// Two adjacent values (idx even).
+__device__ __forceinline__ void kv_put2(float* pool, int bf16, size_t idx, float a, float b) {
+  if (bf16)
+    *reinterpret_cast<__nv_bfloat162*>(reinterpret_cast<__nv_bfloat16*>(pool) + idx) =
+        __floats2bfloat162_rn(a, b);
+  else
+    *reinterpret_cast<float2*>(pool + idx) = make_float2(a, b);
+}
+// Four values at element index idx (a multiple of 4) of a K / V pool.
+__device__ __forceinline__ float4 kv_get4(const float* pool, int bf16, size_t idx) {
+  if (!bf16) return *reinterpret_cast<const float4*>(pool + idx);
+  const uint2 u = *reinterpret_cast<const uint2*>(reinterpret_cast<const __nv_bfloat16*>(pool) + idx);
+  return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u),
+                     __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xffff0000u));
+}
+
 __device__ __forceinline__ size_t kv_row_offset(const int* __restrict__ block_table,
                                                 int bt_stride, int page, int cap,
                                                 int circular, int seq, int p, int kv_dim) {

@@ -73,9 +73,9 @@ __device__ __forceinline__ void epilogue_row(const GemvParams& p, int tile, int 
       } else {
         const size_t off = kv_row_offset(p.kv.block_table, p.kv.bt_stride, p.kv.page, p.kv.cap,
                                          p.kv.circular, p.seq[m], p.pos[m], p.kv.kv_dim);
-        float* base = (td.dst == 1 ? p.kv.k : p.kv.v) + off;
-        base[td.col_lo + g] = a;
-        base[td.col_hi + g] = b;
+        float* pool = td.dst == 1 ? p.kv.k : p.kv.v;
+        kv_put(pool, p.kv.bf16, off + td.col_lo + g, a);
+        kv_put(pool, p.kv.bf16, off + td.col_hi + g, b);
       }
       break;
     }
@@ -87,11 +87,12 @@ __device__ __forceinline__ void epilogue_row(const GemvParams& p, int tile, int 
 // Inputs of epilogue_row that do not depend on the projection's sums, loaded
 // before the main loop so their global-memory latency overlaps it:
 //   kEpiResid : the residual values of columns c, c + 8 (a, b)
-//   kEpiQKV   : the tile descriptor, the destination row (Q row or K / V
-//               cache row) and cos / sin of the RoPE angle (a, b)
+//   kEpiQKV   : the tile descriptor, the destination (Q row, or K / V pool
+//               and row offset) and cos / sin of the RoPE angle (a, b)
 struct EpiPrefetch {
   float a, b;
   float* dst;
+  size_t off;
   QkvTile td;
 };
 
@@ -112,11 +113,12 @@ __device__ __forceinline__ void epilogue_prefetch(const GemvParams& p, int tile,
       e.b = sinf(th);
     }
     if (e.td.dst == 0) {
-      e.dst = p.q_out + (size_t)m * p.ldq;
+      e.dst = p.q_out;
+      e.off = (size_t)m * p.ldq;
     } else {
-      const size_t off = kv_row_offset(p.kv.block_table, p.kv.bt_stride, p.kv.page, p.kv.cap,
-                                       p.kv.circular, p.seq[m], pos, p.kv.kv_dim);
-      e.dst = (e.td.dst == 1 ? p.kv.k : p.kv.v) + off;
+      e.off = kv_row_offset(p.kv.block_table, p.kv.bt_stride, p.kv.page, p.kv.cap, p.kv.circular,
+                            p.seq[m], pos, p.kv.kv_dim);
+      e.dst = e.td.dst == 1 ? p.kv.k : p.kv.v;
     }
   }
 }
@@ -145,8 +147,9 @@ __device__ __forceinline__ void epilogue_row_pre(const GemvParams& p, int tile, 
         a = ra;
         b = rb;
       }
-      e.dst[e.td.col_lo + g] = a;
-      e.dst[e.td.col_hi + g] = b;
+      const int bf = e.td.dst != 0 && p.kv.bf16;
+      kv_put(e.dst, bf, e.off + e.td.col_lo + g, a);
+      kv_put(e.dst, bf, e.off + e.td.col_hi + g, b);
       break;
     }
     default:

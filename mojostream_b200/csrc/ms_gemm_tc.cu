@@ -471,15 +471,19 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const GemvParams
             }
           }
           float* base;
+          size_t off;
+          int bf = 0;
           if (td.dst == 0) {
-            base = p.q_out + (size_t)m * p.ldq;
+            base = p.q_out;
+            off = (size_t)m * p.ldq;
           } else {
-            const size_t off = kv_row_offset(p.kv.block_table, p.kv.bt_stride, p.kv.page, p.kv.cap,
-                                             p.kv.circular, p.seq[m], pos, p.kv.kv_dim);
-            base = (td.dst == 1 ? p.kv.k : p.kv.v) + off;
+            off = kv_row_offset(p.kv.block_table, p.kv.bt_stride, p.kv.page, p.kv.cap,
+                                p.kv.circular, p.seq[m], pos, p.kv.kv_dim);
+            base = td.dst == 1 ? p.kv.k : p.kv.v;
+            bf = p.kv.bf16;
           }
-          *reinterpret_cast<float2*>(base + td.col_lo + g0) = make_float2(lo[0], lo[1]);
-          *reinterpret_cast<float2*>(base + td.col_hi + g0) = make_float2(hi[0], hi[1]);
+          kv_put2(base, bf, off + td.col_lo + g0, lo[0], lo[1]);
+          kv_put2(base, bf, off + td.col_hi + g0, hi[0], hi[1]);
         }
       }
     }

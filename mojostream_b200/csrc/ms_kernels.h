@@ -59,6 +59,7 @@ struct KvView {
   const int* block_table;    // [n_seq][bt_stride] physical page ids
   int bt_stride, page, cap, circular, kv_dim;
   int off32;                 // every row offset of the pool fits 32 bits
+  int bf16;                  // K / V stored as bfloat16 (k, v then point at bf16 pools)
 };
 
 struct GemvParams {

@@ -274,10 +274,13 @@ class Model:
 class KVCache:
     """ms_kv: paged cache for n_seq sequences."""
 
-    def __init__(self, ctx, model, n_seq, max_pos, slide_cap=0):
-        self.ctx, self.n_seq, self.max_pos = ctx, n_seq, max_pos
+    def __init__(self, ctx, model, n_seq, max_pos, slide_cap=0, dtype="f32"):
+        """dtype "f32" (the parity mode) or "bf16" (half the cache bytes)."""
+        self.ctx, self.n_seq, self.max_pos, self.dtype = ctx, n_seq, max_pos, dtype
         h = ctypes.c_void_p()
-        ctx.check(lib().ms_kv_create(ctx.h, model.h, n_seq, max_pos, slide_cap, ctypes.byref(h)))
+        code = {"f32": 0, "bf16": 1}[dtype]
+        ctx.check(lib().ms_kv_create_typed(ctx.h, model.h, n_seq, max_pos, slide_cap, code,
+                                           ctypes.byref(h)))
         self.h = h
 
     @property

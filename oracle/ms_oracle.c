@@ -30,6 +30,18 @@
 
 static int imin(int a, int b) { return a < b ? a : b; }
 
+/* Nearest bfloat16 (ties to even) of a finite float, as a float: keep the top
+ * 16 bits after adding half of the dropped range (IEEE 754 rounding). */
+static float round_bf16(float f)
+{
+    uint32_t u;
+    memcpy(&u, &f, 4);
+    if ((u & 0x7f800000u) != 0x7f800000u) u += 0x7fffu + ((u >> 16) & 1u);
+    u &= 0xffff0000u;
+    memcpy(&f, &u, 4);
+    return f;
+}
+
 /* kernels.mojo:100-108: low nibble -> even column, high nibble -> odd column,
  * value (nibble - 8) * scale. */
 float orc_dequant(const uint8_t *w, int N, int k, int n, float scale)
@@ -362,6 +374,11 @@ int orc_layer_forward(const orc_layer_t *L, int D, float *x, int M,
         const size_t off = ((size_t)seq[r] * kv->cap + slot) * kvd;
         memcpy(kv->k + off, k + (size_t)r * kvd, sizeof(float) * kvd);
         memcpy(kv->v + off, v + (size_t)r * kvd, sizeof(float) * kvd);
+        if (kv->bf16)
+            for (int j = 0; j < kvd; ++j) {
+                kv->k[off + j] = round_bf16(kv->k[off + j]);
+                kv->v[off + j] = round_bf16(kv->v[off + j]);
+            }
     }
     /* 5. attention (main.mojo:445-519; gemma4_e4b.mojo:259-411) */
     for (int r = 0; r < M; ++r) {

@@ -36,13 +36,17 @@ typedef struct {
     float scale[ORC_NMAT];      /* one fp32 scale per tensor                          */
 } orc_layer_t;
 
-/* KV cache of one layer: n_seq sequences x cap slots x kv_dim floats (K and V). */
+/* KV cache of one layer: n_seq sequences x cap slots x kv_dim floats (K and V).
+ * bf16 != 0 stores every K / V value rounded to bfloat16 (round to nearest,
+ * ties to even): the reduced-precision cache of the GPU path, for its own
+ * looser parity check. */
 typedef struct {
     int n_seq;
     int cap;           /* slots per sequence (window>0: circular, slot = pos % cap)  */
     int kv_dim;
     float *k;
     float *v;
+    int bf16;
 } orc_kv_layer_t;
 
 /* kernels.mojo:100-108 (dequant_vec): value of logical column n in row k. */

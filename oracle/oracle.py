@@ -34,7 +34,7 @@ class OrcLayer(ctypes.Structure):
 
 class OrcKVLayer(ctypes.Structure):
     _fields_ = [("n_seq", ctypes.c_int), ("cap", ctypes.c_int), ("kv_dim", ctypes.c_int),
-                ("k", _f32p), ("v", _f32p)]
+                ("k", _f32p), ("v", _f32p), ("bf16", ctypes.c_int)]
 
 
 def build():
@@ -154,10 +154,11 @@ class OracleModel:
     """Runs a ModelSpec on the CPU with the oracle.  KV caches are owned here.
 
     ``slide_cap`` is the slot count of circular (sliding-window) caches; the
-    reference uses exactly the window (gemma4_e4b.mojo:219-228).
+    reference uses exactly the window (gemma4_e4b.mojo:219-228).  ``kv_bf16``
+    keeps K / V rounded to bfloat16 (the GPU's reduced-precision cache).
     """
 
-    def __init__(self, spec, weights, n_seq, max_pos, slide_cap=None, workers=1):
+    def __init__(self, spec, weights, n_seq, max_pos, slide_cap=None, workers=1, kv_bf16=False):
         self.spec, self.w, self.workers = spec, weights, workers
         self._layers, self._kv, self._keep = [], [], []
         for li, ls in enumerate(spec.layers):
@@ -179,6 +180,7 @@ class OracleModel:
             kv = OrcKVLayer()
             kv.n_seq, kv.cap, kv.kv_dim = n_seq, cap, kvd
             kv.k, kv.v = _p(kb, _f32p), _p(vb, _f32p)
+            kv.bf16 = 1 if kv_bf16 else 0
             self._kv.append((kv, kb, vb))
 
     def kv_arrays(self, layer):

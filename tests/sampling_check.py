@@ -13,9 +13,11 @@ import numpy as np
 from test_sampler_oracle import exact_cdf, penalised
 
 
-def check_sampled_ids(oracle_lib, om, prompts, dev, T, pen, seed):
+def check_sampled_ids(oracle_lib, om, prompts, dev, T, pen, seed, tie_rel=1e-4):
     """dev [steps][n]: row 0 the prefill's first ids, then one row per
-    decode step.  Returns (exact, near) counts; asserts on anything else."""
+    decode step.  Returns (exact, near) counts; asserts on anything else.
+    tie_rel: how far (relative to the best) a greedy pick's logit may sit
+    below the oracle's best and still count as fp noise."""
     n = len(prompts)
     steps = dev.shape[0]
     hist = [list(map(int, p)) for p in prompts]
@@ -36,8 +38,8 @@ def check_sampled_ids(oracle_lib, om, prompts, dev, T, pen, seed):
                 continue
             pl = penalised(logits[r], hist[r], pen)
             if T <= 0.01:
-                top = np.sort(pl)[-2:]
-                assert top[1] - top[0] <= 1e-4 * abs(top[1]) and pl[j] >= top[0], (st, r, j, ref)
+                best = pl[ref]
+                assert best - pl[j] <= tie_rel * abs(best), (st, r, j, ref, best - pl[j])
             else:
                 cdf = exact_cdf(pl, T)
                 t = oracle_lib.sample_target(rs)
