@@ -1,5 +1,5 @@
 // ms_attn_prefill.cu -- causal GQA attention for prefill chunks (many query
-// rows of the same sequence per call).
+// rows of the same sequence per call), on the tensor cores.
 //
 // Reference semantics (as the decode kernel in ms_attn.cu):
 // gqa_attention_decode (src/main.mojo:445-519), compute_sliding_attention /
@@ -8,62 +8,123 @@
 // lo = max(0, P + 1 - window) on sliding layers and 0 otherwise;
 // score = (q . k) / sqrt(hd); softmax with the maximum subtracted; out = sum p v.
 //
-// Decode reads every K/V row once per query row.  A prefill chunk has many
-// query rows per sequence, so here one CTA serves a query block (up to R / G
-// consecutive positions of one sequence, G = n_heads / n_kv query heads each:
-// R query vectors) for one KV head, and every K/V chunk it stages in shared
-// memory is used by all R query vectors:
-//   1. scores S[R][32] = Q K^T: thread tile of R/32 rows x 4 keys, float4
-//      steps over the head dimension (padded rows: conflict-free);
-//   2. mask (causal + window), online softmax per row (one warp per row,
-//      expf; running max / sum / rescale factor);
-//   3. O[R][hd] += P V: thread tile of rows x float4 slices of hd.
-// fp32 throughout (CUDA cores): the per-layer parity bound is 1e-4.  A bf16
-// cache is widened to fp32 as the rows are staged.
+// One CTA serves a query block (up to R / G consecutive positions of one
+// sequence, G = n_heads / n_kv query heads each: R query vectors, row
+// r = token * G + head) for one KV head, flash-attention style:
+//   * every warp owns 16 query rows (one mma m-tile); with hd 512 two warps
+//     share the rows and split the output dims;
+//   * K / V arrive in chunks of BK keys, double-buffered (cp.async; a bf16
+//     cache is widened to fp32 while staging);
+//   * S = Q K^T and O += P V run on mma.sync m16n8k8 TF32 with the 3xTF32
+//     split (x = hi + lo, both TF32; hi.hi + hi.lo + lo.hi): products to
+//     about 2^-21 relative, fp32 accumulation -- the per-layer parity bound
+//     of 1e-4 holds as with fp32 CUDA-core math;
+//   * the online softmax runs on the S fragments (row max / sum across the
+//     lane quad), rescaling the O accumulators only when a row's maximum rises.
 #include "ms_common.cuh"
 #include "ms_kernels.h"
 
 namespace ms {
 
-constexpr int kPfThreads = 256;
+constexpr int kPfWarps = 8;
+constexpr int kPfThreads = kPfWarps * kWarp;
 
 template <int HD>
-struct PfShape {
-  static constexpr int R = HD >= 512 ? 32 : 64;           // query vectors per CTA
-  static constexpr int BK = 32;                            // keys per chunk
-  static constexpr int QS = HD + 4;                        // padded Q / K / V row (floats)
-  static constexpr int PS = BK + 1;                        // score row stride
-  static constexpr int TD = (HD / 4) < 32 ? HD / 4 : 32;  // P.V threads along hd (float4)
-  static constexpr int TR = kPfThreads / TD;               // P.V threads along rows
-  static constexpr int RPT = R / TR;                       // P.V rows per thread
-  static constexpr int DPT = HD / 4 / TD;                  // P.V float4 per thread
-  static constexpr int SR = R / 32;                        // score rows per thread
-  static constexpr size_t smem_floats = (size_t)R * QS + 2 * (size_t)BK * QS + (size_t)R * PS + 3 * R;
-  static_assert(R % TR == 0 && (HD / 4) % TD == 0 && R % 32 == 0, "tile shape");
+struct PfTc {
+  static constexpr int WS = HD >= 512 ? 2 : 1;   // warps sharing an m-tile (split of hd)
+  static constexpr int MT = kPfWarps / WS;       // m-tiles per CTA
+  static constexpr int R = 16 * MT;              // query vectors per CTA
+  static constexpr int DH = HD / WS;             // output dims per warp
+  static constexpr int BK = HD >= 512 ? 8 : 16;  // keys per chunk
+  static constexpr int NT = BK / 8;              // S n-tiles per chunk
+  static constexpr int OT = DH / 8;              // O n-tiles per warp
+  static constexpr int KS = 4 / NT;              // S accumulator sets (independent MMA chains)
+  static constexpr int QS = HD + 4;              // Q / K row stride (floats): conflict-free A / B loads
+  static constexpr int VS = HD + 8;              // V row stride: conflict-free transposed B loads
+  static constexpr size_t smem_floats = (size_t)R * QS + 2 * (size_t)BK * (QS + VS);
 };
 
-template <int HD, int G>
+__device__ __forceinline__ uint32_t tf32_hi(float x) {
+  uint32_t h;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(h) : "f"(x));
+  return h;
+}
+// x = hi + lo with hi, lo representable in TF32
+__device__ __forceinline__ void tf32_split(float x, uint32_t& hi, uint32_t& lo) {
+  hi = tf32_hi(x);
+  lo = tf32_hi(x - __uint_as_float(hi));
+}
+
+__device__ __forceinline__ void mma_tf32(float (&c)[4], const uint32_t (&a)[4], uint32_t b0,
+                                         uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// c += a b with both operands split: hi.hi + hi.lo + lo.hi
+__device__ __forceinline__ void mma_3xtf32(float (&c)[4], const uint32_t (&ah)[4],
+                                           const uint32_t (&al)[4], uint32_t bh0, uint32_t bh1,
+                                           uint32_t bl0, uint32_t bl1) {
+  mma_tf32(c, al, bh0, bh1);
+  mma_tf32(c, ah, bl0, bl1);
+  mma_tf32(c, ah, bh0, bh1);
+}
+
+template <int HD, int G, bool BF>
 __global__ void __launch_bounds__(kPfThreads, 1) attn_prefill_kernel(const AttnParams p) {
-  using S = PfShape<HD>;
-  constexpr int R = S::R, BK = S::BK, QS = S::QS, PS = S::PS;
+  using S = PfTc<HD>;
+  constexpr int R = S::R, BK = S::BK, NT = S::NT, OT = S::OT, QS = S::QS, VS = S::VS, KS = S::KS;
   constexpr int BQ = R / G;  // tokens per block
   extern __shared__ __align__(16) float sm[];
-  float* sQ = sm;                       // [R][QS]
-  float* sK = sQ + R * QS;              // [BK][QS]
-  float* sV = sK + BK * QS;             // [BK][QS]
-  float* sP = sV + BK * QS;             // [R][PS]
-  float* sMax = sP + R * PS;            // [R] running maximum
-  float* sSum = sMax + R;               // [R] running sum
-  float* sCorr = sSum + R;              // [R] rescale factor of this chunk
+  float* sQ = sm;                   // [R][QS]
+  float* sK = sQ + R * QS;          // [2][BK][QS]
+  float* sV = sK + 2 * BK * QS;     // [2][BK][VS]
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int mt = warp / S::WS;                // this warp's m-tile
+  const int d_base = (warp % S::WS) * S::DH;  // and its output dims
   const int4 blk = p.blocks[blockIdx.x];
   const int row0 = blk.x, nq = blk.y, seq = blk.z, pos0 = blk.w;
   const int hk = blockIdx.y;
   pdl_wait();
   pdl_trigger();
 
-  // ---- query vectors r = token * G + head ----
+  const int t_begin = p.window > 0 ? max(0, pos0 + 1 - p.window) : 0;
+  const int t_last = pos0 + nq - 1;
+  const size_t head_off = (size_t)hk * HD;
+  const int n_chunks = (t_last - t_begin) / BK + 1;
+
+  // K / V rows t0 .. t0 + BK - 1 into buffer b (rows past t_last: zeros)
+  auto stage = [&](int b, int t0) {
+    float* k = sK + b * BK * QS;
+    float* v = sV + b * BK * VS;
+    for (int i = tid; i < BK * (HD / 4); i += kPfThreads) {
+      const int j = i / (HD / 4), d4 = i % (HD / 4);
+      const int tt = t0 + j;
+      if (tt > t_last) {
+        *reinterpret_cast<float4*>(k + j * QS + 4 * d4) = make_float4(0.f, 0.f, 0.f, 0.f);
+        *reinterpret_cast<float4*>(v + j * VS + 4 * d4) = make_float4(0.f, 0.f, 0.f, 0.f);
+        continue;
+      }
+      const size_t off = kv_row_offset(p.kv.block_table, p.kv.bt_stride, p.kv.page, p.kv.cap,
+                                       p.kv.circular, seq, tt, p.kv.kv_dim) + head_off + 4 * d4;
+      if constexpr (BF) {
+        *reinterpret_cast<float4*>(k + j * QS + 4 * d4) = kv_get4(p.kv.k, 1, off);
+        *reinterpret_cast<float4*>(v + j * VS + 4 * d4) = kv_get4(p.kv.v, 1, off);
+      } else {
+        cp_async16(k + j * QS + 4 * d4, p.kv.k + off);
+        cp_async16(v + j * VS + 4 * d4, p.kv.v + off);
+      }
+    }
+    cp_async_commit();
+  };
+  stage(0, t_begin);
+
+  // ---- query vectors r = token * G + head (padding rows: zeros) ----
   for (int i = tid; i < R * (HD / 4); i += kPfThreads) {
     const int r = i / (HD / 4), d4 = i % (HD / 4);
     const int tok = r / G, h = r % G;
@@ -73,168 +134,175 @@ __global__ void __launch_bounds__(kPfThreads, 1) attn_prefill_kernel(const AttnP
                                            (size_t)(hk * G + h) * HD + 4 * d4);
     *reinterpret_cast<float4*>(sQ + r * QS + 4 * d4) = v;
   }
-  for (int r = tid; r < R; r += kPfThreads) {
-    sMax[r] = -INFINITY;
-    sSum[r] = 0.f;
+
+  // this lane's two rows of the m-tile: g and g + 8
+  int pos_r[2], lo_r[2];
+  bool ok_r[2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int r = mt * 16 + g + 8 * h;
+    const int tok = r / G;
+    ok_r[h] = tok < nq && tok < BQ;
+    pos_r[h] = pos0 + tok;
+    lo_r[h] = p.window > 0 ? max(0, pos_r[h] + 1 - p.window) : 0;
   }
-
-  const int t_begin = p.window > 0 ? max(0, pos0 + 1 - p.window) : 0;
-  const int t_last = pos0 + nq - 1;
-  const size_t head_off = (size_t)hk * HD;
-
-  // P.V accumulators
-  const int pr = tid / S::TD, pd = tid % S::TD;
-  float4 acc[S::RPT][S::DPT];
+  float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
+  float o[OT][4];
 #pragma unroll
-  for (int i = 0; i < S::RPT; ++i)
-#pragma unroll
-    for (int q = 0; q < S::DPT; ++q) acc[i][q] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int n = 0; n < OT; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+  const float* qa = sQ + (mt * 16 + g) * QS + t;
 
-  // score tile: rows sr + 32 i, keys 8 jj + sj
-  const int sj = tid & 7, sr = tid >> 3;
-
-  for (int t0 = t_begin; t0 <= t_last; t0 += BK) {
-    __syncthreads();  // previous chunk's P and V are consumed
-    // ---- stage K / V rows t0 .. t0 + BK - 1 ----
-    for (int i = tid; i < BK * (HD / 4); i += kPfThreads) {
-      const int j = i / (HD / 4), d4 = i % (HD / 4);
-      const int t = t0 + j;
-      float4 kv4 = make_float4(0.f, 0.f, 0.f, 0.f), vv4 = kv4;
-      if (t <= t_last) {
-        const size_t off = kv_row_offset(p.kv.block_table, p.kv.bt_stride, p.kv.page, p.kv.cap,
-                                         p.kv.circular, seq, t, p.kv.kv_dim) + head_off + 4 * d4;
-        kv4 = kv_get4(p.kv.k, p.kv.bf16, off);
-        vv4 = kv_get4(p.kv.v, p.kv.bf16, off);
-      }
-      *reinterpret_cast<float4*>(sK + j * QS + 4 * d4) = kv4;
-      *reinterpret_cast<float4*>(sV + j * QS + 4 * d4) = vv4;
+  for (int c = 0; c < n_chunks; ++c) {
+    const int t0 = t_begin + c * BK;
+    if (c + 1 < n_chunks) {
+      stage((c + 1) & 1, t0 + BK);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
     }
-    __syncthreads();
+    __syncthreads();  // chunk c (and, the first time, Q) is in shared memory
+    const float* k = sK + (c & 1) * BK * QS;
+    const float* v = sV + (c & 1) * BK * VS;
 
-    // ---- scores ----
-    {
-      float s[S::SR][4];
+    // ---- S = Q K^T for this warp's 16 rows x BK keys ----
+    // k-step j accumulates into set j % KS: KS x NT = 4 independent chains
+    float sa[KS][NT][4];
 #pragma unroll
-      for (int i = 0; i < S::SR; ++i)
+    for (int q = 0; q < KS; ++q)
 #pragma unroll
-        for (int jj = 0; jj < 4; ++jj) s[i][jj] = 0.f;
-#pragma unroll 4
-      for (int d4 = 0; d4 < HD / 4; ++d4) {
-        float4 qv[S::SR], kv[4];
+      for (int n = 0; n < NT; ++n) sa[q][n][0] = sa[q][n][1] = sa[q][n][2] = sa[q][n][3] = 0.f;
+#pragma unroll 2
+    for (int k0 = 0; k0 < HD; k0 += 8 * KS) {
 #pragma unroll
-        for (int i = 0; i < S::SR; ++i)
-          qv[i] = *reinterpret_cast<const float4*>(sQ + (sr + 32 * i) * QS + 4 * d4);
+      for (int q = 0; q < KS; ++q) {
+        const int kk = k0 + 8 * q;
+        uint32_t ah[4], al[4];
+        tf32_split(qa[kk], ah[0], al[0]);
+        tf32_split(qa[8 * QS + kk], ah[1], al[1]);
+        tf32_split(qa[kk + 4], ah[2], al[2]);
+        tf32_split(qa[8 * QS + kk + 4], ah[3], al[3]);
 #pragma unroll
-        for (int jj = 0; jj < 4; ++jj)
-          kv[jj] = *reinterpret_cast<const float4*>(sK + (8 * jj + sj) * QS + 4 * d4);
-#pragma unroll
-        for (int i = 0; i < S::SR; ++i)
-#pragma unroll
-          for (int jj = 0; jj < 4; ++jj) {
-            s[i][jj] = fmaf(qv[i].x, kv[jj].x, s[i][jj]);
-            s[i][jj] = fmaf(qv[i].y, kv[jj].y, s[i][jj]);
-            s[i][jj] = fmaf(qv[i].z, kv[jj].z, s[i][jj]);
-            s[i][jj] = fmaf(qv[i].w, kv[jj].w, s[i][jj]);
-          }
-      }
-#pragma unroll
-      for (int i = 0; i < S::SR; ++i) {
-        const int r = sr + 32 * i;
-        const int tok = r / G;
-        const int P = pos0 + tok;
-        const int lo = p.window > 0 ? max(0, P + 1 - p.window) : 0;
-#pragma unroll
-        for (int jj = 0; jj < 4; ++jj) {
-          const int t = t0 + 8 * jj + sj;
-          const bool ok = tok < nq && tok < BQ && t <= P && t >= lo;
-          sP[r * PS + 8 * jj + sj] = ok ? s[i][jj] * p.scale : -INFINITY;
+        for (int n = 0; n < NT; ++n) {
+          const float* kr = k + (8 * n + g) * QS + kk + t;
+          uint32_t bh0, bl0, bh1, bl1;
+          tf32_split(kr[0], bh0, bl0);
+          tf32_split(kr[4], bh1, bl1);
+          mma_3xtf32(sa[q][n], ah, al, bh0, bh1, bl0, bl1);
         }
       }
     }
-    __syncthreads();
-
-    // ---- online softmax: one warp per row ----
-    for (int r = warp; r < R; r += kPfThreads / kWarp) {
-      const float sc = sP[r * PS + lane];
-      const float mx = warp_max(sc);
-      const float m_old = sMax[r];
-      const float m_new = fmaxf(m_old, mx);
-      const float pv = sc == -INFINITY ? 0.f : expf(sc - m_new);
-      const float sum = warp_sum(pv);
-      sP[r * PS + lane] = pv;
-      if (lane == 0) {
-        const float corr = m_old == -INFINITY ? (m_new == -INFINITY ? 1.f : 0.f) : expf(m_old - m_new);
-        sCorr[r] = corr;
-        sSum[r] = sSum[r] * corr + sum;
-        sMax[r] = m_new;
+    float s[NT][4];
+#pragma unroll
+    for (int n = 0; n < NT; ++n)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float v = sa[0][n][e];
+#pragma unroll
+        for (int q = 1; q < KS; ++q) v += sa[q][n][e];
+        s[n][e] = v;
       }
-    }
-    __syncthreads();
 
-    // ---- O = O * corr + P V ----
+    // ---- mask, online softmax on the fragments ----
+    // s[n][0..1]: row g, keys 8n + 2t, +1; s[n][2..3]: row g + 8
 #pragma unroll
-    for (int i = 0; i < S::RPT; ++i) {
-      const float c = sCorr[pr + S::TR * i];
+    for (int h = 0; h < 2; ++h) {
+      float mx = -INFINITY;
 #pragma unroll
-      for (int q = 0; q < S::DPT; ++q) {
-        acc[i][q].x *= c; acc[i][q].y *= c; acc[i][q].z *= c; acc[i][q].w *= c;
-      }
-    }
-#pragma unroll 4
-    for (int j = 0; j < BK; ++j) {
-      float pj[S::RPT];
+      for (int n = 0; n < NT; ++n)
 #pragma unroll
-      for (int i = 0; i < S::RPT; ++i) pj[i] = sP[(pr + S::TR * i) * PS + j];
-#pragma unroll
-      for (int q = 0; q < S::DPT; ++q) {
-        const float4 v = *reinterpret_cast<const float4*>(sV + j * QS + 4 * (pd + S::TD * q));
-#pragma unroll
-        for (int i = 0; i < S::RPT; ++i) {
-          acc[i][q].x = fmaf(pj[i], v.x, acc[i][q].x);
-          acc[i][q].y = fmaf(pj[i], v.y, acc[i][q].y);
-          acc[i][q].z = fmaf(pj[i], v.z, acc[i][q].z);
-          acc[i][q].w = fmaf(pj[i], v.w, acc[i][q].w);
+        for (int e = 0; e < 2; ++e) {
+          const int tt = t0 + 8 * n + 2 * t + e;
+          const bool ok = ok_r[h] && tt <= pos_r[h] && tt >= lo_r[h];
+          const float sv = ok ? s[n][2 * h + e] * p.scale : -INFINITY;
+          s[n][2 * h + e] = sv;
+          mx = fmaxf(mx, sv);
         }
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      if (mx > m_run[h]) {  // the row's maximum rises: rescale (lanes of a quad agree)
+        const float corr = expf(m_run[h] - mx);  // 0 the first time
+        l_run[h] *= corr;
+#pragma unroll
+        for (int n = 0; n < OT; ++n) {
+          o[n][2 * h] *= corr;
+          o[n][2 * h + 1] *= corr;
+        }
+        m_run[h] = mx;
+      }
+#pragma unroll
+      for (int n = 0; n < NT; ++n)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const float sv = s[n][2 * h + e];
+          const float pv = sv == -INFINITY ? 0.f : expf(sv - m_run[h]);
+          s[n][2 * h + e] = pv;
+          l_run[h] += pv;  // this lane's share; the quad is summed at the end
+        }
+    }
+
+    // ---- O += P V ----
+    // A fragment of P for keys 8n .. 8n + 7: (row g, key t), (g + 8, t),
+    // (g, t + 4), (g + 8, t + 4); key j of row g sits in lane (g, j / 2),
+    // element j % 2 of the S fragment
+    const int src = (lane & ~3) | (t >> 1);
+#pragma unroll
+    for (int n = 0; n < NT; ++n) {
+      const float x0 = __shfl_sync(0xffffffffu, s[n][0], src);
+      const float x1 = __shfl_sync(0xffffffffu, s[n][1], src);
+      const float x2 = __shfl_sync(0xffffffffu, s[n][2], src);
+      const float x3 = __shfl_sync(0xffffffffu, s[n][3], src);
+      const float y0 = __shfl_sync(0xffffffffu, s[n][0], src + 2);
+      const float y1 = __shfl_sync(0xffffffffu, s[n][1], src + 2);
+      const float y2 = __shfl_sync(0xffffffffu, s[n][2], src + 2);
+      const float y3 = __shfl_sync(0xffffffffu, s[n][3], src + 2);
+      const bool odd = t & 1;
+      uint32_t ah[4], al[4];
+      tf32_split(odd ? x1 : x0, ah[0], al[0]);  // (g, t)
+      tf32_split(odd ? x3 : x2, ah[1], al[1]);  // (g + 8, t)
+      tf32_split(odd ? y1 : y0, ah[2], al[2]);  // (g, t + 4)
+      tf32_split(odd ? y3 : y2, ah[3], al[3]);  // (g + 8, t + 4)
+      const float* vr = v + (8 * n + t) * VS + d_base + g;
+#pragma unroll
+      for (int d = 0; d < OT; ++d) {
+        uint32_t bh0, bl0, bh1, bl1;
+        tf32_split(vr[8 * d], bh0, bl0);           // (key t, dim 8d + g)
+        tf32_split(vr[4 * VS + 8 * d], bh1, bl1);  // (key t + 4, dim 8d + g)
+        mma_3xtf32(o[d], ah, al, bh0, bh1, bl0, bl1);
       }
     }
+    __syncthreads();  // buffer c & 1 is free for chunk c + 2
   }
-  __syncthreads();
 
-  // ---- out = O / sum ----
+  // ---- out = O / sum (valid rows) ----
 #pragma unroll
-  for (int i = 0; i < S::RPT; ++i) {
-    const int r = pr + S::TR * i;
-    const int tok = r / G, h = r % G;
-    if (tok >= nq || tok >= BQ) continue;
-    const float inv = 1.0f / sSum[r];
-    float* o = p.out + (size_t)(row0 + tok) * p.ldo + (size_t)(hk * G + h) * HD;
+  for (int h = 0; h < 2; ++h) {
+    float l = l_run[h];
+    l += __shfl_xor_sync(0xffffffffu, l, 1);
+    l += __shfl_xor_sync(0xffffffffu, l, 2);
+    if (!ok_r[h]) continue;
+    const int r = mt * 16 + g + 8 * h;
+    const int tok = r / G, hq = r % G;
+    const float inv = 1.0f / l;
+    float* out = p.out + (size_t)(row0 + tok) * p.ldo + (size_t)(hk * G + hq) * HD + d_base + 2 * t;
 #pragma unroll
-    for (int q = 0; q < S::DPT; ++q) {
-      float4 v = acc[i][q];
-      v.x *= inv; v.y *= inv; v.z *= inv; v.w *= inv;
-      *reinterpret_cast<float4*>(o + 4 * (pd + S::TD * q)) = v;
-    }
+    for (int d = 0; d < OT; ++d)
+      *reinterpret_cast<float2*>(out + 8 * d) = make_float2(o[d][2 * h] * inv, o[d][2 * h + 1] * inv);
   }
 }
 
-template <int HD, int G>
-static size_t pf_smem() {
-  return PfShape<HD>::smem_floats * sizeof(float);
-}
-
-template <int HD, int G>
+template <int HD, int G, bool BF>
 static cudaError_t launch_pf(const AttnParams& p, cudaStream_t s, bool pdl) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.n_blocks, p.n_kv, 1);
   cfg.blockDim = dim3(kPfThreads);
-  cfg.dynamicSmemBytes = pf_smem<HD, G>();
+  cfg.dynamicSmemBytes = PfTc<HD>::smem_floats * sizeof(float);
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, attn_prefill_kernel<HD, G>, p);
+  return cudaLaunchKernelEx(&cfg, attn_prefill_kernel<HD, G, BF>, p);
 }
 
 #define MS_PF_CASES(X)                                                                   \
@@ -243,7 +311,7 @@ static cudaError_t launch_pf(const AttnParams& p, cudaStream_t s, bool pdl) {
   X(512, 4)
 
 int attention_prefill_tokens(int hd, int group) {
-  const int R = hd >= 512 ? 32 : 64;
+  const int R = hd >= 512 ? PfTc<512>::R : PfTc<256>::R;
   if (group <= 0 || group > R) return 0;
 #define MS_PF_HAS(HDV, GV) \
   if (hd == HDV && group == GV) return R / GV;
@@ -259,8 +327,9 @@ cudaError_t launch_attention_prefill(const AttnParams& p, cudaStream_t s, bool p
       (p.kv.bf16 && (p.kv.kv_dim & 7)))
     return cudaErrorInvalidConfiguration;
   const int G = p.n_heads / p.n_kv;
-#define MS_PF_CASE(HDV, GV) \
-  if (p.hd == HDV && G == GV) return launch_pf<HDV, GV>(p, s, pdl);
+#define MS_PF_CASE(HDV, GV)                                                  \
+  if (p.hd == HDV && G == GV)                                                \
+    return p.kv.bf16 ? launch_pf<HDV, GV, true>(p, s, pdl) : launch_pf<HDV, GV, false>(p, s, pdl);
   MS_PF_CASES(MS_PF_CASE)
 #undef MS_PF_CASE
   return cudaErrorInvalidConfiguration;
@@ -268,12 +337,15 @@ cudaError_t launch_attention_prefill(const AttnParams& p, cudaStream_t s, bool p
 
 cudaError_t prepare_attention_prefill() {
   cudaError_t e = cudaSuccess;
-#define MS_PF_PREP(HDV, GV)                                                                     \
-  if (e == cudaSuccess)                                                                        \
-    e = cudaFuncSetAttribute(attn_prefill_kernel<HDV, GV>,                                     \
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pf_smem<HDV, GV>());
+#define MS_PF_PREP1(HDV, GV, BFV)                                                            \
+  if (e == cudaSuccess)                                                                      \
+    e = cudaFuncSetAttribute(attn_prefill_kernel<HDV, GV, BFV>,                             \
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,                   \
+                             (int)(PfTc<HDV>::smem_floats * sizeof(float)));
+#define MS_PF_PREP(HDV, GV) MS_PF_PREP1(HDV, GV, false) MS_PF_PREP1(HDV, GV, true)
   MS_PF_CASES(MS_PF_PREP)
 #undef MS_PF_PREP
+#undef MS_PF_PREP1
   return e;
 }
 
