@@ -565,6 +565,16 @@ extern "C" ms_status ms_q4_weight_destroy(ms_ctx* c, ms_q4_weight* w) {
   return MS_OK;
 }
 
+// MS_SPLITK_GLOBAL=1: split merges through global memory and arrival tickets
+// instead of thread-block clusters (the same sums; for comparisons).
+static bool splitk_global_forced() {
+  static const bool on = [] {
+    const char* e = getenv("MS_SPLITK_GLOBAL");
+    return e && e[0] == '1';
+  }();
+  return on;
+}
+
 // Launch plan of one projection: decode kernel (M <= 8) or the tiled kernel,
 // m-group size, chunks per round, k-segment and the number of k-segments.
 struct GemvPlan {
@@ -1371,10 +1381,19 @@ static ms_status run_layer(ms_ctx* c, ms_model* m, const ms_kv* kv, int li, int 
     if (mk) splits = mk_attn_splits(c->sm_count, M, L.d.n_kv_heads);  // one unit per CTA
     splits = std::min(splits, std::max(1, (span + min_per - 1) / min_per));
     splits = std::min(splits, attention_max_splits());
+    // merge inside a thread-block cluster when the splits fit one (up to 16;
+    // a fill-rule count a little above that is trimmed to it), unless
+    // MS_SPLITK_GLOBAL=1 asks for the global-memory merge
+    const int max_cl = attention_max_cluster();
+    const bool try_cl = !mk && max_cl > 0 && !splitk_global_forced();
+    if (try_cl && splits > max_cl && splits <= max_cl + max_cl / 2 &&
+        (span + 255) / 256 <= max_cl)
+      splits = max_cl;
     const int G = L.d.n_heads / L.d.n_kv_heads;
     while (splits > 1 &&
            (size_t)M * L.d.n_kv_heads * splits * G * (L.d.head_dim + 4) > c->part_floats)
       splits = (splits + 1) / 2;
+    a.cluster = try_cl && splits > 1 && splits <= max_cl;
     if ((size_t)M * L.d.n_kv_heads > c->n_counters)
       return fail(c, MS_ERR_CAPACITY, "attention: too many rows for the ticket counters");
     a.chunk = min_per;

@@ -28,6 +28,12 @@
 
 namespace ms {
 
+// Most splits of one (row, KV head) that run as a cluster (a non-portable
+// size: B200 runs clusters of up to 16 CTAs), and whether every attention
+// kernel can hold such a cluster (checked once by prepare_attention).
+constexpr int kAttnMaxCluster = 16;
+static bool g_attn_cluster_ok = false;
+
 // BF: the cache holds bfloat16 K / V (rows half the bytes, widened to fp32
 // as they are read out of the ring).
 template <int HD, int G, bool BF>
@@ -45,9 +51,12 @@ struct WarpAttn {
   static constexpr int PMIN = (G * (HD + 2) * 4 + SLOTB - 1) / SLOTB;
   static constexpr int P1 = P0 > 8 ? 8 : (P0 < 2 ? 2 : P0);
   static constexpr int P = P1 < PMIN ? PMIN : P1;
-  static constexpr size_t smem = (size_t)NW * P * SLOTB;
+  static constexpr size_t ring = (size_t)NW * P * SLOTB;
   static constexpr int ST = HD + 4;                    // partial row stride (16 B)
-  static_assert(NW * G * (HD + 2) * 4 <= NW * P * SLOTB, "combine buffer");
+  // + this split's partial [G][ST] for the cluster merge
+  static constexpr size_t smem = ring + (size_t)G * ST * 4;
+  static_assert(NW * G * (HD + 2) * 4 <= ring, "combine buffer");
+  static_assert(ring % 16 == 0, "partial alignment");
   static_assert(P <= 32, "row offsets are fetched 32 positions at a time");
 };
 
@@ -77,7 +86,7 @@ __global__ void __launch_bounds__(WarpAttn<HD, G, BF>::NT) attn_kernel(const Att
   using S = WarpAttn<HD, G, BF>;
   constexpr int NW = S::NW, NT = S::NT, P = S::P, PL = S::PL, VEC = S::VEC, ST = S::ST;
   constexpr int EB = S::EB;
-  extern __shared__ __align__(128) unsigned char smb[];  // [NW][P][K row | V row]
+  extern __shared__ __align__(128) unsigned char smb[];  // [NW][P][K row | V row], partial
   __shared__ float s_w[G][kAttnMaxSplits];
   __shared__ int s_last;
 
@@ -91,13 +100,19 @@ __global__ void __launch_bounds__(WarpAttn<HD, G, BF>::NT) attn_kernel(const Att
   const int n = pos + 1 - lo;
   const int per = max((n + p.n_splits - 1) / p.n_splits, p.chunk);
   const int ns = (n + per - 1) / per;
-  if (split >= ns) return;  // CTA-uniform
+  // cluster mode: the n_splits CTAs of (row, KV head) are one cluster and
+  // every one of them takes part in both cluster barriers; a split without
+  // positions runs the (empty) loop and writes nothing
+  const bool cl = p.cluster != 0;
+  const bool active = split < ns;
+  if (!active && !cl) return;  // CTA-uniform
   const int t_begin = lo + split * per;
   const int t_end = min(pos + 1, t_begin + per);
   const int n_pos = t_end - t_begin;
   const int cnt = n_pos > warp ? (n_pos - warp + NW - 1) / NW : 0;  // this warp's positions
   const size_t head_off = (size_t)hk * HD;
   unsigned char* ring = smb + (size_t)warp * P * S::SLOTB;
+  float* cpart = reinterpret_cast<float*>(smb + S::ring);  // [G][ST] (cluster mode)
   const unsigned char* kpool = reinterpret_cast<const unsigned char*>(p.kv.k);
   const unsigned char* vpool = reinterpret_cast<const unsigned char*>(p.kv.v);
 
@@ -227,8 +242,15 @@ __global__ void __launch_bounds__(WarpAttn<HD, G, BF>::NT) attn_kernel(const Att
       a = fmaf(c[d], f, a);
       L = fmaf(c[HD + 1], f, L);
     }
-    if (ns == 1) {
+    if (!active) {
+    } else if (ns == 1) {
       p.out[(size_t)m * p.ldo + (hk * G + h) * HD + d] = a / L;
+    } else if (cl) {
+      cpart[h * ST + d] = a;
+      if (d == 0) {
+        cpart[h * ST + HD] = M;
+        cpart[h * ST + HD + 1] = L;
+      }
     } else {
       __stcg(part_base + (size_t)h * ST + d, a);
       if (d == 0) {
@@ -236,6 +258,59 @@ __global__ void __launch_bounds__(WarpAttn<HD, G, BF>::NT) attn_kernel(const Att
         __stcg(part_base + (size_t)h * ST + HD + 1, L);
       }
     }
+  }
+
+  if (cl) {
+    // ---- merge the splits inside the cluster: split sp's partial is in the
+    //      shared memory of CTA sp; every CTA derives the split weights (the
+    //      arithmetic of the global path below) and merges a slice of the
+    //      outputs in split order ---------------------------------------------
+    cluster_arrive();
+    cluster_wait();  // every split's partial is in place
+    if (ns > 1) {
+      const uint32_t cp0 = smem_u32(cpart);
+      for (int h = warp; h < G; h += NW) {
+        const int sp = lane;  // ns <= n_splits <= 32
+        float Mv = -INFINITY, Lv = 0.f;
+        if (sp < ns) {
+          const uint32_t b = dsmem_addr(cp0, (uint32_t)sp) + 4u * (uint32_t)(h * ST + HD);
+          Mv = ld_dsmem(b);
+          Lv = ld_dsmem(b + 4u);
+        }
+        const float Mx = warp_max(Mv);
+        float f = 0.f, L = 0.f;
+        if (sp < ns) {
+          f = expf(Mv - Mx);
+          L = Lv * f;
+        }
+        L = warp_sum(L);
+        const float invL = 1.0f / L;
+        if (sp < ns) s_w[h][sp] = f * invL;
+      }
+      __syncthreads();
+      for (int idx = split * NT + tid; idx < G * HD / 4; idx += p.n_splits * NT) {
+        const int h = idx / (HD / 4), d4 = idx % (HD / 4);
+        const uint32_t off = 4u * (uint32_t)(h * ST + d4 * 4);
+        float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int sp0 = 0; sp0 < ns; sp0 += kAttnMergeBatch) {
+          float4 v[kAttnMergeBatch];
+#pragma unroll
+          for (int b = 0; b < kAttnMergeBatch; ++b)
+            if (sp0 + b < ns) v[b] = ld_dsmem4(dsmem_addr(cp0, (uint32_t)(sp0 + b)) + off);
+#pragma unroll
+          for (int b = 0; b < kAttnMergeBatch; ++b)
+            if (sp0 + b < ns) {
+              const float w = s_w[h][sp0 + b];
+              a.x = fmaf(w, v[b].x, a.x); a.y = fmaf(w, v[b].y, a.y);
+              a.z = fmaf(w, v[b].z, a.z); a.w = fmaf(w, v[b].w, a.w);
+            }
+        }
+        *reinterpret_cast<float4*>(p.out + (size_t)m * p.ldo + (hk * G + h) * HD + d4 * 4) = a;
+      }
+    }
+    cluster_arrive();  // done reading the other CTAs' partials
+    cluster_wait();    // ... and they are done reading this one's
+    return;
   }
   if (ns == 1) return;
 
@@ -306,11 +381,22 @@ static cudaError_t launch_t(const AttnParams& p, cudaStream_t s, bool pdl) {
   cfg.blockDim = dim3(S::NT);
   cfg.dynamicSmemBytes = S::smem;
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  if (pdl) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  if (p.cluster) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = (unsigned)p.n_splits;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = pdl ? 1 : 0;
+  cfg.numAttrs = na;
   return cudaLaunchKernelEx(&cfg, attn_kernel<HD, G, BF>, p);
 }
 
@@ -324,6 +410,7 @@ static cudaError_t launch_t(const AttnParams& p, cudaStream_t s, bool pdl) {
 // n_splits <= 64.
 cudaError_t launch_attention(const AttnParams& p, cudaStream_t s, bool pdl) {
   if (p.n_splits < 1 || p.n_splits > kAttnMaxSplits || p.chunk < 1 || (p.ldq & 3) ||
+      (p.cluster && (p.n_splits > kAttnMaxCluster || !g_attn_cluster_ok)) ||
       (p.ldo & 3) || (p.kv.kv_dim & 3) || (p.kv.bf16 && (p.kv.kv_dim & 7)))
     return cudaErrorInvalidConfiguration;
   const int G = p.n_heads / p.n_kv;
@@ -337,13 +424,48 @@ cudaError_t launch_attention(const AttnParams& p, cudaStream_t s, bool pdl) {
 
 int attention_max_splits() { return kAttnMaxSplits; }
 
+// True when a cluster of kAttnMaxCluster CTAs of this kernel can be resident.
+template <typename Kernel>
+static bool attn_cluster_fits(Kernel fn, int threads, size_t smem) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(kAttnMaxCluster, 1, 1);
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = kAttnMaxCluster;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  const cudaError_t e = cudaOccupancyMaxActiveClusters(&n, fn, &cfg);
+  if (e != cudaSuccess) cudaGetLastError();
+  return e == cudaSuccess && n > 0;
+}
+
+int attention_max_cluster() { return g_attn_cluster_ok ? kAttnMaxCluster : 0; }
+
 cudaError_t prepare_attention() {
   cudaError_t e = cudaSuccess;
+  g_attn_cluster_ok = true;
 #define MS_ATTN_PREP1(HDV, GV, BFV)                                                        \
   if (e == cudaSuccess && WarpAttn<HDV, GV, BFV>::smem > 48 * 1024)                       \
     e = cudaFuncSetAttribute(attn_kernel<HDV, GV, BFV>,                                   \
                              cudaFuncAttributeMaxDynamicSharedMemorySize,                 \
-                             (int)WarpAttn<HDV, GV, BFV>::smem);
+                             (int)WarpAttn<HDV, GV, BFV>::smem);                          \
+  if (e == cudaSuccess && g_attn_cluster_ok) {                                            \
+    /* clusters are an optimisation: without them the global merge runs */               \
+    if (cudaFuncSetAttribute(attn_kernel<HDV, GV, BFV>,                                   \
+                             cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess) { \
+      cudaGetLastError();                                                                 \
+      g_attn_cluster_ok = false;                                                          \
+    } else {                                                                              \
+      g_attn_cluster_ok = attn_cluster_fits(attn_kernel<HDV, GV, BFV>,                    \
+                                            WarpAttn<HDV, GV, BFV>::NT,                   \
+                                            WarpAttn<HDV, GV, BFV>::smem);                \
+    }                                                                                     \
+  }
 #define MS_ATTN_PREP(HDV, GV) MS_ATTN_PREP1(HDV, GV, false) MS_ATTN_PREP1(HDV, GV, true)
   MS_ATTN_CASES(MS_ATTN_PREP)
 #undef MS_ATTN_PREP

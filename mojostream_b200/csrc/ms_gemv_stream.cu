@@ -3,6 +3,8 @@
 // unit (tile group x k-segment) of ms_proj_unit.cuh, which documents the
 // arithmetic.  Weights are issued before griddepcontrol.wait (they do not
 // depend on the previous kernel); the activations after it.
+#include <cstdlib>
+
 #include "ms_proj_unit.cuh"
 
 namespace ms {
@@ -40,24 +42,57 @@ __global__ void __launch_bounds__(kSThreads, 2) gemv_stream_kernel(const GemvPar
         atomicOr(p.err, kErrWaitTimeout);  // consumers time out on the stages never issued
       ring_drain(ring, seq);
     }
+    __syncwarp();
+    if (p.cluster && p.ksplit > 1) {
+      // the consumers' two cluster barriers (partials ready, partials read)
+      cluster_arrive();
+      cluster_wait();
+      cluster_arrive();
+      cluster_wait();
+    }
     return;
   }
   pdl_wait();
   proj_consume<MG>(p, blockIdx.x, blockIdx.y, ring, seq, sB, sh, nullptr);
 }
 
+// The k-segments of a tile group run as one thread-block cluster (2..8 CTAs)
+// and sum their partials through distributed shared memory, unless
+// MS_SPLITK_GLOBAL=1 selects the global-memory partials and arrival tickets
+// (the same sums in the same order).
+static bool splitk_cluster_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("MS_SPLITK_GLOBAL");
+    return !(e && e[0] == '1');
+  }();
+  return on;
+}
+
 template <int MG>
-static cudaError_t launch_stream_t(const GemvParams& p, cudaStream_t s, bool pdl) {
+static cudaError_t launch_stream_t(const GemvParams& p0, cudaStream_t s, bool pdl) {
+  GemvParams p = p0;
+  p.cluster = (p.ksplit > 1 && p.ksplit <= kMaxClusterK && splitk_cluster_enabled()) ? 1 : 0;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(padded_tiles(p.n_tiles) / kGroupTiles, p.ksplit, 1);
   cfg.blockDim = dim3(kSThreads);
   cfg.dynamicSmemBytes = gemv_stream_smem(MG, p.kseg);
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  if (pdl) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  if (p.cluster) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = 1;
+    attr[na].val.clusterDim.y = (unsigned)p.ksplit;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = pdl ? 1 : 0;
+  cfg.numAttrs = na;
   return cudaLaunchKernelEx(&cfg, gemv_stream_kernel<MG>, p);
 }
 

@@ -95,6 +95,10 @@ struct GemvParams {
   // split-K scratch
   float* part;            // partial sums of k-segments
   int* counters;          // arrival tickets (reset by the last arrival)
+  // decode kernel: the ksplit CTAs of a tile group run as one thread-block
+  // cluster and sum their partials through distributed shared memory (part /
+  // counters unused); set by the launcher, 0 in the persistent kernel
+  int cluster;
   int* err;               // error bits for the host (bounded waits)
   // tensor-core path: activation limbs and per-row factors (quant_rows_kernel)
   uint8_t* lq;
@@ -120,6 +124,10 @@ struct AttnParams {
   float scale;
   float* part;    // [M][n_kv][n_splits][G][hd + 4]
   int* counters;  // [M][n_kv]
+  // decode kernel: the n_splits CTAs of (row, KV head) run as one cluster and
+  // merge through distributed shared memory (part / counters unused);
+  // n_splits <= attention_max_cluster()
+  int cluster;
   int* err;       // error bits for the host (bounded waits)
   // prefill kernel: query blocks {row0, n_rows, seq, pos0} of consecutive
   // positions of one sequence (rows row0 .. row0 + n_rows - 1)
@@ -174,6 +182,8 @@ cudaError_t launch_attention(const AttnParams& p, cudaStream_t s, bool pdl);
 cudaError_t launch_attention_prefill(const AttnParams& p, cudaStream_t s, bool pdl);
 int attention_prefill_tokens(int head_dim, int group);  // tokens per query block
 int attention_max_splits();
+// Most splits that can run as one cluster (0: no cluster merge on this GPU).
+int attention_max_cluster();
 // one-time kernel attributes (dynamic shared memory above 48 KB)
 cudaError_t prepare_gemv_stream();
 cudaError_t prepare_attention();

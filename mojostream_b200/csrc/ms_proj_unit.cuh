@@ -25,8 +25,11 @@
 // A producer thread streams the unit's weights with cp.async.bulk (16 KB
 // stages = 4 k-chunks x 8 tiles) through an mbarrier ring; 16 consumer warps,
 // two per tile, each take two chunks of every stage.  Split-K partials of a
-// group are summed by the last unit in k order: results do not depend on
-// timing.  Activations written earlier in the same launch are read through L2
+// group are summed in k order, either inside a thread-block cluster of the
+// group's k-segments (distributed shared memory, no global round trip; the
+// one-launch kernel) or by the last unit through global memory and an
+// arrival ticket (the persistent kernel, and splits above 8): results do not
+// depend on timing.  Activations written earlier in the same launch are read through L2
 // (ld.global.cg), never through the non-coherent L1 / texture path.
 #pragma once
 
@@ -48,6 +51,8 @@ constexpr float kQuantOne = 1073741824.0f;  // 2^30: |q| <= 2^30 at the row maxi
 // most 2560 (MG 1) / 1280 (MG 2) per row, 4 values per item.
 constexpr int kMaxItems = 5;
 constexpr int kConsumerBar = 1;  // named barrier of the 512 consumer threads
+// Most k-segments of one tile group that run as a cluster (portable size).
+constexpr int kMaxClusterK = 8;
 
 // Timeline points inside a unit (profiling builds with -DMS_MK_TRACE only):
 // [cta][op][point], thread 0 of the CTA, first unit of the op.
@@ -297,19 +302,21 @@ __device__ int proj_consume(const GemvParams& p, int group, int kidx, const Stag
         // byte order of a weight word: k 2t, 2t+8, 2t+1, 2t+9
         const int q[4] = {__float2int_rn(va[jt].x * inv), __float2int_rn(vb[jt].x * inv),
                           __float2int_rn(va[jt].y * inv), __float2int_rn(vb[jt].y * inv)};
-        uint32_t wl[4] = {0u, 0u, 0u, 0u};
+        // balanced base-256 limbs q = d0 + 2^8 d1 + 2^16 d2 + 2^24 d3, d0..d2
+        // in [-128, 127], |d3| <= 64: adding 128 to each of the low three
+        // digits makes them the bytes of u = q + 0x808080 (no carries), so
+        // byte l of u ^ 0x808080 is d_l as a signed byte; a byte transpose
+        // then gathers limb l of the four values into word l
+        uint32_t L[4];
 #pragma unroll
         for (int v = 0; v < 4; ++v) {
           qs += q[v];
-          int rest = q[v];
-#pragma unroll
-          for (int l = 0; l < 3; ++l) {  // balanced base-256 limbs
-            const int d = (int)(int8_t)(rest & 0xFF);
-            wl[l] |= ((uint32_t)d & 0xFFu) << (8 * v);
-            rest = (rest - d) >> 8;  // exact: rest - d is a multiple of 256
-          }
-          wl[3] |= ((uint32_t)rest & 0xFFu) << (8 * v);  // |rest| <= 64
+          L[v] = (uint32_t)(q[v] + 0x808080) ^ 0x808080u;
         }
+        const uint32_t t0 = __byte_perm(L[0], L[1], 0x5140), t1 = __byte_perm(L[2], L[3], 0x5140);
+        const uint32_t t2 = __byte_perm(L[0], L[1], 0x7362), t3 = __byte_perm(L[2], L[3], 0x7362);
+        const uint32_t wl[4] = {__byte_perm(t0, t1, 0x5410), __byte_perm(t0, t1, 0x7632),
+                                __byte_perm(t2, t3, 0x5410), __byte_perm(t2, t3, 0x7632)};
         const int kb = i >> 3, h = (i >> 2) & 1, tt = i & 3;
         // lane (g = 4 (r % 2) + l, tt) of column block r / 2, register h
         const int base = ((kb * NJ + (rr >> 1)) * kWarp + 16 * (rr & 1) + tt) * 2 + h;
@@ -411,7 +418,11 @@ __device__ int proj_consume(const GemvParams& p, int group, int kidx, const Stag
     }
   }
   bar_sync_n(kConsumerBar, kSConsumers);
-  if (sh.bad) return kProjFailed;  // CTA-uniform after the barrier
+  // the k-segments of a group run as one cluster (grid-uniform); such a CTA
+  // goes through both cluster barriers below on every path, failed or not
+  const bool cl = p.cluster && p.ksplit > 1;
+  const bool bad = sh.bad != 0;  // CTA-uniform after the barrier
+  if (bad && !cl) return kProjFailed;
   UNIT_TRACE(trace_op, 3);
   if (act && own) {
 #pragma unroll
@@ -421,8 +432,57 @@ __device__ int proj_consume(const GemvParams& p, int group, int kidx, const Stag
     }
   }
 
-  // ---- k-segments of the group: the last unit sums the partials in k order --
-  if (p.ksplit > 1) {
+  bool finish = true;  // this CTA runs the epilogue of its tiles
+  if (cl) {
+    // ---- k-segments as one cluster: every CTA leaves its segment's sums in
+    //      its own shared memory; CTA r (= k-segment r) finishes the tiles tl
+    //      with tl % ksplit == r, summing the ksplit partials in k order (the
+    //      order of the global path below, so the same bits) ----------------
+    if (act && own) {
+#pragma unroll
+      for (int jn = 0; jn < NJ; ++jn) {
+        red[((tl * NJ + jn) * 2 + 0) * kWarp + lane] = rv[jn][0];
+        red[((tl * NJ + jn) * 2 + 1) * kWarp + lane] = rv[jn][1];
+      }
+    }
+    cluster_arrive();
+    cluster_wait();  // every CTA's partials are in its shared memory
+    finish = !bad && (tl % p.ksplit) == kidx;  // warp-uniform
+    if (act && own && finish) {
+      // the loads of kB CTAs' partials are in flight at once
+      constexpr int kB = kMaxClusterK / MG;
+      const uint32_t red0 = smem_u32(red);
+#pragma unroll
+      for (int jn = 0; jn < NJ; ++jn) rv[jn][0] = rv[jn][1] = 0.f;
+#pragma unroll
+      for (int r0 = 0; r0 < kMaxClusterK; r0 += kB) {
+        float v[kB][NJ][2];
+#pragma unroll
+        for (int b = 0; b < kB; ++b) {
+          if (r0 + b < p.ksplit) {
+            const uint32_t rb = dsmem_addr(red0, (uint32_t)(r0 + b));
+#pragma unroll
+            for (int jn = 0; jn < NJ; ++jn) {
+              v[b][jn][0] = ld_dsmem(rb + 4u * (((tl * NJ + jn) * 2 + 0) * kWarp + lane));
+              v[b][jn][1] = ld_dsmem(rb + 4u * (((tl * NJ + jn) * 2 + 1) * kWarp + lane));
+            }
+          }
+        }
+#pragma unroll
+        for (int b = 0; b < kB; ++b) {
+          if (r0 + b < p.ksplit) {
+#pragma unroll
+            for (int jn = 0; jn < NJ; ++jn) {
+              rv[jn][0] += v[b][jn][0];
+              rv[jn][1] += v[b][jn][1];
+            }
+          }
+        }
+      }
+    }
+    cluster_arrive();  // done reading the other CTAs' shared memory
+  } else if (p.ksplit > 1) {
+    // ---- k-segments of the group: the last unit sums the partials in k order
     if (act && own) {
       float* my = p.part + ((size_t)tile * p.ksplit + kidx) * (kTileN * MB);
 #pragma unroll
@@ -468,7 +528,7 @@ __device__ int proj_consume(const GemvParams& p, int group, int kidx, const Stag
   }
 
   // ---- epilogue: half-0 warps finish their tiles ----------------------------
-  if (act && tile < p.n_tiles) {
+  if (finish && act && tile < p.n_tiles) {
 #pragma unroll
     for (int jn = 0; jn < NJ; ++jn) {
       const int m = 2 * jn + (t >> 1);
@@ -490,6 +550,10 @@ __device__ int proj_consume(const GemvParams& p, int group, int kidx, const Stag
     }
   }
   UNIT_TRACE(trace_op, 5);
+  if (cl) {
+    cluster_wait();  // the other CTAs are done reading this CTA's partials
+    return bad ? kProjFailed : kProjFinished;
+  }
   return kProjFinished;
 }
 
