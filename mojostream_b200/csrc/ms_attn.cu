@@ -288,7 +288,9 @@ __global__ void __launch_bounds__(WarpAttn<HD, G, BF>::NT) attn_kernel(const Att
         if (sp < ns) s_w[h][sp] = f * invL;
       }
       __syncthreads();
-      for (int idx = split * NT + tid; idx < G * HD / 4; idx += p.n_splits * NT) {
+      // output float4 items idx = split (mod n_splits): every CTA of the
+      // cluster merges its share, so no one CTA reads all the partials
+      for (int idx = split + tid * p.n_splits; idx < G * HD / 4; idx += p.n_splits * NT) {
         const int h = idx / (HD / 4), d4 = idx % (HD / 4);
         const uint32_t off = 4u * (uint32_t)(h * ST + d4 * 4);
         float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
