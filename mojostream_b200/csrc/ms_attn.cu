@@ -88,6 +88,7 @@ __global__ void __launch_bounds__(WarpAttn<HD, G, BF>::NT) attn_kernel(const Att
   constexpr int EB = S::EB;
   extern __shared__ __align__(128) unsigned char smb[];  // [NW][P][K row | V row], partial
   __shared__ float s_w[G][kAttnMaxSplits];
+  __shared__ float s_f[NW][G], s_M[G], s_L[G];
   __shared__ int s_last;
 
   const int split = blockIdx.x, hk = blockIdx.y, m = blockIdx.z;
@@ -228,20 +229,32 @@ __global__ void __launch_bounds__(WarpAttn<HD, G, BF>::NT) attn_kernel(const Att
     }
   }
   __syncthreads();
-  float* part_base = p.part + (((size_t)m * p.n_kv + hk) * p.n_splits + split) * G * ST;
-  for (int idx = tid; idx < G * HD; idx += NT) {
-    const int h = idx / HD, d = idx % HD;
+  // per head: the maximum over the warps, each warp's weight and the sum
+  // (computed once per head, not per output element)
+  if (tid < G) {
+    const int h = tid;
     float M = -INFINITY;
 #pragma unroll
     for (int w = 0; w < NW; ++w) M = fmaxf(M, comb[((size_t)w * G + h) * (HD + 2) + HD]);
-    float a = 0.f, L = 0.f;
+    float L = 0.f;
 #pragma unroll
     for (int w = 0; w < NW; ++w) {
       const float* c = comb + ((size_t)w * G + h) * (HD + 2);
       const float f = expf(c[HD] - M);  // 0 for warps without positions
-      a = fmaf(c[d], f, a);
+      s_f[w][h] = f;
       L = fmaf(c[HD + 1], f, L);
     }
+    s_M[h] = M;
+    s_L[h] = L;
+  }
+  __syncthreads();
+  float* part_base = p.part + (((size_t)m * p.n_kv + hk) * p.n_splits + split) * G * ST;
+  for (int idx = tid; idx < G * HD; idx += NT) {
+    const int h = idx / HD, d = idx % HD;
+    const float M = s_M[h], L = s_L[h];
+    float a = 0.f;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) a = fmaf(comb[((size_t)w * G + h) * (HD + 2) + d], s_f[w][h], a);
     if (!active) {
     } else if (ns == 1) {
       p.out[(size_t)m * p.ldo + (hk * G + h) * HD + d] = a / L;
