@@ -81,8 +81,12 @@ __device__ __forceinline__ void ld_vec(float* dst, const unsigned char* src) {
   }
 }
 
+MS_STEP_TRACE_DEFINE(ms_trace_attn)
+
 template <int HD, int G, bool BF>
 __global__ void __launch_bounds__(WarpAttn<HD, G, BF>::NT) attn_kernel(const AttnParams p) {
+  ST_NOW(st0);
+  ST_INIT();
   using S = WarpAttn<HD, G, BF>;
   constexpr int NW = S::NW, NT = S::NT, P = S::P, PL = S::PL, VEC = S::VEC, ST = S::ST;
   constexpr int EB = S::EB;
@@ -94,6 +98,7 @@ __global__ void __launch_bounds__(WarpAttn<HD, G, BF>::NT) attn_kernel(const Att
   const int split = blockIdx.x, hk = blockIdx.y, m = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   pdl_wait();
+  ST_NOW(st1);
   pdl_trigger();
 
   const int pos = p.pos[m], seq = p.seq[m];
@@ -106,7 +111,10 @@ __global__ void __launch_bounds__(WarpAttn<HD, G, BF>::NT) attn_kernel(const Att
   // positions runs the (empty) loop and writes nothing
   const bool cl = p.cluster != 0;
   const bool active = split < ns;
-  if (!active && !cl) return;  // CTA-uniform
+  if (!active && !cl) {  // CTA-uniform
+    ST_PUT(p.kv.k, 1, st0, st1);
+    return;
+  }
   const int t_begin = lo + split * per;
   const int t_end = min(pos + 1, t_begin + per);
   const int n_pos = t_end - t_begin;
@@ -146,6 +154,7 @@ __global__ void __launch_bounds__(WarpAttn<HD, G, BF>::NT) attn_kernel(const Att
   unsigned long long offs = row_offsets(0);  // positions 0..31 (P <= 32)
 #pragma unroll
   for (int i = 0; i < P; ++i) issue(i, __shfl_sync(0xffffffffu, offs, i));
+  ST_POINT(0);  // positions and row offsets read, first rows in flight
 
   // this lane's slices: dims (v * 32 + lane) * VEC + e
   float q[G][PL], acc[G][PL], mrun[G], lrun[G];
@@ -212,6 +221,7 @@ __global__ void __launch_bounds__(WarpAttn<HD, G, BF>::NT) attn_kernel(const Att
     }
   }
   cp_async_wait<0>();  // (only empty groups remain)
+  ST_POINT(1);          // this warp's positions done
   __syncthreads();     // every warp is past its ring: it becomes the combine buffer
 
   // ---- combine the warps: comb[w][h][0..HD) outputs, [HD] max, [HD+1] sum ----
@@ -273,6 +283,7 @@ __global__ void __launch_bounds__(WarpAttn<HD, G, BF>::NT) attn_kernel(const Att
     }
   }
 
+  ST_POINT(2);  // warps combined
   if (cl) {
     // ---- merge the splits inside the cluster: split sp's partial is in the
     //      shared memory of CTA sp; every CTA derives the split weights (the
@@ -280,6 +291,7 @@ __global__ void __launch_bounds__(WarpAttn<HD, G, BF>::NT) attn_kernel(const Att
     //      outputs in split order ---------------------------------------------
     cluster_arrive();
     cluster_wait();  // every split's partial is in place
+    ST_POINT(3);
     if (ns > 1) {
       const uint32_t cp0 = smem_u32(cpart);
       for (int h = warp; h < G; h += NW) {
@@ -323,18 +335,26 @@ __global__ void __launch_bounds__(WarpAttn<HD, G, BF>::NT) attn_kernel(const Att
         *reinterpret_cast<float4*>(p.out + (size_t)m * p.ldo + (hk * G + h) * HD + d4 * 4) = a;
       }
     }
+    ST_POINT(4);  // this CTA's share merged
     cluster_arrive();  // done reading the other CTAs' partials
     cluster_wait();    // ... and they are done reading this one's
+    ST_PUT(p.kv.k, 1, st0, st1);
     return;
   }
-  if (ns == 1) return;
+  if (ns == 1) {
+    ST_PUT(p.kv.k, 1, st0, st1);
+    return;
+  }
 
   // ---- merge the splits: the last CTA of (row, KV head) does it in order ---
   __syncthreads();  // partials written
   int* ctr = p.counters + (size_t)m * p.n_kv + hk;
   if (tid == 0) s_last = (ticket_acq_rel(ctr) == ns - 1);
   __syncthreads();
-  if (!s_last) return;
+  if (!s_last) {
+    ST_PUT(p.kv.k, 1, st0, st1);
+    return;
+  }
   for (int h = warp; h < G; h += NW) {
     const float* pr0 = p.part + ((size_t)m * p.n_kv + hk) * p.n_splits * G * ST;
     float Ms[kAttnMaxSplits / kWarp], Ls[kAttnMaxSplits / kWarp];
@@ -386,6 +406,7 @@ __global__ void __launch_bounds__(WarpAttn<HD, G, BF>::NT) attn_kernel(const Att
     *reinterpret_cast<float4*>(p.out + (size_t)m * p.ldo + (hk * G + h) * HD + d4 * 4) = a;
   }
   if (tid == 0) *ctr = 0;
+  ST_PUT(p.kv.k, 1, st0, st1);
 }
 
 template <int HD, int G, bool BF>

@@ -68,9 +68,10 @@ static __device__ unsigned long long g_unit_trace[256 * 256 * 8];  // per transl
     }                                                                            \
   } while (0)
 #else
-#define UNIT_TRACE(op, k) \
-  do {                    \
-  } while (0)
+// the one-launch kernel's timeline (MS_STEP_TRACE builds; nothing otherwise):
+// 6 inputs loaded, 1 quantised, 2 main loop done, 3 halves merged, 4 split-K
+// merged, 5 epilogue done
+#define UNIT_TRACE(op, k) ST_POINT(k)
 #endif
 
 // B fragments of one k-segment: per k32 block, 2*MG MMA column blocks x 32
@@ -481,6 +482,7 @@ __device__ int proj_consume(const GemvParams& p, int group, int kidx, const Stag
       }
     }
     cluster_arrive();  // done reading the other CTAs' shared memory
+    UNIT_TRACE(trace_op, 4);
   } else if (p.ksplit > 1) {
     // ---- k-segments of the group: the last unit sums the partials in k order
     if (act && own) {
