@@ -94,19 +94,25 @@ MS_API ms_status ms_q4_weight_destroy(ms_ctx *ctx, ms_q4_weight *w);
  * A, C: device pointers, row-major, 8-byte aligned. */
 MS_API ms_status ms_q4_gemm(ms_ctx *ctx, const ms_q4_weight *w, float *C, const float *A, int M,
                      int accumulate, void *stream);
-/* No counterpart in the reference.  The same projection as ms_q4_gemm (same
- * plan, same results) for callers that cannot have a call allocate device
- * memory or use the context's scratch (for example a host that reserved all
- * of HBM for its KV pages, or a path where an implicitly synchronising
- * allocation is not allowed).  It allocates nothing: its scratch is one fixed
- * device array of 1 MiB + 16 KiB inside the library (split-K partial sums and
- * arrival tickets).
- *   - Limit: the plan's partial sums and tickets must fit (262144 floats,
- *     4096 tickets), else MS_ERR_CAPACITY with both sizes in the message;
- *     e.g. every projection of the E4B model (K <= 10240) at M <= 4 fits.
+/* No counterpart in the reference.  The same projection as ms_q4_gemm
+ * (results within 2e-5 relative RMSE of it: rows above 8 run on the CUDA-core
+ * tiled kernel, not the tensor-core GEMM) for callers that cannot have a call
+ * allocate device memory or use the context's scratch (for example a host
+ * that reserved all of HBM for its KV pages, or a path where an implicitly
+ * synchronising allocation is not allowed).  It allocates nothing: its
+ * scratch is one fixed device array of 1 MiB + 16 KiB inside the library
+ * (split-K partial sums and arrival tickets).
+ *   - Limit: the partial sums and tickets of the k-split must fit (262144
+ *     floats, 4096 tickets); the call lowers the k-split until they do, down
+ *     to the kernel's smallest split (unsplit for rows above 8), and returns
+ *     MS_ERR_CAPACITY with both sizes in the message only if that does not
+ *     fit.  Only decode rows (M 5..8) of wide or long projections reach the
+ *     limit (e.g. M = 8, K = 13824, N = 5120); every projection of the E4B
+ *     and 14B-class models fits at M <= 4.
  *   - The first call on each device looks up the array's device address
  *     (cudaGetSymbolAddress, which may load the module): make that first
- *     call before any stream capture.
+ *     call before any stream capture.  First calls from several host
+ *     threads at once are safe.
  *   - The arrival tickets must be zero at launch; the call clears the ones
  *     it uses on `stream` before its kernel.
  *   - The scratch is shared by every call on the device: calls that overlap

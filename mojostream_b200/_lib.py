@@ -1,7 +1,7 @@
 """ctypes binding of libmojostream_cuda.so (C-ABI: include/mojostream_cuda.h).
 
 This is the binding a Python host uses; a Mojo host binds the same symbols
-with DLHandle (see INTEGRATION.md).  There is no fallback: if the library is
+with DLHandle.  There is no fallback: if the library is
 missing or does not export a declared symbol, loading fails loudly.
 """
 import ctypes

@@ -16,11 +16,13 @@
 #include <nccl.h>  // types only: the functions are resolved at ms_tp_init (nccl_api)
 
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <mutex>
 #include <set>
 #include <string>
 #include <utility>
@@ -56,7 +58,6 @@ struct ms_ctx {
   size_t lq_bytes = 0;
   float2* rowf = nullptr;
   size_t rowf_n = 0;
-  bool mk_ok = false;  // the persistent decode kernel can be co-resident on every SM
   // ms_sample: chunk partials and per-row arrival tickets (grown on demand)
   float2* samp_part = nullptr;
   size_t samp_part_n = 0;
@@ -119,17 +120,6 @@ struct ms_model {
     int4* d = nullptr;
   };
   std::vector<QBlocks> qblocks;
-  // op lists of the persistent decode kernel: the captured decode step's and
-  // the eager calls' (ms_forward / ms_layer_forward), kept apart so a graph
-  // never sees a list rewritten by a later call
-  struct MkBuf {
-    MkOp* ops = nullptr;
-    GemvParams* gp = nullptr;
-    AttnParams* ap = nullptr;
-    int* done = nullptr;  // [n_ops] counters + abort word
-    int n_ops = 0, mg = 0;
-  };
-  MkBuf mk_graph, mk_eager;
   int* d_seq = nullptr;
   int* d_pos = nullptr;
   int* d_ids = nullptr;
@@ -351,15 +341,6 @@ extern "C" ms_status ms_init(int device, ms_ctx** out) {
       prepare_gemm_tc() != cudaSuccess || prepare_attention_prefill() != cudaSuccess) {
     ms_destroy(c);
     return MS_ERR_CUDA;
-  }
-  {
-    int coop = 0;
-    cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, device);
-    // the persistent decode kernel is opt-in (MS_PERSISTENT_DECODE=1) until it
-    // is faster than the per-op kernels on every measured shape
-    const char* pe = getenv("MS_PERSISTENT_DECODE");
-    c->mk_ok = coop && pe && pe[0] == '1' && prepare_decode_step() == cudaSuccess;
-    cudaGetLastError();
   }
   if (cudaDeviceSynchronize() != cudaSuccess) {
     ms_destroy(c);
@@ -725,10 +706,12 @@ extern "C" ms_status ms_q4_gemm(ms_ctx* c, const ms_q4_weight* w, float* C, cons
 }
 
 // ------------------------------------------------ allocation-free variant --
-// ms_q4_gemm_noalloc runs the same projection as ms_q4_gemm (same plan, same
-// kernels, the same results), but its scratch (split-K partial sums and
-// arrival tickets) lives in one fixed file-scope device array instead of the
-// context's buffers.  Some callers cannot let a call allocate device memory
+// ms_q4_gemm_noalloc runs the same projection as ms_q4_gemm (results within
+// the projection tests' 2e-5 relative RMSE: rows above 8 take the CUDA-core
+// tiled kernel instead of the tensor-core GEMM, and the k-split is lowered
+// when the context's plan would not fit), but its scratch (split-K partial
+// sums and arrival tickets) lives in one fixed file-scope device array instead
+// of the context's buffers.  Some callers cannot let a call allocate device memory
 // or share the context's scratch: a serving host that reserved all of HBM for
 // KV pages up front, or code on a latency-critical path where an allocation
 // (implicitly synchronising) is not allowed.  This entry point allocates
@@ -744,8 +727,11 @@ constexpr int kNaMaxDevices = 64;
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNaBytes];
 
 // Device address of g_noalloc_scratch per device ordinal, resolved on the
-// first call made on that device (with the device current).
-static unsigned char* g_noalloc_addr[kNaMaxDevices] = {};
+// first call made on that device (with the device current).  Host threads
+// may make their first calls at the same time: the lookup runs under a mutex
+// and the address is published through an atomic.
+static std::atomic<unsigned char*> g_noalloc_addr[kNaMaxDevices];
+static std::mutex g_noalloc_mu;
 
 // Partial-sum floats and tickets a projection plan uses (0 without a k-split).
 static void plan_scratch(const GemvPlan& pl, int M, int n_tiles, size_t* floats,
@@ -764,6 +750,39 @@ static void plan_scratch(const GemvPlan& pl, int M, int n_tiles, size_t* floats,
   }
 }
 
+// The largest k-split that fits the static scratch, starting from the
+// context's plan and going down to the kernel's smallest split (the decode
+// kernel holds at most 40 / 20 k-chunks per segment in registers; the tiled
+// kernel runs any K unsplit, which needs no scratch).  False when even that
+// does not fit.
+static bool noalloc_fit(GemvPlan& pl, int M, int K, int n_tiles) {
+  const int chunks = K / kChunkK;
+  auto fits = [&](const GemvPlan& q) {
+    size_t f = 0, t = 0;
+    plan_scratch(q, M, n_tiles, &f, &t);
+    return f <= kNaPartFloats && t <= kNaCounters;
+  };
+  for (int ks = pl.ksplit; ks >= 1; --ks) {
+    GemvPlan q = pl;
+    if (q.dec) {
+      const int seg = (chunks + ks - 1) / ks;
+      if (seg > (q.mg == 1 ? 40 : 20)) break;
+      q.kseg = seg * kChunkK;
+      q.ksplit = (chunks + seg - 1) / seg;
+    } else {
+      const int rounds = (chunks + q.ch - 1) / q.ch;
+      const int per = (rounds + ks - 1) / ks;
+      q.kseg = per * q.ch * kChunkK;
+      q.ksplit = (K + q.kseg - 1) / q.kseg;
+    }
+    if (fits(q)) {
+      pl = q;
+      return true;
+    }
+  }
+  return false;
+}
+
 extern "C" ms_status ms_q4_gemm_noalloc(ms_ctx* c, const ms_q4_weight* w, float* C,
                                         const float* A, int M, int accumulate, void* stream) {
   if (!c || !w || !C || !A) return MS_ERR_INVALID_ARG;
@@ -775,23 +794,30 @@ extern "C" ms_status ms_q4_gemm_noalloc(ms_ctx* c, const ms_q4_weight* w, float*
   const int n_tiles = w->N / kTileN;
   // the plan ms_q4_gemm uses, minus the tensor-core path (whose limb
   // buffer grows with M x K): rows above 8 take the CUDA-core tiled kernel
-  const GemvPlan pl = plan_gemv(c, M, w->K, n_tiles, false);
+  GemvPlan pl = plan_gemv(c, M, w->K, n_tiles, false);
+  if (!noalloc_fit(pl, M, w->K, n_tiles)) {
+    size_t need_floats = 0, need_tickets = 0;
+    plan_scratch(pl, M, n_tiles, &need_floats, &need_tickets);
+    return fail(c, MS_ERR_CAPACITY,
+                "ms_q4_gemm_noalloc: M=%d K=%d N=%d needs %zu partial floats and %zu tickets "
+                "even at its smallest k-split; the static scratch holds %zu and %zu",
+                M, w->K, w->N, need_floats, need_tickets, kNaPartFloats, kNaCounters);
+  }
   size_t need_floats = 0, need_tickets = 0;
   plan_scratch(pl, M, n_tiles, &need_floats, &need_tickets);
-  if (need_floats > kNaPartFloats || need_tickets > kNaCounters)
-    return fail(c, MS_ERR_CAPACITY,
-                "ms_q4_gemm_noalloc: M=%d K=%d N=%d needs %zu partial floats and %zu tickets; "
-                "the static scratch holds %zu and %zu",
-                M, w->K, w->N, need_floats, need_tickets, kNaPartFloats, kNaCounters);
   MS_CUDA(c, cudaSetDevice(c->device));
-  unsigned char* base = g_noalloc_addr[c->device];
+  unsigned char* base = g_noalloc_addr[c->device].load(std::memory_order_acquire);
   if (!base) {
     // one-time set-up for this device: look up the array's device address
     // (may load the module, so the first call belongs before any capture)
-    void* ptr = nullptr;
-    MS_CUDA(c, cudaGetSymbolAddress(&ptr, g_noalloc_scratch));
-    base = static_cast<unsigned char*>(ptr);
-    g_noalloc_addr[c->device] = base;
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    base = g_noalloc_addr[c->device].load(std::memory_order_relaxed);
+    if (!base) {
+      void* ptr = nullptr;
+      MS_CUDA(c, cudaGetSymbolAddress(&ptr, g_noalloc_scratch));
+      base = static_cast<unsigned char*>(ptr);
+      g_noalloc_addr[c->device].store(base, std::memory_order_release);
+    }
   }
   GemvParams p = gemv_base(c, w->w, n_tiles, w->K, M, pl);
   p.part = reinterpret_cast<float*>(base);
@@ -1295,35 +1321,12 @@ static KvView kv_view(const ms_kv* kv, int layer) {
   return v;
 }
 
-// Op list of the persistent decode kernel, filled by run_layer instead of
-// launching the per-op kernels.
-struct MkCollect {
-  std::vector<MkOp> ops;
-  std::vector<GemvParams> gp;
-  std::vector<AttnParams> ap;
-};
-
-static ms_status emit_proj(ms_ctx* c, MkCollect* mk, const GemvParams& p, const GemvPlan& pl,
-                           cudaStream_t s, bool pdl) {
-  if (!mk) {
-    MS_CUDA(c, launch_proj(p, pl, s, pdl));
-    return MS_OK;
-  }
-  // the kernel's fragment region holds a k-segment of 2560 / mg values per row
-  if (!pl.dec || pl.kseg > 2560 / pl.mg)
-    return fail(c, MS_ERR_STATE, "persistent kernel: projection plan outside its limits");
-  const int groups = padded_tiles(p.n_tiles) / kGroupTiles;
-  mk->ops.push_back(MkOp{kMkProj, (int)mk->gp.size(), groups * pl.ksplit, groups, 0});
-  mk->gp.push_back(p);
-  return MS_OK;
-}
-
 // The five kernels of one layer.  x/xs: input rows and their stats (in
 // place: the layer output lands in x, its stats in xs); y/ys: the second
 // residual buffer.
 static ms_status run_layer(ms_ctx* c, ms_model* m, const ms_kv* kv, int li, int M, float* x,
                            float* xs, float* y, float* ys, cudaStream_t s, bool pdl,
-                           bool blocks_valid, MkCollect* mk = nullptr) {
+                           bool blocks_valid) {
   const LayerDev& L = m->layers[li];
   const int D = m->hidden, F = L.d.ffn_dim, nstat = D / kTileN;
   // 1. QKV + RoPE + KV write
@@ -1349,7 +1352,7 @@ static ms_status run_layer(ms_ctx* c, ms_model* m, const ms_kv* kv, int li, int 
     p.pos = m->d_pos;
     p.seq = m->d_seq;
     p.kv = kv_view(kv, li);
-    MS_TRY(emit_proj(c, mk, p, pl, s, pdl));
+    MS_CUDA(c, launch_proj(p, pl, s, pdl));
   }
   // 2. attention
   {
@@ -1378,14 +1381,13 @@ static ms_status run_layer(ms_ctx* c, ms_model* m, const ms_kv* kv, int li, int 
     // long spans: at most ~256 positions per split, so a large batch at long
     // context still has enough CTAs to keep every SM streaming
     splits = std::max(splits, (span + 255) / 256);
-    if (mk) splits = mk_attn_splits(c->sm_count, M, L.d.n_kv_heads);  // one unit per CTA
     splits = std::min(splits, std::max(1, (span + min_per - 1) / min_per));
     splits = std::min(splits, attention_max_splits());
     // merge inside a thread-block cluster when the splits fit one (up to 16;
     // a fill-rule count a little above that is trimmed to it), unless
     // MS_SPLITK_GLOBAL=1 asks for the global-memory merge
     const int max_cl = attention_max_cluster();
-    const bool try_cl = !mk && max_cl > 0 && !splitk_global_forced();
+    const bool try_cl = max_cl > 0 && !splitk_global_forced();
     if (try_cl && splits > max_cl && splits <= max_cl + max_cl / 2 &&
         (span + 255) / 256 <= max_cl)
       splits = max_cl;
@@ -1403,21 +1405,12 @@ static ms_status run_layer(ms_ctx* c, ms_model* m, const ms_kv* kv, int li, int 
     a.err = c->d_err;
     // prefill chunks (query blocks of 4+ rows on average) take the tiled
     // kernel; decode rows and scattered rows the flash-decode kernel
-    if (mk) {
-      const int variant = mk_attn_variant(L.d.head_dim, G);
-      if (variant < 0) return fail(c, MS_ERR_UNSUPPORTED, "persistent kernel: attention shape");
-      mk->ops.push_back(MkOp{kMkAttn, (int)mk->ap.size(), splits * L.d.n_kv_heads * M,
-                             L.d.n_kv_heads * M, variant});
-      mk->ap.push_back(a);
-    }
     const ms_model::QBlocks* qb = nullptr;
     const int bq = attention_prefill_tokens(L.d.head_dim, G);
     if (blocks_valid && M > 8 && bq > 0)
       for (const auto& q : m->qblocks)
         if (q.bq == bq && q.n > 0 && M >= 4 * q.n) qb = &q;
-    if (mk) {
-      // collected above
-    } else if (qb) {
+    if (qb) {
       a.blocks = qb->d;
       a.n_blocks = qb->n;
       MS_CUDA(c, launch_attention_prefill(a, s, pdl));
@@ -1458,7 +1451,7 @@ static ms_status run_layer(ms_ctx* c, ms_model* m, const ms_kv* kv, int li, int 
       p.epi = kEpiStore;
       p.out = m->P;
     }
-    MS_TRY(emit_proj(c, mk, p, pl, s, pdl));
+    MS_CUDA(c, launch_proj(p, pl, s, pdl));
     if (tp && !fused) {
       MS_NCCL(c, nccl_api().all_reduce(m->P, m->P, (size_t)M * D, ncclFloat, ncclSum, c->comm, s));
       MS_CUDA(c, launch_resid_add(y, ys, m->P, x, xs, L.d.ple, M, D, s));
@@ -1481,7 +1474,7 @@ static ms_status run_layer(ms_ctx* c, ms_model* m, const ms_kv* kv, int li, int 
     p.ldo = F;
     p.scale = L.d.scale[4];
     p.scale2 = L.d.scale[5];
-    MS_TRY(emit_proj(c, mk, p, pl, s, pdl));
+    MS_CUDA(c, launch_proj(p, pl, s, pdl));
   }
   // 5. Down + residual
   {
@@ -1512,59 +1505,12 @@ static ms_status run_layer(ms_ctx* c, ms_model* m, const ms_kv* kv, int li, int 
       p.epi = kEpiStore;
       p.out = m->P;
     }
-    MS_TRY(emit_proj(c, mk, p, pl, s, pdl));
+    MS_CUDA(c, launch_proj(p, pl, s, pdl));
     if (tp && !fused) {
       MS_NCCL(c, nccl_api().all_reduce(m->P, m->P, (size_t)M * D, ncclFloat, ncclSum, c->comm, s));
       MS_CUDA(c, launch_resid_add(x, xs, m->P, y, ys, 1.f, M, D, s));
     }
   }
-  return MS_OK;
-}
-
-// The persistent decode kernel serves M <= 8 rows when every layer's
-// attention shape is one it carries.
-static bool mk_usable(const ms_ctx* c, const ms_model* m, const ms_kv* kv, int M) {
-  // (its attention unit reads fp32 caches only)
-  if (!c->mk_ok || c->tp_world > 1 || M < 1 || M > 8 || kv->bf16) return false;
-  for (const LayerDev& L : m->layers)
-    if (mk_attn_variant(L.d.head_dim, L.d.n_heads / L.d.n_kv_heads) < 0) return false;
-  return true;
-}
-
-// Build the op list of layers [l0, l1) and upload it into b (stream-ordered;
-// never called while capturing: the pageable source needs a staged copy).
-static ms_status mk_build(ms_ctx* c, ms_model* m, const ms_kv* kv, int l0, int l1, int M,
-                          float* x, float* xs, float* y, float* ys, ms_model::MkBuf& b,
-                          cudaStream_t s) {
-  MkCollect mk;
-  for (int l = l0; l < l1; ++l) MS_TRY(run_layer(c, m, kv, l, M, x, xs, y, ys, s, false, false, &mk));
-  const int cap = 5 * m->n_layers;
-  if (!b.ops) {
-    MS_TRY(model_alloc(m, &b.ops, (size_t)cap));
-    MS_TRY(model_alloc(m, &b.gp, (size_t)4 * m->n_layers));
-    MS_TRY(model_alloc(m, &b.ap, (size_t)m->n_layers));
-    MS_TRY(model_alloc(m, &b.done, (size_t)cap + 1));
-  }
-  if ((int)mk.ops.size() > cap || mk.gp.size() > (size_t)4 * m->n_layers ||
-      mk.ap.size() > (size_t)m->n_layers)
-    return fail(c, MS_ERR_STATE, "persistent kernel: op list larger than its buffer");
-  MS_CUDA(c, cudaMemcpyAsync(b.ops, mk.ops.data(), mk.ops.size() * sizeof(MkOp),
-                             cudaMemcpyHostToDevice, s));
-  MS_CUDA(c, cudaMemcpyAsync(b.gp, mk.gp.data(), mk.gp.size() * sizeof(GemvParams),
-                             cudaMemcpyHostToDevice, s));
-  if (!mk.ap.empty())
-    MS_CUDA(c, cudaMemcpyAsync(b.ap, mk.ap.data(), mk.ap.size() * sizeof(AttnParams),
-                               cudaMemcpyHostToDevice, s));
-  b.n_ops = (int)mk.ops.size();
-  b.mg = M <= 4 ? 1 : 2;
-  return MS_OK;
-}
-
-// Zero the counters and launch the persistent kernel over b's op list.
-static ms_status mk_launch(ms_ctx* c, const ms_model::MkBuf& b, cudaStream_t s) {
-  MS_CUDA(c, cudaMemsetAsync(b.done, 0, (size_t)(b.n_ops + 1) * sizeof(int), s));
-  MkParams P{b.ops, b.n_ops, b.gp, b.ap, b.done, b.done + b.n_ops, c->d_err};
-  MS_CUDA(c, launch_decode_step(P, b.mg, c->sm_count, s));
   return MS_OK;
 }
 
@@ -1585,10 +1531,6 @@ extern "C" ms_status ms_layer_forward(ms_ctx* c, const ms_model* mc, int layer, 
   cudaStream_t s = pick(c, stream);
   MS_TRY(upload_rows(c, m, seq, pos, M, s));
   MS_CUDA(c, launch_rowstats(m->S[0], x, m->hidden, M, m->hidden, s, false));
-  if (mk_usable(c, m, kv, M)) {
-    MS_TRY(mk_build(c, m, kv, layer, layer + 1, M, x, m->S[0], m->X[1], m->S[1], m->mk_eager, s));
-    return mk_launch(c, m->mk_eager, s);
-  }
   return run_layer(c, m, kv, layer, M, x, m->S[0], m->X[1], m->S[1], s, true, true);
 }
 
@@ -1601,10 +1543,6 @@ extern "C" ms_status ms_forward(ms_ctx* c, const ms_model* mc, float* x, ms_kv* 
   cudaStream_t s = pick(c, stream);
   MS_TRY(upload_rows(c, m, seq, pos, M, s));
   MS_CUDA(c, launch_rowstats(m->S[0], x, m->hidden, M, m->hidden, s, false));
-  if (mk_usable(c, m, kv, M)) {
-    MS_TRY(mk_build(c, m, kv, 0, m->n_layers, M, x, m->S[0], m->X[1], m->S[1], m->mk_eager, s));
-    return mk_launch(c, m->mk_eager, s);
-  }
   for (int l = 0; l < m->n_layers; ++l)
     MS_TRY(run_layer(c, m, kv, l, M, x, m->S[0], m->X[1], m->S[1], s, true, true));
   return MS_OK;
@@ -1773,12 +1711,8 @@ extern "C" ms_status ms_lm_head(ms_ctx* c, const ms_model* mc, const float* x, i
 // One decode step on the device: d_ids / d_seq / d_pos -> d_next.
 static ms_status decode_body(ms_ctx* c, ms_model* m, const ms_kv* kv, int M, cudaStream_t s) {
   MS_TRY(embed_rows(c, m, m->X[0], M, s, true, kv));
-  if (mk_usable(c, m, kv, M)) {
-    MS_TRY(mk_launch(c, m->mk_graph, s));  // op list built before the capture
-  } else {
-    for (int l = 0; l < m->n_layers; ++l)
-      MS_TRY(run_layer(c, m, kv, l, M, m->X[0], m->S[0], m->X[1], m->S[1], s, true, false));
-  }
+  for (int l = 0; l < m->n_layers; ++l)
+    MS_TRY(run_layer(c, m, kv, l, M, m->X[0], m->S[0], m->X[1], m->S[1], s, true, false));
   if (m->sampling()) {
     MS_TRY(lm_head_launch(c, m, m->X[0], m->S[0], M, m->d_logits, nullptr, s, true));
     MS_TRY(sample_rows(c, m, kv, M, m->d_seq, m->d_pos, m->d_next, s));
@@ -1800,9 +1734,6 @@ static ms_status ensure_graph(ms_ctx* c, ms_model* m, const ms_kv* kv, int M) {
   if (m->sampling()) MS_TRY(ensure_sampler(c, m, M));
   cudaStream_t s = c->stream;
   cudaGraph_t g = nullptr;
-  if (mk_usable(c, m, kv, M))
-    MS_TRY(mk_build(c, m, kv, 0, m->n_layers, M, m->X[0], m->S[0], m->X[1], m->S[1],
-                    m->mk_graph, s));
   MS_CUDA(c, cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
   ms_status st = decode_body(c, m, kv, M, s);
   cudaError_t e = cudaStreamEndCapture(s, &g);

@@ -22,11 +22,14 @@
 // softmax, expf), and moves on.  At the end the warps are combined through
 // shared memory (log-sum-exp weights), and the row's splits are merged by the
 // last CTA of the (row, KV head) in split order: results do not depend on
-// timing.  (The persistent decode kernel keeps the chunked unit of
-// ms_attn_unit.cuh, whose shared memory fits next to its weight ring.)
-#include "ms_attn_unit.cuh"
+// timing.
+#include "ms_common.cuh"
+#include "ms_kernels.h"
 
 namespace ms {
+
+constexpr int kAttnMaxSplits = 64;
+constexpr int kAttnMergeBatch = 8;  // partial rows loaded per round of the merge
 
 // Most splits of one (row, KV head) that run as a cluster (a non-portable
 // size: B200 runs clusters of up to 16 CTAs), and whether every attention
@@ -81,12 +84,9 @@ __device__ __forceinline__ void ld_vec(float* dst, const unsigned char* src) {
   }
 }
 
-MS_STEP_TRACE_DEFINE(ms_trace_attn)
 
 template <int HD, int G, bool BF>
 __global__ void __launch_bounds__(WarpAttn<HD, G, BF>::NT) attn_kernel(const AttnParams p) {
-  ST_NOW(st0);
-  ST_INIT();
   using S = WarpAttn<HD, G, BF>;
   constexpr int NW = S::NW, NT = S::NT, P = S::P, PL = S::PL, VEC = S::VEC, ST = S::ST;
   constexpr int EB = S::EB;
@@ -98,7 +98,6 @@ __global__ void __launch_bounds__(WarpAttn<HD, G, BF>::NT) attn_kernel(const Att
   const int split = blockIdx.x, hk = blockIdx.y, m = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   pdl_wait();
-  ST_NOW(st1);
   pdl_trigger();
 
   const int pos = p.pos[m], seq = p.seq[m];
@@ -112,7 +111,6 @@ __global__ void __launch_bounds__(WarpAttn<HD, G, BF>::NT) attn_kernel(const Att
   const bool cl = p.cluster != 0;
   const bool active = split < ns;
   if (!active && !cl) {  // CTA-uniform
-    ST_PUT(p.kv.k, 1, st0, st1);
     return;
   }
   const int t_begin = lo + split * per;
@@ -154,7 +152,6 @@ __global__ void __launch_bounds__(WarpAttn<HD, G, BF>::NT) attn_kernel(const Att
   unsigned long long offs = row_offsets(0);  // positions 0..31 (P <= 32)
 #pragma unroll
   for (int i = 0; i < P; ++i) issue(i, __shfl_sync(0xffffffffu, offs, i));
-  ST_POINT(0);  // positions and row offsets read, first rows in flight
 
   // this lane's slices: dims (v * 32 + lane) * VEC + e
   float q[G][PL], acc[G][PL], mrun[G], lrun[G];
@@ -221,7 +218,6 @@ __global__ void __launch_bounds__(WarpAttn<HD, G, BF>::NT) attn_kernel(const Att
     }
   }
   cp_async_wait<0>();  // (only empty groups remain)
-  ST_POINT(1);          // this warp's positions done
   __syncthreads();     // every warp is past its ring: it becomes the combine buffer
 
   // ---- combine the warps: comb[w][h][0..HD) outputs, [HD] max, [HD+1] sum ----
@@ -283,7 +279,6 @@ __global__ void __launch_bounds__(WarpAttn<HD, G, BF>::NT) attn_kernel(const Att
     }
   }
 
-  ST_POINT(2);  // warps combined
   if (cl) {
     // ---- merge the splits inside the cluster: split sp's partial is in the
     //      shared memory of CTA sp; every CTA derives the split weights (the
@@ -291,7 +286,6 @@ __global__ void __launch_bounds__(WarpAttn<HD, G, BF>::NT) attn_kernel(const Att
     //      outputs in split order ---------------------------------------------
     cluster_arrive();
     cluster_wait();  // every split's partial is in place
-    ST_POINT(3);
     if (ns > 1) {
       const uint32_t cp0 = smem_u32(cpart);
       for (int h = warp; h < G; h += NW) {
@@ -335,14 +329,11 @@ __global__ void __launch_bounds__(WarpAttn<HD, G, BF>::NT) attn_kernel(const Att
         *reinterpret_cast<float4*>(p.out + (size_t)m * p.ldo + (hk * G + h) * HD + d4 * 4) = a;
       }
     }
-    ST_POINT(4);  // this CTA's share merged
     cluster_arrive();  // done reading the other CTAs' partials
     cluster_wait();    // ... and they are done reading this one's
-    ST_PUT(p.kv.k, 1, st0, st1);
     return;
   }
   if (ns == 1) {
-    ST_PUT(p.kv.k, 1, st0, st1);
     return;
   }
 
@@ -352,7 +343,6 @@ __global__ void __launch_bounds__(WarpAttn<HD, G, BF>::NT) attn_kernel(const Att
   if (tid == 0) s_last = (ticket_acq_rel(ctr) == ns - 1);
   __syncthreads();
   if (!s_last) {
-    ST_PUT(p.kv.k, 1, st0, st1);
     return;
   }
   for (int h = warp; h < G; h += NW) {
@@ -406,7 +396,6 @@ __global__ void __launch_bounds__(WarpAttn<HD, G, BF>::NT) attn_kernel(const Att
     *reinterpret_cast<float4*>(p.out + (size_t)m * p.ldo + (hk * G + h) * HD + d4 * 4) = a;
   }
   if (tid == 0) *ctr = 0;
-  ST_PUT(p.kv.k, 1, st0, st1);
 }
 
 template <int HD, int G, bool BF>

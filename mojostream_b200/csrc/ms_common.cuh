@@ -192,6 +192,11 @@ __device__ __forceinline__ float ld_dsmem(uint32_t addr) {
   asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
   return v;
 }
+__device__ __forceinline__ int ld_dsmem_s32(uint32_t addr) {
+  int v;
+  asm volatile("ld.shared::cluster.s32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
+  return v;
+}
 __device__ __forceinline__ float4 ld_dsmem4(uint32_t addr) {
   float4 v;
   asm volatile("ld.shared::cluster.v4.f32 {%0,%1,%2,%3}, [%4];"
@@ -253,97 +258,6 @@ __device__ __forceinline__ bool wait_counter_sys(const int* ctr, int target) {
   }
 }
 
-// ------------------------------------------------------ step timeline --
-// Profiling builds only (-DMS_STEP_TRACE; mojostream_b200.build --trace): the
-// one-launch decode projection and attention kernels record, per CTA, an op
-// key (a pointer that identifies the op within a step: the projection's
-// weights, the layer's K pool), the entry time, the time the dependency was
-// met, up to 8 points inside the kernel, the exit time and the SM.
-// MS_STEP_TRACE_DEFINE(fn) defines the buffer of a translation unit and an
-// exported `int fn(void* dst, size_t bytes, int reset)` that copies the
-// records out, returns their count and optionally restarts the buffer.
-// Without the define every hook below compiles to nothing.
-#ifdef MS_STEP_TRACE
-__device__ __forceinline__ unsigned long long trace_clock() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-struct StepTraceRec {
-  unsigned long long key, t0, t1, t2;  // op, entry, dependency met, exit
-  unsigned long long pts[8];           // points inside the kernel (0: not reached)
-  int cta, kind, smid, pad;            // linear CTA index, 0 projection / 1 attention, SM
-};
-constexpr unsigned int kStepTraceCap = 1u << 17;
-static __shared__ unsigned long long st_pts[8];
-#define MS_STEP_TRACE_DEFINE(FN)                                                           \
-  static __device__ StepTraceRec g_st_rec[kStepTraceCap];                                  \
-  static __device__ unsigned int g_st_n;                                                   \
-  __device__ __forceinline__ void st_put(unsigned long long key, int kind,                 \
-                                         unsigned long long t0, unsigned long long t1) {   \
-    const unsigned int i = atomicAdd(&g_st_n, 1u);                                         \
-    if (i >= kStepTraceCap) return;                                                        \
-    StepTraceRec r;                                                                        \
-    r.key = key;                                                                           \
-    r.t0 = t0;                                                                             \
-    r.t1 = t1;                                                                             \
-    r.t2 = trace_clock();                                                                  \
-    for (int k = 0; k < 8; ++k) r.pts[k] = st_pts[k];                                      \
-    r.cta = (int)(blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z));         \
-    r.kind = kind;                                                                         \
-    unsigned int sm;                                                                       \
-    asm volatile("mov.u32 %0, %%smid;" : "=r"(sm));                                        \
-    r.smid = (int)sm;                                                                      \
-    r.pad = 0;                                                                             \
-    g_st_rec[i] = r;                                                                       \
-  }                                                                                        \
-  extern "C" __attribute__((visibility("default"))) int FN(void* dst, size_t bytes,       \
-                                                          int reset) {                    \
-    unsigned int n = 0;                                                                    \
-    if (cudaMemcpyFromSymbol(&n, g_st_n, sizeof(n)) != cudaSuccess) return -1;             \
-    if (n > kStepTraceCap) n = kStepTraceCap;                                              \
-    size_t want = (size_t)n * sizeof(StepTraceRec);                                        \
-    if (want > bytes) want = bytes;                                                        \
-    if (dst && want && cudaMemcpyFromSymbol(dst, g_st_rec, want) != cudaSuccess) return -1; \
-    if (reset) {                                                                           \
-      const unsigned int z = 0;                                                            \
-      if (cudaMemcpyToSymbol(g_st_n, &z, sizeof(z)) != cudaSuccess) return -1;             \
-    }                                                                                      \
-    return (int)n;                                                                         \
-  }
-#define ST_NOW(v) const unsigned long long v = trace_clock()
-#define ST_INIT()                                      \
-  do {                                                 \
-    if (threadIdx.x == 0)                              \
-      for (int k_ = 0; k_ < 8; ++k_) st_pts[k_] = 0;   \
-  } while (0)
-#define ST_POINT(k)                                     \
-  do {                                                  \
-    if (threadIdx.x == 0) st_pts[(k)] = trace_clock();  \
-  } while (0)
-#define ST_SET(v) (v) = trace_clock()
-#define ST_PUT(key, kind, t0, t1)                                                      \
-  do {                                                                                 \
-    if (threadIdx.x == 0) st_put((unsigned long long)(key), (kind), (t0), (t1));       \
-  } while (0)
-#else
-#define MS_STEP_TRACE_DEFINE(FN)
-#define ST_NOW(v) \
-  do {            \
-  } while (0)
-#define ST_INIT() \
-  do {            \
-  } while (0)
-#define ST_POINT(k) \
-  do {              \
-  } while (0)
-#define ST_SET(v) \
-  do {            \
-  } while (0)
-#define ST_PUT(key, kind, t0, t1) \
-  do {                            \
-  } while (0)
-#endif
 
 // Error bits a kernel can leave for the host (ms_sync reports them).
 constexpr int kErrWaitTimeout = 1;

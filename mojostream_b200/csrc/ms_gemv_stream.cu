@@ -15,12 +15,9 @@ size_t gemv_stream_smem(int mg, int kseg) {
   return (size_t)kStages * kStageBytes + proj_scratch_bytes(mg, kseg);
 }
 
-MS_STEP_TRACE_DEFINE(ms_trace_gemv_stream)
 
 template <int MG>
 __global__ void __launch_bounds__(kSThreads, 2) gemv_stream_kernel(const GemvParams p) {
-  ST_NOW(st0);
-  ST_INIT();
   extern __shared__ __align__(128) uint8_t dsm[];
   __shared__ __align__(8) uint64_t full[kStages], empty[kStages];
   __shared__ ProjShared sh;
@@ -57,9 +54,7 @@ __global__ void __launch_bounds__(kSThreads, 2) gemv_stream_kernel(const GemvPar
     return;
   }
   pdl_wait();
-  ST_NOW(st1);
   proj_consume<MG>(p, blockIdx.x, blockIdx.y, ring, seq, sB, sh, nullptr);
-  ST_PUT(p.w, 0, st0, st1);
 }
 
 // The k-segments of a tile group run as one thread-block cluster (2..8 CTAs)

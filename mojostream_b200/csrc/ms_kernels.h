@@ -97,7 +97,7 @@ struct GemvParams {
   int* counters;          // arrival tickets (reset by the last arrival)
   // decode kernel: the ksplit CTAs of a tile group run as one thread-block
   // cluster and sum their partials through distributed shared memory (part /
-  // counters unused); set by the launcher, 0 in the persistent kernel
+  // counters unused); set by the launcher
   int cluster;
   int* err;               // error bits for the host (bounded waits)
   // tensor-core path: activation limbs and per-row factors (quant_rows_kernel)
@@ -150,24 +150,6 @@ struct LmHeadParams {
   float* maxval;          // [M] the maximum itself (tensor-parallel combine), or null
 };
 
-// Persistent decode-step kernel: the op list of a layer range.
-enum MkKind : int { kMkProj = 0, kMkAttn = 1 };
-struct MkOp {
-  int kind;     // kMkProj / kMkAttn
-  int index;    // into MkParams::gp / ::ap
-  int n_units;  // projection: groups x ksplit; attention: n_splits x n_kv x M
-  int target;   // completions that publish the op (groups / M x n_kv)
-  int variant;  // attention shape id (mk_attn_variant)
-};
-struct MkParams {
-  const MkOp* ops;
-  int n_ops;
-  const GemvParams* gp;
-  const AttnParams* ap;
-  int* done;   // [n_ops] completion counters, zero at launch
-  int* abort;  // zero at launch
-  int* err;
-};
 
 // Launchers (return cudaGetLastError of the launch).
 cudaError_t launch_gemv(const GemvParams& p, int mg, int ch, cudaStream_t s, bool pdl);
@@ -189,10 +171,6 @@ cudaError_t prepare_gemv_stream();
 cudaError_t prepare_attention();
 cudaError_t prepare_gemm_tc();
 cudaError_t prepare_attention_prefill();
-cudaError_t launch_decode_step(const MkParams& p, int mg, int n_cta, cudaStream_t s);
-cudaError_t prepare_decode_step();
-int mk_attn_variant(int hd, int g);       // -1: shape not carried by the persistent kernel
-int mk_attn_splits(int n_cta, int M, int n_kv);
 cudaError_t launch_lm_head(const LmHeadParams& p, cudaStream_t s, bool pdl);
 cudaError_t launch_repack(uint4* out, const uint8_t* const* src, const int* src_n, int n_src,
                           const int* perm, int n_tiles, int K, cudaStream_t s);

@@ -1,7 +1,6 @@
 // ms_proj_unit.cuh -- one unit of the decode Q4 projection (M <= 8 rows): a
-// tile group (8 x 16 output columns) over one k-segment.  Shared by the
-// one-launch-per-projection kernel (ms_gemv_stream.cu) and the persistent
-// decode-step kernel (ms_decode_mk.cu).
+// tile group (8 x 16 output columns) over one k-segment, run by the
+// one-launch-per-projection kernel of ms_gemv_stream.cu.
 //
 // Reference: matmul_q4_bpack_raw (src/linalg/kernels.mojo:201-267) with the
 // steps fused around its call sites (src/main.mojo:538-613,
@@ -26,10 +25,9 @@
 // stages = 4 k-chunks x 8 tiles) through an mbarrier ring; 16 consumer warps,
 // two per tile, each take two chunks of every stage.  Split-K partials of a
 // group are summed in k order, either inside a thread-block cluster of the
-// group's k-segments (distributed shared memory, no global round trip; the
-// one-launch kernel) or by the last unit through global memory and an
-// arrival ticket (the persistent kernel, and splits above 8): results do not
-// depend on timing.  Activations written earlier in the same launch are read through L2
+// group's k-segments (distributed shared memory, no global round trip) or by
+// the last unit through global memory and an arrival ticket (splits above 8):
+// results do not depend on timing.  Activations are read through L2
 // (ld.global.cg), never through the non-coherent L1 / texture path.
 #pragma once
 
@@ -53,26 +51,6 @@ constexpr int kMaxItems = 5;
 constexpr int kConsumerBar = 1;  // named barrier of the 512 consumer threads
 // Most k-segments of one tile group that run as a cluster (portable size).
 constexpr int kMaxClusterK = 8;
-
-// Timeline points inside a unit (profiling builds with -DMS_MK_TRACE only):
-// [cta][op][point], thread 0 of the CTA, first unit of the op.
-#ifdef MS_MK_TRACE
-static __device__ unsigned long long g_unit_trace[256 * 256 * 8];  // per translation unit
-#define UNIT_TRACE(op, k)                                                        \
-  do {                                                                           \
-    if (threadIdx.x == 0 && (op) >= 0 && (op) < 256 && blockIdx.x < 256) {      \
-      unsigned long long t_;                                                     \
-      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                     \
-      unsigned long long* e_ = &g_unit_trace[((size_t)blockIdx.x * 256 + (op)) * 8 + (k)]; \
-      *e_ = t_;                                                                  \
-    }                                                                            \
-  } while (0)
-#else
-// the one-launch kernel's timeline (MS_STEP_TRACE builds; nothing otherwise):
-// 6 inputs loaded, 1 quantised, 2 main loop done, 3 halves merged, 4 split-K
-// merged, 5 epilogue done
-#define UNIT_TRACE(op, k) ST_POINT(k)
-#endif
 
 // B fragments of one k-segment: per k32 block, 2*MG MMA column blocks x 32
 // lanes x 8 bytes = 512*MG bytes (1 KB per 64-k chunk at MG 1).
@@ -194,14 +172,10 @@ enum ProjResult : int {
 // has made the inputs visible (griddepcontrol.wait / a completed dependency).
 // Every consumer thread reaches every barrier; the result is CTA-uniform.
 // sB: the B-fragment / merge buffer (proj_scratch_bytes(MG, p.kseg) bytes).
-// PRE: load the epilogue's inputs before the main loop and batch the split-K
-// merge loads (latency-bound persistent kernel, 96 registers); without it the
-// unit keeps the small register footprint of the one-launch kernel (2 CTAs
-// per SM at 56 registers).
-template <int MG, bool PRE = false>
+template <int MG>
 __device__ int proj_consume(const GemvParams& p, int group, int kidx, const StageRing& r,
                             uint32_t& seq, uint2* sB, ProjShared& sh,
-                            const volatile int* abort, int trace_op = -1) {
+                            const volatile int* abort) {
   constexpr int MB = 4 * MG;  // rows of the m-block
   constexpr int NJ = 2 * MG;  // MMA column blocks: 2 rows x 4 limbs each
   const int tid = threadIdx.x;
@@ -220,7 +194,6 @@ __device__ int proj_consume(const GemvParams& p, int group, int kidx, const Stag
   // the previous unit's readers of sh / sB are done before anything is reused
   bar_sync_n(kConsumerBar, kSConsumers);
   if (tid == 0) sh.bad = 0;
-  UNIT_TRACE(trace_op, 0);
 
   // ---- B fragments, one pass: thread tid owns row tid / kRowThreads and
   //      items (kb, h, t) = 4 values k {2t, 2t+1, 2t+8, 2t+9} of subtile
@@ -243,19 +216,8 @@ __device__ int proj_consume(const GemvParams& p, int group, int kidx, const Stag
       }
     }
   }
-  // epilogue inputs that do not depend on the sums (residual, RoPE, KV row),
-  // loaded now so their latency overlaps the main loop
   const bool act = half == 0;      // half 0 finishes the tile
   const bool own = (t & 1) == 0;   // lanes that carry the values on
-  EpiPrefetch pre[PRE ? NJ : 1];
-  if constexpr (PRE) {
-#pragma unroll
-    for (int jn = 0; jn < NJ; ++jn) {
-      const int m = 2 * jn + (t >> 1);
-      pre[jn].dst = nullptr;
-      if (act && own && m < p.M && tile < p.n_tiles) epilogue_prefetch(p, tile, g, m, pre[jn]);
-    }
-  }
   // per-row factors of the epilogue (warps < MB), while the loads fly
   if (warp < MB) {
     const int m = warp;
@@ -284,9 +246,7 @@ __device__ int proj_consume(const GemvParams& p, int group, int kidx, const Stag
     amax = warp_max(amax);
     if (lane == 0) sh.pmax[warp] = amax;
   }
-  UNIT_TRACE(trace_op, 6);
   bar_sync_n(kConsumerBar, kSConsumers);
-  UNIT_TRACE(trace_op, 7);
   {
     const int rr = xr_row;
     float a = 0.f;
@@ -330,7 +290,6 @@ __device__ int proj_consume(const GemvParams& p, int group, int kidx, const Stag
     if (lane == 0) sh.wq[warp] = qs;
   }
   bar_sync_n(kConsumerBar, kSConsumers);
-  UNIT_TRACE(trace_op, 1);
 
   // ---- main loop: 2 k32 blocks per chunk, 2 accumulator chains --------------
   int acc[2][NJ][4];
@@ -406,7 +365,6 @@ __device__ int proj_consume(const GemvParams& p, int group, int kidx, const Stag
     rv[jn][0] = (float)(vg - corr) * dq;
     rv[jn][1] = (float)(vh - corr) * dq;
   }
-  UNIT_TRACE(trace_op, 2);
 
   // ---- merge the two halves of each tile (half 0 + half 1, fixed order) ------
   float* red = reinterpret_cast<float*>(sB);  // the fragments are consumed
@@ -424,7 +382,6 @@ __device__ int proj_consume(const GemvParams& p, int group, int kidx, const Stag
   const bool cl = p.cluster && p.ksplit > 1;
   const bool bad = sh.bad != 0;  // CTA-uniform after the barrier
   if (bad && !cl) return kProjFailed;
-  UNIT_TRACE(trace_op, 3);
   if (act && own) {
 #pragma unroll
     for (int jn = 0; jn < NJ; ++jn) {
@@ -447,8 +404,18 @@ __device__ int proj_consume(const GemvParams& p, int group, int kidx, const Stag
       }
     }
     cluster_arrive();
-    cluster_wait();  // every CTA's partials are in its shared memory
+    cluster_wait();  // every CTA's partials and bad flag are in its shared memory
     finish = !bad && (tl % p.ksplit) == kidx;  // warp-uniform
+    if (finish) {
+      // a CTA whose weight stream gave up left unfinished partials: no CTA
+      // of the cluster writes tiles from them (every lane reads the same flags)
+      const uint32_t bad0 = smem_u32(&sh.bad);
+      int any = 0;
+#pragma unroll
+      for (int r0 = 0; r0 < kMaxClusterK; ++r0)
+        if (r0 < p.ksplit) any |= ld_dsmem_s32(dsmem_addr(bad0, (uint32_t)r0));
+      finish = any == 0;
+    }
     if (act && own && finish) {
       // the loads of kB CTAs' partials are in flight at once
       constexpr int kB = kMaxClusterK / MG;
@@ -482,7 +449,6 @@ __device__ int proj_consume(const GemvParams& p, int group, int kidx, const Stag
       }
     }
     cluster_arrive();  // done reading the other CTAs' shared memory
-    UNIT_TRACE(trace_op, 4);
   } else if (p.ksplit > 1) {
     // ---- k-segments of the group: the last unit sums the partials in k order
     if (act && own) {
@@ -497,11 +463,10 @@ __device__ int proj_consume(const GemvParams& p, int group, int kidx, const Stag
     bar_sync_n(kConsumerBar, kSConsumers);  // partials written
     if (tid == 0) sh.last = (ticket_acq_rel(p.counters + group) == p.ksplit - 1);
     bar_sync_n(kConsumerBar, kSConsumers);
-    UNIT_TRACE(trace_op, 4);
     if (!sh.last) return kProjPartial;  // CTA-uniform
     if (act && own) {
       // sum in k order; the loads of kB segments are in flight at once
-      constexpr int kB = PRE ? 8 / MG : 2;
+      constexpr int kB = 2;
 #pragma unroll
       for (int jn = 0; jn < NJ; ++jn) rv[jn][0] = rv[jn][1] = 0.f;
       for (int k0 = 0; k0 < p.ksplit; k0 += kB) {
@@ -537,10 +502,7 @@ __device__ int proj_consume(const GemvParams& p, int group, int kidx, const Stag
       float sq = 0.f;
       if (own && m < p.M) {
         const float f = sh.fin[m];
-        if constexpr (PRE)
-          epilogue_row_pre(p, tile, g, m, rv[jn][0] * f, rv[jn][1] * f, sh.fres[m], pre[jn], sq);
-        else
-          epilogue_row(p, tile, g, m, rv[jn][0] * f, rv[jn][1] * f, sh.fres[m], sq);
+        epilogue_row(p, tile, g, m, rv[jn][0] * f, rv[jn][1] * f, sh.fres[m], sq);
       }
       if (p.epi == kEpiResid && p.out_stats) {
         // sum over the 8 lane groups g (rows g and g+8 of the tile)
@@ -551,7 +513,6 @@ __device__ int proj_consume(const GemvParams& p, int group, int kidx, const Stag
       }
     }
   }
-  UNIT_TRACE(trace_op, 5);
   if (cl) {
     cluster_wait();  // the other CTAs are done reading this CTA's partials
     return bad ? kProjFailed : kProjFinished;
