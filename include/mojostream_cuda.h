@@ -235,6 +235,21 @@ enum { MS_KV_F32 = 0, MS_KV_BF16 = 1 };
 MS_API ms_status ms_kv_create_typed(ms_ctx *ctx, const ms_model *model, int n_seq, int max_pos,
                                     int slide_cap, int dtype, ms_kv **out);
 MS_API ms_status ms_kv_destroy(ms_ctx *ctx, ms_kv *kv);
+/* K / V rows of positions pos0 .. pos0 + n - 1 of sequence seq in layer
+ * `layer`, to or from dense fp32 device buffers k, v [n][kv_dim] (the
+ * layer's n_kv_heads * head_dim).  write_kv_sliding / write_kv_full
+ * (src/inference/gemma4_e4b.mojo:211-249) for n rows at once: full layers
+ * hold position p at row p; sliding layers at slot p % slide_cap, so n <=
+ * slide_cap, and a read of position p returns what the last write of a
+ * position congruent to p mod slide_cap left there.  A bf16 cache rounds on
+ * write as the forward pass does.  For importing or exporting a sequence's
+ * cache (a shared prompt prefix copied into another slot, a sequence moved
+ * between contexts); the token history is not touched.  Asynchronous on
+ * `stream`; MS_ERR_CAPACITY for positions outside the cache. */
+MS_API ms_status ms_kv_write(ms_ctx *ctx, ms_kv *kv, int layer, int seq, int pos0, int n,
+                             const float *k, const float *v, void *stream);
+MS_API ms_status ms_kv_read(ms_ctx *ctx, const ms_kv *kv, int layer, int seq, int pos0, int n,
+                            float *k, float *v, void *stream);
 MS_API ms_status ms_kv_reset(ms_ctx *ctx, ms_kv *kv);
 MS_API size_t ms_kv_bytes(const ms_kv *kv);
 

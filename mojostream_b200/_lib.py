@@ -91,6 +91,10 @@ SIGNATURES = {
     "ms_kv_destroy": (ctypes.c_int, [_vp, _vp]),
     "ms_kv_reset": (ctypes.c_int, [_vp, _vp]),
     "ms_kv_bytes": (ctypes.c_size_t, [_vp]),
+    "ms_kv_write": (ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                   ctypes.c_int, _vp, _vp, _vp]),
+    "ms_kv_read": (ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                  ctypes.c_int, _vp, _vp, _vp]),
     "ms_layer_forward": (ctypes.c_int, [_vp, _vp, ctypes.c_int, _vp, _vp, _ip, _ip,
                                         ctypes.c_int, _vp]),
     "ms_forward": (ctypes.c_int, [_vp, _vp, _vp, _vp, _ip, _ip, ctypes.c_int, _vp]),

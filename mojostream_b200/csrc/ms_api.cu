@@ -1247,6 +1247,46 @@ extern "C" ms_status ms_kv_reset(ms_ctx* c, ms_kv* kv) {
 
 extern "C" size_t ms_kv_bytes(const ms_kv* kv) { return kv ? kv->bytes : 0; }
 
+static KvView kv_view(const ms_kv* kv, int layer);
+
+// Shared checks of ms_kv_write / ms_kv_read.
+static ms_status kv_rows_check(ms_ctx* c, const ms_kv* kv, int layer, int seq, int pos0, int n,
+                               const void* k, const void* v, const char* what) {
+  if (layer < 0 || layer >= (int)kv->k.size())
+    return fail(c, MS_ERR_INVALID_ARG, "%s: layer %d", what, layer);
+  if (seq < 0 || seq >= kv->n_seq)
+    return fail(c, MS_ERR_INVALID_ARG, "%s: sequence %d outside 0..%d", what, seq, kv->n_seq - 1);
+  if (n <= 0 || pos0 < 0 || (long)pos0 + n > kv->max_pos)
+    return fail(c, MS_ERR_CAPACITY, "%s: positions %d..%ld outside the cache (max_pos %d)", what,
+                pos0, (long)pos0 + n - 1, kv->max_pos);
+  if (kv->model->layers[layer].d.window > 0 && n > kv->slide_cap)
+    return fail(c, MS_ERR_CAPACITY, "%s: %d positions exceed the sliding ring (%d slots)", what,
+                n, kv->slide_cap);
+  if (!k || !v) return fail(c, MS_ERR_INVALID_ARG, "%s: null buffer", what);
+  if (((uintptr_t)k & 3) || ((uintptr_t)v & 3))
+    return fail(c, MS_ERR_ALIGN, "%s: buffers must be 4-byte aligned", what);
+  if (!is_device_ptr(k) || !is_device_ptr(v))
+    return fail(c, MS_ERR_INVALID_ARG, "%s: k / v must be device pointers", what);
+  return MS_OK;
+}
+
+extern "C" ms_status ms_kv_write(ms_ctx* c, ms_kv* kv, int layer, int seq, int pos0, int n,
+                                 const float* k, const float* v, void* stream) {
+  if (!c || !kv) return MS_ERR_INVALID_ARG;
+  MS_TRY(kv_rows_check(c, kv, layer, seq, pos0, n, k, v, "ms_kv_write"));
+  MS_CUDA(c, launch_kv_copy(kv_view(kv, layer), seq, pos0, n, const_cast<float*>(k),
+                            const_cast<float*>(v), 0, pick(c, stream)));
+  return MS_OK;
+}
+
+extern "C" ms_status ms_kv_read(ms_ctx* c, const ms_kv* kv, int layer, int seq, int pos0, int n,
+                                float* k, float* v, void* stream) {
+  if (!c || !kv) return MS_ERR_INVALID_ARG;
+  MS_TRY(kv_rows_check(c, kv, layer, seq, pos0, n, k, v, "ms_kv_read"));
+  MS_CUDA(c, launch_kv_copy(kv_view(kv, layer), seq, pos0, n, k, v, 1, pick(c, stream)));
+  return MS_OK;
+}
+
 // ----------------------------------------------------------------- forward --
 
 // Host-side validation of one call's rows against the cache.

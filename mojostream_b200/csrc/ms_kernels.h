@@ -207,6 +207,10 @@ cudaError_t launch_resid_add(float* out, float* out_stats, const float* partial,
 cudaError_t launch_argmax_pack(unsigned long long* key, const float* val, const int* idx, int M,
                                int v0, cudaStream_t s);
 cudaError_t launch_argmax_unpack(int* ids, const unsigned long long* key, int M, cudaStream_t s);
+// K / V rows of positions pos0 .. pos0 + n - 1 of one sequence to (dir 0) or
+// from (dir 1) dense fp32 device buffers [n][kv_dim].
+cudaError_t launch_kv_copy(const KvView& kv, int seq, int pos0, int n, float* k, float* v,
+                           int dir, cudaStream_t s);
 cudaError_t launch_rowstats(float* stats, const float* x, int ldx, int M, int D,
                             cudaStream_t s, bool pdl);
 cudaError_t launch_advance_step(int* ids, const int* next, int* pos, int* hist, int* step, int M,

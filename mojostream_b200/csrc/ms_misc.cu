@@ -470,6 +470,37 @@ cudaError_t launch_argmax_unpack(int* ids, const unsigned long long* key, int M,
   return cudaGetLastError();
 }
 
+// K / V rows of positions pos0 .. pos0 + n - 1 of sequence seq between a
+// layer's paged pool and dense fp32 buffers [n][kv_dim]: dir 0 writes the
+// cache (rounding to bfloat16 for a bf16 cache, as the QKV epilogue does),
+// dir 1 reads it (widened to fp32).  One CTA per position.
+__global__ void kv_copy_kernel(KvView kv, int seq, int pos0, float* k, float* v, int dir) {
+  const size_t off = kv_row_offset(kv.block_table, kv.bt_stride, kv.page, kv.cap, kv.circular,
+                                   seq, pos0 + (int)blockIdx.x, kv.kv_dim);
+  float* kr = k + (size_t)blockIdx.x * kv.kv_dim;
+  float* vr = v + (size_t)blockIdx.x * kv.kv_dim;
+  for (int i = threadIdx.x; i < kv.kv_dim; i += blockDim.x) {
+    if (dir == 0) {
+      kv_put(kv.k, kv.bf16, off + i, kr[i]);
+      kv_put(kv.v, kv.bf16, off + i, vr[i]);
+    } else if (kv.bf16) {
+      const unsigned short* kb = reinterpret_cast<const unsigned short*>(kv.k);
+      const unsigned short* vb = reinterpret_cast<const unsigned short*>(kv.v);
+      kr[i] = __uint_as_float((uint32_t)kb[off + i] << 16);
+      vr[i] = __uint_as_float((uint32_t)vb[off + i] << 16);
+    } else {
+      kr[i] = kv.k[off + i];
+      vr[i] = kv.v[off + i];
+    }
+  }
+}
+
+cudaError_t launch_kv_copy(const KvView& kv, int seq, int pos0, int n, float* k, float* v,
+                           int dir, cudaStream_t s) {
+  kv_copy_kernel<<<n, 256, 0, s>>>(kv, seq, pos0, k, v, dir);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_advance_step(int* ids, const int* next, int* pos, int* hist, int* step, int M,
                                 cudaStream_t s, bool pdl) {
   cudaLaunchConfig_t cfg = {};

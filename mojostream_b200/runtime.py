@@ -290,6 +290,22 @@ class KVCache:
     def reset(self):
         self.ctx.check(lib().ms_kv_reset(self.ctx.h, self.h))
 
+    def write(self, layer, seq, pos0, k, v):
+        """ms_kv_write: rows k, v (fp32 device tensors [n][kv_dim]) become the
+        cached K / V of positions pos0 .. pos0 + n - 1 of sequence seq."""
+        self.ctx.check(lib().ms_kv_write(self.ctx.h, self.h, layer, seq, pos0, k.shape[0],
+                                         _ptr(k), _ptr(v), _stream()))
+
+    def read(self, layer, seq, pos0, n, kv_dim):
+        """ms_kv_read: the cached K / V rows of positions pos0 .. pos0 + n - 1
+        as two fp32 device tensors [n][kv_dim]."""
+        import torch
+        k = torch.empty((n, kv_dim), dtype=torch.float32, device="cuda")
+        v = torch.empty((n, kv_dim), dtype=torch.float32, device="cuda")
+        self.ctx.check(lib().ms_kv_read(self.ctx.h, self.h, layer, seq, pos0, n, _ptr(k),
+                                        _ptr(v), _stream()))
+        return k, v
+
     def close(self):
         if self.h:
             lib().ms_kv_destroy(self.ctx.h, self.h)

@@ -167,6 +167,8 @@ def run_teacher_forced(ctx, torch, oracle_lib, spec, weights, n_seq, max_pos, ca
     rng = np.random.default_rng(11)
     prng = np.random.default_rng(12)
     worst = 0.0
+    widened = []  # (layer, error, effective bound) where the bound exceeds tol
+    max_err = 0.0
     for seq, pos in calls:
         x = (rng.standard_normal((len(seq), spec.hidden)) * 2.0).astype(np.float32)
         for l in range(spec.n_layers):
@@ -179,8 +181,15 @@ def run_teacher_forced(ctx, torch, oracle_lib, spec, weights, n_seq, max_pos, ca
             err = rel_rmse(xg.cpu().numpy(), y_ref)
             bound = max(tol, 2.0 * rel_rmse(y_p, y_ref))
             worst = max(worst, err / bound)
+            max_err = max(max_err, err)
+            if bound > tol:
+                widened.append((l, err, bound))
             assert err < bound, (l, seq, pos, err, bound)
             x = y_ref
+    over = [w for w in widened if w[1] >= tol]
+    print(f"teacher-forced: max rel-RMSE {max_err:.3g}; bound widened past {tol:g} on "
+          f"{len(widened)} layer calls (max {max((b for _, _, b in widened), default=tol):.3g}), "
+          f"{len(over)} of them with an error above {tol:g}: {over[:8]}")
     return worst
 
 
