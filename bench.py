@@ -71,6 +71,11 @@ def parse():
                     help="repetition penalty (the reference's e4b loop uses 1.2)")
     ap.add_argument("--kv", default="f32", choices=["f32", "bf16"],
                     help="KV cache element type (f32: the parity mode; bf16: half the bytes)")
+    ap.add_argument("--kv-fill", default="prefill", choices=["prefill", "seeded"],
+                    help="prefill: the prompts run through ms_prefill (TTFT measured); seeded: "
+                         "the cache below the prompt length is filled with seeded K / V values "
+                         "(ms_kv_write) and no TTFT is measured -- decode-step profiling without "
+                         "a long prefill")
     ap.add_argument("--m", type=int, default=None)
     ap.add_argument("--k", type=int, default=2560)
     ap.add_argument("--n", type=int, default=20480)
@@ -199,23 +204,46 @@ def events():
     return torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
 
 
-def decode_loop(model, kv, B, P, args, D, lib_stream, clocks_gpu=None):
+def seeded_fill(model, kv, B, P, slide_cap):
+    """Seeded K / V values at positions below P of every sequence and layer
+    (ms_kv_write; sliding layers: the slots the ring holds), in place of a
+    prefill; returns seeded first ids."""
+    import torch
+    g = torch.Generator(device="cuda").manual_seed(11)
+    for l, ls in enumerate(model.spec.layers):
+        lo = max(0, P - slide_cap) if ls.window > 0 else 0
+        for s in range(B):
+            k = torch.randn((P - lo, ls.kv_dim), device="cuda", generator=g)
+            v = torch.randn((P - lo, ls.kv_dim), device="cuda", generator=g)
+            kv.write(l, s, lo, k, v)
+    torch.cuda.synchronize()
+    return [int(t) for t in np.random.default_rng(12).integers(0, model.spec.vocab, size=B)]
+
+
+def decode_loop(model, kv, B, P, args, D, lib_stream, clocks_gpu=None, slide_cap=0):
     """TTFT (B x P prefill + first token), then warm-up and the timed
     device-resident loop (ms_generate), then the same through ms_decode_step
-    with host buffers.  Returns a dict of device times (max over ranks)."""
-    ids = sum(prompts(B, P, model.spec.vocab), [])
-    seq = sum([[s] * P for s in range(B)], [])
-    pos = sum([list(range(P)) for _ in range(B)], [])
-    n_warm = min(len(ids), MAX_ROWS)
-    model.prefill(kv, ids[:n_warm], seq[:n_warm], pos[:n_warm])  # kernel attributes, buffers
-    kv.reset()
-    D.barrier()
+    with host buffers.  Returns a dict of device times (max over ranks).
+    With args.kv_fill == "seeded" the cache is filled with seeded values
+    instead of the prefill (ttft_ms is then None)."""
+    if getattr(args, "kv_fill", "prefill") == "seeded":
+        first = seeded_fill(model, kv, B, P, slide_cap)
+        ttft_ms = None
+    else:
+        ids = sum(prompts(B, P, model.spec.vocab), [])
+        seq = sum([[s] * P for s in range(B)], [])
+        pos = sum([list(range(P)) for _ in range(B)], [])
+        n_warm = min(len(ids), MAX_ROWS)
+        model.prefill(kv, ids[:n_warm], seq[:n_warm], pos[:n_warm])  # kernel attributes, buffers
+        kv.reset()
+        D.barrier()
+        e0, e1 = events()
+        e0.record(lib_stream)
+        first = model.prefill(kv, ids, seq, pos)
+        e1.record(lib_stream)
+        e1.synchronize()
+        ttft_ms = D.max(e0.elapsed_time(e1))
     e0, e1 = events()
-    e0.record(lib_stream)
-    first = model.prefill(kv, ids, seq, pos)
-    e1.record(lib_stream)
-    e1.synchronize()
-    ttft_ms = D.max(e0.elapsed_time(e1))
     seqs = list(range(B))
     gen = model.generate(kv, first, seqs, [P] * B, args.warmup)
     cur = [int(t) for t in gen[-1]]
@@ -265,10 +293,11 @@ def run_ours(args, ws, rank, local):
     max_pos = ((PROMPT + args.warmup + 2 * args.steps + 8 + 63) // 64) * 64
     # sliding ring: the window plus the rows of one sequence in one prefill call
     window = max(l.window for l in spec.layers)
-    kv = KVCache(ctx, model, BATCH, max_pos, slide_cap=window + min(PROMPT, MAX_ROWS),
-                 dtype=args.kv)
+    slide_cap = window + min(PROMPT, MAX_ROWS)
+    kv = KVCache(ctx, model, BATCH, max_pos, slide_cap=slide_cap, dtype=args.kv)
     lib_stream = torch.cuda.ExternalStream(ctx.stream_ptr)
-    r = decode_loop(model, kv, BATCH, PROMPT, args, D, lib_stream, clocks_gpu=local)
+    r = decode_loop(model, kv, BATCH, PROMPT, args, D, lib_stream, clocks_gpu=local,
+                    slide_cap=slide_cap)
 
     # ---- dominant kernels timed alone (CUDA events on their stream) --------
     hbm, tf, peak_kind = measured_peaks()
@@ -305,6 +334,8 @@ def run_ours(args, ws, rank, local):
     if args.temperature > 0.01 or args.penalty > 1.0:
         cfg["sampling"] = {"temperature": args.temperature, "penalty": args.penalty}
     cfg["positions"] = [PROMPT + args.warmup, PROMPT + args.warmup + args.steps]
+    if args.kv_fill == "seeded":
+        cfg["kv_fill"] = "seeded values below the prompt length (no prefill)"
 
     result = {
         "metric": METRIC,
@@ -320,7 +351,7 @@ def run_ours(args, ws, rank, local):
         "dtype": DTYPE,
         "data": "synthetic (seeded random Q4 weights, N(0,0.02) fp32 lm_head, seeded token ids)",
         "config": cfg,
-        "ttft_ms": round(r["ttft_ms"], 3),
+        "ttft_ms": round(r["ttft_ms"], 3) if r["ttft_ms"] is not None else None,
         "e2e": {"value": round(e2e_val, 2), "unit": "tokens/s",
                 "h2d_bytes_per_step": 3 * 4 * BATCH, "d2h_bytes_per_step": 4 * BATCH,
                 "wall_s": round(r["wall"], 4)},

@@ -406,15 +406,18 @@ __device__ int proj_consume(const GemvParams& p, int group, int kidx, const Stag
     cluster_arrive();
     cluster_wait();  // every CTA's partials and bad flag are in its shared memory
     finish = !bad && (tl % p.ksplit) == kidx;  // warp-uniform
+    // a CTA whose weight stream gave up left unfinished partials: no CTA of
+    // the cluster writes tiles from them.  The flags are loaded together with
+    // the partials below (one distributed-shared-memory round trip) and
+    // checked after (every lane reads the same flags: warp-uniform).
+    int peer_bad[kMaxClusterK];
+#pragma unroll
+    for (int r0 = 0; r0 < kMaxClusterK; ++r0) peer_bad[r0] = 0;
     if (finish) {
-      // a CTA whose weight stream gave up left unfinished partials: no CTA
-      // of the cluster writes tiles from them (every lane reads the same flags)
       const uint32_t bad0 = smem_u32(&sh.bad);
-      int any = 0;
 #pragma unroll
       for (int r0 = 0; r0 < kMaxClusterK; ++r0)
-        if (r0 < p.ksplit) any |= ld_dsmem_s32(dsmem_addr(bad0, (uint32_t)r0));
-      finish = any == 0;
+        if (r0 < p.ksplit) peer_bad[r0] = ld_dsmem_s32(dsmem_addr(bad0, (uint32_t)r0));
     }
     if (act && own && finish) {
       // the loads of kB CTAs' partials are in flight at once
@@ -448,6 +451,10 @@ __device__ int proj_consume(const GemvParams& p, int group, int kidx, const Stag
         }
       }
     }
+    int any_bad = 0;
+#pragma unroll
+    for (int r0 = 0; r0 < kMaxClusterK; ++r0) any_bad |= peer_bad[r0];
+    finish = finish && any_bad == 0;
     cluster_arrive();  // done reading the other CTAs' shared memory
   } else if (p.ksplit > 1) {
     // ---- k-segments of the group: the last unit sums the partials in k order

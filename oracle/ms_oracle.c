@@ -369,7 +369,7 @@ int orc_layer_forward(const orc_layer_t *L, int D, float *x, int M,
     }
     /* 4. KV write (main.mojo:584-592; gemma4_e4b.mojo:211-249) */
     const int circular = L->window > 0;
-    for (int r = 0; r < M; ++r) {
+    for (int r = 0; r < M && !kv->frozen; ++r) {
         const int slot = circular ? pos[r] % kv->cap : pos[r];
         const size_t off = ((size_t)seq[r] * kv->cap + slot) * kvd;
         memcpy(kv->k + off, k + (size_t)r * kvd, sizeof(float) * kvd);

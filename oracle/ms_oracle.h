@@ -47,6 +47,9 @@ typedef struct {
     float *k;
     float *v;
     int bf16;
+    int frozen;        /* != 0: orc_layer_forward attends over the cache as it is and
+                          writes no K / V row (a checker that has copied another
+                          implementation's rows in compares only the arithmetic) */
 } orc_kv_layer_t;
 
 /* kernels.mojo:100-108 (dequant_vec): value of logical column n in row k. */

@@ -34,7 +34,7 @@ class OrcLayer(ctypes.Structure):
 
 class OrcKVLayer(ctypes.Structure):
     _fields_ = [("n_seq", ctypes.c_int), ("cap", ctypes.c_int), ("kv_dim", ctypes.c_int),
-                ("k", _f32p), ("v", _f32p), ("bf16", ctypes.c_int)]
+                ("k", _f32p), ("v", _f32p), ("bf16", ctypes.c_int), ("frozen", ctypes.c_int)]
 
 
 def build():
@@ -185,6 +185,12 @@ class OracleModel:
 
     def kv_arrays(self, layer):
         return self._kv[layer][1], self._kv[layer][2]
+
+    def set_kv_frozen(self, on):
+        """While on, layer_forward writes no K / V rows: it attends over the
+        cache as it stands (rows copied in from the implementation under test)."""
+        for kv, _, _ in self._kv:
+            kv.frozen = 1 if on else 0
 
     def layer_forward(self, layer, x, seq, pos):
         x = _f32(x).copy()
