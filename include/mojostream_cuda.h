@@ -234,6 +234,34 @@ enum { MS_KV_F32 = 0, MS_KV_BF16 = 1 };
  * softmax and accumulation stay fp32; needs every kv_dim % 8 == 0). */
 MS_API ms_status ms_kv_create_typed(ms_ctx *ctx, const ms_model *model, int n_seq, int max_pos,
                                     int slide_cap, int dtype, ms_kv **out);
+/* A cache for serving requests that come and go (the reference's roadmap:
+ * paged KV allocator / continuous batching, README.md:487-489).  The
+ * full-attention layers draw 16-position pages from one pool of pool_pages
+ * pages (a page id indexes every full layer's pool) instead of holding
+ * max_pos positions for each of the n_seq sequence slots: a page is given to
+ * a slot the first time a call writes (or a decode loop will reach) one of
+ * its positions, together with every page below it, so short and long
+ * sequences share the pool in proportion to their lengths.  Sliding layers
+ * keep a ring of slide_cap slots per slot (they never grow past it).
+ * MS_ERR_CAPACITY when the pool runs out (before any launch).  Every other
+ * call works on it as on an ms_kv_create cache. */
+MS_API ms_status ms_kv_create_pooled(ms_ctx *ctx, const ms_model *model, int n_seq, int max_pos,
+                                     int slide_cap, int dtype, int pool_pages, ms_kv **out);
+/* Slot `seq` is free for a new request: its pages go back to the pool (pages
+ * it shares stay with the other holders) and its token history is cleared.
+ * Any cache; stream-ordered on the context stream. */
+MS_API ms_status ms_kv_release(ms_ctx *ctx, ms_kv *kv, int seq);
+/* Slot dst starts as a copy of the first n_pos positions of slot src (a
+ * prompt prefix computed once and reused): on a pooled cache dst's table
+ * points at src's whole pages below n_pos (shared, reference-counted; a
+ * later write into a shared page gets a private copy first) and the page the
+ * prefix ends in is copied; the sliding rings and the token history are
+ * copied.  dst must hold no pages (a new or released slot).  Continue dst at
+ * position n_pos. */
+MS_API ms_status ms_kv_share_prefix(ms_ctx *ctx, ms_kv *kv, int src_seq, int dst_seq, int n_pos);
+/* Full-attention pages in use and in total (pooled: the pool; otherwise
+ * n_seq x ceil(max_pos / 16), all of them in use). */
+MS_API ms_status ms_kv_pages(const ms_kv *kv, int *used, int *total);
 MS_API ms_status ms_kv_destroy(ms_ctx *ctx, ms_kv *kv);
 /* K / V rows of positions pos0 .. pos0 + n - 1 of sequence seq in layer
  * `layer`, to or from dense fp32 device buffers k, v [n][kv_dim] (the

@@ -88,6 +88,12 @@ SIGNATURES = {
                                     ctypes.POINTER(_vp)]),
     "ms_kv_create_typed": (ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                           ctypes.c_int, ctypes.POINTER(_vp)]),
+    "ms_kv_create_pooled": (ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                           ctypes.c_int, ctypes.c_int, ctypes.POINTER(_vp)]),
+    "ms_kv_release": (ctypes.c_int, [_vp, _vp, ctypes.c_int]),
+    "ms_kv_share_prefix": (ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int]),
+    "ms_kv_pages": (ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_int),
+                                   ctypes.POINTER(ctypes.c_int)]),
     "ms_kv_destroy": (ctypes.c_int, [_vp, _vp]),
     "ms_kv_reset": (ctypes.c_int, [_vp, _vp]),
     "ms_kv_bytes": (ctypes.c_size_t, [_vp]),

@@ -156,6 +156,14 @@ struct ms_kv {
   int* tok = nullptr;  // [n_seq][max_pos] token fed at each position (-1: none)
   int bf16 = 0;        // K / V pools hold bfloat16
   size_t bytes = 0;
+  // pooled mode (ms_kv_create_pooled): the full-attention layers draw pages
+  // from one pool of pool_pages pages (a page id indexes every full layer's
+  // pool), assigned on first use and shared by reference (prefixes); the
+  // host mirror of bt_full, the free list and per-page reference counts
+  int pooled = 0, pool_pages = 0;
+  std::vector<int> bt_host;
+  std::vector<int> free_pages;
+  std::vector<int> refs;
 };
 
 struct ms_q4_weight {
@@ -1145,8 +1153,8 @@ extern "C" ms_status ms_kv_create(ms_ctx* c, const ms_model* m, int n_seq, int m
   return ms_kv_create_typed(c, m, n_seq, max_pos, slide_cap, MS_KV_F32, out);
 }
 
-extern "C" ms_status ms_kv_create_typed(ms_ctx* c, const ms_model* m, int n_seq, int max_pos,
-                                        int slide_cap, int dtype, ms_kv** out) {
+static ms_status kv_create(ms_ctx* c, const ms_model* m, int n_seq, int max_pos, int slide_cap,
+                           int dtype, int pool_pages, ms_kv** out) {
   if (!c || !m || !out) return MS_ERR_INVALID_ARG;
   *out = nullptr;
   if (m->ctx != c) return fail(c, MS_ERR_STATE, "model belongs to another context");
@@ -1185,20 +1193,30 @@ extern "C" ms_status ms_kv_create_typed(ms_ctx* c, const ms_model* m, int n_seq,
     ms_kv_destroy(c, kv);
     return s;
   };
-  // block tables: sequence s owns pages [s * P, (s + 1) * P) of every pool
+  if (pool_pages > 0) {
+    kv->pooled = 1;
+    kv->pool_pages = pool_pages;
+    kv->refs.assign((size_t)pool_pages, 0);
+    for (int p = pool_pages - 1; p >= 0; --p) kv->free_pages.push_back(p);  // pop_back: 0, 1, ...
+  }
+  // block tables: sequence s owns pages [s * P, (s + 1) * P) of every pool,
+  // except the full-attention pages of a pooled cache (unassigned: -1)
   std::vector<int> bt((size_t)n_seq * std::max(kv->pages_full, kv->pages_slide));
   for (int pass = 0; pass < 2; ++pass) {
     const int P = pass == 0 ? kv->pages_full : kv->pages_slide;
     if (P == 0) continue;
     for (int s = 0; s < n_seq; ++s)
-      for (int j = 0; j < P; ++j) bt[(size_t)s * P + j] = s * P + j;
+      for (int j = 0; j < P; ++j) bt[(size_t)s * P + j] = (pass == 0 && kv->pooled) ? -1 : s * P + j;
+    if (pass == 0 && kv->pooled) kv->bt_host.assign(bt.begin(), bt.begin() + (size_t)n_seq * P);
     int** dst = pass == 0 ? &kv->bt_full : &kv->bt_slide;
     if (dev_alloc(c, (void**)dst, (size_t)n_seq * P * sizeof(int)) != MS_OK) return cleanup(MS_ERR_OOM);
     cudaMemcpy(*dst, bt.data(), (size_t)n_seq * P * sizeof(int), cudaMemcpyHostToDevice);
   }
   for (const LayerDev& L : m->layers) {
     const int P = L.d.window > 0 ? kv->pages_slide : kv->pages_full;
-    const size_t n = (size_t)n_seq * P * kv->page * L.kv_dim;
+    const size_t n = (L.d.window == 0 && kv->pooled)
+                         ? (size_t)kv->pool_pages * kv->page * L.kv_dim
+                         : (size_t)n_seq * P * kv->page * L.kv_dim;
     float *k = nullptr, *v = nullptr;
     if (dev_alloc(c, (void**)&k, n * eb) != MS_OK) return cleanup(MS_ERR_OOM);
     kv->k.push_back(k);
@@ -1217,6 +1235,18 @@ extern "C" ms_status ms_kv_create_typed(ms_ctx* c, const ms_model* m, int n_seq,
   return MS_OK;
 }
 
+extern "C" ms_status ms_kv_create_typed(ms_ctx* c, const ms_model* m, int n_seq, int max_pos,
+                                        int slide_cap, int dtype, ms_kv** out) {
+  return kv_create(c, m, n_seq, max_pos, slide_cap, dtype, 0, out);
+}
+
+extern "C" ms_status ms_kv_create_pooled(ms_ctx* c, const ms_model* m, int n_seq, int max_pos,
+                                         int slide_cap, int dtype, int pool_pages, ms_kv** out) {
+  if (!c || !out) return MS_ERR_INVALID_ARG;
+  if (pool_pages <= 0) return fail(c, MS_ERR_SHAPE, "kv: pool_pages %d", pool_pages);
+  return kv_create(c, m, n_seq, max_pos, slide_cap, dtype, pool_pages, out);
+}
+
 extern "C" ms_status ms_kv_destroy(ms_ctx* c, ms_kv* kv) {
   if (!c || !kv) return MS_ERR_INVALID_ARG;
   cudaSetDevice(c->device);
@@ -1233,15 +1263,200 @@ extern "C" ms_status ms_kv_destroy(ms_ctx* c, ms_kv* kv) {
 extern "C" ms_status ms_kv_reset(ms_ctx* c, ms_kv* kv) {
   if (!c || !kv) return MS_ERR_INVALID_ARG;
   // positions are explicit per call; the contents need no clearing, but do it
-  // so a reset cache is indistinguishable from a new one
+  // so a reset cache is indistinguishable from a new one (a pooled cache
+  // also gets all its pages back)
   for (size_t i = 0; i < kv->k.size(); ++i) {
     const LayerDev& L = kv->model->layers[i];
     const int P = L.d.window > 0 ? kv->pages_slide : kv->pages_full;
-    const size_t n = (size_t)kv->n_seq * P * kv->page * L.kv_dim * (kv->bf16 ? 2 : 4);
+    const size_t pages = (L.d.window == 0 && kv->pooled) ? (size_t)kv->pool_pages
+                                                         : (size_t)kv->n_seq * P;
+    const size_t n = pages * kv->page * L.kv_dim * (kv->bf16 ? 2 : 4);
     MS_CUDA(c, cudaMemsetAsync(kv->k[i], 0, n, c->stream));
     MS_CUDA(c, cudaMemsetAsync(kv->v[i], 0, n, c->stream));
   }
   MS_CUDA(c, cudaMemsetAsync(kv->tok, 0xFF, (size_t)kv->n_seq * kv->max_pos * sizeof(int), c->stream));
+  if (kv->pooled) {
+    std::fill(kv->bt_host.begin(), kv->bt_host.end(), -1);
+    std::fill(kv->refs.begin(), kv->refs.end(), 0);
+    kv->free_pages.clear();
+    for (int p = kv->pool_pages - 1; p >= 0; --p) kv->free_pages.push_back(p);
+    MS_CUDA(c, cudaMemcpyAsync(kv->bt_full, kv->bt_host.data(), kv->bt_host.size() * sizeof(int),
+                               cudaMemcpyHostToDevice, c->stream));
+  }
+  return MS_OK;
+}
+
+// ------------------------------------------------------ pooled KV pages --
+
+static std::vector<int> full_layers(const ms_kv* kv) {
+  std::vector<int> f;
+  for (size_t l = 0; l < kv->model->layers.size(); ++l)
+    if (kv->model->layers[l].d.window == 0) f.push_back((int)l);
+  return f;
+}
+
+// Copy page `from` to page `to` in every full-attention layer's K and V pool.
+static ms_status kv_copy_page(ms_ctx* c, ms_kv* kv, int from, int to, cudaStream_t s) {
+  const size_t eb = kv->bf16 ? 2 : 4;
+  for (int l : full_layers(kv)) {
+    const size_t row = (size_t)kv->page * kv->model->layers[l].kv_dim * eb;
+    char* k = reinterpret_cast<char*>(kv->k[l]);
+    char* v = reinterpret_cast<char*>(kv->v[l]);
+    MS_CUDA(c, cudaMemcpyAsync(k + to * row, k + from * row, row, cudaMemcpyDeviceToDevice, s));
+    MS_CUDA(c, cudaMemcpyAsync(v + to * row, v + from * row, row, cudaMemcpyDeviceToDevice, s));
+  }
+  return MS_OK;
+}
+
+// Pooled cache: give sequence seq pages for every position up to pos_hi (all
+// pages below it too, so no position a kernel may read maps to no page), and
+// a private copy of any page shared with another sequence that positions
+// lo_write .. pos_hi fall in (copy on write).  dirty: the sequence's table
+// row changed.
+static ms_status kv_assign(ms_ctx* c, ms_kv* kv, int seq, int lo_write, int pos_hi, bool* dirty,
+                           cudaStream_t s) {
+  const int P = kv->pages_full;
+  int* row = kv->bt_host.data() + (size_t)seq * P;
+  const int j_hi = pos_hi / kv->page;
+  for (int j = 0; j <= j_hi; ++j) {
+    const bool written = j >= lo_write / kv->page;
+    if (row[j] >= 0 && !(written && kv->refs[row[j]] > 1)) continue;
+    if (kv->free_pages.empty())
+      return fail(c, MS_ERR_CAPACITY,
+                  "kv: the page pool (%d pages of %d positions) is exhausted (sequence %d, "
+                  "position %d); release finished sequences", kv->pool_pages, kv->page, seq,
+                  j * kv->page);
+    const int fresh = kv->free_pages.back();
+    kv->free_pages.pop_back();
+    if (row[j] >= 0) {  // shared page about to be written: private copy
+      MS_TRY(kv_copy_page(c, kv, row[j], fresh, s));
+      --kv->refs[row[j]];
+    }
+    kv->refs[fresh] = 1;
+    row[j] = fresh;
+    *dirty = true;
+  }
+  return MS_OK;
+}
+
+static ms_status kv_upload_row(ms_ctx* c, ms_kv* kv, int seq, cudaStream_t s) {
+  const size_t P = (size_t)kv->pages_full;
+  MS_CUDA(c, cudaMemcpyAsync(kv->bt_full + seq * P, kv->bt_host.data() + seq * P, P * sizeof(int),
+                             cudaMemcpyHostToDevice, s));
+  return MS_OK;
+}
+
+// Before a call that writes rows (seq[r], pos[r]) (and, for a decode loop,
+// the `extra` positions after each): assign the pages they need.
+static ms_status kv_prepare(ms_ctx* c, ms_kv* kv, const int* seq, const int* pos, int M, int extra,
+                            cudaStream_t s) {
+  if (!kv->pooled) return MS_OK;
+  std::vector<int> lo(kv->n_seq, 1 << 30), hi(kv->n_seq, -1);
+  for (int r = 0; r < M; ++r) {
+    lo[seq[r]] = std::min(lo[seq[r]], pos[r]);
+    hi[seq[r]] = std::max(hi[seq[r]], pos[r] + extra);
+  }
+  for (int q = 0; q < kv->n_seq; ++q) {
+    if (hi[q] < 0) continue;
+    if (hi[q] >= kv->max_pos)
+      return fail(c, MS_ERR_CAPACITY, "sequence %d: position %d outside the cache (max_pos %d)", q,
+                  hi[q], kv->max_pos);
+    bool dirty = false;
+    MS_TRY(kv_assign(c, kv, q, lo[q], hi[q], &dirty, s));
+    if (dirty) MS_TRY(kv_upload_row(c, kv, q, s));
+  }
+  return MS_OK;
+}
+
+extern "C" ms_status ms_kv_release(ms_ctx* c, ms_kv* kv, int seq) {
+  if (!c || !kv) return MS_ERR_INVALID_ARG;
+  if (seq < 0 || seq >= kv->n_seq)
+    return fail(c, MS_ERR_INVALID_ARG, "ms_kv_release: sequence %d outside 0..%d", seq,
+                kv->n_seq - 1);
+  cudaStream_t s = c->stream;
+  MS_CUDA(c, cudaMemsetAsync(kv->tok + (size_t)seq * kv->max_pos, 0xFF, kv->max_pos * sizeof(int), s));
+  if (!kv->pooled) return MS_OK;
+  int* row = kv->bt_host.data() + (size_t)seq * kv->pages_full;
+  for (int j = 0; j < kv->pages_full; ++j) {
+    if (row[j] < 0) continue;
+    if (--kv->refs[row[j]] == 0) kv->free_pages.push_back(row[j]);
+    row[j] = -1;
+  }
+  return kv_upload_row(c, kv, seq, s);
+}
+
+extern "C" ms_status ms_kv_share_prefix(ms_ctx* c, ms_kv* kv, int src, int dst, int n_pos) {
+  if (!c || !kv) return MS_ERR_INVALID_ARG;
+  if (src < 0 || src >= kv->n_seq || dst < 0 || dst >= kv->n_seq || src == dst)
+    return fail(c, MS_ERR_INVALID_ARG, "ms_kv_share_prefix: sequences %d -> %d", src, dst);
+  if (n_pos <= 0 || n_pos > kv->max_pos)
+    return fail(c, MS_ERR_CAPACITY, "ms_kv_share_prefix: %d positions (max_pos %d)", n_pos,
+                kv->max_pos);
+  cudaStream_t s = c->stream;
+  const size_t P = (size_t)kv->pages_full;
+  if (kv->pooled) {
+    int* rs = kv->bt_host.data() + src * P;
+    int* rd = kv->bt_host.data() + dst * P;
+    for (size_t j = 0; j < P; ++j)
+      if (rd[j] >= 0)
+        return fail(c, MS_ERR_STATE, "ms_kv_share_prefix: sequence %d holds pages (release it)", dst);
+    const int full = n_pos / kv->page, part = n_pos % kv->page;
+    for (int j = 0; j < full + (part ? 1 : 0); ++j)
+      if (rs[j] < 0)
+        return fail(c, MS_ERR_STATE, "ms_kv_share_prefix: sequence %d has no page at position %d",
+                    src, j * kv->page);
+    if (part && kv->free_pages.empty())
+      return fail(c, MS_ERR_CAPACITY, "ms_kv_share_prefix: the page pool is exhausted");
+    for (int j = 0; j < full; ++j) {  // whole pages: shared by reference
+      rd[j] = rs[j];
+      ++kv->refs[rs[j]];
+    }
+    if (part) {  // the page the prefix ends in: a private copy
+      const int fresh = kv->free_pages.back();
+      kv->free_pages.pop_back();
+      MS_TRY(kv_copy_page(c, kv, rs[full], fresh, s));
+      kv->refs[fresh] = 1;
+      rd[full] = fresh;
+    }
+    MS_TRY(kv_upload_row(c, kv, dst, s));
+  } else {
+    // fixed pages: copy the prefix rows of every full-attention layer
+    const size_t eb = kv->bf16 ? 2 : 4;
+    for (int l : full_layers(kv)) {
+      const size_t bytes = (size_t)n_pos * kv->model->layers[l].kv_dim * eb;
+      const size_t off = (size_t)P * kv->page * kv->model->layers[l].kv_dim * eb;
+      char* k = reinterpret_cast<char*>(kv->k[l]);
+      char* v = reinterpret_cast<char*>(kv->v[l]);
+      MS_CUDA(c, cudaMemcpyAsync(k + dst * off, k + src * off, bytes, cudaMemcpyDeviceToDevice, s));
+      MS_CUDA(c, cudaMemcpyAsync(v + dst * off, v + src * off, bytes, cudaMemcpyDeviceToDevice, s));
+    }
+  }
+  // sliding layers: the ring holds position p at slot p % slide_cap in both
+  // sequences, so the whole ring is copied (slots past the prefix are
+  // overwritten before they are read)
+  const size_t eb = kv->bf16 ? 2 : 4;
+  for (size_t l = 0; l < kv->k.size(); ++l) {
+    const LayerDev& L = kv->model->layers[l];
+    if (L.d.window == 0) continue;
+    const size_t ring = (size_t)kv->pages_slide * kv->page * L.kv_dim * eb;
+    char* k = reinterpret_cast<char*>(kv->k[l]);
+    char* v = reinterpret_cast<char*>(kv->v[l]);
+    MS_CUDA(c, cudaMemcpyAsync(k + dst * ring, k + src * ring, ring, cudaMemcpyDeviceToDevice, s));
+    MS_CUDA(c, cudaMemcpyAsync(v + dst * ring, v + src * ring, ring, cudaMemcpyDeviceToDevice, s));
+  }
+  // the repetition-penalty history of the prefix
+  MS_CUDA(c, cudaMemsetAsync(kv->tok + (size_t)dst * kv->max_pos, 0xFF, kv->max_pos * sizeof(int), s));
+  MS_CUDA(c, cudaMemcpyAsync(kv->tok + (size_t)dst * kv->max_pos, kv->tok + (size_t)src * kv->max_pos,
+                             n_pos * sizeof(int), cudaMemcpyDeviceToDevice, s));
+  return MS_OK;
+}
+
+extern "C" ms_status ms_kv_pages(const ms_kv* kv, int* used, int* total) {
+  if (!kv) return MS_ERR_INVALID_ARG;
+  const int tot = kv->pooled ? kv->pool_pages : kv->n_seq * kv->pages_full;
+  const int fr = kv->pooled ? (int)kv->free_pages.size() : 0;
+  if (used) *used = tot - fr;
+  if (total) *total = tot;
   return MS_OK;
 }
 
@@ -1274,6 +1489,11 @@ extern "C" ms_status ms_kv_write(ms_ctx* c, ms_kv* kv, int layer, int seq, int p
                                  const float* k, const float* v, void* stream) {
   if (!c || !kv) return MS_ERR_INVALID_ARG;
   MS_TRY(kv_rows_check(c, kv, layer, seq, pos0, n, k, v, "ms_kv_write"));
+  if (kv->pooled && kv->model->layers[layer].d.window == 0) {
+    bool dirty = false;
+    MS_TRY(kv_assign(c, kv, seq, pos0, pos0 + n - 1, &dirty, pick(c, stream)));
+    if (dirty) MS_TRY(kv_upload_row(c, kv, seq, pick(c, stream)));
+  }
   MS_CUDA(c, launch_kv_copy(kv_view(kv, layer), seq, pos0, n, const_cast<float*>(k),
                             const_cast<float*>(v), 0, pick(c, stream)));
   return MS_OK;
@@ -1283,6 +1503,11 @@ extern "C" ms_status ms_kv_read(ms_ctx* c, const ms_kv* kv, int layer, int seq, 
                                 float* k, float* v, void* stream) {
   if (!c || !kv) return MS_ERR_INVALID_ARG;
   MS_TRY(kv_rows_check(c, kv, layer, seq, pos0, n, k, v, "ms_kv_read"));
+  if (kv->pooled && kv->model->layers[layer].d.window == 0)
+    for (int j = pos0 / kv->page; j <= (pos0 + n - 1) / kv->page; ++j)
+      if (kv->bt_host[(size_t)seq * kv->pages_full + j] < 0)
+        return fail(c, MS_ERR_STATE, "ms_kv_read: sequence %d has no page at position %d", seq,
+                    j * kv->page);
   MS_CUDA(c, launch_kv_copy(kv_view(kv, layer), seq, pos0, n, k, v, 1, pick(c, stream)));
   return MS_OK;
 }
@@ -1356,7 +1581,9 @@ static KvView kv_view(const ms_kv* kv, int layer) {
   v.cap = slide ? kv->slide_cap : kv->pages_full * kv->page;
   v.circular = slide ? 1 : 0;
   v.kv_dim = L.kv_dim;
-  v.off32 = (size_t)kv->n_seq * v.bt_stride * v.page * v.kv_dim < ((size_t)1 << 32);
+  const size_t pages = (!slide && kv->pooled) ? (size_t)kv->pool_pages
+                                              : (size_t)kv->n_seq * v.bt_stride;
+  v.off32 = pages * v.page * v.kv_dim < ((size_t)1 << 32);
   v.bf16 = kv->bf16;
   return v;
 }
@@ -1569,6 +1796,7 @@ extern "C" ms_status ms_layer_forward(ms_ctx* c, const ms_model* mc, int layer, 
   MS_TRY(check_x(c, x));
   MS_TRY(check_rows(c, m, kv, seq, pos, M));
   cudaStream_t s = pick(c, stream);
+  MS_TRY(kv_prepare(c, kv, seq, pos, M, 0, s));
   MS_TRY(upload_rows(c, m, seq, pos, M, s));
   MS_CUDA(c, launch_rowstats(m->S[0], x, m->hidden, M, m->hidden, s, false));
   return run_layer(c, m, kv, layer, M, x, m->S[0], m->X[1], m->S[1], s, true, true);
@@ -1581,6 +1809,7 @@ extern "C" ms_status ms_forward(ms_ctx* c, const ms_model* mc, float* x, ms_kv* 
   MS_TRY(check_x(c, x));
   MS_TRY(check_rows(c, m, kv, seq, pos, M));
   cudaStream_t s = pick(c, stream);
+  MS_TRY(kv_prepare(c, kv, seq, pos, M, 0, s));
   MS_TRY(upload_rows(c, m, seq, pos, M, s));
   MS_CUDA(c, launch_rowstats(m->S[0], x, m->hidden, M, m->hidden, s, false));
   for (int l = 0; l < m->n_layers; ++l)
@@ -1793,7 +2022,7 @@ static ms_status ensure_graph(ms_ctx* c, ms_model* m, const ms_kv* kv, int M) {
 
 // Validate a decode call and stage its rows (ids / seq / pos) through pinned
 // host memory into the device row buffers.
-static ms_status stage_rows(ms_ctx* c, ms_model* m, const ms_kv* kv, const int* ids,
+static ms_status stage_rows(ms_ctx* c, ms_model* m, ms_kv* kv, const int* ids,
                             const int* seq, const int* pos, int M, int steps, cudaStream_t s) {
   if (m->vocab <= 0) return fail(c, MS_ERR_STATE, "model has no lm_head");
   MS_TRY(check_rows(c, m, kv, seq, pos, M));
@@ -1802,6 +2031,7 @@ static ms_status stage_rows(ms_ctx* c, ms_model* m, const ms_kv* kv, const int* 
     for (int& p : last) p += steps - 1;
     MS_TRY(check_rows(c, m, kv, seq, last.data(), M));
   }
+  MS_TRY(kv_prepare(c, kv, seq, pos, M, steps - 1, s));
   for (int r = 0; r < M; ++r)
     if (ids[r] < 0 || ids[r] >= m->vocab)
       return fail(c, MS_ERR_INVALID_ARG, "token id %d outside 0..%d", ids[r], m->vocab - 1);
@@ -1957,6 +2187,8 @@ extern "C" ms_status ms_prefill(ms_ctx* c, const ms_model* mc, ms_kv* kv, const 
   for (int r0 = 0; r0 < n_tokens && st == MS_OK; r0 += m->max_rows) {
     const int M = std::min(m->max_rows, n_tokens - r0);
     st = check_rows(c, m, kv, seq + r0, pos + r0, M);
+    if (st != MS_OK) break;
+    st = kv_prepare(c, kv, seq + r0, pos + r0, M, 0, s);
     if (st != MS_OK) break;
     st = upload_rows(c, m, seq + r0, pos + r0, M, s);
     if (st != MS_OK) break;

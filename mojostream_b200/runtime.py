@@ -274,14 +274,34 @@ class Model:
 class KVCache:
     """ms_kv: paged cache for n_seq sequences."""
 
-    def __init__(self, ctx, model, n_seq, max_pos, slide_cap=0, dtype="f32"):
-        """dtype "f32" (the parity mode) or "bf16" (half the cache bytes)."""
+    def __init__(self, ctx, model, n_seq, max_pos, slide_cap=0, dtype="f32", pool_pages=0):
+        """dtype "f32" (the parity mode) or "bf16" (half the cache bytes);
+        pool_pages > 0: the full-attention layers share a pool of that many
+        16-position pages (ms_kv_create_pooled)."""
         self.ctx, self.n_seq, self.max_pos, self.dtype = ctx, n_seq, max_pos, dtype
         h = ctypes.c_void_p()
         code = {"f32": 0, "bf16": 1}[dtype]
-        ctx.check(lib().ms_kv_create_typed(ctx.h, model.h, n_seq, max_pos, slide_cap, code,
-                                           ctypes.byref(h)))
+        if pool_pages:
+            ctx.check(lib().ms_kv_create_pooled(ctx.h, model.h, n_seq, max_pos, slide_cap, code,
+                                                pool_pages, ctypes.byref(h)))
+        else:
+            ctx.check(lib().ms_kv_create_typed(ctx.h, model.h, n_seq, max_pos, slide_cap, code,
+                                               ctypes.byref(h)))
         self.h = h
+
+    def release(self, seq):
+        """ms_kv_release: slot seq is free for a new request."""
+        self.ctx.check(lib().ms_kv_release(self.ctx.h, self.h, seq))
+
+    def share_prefix(self, src, dst, n_pos):
+        """ms_kv_share_prefix: slot dst starts with src's first n_pos positions."""
+        self.ctx.check(lib().ms_kv_share_prefix(self.ctx.h, self.h, src, dst, n_pos))
+
+    def pages(self):
+        """(used, total) full-attention pages."""
+        u, t = ctypes.c_int(), ctypes.c_int()
+        check(lib().ms_kv_pages(self.h, ctypes.byref(u), ctypes.byref(t)))
+        return u.value, t.value
 
     @property
     def nbytes(self):
