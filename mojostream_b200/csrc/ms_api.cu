@@ -346,7 +346,8 @@ extern "C" ms_status ms_init(int device, ms_ctx** out) {
   cudaEventCreate(&c->ev[0]);
   cudaEventCreate(&c->ev[1]);
   if (prepare_gemv_stream() != cudaSuccess || prepare_attention() != cudaSuccess ||
-      prepare_gemm_tc() != cudaSuccess || prepare_attention_prefill() != cudaSuccess) {
+      prepare_gemm_tc() != cudaSuccess || prepare_gemm_sk() != cudaSuccess ||
+      prepare_attention_prefill() != cudaSuccess) {
     ms_destroy(c);
     return MS_ERR_CUDA;
   }
@@ -567,7 +568,7 @@ static bool splitk_global_forced() {
 // Launch plan of one projection: decode kernel (M <= 8) or the tiled kernel,
 // m-group size, chunks per round, k-segment and the number of k-segments.
 struct GemvPlan {
-  bool dec, tc;
+  bool dec, tc, sk;  // sk: the decode-batch tensor-core kernel (tc is set too)
   int mg, ch, kseg, ksplit;
 };
 
@@ -603,9 +604,22 @@ static ms_status ensure_tc_scratch(ms_ctx* c, int M, int K) {
   return MS_OK;
 }
 
-static GemvPlan plan_gemv(const ms_ctx* c, int M, int K, int n_tiles, bool allow_tc = true) {
+static GemvPlan plan_gemv(const ms_ctx* c, int M, int K, int n_tiles, bool allow_tc = true,
+                          bool allow_sk = true) {
   GemvPlan pl{};
   const int chunks = K / kChunkK;
+  if (allow_tc && allow_sk && M >= kTcMinRows && M <= sk_rows_max()) {
+    // decode batches: weights on the MMA's 128-row side, about one CTA per SM
+    // (tile groups x k-slices), the slices of a group one cluster (<= 8)
+    pl.tc = pl.sk = true;
+    const int groups = padded_tiles(n_tiles) / kGroupTiles;
+    int ks = std::max(1, (c->sm_count + groups / 2) / groups);
+    ks = std::min(std::min(ks, 8), chunks);
+    const int seg = (chunks + ks - 1) / ks;
+    pl.kseg = seg * kChunkK;
+    pl.ksplit = (chunks + seg - 1) / seg;
+    return pl;
+  }
   if (allow_tc && M >= kTcMinRows) {
     // one CTA per (tile group, 128-row tile), all of K -- or k slices when
     // that grid cannot fill the GPU (small batches of narrow projections);
@@ -666,6 +680,7 @@ static GemvPlan plan_gemv(const ms_ctx* c, int M, int K, int n_tiles, bool allow
 }
 
 static cudaError_t launch_proj(const GemvParams& p, const GemvPlan& pl, cudaStream_t s, bool pdl) {
+  if (pl.sk) return launch_gemm_sk(p, s, pdl);
   if (pl.tc) return launch_gemm_tc(p, s, pdl);
   return pl.dec ? launch_gemv_stream(p, pl.mg, s, pdl) : launch_gemv(p, pl.mg, pl.ch, s, pdl);
 }
@@ -1689,7 +1704,8 @@ static ms_status run_layer(ms_ctx* c, ms_model* m, const ms_kv* kv, int li, int 
   //    partial sums, all-reduce, then the residual)
   const bool tp = c->tp_world > 1;
   {
-    GemvPlan pl = plan_gemv(c, M, L.q_dim, D / kTileN);
+    // tensor parallel: the prefill GEMM, whose epilogue sums the ranks' tiles
+    GemvPlan pl = plan_gemv(c, M, L.q_dim, D / kTileN, true, !tp);
     GemvParams p = gemv_base(c, L.wo, D / kTileN, L.q_dim, M, pl);
     p.lq = m->lq;
     p.rowf = m->rowf;
@@ -1745,7 +1761,7 @@ static ms_status run_layer(ms_ctx* c, ms_model* m, const ms_kv* kv, int li, int 
   }
   // 5. Down + residual
   {
-    GemvPlan pl = plan_gemv(c, M, F, D / kTileN);
+    GemvPlan pl = plan_gemv(c, M, F, D / kTileN, true, !tp);
     GemvParams p = gemv_base(c, L.wd, D / kTileN, F, M, pl);
     p.lq = m->lq;
     p.rowf = m->rowf;

@@ -1,0 +1,335 @@
+// ms_gemm_sk.cu -- Q4 projection for decode batches of 9..64 rows on the
+// 5th-generation tensor cores, weights on the MMA's 128-row side.
+// Reference: matmul_q4_bpack_raw (src/linalg/kernels.mojo:201-267) with the
+// steps fused around its call sites (src/main.mojo:538-613,
+// src/inference/gemma4_e4b.mojo:459-540) in the epilogue.
+//
+// Why a second tensor-core kernel: with batch rows on the MMA's M side (the
+// prefill GEMM, ms_gemm_tc.cu) a batch of 16 or 64 rows fills a 128-row tile
+// to 1/8 or 1/2, and every 64-k chunk moves 24 KB of activation limbs for
+// 4 KB of weights.  Here the tile is transposed: the MMA's A operand is 128
+// output columns of the weights (M = 128), B is the batch's activation limbs
+// (N = rows rounded up to 16), so a chunk moves 4 KB of weights and
+// 3 x N x 64 bytes of limbs, and no MMA work is spent on padding rows beyond
+// the next multiple of 16.
+//
+// Arithmetic: exactly that of the prefill GEMM -- rows quantised once per
+// projection by quant_rows_kernel into three signed 8-bit limbs (q =
+// d0 + 2^8 d1 + 2^16 d2, |q| <= 2^22 of the row maximum), weights unpacked to
+// s8 (u - 8), one s8 x s8 -> s32 MMA chain per limb, limbs combined in int64
+// and scaled by (a / 2^22) * (RMSNorm factor) in the epilogue, the weight
+// scale applied there once.
+//
+// CTA: one tile group (128 output columns) over one k-slice.  Warp 0 streams
+// stages with cp.async.bulk (4 KB packed nibbles + the N rows of the three
+// limb planes per 64-k chunk; the weight copies of the first stages go out
+// before griddepcontrol.wait, since no earlier kernel writes them); warp 1
+// allocates 256 tensor-memory columns and one thread issues the MMAs;
+// warps 2-9 unpack nibbles into the A operand; warps 2-5 run the epilogue
+// (tensor-memory lane = output column, columns = batch rows).  The k-slices
+// of a group run as one thread-block cluster (<= 8 CTAs): each leaves its
+// partial tile in shared memory and CTA r finishes the rows m = r (mod
+// slices), summing the slices in k order through distributed shared memory
+// (the same order on every run).  Every wait is bounded (error word).
+#include "ms_common.cuh"
+#include "ms_epilogue.cuh"
+#include "ms_kernels.h"
+#include "ms_tc.cuh"
+
+namespace ms {
+
+constexpr int kSkStages = 4;
+constexpr int kSkLimbs = 3;
+constexpr int kSkMaxN = 64;                                // batch rows per launch
+constexpr int kSkAConv = 128 * kChunkK;                    // 8 KB: s8 weights, 128 x 64
+constexpr int kSkAPacked = kGroupTiles * kWarp * 16;       // 4 KB: packed nibbles
+constexpr int kSkPlane = 128 * kChunkK;                    // a quantiser limb plane (128 rows)
+constexpr int kSkBMax = kSkLimbs * kSkMaxN * kChunkK;      // 12 KB: limbs of 64 rows
+constexpr int kSkStageBytes = kSkAConv + kSkAPacked + kSkBMax;  // 24 KB
+constexpr int kSkConvWarps = 8;
+constexpr int kSkThreads = (2 + kSkConvWarps) * kWarp;     // 320
+constexpr uint32_t kSkCols = 256;                          // >= 3 x 64 accumulator columns
+constexpr int kSkRowS = 128 + 4;                           // staged partial row (floats)
+constexpr size_t kSkSmem = (size_t)kSkStages * kSkStageBytes;
+constexpr int kSkMaxCluster = 8;
+constexpr uint32_t kSkLbo = 128, kSkSbo = 512;
+
+static_assert(kSkStageBytes % 1024 == 0, "stage alignment");
+static_assert((size_t)kSkMaxN * kSkRowS * 4 <= kSkSmem, "staged partial fits the ring");
+
+int sk_rows_max() { return kSkMaxN; }
+
+__global__ void __launch_bounds__(kSkThreads, 2) gemm_sk_kernel(const GemvParams p, int N) {
+  extern __shared__ __align__(1024) uint8_t dsm[];
+  __shared__ __align__(8) uint64_t full[kSkStages], conv[kSkStages], empty[kSkStages], done;
+  __shared__ uint32_t s_tmem;
+  __shared__ volatile int s_bad;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int group = blockIdx.x;
+  const int nchunks = p.K / kChunkK;
+  const int kidx = blockIdx.z, seg = p.kseg / kChunkK;
+  const int c_begin = kidx * seg;
+  const int n_loc = min(nchunks, c_begin + seg) - c_begin;
+  const bool cl = p.ksplit > 1;
+  const uint32_t b_bytes = (uint32_t)N * kChunkK;  // one limb's N rows of a chunk
+
+  if (threadIdx.x == 0) {
+    s_bad = 0;
+    for (int s = 0; s < kSkStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&conv[s], kSkConvWarps);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(&done, 1);
+    mbar_fence_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&s_tmem, kSkCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s_tmem;
+  pdl_trigger();
+
+  if (warp == 0) {
+    // ------------------------------------------------------- producer --
+    if (lane == 0) {
+      const uint4* a_src = p.w + ((size_t)group * nchunks + c_begin) * kGroupTiles * kWarp;
+      const uint8_t* b_src = p.lq + (size_t)c_begin * kSkLimbs * kSkPlane;
+      const int first = min(n_loc, kSkStages);
+      // weights first: they do not depend on the previous kernel
+      for (int c = 0; c < first; ++c) {
+        uint8_t* st = dsm + (size_t)c * kSkStageBytes;
+        mbar_expect_tx(&full[c], kSkAPacked + kSkLimbs * b_bytes);
+        bulk_g2s(st + kSkAConv, a_src + (size_t)c * kGroupTiles * kWarp, kSkAPacked, &full[c]);
+      }
+      pdl_wait();  // the limbs are the quantiser's output
+      for (int c = 0; c < first; ++c) {
+        uint8_t* st = dsm + (size_t)c * kSkStageBytes + kSkAConv + kSkAPacked;
+        for (int l = 0; l < kSkLimbs; ++l)
+          bulk_g2s(st + l * b_bytes, b_src + ((size_t)c * kSkLimbs + l) * kSkPlane, b_bytes,
+                   &full[c]);
+      }
+      int c = first;
+      for (; c < n_loc; ++c) {
+        const int s = c % kSkStages;
+        if (!mbar_wait(&empty[s], ((c / kSkStages) - 1) & 1)) {
+          atomicOr(p.err, kErrWaitTimeout);
+          s_bad = 1;
+          break;
+        }
+        uint8_t* st = dsm + (size_t)s * kSkStageBytes;
+        mbar_expect_tx(&full[s], kSkAPacked + kSkLimbs * b_bytes);
+        bulk_g2s(st + kSkAConv, a_src + (size_t)c * kGroupTiles * kWarp, kSkAPacked, &full[s]);
+        for (int l = 0; l < kSkLimbs; ++l)
+          bulk_g2s(st + kSkAConv + kSkAPacked + l * b_bytes,
+                   b_src + ((size_t)c * kSkLimbs + l) * kSkPlane, b_bytes, &full[s]);
+      }
+      if (s_bad) {
+        // let the copies already issued land before the CTA can exit
+        for (int j = c - 1; j >= 0 && j >= c - kSkStages; --j)
+          if (!mbar_wait(&full[j % kSkStages], (j / kSkStages) & 1)) break;
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------ MMA issuer --
+    if (lane == 0) {
+      const uint32_t idesc = idesc_i8(128, N);
+      for (int c = 0; c < n_loc; ++c) {
+        const int s = c % kSkStages;
+        const uint32_t ph = (c / kSkStages) & 1;
+        if (!mbar_wait(&full[s], ph) || !mbar_wait(&conv[s], ph)) {
+          atomicOr(p.err, kErrWaitTimeout);
+          s_bad = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t a0 = smem_u32(dsm + (size_t)s * kSkStageBytes);
+        const uint32_t b0 = a0 + kSkAConv + kSkAPacked;
+#pragma unroll
+        for (int kk = 0; kk < 2; ++kk) {
+          const uint64_t da = umma_desc(a0 + kk * 256, kSkLbo, kSkSbo);
+#pragma unroll
+          for (int l = 0; l < kSkLimbs; ++l)
+            umma_i8(tmem + l * N, da, umma_desc(b0 + l * b_bytes + kk * 256, kSkLbo, kSkSbo),
+                    idesc, (c | kk) != 0);
+        }
+        umma_commit(&empty[s]);
+      }
+      umma_commit(&done);  // arrives when every MMA issued above has finished
+    }
+  } else {
+    // ---------------------------------------------- nibble unpacking --
+    // thread ci: tile ci / 32 of the group, fragment lane (g, t) = ci % 32;
+    // low nibbles are tile row g (A row 16 tile + g), high nibbles row g + 8.
+    const int ci = threadIdx.x - 2 * kWarp;
+    const int tl = ci >> 5, g = (ci & 31) >> 2, t = ci & 3;
+    for (int c = 0; c < n_loc; ++c) {
+      const int s = c % kSkStages;
+      if (!mbar_wait(&full[s], (c / kSkStages) & 1)) {
+        atomicOr(p.err, kErrWaitTimeout);
+        s_bad = 1;
+        break;
+      }
+      uint8_t* st = dsm + (size_t)s * kSkStageBytes;
+      const uint4 wv = lds_u4(reinterpret_cast<const uint4*>(st + kSkAConv) + ci);
+      uint8_t* ac = st + g * 16 + 4 * t;
+      const uint32_t wd[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+        // (u + 0x78) ^ 0x80 per byte = two's complement of u - 8 (no carries)
+        const uint32_t lo = ((wd[w] & 0x0F0F0F0Fu) + 0x78787878u) ^ 0x80808080u;
+        const uint32_t hi = (((wd[w] >> 4) & 0x0F0F0F0Fu) + 0x78787878u) ^ 0x80808080u;
+        sts_u32(ac + ((2 * tl) * 4 + w) * 128, lo);
+        sts_u32(ac + ((2 * tl + 1) * 4 + w) * 128, hi);
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&conv[s]);
+    }
+  }
+
+  // ------------------------------------------------------------ epilogue --
+  // Warps 2-5: tensor-memory lanes 32 (warp % 4) .. +31 = A rows = the
+  // group's output columns 32 (warp % 4) + lane; lane ^ 8 holds the partner
+  // row (g <-> g + 8) of the same 16-column tile.
+  const bool epi_warp = warp >= 2 && warp < 6;
+  const int quad = warp & 3;
+  const int arow = quad * kWarp + lane;                // A row in the group
+  const int tile = group * kGroupTiles + (arow >> 4);
+  const int g = arow & 7;
+  const bool owner = (arow & 8) == 0;                  // holds tile row g, gets g + 8
+  float* S = reinterpret_cast<float*>(dsm);            // [N][kSkRowS] partial (cluster mode)
+  bool ok = true;
+  if (epi_warp) {
+    pdl_wait();
+    ok = mbar_wait(&done, 0);
+    tc_fence_after();
+    if (!ok && lane == 0) atomicOr(p.err, kErrWaitTimeout);
+  }
+  // the finished sums of this thread's column for rows m0 .. m0 + 15
+  auto column_rows = [&](int m0, float (&v)[16]) {
+    uint32_t a0[16], a1[16], a2[16];
+    const uint32_t ta = tmem + ((uint32_t)(quad * kWarp) << 16) + m0;
+    tmem_ld16(ta, a0);
+    tmem_ld16(ta + N, a1);
+    tmem_ld16(ta + 2 * N, a2);
+    tmem_wait_ld();
+#pragma unroll
+    for (int q = 0; q < 16; ++q) {
+      const int m = m0 + q;
+      const long long iv = (long long)(int)a0[q] + 256LL * (long long)(int)a1[q] +
+                           65536LL * (long long)(int)a2[q];
+      v[q] = m < p.M ? (float)iv * p.rowf[m].x : 0.f;
+    }
+  };
+  auto finish_row = [&](int m, float v) {
+    // every lane of the warp takes part (the partner shuffle); owners of a
+    // live tile run the fused epilogue
+    const float v1 = __shfl_xor_sync(0xffffffffu, v, 8);
+    float sq = 0.f;
+    if (owner && tile < p.n_tiles) epilogue_row(p, tile, g, m, v, v1, p.rowf[m].y, sq);
+    if (p.epi == kEpiResid && p.out_stats) {
+      sq += __shfl_xor_sync(0xffffffffu, sq, 1);
+      sq += __shfl_xor_sync(0xffffffffu, sq, 2);
+      sq += __shfl_xor_sync(0xffffffffu, sq, 4);
+      if ((arow & 15) == 0 && tile < p.n_tiles) p.out_stats[(size_t)tile * p.M + m] = sq;
+    }
+  };
+
+  if (!cl) {
+    if (epi_warp && ok && !s_bad) {
+      for (int m0 = 0; m0 < N; m0 += 16) {
+        float v[16];
+        column_rows(m0, v);
+#pragma unroll
+        for (int q = 0; q < 16; ++q)
+          if (m0 + q < p.M) finish_row(m0 + q, v[q]);  // warp-uniform
+      }
+    }
+  } else {
+    // ---- k-slices as one cluster: stage, exchange, finish rows m = r mod ks
+    if (epi_warp && ok) {
+      for (int m0 = 0; m0 < N; m0 += 16) {
+        float v[16];
+        column_rows(m0, v);
+#pragma unroll
+        for (int q = 0; q < 16; ++q) S[(m0 + q) * kSkRowS + arow] = v[q];
+      }
+    }
+    if (epi_warp && !ok && lane == 0) s_bad = 1;
+    __syncthreads();  // every epilogue warp's flag and stores are in place
+    cluster_arrive();
+    cluster_wait();   // every CTA's partial and flag are in its shared memory
+    if (epi_warp) {
+      const uint32_t bad0 = smem_u32(const_cast<int*>(&s_bad));
+      int any = 0;
+      for (int r = 0; r < p.ksplit; ++r) any |= ld_dsmem_s32(dsmem_addr(bad0, (uint32_t)r));
+      if (!any) {
+        const uint32_t s0 = smem_u32(S);
+        for (int m = kidx; m < p.M; m += p.ksplit) {  // warp-uniform
+          float acc = 0.f;
+#pragma unroll
+          for (int r = 0; r < kSkMaxCluster; ++r)
+            if (r < p.ksplit)
+              acc += ld_dsmem(dsmem_addr(s0, (uint32_t)r) + 4u * (m * kSkRowS + arow));
+          finish_row(m, acc);
+        }
+      }
+    }
+    cluster_arrive();  // done reading the other CTAs' partials
+    cluster_wait();    // ... and they are done reading this one's
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    // no MMA may still write the columns being freed (bounded, as every wait)
+    mbar_wait(&done, 0);
+    tc_fence_after();
+    tmem_dealloc(tmem, kSkCols);
+  }
+}
+
+// Rows quantised by quant_rows_kernel (only the first roundup(M, 16) rows of
+// the limb planes are read), then the GEMM; both with PDL.
+cudaError_t launch_gemm_sk(const GemvParams& p, cudaStream_t s, bool pdl) {
+  const int N = (p.M + 15) / 16 * 16;
+  if (p.M < 1 || N > kSkMaxN || p.ksplit < 1 || p.ksplit > kSkMaxCluster || p.kseg % kChunkK ||
+      p.kseg <= 0 || (long long)p.kseg * (p.ksplit - 1) >= p.K)
+    return cudaErrorInvalidConfiguration;
+  if (p.K % kChunkK || !p.lq || !p.rowf || !p.x || (p.ldx & 3) || ((uintptr_t)p.x & 15) ||
+      ((uintptr_t)p.lq & 15) || ((uintptr_t)p.rowf & 7))
+    return cudaErrorInvalidConfiguration;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaError_t e = launch_quant_rows(p, N, s, pdl);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(padded_tiles(p.n_tiles) / kGroupTiles, 1, p.ksplit);
+  cfg.blockDim = dim3(kSkThreads);
+  cfg.dynamicSmemBytes = kSkSmem;
+  cfg.stream = s;
+  int na = 1;  // the quantiser just before it is always a PDL-aware kernel
+  if (p.ksplit > 1) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = 1;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = (unsigned)p.ksplit;
+    ++na;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  return cudaLaunchKernelEx(&cfg, gemm_sk_kernel, p, N);
+}
+
+cudaError_t prepare_gemm_sk() {
+  return cudaFuncSetAttribute(gemm_sk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              (int)kSkSmem);
+}
+
+}  // namespace ms

@@ -499,6 +499,26 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const GemvParams
   }
 }
 
+// The first `rows` rows (a multiple of 8; rows >= M written as zeros) of the
+// limb planes and their row factors.
+cudaError_t launch_quant_rows(const GemvParams& p, int rows, cudaStream_t s, bool pdl) {
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  // k slices so that a small batch still has about one CTA per SM (each
+  // slice re-reads the rows for their maximum, so large batches keep one)
+  const int groups = rows / 8, nsub = p.K / 16;
+  int ks = (148 + groups - 1) / groups;
+  ks = ks < 1 ? 1 : (ks > nsub / 32 ? (nsub / 32 > 0 ? nsub / 32 : 1) : ks);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(groups, ks);
+  cfg.blockDim = dim3(kQThreads);
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, quant_rows_kernel, p);
+}
+
 cudaError_t launch_gemm_tc(const GemvParams& p, cudaStream_t s, bool pdl) {
   if (p.ksplit < 1 || p.kseg % kChunkK || p.kseg <= 0 || (p.ksplit > 1 && (!p.part || !p.counters)) ||
       (long long)p.kseg * (p.ksplit - 1) >= p.K)
@@ -510,21 +530,8 @@ cudaError_t launch_gemm_tc(const GemvParams& p, cudaStream_t s, bool pdl) {
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   const int m_pad = tc_rows_pad(p.M);
-  {
-    // k slices so that a small batch still has about one CTA per SM (each
-    // slice re-reads the rows for their maximum, so large batches keep one)
-    const int groups = m_pad / 8, nsub = p.K / 16;
-    int ks = (148 + groups - 1) / groups;
-    ks = ks < 1 ? 1 : (ks > nsub / 32 ? (nsub / 32 > 0 ? nsub / 32 : 1) : ks);
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(groups, ks);
-    cfg.blockDim = dim3(kQThreads);
-    cfg.stream = s;
-    cfg.attrs = attr;
-    cfg.numAttrs = pdl ? 1 : 0;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, quant_rows_kernel, p);
-    if (e != cudaSuccess) return e;
-  }
+  cudaError_t e = launch_quant_rows(p, m_pad, s, pdl);
+  if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(padded_tiles(p.n_tiles) / kGroupTiles, m_pad / kTcBM, p.ksplit);
   cfg.blockDim = dim3(kTcThreads);

@@ -158,6 +158,13 @@ size_t gemv_stream_smem(int mg, int kseg);
 // tcgen05 path (prefill / large batches): quantiser + GEMM, two launches
 cudaError_t launch_gemm_tc(const GemvParams& p, cudaStream_t s, bool pdl);
 int tc_rows_pad(int M);
+// rows of limb planes + factors (quantiser only; the GEMMs launch it themselves)
+cudaError_t launch_quant_rows(const GemvParams& p, int rows, cudaStream_t s, bool pdl);
+// decode batches of 9..sk_rows_max() rows: weights on the MMA's 128-row side,
+// k-slices (<= 8) merged inside a thread-block cluster; quantiser + GEMM
+cudaError_t launch_gemm_sk(const GemvParams& p, cudaStream_t s, bool pdl);
+cudaError_t prepare_gemm_sk();
+int sk_rows_max();
 size_t tc_limb_bytes(int M, int K);
 cudaError_t launch_attention(const AttnParams& p, cudaStream_t s, bool pdl);
 // tiled attention for prefill: one CTA per (query block, KV head)
