@@ -35,18 +35,13 @@ import numpy as np
 import pytest
 
 from mojostream_b200.model import ModelSpec, b14_spec, e4b_spec, synth_weights
+from parity_util import layer_step, rel_rmse, to_dev
 
 pytestmark = pytest.mark.gpu
 
 LAYER_TOL = 1e-4
 LOGIT_TOL = 1e-3
 TIE_REL = 1e-5
-
-
-def rel_rmse(a, b):
-    a = np.asarray(a, np.float64)
-    b = np.asarray(b, np.float64)
-    return float(np.sqrt(((a - b) ** 2).mean()) / (np.sqrt((b ** 2).mean()) + 1e-12))
 
 
 @pytest.fixture(scope="module")
@@ -65,35 +60,6 @@ def ctx(torch_cuda):
     c.close()
 
 
-def to_dev(torch, a):
-    return torch.from_numpy(np.ascontiguousarray(a, np.float32)).cuda()
-
-
-def sync_kv_rows(torch, kv, om, layer, seq, pos, bf16):
-    """The K / V rows the GPU just wrote for (seq, pos) against the oracle's
-    own: within 1e-5 of the row's largest magnitude (fp32 noise of the
-    projection), plus for a bf16 cache one bfloat16 rounding step of the
-    element (a value within fp32 noise of a rounding boundary rounds
-    differently on the two sides).  The oracle's rows are then replaced by
-    the GPU's; returns how many elements differed."""
-    ls = om.spec.layers[layer]
-    kb, vb = om.kv_arrays(layer)
-    flips = 0
-    for s, p in zip(seq, pos):
-        kg, vg = kv.read(layer, s, p, 1, ls.kv_dim)
-        kg, vg = kg.cpu().numpy()[0], vg.cpu().numpy()[0]
-        slot = p % kb.shape[1] if ls.window > 0 else p
-        for g, o in ((kg, kb[s, slot]), (vg, vb[s, slot])):
-            d = np.abs(g.astype(np.float64) - o)
-            lim = (2.0 ** -7 if bf16 else 0.0) * np.maximum(np.abs(o), np.abs(g)) \
-                + 1e-5 * float(np.abs(o).max()) + 1e-30
-            assert (d <= lim).all(), (layer, s, p, float((d / lim).max()))
-            flips += int((g != o).sum())
-        kb[s, slot] = kg
-        vb[s, slot] = vg
-    return flips
-
-
 def teacher_forced(torch, model, kv, om, calls, x_of, label, kv_sync=None, quiet=False):
     """Every call (seq list, pos list) runs every layer on both sides with the
     same input rows (x_of(call index, seq, pos) gives the first layer's input;
@@ -108,18 +74,9 @@ def teacher_forced(torch, model, kv, om, calls, x_of, label, kv_sync=None, quiet
     for ci, (seq, pos) in enumerate(calls):
         x = x_of(ci, seq, pos)
         for l in range(model.spec.n_layers):
-            xg = to_dev(torch, x)
-            model.layer_forward(l, xg, kv, seq, pos)
-            y = om.layer_forward(l, x, seq, pos)
-            torch.cuda.synchronize()
-            if kv_sync:
-                f = sync_kv_rows(torch, kv, om, l, seq, pos, kv_sync == "bf16")
-                if f:
-                    flips += f
-                    om.set_kv_frozen(True)
-                    y = om.layer_forward(l, x, seq, pos)
-                    om.set_kv_frozen(False)
-            err = rel_rmse(xg.cpu().numpy(), y)
+            got, y, f = layer_step(torch, model, kv, om, l, x, seq, pos, kv_sync)
+            flips += f
+            err = rel_rmse(got, y)
             errs.append(err)
             worst = max(worst, err)
             assert err <= LAYER_TOL, (label, ci, l, err)
