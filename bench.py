@@ -396,7 +396,7 @@ def run_ours(args, ws, rank, local):
             result["demo"] = run_demo_block(args, local)
             result["q4_sweep"] = run_q4_sweep(local)
         result["tp"] = run_tp_block(args, ws, rank, local, D)
-    if rank == 0 and not args.no_cpu_baseline:
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(spec, args)
     if rank == 0:
         print(json.dumps(result), flush=True)
