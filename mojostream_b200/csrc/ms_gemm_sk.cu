@@ -24,8 +24,7 @@
 // stages with cp.async.bulk (4 KB packed nibbles + the N rows of the three
 // limb planes per 64-k chunk; the weight copies of the first stages go out
 // before griddepcontrol.wait, since no earlier kernel writes them); warp 1
-// allocates 256 tensor-memory columns and one thread issues the MMAs (8
-// stages of 24 KB: one CTA per SM, 8 chunks of weights and limbs in flight);
+// allocates 256 tensor-memory columns and one thread issues the MMAs;
 // warps 2-9 unpack nibbles into the A operand; warps 2-5 run the epilogue
 // (tensor-memory lane = output column, columns = batch rows).  The k-slices
 // of a group run as one thread-block cluster (<= 8 CTAs): each leaves its
@@ -39,7 +38,7 @@
 
 namespace ms {
 
-constexpr int kSkStages = 8;  // 192 KB: one CTA per SM, 8 chunks in flight
+constexpr int kSkStages = 4;
 constexpr int kSkLimbs = 3;
 constexpr int kSkMaxN = 64;                                // batch rows per launch
 constexpr int kSkAConv = 128 * kChunkK;                    // 8 KB: s8 weights, 128 x 64
@@ -60,7 +59,7 @@ static_assert((size_t)kSkMaxN * kSkRowS * 4 <= kSkSmem, "staged partial fits the
 
 int sk_rows_max() { return kSkMaxN; }
 
-__global__ void __launch_bounds__(kSkThreads, 1) gemm_sk_kernel(const GemvParams p, int N) {
+__global__ void __launch_bounds__(kSkThreads, 2) gemm_sk_kernel(const GemvParams p, int N) {
   extern __shared__ __align__(1024) uint8_t dsm[];
   __shared__ __align__(8) uint64_t full[kSkStages], conv[kSkStages], empty[kSkStages], done;
   __shared__ uint32_t s_tmem;
