@@ -25,7 +25,7 @@
 // limb planes per 64-k chunk; the weight copies of the first stages go out
 // before griddepcontrol.wait, since no earlier kernel writes them); warp 1
 // allocates 256 tensor-memory columns and one thread issues the MMAs;
-// warps 2-9 unpack nibbles into the A operand; warps 2-5 run the epilogue
+// warps 2-9 unpack nibbles into the A operand and then run the epilogue
 // (tensor-memory lane = output column, columns = batch rows).  The k-slices
 // of a group run as one thread-block cluster (<= 8 CTAs): each leaves its
 // partial tile in shared memory and CTA r finishes the rows m = r (mod
@@ -193,22 +193,31 @@ __global__ void __launch_bounds__(kSkThreads, 2) gemm_sk_kernel(const GemvParams
   }
 
   // ------------------------------------------------------------ epilogue --
-  // Warps 2-5: tensor-memory lanes 32 (warp % 4) .. +31 = A rows = the
-  // group's output columns 32 (warp % 4) + lane; lane ^ 8 holds the partner
-  // row (g <-> g + 8) of the same 16-column tile.
-  const bool epi_warp = warp >= 2 && warp < 6;
-  const int quad = warp & 3;
+  // Warps 2-9, two per tensor-memory lane quarter: warp w reads lanes
+  // 32 (w % 4) .. +31 = A rows = the group's output columns 32 (w % 4) +
+  // lane, and the two warps of a quarter share the batch rows (half = which
+  // one).  Lane ^ 8 holds the partner row (g <-> g + 8) of the same
+  // 16-column tile.  The row factors (the quantiser's output) are read once
+  // into shared memory; residual loads are issued kRB rows at a time.
+  constexpr int kRB = 4;
+  __shared__ float2 s_rowf[kSkMaxN];
+  const bool epi_warp = warp >= 2;
+  const int quad = warp & 3, half = (warp - 2) >> 2;
   const int arow = quad * kWarp + lane;                // A row in the group
   const int tile = group * kGroupTiles + (arow >> 4);
+  const bool tile_ok = tile < p.n_tiles;
   const int g = arow & 7;
   const bool owner = (arow & 8) == 0;                  // holds tile row g, gets g + 8
   float* S = reinterpret_cast<float*>(dsm);            // [N][kSkRowS] partial (cluster mode)
   bool ok = true;
   if (epi_warp) {
     pdl_wait();
+    for (int m = threadIdx.x - 2 * kWarp; m < N; m += kSkConvWarps * kWarp)
+      s_rowf[m] = m < p.M ? p.rowf[m] : make_float2(0.f, 0.f);
     ok = mbar_wait(&done, 0);
     tc_fence_after();
     if (!ok && lane == 0) atomicOr(p.err, kErrWaitTimeout);
+    bar_sync_n(1, kSkConvWarps * kWarp);  // s_rowf complete
   }
   // the finished sums of this thread's column for rows m0 .. m0 + 15
   auto column_rows = [&](int m0, float (&v)[16]) {
@@ -220,40 +229,80 @@ __global__ void __launch_bounds__(kSkThreads, 2) gemm_sk_kernel(const GemvParams
     tmem_wait_ld();
 #pragma unroll
     for (int q = 0; q < 16; ++q) {
-      const int m = m0 + q;
       const long long iv = (long long)(int)a0[q] + 256LL * (long long)(int)a1[q] +
                            65536LL * (long long)(int)a2[q];
-      v[q] = m < p.M ? (float)iv * p.rowf[m].x : 0.f;
+      v[q] = (float)iv * s_rowf[m0 + q].x;
     }
   };
-  auto finish_row = [&](int m, float v) {
-    // every lane of the warp takes part (the partner shuffle); owners of a
-    // live tile run the fused epilogue
-    const float v1 = __shfl_xor_sync(0xffffffffu, v, 8);
-    float sq = 0.f;
-    if (owner && tile < p.n_tiles) epilogue_row(p, tile, g, m, v, v1, p.rowf[m].y, sq);
-    if (p.epi == kEpiResid && p.out_stats) {
-      sq += __shfl_xor_sync(0xffffffffu, sq, 1);
-      sq += __shfl_xor_sync(0xffffffffu, sq, 2);
-      sq += __shfl_xor_sync(0xffffffffu, sq, 4);
-      if ((arow & 15) == 0 && tile < p.n_tiles) p.out_stats[(size_t)tile * p.M + m] = sq;
+  // rows m_first + m_step i (i < cnt <= 16) with their sums v[i]; every lane
+  // of the warp takes part (partner shuffle, statistics), owners of a live
+  // tile write.  kEpiResid: the arithmetic of epilogue_row with the residual
+  // values loaded ahead, kRB rows at a time.
+  auto finish_rows = [&](int m_first, int m_step, int cnt, const float (&v)[16]) {
+    const bool resid = p.epi == kEpiResid;
+#pragma unroll
+    for (int i0 = 0; i0 < 16; i0 += kRB) {
+      if (i0 >= cnt) break;  // warp-uniform
+      float rr[kRB][2];
+#pragma unroll
+      for (int j = 0; j < kRB; ++j) {
+        rr[j][0] = rr[j][1] = 0.f;
+        const int m = m_first + m_step * (i0 + j);
+        if (resid && owner && tile_ok && i0 + j < cnt) {
+          const float* r = p.resid + (size_t)m * p.ldr + tile * kTileN + g;
+          rr[j][0] = __ldcg(r);
+          rr[j][1] = __ldcg(r + 8);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < kRB; ++j) {
+        if (i0 + j >= cnt) break;  // warp-uniform
+        const int m = m_first + m_step * (i0 + j);
+        const float v0 = v[i0 + j];
+        const float v1 = __shfl_xor_sync(0xffffffffu, v0, 8);
+        float sq = 0.f;
+        if (owner && tile_ok) {
+          if (resid) {
+            const float inv_res = s_rowf[m].y;
+            const float a = (rr[j][0] * p.resid_ple) * inv_res + p.scale * v0;
+            const float b = (rr[j][1] * p.resid_ple) * inv_res + p.scale * v1;
+            float* o = p.out + (size_t)m * p.ldo + tile * kTileN + g;
+            o[0] = a;
+            o[8] = b;
+            sq = a * a + b * b;
+          } else {
+            epilogue_row(p, tile, g, m, v0, v1, s_rowf[m].y, sq);
+          }
+        }
+        if (resid && p.out_stats) {
+          sq += __shfl_xor_sync(0xffffffffu, sq, 1);
+          sq += __shfl_xor_sync(0xffffffffu, sq, 2);
+          sq += __shfl_xor_sync(0xffffffffu, sq, 4);
+          if ((arow & 15) == 0 && tile_ok) p.out_stats[(size_t)tile * p.M + m] = sq;
+        }
+      }
     }
   };
 
   if (!cl) {
+    // each 16-row block: half 0 finishes rows 0-7, half 1 rows 8-15
     if (epi_warp && ok && !s_bad) {
       for (int m0 = 0; m0 < N; m0 += 16) {
         float v[16];
         column_rows(m0, v);
+        float w[16];
 #pragma unroll
-        for (int q = 0; q < 16; ++q)
-          if (m0 + q < p.M) finish_row(m0 + q, v[q]);  // warp-uniform
+        for (int q = 0; q < 8; ++q) w[q] = v[8 * half + q];
+#pragma unroll
+        for (int q = 8; q < 16; ++q) w[q] = 0.f;
+        const int mf = m0 + 8 * half;
+        finish_rows(mf, 1, max(0, min(8, p.M - mf)), w);
       }
     }
   } else {
     // ---- k-slices as one cluster: stage, exchange, finish rows m = r mod ks
     if (epi_warp && ok) {
-      for (int m0 = 0; m0 < N; m0 += 16) {
+      for (int m0 = 16 * half; m0 < N; m0 += 32) {
         float v[16];
         column_rows(m0, v);
 #pragma unroll
@@ -269,15 +318,24 @@ __global__ void __launch_bounds__(kSkThreads, 2) gemm_sk_kernel(const GemvParams
       int any = 0;
       for (int r = 0; r < p.ksplit; ++r) any |= ld_dsmem_s32(dsmem_addr(bad0, (uint32_t)r));
       if (!any) {
+        // this CTA's rows m = kidx + ks i, alternately to the two halves:
+        // rows m_first + m_step j, j < cnt (<= 16: 64 rows, >= 2 slices)
+        const int m_first = kidx + p.ksplit * half, m_step = 2 * p.ksplit;
+        const int cnt = m_first < p.M ? (p.M - m_first + m_step - 1) / m_step : 0;
         const uint32_t s0 = smem_u32(S);
-        for (int m = kidx; m < p.M; m += p.ksplit) {  // warp-uniform
-          float acc = 0.f;
+        float v[16];
 #pragma unroll
-          for (int r = 0; r < kSkMaxCluster; ++r)
-            if (r < p.ksplit)
-              acc += ld_dsmem(dsmem_addr(s0, (uint32_t)r) + 4u * (m * kSkRowS + arow));
-          finish_row(m, acc);
+        for (int j = 0; j < 16; ++j) {
+          v[j] = 0.f;
+          if (j < cnt) {
+            const int m = m_first + m_step * j;
+#pragma unroll
+            for (int r = 0; r < kSkMaxCluster; ++r)
+              if (r < p.ksplit)
+                v[j] += ld_dsmem(dsmem_addr(s0, (uint32_t)r) + 4u * (m * kSkRowS + arow));
+          }
         }
+        finish_rows(m_first, m_step, cnt, v);
       }
     }
     cluster_arrive();  // done reading the other CTAs' partials

@@ -62,10 +62,12 @@ size_t tc_limb_bytes(int M, int K) { return (size_t)tc_rows_pad(M) * K * kTcLimb
 // 16-k subtile (t = j / 4, e = j % 4): the order of the weight words.
 // rowf[m] = {(a / 2^22) * fin, fres}: the factors the epilogue applies.
 // CTA (row group, k slice): 8 rows, 256 threads; thread (row tid % 8,
-// subtile tid / 8 + 32 j).  Every CTA of a row group takes the maximum over
-// the whole row (so small batches still spread over many CTAs) and
-// quantises its slice of the subtiles; slice 0 writes the row factors.
-// Rows >= M are written as zeros.
+// subtile tid / 8 + 32 j).  The k slices of a row group (up to 8, so small
+// batches still spread over many CTAs) run as one thread-block cluster: each
+// CTA takes the maximum over its own slice, the row maxima are exchanged
+// through distributed shared memory, and every CTA quantises its slice with
+// the whole row's maximum; slice 0 writes the row factors.  Rows >= M are
+// written as zeros.
 constexpr int kQThreads = 256;
 __global__ void __launch_bounds__(kQThreads) quant_rows_kernel(const GemvParams p) {
   __shared__ float s_max[kQThreads / kWarp][8];
@@ -81,7 +83,7 @@ __global__ void __launch_bounds__(kQThreads) quant_rows_kernel(const GemvParams 
   const float* x = p.x + (size_t)(live ? m : 0) * p.ldx;
   float a = 0.f;
   if (live)
-    for (int i = sub0; i < nsub; i += kQThreads / 8) {
+    for (int i = s_begin + sub0; i < s_end; i += kQThreads / 8) {
       const float4* v4 = reinterpret_cast<const float4*>(x + 16 * i);
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
@@ -96,6 +98,17 @@ __global__ void __launch_bounds__(kQThreads) quant_rows_kernel(const GemvParams 
   __syncthreads();
 #pragma unroll
   for (int w = 0; w < kQThreads / kWarp; ++w) a = fmaxf(a, s_max[w][r8]);
+  if (gridDim.y > 1) {
+    // the other slices' maxima of these rows (the slices are one cluster)
+    __shared__ float s_slice_max[8];
+    if (threadIdx.x < 8) s_slice_max[threadIdx.x] = a;  // thread r8 = threadIdx.x
+    cluster_arrive();
+    cluster_wait();
+    const uint32_t m0 = smem_u32(&s_slice_max[r8]);
+    for (uint32_t r = 0; r < gridDim.y; ++r) a = fmaxf(a, ld_dsmem(dsmem_addr(m0, r)));
+    cluster_arrive();  // done reading the other CTAs' maxima
+    cluster_wait();
+  }
   const float inv = a > 0.f ? kTcQuantOne / a : 0.f;
 
   // RMSNorm factors from the per-tile sums of squares: the 32 threads of a
@@ -510,12 +523,22 @@ cudaError_t launch_quant_rows(const GemvParams& p, int rows, cudaStream_t s, boo
   const int groups = rows / 8, nsub = p.K / 16;
   int ks = (148 + groups - 1) / groups;
   ks = ks < 1 ? 1 : (ks > nsub / 32 ? (nsub / 32 > 0 ? nsub / 32 : 1) : ks);
+  ks = ks > 8 ? 8 : ks;  // the slices of a row group form one (portable) cluster
+  cudaLaunchAttribute attr2[2] = {attr[0], {}};
+  int na = pdl ? 1 : 0;
+  if (ks > 1) {
+    attr2[na].id = cudaLaunchAttributeClusterDimension;
+    attr2[na].val.clusterDim.x = 1;
+    attr2[na].val.clusterDim.y = (unsigned)ks;
+    attr2[na].val.clusterDim.z = 1;
+    ++na;
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(groups, ks);
   cfg.blockDim = dim3(kQThreads);
   cfg.stream = s;
-  cfg.attrs = attr;
-  cfg.numAttrs = pdl ? 1 : 0;
+  cfg.attrs = attr2;
+  cfg.numAttrs = na;
   return cudaLaunchKernelEx(&cfg, quant_rows_kernel, p);
 }
 
