@@ -23,6 +23,16 @@ namespace ms {
 constexpr int kLmThreads = 128;  // CTA size of the 4-row pass (decode batches)
 constexpr int kLmUnroll = 8;
 
+// d = a * b + c on two lanes of fp32 at once (sm_100's packed FMA: each
+// element rounds exactly as fmaf does, one instruction for both).
+__device__ __forceinline__ void fma2(float2& d, float2 a, float2 b) {
+  unsigned long long& dd = reinterpret_cast<unsigned long long&>(d);
+  asm("fma.rn.f32x2 %0, %1, %2, %0;"
+      : "+l"(dd)
+      : "l"(reinterpret_cast<const unsigned long long&>(a)),
+        "l"(reinterpret_cast<const unsigned long long&>(b)));
+}
+
 __device__ __forceinline__ void argmax_merge(float& v, int& i, float v2, int i2) {
   if (v2 > v || (v2 == v && i2 < i)) {
     v = v2;
@@ -76,9 +86,11 @@ __global__ void __launch_bounds__(NT) lm_head_kernel(const LmHeadParams p, int r
   }
   __syncthreads();
 
-  float acc[MR][4];
+  // accumulators of columns (col, col + 1) and (col + 2, col + 3), packed
+  // FMAs over the k order of the reference's loop
+  float2 acc2[MR][2];
 #pragma unroll
-  for (int r = 0; r < MR; ++r) acc[r][0] = acc[r][1] = acc[r][2] = acc[r][3] = 0.f;
+  for (int r = 0; r < MR; ++r) acc2[r][0] = acc2[r][1] = make_float2(0.f, 0.f);
   if (col_ok) {
     int k0 = 0;
     for (; k0 + LU <= p.D; k0 += LU) {
@@ -92,27 +104,35 @@ __global__ void __launch_bounds__(NT) lm_head_kernel(const LmHeadParams p, int r
           pre[u] = ld_stream_f4(reinterpret_cast<const float4*>(p.W + (size_t)(kn + u) * p.V + col));
 #pragma unroll
       for (int u = 0; u < LU; ++u) {
+        const float2 wl = make_float2(w[u].x, w[u].y), wh = make_float2(w[u].z, w[u].w);
 #pragma unroll
         for (int r = 0; r < MR; ++r) {
           const float a = xs[r * p.D + k0 + u];
-          acc[r][0] = fmaf(a, w[u].x, acc[r][0]);
-          acc[r][1] = fmaf(a, w[u].y, acc[r][1]);
-          acc[r][2] = fmaf(a, w[u].z, acc[r][2]);
-          acc[r][3] = fmaf(a, w[u].w, acc[r][3]);
+          const float2 aa = make_float2(a, a);
+          fma2(acc2[r][0], aa, wl);
+          fma2(acc2[r][1], aa, wh);
         }
       }
     }
     for (int u = 0; k0 + u < p.D; ++u) {  // D not a multiple of the unroll
       const float4 w = pre[u];
+      const float2 wl = make_float2(w.x, w.y), wh = make_float2(w.z, w.w);
 #pragma unroll
       for (int r = 0; r < MR; ++r) {
         const float a = xs[r * p.D + k0 + u];
-        acc[r][0] = fmaf(a, w.x, acc[r][0]);
-        acc[r][1] = fmaf(a, w.y, acc[r][1]);
-        acc[r][2] = fmaf(a, w.z, acc[r][2]);
-        acc[r][3] = fmaf(a, w.w, acc[r][3]);
+        const float2 aa = make_float2(a, a);
+        fma2(acc2[r][0], aa, wl);
+        fma2(acc2[r][1], aa, wh);
       }
     }
+  }
+  float acc[MR][4];
+#pragma unroll
+  for (int r = 0; r < MR; ++r) {
+    acc[r][0] = acc2[r][0].x;
+    acc[r][1] = acc2[r][0].y;
+    acc[r][2] = acc2[r][1].x;
+    acc[r][3] = acc2[r][1].y;
   }
 
   // logits (optional) and the per-CTA argmax of every row
