@@ -1704,8 +1704,10 @@ static ms_status run_layer(ms_ctx* c, ms_model* m, const ms_kv* kv, int li, int 
   //    partial sums, all-reduce, then the residual)
   const bool tp = c->tp_world > 1;
   {
-    // tensor parallel: the prefill GEMM, whose epilogue sums the ranks' tiles
-    GemvPlan pl = plan_gemv(c, M, L.q_dim, D / kTileN, true, !tp);
+    // tensor parallel: the decode-batch kernel sums the ranks' tiles in its
+    // cluster epilogue (so it needs k-slices), the prefill GEMM in its own
+    GemvPlan pl = plan_gemv(c, M, L.q_dim, D / kTileN);
+    if (tp && pl.sk && pl.ksplit < 2) pl = plan_gemv(c, M, L.q_dim, D / kTileN, true, false);
     GemvParams p = gemv_base(c, L.wo, D / kTileN, L.q_dim, M, pl);
     p.lq = m->lq;
     p.rowf = m->rowf;
@@ -1761,7 +1763,8 @@ static ms_status run_layer(ms_ctx* c, ms_model* m, const ms_kv* kv, int li, int 
   }
   // 5. Down + residual
   {
-    GemvPlan pl = plan_gemv(c, M, F, D / kTileN, true, !tp);
+    GemvPlan pl = plan_gemv(c, M, F, D / kTileN);
+    if (tp && pl.sk && pl.ksplit < 2) pl = plan_gemv(c, M, F, D / kTileN, true, false);
     GemvParams p = gemv_base(c, L.wd, D / kTileN, F, M, pl);
     p.lq = m->lq;
     p.rowf = m->rowf;

@@ -30,7 +30,11 @@
 // of a group run as one thread-block cluster (<= 8 CTAs): each leaves its
 // partial tile in shared memory and CTA r finishes the rows m = r (mod
 // slices), summing the slices in k order through distributed shared memory
-// (the same order on every run).  Every wait is bounded (error word).
+// (the same order on every run).  Tensor parallel (O / down): the finished
+// rows go to this rank's peer-visible buffer, CTA 0 of the cluster publishes
+// the tile with a system-scope release, and each CTA sums every rank's rows
+// in rank order after the peers' counters reached the same use (the protocol
+// of the prefill GEMM's epilogue).  Every wait is bounded (error word).
 #include "ms_common.cuh"
 #include "ms_epilogue.cuh"
 #include "ms_kernels.h"
@@ -313,33 +317,81 @@ __global__ void __launch_bounds__(kSkThreads, 2) gemm_sk_kernel(const GemvParams
     __syncthreads();  // every epilogue warp's flag and stores are in place
     cluster_arrive();
     cluster_wait();   // every CTA's partial and flag are in its shared memory
+    // this CTA's rows m = kidx + ks i, alternately to the two halves:
+    // rows m_first + m_step j, j < cnt (<= 16: 64 rows, >= 2 slices)
+    const int m_first = kidx + p.ksplit * half, m_step = 2 * p.ksplit;
+    const int cnt = (epi_warp && m_first < p.M) ? (p.M - m_first + m_step - 1) / m_step : 0;
+    const bool tp = p.peer_tiles != nullptr;  // grid-uniform
+    float* mine = tp ? p.peer_tiles[p.tp_rank] + (size_t)group * (128 * 128) : nullptr;
+    float v[16];
+    int any = 0;
     if (epi_warp) {
       const uint32_t bad0 = smem_u32(const_cast<int*>(&s_bad));
-      int any = 0;
       for (int r = 0; r < p.ksplit; ++r) any |= ld_dsmem_s32(dsmem_addr(bad0, (uint32_t)r));
-      if (!any) {
-        // this CTA's rows m = kidx + ks i, alternately to the two halves:
-        // rows m_first + m_step j, j < cnt (<= 16: 64 rows, >= 2 slices)
-        const int m_first = kidx + p.ksplit * half, m_step = 2 * p.ksplit;
-        const int cnt = m_first < p.M ? (p.M - m_first + m_step - 1) / m_step : 0;
-        const uint32_t s0 = smem_u32(S);
-        float v[16];
+      const uint32_t s0 = smem_u32(S);
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          v[j] = 0.f;
-          if (j < cnt) {
-            const int m = m_first + m_step * j;
+      for (int j = 0; j < 16; ++j) {
+        v[j] = 0.f;
+        if (j < cnt && !any) {
+          const int m = m_first + m_step * j;
 #pragma unroll
-            for (int r = 0; r < kSkMaxCluster; ++r)
-              if (r < p.ksplit)
-                v[j] += ld_dsmem(dsmem_addr(s0, (uint32_t)r) + 4u * (m * kSkRowS + arow));
+          for (int r = 0; r < kSkMaxCluster; ++r)
+            if (r < p.ksplit)
+              v[j] += ld_dsmem(dsmem_addr(s0, (uint32_t)r) + 4u * (m * kSkRowS + arow));
+        }
+      }
+      // tensor parallel: this rank's share of the tile, row m at m * 128
+      if (tp && !any)
+        for (int j = 0; j < cnt; ++j) __stcg(mine + (size_t)(m_first + m_step * j) * 128 + arow, v[j]);
+    }
+    cluster_arrive();  // done reading the other CTAs' partials (and, tensor
+    cluster_wait();    // parallel, every CTA's rows are in this rank's buffer)
+    if (tp) {
+      // ---- sum over the ranks: CTA 0 publishes one use of the tile (system
+      //      scope release), every CTA waits for each peer's counter to reach
+      //      it, then sums the ranks' rows in rank order (the same bits on
+      //      every rank) -- the protocol of the prefill GEMM's epilogue
+      __shared__ int s_use, s_tp_ok;
+      if (threadIdx.x == 2 * kWarp) {
+        s_use = 0;
+        if (kidx == 0 && !s_bad) {
+          const uint32_t bad0 = smem_u32(const_cast<int*>(&s_bad));
+          int bad_any = 0;
+          for (int r = 0; r < p.ksplit; ++r) bad_any |= ld_dsmem_s32(dsmem_addr(bad0, (uint32_t)r));
+          if (!bad_any) {
+            fence_acq_rel_sys();
+            s_use = atomicAdd_system(p.peer_flags[p.tp_rank] + group, 1) + 1;
           }
         }
-        finish_rows(m_first, m_step, cnt, v);
       }
+      cluster_arrive();
+      cluster_wait();  // CTA 0's use is in its shared memory
+      if (threadIdx.x == 2 * kWarp) {
+        const int use = ld_dsmem_s32(dsmem_addr(smem_u32(&s_use), 0u));
+        int ok_all = use > 0;
+        for (int r = 0; r < p.tp_world && ok_all; ++r)
+          if (r != p.tp_rank) ok_all = wait_counter_sys(p.peer_flags[r] + group, use);
+        if (use > 0 && !ok_all) atomicOr(p.err, kErrWaitTimeout);
+        fence_acq_rel_sys();
+        s_tp_ok = ok_all;
+      }
+      __syncthreads();
+      if (epi_warp && s_tp_ok && !any) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          if (j < cnt) {
+            const size_t off = (size_t)group * (128 * 128) + (size_t)(m_first + m_step * j) * 128 + arow;
+            float t = 0.f;
+            for (int rk = 0; rk < p.tp_world; ++rk) t += ld_sys_f32(p.peer_tiles[rk] + off);
+            v[j] = t;
+          }
+        }
+      }
+      if (epi_warp && !(s_tp_ok && !any)) any = 1;
     }
-    cluster_arrive();  // done reading the other CTAs' partials
-    cluster_wait();    // ... and they are done reading this one's
+    if (epi_warp && !any) finish_rows(m_first, m_step, cnt, v);
+    cluster_arrive();  // the other CTAs are done reading this one's shared memory
+    cluster_wait();
   }
 
   tc_fence_before();
@@ -356,6 +408,9 @@ __global__ void __launch_bounds__(kSkThreads, 2) gemm_sk_kernel(const GemvParams
 // the limb planes are read), then the GEMM; both with PDL.
 cudaError_t launch_gemm_sk(const GemvParams& p, cudaStream_t s, bool pdl) {
   const int N = (p.M + 15) / 16 * 16;
+  // the rank sum runs in the cluster epilogue: tensor parallel needs k-slices
+  if (p.peer_tiles && (p.ksplit < 2 || !p.peer_flags || p.tp_world < 2))
+    return cudaErrorInvalidConfiguration;
   if (p.M < 1 || N > kSkMaxN || p.ksplit < 1 || p.ksplit > kSkMaxCluster || p.kseg % kChunkK ||
       p.kseg <= 0 || (long long)p.kseg * (p.ksplit - 1) >= p.K)
     return cudaErrorInvalidConfiguration;
