@@ -59,7 +59,8 @@ constexpr int kSkMaxCluster = 8;
 constexpr uint32_t kSkLbo = 128, kSkSbo = 512;
 
 static_assert(kSkStageBytes % 1024 == 0, "stage alignment");
-static_assert((size_t)kSkMaxN * kSkRowS * 4 <= kSkSmem, "staged partial fits the ring");
+static_assert((size_t)(kSkMaxN + kSkMaxN / 2) * kSkRowS * 4 <= kSkSmem,
+              "staged partial + finished rows fit the ring");
 
 int sk_rows_max() { return kSkMaxN; }
 
@@ -197,201 +198,223 @@ __global__ void __launch_bounds__(kSkThreads, 2) gemm_sk_kernel(const GemvParams
   }
 
   // ------------------------------------------------------------ epilogue --
-  // Warps 2-9, two per tensor-memory lane quarter: warp w reads lanes
-  // 32 (w % 4) .. +31 = A rows = the group's output columns 32 (w % 4) +
-  // lane, and the two warps of a quarter share the batch rows (half = which
-  // one).  Lane ^ 8 holds the partner row (g <-> g + 8) of the same
-  // 16-column tile.  The row factors (the quantiser's output) are read once
-  // into shared memory; residual loads are issued kRB rows at a time.
-  constexpr int kRB = 4;
+  // 1. warps 2-9 copy the accumulators to a staged partial tile S[m][c]
+  //    (two warps per tensor-memory lane quarter: warp w reads lanes
+  //    32 (w % 4) .. +31 = the group's tile rows c; the two warps of a
+  //    quarter take alternate 16-row blocks); c = 16 tile + (g or g + 8) is
+  //    the prefill GEMM's staged layout, so the row epilogue below is its;
+  // 2. cluster: this CTA's rows m = kidx + ks i are summed over the slices
+  //    in k order with 128-bit distributed-shared-memory loads into F[i][c];
+  // 3. tensor parallel: the rows' rank sum (peer-visible buffers);
+  // 4. rows finished with lanes along the columns (128-bit loads / stores).
   __shared__ float2 s_rowf[kSkMaxN];
+  __shared__ int s_use, s_tp_ok;
   const bool epi_warp = warp >= 2;
+  const int t8 = threadIdx.x - 2 * kWarp;              // 0 .. 255 on warps 2-9
   const int quad = warp & 3, half = (warp - 2) >> 2;
-  const int arow = quad * kWarp + lane;                // A row in the group
-  const int tile = group * kGroupTiles + (arow >> 4);
-  const bool tile_ok = tile < p.n_tiles;
-  const int g = arow & 7;
-  const bool owner = (arow & 8) == 0;                  // holds tile row g, gets g + 8
-  float* S = reinterpret_cast<float*>(dsm);            // [N][kSkRowS] partial (cluster mode)
+  const int arow = quad * kWarp + lane;                // tile row of the group (TMEM lane)
+  float* S = reinterpret_cast<float*>(dsm);            // [kSkMaxN][kSkRowS]
+  float* F = S + kSkMaxN * kSkRowS;                    // [kSkMaxN / 2][kSkRowS]
   bool ok = true;
   if (epi_warp) {
     pdl_wait();
-    for (int m = threadIdx.x - 2 * kWarp; m < N; m += kSkConvWarps * kWarp)
+    for (int m = t8; m < N; m += kSkConvWarps * kWarp)
       s_rowf[m] = m < p.M ? p.rowf[m] : make_float2(0.f, 0.f);
     ok = mbar_wait(&done, 0);
     tc_fence_after();
-    if (!ok && lane == 0) atomicOr(p.err, kErrWaitTimeout);
-    bar_sync_n(1, kSkConvWarps * kWarp);  // s_rowf complete
-  }
-  // the finished sums of this thread's column for rows m0 .. m0 + 15
-  auto column_rows = [&](int m0, float (&v)[16]) {
-    uint32_t a0[16], a1[16], a2[16];
-    const uint32_t ta = tmem + ((uint32_t)(quad * kWarp) << 16) + m0;
-    tmem_ld16(ta, a0);
-    tmem_ld16(ta + N, a1);
-    tmem_ld16(ta + 2 * N, a2);
-    tmem_wait_ld();
-#pragma unroll
-    for (int q = 0; q < 16; ++q) {
-      const long long iv = (long long)(int)a0[q] + 256LL * (long long)(int)a1[q] +
-                           65536LL * (long long)(int)a2[q];
-      v[q] = (float)iv * s_rowf[m0 + q].x;
+    if (!ok && lane == 0) {
+      atomicOr(p.err, kErrWaitTimeout);
+      s_bad = 1;
     }
-  };
-  // rows m_first + m_step i (i < cnt <= 16) with their sums v[i]; every lane
-  // of the warp takes part (partner shuffle, statistics), owners of a live
-  // tile write.  kEpiResid: the arithmetic of epilogue_row with the residual
-  // values loaded ahead, kRB rows at a time.
-  auto finish_rows = [&](int m_first, int m_step, int cnt, const float (&v)[16]) {
-    const bool resid = p.epi == kEpiResid;
+    bar_sync_n(1, kSkConvWarps * kWarp);  // s_rowf complete
+    if (ok) {
+      for (int m0 = 16 * half; m0 < N; m0 += 32) {
+        uint32_t a0[16], a1[16], a2[16];
+        const uint32_t ta = tmem + ((uint32_t)(quad * kWarp) << 16) + m0;
+        tmem_ld16(ta, a0);
+        tmem_ld16(ta + N, a1);
+        tmem_ld16(ta + 2 * N, a2);
+        tmem_wait_ld();
 #pragma unroll
-    for (int i0 = 0; i0 < 16; i0 += kRB) {
-      if (i0 >= cnt) break;  // warp-uniform
-      float rr[kRB][2];
-#pragma unroll
-      for (int j = 0; j < kRB; ++j) {
-        rr[j][0] = rr[j][1] = 0.f;
-        const int m = m_first + m_step * (i0 + j);
-        if (resid && owner && tile_ok && i0 + j < cnt) {
-          const float* r = p.resid + (size_t)m * p.ldr + tile * kTileN + g;
-          rr[j][0] = __ldcg(r);
-          rr[j][1] = __ldcg(r + 8);
+        for (int q = 0; q < 16; ++q) {
+          const long long iv = (long long)(int)a0[q] + 256LL * (long long)(int)a1[q] +
+                               65536LL * (long long)(int)a2[q];
+          S[(m0 + q) * kSkRowS + arow] = (float)iv * s_rowf[m0 + q].x;
         }
       }
+    }
+  }
+  __syncthreads();  // S and every warp's flag are in place
+  // the rows this CTA finishes: m = m_first + m_step i, i < n_rows, values in Fr
+  const int m_first = cl ? kidx : 0, m_step = cl ? p.ksplit : 1;
+  const int n_rows = m_first < p.M ? (p.M - m_first + m_step - 1) / m_step : 0;
+  const float* Fr = cl ? F : S;
+  int any = s_bad;
+  if (cl) {
+    cluster_arrive();
+    cluster_wait();  // every CTA's partial tile and flag are in its shared memory
+    const uint32_t bad0 = smem_u32(const_cast<int*>(&s_bad));
+    any = 0;
+    for (int r = 0; r < p.ksplit; ++r) any |= ld_dsmem_s32(dsmem_addr(bad0, (uint32_t)r));
+    if (epi_warp && !any) {
+      const uint32_t s0 = smem_u32(S);
+      for (int it = t8; it < n_rows * (128 / 4); it += kSkConvWarps * kWarp) {
+        const int i = it >> 5, c4 = it & 31;
+        const uint32_t off = 4u * ((m_first + m_step * i) * kSkRowS + 4 * c4);
+        float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+        float4 v[kSkMaxCluster];
 #pragma unroll
-      for (int j = 0; j < kRB; ++j) {
-        if (i0 + j >= cnt) break;  // warp-uniform
-        const int m = m_first + m_step * (i0 + j);
-        const float v0 = v[i0 + j];
-        const float v1 = __shfl_xor_sync(0xffffffffu, v0, 8);
+        for (int r = 0; r < kSkMaxCluster; ++r)
+          if (r < p.ksplit) v[r] = ld_dsmem4(dsmem_addr(s0 + off, (uint32_t)r));
+#pragma unroll
+        for (int r = 0; r < kSkMaxCluster; ++r)
+          if (r < p.ksplit) {
+            a.x += v[r].x; a.y += v[r].y; a.z += v[r].z; a.w += v[r].w;
+          }
+        *reinterpret_cast<float4*>(F + i * kSkRowS + 4 * c4) = a;
+      }
+    }
+    cluster_arrive();  // done reading the other CTAs' partials
+    cluster_wait();
+  }
+  if (p.peer_tiles) {
+    // ---- tensor parallel (cluster mode, checked at launch): this rank's
+    //      rows to its peer-visible buffer (row m at m * 128); CTA 0
+    //      publishes one use of the tile after every CTA's rows are written
+    //      (system-scope release); each CTA waits for every peer's counter to
+    //      reach it and sums the ranks' rows in rank order (the same bits on
+    //      every rank) -- the protocol of the prefill GEMM's epilogue
+    float* mine = p.peer_tiles[p.tp_rank] + (size_t)group * (128 * 128);
+    if (epi_warp && !any)
+      for (int it = t8; it < n_rows * 32; it += kSkConvWarps * kWarp) {
+        const int i = it >> 5, c4 = it & 31;
+        __stcg(reinterpret_cast<float4*>(mine + (size_t)(m_first + m_step * i) * 128) + c4,
+               *reinterpret_cast<const float4*>(F + i * kSkRowS + 4 * c4));
+      }
+    __syncthreads();
+    cluster_arrive();
+    cluster_wait();  // every CTA's rows are written
+    if (threadIdx.x == 2 * kWarp) {
+      s_use = 0;
+      if (kidx == 0 && !any) {
+        fence_acq_rel_sys();
+        s_use = atomicAdd_system(p.peer_flags[p.tp_rank] + group, 1) + 1;
+      }
+    }
+    cluster_arrive();
+    cluster_wait();  // CTA 0's use is in its shared memory
+    if (threadIdx.x == 2 * kWarp) {
+      const int use = ld_dsmem_s32(dsmem_addr(smem_u32(&s_use), 0u));
+      int ok_all = use > 0;
+      for (int r = 0; r < p.tp_world && ok_all; ++r)
+        if (r != p.tp_rank) ok_all = wait_counter_sys(p.peer_flags[r] + group, use);
+      if (use > 0 && !ok_all) atomicOr(p.err, kErrWaitTimeout);
+      fence_acq_rel_sys();
+      s_tp_ok = ok_all;
+    }
+    __syncthreads();
+    if (!s_tp_ok) any = 1;
+    if (epi_warp && !any) {
+      for (int it = t8; it < n_rows * 32; it += kSkConvWarps * kWarp) {
+        const int i = it >> 5, c4 = it & 31;
+        const size_t off = (size_t)group * (128 * 128) + (size_t)(m_first + m_step * i) * 128;
+        float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int rk = 0; rk < p.tp_world; ++rk) {
+          const float4 v = ld_sys_f4(reinterpret_cast<const float4*>(p.peer_tiles[rk] + off) + c4);
+          a.x += v.x; a.y += v.y; a.z += v.z; a.w += v.w;
+        }
+        *reinterpret_cast<float4*>(F + i * kSkRowS + 4 * c4) = a;
+      }
+    }
+    cluster_arrive();  // CTA 0's shared memory may be released
+    cluster_wait();
+  }
+  if (epi_warp && !any) {
+    bar_sync_n(1, kSkConvWarps * kWarp);  // F complete
+    const int w8 = warp - 2;
+    const int jt = lane >> 2;             // tile of the group this lane covers
+    const int tile = group * kGroupTiles + jt;
+    const bool tile_ok = tile < p.n_tiles;
+    for (int i = w8; i < n_rows; i += kSkConvWarps) {
+      const int m = m_first + m_step * i;
+      const float* Sr = Fr + (cl ? i : m) * kSkRowS;
+      if (p.epi == kEpiStore || p.epi == kEpiAccum || p.epi == kEpiResid) {
+        const int c = group * 128 + 4 * lane;
+        const float4 v = *reinterpret_cast<const float4*>(Sr + 4 * lane);
+        float4 o;
         float sq = 0.f;
-        if (owner && tile_ok) {
-          if (resid) {
-            const float inv_res = s_rowf[m].y;
-            const float a = (rr[j][0] * p.resid_ple) * inv_res + p.scale * v0;
-            const float b = (rr[j][1] * p.resid_ple) * inv_res + p.scale * v1;
-            float* o = p.out + (size_t)m * p.ldo + tile * kTileN + g;
-            o[0] = a;
-            o[8] = b;
-            sq = a * a + b * b;
-          } else {
-            epilogue_row(p, tile, g, m, v0, v1, s_rowf[m].y, sq);
+        if (p.epi == kEpiResid) {
+          const float fres = s_rowf[m].y;
+          const float4 rr = __ldcg(reinterpret_cast<const float4*>(p.resid + (size_t)m * p.ldr + c));
+          o.x = (rr.x * p.resid_ple) * fres + p.scale * v.x;
+          o.y = (rr.y * p.resid_ple) * fres + p.scale * v.y;
+          o.z = (rr.z * p.resid_ple) * fres + p.scale * v.z;
+          o.w = (rr.w * p.resid_ple) * fres + p.scale * v.w;
+          sq = o.x * o.x + o.y * o.y + o.z * o.z + o.w * o.w;
+        } else {
+          o = make_float4(p.scale * v.x, p.scale * v.y, p.scale * v.z, p.scale * v.w);
+          if (p.epi == kEpiAccum && tile_ok) {
+            const float4 cur = __ldcg(reinterpret_cast<const float4*>(p.out + (size_t)m * p.ldo + c));
+            o.x = cur.x + o.x; o.y = cur.y + o.y; o.z = cur.z + o.z; o.w = cur.w + o.w;
           }
         }
-        if (resid && p.out_stats) {
+        if (tile_ok) *reinterpret_cast<float4*>(p.out + (size_t)m * p.ldo + c) = o;
+        if (p.epi == kEpiResid && p.out_stats) {
           sq += __shfl_xor_sync(0xffffffffu, sq, 1);
           sq += __shfl_xor_sync(0xffffffffu, sq, 2);
-          sq += __shfl_xor_sync(0xffffffffu, sq, 4);
-          if ((arow & 15) == 0 && tile_ok) p.out_stats[(size_t)tile * p.M + m] = sq;
+          if (tile_ok && (lane & 3) == 0) p.out_stats[(size_t)tile * p.M + m] = sq;
         }
-      }
-    }
-  };
-
-  if (!cl) {
-    // each 16-row block: half 0 finishes rows 0-7, half 1 rows 8-15
-    if (epi_warp && ok && !s_bad) {
-      for (int m0 = 0; m0 < N; m0 += 16) {
-        float v[16];
-        column_rows(m0, v);
-        float w[16];
+      } else if (p.epi == kEpiSwiGLU) {
+        // tile rows 0-7 gate, 8-15 up of the same output column
+        const int g0 = 2 * (lane & 3);
+        const float2 gv = *reinterpret_cast<const float2*>(Sr + 16 * jt + g0);
+        const float2 uv = *reinterpret_cast<const float2*>(Sr + 16 * jt + 8 + g0);
+        float h[2];
+        const float gs[2] = {gv.x, gv.y}, us[2] = {uv.x, uv.y};
 #pragma unroll
-        for (int q = 0; q < 8; ++q) w[q] = v[8 * half + q];
-#pragma unroll
-        for (int q = 8; q < 16; ++q) w[q] = 0.f;
-        const int mf = m0 + 8 * half;
-        finish_rows(mf, 1, max(0, min(8, p.M - mf)), w);
-      }
-    }
-  } else {
-    // ---- k-slices as one cluster: stage, exchange, finish rows m = r mod ks
-    if (epi_warp && ok) {
-      for (int m0 = 16 * half; m0 < N; m0 += 32) {
-        float v[16];
-        column_rows(m0, v);
-#pragma unroll
-        for (int q = 0; q < 16; ++q) S[(m0 + q) * kSkRowS + arow] = v[q];
-      }
-    }
-    if (epi_warp && !ok && lane == 0) s_bad = 1;
-    __syncthreads();  // every epilogue warp's flag and stores are in place
-    cluster_arrive();
-    cluster_wait();   // every CTA's partial and flag are in its shared memory
-    // this CTA's rows m = kidx + ks i, alternately to the two halves:
-    // rows m_first + m_step j, j < cnt (<= 16: 64 rows, >= 2 slices)
-    const int m_first = kidx + p.ksplit * half, m_step = 2 * p.ksplit;
-    const int cnt = (epi_warp && m_first < p.M) ? (p.M - m_first + m_step - 1) / m_step : 0;
-    const bool tp = p.peer_tiles != nullptr;  // grid-uniform
-    float* mine = tp ? p.peer_tiles[p.tp_rank] + (size_t)group * (128 * 128) : nullptr;
-    float v[16];
-    int any = 0;
-    if (epi_warp) {
-      const uint32_t bad0 = smem_u32(const_cast<int*>(&s_bad));
-      for (int r = 0; r < p.ksplit; ++r) any |= ld_dsmem_s32(dsmem_addr(bad0, (uint32_t)r));
-      const uint32_t s0 = smem_u32(S);
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        v[j] = 0.f;
-        if (j < cnt && !any) {
-          const int m = m_first + m_step * j;
-#pragma unroll
-          for (int r = 0; r < kSkMaxCluster; ++r)
-            if (r < p.ksplit)
-              v[j] += ld_dsmem(dsmem_addr(s0, (uint32_t)r) + 4u * (m * kSkRowS + arow));
+        for (int e = 0; e < 2; ++e) {
+          const float gt = p.scale * gs[e], up = p.scale2 * us[e];
+          const float sig = 1.0f / (1.0f + expf(-gt));
+          h[e] = up * gt * sig;
         }
-      }
-      // tensor parallel: this rank's share of the tile, row m at m * 128
-      if (tp && !any)
-        for (int j = 0; j < cnt; ++j) __stcg(mine + (size_t)(m_first + m_step * j) * 128 + arow, v[j]);
-    }
-    cluster_arrive();  // done reading the other CTAs' partials (and, tensor
-    cluster_wait();    // parallel, every CTA's rows are in this rank's buffer)
-    if (tp) {
-      // ---- sum over the ranks: CTA 0 publishes one use of the tile (system
-      //      scope release), every CTA waits for each peer's counter to reach
-      //      it, then sums the ranks' rows in rank order (the same bits on
-      //      every rank) -- the protocol of the prefill GEMM's epilogue
-      __shared__ int s_use, s_tp_ok;
-      if (threadIdx.x == 2 * kWarp) {
-        s_use = 0;
-        if (kidx == 0 && !s_bad) {
-          const uint32_t bad0 = smem_u32(const_cast<int*>(&s_bad));
-          int bad_any = 0;
-          for (int r = 0; r < p.ksplit; ++r) bad_any |= ld_dsmem_s32(dsmem_addr(bad0, (uint32_t)r));
-          if (!bad_any) {
-            fence_acq_rel_sys();
-            s_use = atomicAdd_system(p.peer_flags[p.tp_rank] + group, 1) + 1;
+        if (tile_ok)
+          *reinterpret_cast<float2*>(p.out + (size_t)m * p.ldo + group * 64 + 2 * lane) =
+              make_float2(h[0], h[1]);
+      } else if (p.epi == kEpiQKV && tile_ok) {
+        const int g0 = 2 * (lane & 3);
+        const QkvTile td = p.tiles[tile];
+        const float sc = td.dst == 0 ? p.sq : (td.dst == 1 ? p.sk : p.sv);
+        const float2 lv = *reinterpret_cast<const float2*>(Sr + 16 * jt + g0);
+        const float2 hv = *reinterpret_cast<const float2*>(Sr + 16 * jt + 8 + g0);
+        float lo[2] = {sc * lv.x, sc * lv.y}, hi[2] = {sc * hv.x, sc * hv.y};
+        const int pos = p.pos[m];
+        if (td.rope_i0 >= 0) {
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const float th = (float)pos * p.inv_freq[td.rope_i0 + g0 + e];
+            const float cs = cosf(th), sn = sinf(th);
+            const float ra = lo[e] * cs - hi[e] * sn;
+            const float rb = lo[e] * sn + hi[e] * cs;
+            lo[e] = ra;
+            hi[e] = rb;
           }
         }
-      }
-      cluster_arrive();
-      cluster_wait();  // CTA 0's use is in its shared memory
-      if (threadIdx.x == 2 * kWarp) {
-        const int use = ld_dsmem_s32(dsmem_addr(smem_u32(&s_use), 0u));
-        int ok_all = use > 0;
-        for (int r = 0; r < p.tp_world && ok_all; ++r)
-          if (r != p.tp_rank) ok_all = wait_counter_sys(p.peer_flags[r] + group, use);
-        if (use > 0 && !ok_all) atomicOr(p.err, kErrWaitTimeout);
-        fence_acq_rel_sys();
-        s_tp_ok = ok_all;
-      }
-      __syncthreads();
-      if (epi_warp && s_tp_ok && !any) {
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          if (j < cnt) {
-            const size_t off = (size_t)group * (128 * 128) + (size_t)(m_first + m_step * j) * 128 + arow;
-            float t = 0.f;
-            for (int rk = 0; rk < p.tp_world; ++rk) t += ld_sys_f32(p.peer_tiles[rk] + off);
-            v[j] = t;
-          }
+        float* base;
+        size_t off;
+        int bf = 0;
+        if (td.dst == 0) {
+          base = p.q_out;
+          off = (size_t)m * p.ldq;
+        } else {
+          off = kv_row_offset(p.kv.block_table, p.kv.bt_stride, p.kv.page, p.kv.cap, p.kv.circular,
+                              p.seq[m], pos, p.kv.kv_dim);
+          base = td.dst == 1 ? p.kv.k : p.kv.v;
+          bf = p.kv.bf16;
         }
+        kv_put2(base, bf, off + td.col_lo + g0, lo[0], lo[1]);
+        kv_put2(base, bf, off + td.col_hi + g0, hi[0], hi[1]);
       }
-      if (epi_warp && !(s_tp_ok && !any)) any = 1;
     }
-    if (epi_warp && !any) finish_rows(m_first, m_step, cnt, v);
-    cluster_arrive();  // the other CTAs are done reading this one's shared memory
-    cluster_wait();
   }
 
   tc_fence_before();
