@@ -69,8 +69,9 @@ def parse():
                          "reference's e4b loop uses 0.7)")
     ap.add_argument("--penalty", type=float, default=1.0,
                     help="repetition penalty (the reference's e4b loop uses 1.2)")
-    ap.add_argument("--kv", default="f32", choices=["f32", "bf16"],
-                    help="KV cache element type (f32: the parity mode; bf16: half the bytes)")
+    ap.add_argument("--kv", default="f32", choices=["f32", "bf16", "i8"],
+                    help="KV cache element type (f32: the parity mode; bf16: half the bytes; "
+                         "i8: int8 with a scale per position and KV head)")
     ap.add_argument("--kv-fill", default="prefill", choices=["prefill", "seeded"],
                     help="prefill: the prompts run through ms_prefill (TTFT measured); seeded: "
                          "the cache below the prompt length is filled with seeded K / V values "
@@ -318,15 +319,13 @@ def run_ours(args, ws, rank, local):
     proj_gbs = proj_bytes / (proj_ms / 1e3) / 1e9
 
     q4 = spec.q4_bytes()
-    kv_read = BATCH * spec.kv_bytes_per_seq(PROMPT + args.warmup + args.steps // 2)
-    if args.kv == "bf16":
-        kv_read //= 2
+    kv_read = BATCH * spec.kv_bytes_per_seq(PROMPT + args.warmup + args.steps // 2, dtype=args.kv)
     step_bytes = q4 + spec.lm_head_bytes() + kv_read
     step_ms = r["dev_ms"] / args.steps
     tokens = BATCH * args.steps * ws
     value = tokens / (r["dev_ms"] / 1000.0)
     e2e_val = tokens / (r["e2e_ms"] / 1000.0)
-    launches_per_step = 1 + 5 * spec.n_layers + (BATCH + 3) // 4 + 1
+    launches_per_step = 1 + (6 if args.kv == "i8" else 5) * spec.n_layers + (BATCH + 3) // 4 + 1
     if args.temperature > 0.01 or args.penalty > 1.0:
         launches_per_step += 1  # the sampler after the lm_head
     cfg = main_config(spec, ws)
@@ -410,8 +409,8 @@ def run_long(args, ctx, model, lib_stream, hbm, B=64, P=4096, steps=32, warmup=4
     """Batch 64 at 4096-token prompts on the same E4B model (a fresh cache):
     TTFT of 262144 prompt tokens, then the decode loop (f32 cache, the
     parity mode); then the decode loop again on a bf16 cache (half the KV
-    bytes; its cache filled with seeded values instead of a second prefill,
-    since decode timing does not depend on them)."""
+    bytes) and on an int8 cache (a quarter), each filled with seeded values
+    instead of a second prefill, since decode timing does not depend on them."""
     import torch
 
     from mojostream_b200.runtime import KVCache
@@ -427,13 +426,23 @@ def run_long(args, ctx, model, lib_stream, hbm, B=64, P=4096, steps=32, warmup=4
     kv.close()
     torch.cuda.empty_cache()
     slide_cap = window + MAX_ROWS
-    kvb = KVCache(ctx, model, B, max_pos, slide_cap=slide_cap, dtype="bf16")
-    ab = argparse.Namespace(steps=steps, warmup=warmup, kv_fill="seeded")
-    rb = decode_loop(model, kvb, B, P, ab, Dist(1), lib_stream, slide_cap=slide_cap)
-    kvb.close()
-    torch.cuda.empty_cache()
-    bf_bytes = spec.q4_bytes() + spec.lm_head_bytes() + kv_read // 2
-    bf_ms = rb["dev_ms"] / steps
+    legs = {}
+    for dt in ("bf16", "i8"):
+        kvb = KVCache(ctx, model, B, max_pos, slide_cap=slide_cap, dtype=dt)
+        ab = argparse.Namespace(steps=steps, warmup=warmup, kv_fill="seeded")
+        rb = decode_loop(model, kvb, B, P, ab, Dist(1), lib_stream, slide_cap=slide_cap)
+        kvb.close()
+        torch.cuda.empty_cache()
+        b = spec.q4_bytes() + spec.lm_head_bytes() + \
+            B * spec.kv_bytes_per_seq(P + warmup + steps // 2, dtype=dt)
+        ms = rb["dev_ms"] / steps
+        legs[dt] = {"value": round(B * steps / (rb["dev_ms"] / 1e3), 2), "unit": "tokens/s",
+                    "ms_per_step": round(ms, 4),
+                    "step_roofline": {"bytes_per_step": b, "peak": hbm,
+                                      "frac": round(b / (ms / 1e3) / 1e9 / hbm, 4)}}
+    legs["bf16"]["note"] = "bf16 cache (K / V rounded on write), seeded values below 4096"
+    legs["i8"]["note"] = ("int8 cache (one fp32 scale per position and KV head), seeded "
+                          "values below 4096")
     return {
         "metric": "decode tokens/s (batch 64, 4096-token prompts), E4B-shaped Q4 model",
         "value": round(B * steps / (r["dev_ms"] / 1e3), 2), "unit": "tokens/s",
@@ -447,11 +456,8 @@ def run_long(args, ctx, model, lib_stream, hbm, B=64, P=4096, steps=32, warmup=4
         "config": {"batch": B, "prompt": P, "kv_dtype": "f32",
                    "positions": [P + warmup, P + warmup + steps]},
         "first_ids": r["first"][:4],
-        "bf16_kv": {"value": round(B * steps / (rb["dev_ms"] / 1e3), 2), "unit": "tokens/s",
-                    "ms_per_step": round(bf_ms, 4),
-                    "step_roofline": {"bytes_per_step": bf_bytes, "peak": hbm,
-                                      "frac": round(bf_bytes / (bf_ms / 1e3) / 1e9 / hbm, 4)},
-                    "note": "bf16 cache (K / V rounded on write), seeded values below 4096"},
+        "bf16_kv": legs["bf16"],
+        "i8_kv": legs["i8"],
     }
 
 

@@ -155,6 +155,12 @@ struct ms_kv {
   int* bt_slide = nullptr;
   int* tok = nullptr;  // [n_seq][max_pos] token fed at each position (-1: none)
   int bf16 = 0;        // K / V pools hold bfloat16
+  // int8 pools (value = int8 * scale, one fp32 scale per position and KV head
+  // behind the row's values) and the fp32 rows the projections write before
+  // launch_kv_quant moves them in: K [max_rows][stage_ld], then V
+  int i8 = 0;
+  float* stage = nullptr;
+  int stage_ld = 0;
   size_t bytes = 0;
   // pooled mode (ms_kv_create_pooled): the full-attention layers draw pages
   // from one pool of pool_pages pages (a page id indexes every full layer's
@@ -1168,6 +1174,21 @@ extern "C" ms_status ms_kv_create(ms_ctx* c, const ms_model* m, int n_seq, int m
   return ms_kv_create_typed(c, m, n_seq, max_pos, slide_cap, MS_KV_F32, out);
 }
 
+// Bytes of one cached position of layer L (one of the K or V pools): kv_dim
+// values, or for int8 kv_dim bytes then n_kv fp32 scales, padded to 16 bytes.
+static size_t kv_row_bytes(const ms_kv* kv, const LayerDev& L) {
+  if (kv->i8) return (size_t)L.kv_dim + 16 * (size_t)((L.d.n_kv_heads + 3) / 4);
+  return (size_t)L.kv_dim * (kv->bf16 ? 2 : 4);
+}
+// Pages in layer L's pool, and the pool's bytes (K or V).
+static size_t kv_pool_pages(const ms_kv* kv, const LayerDev& L) {
+  if (L.d.window == 0 && kv->pooled) return (size_t)kv->pool_pages;
+  return (size_t)kv->n_seq * (L.d.window > 0 ? kv->pages_slide : kv->pages_full);
+}
+static size_t kv_pool_bytes(const ms_kv* kv, const LayerDev& L) {
+  return kv_pool_pages(kv, L) * kv->page * kv_row_bytes(kv, L);
+}
+
 static ms_status kv_create(ms_ctx* c, const ms_model* m, int n_seq, int max_pos, int slide_cap,
                            int dtype, int pool_pages, ms_kv** out) {
   if (!c || !m || !out) return MS_ERR_INVALID_ARG;
@@ -1175,17 +1196,22 @@ static ms_status kv_create(ms_ctx* c, const ms_model* m, int n_seq, int max_pos,
   if (m->ctx != c) return fail(c, MS_ERR_STATE, "model belongs to another context");
   if (n_seq <= 0 || max_pos <= 0 || slide_cap < 0)
     return fail(c, MS_ERR_SHAPE, "kv: n_seq %d max_pos %d slide_cap %d", n_seq, max_pos, slide_cap);
-  if (dtype != MS_KV_F32 && dtype != MS_KV_BF16)
+  if (dtype != MS_KV_F32 && dtype != MS_KV_BF16 && dtype != MS_KV_I8)
     return fail(c, MS_ERR_INVALID_ARG, "kv: dtype %d", dtype);
   if (dtype == MS_KV_BF16)
     for (const LayerDev& L : m->layers)
       if (L.kv_dim % 8)
         return fail(c, MS_ERR_SHAPE, "kv: a bf16 cache needs kv_dim %% 8 == 0 (%d)", L.kv_dim);
+  if (dtype == MS_KV_I8)
+    for (const LayerDev& L : m->layers)
+      if (L.d.head_dim % 16)
+        return fail(c, MS_ERR_SHAPE, "kv: an int8 cache needs head_dim %% 16 == 0 (%d)",
+                    L.d.head_dim);
   cudaSetDevice(c->device);
   ms_kv* kv = new ms_kv();
   kv->model = m;
   kv->bf16 = dtype == MS_KV_BF16;
-  const size_t eb = kv->bf16 ? 2 : 4;  // bytes per cached value
+  kv->i8 = dtype == MS_KV_I8;
   kv->n_seq = n_seq;
   kv->max_pos = max_pos;
   int win = 0;
@@ -1228,18 +1254,21 @@ static ms_status kv_create(ms_ctx* c, const ms_model* m, int n_seq, int max_pos,
     cudaMemcpy(*dst, bt.data(), (size_t)n_seq * P * sizeof(int), cudaMemcpyHostToDevice);
   }
   for (const LayerDev& L : m->layers) {
-    const int P = L.d.window > 0 ? kv->pages_slide : kv->pages_full;
-    const size_t n = (L.d.window == 0 && kv->pooled)
-                         ? (size_t)kv->pool_pages * kv->page * L.kv_dim
-                         : (size_t)n_seq * P * kv->page * L.kv_dim;
+    const size_t n = kv_pool_bytes(kv, L);
     float *k = nullptr, *v = nullptr;
-    if (dev_alloc(c, (void**)&k, n * eb) != MS_OK) return cleanup(MS_ERR_OOM);
+    if (dev_alloc(c, (void**)&k, n) != MS_OK) return cleanup(MS_ERR_OOM);
     kv->k.push_back(k);
-    if (dev_alloc(c, (void**)&v, n * eb) != MS_OK) return cleanup(MS_ERR_OOM);
+    if (dev_alloc(c, (void**)&v, n) != MS_OK) return cleanup(MS_ERR_OOM);
     kv->v.push_back(v);
-    cudaMemset(k, 0, n * eb);
-    cudaMemset(v, 0, n * eb);
-    kv->bytes += 2 * n * eb;
+    cudaMemset(k, 0, n);
+    cudaMemset(v, 0, n);
+    kv->bytes += 2 * n;
+  }
+  if (kv->i8) {
+    for (const LayerDev& L : m->layers) kv->stage_ld = std::max(kv->stage_ld, L.kv_dim);
+    if (dev_alloc(c, (void**)&kv->stage, 2 * (size_t)m->max_rows * kv->stage_ld * sizeof(float)) !=
+        MS_OK)
+      return cleanup(MS_ERR_OOM);
   }
   // the repetition-penalty history of every sequence
   if (dev_alloc(c, (void**)&kv->tok, (size_t)n_seq * max_pos * sizeof(int)) != MS_OK)
@@ -1271,6 +1300,7 @@ extern "C" ms_status ms_kv_destroy(ms_ctx* c, ms_kv* kv) {
   cudaFree(kv->bt_full);
   cudaFree(kv->bt_slide);
   cudaFree(kv->tok);
+  cudaFree(kv->stage);
   delete kv;
   return MS_OK;
 }
@@ -1281,11 +1311,7 @@ extern "C" ms_status ms_kv_reset(ms_ctx* c, ms_kv* kv) {
   // so a reset cache is indistinguishable from a new one (a pooled cache
   // also gets all its pages back)
   for (size_t i = 0; i < kv->k.size(); ++i) {
-    const LayerDev& L = kv->model->layers[i];
-    const int P = L.d.window > 0 ? kv->pages_slide : kv->pages_full;
-    const size_t pages = (L.d.window == 0 && kv->pooled) ? (size_t)kv->pool_pages
-                                                         : (size_t)kv->n_seq * P;
-    const size_t n = pages * kv->page * L.kv_dim * (kv->bf16 ? 2 : 4);
+    const size_t n = kv_pool_bytes(kv, kv->model->layers[i]);
     MS_CUDA(c, cudaMemsetAsync(kv->k[i], 0, n, c->stream));
     MS_CUDA(c, cudaMemsetAsync(kv->v[i], 0, n, c->stream));
   }
@@ -1312,9 +1338,8 @@ static std::vector<int> full_layers(const ms_kv* kv) {
 
 // Copy page `from` to page `to` in every full-attention layer's K and V pool.
 static ms_status kv_copy_page(ms_ctx* c, ms_kv* kv, int from, int to, cudaStream_t s) {
-  const size_t eb = kv->bf16 ? 2 : 4;
   for (int l : full_layers(kv)) {
-    const size_t row = (size_t)kv->page * kv->model->layers[l].kv_dim * eb;
+    const size_t row = (size_t)kv->page * kv_row_bytes(kv, kv->model->layers[l]);
     char* k = reinterpret_cast<char*>(kv->k[l]);
     char* v = reinterpret_cast<char*>(kv->v[l]);
     MS_CUDA(c, cudaMemcpyAsync(k + to * row, k + from * row, row, cudaMemcpyDeviceToDevice, s));
@@ -1436,10 +1461,10 @@ extern "C" ms_status ms_kv_share_prefix(ms_ctx* c, ms_kv* kv, int src, int dst, 
     MS_TRY(kv_upload_row(c, kv, dst, s));
   } else {
     // fixed pages: copy the prefix rows of every full-attention layer
-    const size_t eb = kv->bf16 ? 2 : 4;
     for (int l : full_layers(kv)) {
-      const size_t bytes = (size_t)n_pos * kv->model->layers[l].kv_dim * eb;
-      const size_t off = (size_t)P * kv->page * kv->model->layers[l].kv_dim * eb;
+      const size_t rb = kv_row_bytes(kv, kv->model->layers[l]);
+      const size_t bytes = (size_t)n_pos * rb;
+      const size_t off = (size_t)P * kv->page * rb;
       char* k = reinterpret_cast<char*>(kv->k[l]);
       char* v = reinterpret_cast<char*>(kv->v[l]);
       MS_CUDA(c, cudaMemcpyAsync(k + dst * off, k + src * off, bytes, cudaMemcpyDeviceToDevice, s));
@@ -1449,11 +1474,10 @@ extern "C" ms_status ms_kv_share_prefix(ms_ctx* c, ms_kv* kv, int src, int dst, 
   // sliding layers: the ring holds position p at slot p % slide_cap in both
   // sequences, so the whole ring is copied (slots past the prefix are
   // overwritten before they are read)
-  const size_t eb = kv->bf16 ? 2 : 4;
   for (size_t l = 0; l < kv->k.size(); ++l) {
     const LayerDev& L = kv->model->layers[l];
     if (L.d.window == 0) continue;
-    const size_t ring = (size_t)kv->pages_slide * kv->page * L.kv_dim * eb;
+    const size_t ring = (size_t)kv->pages_slide * kv->page * kv_row_bytes(kv, L);
     char* k = reinterpret_cast<char*>(kv->k[l]);
     char* v = reinterpret_cast<char*>(kv->v[l]);
     MS_CUDA(c, cudaMemcpyAsync(k + dst * ring, k + src * ring, ring, cudaMemcpyDeviceToDevice, s));
@@ -1495,6 +1519,8 @@ static ms_status kv_rows_check(ms_ctx* c, const ms_kv* kv, int layer, int seq, i
   if (!k || !v) return fail(c, MS_ERR_INVALID_ARG, "%s: null buffer", what);
   if (((uintptr_t)k & 3) || ((uintptr_t)v & 3))
     return fail(c, MS_ERR_ALIGN, "%s: buffers must be 4-byte aligned", what);
+  if (kv->i8 && (((uintptr_t)k & 15) || ((uintptr_t)v & 15)))
+    return fail(c, MS_ERR_ALIGN, "%s: an int8 cache takes 16-byte aligned buffers", what);
   if (!is_device_ptr(k) || !is_device_ptr(v))
     return fail(c, MS_ERR_INVALID_ARG, "%s: k / v must be device pointers", what);
   return MS_OK;
@@ -1600,6 +1626,13 @@ static KvView kv_view(const ms_kv* kv, int layer) {
                                               : (size_t)kv->n_seq * v.bt_stride;
   v.off32 = pages * v.page * v.kv_dim < ((size_t)1 << 32);
   v.bf16 = kv->bf16;
+  v.i8 = kv->i8;
+  v.row_bytes = (int)kv_row_bytes(kv, L);
+  v.hd = L.d.head_dim;
+  if (kv->i8) {
+    v.stage_k = kv->stage;
+    v.stage_v = kv->stage + (size_t)kv->model->max_rows * kv->stage_ld;
+  }
   return v;
 }
 
@@ -1635,6 +1668,7 @@ static ms_status run_layer(ms_ctx* c, ms_model* m, const ms_kv* kv, int li, int 
     p.seq = m->d_seq;
     p.kv = kv_view(kv, li);
     MS_CUDA(c, launch_proj(p, pl, s, pdl));
+    if (kv->i8) MS_CUDA(c, launch_kv_quant(p.kv, m->d_seq, m->d_pos, M, s, pdl));
   }
   // 2. attention
   {

@@ -37,17 +37,20 @@ constexpr int kAttnMergeBatch = 8;  // partial rows loaded per round of the merg
 constexpr int kAttnMaxCluster = 16;
 static bool g_attn_cluster_ok = false;
 
-// BF: the cache holds bfloat16 K / V (rows half the bytes, widened to fp32
-// as they are read out of the ring).
-template <int HD, int G, bool BF>
+// DT: the cache's element type -- 0 fp32; 1 bfloat16 (rows half the bytes,
+// widened to fp32 as they are read out of the ring); 2 int8 with one fp32
+// scale per (position, KV head) (a quarter of the bytes; the two scales ride
+// in the slot behind the K and V rows, the score takes the K scale after the
+// dot product and the V weight the V scale).
+template <int HD, int G, int DT>
 struct WarpAttn {
   static constexpr int NW = (G * HD >= 2048) ? 4 : 8;  // warps (registers: q + out slices)
   static constexpr int NT = NW * kWarp;
   static constexpr int VEC = HD >= 128 ? 4 : 2;        // values per lane load
   static constexpr int NV = HD / (kWarp * VEC);        // loads per lane per row
   static constexpr int PL = NV * VEC;                  // dims per lane
-  static constexpr int EB = BF ? 2 : 4;                // bytes per cached value
-  static constexpr int SLOTB = 2 * HD * EB;            // bytes: K row then V row
+  static constexpr int EB = DT == 0 ? 4 : (DT == 1 ? 2 : 1);  // bytes per cached value
+  static constexpr int SLOTB = 2 * HD * EB + (DT == 2 ? 16 : 0);  // K row, V row (, scales)
   // slots per warp: about 64 KB of rows in flight per CTA, and at least enough
   // for the end-of-unit combine (NW x G x (HD + 2) floats) to reuse the rings
   static constexpr int P0 = 65536 / (NW * SLOTB);
@@ -64,9 +67,17 @@ struct WarpAttn {
 };
 
 // VEC cached values at src (shared memory) as floats.
-template <int VEC, bool BF>
+template <int VEC, int DT>
 __device__ __forceinline__ void ld_vec(float* dst, const unsigned char* src) {
-  if constexpr (BF) {
+  if constexpr (DT == 2) {  // int8: sign-extended bytes (exact in fp32)
+    if constexpr (VEC == 4) {
+      i8x4_to_f32(*reinterpret_cast<const uint32_t*>(src), dst);
+    } else {
+      float t[4];
+      i8x4_to_f32(*reinterpret_cast<const unsigned short*>(src), t);
+      dst[0] = t[0]; dst[1] = t[1];
+    }
+  } else if constexpr (DT == 1) {
     if constexpr (VEC == 4) {
       const uint2 u = *reinterpret_cast<const uint2*>(src);
       dst[0] = __uint_as_float(u.x << 16); dst[1] = __uint_as_float(u.x & 0xffff0000u);
@@ -85,9 +96,9 @@ __device__ __forceinline__ void ld_vec(float* dst, const unsigned char* src) {
 }
 
 
-template <int HD, int G, bool BF>
-__global__ void __launch_bounds__(WarpAttn<HD, G, BF>::NT) attn_kernel(const AttnParams p) {
-  using S = WarpAttn<HD, G, BF>;
+template <int HD, int G, int DT>
+__global__ void __launch_bounds__(WarpAttn<HD, G, DT>::NT) attn_kernel(const AttnParams p) {
+  using S = WarpAttn<HD, G, DT>;
   constexpr int NW = S::NW, NT = S::NT, P = S::P, PL = S::PL, VEC = S::VEC, ST = S::ST;
   constexpr int EB = S::EB;
   extern __shared__ __align__(128) unsigned char smb[];  // [NW][P][K row | V row], partial
@@ -123,28 +134,36 @@ __global__ void __launch_bounds__(WarpAttn<HD, G, BF>::NT) attn_kernel(const Att
   const unsigned char* kpool = reinterpret_cast<const unsigned char*>(p.kv.k);
   const unsigned char* vpool = reinterpret_cast<const unsigned char*>(p.kv.v);
 
-  // Row offsets of this warp's positions, 32 at a time: lane j holds that of
-  // position base + j (one batch of independent block-table loads instead of
-  // a dependent load before every copy).
+  // Byte offsets of this warp's positions' head rows, 32 at a time: lane j
+  // holds that of position base + j (one batch of independent block-table
+  // loads instead of a dependent load before every copy).
   auto row_offsets = [&](int base) -> unsigned long long {
     const int i = base + lane;
     if (i >= cnt) return 0ull;
-    return kv_row_offset(p.kv.block_table, p.kv.bt_stride, p.kv.page, p.kv.cap, p.kv.circular,
-                         seq, t_begin + warp + NW * i, p.kv.kv_dim) + head_off;
+    const size_t row = kv_row_index(p.kv, seq, t_begin + warp + NW * i);
+    if constexpr (DT == 2) return row * (size_t)p.kv.row_bytes + head_off;
+    return (row * (size_t)p.kv.kv_dim + head_off) * EB;
   };
-  // the warp streams position i (t_begin + warp + NW i), whose row offset is
-  // `off`, into slot i % P, then closes the position's commit group (always,
-  // so that group j is position j's)
+  // the warp streams position i (t_begin + warp + NW i), whose head rows
+  // start `off` bytes into the pools, into slot i % P, then closes the
+  // position's commit group (always, so that group j is position j's)
   auto issue = [&](int i, unsigned long long off) {
     if (i < cnt) {
       unsigned char* dst = ring + (i % P) * S::SLOTB;
-      const unsigned char* ks = kpool + off * EB;
-      const unsigned char* vs = vpool + off * EB;
+      const unsigned char* ks = kpool + off;
+      const unsigned char* vs = vpool + off;
       constexpr int CH = HD * EB / 16;  // 16-byte chunks per row
 #pragma unroll
       for (int c = lane; c < CH; c += kWarp) {
         cp_async16(dst + c * 16, ks + c * 16);
         cp_async16(dst + HD * EB + c * 16, vs + c * 16);
+      }
+      if constexpr (DT == 2) {
+        if (lane == 0) {  // the row's scales: behind its kv_dim values
+          const size_t so = (size_t)p.kv.kv_dim - head_off + 4 * (size_t)hk;
+          cp_async4(dst + 2 * HD, ks + so);
+          cp_async4(dst + 2 * HD + 4, vs + so);
+        }
       }
     }
     cp_async_commit();
@@ -182,8 +201,13 @@ __global__ void __launch_bounds__(WarpAttn<HD, G, BF>::NT) attn_kernel(const Att
     const unsigned char* kr = ring + slot * S::SLOTB;
 #pragma unroll
     for (int v = 0; v < S::NV; ++v) {
-      ld_vec<VEC, BF>(&kk[v * VEC], kr + (v * kWarp + lane) * VEC * EB);
-      ld_vec<VEC, BF>(&vv[v * VEC], kr + (HD + (v * kWarp + lane) * VEC) * EB);
+      ld_vec<VEC, DT>(&kk[v * VEC], kr + (v * kWarp + lane) * VEC * EB);
+      ld_vec<VEC, DT>(&vv[v * VEC], kr + (HD + (v * kWarp + lane) * VEC) * EB);
+    }
+    float kscale = p.scale, vscale = 1.f;
+    if constexpr (DT == 2) {
+      kscale = reinterpret_cast<const float*>(kr + 2 * HD)[0] * p.scale;
+      vscale = reinterpret_cast<const float*>(kr + 2 * HD)[1];
     }
     __syncwarp();  // every lane holds its slice: the slot can be refilled
     if (((i + P) & 31) == 0) offs = row_offsets(i + P);  // warp-uniform
@@ -197,7 +221,7 @@ __global__ void __launch_bounds__(WarpAttn<HD, G, BF>::NT) attn_kernel(const Att
       sc[h] = d;
     }
 #pragma unroll
-    for (int h = 0; h < G; ++h) sc[h] = warp_sum(sc[h]) * p.scale;  // G independent chains
+    for (int h = 0; h < G; ++h) sc[h] = warp_sum(sc[h]) * kscale;  // G independent chains
 #pragma unroll
     for (int h = 0; h < G; ++h) {
       const float s = sc[h];
@@ -213,8 +237,9 @@ __global__ void __launch_bounds__(WarpAttn<HD, G, BF>::NT) attn_kernel(const Att
       }
       const float ew = expf(s - mrun[h]);
       lrun[h] += ew;
+      const float wv = DT == 2 ? ew * vscale : ew;
 #pragma unroll
-      for (int e = 0; e < PL; ++e) acc[h][e] = fmaf(ew, vv[e], acc[h][e]);
+      for (int e = 0; e < PL; ++e) acc[h][e] = fmaf(wv, vv[e], acc[h][e]);
     }
   }
   cp_async_wait<0>();  // (only empty groups remain)
@@ -398,9 +423,9 @@ __global__ void __launch_bounds__(WarpAttn<HD, G, BF>::NT) attn_kernel(const Att
   if (tid == 0) *ctr = 0;
 }
 
-template <int HD, int G, bool BF>
+template <int HD, int G, int DT>
 static cudaError_t launch_t(const AttnParams& p, cudaStream_t s, bool pdl) {
-  using S = WarpAttn<HD, G, BF>;
+  using S = WarpAttn<HD, G, DT>;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.n_splits, p.n_kv, p.M);
   cfg.blockDim = dim3(S::NT);
@@ -422,7 +447,7 @@ static cudaError_t launch_t(const AttnParams& p, cudaStream_t s, bool pdl) {
   }
   cfg.attrs = attr;
   cfg.numAttrs = na;
-  return cudaLaunchKernelEx(&cfg, attn_kernel<HD, G, BF>, p);
+  return cudaLaunchKernelEx(&cfg, attn_kernel<HD, G, DT>, p);
 }
 
 #define MS_ATTN_CASES(X)                                                        \
@@ -431,17 +456,19 @@ static cudaError_t launch_t(const AttnParams& p, cudaStream_t s, bool pdl) {
   X(512, 1) X(512, 2) X(512, 4)
 
 // q, out: 16-byte aligned rows (ldq, ldo multiples of 4); the KV pools 16-byte
-// aligned, rows on 16-byte boundaries (kv_dim a multiple of 4, of 8 for bf16);
-// n_splits <= 64.
+// aligned, rows on 16-byte boundaries (kv_dim a multiple of 4, of 8 for bf16;
+// int8: row_bytes a multiple of 16); n_splits <= 64.
 cudaError_t launch_attention(const AttnParams& p, cudaStream_t s, bool pdl) {
   if (p.n_splits < 1 || p.n_splits > kAttnMaxSplits || p.chunk < 1 || (p.ldq & 3) ||
       (p.cluster && (p.n_splits > kAttnMaxCluster || !g_attn_cluster_ok)) ||
-      (p.ldo & 3) || (p.kv.kv_dim & 3) || (p.kv.bf16 && (p.kv.kv_dim & 7)))
+      (p.ldo & 3) || (p.kv.kv_dim & 3) || (p.kv.bf16 && (p.kv.kv_dim & 7)) ||
+      (p.kv.i8 && ((p.kv.row_bytes & 15) || p.kv.hd != p.hd)))
     return cudaErrorInvalidConfiguration;
   const int G = p.n_heads / p.n_kv;
 #define MS_ATTN_CASE(HDV, GV)                                                   \
   if (p.hd == HDV && G == GV)                                                   \
-    return p.kv.bf16 ? launch_t<HDV, GV, true>(p, s, pdl) : launch_t<HDV, GV, false>(p, s, pdl);
+    return p.kv.i8 ? launch_t<HDV, GV, 2>(p, s, pdl)                            \
+                   : (p.kv.bf16 ? launch_t<HDV, GV, 1>(p, s, pdl) : launch_t<HDV, GV, 0>(p, s, pdl));
   MS_ATTN_CASES(MS_ATTN_CASE)
 #undef MS_ATTN_CASE
   return cudaErrorInvalidConfiguration;
@@ -474,24 +501,24 @@ int attention_max_cluster() { return g_attn_cluster_ok ? kAttnMaxCluster : 0; }
 cudaError_t prepare_attention() {
   cudaError_t e = cudaSuccess;
   g_attn_cluster_ok = true;
-#define MS_ATTN_PREP1(HDV, GV, BFV)                                                        \
-  if (e == cudaSuccess && WarpAttn<HDV, GV, BFV>::smem > 48 * 1024)                       \
-    e = cudaFuncSetAttribute(attn_kernel<HDV, GV, BFV>,                                   \
+#define MS_ATTN_PREP1(HDV, GV, DTV)                                                        \
+  if (e == cudaSuccess && WarpAttn<HDV, GV, DTV>::smem > 48 * 1024)                       \
+    e = cudaFuncSetAttribute(attn_kernel<HDV, GV, DTV>,                                   \
                              cudaFuncAttributeMaxDynamicSharedMemorySize,                 \
-                             (int)WarpAttn<HDV, GV, BFV>::smem);                          \
+                             (int)WarpAttn<HDV, GV, DTV>::smem);                          \
   if (e == cudaSuccess && g_attn_cluster_ok) {                                            \
     /* clusters are an optimisation: without them the global merge runs */               \
-    if (cudaFuncSetAttribute(attn_kernel<HDV, GV, BFV>,                                   \
+    if (cudaFuncSetAttribute(attn_kernel<HDV, GV, DTV>,                                   \
                              cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess) { \
       cudaGetLastError();                                                                 \
       g_attn_cluster_ok = false;                                                          \
     } else {                                                                              \
-      g_attn_cluster_ok = attn_cluster_fits(attn_kernel<HDV, GV, BFV>,                    \
-                                            WarpAttn<HDV, GV, BFV>::NT,                   \
-                                            WarpAttn<HDV, GV, BFV>::smem);                \
+      g_attn_cluster_ok = attn_cluster_fits(attn_kernel<HDV, GV, DTV>,                    \
+                                            WarpAttn<HDV, GV, DTV>::NT,                   \
+                                            WarpAttn<HDV, GV, DTV>::smem);                \
     }                                                                                     \
   }
-#define MS_ATTN_PREP(HDV, GV) MS_ATTN_PREP1(HDV, GV, false) MS_ATTN_PREP1(HDV, GV, true)
+#define MS_ATTN_PREP(HDV, GV) MS_ATTN_PREP1(HDV, GV, 0) MS_ATTN_PREP1(HDV, GV, 1) MS_ATTN_PREP1(HDV, GV, 2)
   MS_ATTN_CASES(MS_ATTN_PREP)
 #undef MS_ATTN_PREP
 #undef MS_ATTN_PREP1

@@ -14,7 +14,8 @@
 //   * every warp owns 16 query rows (one mma m-tile); with hd 512 two warps
 //     share the rows and split the output dims;
 //   * K / V arrive in chunks of BK keys, double-buffered (cp.async; a bf16
-//     cache is widened to fp32 while staging);
+//     cache is widened to fp32 while staging, an int8 cache multiplied out by
+//     its (position, KV head) scale);
 //   * S = Q K^T and O += P V run on mma.sync m16n8k8 TF32 with the 3xTF32
 //     split (x = hi + lo, both TF32; hi.hi + hi.lo + lo.hi): products to
 //     about 2^-21 relative, fp32 accumulation -- the per-layer parity bound
@@ -73,7 +74,7 @@ __device__ __forceinline__ void mma_3xtf32(float (&c)[4], const uint32_t (&ah)[4
   mma_tf32(c, ah, bh0, bh1);
 }
 
-template <int HD, int G, bool BF>
+template <int HD, int G, int DT>
 __global__ void __launch_bounds__(kPfThreads, 1) attn_prefill_kernel(const AttnParams p) {
   using S = PfTc<HD>;
   constexpr int R = S::R, BK = S::BK, NT = S::NT, OT = S::OT, QS = S::QS, VS = S::VS, KS = S::KS;
@@ -110,9 +111,27 @@ __global__ void __launch_bounds__(kPfThreads, 1) attn_prefill_kernel(const AttnP
         *reinterpret_cast<float4*>(v + j * VS + 4 * d4) = make_float4(0.f, 0.f, 0.f, 0.f);
         continue;
       }
+      if constexpr (DT == 2) {
+        const size_t rb = kv_row_index(p.kv, seq, tt) * (size_t)p.kv.row_bytes;
+        const unsigned char* kb = reinterpret_cast<const unsigned char*>(p.kv.k) + rb;
+        const unsigned char* vb = reinterpret_cast<const unsigned char*>(p.kv.v) + rb;
+        const float ks = reinterpret_cast<const float*>(kb + p.kv.kv_dim)[hk];
+        const float vs = reinterpret_cast<const float*>(vb + p.kv.kv_dim)[hk];
+        const uint32_t ku = *reinterpret_cast<const uint32_t*>(kb + head_off + 4 * d4);
+        const uint32_t vu = *reinterpret_cast<const uint32_t*>(vb + head_off + 4 * d4);
+        auto deq = [](uint32_t u, float s) {
+          float f[4];
+          i8x4_to_f32(u, f);
+          return make_float4(__fmul_rn(f[0], s), __fmul_rn(f[1], s), __fmul_rn(f[2], s),
+                             __fmul_rn(f[3], s));
+        };
+        *reinterpret_cast<float4*>(k + j * QS + 4 * d4) = deq(ku, ks);
+        *reinterpret_cast<float4*>(v + j * VS + 4 * d4) = deq(vu, vs);
+        continue;
+      }
       const size_t off = kv_row_offset(p.kv.block_table, p.kv.bt_stride, p.kv.page, p.kv.cap,
                                        p.kv.circular, seq, tt, p.kv.kv_dim) + head_off + 4 * d4;
-      if constexpr (BF) {
+      if constexpr (DT == 1) {
         *reinterpret_cast<float4*>(k + j * QS + 4 * d4) = kv_get4(p.kv.k, 1, off);
         *reinterpret_cast<float4*>(v + j * VS + 4 * d4) = kv_get4(p.kv.v, 1, off);
       } else {
@@ -290,7 +309,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) attn_prefill_kernel(const AttnP
   }
 }
 
-template <int HD, int G, bool BF>
+template <int HD, int G, int DT>
 static cudaError_t launch_pf(const AttnParams& p, cudaStream_t s, bool pdl) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.n_blocks, p.n_kv, 1);
@@ -302,7 +321,7 @@ static cudaError_t launch_pf(const AttnParams& p, cudaStream_t s, bool pdl) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, attn_prefill_kernel<HD, G, BF>, p);
+  return cudaLaunchKernelEx(&cfg, attn_prefill_kernel<HD, G, DT>, p);
 }
 
 #define MS_PF_CASES(X)                                                                   \
@@ -324,12 +343,14 @@ int attention_prefill_tokens(int hd, int group) {
 // 16-byte aligned; every block has at most attention_prefill_tokens() rows.
 cudaError_t launch_attention_prefill(const AttnParams& p, cudaStream_t s, bool pdl) {
   if (p.n_blocks < 1 || !p.blocks || (p.ldq & 3) || (p.ldo & 3) || (p.kv.kv_dim & 3) ||
-      (p.kv.bf16 && (p.kv.kv_dim & 7)))
+      (p.kv.bf16 && (p.kv.kv_dim & 7)) ||
+      (p.kv.i8 && ((p.kv.row_bytes & 15) || p.kv.hd != p.hd)))
     return cudaErrorInvalidConfiguration;
   const int G = p.n_heads / p.n_kv;
 #define MS_PF_CASE(HDV, GV)                                                  \
   if (p.hd == HDV && G == GV)                                                \
-    return p.kv.bf16 ? launch_pf<HDV, GV, true>(p, s, pdl) : launch_pf<HDV, GV, false>(p, s, pdl);
+    return p.kv.i8 ? launch_pf<HDV, GV, 2>(p, s, pdl)                        \
+                   : (p.kv.bf16 ? launch_pf<HDV, GV, 1>(p, s, pdl) : launch_pf<HDV, GV, 0>(p, s, pdl));
   MS_PF_CASES(MS_PF_CASE)
 #undef MS_PF_CASE
   return cudaErrorInvalidConfiguration;
@@ -337,12 +358,12 @@ cudaError_t launch_attention_prefill(const AttnParams& p, cudaStream_t s, bool p
 
 cudaError_t prepare_attention_prefill() {
   cudaError_t e = cudaSuccess;
-#define MS_PF_PREP1(HDV, GV, BFV)                                                            \
+#define MS_PF_PREP1(HDV, GV, DTV)                                                            \
   if (e == cudaSuccess)                                                                      \
-    e = cudaFuncSetAttribute(attn_prefill_kernel<HDV, GV, BFV>,                             \
+    e = cudaFuncSetAttribute(attn_prefill_kernel<HDV, GV, DTV>,                             \
                              cudaFuncAttributeMaxDynamicSharedMemorySize,                   \
                              (int)(PfTc<HDV>::smem_floats * sizeof(float)));
-#define MS_PF_PREP(HDV, GV) MS_PF_PREP1(HDV, GV, false) MS_PF_PREP1(HDV, GV, true)
+#define MS_PF_PREP(HDV, GV) MS_PF_PREP1(HDV, GV, 0) MS_PF_PREP1(HDV, GV, 1) MS_PF_PREP1(HDV, GV, 2)
   MS_PF_CASES(MS_PF_PREP)
 #undef MS_PF_PREP
 #undef MS_PF_PREP1

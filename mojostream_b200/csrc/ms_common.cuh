@@ -147,6 +147,11 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src)
                : "memory");
 }
+// 4-byte form (through L1; cp.async.cg takes only 16 bytes).
+__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src)
+               : "memory");
+}
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>
 __device__ __forceinline__ void cp_async_wait() {
@@ -266,6 +271,18 @@ __device__ __forceinline__ bool wait_counter_sys(const int* ctr, int target) {
 
 // Error bits a kernel can leave for the host (ms_sync reports them).
 constexpr int kErrWaitTimeout = 1;
+
+// Four int8 values (bytes of w, lowest first) as exact floats without the
+// quarter-rate int-to-float conversion: with the sign bits flipped a byte is
+// b + 128 in 0..255; placed in the mantissa of 2^23 (0x4B0000xx) it is the
+// float 2^23 + b + 128, and subtracting 2^23 + 128 leaves b exactly.
+__device__ __forceinline__ void i8x4_to_f32(uint32_t w, float* f) {
+  const uint32_t u = w ^ 0x80808080u;
+  f[0] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7650)) - 8388736.0f;
+  f[1] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7651)) - 8388736.0f;
+  f[2] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7652)) - 8388736.0f;
+  f[3] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7653)) - 8388736.0f;
+}
 
 // Slot of absolute position p in a sequence's KV ring (circular: p % cap).
 // Store one value into a K / V pool at element index idx: fp32, or bfloat16

@@ -70,11 +70,11 @@ __device__ __forceinline__ void epilogue_row(const GemvParams& p, int tile, int 
         o[td.col_lo + g] = a;
         o[td.col_hi + g] = b;
       } else {
-        const size_t off = kv_row_offset(p.kv.block_table, p.kv.bt_stride, p.kv.page, p.kv.cap,
-                                         p.kv.circular, p.seq[m], p.pos[m], p.kv.kv_dim);
-        float* pool = td.dst == 1 ? p.kv.k : p.kv.v;
-        kv_put(pool, p.kv.bf16, off + td.col_lo + g, a);
-        kv_put(pool, p.kv.bf16, off + td.col_hi + g, b);
+        size_t off;
+        int bf;
+        float* pool = kv_dst(p.kv, td.dst, m, p.seq[m], p.pos[m], off, bf);
+        kv_put(pool, bf, off + td.col_lo + g, a);
+        kv_put(pool, bf, off + td.col_hi + g, b);
       }
       break;
     }

@@ -490,10 +490,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const GemvParams
             base = p.q_out;
             off = (size_t)m * p.ldq;
           } else {
-            off = kv_row_offset(p.kv.block_table, p.kv.bt_stride, p.kv.page, p.kv.cap,
-                                p.kv.circular, p.seq[m], pos, p.kv.kv_dim);
-            base = td.dst == 1 ? p.kv.k : p.kv.v;
-            bf = p.kv.bf16;
+            base = kv_dst(p.kv, td.dst, m, p.seq[m], pos, off, bf);
           }
           kv_put2(base, bf, off + td.col_lo + g0, lo[0], lo[1]);
           kv_put2(base, bf, off + td.col_hi + g0, hi[0], hi[1]);

@@ -60,7 +60,50 @@ struct KvView {
   int bt_stride, page, cap, circular, kv_dim;
   int off32;                 // every row offset of the pool fits 32 bits
   int bf16;                  // K / V stored as bfloat16 (k, v then point at bf16 pools)
+  // int8 cache: a position's row is kv_dim int8 values, then one fp32 scale
+  // per KV head (hd values each), padded to row_bytes (a 16-byte multiple);
+  // value = int8 * scale.  The projections write fp32 rows [M][kv_dim] to
+  // stage_k / stage_v, and launch_kv_quant moves them into the cache.
+  int i8, row_bytes, hd;
+  float* stage_k;
+  float* stage_v;
 };
+
+// Row index (page * page_size + slot within the page) of absolute position p
+// of sequence seq in a layer's pool.
+__device__ __forceinline__ size_t kv_row_index(const KvView& kv, int seq, int p) {
+  const int slot = kv.circular ? (p % kv.cap) : p;
+  const int phys = kv.block_table[seq * kv.bt_stride + slot / kv.page];
+  return (size_t)phys * (size_t)kv.page + (size_t)(slot % kv.page);
+}
+
+// Where a projection writes the K (dst 1) or V (dst 2) values of its row m
+// (sequence seq, position pos): element `off` of the returned fp32 / bf16
+// pool, or for an int8 cache row m of the fp32 staging rows.
+__device__ __forceinline__ float* kv_dst(const KvView& kv, int dst, int m, int seq, int pos,
+                                         size_t& off, int& bf) {
+  if (kv.i8) {
+    off = (size_t)m * kv.kv_dim;
+    bf = 0;
+    return dst == 1 ? kv.stage_k : kv.stage_v;
+  }
+  off = kv_row_index(kv, seq, pos) * (size_t)kv.kv_dim;
+  bf = kv.bf16;
+  return dst == 1 ? kv.k : kv.v;
+}
+
+// int8 cache quantisation of one head row with absolute maximum amax:
+// scale = amax / 127, q = rint(v * (127 / amax)) clamped to [-127, 127]
+// (every step one IEEE-rounded operation, so a CPU restatement reproduces
+// it bit for bit); an all-zero row has scale 0 and q 0.
+__device__ __forceinline__ void i8_scale(float amax, float& scale, float& inv) {
+  scale = __fdiv_rn(amax, 127.0f);
+  inv = amax > 0.f ? __fdiv_rn(127.0f, amax) : 0.f;
+}
+__device__ __forceinline__ int i8_quant(float v, float inv) {
+  const float r = rintf(__fmul_rn(v, inv));
+  return (int)fminf(fmaxf(r, -127.f), 127.f);
+}
 
 struct GemvParams {
   const uint4* w;    // fragment tiles
@@ -218,6 +261,10 @@ cudaError_t launch_argmax_unpack(int* ids, const unsigned long long* key, int M,
 // from (dir 1) dense fp32 device buffers [n][kv_dim].
 cudaError_t launch_kv_copy(const KvView& kv, int seq, int pos0, int n, float* k, float* v,
                            int dir, cudaStream_t s);
+// int8 cache: quantise the M staged fp32 K / V rows (kv.stage_k / stage_v)
+// into the cache rows of (seq[m], pos[m]), one scale per KV head.
+cudaError_t launch_kv_quant(const KvView& kv, const int* seq, const int* pos, int M,
+                            cudaStream_t s, bool pdl);
 cudaError_t launch_rowstats(float* stats, const float* x, int ldx, int M, int D,
                             cudaStream_t s, bool pdl);
 cudaError_t launch_advance_step(int* ids, const int* next, int* pos, int* hist, int* step, int M,

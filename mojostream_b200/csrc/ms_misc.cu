@@ -494,11 +494,82 @@ cudaError_t launch_argmax_unpack(int* ids, const unsigned long long* key, int M,
 // layer's paged pool and dense fp32 buffers [n][kv_dim]: dir 0 writes the
 // cache (rounding to bfloat16 for a bf16 cache, as the QKV epilogue does),
 // dir 1 reads it (widened to fp32).  One CTA per position.
+// One warp: head row src[0 .. hd) of an int8 cache into dst (hd bytes) and
+// its scale (i8_scale / i8_quant).
+__device__ void i8_head_row(const float* src, unsigned char* dst, float* scale_out, int hd,
+                            int lane) {
+  float amax = 0.f;
+  for (int i = lane; i < hd / 4; i += kWarp) {
+    const float4 t = __ldcg(reinterpret_cast<const float4*>(src) + i);
+    amax = fmaxf(amax, fmaxf(fmaxf(fabsf(t.x), fabsf(t.y)), fmaxf(fabsf(t.z), fabsf(t.w))));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  float scale, inv;
+  i8_scale(amax, scale, inv);
+  for (int i = lane; i < hd / 4; i += kWarp) {
+    const float4 t = __ldcg(reinterpret_cast<const float4*>(src) + i);
+    const uint32_t w = (uint32_t)(i8_quant(t.x, inv) & 0xff) |
+                       ((uint32_t)(i8_quant(t.y, inv) & 0xff) << 8) |
+                       ((uint32_t)(i8_quant(t.z, inv) & 0xff) << 16) |
+                       ((uint32_t)(i8_quant(t.w, inv) & 0xff) << 24);
+    reinterpret_cast<uint32_t*>(dst)[i] = w;
+  }
+  if (lane == 0) *scale_out = scale;
+}
+
+// int8 cache: grid (M, n_kv), warp 0 quantises row m's K head hk, warp 1
+// its V head.
+__global__ void kv_quant_kernel(KvView kv, const int* seq, const int* pos) {
+  const int m = blockIdx.x, hk = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pdl_wait();
+  pdl_trigger();
+  const size_t row = kv_row_index(kv, seq[m], pos[m]);
+  unsigned char* base = reinterpret_cast<unsigned char*>(warp == 0 ? kv.k : kv.v) +
+                        row * (size_t)kv.row_bytes;
+  const float* src = (warp == 0 ? kv.stage_k : kv.stage_v) + (size_t)m * kv.kv_dim + hk * kv.hd;
+  i8_head_row(src, base + (size_t)hk * kv.hd,
+              reinterpret_cast<float*>(base + kv.kv_dim) + hk, kv.hd, lane);
+}
+
+cudaError_t launch_kv_quant(const KvView& kv, const int* seq, const int* pos, int M,
+                            cudaStream_t s, bool pdl) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(M, kv.kv_dim / kv.hd);
+  cfg.blockDim = dim3(2 * kWarp);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kv_quant_kernel, kv, seq, pos);
+}
+
 __global__ void kv_copy_kernel(KvView kv, int seq, int pos0, float* k, float* v, int dir) {
-  const size_t off = kv_row_offset(kv.block_table, kv.bt_stride, kv.page, kv.cap, kv.circular,
-                                   seq, pos0 + (int)blockIdx.x, kv.kv_dim);
   float* kr = k + (size_t)blockIdx.x * kv.kv_dim;
   float* vr = v + (size_t)blockIdx.x * kv.kv_dim;
+  if (kv.i8) {  // one head row of K or V per warp (int8 values + scale)
+    const size_t row = kv_row_index(kv, seq, pos0 + (int)blockIdx.x);
+    const int n_kv = kv.kv_dim / kv.hd, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int t = warp; t < 2 * n_kv; t += blockDim.x >> 5) {
+      const int h = t % n_kv;
+      unsigned char* base = reinterpret_cast<unsigned char*>(t < n_kv ? kv.k : kv.v) +
+                            row * (size_t)kv.row_bytes;
+      float* sc = reinterpret_cast<float*>(base + kv.kv_dim) + h;
+      float* f = (t < n_kv ? kr : vr) + (size_t)h * kv.hd;
+      if (dir == 0) {
+        i8_head_row(f, base + (size_t)h * kv.hd, sc, kv.hd, lane);
+      } else {
+        const float scale = *sc;
+        const signed char* q = reinterpret_cast<const signed char*>(base + (size_t)h * kv.hd);
+        for (int i = lane; i < kv.hd; i += kWarp) f[i] = __fmul_rn((float)q[i], scale);
+      }
+    }
+    return;
+  }
+  const size_t off = kv_row_offset(kv.block_table, kv.bt_stride, kv.page, kv.cap, kv.circular,
+                                   seq, pos0 + (int)blockIdx.x, kv.kv_dim);
   for (int i = threadIdx.x; i < kv.kv_dim; i += blockDim.x) {
     if (dir == 0) {
       kv_put(kv.k, kv.bf16, off + i, kr[i]);

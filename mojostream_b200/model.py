@@ -70,12 +70,15 @@ class ModelSpec:
     def lm_head_bytes(self):
         return 4 * self.hidden * self.vocab
 
-    def kv_bytes_per_seq(self, seq_len, slide_cap=None):
-        """fp32 K+V bytes one decode step reads for a sequence of seq_len."""
+    def kv_bytes_per_seq(self, seq_len, slide_cap=None, dtype="f32"):
+        """K+V bytes one decode step reads for a sequence of seq_len: fp32,
+        bf16, or int8 (a byte per value plus a 4-byte scale per KV head)."""
         total = 0
         for l in self.layers:
             n = min(seq_len, l.window) if l.window > 0 else seq_len
-            total += 2 * 4 * n * l.kv_dim
+            row = {"f32": 4 * l.kv_dim, "bf16": 2 * l.kv_dim,
+                   "i8": l.kv_dim + 4 * l.n_kv_heads}[dtype]
+            total += 2 * n * row
         return total
 
 

@@ -275,12 +275,13 @@ class KVCache:
     """ms_kv: paged cache for n_seq sequences."""
 
     def __init__(self, ctx, model, n_seq, max_pos, slide_cap=0, dtype="f32", pool_pages=0):
-        """dtype "f32" (the parity mode) or "bf16" (half the cache bytes);
+        """dtype "f32" (the parity mode), "bf16" (half the cache bytes) or
+        "i8" (int8 with one scale per position and KV head: about a quarter);
         pool_pages > 0: the full-attention layers share a pool of that many
         16-position pages (ms_kv_create_pooled)."""
         self.ctx, self.n_seq, self.max_pos, self.dtype = ctx, n_seq, max_pos, dtype
         h = ctypes.c_void_p()
-        code = {"f32": 0, "bf16": 1}[dtype]
+        code = {"f32": 0, "bf16": 1, "i8": 2}[dtype]
         if pool_pages:
             ctx.check(lib().ms_kv_create_pooled(ctx.h, model.h, n_seq, max_pos, slide_cap, code,
                                                 pool_pages, ctypes.byref(h)))

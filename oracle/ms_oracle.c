@@ -42,6 +42,39 @@ static float round_bf16(float f)
     return f;
 }
 
+void orc_quant_i8(const float *x, int n, signed char *q, float *scale)
+{
+    float amax = 0.0f;
+    for (int i = 0; i < n; ++i) {
+        const float a = fabsf(x[i]);
+        if (a > amax) amax = a;
+    }
+    const float s = amax / 127.0f;
+    const float inv = amax > 0.0f ? 127.0f / amax : 0.0f;
+    for (int i = 0; i < n; ++i) {
+        float r = rintf(x[i] * inv);
+        if (r > 127.0f) r = 127.0f;
+        if (r < -127.0f) r = -127.0f;
+        q[i] = (signed char)r;
+    }
+    *scale = s;
+}
+
+void orc_quant_i8_rows(const float *x, int rows, int n, signed char *q, float *scale)
+{
+    for (int r = 0; r < rows; ++r)
+        orc_quant_i8(x + (size_t)r * n, n, q + (size_t)r * n, scale + r);
+}
+
+/* A head row as the int8 cache holds it: q * scale, in place. */
+static void round_i8_row(float *x, int n)
+{
+    signed char q[1024];
+    float s;
+    orc_quant_i8(x, n, q, &s);
+    for (int i = 0; i < n; ++i) x[i] = (float)q[i] * s;
+}
+
 /* kernels.mojo:100-108: low nibble -> even column, high nibble -> odd column,
  * value (nibble - 8) * scale. */
 float orc_dequant(const uint8_t *w, int N, int k, int n, float scale)
@@ -378,6 +411,11 @@ int orc_layer_forward(const orc_layer_t *L, int D, float *x, int M,
             for (int j = 0; j < kvd; ++j) {
                 kv->k[off + j] = round_bf16(kv->k[off + j]);
                 kv->v[off + j] = round_bf16(kv->v[off + j]);
+            }
+        if (kv->i8)
+            for (int h = 0; h < nkv; ++h) {
+                round_i8_row(kv->k + off + (size_t)h * hd, hd);
+                round_i8_row(kv->v + off + (size_t)h * hd, hd);
             }
     }
     /* 5. attention (main.mojo:445-519; gemma4_e4b.mojo:259-411) */

@@ -50,7 +50,17 @@ typedef struct {
     int frozen;        /* != 0: orc_layer_forward attends over the cache as it is and
                           writes no K / V row (a checker that has copied another
                           implementation's rows in compares only the arithmetic) */
+    int i8;            /* != 0: every K / V head row is stored as the int8 cache
+                          reads it back (orc_quant_i8, then q * scale) */
 } orc_kv_layer_t;
+
+/* int8 KV cache quantisation of one head row x[0..n): scale = amax / 127,
+ * q[i] = rint(x[i] * (127 / amax)) clamped to [-127, 127] (amax = max |x|;
+ * an all-zero row has scale 0).  Each step is one IEEE-rounded float
+ * operation: the GPU cache computes the same bits. */
+void orc_quant_i8(const float *x, int n, signed char *q, float *scale);
+/* orc_quant_i8 over rows head rows of n values each (x, q: [rows][n]). */
+void orc_quant_i8_rows(const float *x, int rows, int n, signed char *q, float *scale);
 
 /* kernels.mojo:100-108 (dequant_vec): value of logical column n in row k. */
 float orc_dequant(const uint8_t *w, int N, int k, int n, float scale);

@@ -34,7 +34,8 @@ class OrcLayer(ctypes.Structure):
 
 class OrcKVLayer(ctypes.Structure):
     _fields_ = [("n_seq", ctypes.c_int), ("cap", ctypes.c_int), ("kv_dim", ctypes.c_int),
-                ("k", _f32p), ("v", _f32p), ("bf16", ctypes.c_int), ("frozen", ctypes.c_int)]
+                ("k", _f32p), ("v", _f32p), ("bf16", ctypes.c_int), ("frozen", ctypes.c_int),
+                ("i8", ctypes.c_int)]
 
 
 def build():
@@ -76,6 +77,9 @@ def lib():
         L.orc_temperature_sampling.restype = ctypes.c_int
         L.orc_sample_target.argtypes = [ctypes.c_uint64]
         L.orc_sample_target.restype = ctypes.c_float
+        L.orc_quant_i8.argtypes = [_f32p, ctypes.c_int, ctypes.POINTER(ctypes.c_int8), _f32p]
+        L.orc_quant_i8_rows.argtypes = [_f32p, ctypes.c_int, ctypes.c_int,
+                                        ctypes.POINTER(ctypes.c_int8), _f32p]
         _lib = L
     return _lib
 
@@ -119,6 +123,17 @@ def dequant(W, N, scale):
     return out
 
 
+def quant_i8(x):
+    """int8 KV cache quantisation of each row of x (one head row per row):
+    (q int8 [n][hd], scale fp32 [n]); the row reads back as q * scale."""
+    x = _f32(np.atleast_2d(x))
+    q = np.empty(x.shape, np.int8)
+    s = np.empty(x.shape[0], np.float32)
+    lib().orc_quant_i8_rows(_p(x, _f32p), x.shape[0], x.shape[1],
+                            q.ctypes.data_as(ctypes.POINTER(ctypes.c_int8)), _p(s, _f32p))
+    return q, s
+
+
 def rmsnorm(x):
     x = _f32(x).copy()
     lib().orc_rmsnorm(_p(x, _f32p), x.shape[0], x.shape[1])
@@ -155,10 +170,12 @@ class OracleModel:
 
     ``slide_cap`` is the slot count of circular (sliding-window) caches; the
     reference uses exactly the window (gemma4_e4b.mojo:219-228).  ``kv_bf16``
-    keeps K / V rounded to bfloat16 (the GPU's reduced-precision cache).
+    keeps K / V rounded to bfloat16 (the GPU's reduced-precision cache);
+    ``kv_i8`` keeps each K / V head row as the int8 cache reads it back.
     """
 
-    def __init__(self, spec, weights, n_seq, max_pos, slide_cap=None, workers=1, kv_bf16=False):
+    def __init__(self, spec, weights, n_seq, max_pos, slide_cap=None, workers=1, kv_bf16=False,
+                 kv_i8=False):
         self.spec, self.w, self.workers = spec, weights, workers
         self._layers, self._kv, self._keep = [], [], []
         for li, ls in enumerate(spec.layers):
@@ -181,6 +198,7 @@ class OracleModel:
             kv.n_seq, kv.cap, kv.kv_dim = n_seq, cap, kvd
             kv.k, kv.v = _p(kb, _f32p), _p(vb, _f32p)
             kv.bf16 = 1 if kv_bf16 else 0
+            kv.i8 = 1 if kv_i8 else 0
             self._kv.append((kv, kb, vb))
 
     def kv_arrays(self, layer):

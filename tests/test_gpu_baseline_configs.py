@@ -65,7 +65,7 @@ def teacher_forced(torch, model, kv, om, calls, x_of, label, kv_sync=None, quiet
     same input rows (x_of(call index, seq, pos) gives the first layer's input;
     each later layer takes the oracle's output).  Asserts the flat per-layer
     bar and returns (worst error, the oracle's last-layer rows of the last call).
-    kv_sync ("bf16" / "f32"): after each layer the rows the GPU wrote are
+    kv_sync ("bf16" / "i8" / "f32"): after each layer the rows the GPU wrote are
     checked against the oracle's and copied into the oracle's cache; if any
     element differed the oracle layer is re-run over the synchronised cache, so
     the layer comparison sees identical inputs and cache."""
@@ -252,13 +252,20 @@ def e4b_two_layers():
     return ModelSpec("e4b-2", 2560, [slide, full], 0, (0.005, 0.02))
 
 
-@pytest.mark.parametrize("kv_dtype", ["f32", "bf16"])
+def i8_roundtrip(oracle_lib, a, hd):
+    """Rows a [n][kv_dim] as the int8 cache holds them (oracle quantiser)."""
+    q, s = oracle_lib.quant_i8(a.reshape(-1, hd))
+    return (q.astype(np.float32) * s[:, None]).reshape(a.shape)
+
+
+@pytest.mark.parametrize("kv_dtype", ["f32", "bf16", "i8"])
 def test_long_context_decode_global_merge(ctx, torch_cuda, oracle_lib, kv_dtype):
     """Batch 8 decode rows at positions 4100..4400 of an 8192-position cache
     (full layer: 32 splits per (row, KV head), merged through global memory
     and the last CTA; sliding layer: the 512 window of a wrapped ring).  The
     caches hold seeded K / V values below the rows' positions, written into
-    both sides (ms_kv_write on the GPU)."""
+    both sides (ms_kv_write on the GPU; for the int8 cache the oracle holds
+    its own quantisation of them, which the GPU's must equal bit for bit)."""
     from mojostream_b200.runtime import KVCache, Model
     torch = torch_cuda
     spec = e4b_two_layers()
@@ -266,7 +273,8 @@ def test_long_context_decode_global_merge(ctx, torch_cuda, oracle_lib, kv_dtype)
     B, cap = 8, 8192
     model = Model(ctx, spec, w, max_rows=B)
     kv = KVCache(ctx, model, B, cap, slide_cap=528, dtype=kv_dtype)
-    om = oracle_lib.OracleModel(spec, w, B, cap, slide_cap=528, kv_bf16=kv_dtype == "bf16")
+    om = oracle_lib.OracleModel(spec, w, B, cap, slide_cap=528, kv_bf16=kv_dtype == "bf16",
+                                kv_i8=kv_dtype == "i8")
     base = [4100 + 37 * s for s in range(B)]
     rng = np.random.default_rng(77)
     for l, ls in enumerate(spec.layers):
@@ -283,6 +291,8 @@ def test_long_context_decode_global_merge(ctx, torch_cuda, oracle_lib, kv_dtype)
                 k = (k.view(np.uint32) & 0xFFFF0000).view(np.float32)
                 v = (v.view(np.uint32) & 0xFFFF0000).view(np.float32)
             kv.write(l, s, p0, to_dev(torch, k), to_dev(torch, v))
+            if kv_dtype == "i8":  # what the int8 cache reads back
+                k, v = (i8_roundtrip(oracle_lib, a, ls.head_dim) for a in (k, v))
             slots = np.arange(p0, n) % kb.shape[1]
             kb[s, slots] = k
             vb[s, slots] = v

@@ -173,6 +173,40 @@ def test_shared_prefix(ctx, torch_cuda, oracle_lib, model_w, pool_pages):
     model.close()
 
 
+@pytest.mark.parametrize("pool_pages", [0, 16])
+def test_i8_shared_prefix_copies_scales(ctx, torch_cuda, model_w, pool_pages):
+    """int8 cache: a shared prefix (whole pages by reference, the last page
+    copied; sliding rings copied) reads back in the new slot bit for bit,
+    scales included, and a copy-on-write leaves the source slot alone."""
+    from mojostream_b200.runtime import KVCache, Model
+    torch = torch_cuda
+    spec, w = model_w
+    (prefix,) = prompts([40], 49)
+    model = Model(ctx, spec, w, max_rows=64)
+    kv = KVCache(ctx, model, 2, 128, slide_cap=96, dtype="i8", pool_pages=pool_pages)
+    ids, seq, pos = prefill_rows([prefix], [0])
+    model.prefill(kv, ids, seq, pos)
+    kv.share_prefix(0, 1, 40)
+    for l, ls in enumerate(spec.layers):
+        a = kv.read(l, 0, 0, 40, ls.kv_dim)
+        b = kv.read(l, 1, 0, 40, ls.kv_dim)
+        torch.cuda.synchronize()
+        assert torch.equal(a[0], b[0]) and torch.equal(a[1], b[1]), l
+        assert float(a[0].abs().max()) > 0
+    full = [l for l, ls in enumerate(spec.layers) if ls.window == 0][0]
+    kvd = spec.layers[full].kv_dim
+    k0, _ = kv.read(full, 0, 5, 1, kvd)
+    z = torch.full((1, kvd), 0.5, device="cuda")
+    kv.write(full, 1, 5, z, z)
+    k0b, _ = kv.read(full, 0, 5, 1, kvd)
+    k1b, _ = kv.read(full, 1, 5, 1, kvd)
+    torch.cuda.synchronize()
+    want = float(np.float32(127) * (np.float32(0.5) / np.float32(127)))  # q 127, scale 0.5 / 127
+    assert torch.equal(k0, k0b) and bool((k1b == want).all())
+    kv.close()
+    model.close()
+
+
 def test_pool_exhaustion_is_an_error_before_launch(ctx, torch_cuda, model_w):
     from mojostream_b200._lib import MsError
     from mojostream_b200.runtime import KVCache, Model

@@ -141,14 +141,15 @@ def run_teacher_forced(ctx, torch, oracle_lib, spec, weights, n_seq, max_pos, ca
     wrote are compared with the oracle's and copied into the oracle's cache
     (parity_util.sync_kv_rows), so both sides attend over identical caches.
     The bar is a flat `tol` per layer.  kv_dtype "bf16": the GPU cache holds
-    bfloat16 and the oracle rounds its K / V the same way.  Returns the worst
-    per-layer rel-RMSE."""
+    bfloat16 and the oracle rounds its K / V the same way; "i8": int8 with a
+    scale per head row, and the oracle stores each row as that cache reads it
+    back.  Returns the worst per-layer rel-RMSE."""
     from mojostream_b200.runtime import KVCache, Model
     M = max(len(s) for s, _ in calls)
     model = Model(ctx, spec, weights, max_rows=M)
     kv = KVCache(ctx, model, n_seq, max_pos, slide_cap, dtype=kv_dtype)
     om = oracle_lib.OracleModel(spec, weights, n_seq, max_pos, slide_cap=slide_cap or None,
-                                kv_bf16=kv_dtype == "bf16")
+                                kv_bf16=kv_dtype == "bf16", kv_i8=kv_dtype == "i8")
     rng = np.random.default_rng(11)
     worst, flips, n = 0.0, 0, 0
     for seq, pos in calls:
@@ -310,6 +311,144 @@ def test_bf16_kv_greedy_generate_matches_oracle(ctx, torch_cuda, oracle_lib):
     print(f"bf16 KV greedy ids: {exact} exact, near-ties {near}")
     assert exact >= 0.8 * dev.size, (exact, near)
     assert kv.nbytes * 2 == KVCache(ctx, model, 3, 128, slide_cap=64).nbytes
+
+
+# ------------------------------------------------------------ int8 KV --
+
+def test_i8_kv_write_read_bit_exact(ctx, torch_cuda, oracle_lib):
+    """ms_kv_write into an int8 cache quantises each head row exactly as the
+    oracle's quantiser (int8 q, scale = max|v| / 127; read back as q * scale,
+    bit for bit), for sliding (ring) and full layers, rows of very different
+    magnitudes and an all-zero row; the cache is about a quarter of fp32."""
+    from mojostream_b200.runtime import KVCache, Model
+    torch = torch_cuda
+    spec = small_spec(vocab=0, n_layers=2, window=32)
+    w = synth_weights(spec, seed=51)
+    model = Model(ctx, spec, w, max_rows=16)
+    kv = KVCache(ctx, model, 2, 96, slide_cap=48, dtype="i8")
+    rng = np.random.default_rng(52)
+    for l, ls in enumerate(spec.layers):
+        n = 40
+        k = rng.standard_normal((n, ls.kv_dim)).astype(np.float32)
+        v = rng.standard_normal((n, ls.kv_dim)).astype(np.float32)
+        k *= np.float32(10.0) ** rng.integers(-6, 6, size=(n, 1)).astype(np.float32)
+        k[3] = 0.0
+        v[7, : ls.head_dim] = 0.0
+        kv.write(l, 1, 20, to_dev(torch, k), to_dev(torch, v))
+        kg, vg = kv.read(l, 1, 20, n, ls.kv_dim)
+        torch.cuda.synchronize()
+        for a, g in ((k, kg), (v, vg)):
+            q, s = oracle_lib.quant_i8(a.reshape(-1, ls.head_dim))
+            want = (q.astype(np.float32) * s[:, None]).reshape(a.shape)
+            assert np.array_equal(g.cpu().numpy(), want), l
+    f32 = KVCache(ctx, model, 2, 96, slide_cap=48)
+    assert kv.nbytes < 0.3 * f32.nbytes, (kv.nbytes, f32.nbytes)
+    f32.close()
+    kv.close()
+    model.close()
+
+
+def test_i8_kv_small_hybrid_decode(ctx, torch_cuda, oracle_lib):
+    """int8 cache (decode kernel, window wraps) against the oracle holding
+    the same int8 values: the fp32 bound of 1e-4 per layer."""
+    spec = small_spec(vocab=0, n_layers=6, window=32)
+    w = synth_weights(spec, seed=53)
+    calls = [([0, 1, 2], [p, p + 3, p + 9]) for p in range(0, 80)]
+    run_teacher_forced(ctx, torch_cuda, oracle_lib, spec, w, 3, 128, calls, kv_dtype="i8")
+
+
+def test_i8_kv_e4b_dims_prefill_and_decode(ctx, torch_cuda, oracle_lib):
+    """E4B layer shapes with an int8 cache: 64-row prefill chunks (tensor-core
+    projections staging K / V, the quantiser, the prefill attention
+    dequantising) past the sliding wrap, then decode rows."""
+    spec = e4b_spec(n_layers=6, vocab=0)
+    w = synth_weights(spec, seed=54)
+    calls = [([0] * 64, list(range(p, p + 64))) for p in range(0, 640, 64)]
+    calls += [([0], [640 + i]) for i in range(3)]
+    run_teacher_forced(ctx, torch_cuda, oracle_lib, spec, w, 1, 1024, calls, slide_cap=576,
+                       kv_dtype="i8")
+
+
+def test_i8_kv_changes_results_by_quantisation_only(ctx, torch_cuda, oracle_lib):
+    """Against the fp32 oracle the int8 cache moves a layer's output by the
+    quantisation of K / V (~1e-2 relative), far above fp32 noise and below
+    a wrong result."""
+    from mojostream_b200.runtime import KVCache, Model
+    torch = torch_cuda
+    spec = small_spec(vocab=0, n_layers=2, window=32)
+    w = synth_weights(spec, seed=55)
+    model = Model(ctx, spec, w, max_rows=16)
+    kv = KVCache(ctx, model, 1, 64, slide_cap=48, dtype="i8")
+    om = oracle_lib.OracleModel(spec, w, 1, 64, slide_cap=48)
+    x = (np.random.default_rng(3).standard_normal((16, spec.hidden)) * 2).astype(np.float32)
+    for l in range(2):
+        xg = to_dev(torch, x)
+        model.layer_forward(l, xg, kv, [0] * 16, list(range(16)))
+        y = om.layer_forward(l, x, [0] * 16, list(range(16)))
+        err = rel_rmse(xg.cpu().numpy(), y)
+        assert 1e-5 < err < 5e-2, (l, err)
+        x = y
+    kv.close()
+    model.close()
+
+
+def test_i8_kv_greedy_generate_matches_oracle(ctx, torch_cuda, oracle_lib):
+    """Greedy generation with an int8 cache (prefill, then the captured decode
+    loop), replayed on the oracle over the GPU's own cache: the cache the GPU
+    ended with (every layer, every written position; no ring wrapped) is
+    copied into the oracle, which then runs the prompts and the GPU's ids
+    without writing K / V.  With the caches identical only fp32 noise
+    separates the two sides: every GPU id is the oracle's best, or (once at
+    most) a near-tie within 1e-3 of the best logit; the free-running
+    comparison would instead measure the int8 rounding (a value within fp32
+    noise of a rounding boundary moves by a whole step, max|row| / 127, on
+    one side), which this model turns into logit moves of about 1."""
+    from mojostream_b200.runtime import KVCache, Model
+    torch = torch_cuda
+    spec = small_spec(vocab=4096, n_layers=6, window=32)
+    w = synth_weights(spec, seed=57, symmetric=True)
+    rng = np.random.default_rng(58)
+    prompts = [list(rng.integers(0, 4096, size=n)) for n in (9, 20, 3)]
+    steps = 16
+    model = Model(ctx, spec, w, max_rows=32)
+    kv = KVCache(ctx, model, 3, 128, slide_cap=64, dtype="i8")
+    ids = sum(prompts, [])
+    seq = sum([[s] * len(p) for s, p in enumerate(prompts)], [])
+    pos = sum([list(range(len(p))) for p in prompts], [])
+    first = model.prefill(kv, ids, seq, pos)
+    gen = model.generate(kv, first, [0, 1, 2], [len(p) for p in prompts], steps - 1)
+    dev = np.vstack([np.array(first)[None, :], gen])
+
+    om = oracle_lib.OracleModel(spec, w, 3, 128, slide_cap=64)
+    for l, ls in enumerate(spec.layers):
+        kb, vb = om.kv_arrays(l)
+        for s, p in enumerate(prompts):
+            n = len(p) + steps - 1  # positions written: the prompt and steps - 1 decode rows
+            kg, vg = kv.read(l, s, 0, n, ls.kv_dim)
+            kb[s, :n] = kg.cpu().numpy()
+            vb[s, :n] = vg.cpu().numpy()
+    om.set_kv_frozen(True)
+    last = [om.forward(om.embed(p), [s] * len(p), list(range(len(p))))[-1]
+            for s, p in enumerate(prompts)]
+    lg = om.lm_head(np.stack(last))
+    cur = [len(p) for p in prompts]
+    ties = []
+    for st in range(steps):
+        for r in range(3):
+            j, best = int(dev[st, r]), int(np.argmax(lg[r]))
+            if j != best:
+                gap = float(lg[r][best] - lg[r][j])
+                assert gap <= 1e-3 * abs(float(lg[r][best])) + 1e-4, (st, r, j, best, gap)
+                ties.append((st, r, gap))
+        if st + 1 < steps:
+            lg = om.lm_head(om.forward(om.embed([int(v) for v in dev[st]]), [0, 1, 2], cur))
+            cur = [c + 1 for c in cur]
+    print(f"int8 KV greedy ids over the GPU's cache: {dev.size - len(ties)} of {dev.size} "
+          f"identical, near-ties {ties}")
+    assert len(ties) <= 1, ties
+    assert len(set(dev.ravel().tolist())) >= 4
+    kv.close()
+    model.close()
 
 
 # ------------------------------------------------------------- lm_head --
