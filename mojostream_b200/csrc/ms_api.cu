@@ -111,6 +111,7 @@ struct ms_model {
   float* ATT = nullptr;
   float* H = nullptr;
   uint8_t* lq = nullptr;    // tensor-core scratch: limb planes (max_rows x widest K)
+  size_t lq_bytes = 0;
   float2* rowf = nullptr;   // and per-row factors
   // prefill attention: query blocks (runs of consecutive positions of one
   // sequence, at most `bq` rows each) of the rows last uploaded, per distinct
@@ -353,6 +354,7 @@ extern "C" ms_status ms_init(int device, ms_ctx** out) {
   cudaEventCreate(&c->ev[1]);
   if (prepare_gemv_stream() != cudaSuccess || prepare_attention() != cudaSuccess ||
       prepare_gemm_tc() != cudaSuccess || prepare_gemm_sk() != cudaSuccess ||
+      prepare_lm_tc() != cudaSuccess ||
       prepare_attention_prefill() != cudaSuccess) {
     ms_destroy(c);
     return MS_ERR_CUDA;
@@ -1101,6 +1103,7 @@ extern "C" ms_status ms_model_create(ms_ctx* c, const ms_model_desc* desc, ms_mo
     int kmax = std::max(D, m->max_f);
     kmax = std::max(kmax, m->max_q);
     st = model_alloc(m, &m->lq, tc_limb_bytes(R, kmax));
+    if (st == MS_OK) m->lq_bytes = tc_limb_bytes(R, kmax);
     if (st == MS_OK) st = model_alloc(m, &m->rowf, (size_t)tc_rows_pad(R));
   }
   for (const LayerDev& ld : m->layers) {
@@ -1891,9 +1894,18 @@ static ms_status lm_head_launch(ms_ctx* c, ms_model* m, const float* x, const fl
     p.argmax = m->d_lidx;
     p.maxval = m->d_maxv;
   }
-  const size_t ctas = (m->vocab_local + 511) / 512;
+  p.planes = m->lq;
+  p.planes_bytes = m->lq_bytes;
+  p.err = c->d_err;
+  // batches of 9+ rows: the tensor-core kernel (two persistent CTAs per SM,
+  // one read of the table per 64 rows); smaller ones: the CUDA-core kernel
+  const bool tc = lm_tc_ok(p);
+  const size_t ctas = tc ? (size_t)2 * c->sm_count : (m->vocab_local + 511) / 512;
   if (ctas * M > c->lm_parts) return fail(c, MS_ERR_CAPACITY, "lm_head: too many rows");
-  MS_CUDA(c, launch_lm_head(p, s, pdl));
+  if (tc)
+    MS_CUDA(c, launch_lm_tc(p, (int)ctas, s, pdl));
+  else
+    MS_CUDA(c, launch_lm_head(p, s, pdl));
   if (tp) {
     MS_CUDA(c, launch_argmax_pack(m->d_key, m->d_maxv, m->d_lidx, M, m->vocab0, s));
     MS_NCCL(c, nccl_api().all_reduce(m->d_key, m->d_key, M, ncclUint64, ncclMax, c->comm, s));

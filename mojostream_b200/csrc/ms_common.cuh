@@ -272,6 +272,15 @@ __device__ __forceinline__ bool wait_counter_sys(const int* ctr, int target) {
 // Error bits a kernel can leave for the host (ms_sync reports them).
 constexpr int kErrWaitTimeout = 1;
 
+// Greedy pick: the larger value, and among equal values the smaller index
+// (the first maximum of a left-to-right scan).
+__device__ __forceinline__ void argmax_merge(float& v, int& i, float v2, int i2) {
+  if (v2 > v || (v2 == v && i2 < i)) {
+    v = v2;
+    i = i2;
+  }
+}
+
 // Four int8 values (bytes of w, lowest first) as exact floats without the
 // quarter-rate int-to-float conversion: with the sign bits flipped a byte is
 // b + 128 in 0..255; placed in the mantissa of 2^23 (0x4B0000xx) it is the

@@ -191,6 +191,11 @@ struct LmHeadParams {
   int* counter;
   int* argmax;            // [M] or null
   float* maxval;          // [M] the maximum itself (tensor-parallel combine), or null
+  // tensor-core path (lm_tc_ok): scratch for the rows' bf16 hi / lo planes
+  // and the error word of its bounded waits
+  uint8_t* planes;
+  size_t planes_bytes;
+  int* err;
 };
 
 
@@ -263,6 +268,11 @@ cudaError_t launch_kv_copy(const KvView& kv, int seq, int pos0, int n, float* k,
                            int dir, cudaStream_t s);
 // int8 cache: quantise the M staged fp32 K / V rows (kv.stage_k / stage_v)
 // into the cache rows of (seq[m], pos[m]), one scale per KV head.
+// lm_head on the tensor cores (ms_lm_tc.cu) for batches of 9+ rows:
+// usable when lm_tc_ok(p); at most `ctas` persistent CTAs.
+bool lm_tc_ok(const LmHeadParams& p);
+cudaError_t launch_lm_tc(const LmHeadParams& p, int ctas, cudaStream_t s, bool pdl);
+cudaError_t prepare_lm_tc();
 cudaError_t launch_kv_quant(const KvView& kv, const int* seq, const int* pos, int M,
                             cudaStream_t s, bool pdl);
 cudaError_t launch_rowstats(float* stats, const float* x, int ldx, int M, int D,

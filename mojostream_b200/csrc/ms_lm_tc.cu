@@ -1,0 +1,410 @@
+// ms_lm_tc.cu -- the lm_head for batches of 9 or more rows on the
+// 5th-generation tensor cores.
+// Reference: apply_final_norm (src/inference/lm_head.mojo:119-130 ->
+// rmsnorm_weighted_inplace, src/linalg/kernels.mojo:598-613), project_lm_head
+// (lm_head.mojo:146-168 -> matmul_fp32_raw, kernels.mojo:616-671) and the
+// greedy branch of temperature_sampling (lm_head.mojo:224-230: the first
+// maximum wins).
+//
+// Why: the CUDA-core kernel (ms_misc.cu) keeps 16 normalised rows per pass
+// in shared memory and is bound by FMA issue from 8 rows up (4 passes over
+// the 2.68 GB table at batch 64 take 2.5 ms; one read of the table at the
+// measured copy bandwidth takes 0.42 ms).
+//
+// Arithmetic: logits[m][v] = sum_k xn[m][k] W[k][v] with xn the normalised
+// row exactly as the CUDA-core kernel forms it (x * inv_rms * gamma, fp32).
+// Both operands are split into bfloat16 pairs, a = a_hi + a_lo with
+// a_hi = bf16(a), a_lo = bf16(a - a_hi) (|a - a_hi - a_lo| <= 2^-18 |a|), and
+// three MMAs per k-step accumulate a_hi b_hi + a_hi b_lo + a_lo b_hi in fp32
+// tensor memory (the dropped a_lo b_lo is below 2^-16 of the product): about
+// 1e-5 relative per product, far inside the 1e-3 logits bar.
+//
+// Layout: the MMA's A operand (M = 128) is 128 vocabulary columns of W, B is
+// the batch (N = rows rounded up to 16, <= 64 per launch).  lm_rows_kernel
+// writes the rows' hi / lo planes once per launch, [k-chunk][hi | lo][N rows
+// x 32 k] in the no-swizzle K-major core-matrix layout.  The main kernel is
+// persistent: CTA b takes vocabulary groups b, b + grid, ...; per 32-k chunk
+// warp 0 bulk-copies the 32 W rows of the group (512 bytes each) and the
+// chunk's planes, warps 2-5 convert the fp32 tile in place to the hi | lo
+// core matrices, warp 1 issues the MMAs into one of two tensor-memory
+// accumulators (a group's MMAs overlap the previous group's epilogue), and
+// warps 6-9 read the finished accumulator (lane = column, column = row),
+// store the logits if asked and keep each row's running (max, first index).
+// The CTAs' per-row results are merged by the last CTA (ticket) in index
+// order.  Every wait is bounded (error word).
+#include "ms_common.cuh"
+#include "ms_kernels.h"
+#include "ms_tc.cuh"
+
+namespace ms {
+
+constexpr int kLtK = 32;                           // k per chunk: 64 bytes of bf16 per row
+constexpr int kLtV = 128;                          // vocabulary columns per group (MMA M)
+constexpr int kLtStages = 4;
+constexpr int kLtMaxN = 64;                        // rows per launch
+constexpr int kLtA = kLtV * kLtK * 4;              // 16 KB: fp32 [32 k][128 v], then hi | lo
+constexpr int kLtHalf = kLtV * kLtK * 2;           // 8 KB: one bf16 part of A
+constexpr int kLtBMax = 2 * kLtMaxN * kLtK * 2;    // 8 KB: hi | lo planes of 64 rows
+constexpr int kLtStage = kLtA + kLtBMax;           // 24 KB
+constexpr int kLtConvWarps = 4, kLtEpiWarps = 4;
+constexpr int kLtThreads = (2 + kLtConvWarps + kLtEpiWarps) * kWarp;  // 320
+constexpr uint32_t kLtCols = 2 * kLtMaxN;          // two accumulators of up to 64 columns
+constexpr uint32_t kLtLbo = 128, kLtSbo = 512;
+constexpr size_t kLtSmem = (size_t)kLtStages * kLtStage;
+
+static_assert(kLtStage % 1024 == 0, "stage alignment");
+
+// Byte offset of (row r, k-core kc) in a K-major no-swizzle operand whose
+// rows hold 64 bytes (4 core matrices along k).
+__device__ __forceinline__ uint32_t lm_core_off(int r, int kc) {
+  return (uint32_t)((r >> 3) * kLtSbo + kc * kLtLbo + (r & 7) * 16);
+}
+
+// Eight fp32 values as bf16 hi and lo halves, packed in k order.
+__device__ __forceinline__ void lm_split8(const float* v, uint4& hi, uint4& lo) {
+  uint32_t h[8], l[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) split_bf16(v[j], h[j], l[j]);
+  hi = make_uint4(h[0] | (h[1] << 16), h[2] | (h[3] << 16), h[4] | (h[5] << 16), h[6] | (h[7] << 16));
+  lo = make_uint4(l[0] | (l[1] << 16), l[2] | (l[3] << 16), l[4] | (l[5] << 16), l[6] | (l[7] << 16));
+}
+
+// One CTA per plane row r (N of them; rows past the batch are zeros):
+// xn = x * inv_rms * gamma as the CUDA-core kernel forms it, split to hi / lo.
+__global__ void __launch_bounds__(256) lm_rows_kernel(const LmHeadParams p, int row0, int N) {
+  __shared__ float s_inv;
+  const int r = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const bool live = row0 + r < p.M;
+  pdl_wait();
+  pdl_trigger();
+  if (warp == 0) {
+    float inv = 1.f;
+    if (live && p.stats) {
+      float s = 0.f;
+      for (int i = lane; i < p.nstat; i += kWarp) s += p.stats[(size_t)i * p.M + row0 + r];
+      s = warp_sum(s);
+      inv = 1.0f / sqrtf(s / (float)p.D + 1e-6f);
+    }
+    if (lane == 0) s_inv = inv;
+  }
+  __syncthreads();
+  const float inv = s_inv;
+  const size_t chunk = (size_t)2 * N * 64;  // hi | lo planes of one 32-k chunk
+  for (int i = threadIdx.x; i < p.D / 8; i += blockDim.x) {
+    const int k0 = 8 * i;
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float a = 0.f;
+      if (live) {
+        a = p.x[(size_t)(row0 + r) * p.D + k0 + j] * inv;
+        if (p.gamma) a = a * p.gamma[k0 + j];
+      }
+      v[j] = a;
+    }
+    uint4 hi, lo;
+    lm_split8(v, hi, lo);
+    uint8_t* dst = p.planes + (size_t)(k0 / kLtK) * chunk + lm_core_off(r, (k0 % kLtK) / 8);
+    *reinterpret_cast<uint4*>(dst) = hi;
+    *reinterpret_cast<uint4*>(dst + (size_t)N * 64) = lo;
+  }
+}
+
+__global__ void __launch_bounds__(kLtThreads, 2) lm_tc_kernel(const LmHeadParams p, int row0,
+                                                              int N) {
+  extern __shared__ __align__(1024) uint8_t dsm[];
+  __shared__ __align__(8) uint64_t full[kLtStages], conv[kLtStages], empty[kLtStages];
+  __shared__ __align__(8) uint64_t acc_full[2], acc_empty[2], done;
+  __shared__ uint32_t s_tmem;
+  __shared__ volatile int s_bad, s_conv_bad;
+  __shared__ float s_bv[kLtEpiWarps][kLtMaxN];
+  __shared__ int s_bi[kLtEpiWarps][kLtMaxN];
+  __shared__ int s_last;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_groups = p.V / kLtV, nk = p.D / kLtK;
+  const int ng = n_groups > (int)blockIdx.x
+                     ? (n_groups - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x
+                     : 0;
+  const int total = ng * nk;  // chunks this CTA streams
+  const int rows = min(N, p.M - row0);
+  const uint32_t b_bytes = (uint32_t)N * 64;  // one plane of a chunk
+
+  if (threadIdx.x == 0) {
+    s_bad = 0;
+    s_conv_bad = 0;
+    for (int s = 0; s < kLtStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&conv[s], kLtConvWarps);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], kLtEpiWarps);
+    }
+    mbar_init(&done, 1);
+    mbar_fence_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&s_tmem, kLtCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s_tmem;
+  pdl_trigger();
+
+  auto fail = [&]() {
+    atomicOr(p.err, kErrWaitTimeout);
+    s_bad = 1;
+  };
+
+  if (warp == 0) {
+    // ------------------------------------------------------- producer --
+    if (lane == 0) {
+      auto w_rows = [&](int t, uint8_t* st) {  // the 32 W rows of chunk t
+        const int j = t / nk, c = t % nk;
+        const int g = (int)blockIdx.x + j * (int)gridDim.x;
+        const float* src = p.W + (size_t)(c * kLtK) * p.V + (size_t)g * kLtV;
+        for (int r = 0; r < kLtK; ++r)
+          bulk_g2s(st + r * (kLtV * 4), src + (size_t)r * p.V, kLtV * 4, &full[t % kLtStages]);
+      };
+      auto planes = [&](int t, uint8_t* st) {
+        const int c = t % nk;
+        bulk_g2s(st + kLtA, p.planes + (size_t)c * 2 * b_bytes, 2 * b_bytes,
+                 &full[t % kLtStages]);
+      };
+      const int first = min(total, kLtStages);
+      for (int t = 0; t < first; ++t) {  // W does not depend on earlier kernels
+        uint8_t* st = dsm + (size_t)t * kLtStage;
+        mbar_expect_tx(&full[t], kLtA + 2 * b_bytes);
+        w_rows(t, st);
+      }
+      pdl_wait();  // the planes are lm_rows_kernel's output
+      for (int t = 0; t < first; ++t) planes(t, dsm + (size_t)t * kLtStage);
+      int t = first;
+      for (; t < total; ++t) {
+        const int s = t % kLtStages;
+        if (!mbar_wait(&empty[s], ((t / kLtStages) - 1) & 1)) {
+          fail();
+          break;
+        }
+        uint8_t* st = dsm + (size_t)s * kLtStage;
+        mbar_expect_tx(&full[s], kLtA + 2 * b_bytes);
+        w_rows(t, st);
+        planes(t, st);
+      }
+      if (s_bad) {  // let the copies already issued land before the CTA can exit
+        for (int j = t - 1; j >= 0 && j >= t - kLtStages; --j)
+          if (!mbar_wait(&full[j % kLtStages], (j / kLtStages) & 1)) break;
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------ MMA issuer --
+    if (lane == 0) {
+      const uint32_t idesc = idesc_bf16(kLtV, N);
+      for (int j = 0; j < ng && !s_bad; ++j) {
+        const int a = j & 1;
+        if (j >= 2 && !mbar_wait(&acc_empty[a], ((j >> 1) - 1) & 1)) {
+          fail();
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)(a * kLtMaxN);
+        for (int c = 0; c < nk; ++c) {
+          const int t = j * nk + c, s = t % kLtStages;
+          const uint32_t ph = (t / kLtStages) & 1;
+          if (!mbar_wait(&full[s], ph) || !mbar_wait(&conv[s], ph)) {
+            fail();
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(dsm + (size_t)s * kLtStage);
+          const uint32_t b0 = a0 + kLtA;
+#pragma unroll
+          for (int kk = 0; kk < 2; ++kk) {
+            const uint64_t ah = umma_desc(a0 + kk * 256, kLtLbo, kLtSbo);
+            const uint64_t al = umma_desc(a0 + kLtHalf + kk * 256, kLtLbo, kLtSbo);
+            const uint64_t bh = umma_desc(b0 + kk * 256, kLtLbo, kLtSbo);
+            const uint64_t bl = umma_desc(b0 + b_bytes + kk * 256, kLtLbo, kLtSbo);
+            umma_bf16(d, ah, bh, idesc, (c | kk) != 0);
+            umma_bf16(d, ah, bl, idesc, 1);
+            umma_bf16(d, al, bh, idesc, 1);
+          }
+          umma_commit(&empty[s]);
+        }
+        if (s_bad) break;
+        umma_commit(&acc_full[a]);
+      }
+      umma_commit(&done);  // arrives when every MMA issued above has finished
+    }
+  } else if (warp < 2 + kLtConvWarps) {
+    // ------------------------------------------- fp32 -> bf16 hi | lo --
+    // thread v: column v of the group; reads its 32 k values (consecutive
+    // threads, consecutive words: no bank conflicts), then, after every
+    // converter has read the tile, writes its row of the hi and lo operands
+    // over it.
+    // A timed-out wait is recorded in s_conv_bad before the barrier and
+    // read after it, so every converter warp leaves at the same chunk (none
+    // is left waiting at the barrier).
+    const int v = threadIdx.x - 2 * kWarp;
+    for (int t = 0; t < total; ++t) {
+      const int s = t % kLtStages;
+      uint8_t* st = dsm + (size_t)s * kLtStage;
+      float w[kLtK];
+      if (mbar_wait(&full[s], (t / kLtStages) & 1)) {
+        const float* raw = reinterpret_cast<const float*>(st);
+#pragma unroll
+        for (int k = 0; k < kLtK; ++k) w[k] = raw[k * kLtV + v];
+      } else {
+        s_conv_bad = 1;
+        fail();
+      }
+      bar_sync_n(1, kLtConvWarps * kWarp);  // the whole tile is read
+      if (s_conv_bad) break;
+#pragma unroll
+      for (int kc = 0; kc < kLtK / 8; ++kc) {
+        uint4 hi, lo;
+        lm_split8(w + 8 * kc, hi, lo);
+        *reinterpret_cast<uint4*>(st + lm_core_off(v, kc)) = hi;
+        *reinterpret_cast<uint4*>(st + kLtHalf + lm_core_off(v, kc)) = lo;
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&conv[s]);
+    }
+  } else {
+    // ------------------------------------------------------- epilogue --
+    // warp w reads tensor-memory lanes 32 (w % 4) .. +31: columns
+    // g * 128 + 32 (w % 4) + lane; its running (max, index) per row stays in
+    // registers of lane m % 32 (rows m and m + 32 -> two slots).
+    const int quad = warp & 3, e = warp - 2 - kLtConvWarps;
+    float bv0 = -INFINITY, bv1 = -INFINITY;
+    int bi0 = 0x7fffffff, bi1 = 0x7fffffff;
+    for (int j = 0; j < ng; ++j) {
+      const int a = j & 1;
+      if (!mbar_wait(&acc_full[a], (j >> 1) & 1)) {
+        fail();
+        break;
+      }
+      tc_fence_after();
+      const int col = ((int)blockIdx.x + j * (int)gridDim.x) * kLtV + quad * kWarp + lane;
+      for (int m0 = 0; m0 < N; m0 += 16) {
+        uint32_t r[16];
+        tmem_ld16(tmem + ((uint32_t)(quad * kWarp) << 16) + (uint32_t)(a * kLtMaxN + m0), r);
+        tmem_wait_ld();
+#pragma unroll
+        for (int q = 0; q < 16; ++q) {
+          const int m = m0 + q;
+          if (m >= rows) break;  // warp-uniform
+          float v = __uint_as_float(r[q]);
+          if (p.logits) p.logits[(size_t)(row0 + m) * p.V + col] = v;
+          int i = col;
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, i, o);
+            argmax_merge(v, i, ov, oi);
+          }
+          if (lane == (m & 31)) {
+            if (m < 32)
+              argmax_merge(bv0, bi0, v, i);
+            else
+              argmax_merge(bv1, bi1, v, i);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[a]);
+    }
+    s_bv[e][lane] = bv0;
+    s_bi[e][lane] = bi0;
+    s_bv[e][32 + lane] = bv1;
+    s_bi[e][32 + lane] = bi1;
+  }
+
+  // ---------------------------------------------------- CTA results --
+  __syncthreads();
+  if (threadIdx.x < rows) {
+    const int m = threadIdx.x;
+    float v = s_bv[0][m];
+    int i = s_bi[0][m];
+    for (int w = 1; w < kLtEpiWarps; ++w) argmax_merge(v, i, s_bv[w][m], s_bi[w][m]);
+    p.part_val[(size_t)(row0 + m) * gridDim.x + blockIdx.x] = v;
+    p.part_idx[(size_t)(row0 + m) * gridDim.x + blockIdx.x] = i;
+  }
+  if (warp == 1) {
+    // no MMA may still write the columns being freed (bounded, as every wait)
+    if (!mbar_wait(&done, 0)) atomicOr(p.err, kErrWaitTimeout);
+    tc_fence_after();
+  }
+  tc_fence_before();
+  __syncthreads();  // partials written; the MMAs are finished
+  if (warp == 1) tmem_dealloc(tmem, kLtCols);
+  if (!p.argmax) return;
+  if (threadIdx.x == 0) s_last = (ticket_acq_rel(p.counter) == (int)gridDim.x - 1);
+  __syncthreads();
+  if (!s_last) return;
+  const int nw = kLtThreads / kWarp;
+  for (int m = warp; m < rows; m += nw) {
+    float v = -INFINITY;
+    int i = 0x7fffffff;
+    for (int c = lane; c < (int)gridDim.x; c += kWarp)
+      argmax_merge(v, i, __ldcg(p.part_val + (size_t)(row0 + m) * gridDim.x + c),
+                         __ldcg(p.part_idx + (size_t)(row0 + m) * gridDim.x + c));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, i, o);
+      argmax_merge(v, i, ov, oi);
+    }
+    if (lane == 0) {
+      p.argmax[row0 + m] = i;
+      if (p.maxval) p.maxval[row0 + m] = v;
+    }
+  }
+  if (threadIdx.x == 0) *p.counter = 0;
+}
+
+bool lm_tc_ok(const LmHeadParams& p) {
+  return p.planes && p.err && p.M > 8 && p.V % kLtV == 0 && p.D % kLtK == 0 &&
+         (size_t)2 * kLtMaxN * p.D * 2 <= p.planes_bytes;
+}
+
+cudaError_t prepare_lm_tc() {
+  return cudaFuncSetAttribute(lm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              (int)kLtSmem);
+}
+
+// Rows in launches of up to 64: the planes kernel, then the persistent GEMM
+// over at most `ctas` CTAs (each pass reads the table once).
+cudaError_t launch_lm_tc(const LmHeadParams& p, int ctas, cudaStream_t s, bool pdl) {
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  const int n_groups = p.V / kLtV;
+  const int grid = ctas < n_groups ? ctas : n_groups;
+  for (int row0 = 0; row0 < p.M; row0 += kLtMaxN) {
+    const int n = p.M - row0 < kLtMaxN ? p.M - row0 : kLtMaxN;
+    const int N = (n + 15) / 16 * 16;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(N);
+    cfg.blockDim = dim3(256);
+    cfg.stream = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = (pdl || row0 > 0) ? 1 : 0;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, lm_rows_kernel, p, row0, N);
+    if (e != cudaSuccess) return e;
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kLtThreads);
+    cfg.dynamicSmemBytes = kLtSmem;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, lm_tc_kernel, p, row0, N);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+}  // namespace ms

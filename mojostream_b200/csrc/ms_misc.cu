@@ -33,13 +33,6 @@ __device__ __forceinline__ void fma2(float2& d, float2 a, float2 b) {
         "l"(reinterpret_cast<const unsigned long long&>(b)));
 }
 
-__device__ __forceinline__ void argmax_merge(float& v, int& i, float v2, int i2) {
-  if (v2 > v || (v2 == v && i2 < i)) {
-    v = v2;
-    i = i2;
-  }
-}
-
 template <int MR, int NT>
 __global__ void __launch_bounds__(NT) lm_head_kernel(const LmHeadParams p, int row0) {
   constexpr int LU = MR >= 16 ? 4 : kLmUnroll;  // W rows in flight (registers)

@@ -39,6 +39,23 @@ __device__ __forceinline__ void umma_i8(uint32_t d_tmem, uint64_t da, uint64_t d
       : "memory");
 }
 
+// Instruction descriptor of kind::f16 with bfloat16 A and B (bits 7-9,
+// 10-12 = 1) and an f32 accumulator (bits 4-5 = 1), both K-major.
+__host__ __device__ constexpr uint32_t idesc_bf16(int m, int n) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) |
+         ((uint32_t)(m >> 4) << 24);
+}
+
+// D[tmem] (+)= A[smem] * B[smem]^T, bf16 x bf16 -> f32 (K = 16 per call).
+__device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t da, uint64_t db,
+                                          uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(d_tmem),
+      "l"(da), "l"(db), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Arrive once on `bar` when every tcgen05 operation this thread issued so far
 // has completed (also when there is none).
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {

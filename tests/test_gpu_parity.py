@@ -470,9 +470,11 @@ def test_lm_head_logits_and_argmax(ctx, torch_cuda, oracle_lib):
     assert am.cpu().tolist() == om.argmax(ref)
 
 
-def test_argmax_ties_pick_the_first(ctx, torch_cuda):
+@pytest.mark.parametrize("M", [2, 12])
+def test_argmax_ties_pick_the_first(ctx, torch_cuda, M):
     """temperature_sampling's strict '>' (lm_head.mojo:226-229): among equal
-    maxima the smallest index wins, also across CTAs of the kernel."""
+    maxima the smallest index wins, also across CTAs of the kernel (2 rows:
+    the CUDA-core kernel; 12 rows: the tensor-core kernel)."""
     from mojostream_b200.runtime import Model
     torch = torch_cuda
     spec = small_spec(vocab=8192, n_layers=1)
@@ -480,11 +482,53 @@ def test_argmax_ties_pick_the_first(ctx, torch_cuda):
     w.lm_head[:] = 0.0
     w.lm_head[:, [700, 5000, 7000]] = 1.0  # three equal maxima in different CTAs
     w.final_gamma[:] = 1.0
-    model = Model(ctx, spec, w, max_rows=2)
-    x = np.ones((2, spec.hidden), np.float32)
+    model = Model(ctx, spec, w, max_rows=M)
+    x = np.ones((M, spec.hidden), np.float32)
     _, am = model.lm_head(to_dev(torch, x), logits=False)
     torch.cuda.synchronize()
-    assert am.cpu().tolist() == [700, 700]
+    assert am.cpu().tolist() == [700] * M
+
+
+@pytest.fixture(scope="module")
+def wide_lm_model():
+    """hidden 2560 (E4B's D) and 131072 vocabulary columns: 1024 column
+    groups, so each persistent CTA of the tensor-core lm_head takes several
+    (both tensor-memory accumulators, ring phases wrapping)."""
+    l = LayerSpec(64, 4, 2, 0, 64, 512, 1e4)
+    spec = ModelSpec("wide-lm", 2560, [l], 131072, (0.02, 0.06))
+    return spec, synth_weights(spec, seed=61)
+
+
+@pytest.mark.parametrize("M", [9, 16, 33, 64, 130])
+def test_lm_head_tensor_cores_match_oracle(ctx, torch_cuda, oracle_lib, wide_lm_model, M):
+    """Batches of 9+ rows run the lm_head on the tensor cores (operands split
+    into bfloat16 hi + lo, three MMAs per k-step, fp32 accumulation).  The
+    logits bar is 1e-3 rel-RMSE; the split gives about 1e-5, so the test holds
+    it to 1e-4, which a missing low part (about 2e-3) would fail.  Ids equal
+    the oracle's, except where its two best logits are closer than 1e-4 of
+    their size (then either id)."""
+    from mojostream_b200.runtime import Model
+    torch = torch_cuda
+    spec, w = wide_lm_model
+    model = Model(ctx, spec, w, max_rows=M)
+    om = oracle_lib.OracleModel(spec, w, 1, 16, workers=8)
+    x = (np.random.default_rng(M).standard_normal((M, spec.hidden)) * 3).astype(np.float32)
+    logits, am = model.lm_head(to_dev(torch, x))
+    torch.cuda.synchronize()
+    ref = om.lm_head(x)
+    err = rel_rmse(logits.cpu().numpy(), ref)
+    print(f"M={M}: logits rel-RMSE {err:.3g}")
+    assert err < 1e-4, err
+    got = am.cpu().tolist()
+    want = om.argmax(ref)
+    for r in range(M):
+        if got[r] != want[r]:
+            top = float(ref[r][want[r]])
+            assert top - float(ref[r][got[r]]) <= 1e-4 * abs(top), (r, got[r], want[r])
+    _, am2 = model.lm_head(to_dev(torch, x), logits=False)  # argmax without the logits store
+    torch.cuda.synchronize()
+    assert am2.cpu().tolist() == got
+    model.close()
 
 
 # ---------------------------------------------------------- end to end --
