@@ -112,6 +112,9 @@ struct ms_model {
   float* H = nullptr;
   uint8_t* lq = nullptr;    // tensor-core scratch: limb planes (max_rows x widest K)
   size_t lq_bytes = 0;
+  // tensor map over the lm_head table (the tensor-core lm_head), made on first use
+  alignas(64) unsigned char lm_map[128];
+  int lm_map_state = 0;  // 0 not tried, 1 made, -1 unavailable
   float2* rowf = nullptr;   // and per-row factors
   // prefill attention: query blocks (runs of consecutive positions of one
   // sequence, at most `bq` rows each) of the rows last uploaded, per distinct
@@ -1899,11 +1902,14 @@ static ms_status lm_head_launch(ms_ctx* c, ms_model* m, const float* x, const fl
   p.err = c->d_err;
   // batches of 9+ rows: the tensor-core kernel (two persistent CTAs per SM,
   // one read of the table per 64 rows); smaller ones: the CUDA-core kernel
-  const bool tc = lm_tc_ok(p);
+  bool tc = lm_tc_ok(p);
+  if (tc && m->lm_map_state == 0)
+    m->lm_map_state = lm_tc_make_map(m->lm_map, m->lm_head, m->hidden, m->vocab_local) ? 1 : -1;
+  tc = tc && m->lm_map_state == 1;
   const size_t ctas = tc ? (size_t)2 * c->sm_count : (m->vocab_local + 511) / 512;
   if (ctas * M > c->lm_parts) return fail(c, MS_ERR_CAPACITY, "lm_head: too many rows");
   if (tc)
-    MS_CUDA(c, launch_lm_tc(p, (int)ctas, s, pdl));
+    MS_CUDA(c, launch_lm_tc(p, m->lm_map, (int)ctas, s, pdl));
   else
     MS_CUDA(c, launch_lm_head(p, s, pdl));
   if (tp) {

@@ -269,9 +269,13 @@ cudaError_t launch_kv_copy(const KvView& kv, int seq, int pos0, int n, float* k,
 // int8 cache: quantise the M staged fp32 K / V rows (kv.stage_k / stage_v)
 // into the cache rows of (seq[m], pos[m]), one scale per KV head.
 // lm_head on the tensor cores (ms_lm_tc.cu) for batches of 9+ rows:
-// usable when lm_tc_ok(p); at most `ctas` persistent CTAs.
+// usable when lm_tc_ok(p) and a tensor map over W was made (lm_tc_make_map
+// writes 128 bytes, 64-byte aligned, into map_out); at most `ctas`
+// persistent CTAs.
 bool lm_tc_ok(const LmHeadParams& p);
-cudaError_t launch_lm_tc(const LmHeadParams& p, int ctas, cudaStream_t s, bool pdl);
+bool lm_tc_make_map(void* map_out, const float* W, int D, int V);
+cudaError_t launch_lm_tc(const LmHeadParams& p, const void* wmap, int ctas, cudaStream_t s,
+                         bool pdl);
 cudaError_t prepare_lm_tc();
 cudaError_t launch_kv_quant(const KvView& kv, const int* seq, const int* pos, int M,
                             cudaStream_t s, bool pdl);

@@ -24,19 +24,34 @@
 // writes the rows' hi / lo planes once per launch, [k-chunk][hi | lo][N rows
 // x 32 k] in the no-swizzle K-major core-matrix layout.  The main kernel is
 // persistent: CTA b takes vocabulary groups b, b + grid, ...; per 32-k chunk
-// warp 0 bulk-copies the 32 W rows of the group (512 bytes each) and the
-// chunk's planes, warps 2-5 convert the fp32 tile in place to the hi | lo
+// warp 0 copies the group's 32 x 128 fp32 tile of W with one 2-D tensor copy
+// (a tensor map over W; 32 row copies of 512 bytes each were bounded by the
+// per-SM rate of copy requests) and the chunk's planes, warps 2-5 convert the fp32 tile in place to the hi | lo
 // core matrices, warp 1 issues the MMAs into one of two tensor-memory
 // accumulators (a group's MMAs overlap the previous group's epilogue), and
 // warps 6-9 read the finished accumulator (lane = column, column = row),
 // store the logits if asked and keep each row's running (max, first index).
 // The CTAs' per-row results are merged by the last CTA (ticket) in index
 // order.  Every wait is bounded (error word).
+#include <cuda.h>
+
 #include "ms_common.cuh"
 #include "ms_kernels.h"
 #include "ms_tc.cuh"
 
 namespace ms {
+
+// The 2-D box [y, y + 32) x [x, x + 128) of the tensor map into dst
+// (row-major, no swizzle), completing on bar.  x * 4 bytes is a multiple of
+// 16 (x is a multiple of 128); dst is 128-byte aligned.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
 
 constexpr int kLtK = 32;                           // k per chunk: 64 bytes of bf16 per row
 constexpr int kLtV = 128;                          // vocabulary columns per group (MMA M)
@@ -111,7 +126,8 @@ __global__ void __launch_bounds__(256) lm_rows_kernel(const LmHeadParams p, int 
 }
 
 __global__ void __launch_bounds__(kLtThreads, 2) lm_tc_kernel(const LmHeadParams p, int row0,
-                                                              int N) {
+                                                              int N,
+                                                              const __grid_constant__ CUtensorMap wmap) {
   extern __shared__ __align__(1024) uint8_t dsm[];
   __shared__ __align__(8) uint64_t full[kLtStages], conv[kLtStages], empty[kLtStages];
   __shared__ __align__(8) uint64_t acc_full[2], acc_empty[2], done;
@@ -163,12 +179,10 @@ __global__ void __launch_bounds__(kLtThreads, 2) lm_tc_kernel(const LmHeadParams
   if (warp == 0) {
     // ------------------------------------------------------- producer --
     if (lane == 0) {
-      auto w_rows = [&](int t, uint8_t* st) {  // the 32 W rows of chunk t
+      auto w_rows = [&](int t, uint8_t* st) {  // the W tile of chunk t
         const int j = t / nk, c = t % nk;
         const int g = (int)blockIdx.x + j * (int)gridDim.x;
-        const float* src = p.W + (size_t)(c * kLtK) * p.V + (size_t)g * kLtV;
-        for (int r = 0; r < kLtK; ++r)
-          bulk_g2s(st + r * (kLtV * 4), src + (size_t)r * p.V, kLtV * 4, &full[t % kLtStages]);
+        tma_load_2d(st, &wmap, g * kLtV, c * kLtK, &full[t % kLtStages]);
       };
       auto planes = [&](int t, uint8_t* st) {
         const int c = t % nk;
@@ -373,6 +387,35 @@ bool lm_tc_ok(const LmHeadParams& p) {
          (size_t)2 * kLtMaxN * p.D * 2 <= p.planes_bytes;
 }
 
+// Tensor map over the fp32 table W [D][V] (V contiguous) with 32 x 128 boxes.
+bool lm_tc_make_map(void* map_out, const float* W, int D, int V) {
+  using Encode = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                              const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                              const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                              CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+  static Encode encode = nullptr;
+  if (!encode) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) !=
+            cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || !fn) {
+      cudaGetLastError();
+      return false;
+    }
+    encode = reinterpret_cast<Encode>(fn);
+  }
+  if (((uintptr_t)W & 15) || V % kLtV || D % kLtK) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)V, (cuuint64_t)D};
+  const cuuint64_t strides[1] = {(cuuint64_t)V * sizeof(float)};
+  const cuuint32_t box[2] = {kLtV, kLtK};
+  const cuuint32_t estr[2] = {1, 1};
+  return encode(reinterpret_cast<CUtensorMap*>(map_out), CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2,
+                const_cast<float*>(W), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 cudaError_t prepare_lm_tc() {
   return cudaFuncSetAttribute(lm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                               (int)kLtSmem);
@@ -380,7 +423,9 @@ cudaError_t prepare_lm_tc() {
 
 // Rows in launches of up to 64: the planes kernel, then the persistent GEMM
 // over at most `ctas` CTAs (each pass reads the table once).
-cudaError_t launch_lm_tc(const LmHeadParams& p, int ctas, cudaStream_t s, bool pdl) {
+cudaError_t launch_lm_tc(const LmHeadParams& p, const void* wmap, int ctas, cudaStream_t s,
+                         bool pdl) {
+  const CUtensorMap map = *reinterpret_cast<const CUtensorMap*>(wmap);
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
@@ -401,7 +446,7 @@ cudaError_t launch_lm_tc(const LmHeadParams& p, int ctas, cudaStream_t s, bool p
     cfg.blockDim = dim3(kLtThreads);
     cfg.dynamicSmemBytes = kLtSmem;
     cfg.numAttrs = 1;
-    e = cudaLaunchKernelEx(&cfg, lm_tc_kernel, p, row0, N);
+    e = cudaLaunchKernelEx(&cfg, lm_tc_kernel, p, row0, N, map);
     if (e != cudaSuccess) return e;
   }
   return cudaSuccess;
