@@ -394,7 +394,10 @@ def run_ours(args, ws, rank, local):
         if ws == 1:
             result["demo"] = run_demo_block(args, local)
             result["q4_sweep"] = run_q4_sweep(local)
-        result["tp"] = run_tp_block(args, ws, rank, local, D)
+        try:  # a failure here (same shapes on every rank) is reported, not fatal to the line
+            result["tp"] = run_tp_block(args, ws, rank, local, D)
+        except Exception as e:  # noqa: BLE001
+            result["tp"] = {"error": f"{type(e).__name__}: {e}"[:300]}
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(spec, args)
     if rank == 0:
