@@ -212,13 +212,15 @@ __global__ void __launch_bounds__(WarpAttn<HD, G, DT>::NT) attn_kernel(const Att
     __syncwarp();  // every lane holds its slice: the slot can be refilled
     if (((i + P) & 31) == 0) offs = row_offsets(i + P);  // warp-uniform
     issue(i + P, __shfl_sync(0xffffffffu, offs, (i + P) & 31));
+    // dot products on packed FMAs: dims 2j and 2j + 1 in two chains, added at the end
     float sc[G];
 #pragma unroll
     for (int h = 0; h < G; ++h) {
-      float d = 0.f;
+      float2 d2 = make_float2(0.f, 0.f);
 #pragma unroll
-      for (int e = 0; e < PL; ++e) d = fmaf(q[h][e], kk[e], d);
-      sc[h] = d;
+      for (int e = 0; e < PL; e += 2)
+        fma2(d2, make_float2(q[h][e], q[h][e + 1]), make_float2(kk[e], kk[e + 1]));
+      sc[h] = d2.x + d2.y;
     }
 #pragma unroll
     for (int h = 0; h < G; ++h) sc[h] = warp_sum(sc[h]) * kscale;  // G independent chains
@@ -239,7 +241,12 @@ __global__ void __launch_bounds__(WarpAttn<HD, G, DT>::NT) attn_kernel(const Att
       lrun[h] += ew;
       const float wv = DT == 2 ? ew * vscale : ew;
 #pragma unroll
-      for (int e = 0; e < PL; ++e) acc[h][e] = fmaf(wv, vv[e], acc[h][e]);
+      for (int e = 0; e < PL; e += 2) {
+        float2 a2 = make_float2(acc[h][e], acc[h][e + 1]);
+        fma2(a2, make_float2(wv, wv), make_float2(vv[e], vv[e + 1]));
+        acc[h][e] = a2.x;
+        acc[h][e + 1] = a2.y;
+      }
     }
   }
   cp_async_wait<0>();  // (only empty groups remain)

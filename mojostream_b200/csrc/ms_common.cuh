@@ -272,6 +272,16 @@ __device__ __forceinline__ bool wait_counter_sys(const int* ctr, int target) {
 // Error bits a kernel can leave for the host (ms_sync reports them).
 constexpr int kErrWaitTimeout = 1;
 
+// d = a * b + d on two lanes of fp32 at once (sm_100's packed FMA: each
+// element rounds exactly as fmaf does, one instruction for both).
+__device__ __forceinline__ void fma2(float2& d, float2 a, float2 b) {
+  unsigned long long& dd = reinterpret_cast<unsigned long long&>(d);
+  asm("fma.rn.f32x2 %0, %1, %2, %0;"
+      : "+l"(dd)
+      : "l"(reinterpret_cast<const unsigned long long&>(a)),
+        "l"(reinterpret_cast<const unsigned long long&>(b)));
+}
+
 // Greedy pick: the larger value, and among equal values the smaller index
 // (the first maximum of a left-to-right scan).
 __device__ __forceinline__ void argmax_merge(float& v, int& i, float v2, int i2) {

@@ -23,16 +23,6 @@ namespace ms {
 constexpr int kLmThreads = 128;  // CTA size of the 4-row pass (decode batches)
 constexpr int kLmUnroll = 8;
 
-// d = a * b + c on two lanes of fp32 at once (sm_100's packed FMA: each
-// element rounds exactly as fmaf does, one instruction for both).
-__device__ __forceinline__ void fma2(float2& d, float2 a, float2 b) {
-  unsigned long long& dd = reinterpret_cast<unsigned long long&>(d);
-  asm("fma.rn.f32x2 %0, %1, %2, %0;"
-      : "+l"(dd)
-      : "l"(reinterpret_cast<const unsigned long long&>(a)),
-        "l"(reinterpret_cast<const unsigned long long&>(b)));
-}
-
 template <int MR, int NT>
 __global__ void __launch_bounds__(NT) lm_head_kernel(const LmHeadParams p, int row0) {
   constexpr int LU = MR >= 16 ? 4 : kLmUnroll;  // W rows in flight (registers)
