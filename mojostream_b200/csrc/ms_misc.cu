@@ -223,24 +223,26 @@ cudaError_t launch_lm_head(const LmHeadParams& p, cudaStream_t s, bool pdl) {
 __global__ void embed_kernel(float* x, float* stats, const float* __restrict__ W,
                              const int* __restrict__ ids, int M, int D, int V, int v0,
                              TokenLog log, const float* __restrict__ bos, int bos_id) {
+  // grid (M, D / 256): one value per thread, so the strided column reads of a
+  // row (one table row apart each) are all in flight at once across many SMs
   pdl_trigger();
   pdl_wait();
-  const int m = blockIdx.x;
-  if (log.tok && threadIdx.x == 0) log.tok[(size_t)log.seq[m] * log.ld + log.pos[m]] = ids[m];
+  const int m = blockIdx.x, d = blockIdx.y * blockDim.x + threadIdx.x;
+  if (log.tok && blockIdx.y == 0 && threadIdx.x == 0)
+    log.tok[(size_t)log.seq[m] * log.ld + log.pos[m]] = ids[m];
   const bool is_bos = bos && ids[m] == bos_id;
   const int id = ids[m] - v0;
   const bool mine = is_bos ? v0 == 0 : (id >= 0 && id < V);
-  for (int t = threadIdx.x; t < D / kTileN; t += blockDim.x) {
-    float sq = 0.f;
-#pragma unroll
-    for (int j = 0; j < kTileN; ++j) {
-      const int d = t * kTileN + j;
-      const float v = mine ? (is_bos ? bos[d] : W[(size_t)d * V + id]) : 0.f;
-      x[(size_t)m * D + d] = v;
-      sq += v * v;
-    }
-    stats[(size_t)t * M + m] = sq;
+  float v = 0.f;
+  if (d < D) {
+    v = mine ? (is_bos ? bos[d] : W[(size_t)d * V + id]) : 0.f;
+    x[(size_t)m * D + d] = v;
   }
+  // the 16 values of tile d / 16 sit in 16 consecutive lanes (D % 16 == 0)
+  float sq = v * v;
+#pragma unroll
+  for (int o = 1; o < kTileN; o <<= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+  if (d < D && (d % kTileN) == 0) stats[(size_t)(d / kTileN) * M + m] = sq;
 }
 
 // Row statistics of caller-provided rows: stats[t][m] = sum of squares of the
@@ -363,8 +365,8 @@ cudaError_t launch_embed_stats(float* x, float* stats, const float* W,
                                const int* ids, int M, int D, int V, cudaStream_t s, bool pdl,
                                int v0, TokenLog log, const float* bos, int bos_id) {
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(M);
-  cfg.blockDim = dim3(128);
+  cfg.gridDim = dim3(M, (D + 255) / 256);
+  cfg.blockDim = dim3(256);
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
