@@ -615,6 +615,8 @@ static ms_status ensure_tc_scratch(ms_ctx* c, int M, int K) {
   return MS_OK;
 }
 
+constexpr int kMaxDecodeCluster = 8;  // k-segments that merge inside one cluster
+
 static GemvPlan plan_gemv(const ms_ctx* c, int M, int K, int n_tiles, bool allow_tc = true,
                           bool allow_sk = true) {
   GemvPlan pl{};
@@ -656,7 +658,8 @@ static GemvPlan plan_gemv(const ms_ctx* c, int M, int K, int n_tiles, bool allow
     const int mb = 4 * pl.mg;
     const int groups = padded_tiles(n_tiles) / kGroupTiles;
     const int seg_max = pl.mg == 1 ? 40 : 20;
-    int ksplit = std::max(1, (c->sm_count + groups / 2) / groups);
+    // at least one CTA per SM (rounded up; at most a cluster of 8 k-segments)
+    int ksplit = std::max(1, std::min(kMaxDecodeCluster, (c->sm_count + groups - 1) / groups));
     ksplit = std::max(ksplit, (chunks + seg_max - 1) / seg_max);
     ksplit = std::min(ksplit, chunks);
     // a group whose whole K is at most 32 chunks (128 KB of weights, twice
