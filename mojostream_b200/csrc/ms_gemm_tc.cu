@@ -81,15 +81,27 @@ __global__ void __launch_bounds__(kQThreads) quant_rows_kernel(const GemvParams 
   pdl_wait();
   pdl_trigger();
   const float* x = p.x + (size_t)(live ? m : 0) * p.ldx;
+  // a thread's subtiles are i = s_begin + sub0 + 32 u; they are loaded kQB at
+  // a time (all loads of a batch issued before any use)
+  constexpr int kQB = 4, kQStep = kQThreads / 8;
   float a = 0.f;
   if (live)
-    for (int i = s_begin + sub0; i < s_end; i += kQThreads / 8) {
-      const float4* v4 = reinterpret_cast<const float4*>(x + 16 * i);
+    for (int i0 = s_begin + sub0; i0 < s_end; i0 += kQB * kQStep) {
+      float4 b[kQB][4];
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const float4 v = __ldg(v4 + q);
-        a = fmaxf(a, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+      for (int u = 0; u < kQB; ++u) {
+        const int i = i0 + u * kQStep;
+        const float4* v4 = reinterpret_cast<const float4*>(x + 16 * i);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) b[u][q] = i < s_end ? __ldg(v4 + q) : make_float4(0.f, 0.f, 0.f, 0.f);
       }
+#pragma unroll
+      for (int u = 0; u < kQB; ++u)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float4 v = b[u][q];
+          a = fmaxf(a, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+        }
     }
   // lanes with equal lane % 8 share a row
   a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 8));
@@ -139,46 +151,50 @@ __global__ void __launch_bounds__(kQThreads) quant_rows_kernel(const GemvParams 
     }
   }
 
-  for (int i = s_begin + sub0; i < s_end; i += kQThreads / 8) {
-    float v[16];
-    if (live) {
+  for (int i0 = s_begin + sub0; i0 < s_end; i0 += kQB * kQStep) {
+    float4 b[kQB][4];
+#pragma unroll
+    for (int u = 0; u < kQB; ++u) {
+      const int i = i0 + u * kQStep;
       const float4* v4 = reinterpret_cast<const float4*>(x + 16 * i);
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const float4 t4 = __ldg(v4 + q);
-        v[4 * q] = t4.x;
-        v[4 * q + 1] = t4.y;
-        v[4 * q + 2] = t4.z;
-        v[4 * q + 3] = t4.w;
+      for (int q = 0; q < 4; ++q)
+        b[u][q] = (live && i < s_end) ? __ldg(v4 + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int u = 0; u < kQB; ++u) {
+      const int i = i0 + u * kQStep;
+      if (i >= s_end) break;
+      const float v[16] = {b[u][0].x, b[u][0].y, b[u][0].z, b[u][0].w,
+                           b[u][1].x, b[u][1].y, b[u][1].z, b[u][1].w,
+                           b[u][2].x, b[u][2].y, b[u][2].z, b[u][2].w,
+                           b[u][3].x, b[u][3].y, b[u][3].z, b[u][3].w};
+      uint32_t wl[kTcLimbs][4];
+#pragma unroll
+      for (int l = 0; l < kTcLimbs; ++l)
+#pragma unroll
+        for (int t = 0; t < 4; ++t) wl[l][t] = 0u;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int t = j >> 2, e = j & 3;
+        const int k = 2 * t + (e & 1) * 8 + (e >> 1);
+        int q = __float2int_rn(v[k] * inv);
+        const int d0 = (int)(int8_t)(q & 0xFF);
+        q = (q - d0) >> 8;  // exact: a multiple of 256
+        const int d1 = (int)(int8_t)(q & 0xFF);
+        q = (q - d1) >> 8;  // |q| <= 64
+        wl[0][t] |= ((uint32_t)d0 & 0xFFu) << (8 * e);
+        wl[1][t] |= ((uint32_t)d1 & 0xFFu) << (8 * e);
+        wl[2][t] |= ((uint32_t)q & 0xFFu) << (8 * e);
       }
-    } else {
+      const int c = i >> 2, s = i & 3;
+      uint8_t* dst = p.lq + (size_t)(mt * nchunks + c) * kTcAStage + ((r >> 3) * 4 + s) * 128 +
+                     (r & 7) * 16;
 #pragma unroll
-      for (int q = 0; q < 16; ++q) v[q] = 0.f;
+      for (int l = 0; l < kTcLimbs; ++l)
+        *reinterpret_cast<uint4*>(dst + l * kTcPlane) =
+            make_uint4(wl[l][0], wl[l][1], wl[l][2], wl[l][3]);
     }
-    uint32_t wl[kTcLimbs][4];
-#pragma unroll
-    for (int l = 0; l < kTcLimbs; ++l)
-#pragma unroll
-      for (int t = 0; t < 4; ++t) wl[l][t] = 0u;
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const int t = j >> 2, e = j & 3;
-      const int k = 2 * t + (e & 1) * 8 + (e >> 1);
-      int q = __float2int_rn(v[k] * inv);
-      const int d0 = (int)(int8_t)(q & 0xFF);
-      q = (q - d0) >> 8;  // exact: a multiple of 256
-      const int d1 = (int)(int8_t)(q & 0xFF);
-      q = (q - d1) >> 8;  // |q| <= 64
-      wl[0][t] |= ((uint32_t)d0 & 0xFFu) << (8 * e);
-      wl[1][t] |= ((uint32_t)d1 & 0xFFu) << (8 * e);
-      wl[2][t] |= ((uint32_t)q & 0xFFu) << (8 * e);
-    }
-    const int c = i >> 2, s = i & 3;
-    uint8_t* dst = p.lq + (size_t)(mt * nchunks + c) * kTcAStage + ((r >> 3) * 4 + s) * 128 +
-                   (r & 7) * 16;
-#pragma unroll
-    for (int l = 0; l < kTcLimbs; ++l)
-      *reinterpret_cast<uint4*>(dst + l * kTcPlane) = make_uint4(wl[l][0], wl[l][1], wl[l][2], wl[l][3]);
   }
 }
 
