@@ -366,11 +366,12 @@ def run_ours(args, ws, rank, local):
             "launch_ms": round(proj_ms, 5),
         },
         "roofline_lm_head": {
-            "kernel": "lm_head_kernel (fp32 [2560 x 262144], argmax fused)",
+            "kernel": "lm_ring_kernel (fp32 [2560 x 262144] streamed by 2-D tensor copies, "
+                      "argmax fused)",
             "bound": "hbm", "achieved": round(lm_bytes / (lm_ms / 1e3) / 1e9, 1),
             "peak": hbm, "unit": "GB/s",
             "frac": round(lm_bytes / (lm_ms / 1e3) / 1e9 / hbm, 4),
-            "traffic": profile_traffic("lm_head_kernel"),
+            "traffic": profile_traffic("lm_ring_kernel"),
             "traffic_source": "ncu capture summarised in profiles/ (not this run)",
             "algorithmic_bytes": lm_bytes, "peak_source": peak_kind,
             "launch_ms": round(lm_ms, 4),

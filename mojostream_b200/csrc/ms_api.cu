@@ -1910,15 +1910,21 @@ static ms_status lm_head_launch(ms_ctx* c, ms_model* m, const float* x, const fl
   p.planes_bytes = m->lq_bytes;
   p.err = c->d_err;
   // batches of 9+ rows: the tensor-core kernel (two persistent CTAs per SM,
-  // one read of the table per 64 rows); smaller ones: the CUDA-core kernel
-  bool tc = lm_tc_ok(p);
-  if (tc && m->lm_map_state == 0)
+  // one read of the table per 64 rows); up to 8 rows: the CUDA-core kernel
+  // fed by a ring of tensor copies (one persistent CTA per SM), or, when its
+  // rows do not fit beside the ring, the register-staged CUDA-core kernel
+  bool tc = lm_tc_ok(p), ring = !tc && lm_ring_ok(p);
+  if ((tc || ring) && m->lm_map_state == 0)
     m->lm_map_state = lm_tc_make_map(m->lm_map, m->lm_head, m->hidden, m->vocab_local) ? 1 : -1;
   tc = tc && m->lm_map_state == 1;
-  const size_t ctas = tc ? (size_t)2 * c->sm_count : (m->vocab_local + 511) / 512;
+  ring = ring && m->lm_map_state == 1;
+  const size_t ctas = tc ? (size_t)2 * c->sm_count
+                          : ring ? (size_t)c->sm_count : (m->vocab_local + 511) / 512;
   if (ctas * M > c->lm_parts) return fail(c, MS_ERR_CAPACITY, "lm_head: too many rows");
   if (tc)
     MS_CUDA(c, launch_lm_tc(p, m->lm_map, (int)ctas, s, pdl));
+  else if (ring)
+    MS_CUDA(c, launch_lm_ring(p, m->lm_map, (int)ctas, s, pdl));
   else
     MS_CUDA(c, launch_lm_head(p, s, pdl));
   if (tp) {

@@ -274,6 +274,11 @@ cudaError_t launch_kv_copy(const KvView& kv, int seq, int pos0, int n, float* k,
 // persistent CTAs.
 bool lm_tc_ok(const LmHeadParams& p);
 bool lm_tc_make_map(void* map_out, const float* W, int D, int V);
+// Up to 8 rows on CUDA cores with the table streamed through a shared-memory
+// ring of tensor copies (same tensor map); one persistent CTA per SM.
+bool lm_ring_ok(const LmHeadParams& p);
+cudaError_t launch_lm_ring(const LmHeadParams& p, const void* wmap, int ctas, cudaStream_t s,
+                           bool pdl);
 cudaError_t launch_lm_tc(const LmHeadParams& p, const void* wmap, int ctas, cudaStream_t s,
                          bool pdl);
 cudaError_t prepare_lm_tc();

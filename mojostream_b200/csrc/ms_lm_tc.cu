@@ -382,6 +382,235 @@ __global__ void __launch_bounds__(kLtThreads, 2) lm_tc_kernel(const LmHeadParams
   if (threadIdx.x == 0) *p.counter = 0;
 }
 
+// =========================================================================
+// Up to 8 rows: fp32 FMAs on CUDA cores (the reference's arithmetic), with
+// the table streamed through shared memory.  One persistent CTA per SM holds
+// the normalised rows once and walks vocabulary groups b, b + grid, ...;
+// warp 8 streams each group's 32 x 128 W tiles through an 8-stage ring of
+// 2-D tensor copies (128 KB in flight per SM; the register-staged kernel in
+// ms_misc.cu keeps about 57 KB in flight and its 40 KB of rows per CTA cap
+// how many CTAs an SM holds).  Warps 0-7: thread (column c = t % 128,
+// k-half h = t / 128) sums rows 16 h .. 16 h + 15 of every tile in k order;
+// the halves are added per group (half 0 + half 1), then logits and each
+// row's running (max, first index).
+// =========================================================================
+constexpr int kLrStages = 8;
+constexpr int kLrWarps = 8;                        // compute warps
+constexpr int kLrThreads = (kLrWarps + 1) * kWarp;  // + the copy warp
+constexpr int kLrMaxM = 8;
+constexpr size_t kLrRing = (size_t)kLrStages * kLtA;  // 128 KB
+
+template <int MR>
+__global__ void __launch_bounds__(kLrThreads, 1) lm_ring_kernel(const LmHeadParams p,
+                                                                const __grid_constant__ CUtensorMap wmap) {
+  extern __shared__ __align__(1024) uint8_t dsm[];
+  float* ring = reinterpret_cast<float*>(dsm);                 // [stages][32][128]
+  float* xs = reinterpret_cast<float*>(dsm + kLrRing);         // [MR][D]
+  float* red = xs + (size_t)MR * p.D;                          // [MR][128] half-1 sums
+  __shared__ __align__(8) uint64_t full[kLrStages], empty[kLrStages];
+  __shared__ float s_inv[MR];
+  __shared__ float s_bv[kLrWarps / 2][MR];
+  __shared__ int s_bi[kLrWarps / 2][MR];
+  __shared__ int s_last;
+  __shared__ volatile int s_bad;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int n_groups = p.V / kLtV, nk = p.D / kLtK;
+  const int ng = n_groups > (int)blockIdx.x
+                     ? (n_groups - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x
+                     : 0;
+  const int total = ng * nk;
+  const int rows = min(MR, p.M);
+
+  if (tid == 0) {
+    s_bad = 0;
+    for (int s = 0; s < kLrStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kLrWarps);
+    }
+    mbar_fence_init();
+  }
+  __syncthreads();
+  pdl_trigger();
+
+  if (warp == kLrWarps) {
+    // ------------------------------------------------ tile copies --
+    if (lane == 0) {
+      auto issue = [&](int t) {
+        const int s = t % kLrStages, j = t / nk, c = t % nk;
+        mbar_expect_tx(&full[s], kLtA);
+        tma_load_2d(ring + (size_t)s * (kLtA / 4), &wmap,
+                    ((int)blockIdx.x + j * (int)gridDim.x) * kLtV, c * kLtK, &full[s]);
+      };
+      const int first = min(total, kLrStages);
+      for (int t = 0; t < first; ++t) issue(t);  // W does not depend on earlier kernels
+      int t = first;
+      for (; t < total; ++t) {
+        if (!mbar_wait(&empty[t % kLrStages], ((t / kLrStages) - 1) & 1)) {
+          atomicOr(p.err, kErrWaitTimeout);
+          s_bad = 1;
+          break;
+        }
+        issue(t);
+      }
+      if (s_bad)  // let the copies already issued land before the CTA can exit
+        for (int j = t - 1; j >= 0 && j >= t - kLrStages; --j)
+          if (!mbar_wait(&full[j % kLrStages], (j / kLrStages) & 1)) break;
+    }
+    pdl_wait();
+  } else {
+    // --------------------------------------------- rows, then FMAs --
+    pdl_wait();
+    for (int r = warp; r < MR; r += kLrWarps) {
+      float inv = 1.f;
+      if (r < rows && p.stats) {
+        float s = 0.f;
+        for (int i = lane; i < p.nstat; i += kWarp) s += p.stats[(size_t)i * p.M + r];
+        s = warp_sum(s);
+        inv = 1.0f / sqrtf(s / (float)p.D + 1e-6f);
+      }
+      if (lane == 0) s_inv[r] = inv;
+    }
+    bar_sync_n(1, kLrWarps * kWarp);
+    for (int idx = tid; idx < MR * p.D; idx += kLrWarps * kWarp) {
+      const int r = idx / p.D, k = idx % p.D;
+      float v = 0.f;
+      if (r < rows) {
+        v = p.x[(size_t)r * p.D + k] * s_inv[r];
+        if (p.gamma) v = v * p.gamma[k];
+      }
+      xs[idx] = v;
+    }
+    bar_sync_n(1, kLrWarps * kWarp);
+
+    const int c = tid & (kLtV - 1), h = tid >> 7;  // column of the group, k-half
+    float bv[MR];
+    int bi[MR];
+#pragma unroll
+    for (int r = 0; r < MR; ++r) {
+      bv[r] = -INFINITY;
+      bi[r] = 0x7fffffff;
+    }
+    // Every compute thread walks every group and takes every barrier; after
+    // a timed-out wait it stops waiting (the error word is set) and sums
+    // whatever the ring holds, so no warp is left at a barrier.
+    bool failed = false;
+    for (int j = 0; j < ng; ++j) {
+      float acc[MR];
+#pragma unroll
+      for (int r = 0; r < MR; ++r) acc[r] = 0.f;
+      for (int ck = 0; ck < nk; ++ck) {
+        const int t = j * nk + ck, s = t % kLrStages;
+        if (!failed && !mbar_wait(&full[s], (t / kLrStages) & 1)) {
+          atomicOr(p.err, kErrWaitTimeout);
+          failed = true;
+        }
+        const float* w = ring + (size_t)s * (kLtA / 4) + (16 * h) * kLtV + c;
+        const float* xk = xs + ck * kLtK + 16 * h;
+#pragma unroll
+        for (int u = 0; u < 16; ++u) {
+          const float wv = w[u * kLtV];
+#pragma unroll
+          for (int r = 0; r < MR; ++r) acc[r] = fmaf(xk[r * p.D + u], wv, acc[r]);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+      }
+      // the two halves of each column: half 1 parks its sums, half 0 adds them
+      if (h == 1)
+#pragma unroll
+        for (int r = 0; r < MR; ++r) red[r * kLtV + c] = acc[r];
+      bar_sync_n(1, kLrWarps * kWarp);
+      if (h == 0) {
+        const int col = ((int)blockIdx.x + j * (int)gridDim.x) * kLtV + c;
+#pragma unroll
+        for (int r = 0; r < MR; ++r) {
+          float v = acc[r] + red[r * kLtV + c];
+          if (r < rows && p.logits) p.logits[(size_t)r * p.V + col] = v;
+          int i = col;
+          if (r >= rows) v = -INFINITY;
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, i, o);
+            argmax_merge(v, i, ov, oi);
+          }
+          argmax_merge(bv[r], bi[r], v, i);
+        }
+      }
+      bar_sync_n(1, kLrWarps * kWarp);  // red is free for the next group
+    }
+    if (h == 0 && lane == 0)
+#pragma unroll
+      for (int r = 0; r < MR; ++r) {
+        s_bv[warp][r] = bv[r];
+        s_bi[warp][r] = bi[r];
+      }
+  }
+  __syncthreads();
+  if (tid < rows) {
+    float v = s_bv[0][tid];
+    int i = s_bi[0][tid];
+    for (int w = 1; w < kLrWarps / 2; ++w) argmax_merge(v, i, s_bv[w][tid], s_bi[w][tid]);
+    p.part_val[(size_t)tid * gridDim.x + blockIdx.x] = v;
+    p.part_idx[(size_t)tid * gridDim.x + blockIdx.x] = i;
+  }
+  if (!p.argmax) return;
+  __syncthreads();  // partials written
+  if (tid == 0) s_last = (ticket_acq_rel(p.counter) == (int)gridDim.x - 1);
+  __syncthreads();
+  if (!s_last) return;
+  for (int r = warp; r < rows; r += kLrThreads / kWarp) {
+    float v = -INFINITY;
+    int i = 0x7fffffff;
+    for (int cc = lane; cc < (int)gridDim.x; cc += kWarp)
+      argmax_merge(v, i, __ldcg(p.part_val + (size_t)r * gridDim.x + cc),
+                   __ldcg(p.part_idx + (size_t)r * gridDim.x + cc));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, i, o);
+      argmax_merge(v, i, ov, oi);
+    }
+    if (lane == 0) {
+      p.argmax[r] = i;
+      if (p.maxval) p.maxval[r] = v;
+    }
+  }
+  if (tid == 0) *p.counter = 0;
+}
+
+static size_t lm_ring_smem(int mr, int D) {
+  return kLrRing + (size_t)mr * D * 4 + (size_t)mr * kLtV * 4;
+}
+
+bool lm_ring_ok(const LmHeadParams& p) {
+  return p.err && p.M >= 1 && p.M <= kLrMaxM && p.V % kLtV == 0 && p.D % kLtK == 0 &&
+         lm_ring_smem(p.M <= 4 ? 4 : 8, p.D) <= 220 * 1024;
+}
+
+cudaError_t launch_lm_ring(const LmHeadParams& p, const void* wmap, int ctas, cudaStream_t s,
+                           bool pdl) {
+  const CUtensorMap map = *reinterpret_cast<const CUtensorMap*>(wmap);
+  const int mr = p.M <= 4 ? 4 : 8;
+  const size_t smem = lm_ring_smem(mr, p.D);
+  auto kern = mr == 4 ? lm_ring_kernel<4> : lm_ring_kernel<8>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  const int n_groups = p.V / kLtV;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(ctas < n_groups ? ctas : n_groups);
+  cfg.blockDim = dim3(kLrThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, p, map);
+}
+
 bool lm_tc_ok(const LmHeadParams& p) {
   return p.planes && p.err && p.M > 8 && p.V % kLtV == 0 && p.D % kLtK == 0 &&
          (size_t)2 * kLtMaxN * p.D * 2 <= p.planes_bytes;
