@@ -147,11 +147,13 @@ struct ms_model {
   cudaGraphExec_t gexec = nullptr;
   int g_M = 0, g_samp = -1;
   const ms_kv* g_kv = nullptr;
+  unsigned long long g_kv_uid = 0;  // the cache's id: a new cache may reuse a freed one's address
   std::vector<void*> allocs;
 };
 
 struct ms_kv {
   const ms_model* model = nullptr;
+  unsigned long long uid = 0;  // never reused (kv_create numbers every cache)
   int n_seq = 0, max_pos = 0, slide_cap = 0, page = 16;
   int pages_full = 0, pages_slide = 0;  // per sequence
   std::vector<float*> k, v;
@@ -1223,7 +1225,9 @@ static ms_status kv_create(ms_ctx* c, const ms_model* m, int n_seq, int max_pos,
         return fail(c, MS_ERR_SHAPE, "kv: an int8 cache needs head_dim %% 16 == 0 (%d)",
                     L.d.head_dim);
   cudaSetDevice(c->device);
+  static std::atomic<unsigned long long> next_uid{1};
   ms_kv* kv = new ms_kv();
+  kv->uid = next_uid.fetch_add(1);
   kv->model = m;
   kv->bf16 = dtype == MS_KV_BF16;
   kv->i8 = dtype == MS_KV_I8;
@@ -2079,9 +2083,13 @@ static ms_status decode_body(ms_ctx* c, ms_model* m, const ms_kv* kv, int M, cud
 
 // The decode step captured as a CUDA graph.  No launch shape depends on the
 // positions (they are read from d_pos on the device), so one graph serves a
-// whole generation.
+// whole generation.  The graph holds the cache's device pointers, so it is
+// reused only for the same cache: same address and same id (a cache created
+// after another was destroyed can get its address).
 static ms_status ensure_graph(ms_ctx* c, ms_model* m, const ms_kv* kv, int M) {
-  if (m->gexec && m->g_M == M && m->g_kv == kv && m->g_samp == m->samp_ver) return MS_OK;
+  if (m->gexec && m->g_M == M && m->g_kv == kv && m->g_kv_uid == kv->uid &&
+      m->g_samp == m->samp_ver)
+    return MS_OK;
   if (m->gexec) {
     cudaGraphExecDestroy(m->gexec);
     m->gexec = nullptr;
@@ -2102,6 +2110,7 @@ static ms_status ensure_graph(ms_ctx* c, ms_model* m, const ms_kv* kv, int M) {
   if (e != cudaSuccess) return fail(c, MS_ERR_CUDA, "graph instantiate: %s", cudaGetErrorString(e));
   m->g_M = M;
   m->g_kv = kv;
+  m->g_kv_uid = kv->uid;
   m->g_samp = m->samp_ver;
   return MS_OK;
 }

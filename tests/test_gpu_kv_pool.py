@@ -207,6 +207,29 @@ def test_i8_shared_prefix_copies_scales(ctx, torch_cuda, model_w, pool_pages):
     model.close()
 
 
+def test_generate_with_a_new_cache_after_one_was_closed(ctx, torch_cuda, oracle_lib, model_w):
+    """ms_generate keeps its decode step as a captured graph that holds the
+    cache's device pointers.  Caches of different sizes are created, used and
+    closed one after another on one model (a new cache can get a closed one's
+    host address); each must get its own graph: every run's ids equal the
+    oracle's."""
+    from mojostream_b200.runtime import KVCache, Model
+    spec, w = model_w
+    P = prompts([12, 7], 51)
+    model = Model(ctx, spec, w, max_rows=32)
+    ids, seq, pos = prefill_rows(P, [0, 1])
+    refs = [oracle_run(oracle_lib, spec, w, p, 6, 48) for p in P]
+    for max_pos in (128, 256, 192):
+        kv = KVCache(ctx, model, 2, max_pos, slide_cap=48)
+        first = model.prefill(kv, ids, seq, pos)
+        gen = model.generate(kv, first, [0, 1], [len(p) for p in P], 6)
+        got = np.vstack([np.array(first)[None, :], gen])
+        for s in range(2):
+            assert list(got[:, s]) == refs[s], (max_pos, s)
+        kv.close()
+    model.close()
+
+
 def test_pool_exhaustion_is_an_error_before_launch(ctx, torch_cuda, model_w):
     from mojostream_b200._lib import MsError
     from mojostream_b200.runtime import KVCache, Model
