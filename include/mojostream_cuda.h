@@ -266,6 +266,18 @@ MS_API ms_status ms_kv_share_prefix(ms_ctx *ctx, ms_kv *kv, int src_seq, int dst
 /* Full-attention pages in use and in total (pooled: the pool; otherwise
  * n_seq x ceil(max_pos / 16), all of them in use). */
 MS_API ms_status ms_kv_pages(const ms_kv *kv, int *used, int *total);
+/* allow != 0: calls may hold rows of one sequence whose sliding-window slots
+ * overlap slots that other rows of the same call still attend.  By default
+ * such a call is rejected (MS_ERR_CAPACITY) before any kernel runs.  With it
+ * allowed, the call behaves as the reference's E4B runner: every row's K / V
+ * is written (slot p % slide_cap) before any row attends, so a row reads
+ * whatever the call left in its window's slots.  That is the runner's
+ * padding quirk: row 0 plus three zero rows at positions p+1..p+3
+ * (src/inference/lm_head.mojo:133-143, gemma4_e4b_infer.mojo:45-54), whose
+ * K / V overwrite slots 512 positions back once p >= 511
+ * (write_kv_sliding, src/inference/gemma4_e4b.mojo:211-228).  Reproducing it
+ * exactly needs slide_cap equal to the window (slide_cap 0 at ms_kv_create). */
+MS_API ms_status ms_kv_allow_window_overwrite(ms_ctx *ctx, ms_kv *kv, int allow);
 MS_API ms_status ms_kv_destroy(ms_ctx *ctx, ms_kv *kv);
 /* K / V rows of positions pos0 .. pos0 + n - 1 of sequence seq in layer
  * `layer`, to or from dense fp32 device buffers k, v [n][kv_dim] (the

@@ -94,6 +94,7 @@ SIGNATURES = {
     "ms_kv_share_prefix": (ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int]),
     "ms_kv_pages": (ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_int),
                                    ctypes.POINTER(ctypes.c_int)]),
+    "ms_kv_allow_window_overwrite": (ctypes.c_int, [_vp, _vp, ctypes.c_int]),
     "ms_kv_destroy": (ctypes.c_int, [_vp, _vp]),
     "ms_kv_reset": (ctypes.c_int, [_vp, _vp]),
     "ms_kv_bytes": (ctypes.c_size_t, [_vp]),

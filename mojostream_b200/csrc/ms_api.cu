@@ -161,6 +161,7 @@ struct ms_kv {
   int* bt_slide = nullptr;
   int* tok = nullptr;  // [n_seq][max_pos] token fed at each position (-1: none)
   int bf16 = 0;        // K / V pools hold bfloat16
+  int allow_overwrite = 0;  // calls may overwrite sliding slots still in a window
   // int8 pools (value = int8 * scale, one fp32 scale per position and KV head
   // behind the row's values) and the fp32 rows the projections write before
   // launch_kv_quant moves them in: K [max_rows][stage_ld], then V
@@ -1509,6 +1510,12 @@ extern "C" ms_status ms_kv_share_prefix(ms_ctx* c, ms_kv* kv, int src, int dst, 
   return MS_OK;
 }
 
+extern "C" ms_status ms_kv_allow_window_overwrite(ms_ctx* c, ms_kv* kv, int allow) {
+  if (!c || !kv) return MS_ERR_INVALID_ARG;
+  kv->allow_overwrite = allow != 0;
+  return MS_OK;
+}
+
 extern "C" ms_status ms_kv_pages(const ms_kv* kv, int* used, int* total) {
   if (!kv) return MS_ERR_INVALID_ARG;
   const int tot = kv->pooled ? kv->pool_pages : kv->n_seq * kv->pages_full;
@@ -1595,7 +1602,7 @@ static ms_status check_rows(ms_ctx* c, const ms_model* m, const ms_kv* kv, const
     pmin[seq[r]] = std::min(pmin[seq[r]], pos[r]);
     pmax[seq[r]] = std::max(pmax[seq[r]], pos[r]);
   }
-  if (kv->slide_cap > 0) {
+  if (kv->slide_cap > 0 && !kv->allow_overwrite) {
     int win = 0;
     for (const LayerDev& L : m->layers) win = std::max(win, L.d.window);
     for (int s = 0; s < kv->n_seq; ++s)

@@ -298,6 +298,12 @@ class KVCache:
         """ms_kv_share_prefix: slot dst starts with src's first n_pos positions."""
         self.ctx.check(lib().ms_kv_share_prefix(self.ctx.h, self.h, src, dst, n_pos))
 
+    def allow_window_overwrite(self, allow=True):
+        """ms_kv_allow_window_overwrite: accept calls whose rows overwrite
+        sliding slots other rows of the call still attend (the reference
+        E4B runner's zero padding rows)."""
+        self.ctx.check(lib().ms_kv_allow_window_overwrite(self.ctx.h, self.h, int(allow)))
+
     def pages(self):
         """(used, total) full-attention pages."""
         u, t = ctypes.c_int(), ctypes.c_int()

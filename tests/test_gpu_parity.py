@@ -313,6 +313,49 @@ def test_bf16_kv_greedy_generate_matches_oracle(ctx, torch_cuda, oracle_lib):
     assert kv.nbytes * 2 == KVCache(ctx, model, 3, 128, slide_cap=64).nbytes
 
 
+# ----------------------------------------------- reference runner quirk --
+
+def test_rx_padding_rows_overwrite_the_window(ctx, torch_cuda, oracle_lib):
+    """The reference E4B runner's batch: the real token in row 0 at position
+    p and three zero rows at p+1..p+3 of the same sequence, every step
+    (src/inference/lm_head.mojo:133-143, gemma4_e4b_infer.mojo:45-54).  With
+    slide_cap equal to the window their K / V land in slots row 0 still
+    attends once p >= window - 3.  The call is rejected by default; with
+    ms_kv_allow_window_overwrite the GPU reproduces the runner: every layer
+    within 1e-4 of the oracle fed the same rows (which writes every row's
+    K / V, then attends by slot, as write_kv_sliding /
+    compute_sliding_attention do)."""
+    from mojostream_b200._lib import MsError
+    from mojostream_b200.runtime import KVCache, Model
+    torch = torch_cuda
+    spec = small_spec(vocab=0, n_layers=6, window=32)
+    w = synth_weights(spec, seed=71)
+    model = Model(ctx, spec, w, max_rows=4)
+    kv = KVCache(ctx, model, 1, 128, slide_cap=32)
+    om = oracle_lib.OracleModel(spec, w, 1, 128, slide_cap=32)
+    seq = [0, 0, 0, 0]
+    with pytest.raises(MsError) as e:
+        model.layer_forward(0, to_dev(torch, np.zeros((4, spec.hidden), np.float32)), kv, seq,
+                            [0, 1, 2, 3])
+    assert e.value.name == "MS_ERR_CAPACITY"
+    kv.allow_window_overwrite(True)
+    rng = np.random.default_rng(72)
+    worst = 0.0
+    for p in range(48):
+        x = np.zeros((4, spec.hidden), np.float32)
+        x[0] = rng.standard_normal(spec.hidden) * 2.0
+        pos = [p, p + 1, p + 2, p + 3]
+        for l in range(spec.n_layers):
+            got, y, _ = layer_step(torch, model, kv, om, l, x, seq, pos, "f32")
+            err = rel_rmse(got, y)
+            worst = max(worst, err)
+            assert err < 1e-4, (p, l, err)
+            x = y
+    print(f"runner padding quirk: 48 steps x 6 layers, max rel-RMSE {worst:.3g}")
+    kv.close()
+    model.close()
+
+
 # ------------------------------------------------------------ int8 KV --
 
 def test_i8_kv_write_read_bit_exact(ctx, torch_cuda, oracle_lib):
