@@ -97,7 +97,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvParams p) 
   for (int c0 = c_begin; c0 < c_end; c0 += CH) {
     const int nch = min(CH, c_end - c0);
     __syncthreads();  // norm factors ready / previous round's fragments consumed
-    // ---- 3. B fragments of this round: x -> (ple x) inv -> bf16 hi | lo ----
+    // ---- 3. B fragments of this pass: x -> (ple x) inv -> bf16 hi | lo ----
     {
       const int k_base = c0 * kChunkK;
       const int items = nch * 4 * MB * 8;
