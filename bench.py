@@ -356,7 +356,7 @@ def run_ours(args, ws, rank, local):
                 "wall_s": round(r["wall"], 4)},
         "gpu_launches": launches_per_step * args.steps,
         "roofline": {
-            "kernel": (f"{'gemv_stream_kernel' if BATCH <= 8 else 'gemm_tc_kernel'} "
+            "kernel": (f"{'gemv_stream_kernel' if BATCH <= 8 else ('gemm_sk_kernel' if BATCH <= 64 else 'gemm_tc_kernel')} "
                        f"(Q4 projection, M {BATCH}, gate|up K 2560 x N 20480)"),
             "bound": "hbm", "achieved": round(proj_gbs, 1), "peak": hbm, "unit": "GB/s",
             "frac": round(proj_gbs / hbm, 4),
@@ -366,12 +366,14 @@ def run_ours(args, ws, rank, local):
             "launch_ms": round(proj_ms, 5),
         },
         "roofline_lm_head": {
-            "kernel": "lm_ring_kernel (fp32 [2560 x 262144] streamed by 2-D tensor copies, "
-                      "argmax fused)",
+            "kernel": ("lm_ring_kernel (fp32 [2560 x 262144] streamed by 2-D tensor copies, "
+                       "argmax fused)" if BATCH <= 8 else
+                       "lm_tc_kernel (fp32 [2560 x 262144] split into bf16 hi + lo on the "
+                       "tensor cores, argmax fused)"),
             "bound": "hbm", "achieved": round(lm_bytes / (lm_ms / 1e3) / 1e9, 1),
             "peak": hbm, "unit": "GB/s",
             "frac": round(lm_bytes / (lm_ms / 1e3) / 1e9 / hbm, 4),
-            "traffic": profile_traffic("lm_ring_kernel"),
+            "traffic": profile_traffic("lm_ring_kernel" if BATCH <= 8 else "lm_tc_kernel"),
             "traffic_source": "ncu capture summarised in profiles/ (not this run)",
             "algorithmic_bytes": lm_bytes, "peak_source": peak_kind,
             "launch_ms": round(lm_ms, 4),
