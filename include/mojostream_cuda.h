@@ -223,7 +223,10 @@ MS_API ms_status ms_load_stats(const ms_ctx *ctx, double *seconds, uint64_t *byt
  * HybridKVCache, src/inference/gemma4_e4b.mojo:83-116).  Full-attention
  * layers hold max_pos positions; sliding layers hold slide_cap slots
  * (0 = the window, as in the reference; a prefill chunk of L tokens needs
- * slide_cap >= window + L - 1). */
+ * slide_cap >= window + L - 1).  A cache refers to its model: destroy it
+ * before the model (ms_kv_destroy alone may follow the model's destroy).
+ * Calls that pair a cache with a model other than the one it was made for,
+ * a later model at a freed one's address included, fail with MS_ERR_STATE. */
 MS_API ms_status ms_kv_create(ms_ctx *ctx, const ms_model *model, int n_seq, int max_pos,
                        int slide_cap, ms_kv **out);
 /* Element type of the cached K / V values. */

@@ -84,6 +84,7 @@ struct LayerDev {
 
 struct ms_model {
   ms_ctx* ctx = nullptr;
+  unsigned long long uid = 0;  // never reused: a new model may get a freed one's address
   int hidden = 0, n_layers = 0, vocab = 0, max_rows = 0;
   int vocab_local = 0, vocab0 = 0;  // this rank's lm_head columns (all of them without TP)
   float* P = nullptr;               // TP: partial sums of the row-parallel projections
@@ -153,6 +154,7 @@ struct ms_model {
 
 struct ms_kv {
   const ms_model* model = nullptr;
+  unsigned long long model_uid = 0;  // the model's uid when the cache was made
   unsigned long long uid = 0;  // never reused (kv_create numbers every cache)
   int n_seq = 0, max_pos = 0, slide_cap = 0, page = 16;
   int pages_full = 0, pages_slide = 0;  // per sequence
@@ -1023,8 +1025,10 @@ extern "C" ms_status ms_model_create(ms_ctx* c, const ms_model_desc* desc, ms_mo
     return fail(c, MS_ERR_SHAPE, "vocab %d does not split over %d ranks", desc->vocab, TW);
   cudaSetDevice(c->device);
 
+  static std::atomic<unsigned long long> next_model_uid{1};
   ms_model* m = new ms_model();
   m->ctx = c;
+  m->uid = next_model_uid.fetch_add(1);
   m->hidden = D;
   m->n_layers = desc->n_layers;
   m->vocab = desc->vocab;
@@ -1230,6 +1234,7 @@ static ms_status kv_create(ms_ctx* c, const ms_model* m, int n_seq, int max_pos,
   ms_kv* kv = new ms_kv();
   kv->uid = next_uid.fetch_add(1);
   kv->model = m;
+  kv->model_uid = m->uid;
   kv->bf16 = dtype == MS_KV_BF16;
   kv->i8 = dtype == MS_KV_I8;
   kv->n_seq = n_seq;
@@ -1587,7 +1592,8 @@ static ms_status check_rows(ms_ctx* c, const ms_model* m, const ms_kv* kv, const
   if (!seq || !pos) return fail(c, MS_ERR_INVALID_ARG, "seq_ids / pos are null");
   if (M <= 0 || M > m->max_rows)
     return fail(c, MS_ERR_CAPACITY, "M=%d outside 1..max_rows=%d", M, m->max_rows);
-  if (kv->model != m) return fail(c, MS_ERR_STATE, "KV cache was made for another model");
+  if (kv->model != m || kv->model_uid != m->uid)
+    return fail(c, MS_ERR_STATE, "KV cache was made for another model");
   std::set<std::pair<int, int>> seen;
   std::vector<int> pmin(kv->n_seq, 1 << 30), pmax(kv->n_seq, -1);
   for (int r = 0; r < M; ++r) {

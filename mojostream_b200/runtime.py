@@ -280,6 +280,7 @@ class KVCache:
         pool_pages > 0: the full-attention layers share a pool of that many
         16-position pages (ms_kv_create_pooled)."""
         self.ctx, self.n_seq, self.max_pos, self.dtype = ctx, n_seq, max_pos, dtype
+        self.model = model  # the cache reads its model's layer shapes: keep it alive
         h = ctypes.c_void_p()
         code = {"f32": 0, "bf16": 1, "i8": 2}[dtype]
         if pool_pages:

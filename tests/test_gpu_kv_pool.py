@@ -230,6 +230,27 @@ def test_generate_with_a_new_cache_after_one_was_closed(ctx, torch_cuda, oracle_
     model.close()
 
 
+def test_cache_of_a_destroyed_model_is_refused(ctx, torch_cuda, model_w):
+    """A cache refers to the model it was made for.  After that model is
+    destroyed, a new model (which may get the freed one's host address) must
+    refuse the cache before any kernel runs, address reused or not."""
+    from mojostream_b200._lib import MsError
+    from mojostream_b200.runtime import KVCache, Model
+    spec, w = model_w
+    a = Model(ctx, spec, w, max_rows=8)
+    kv = KVCache(ctx, a, 1, 64, slide_cap=48)
+    a.close()
+    b = Model(ctx, spec, w, max_rows=8)
+    with pytest.raises(MsError) as e:
+        b.decode_step(kv, [1], [0], [0])
+    assert e.value.name == "MS_ERR_STATE"
+    kv.close()
+    fresh = KVCache(ctx, b, 1, 64, slide_cap=48)
+    assert len(b.decode_step(fresh, [1], [0], [0])) == 1
+    fresh.close()
+    b.close()
+
+
 def test_pool_exhaustion_is_an_error_before_launch(ctx, torch_cuda, model_w):
     from mojostream_b200._lib import MsError
     from mojostream_b200.runtime import KVCache, Model
