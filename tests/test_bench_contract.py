@@ -43,3 +43,25 @@ def test_defaults_meet_the_timing_rules(monkeypatch):
     args = bench.parse()
     assert args.gpus == 1 and args.warmup >= 3 and 16 <= args.steps <= 512
     assert args.impl == "ours" and args.case == "decode" and args.extras == "all"
+
+
+def test_reference_arm_under_torchrun_prints_one_line():
+    """Launched as the driver launches N > 1 (torchrun, one process per
+    rank): rank 0 alone runs the reference's CPU path and prints the line,
+    the other rank exits 0 without work."""
+    import socket
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    out = subprocess.run(
+        [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
+         "--master-addr", "127.0.0.1", "--master-port", str(port),
+         "bench.py", "--impl", "reference", "--gpus", "2", "--steps", "1", "--warmup", "0",
+         "--layers", "2"],
+        cwd=ROOT, capture_output=True, text=True, timeout=600)
+    assert out.returncode == 0, out.stderr[-2000:]
+    lines = [l for l in out.stdout.splitlines() if l.startswith("{")]
+    assert len(lines) == 1, out.stdout[-2000:]
+    d = json.loads(lines[0])
+    assert d["impl"] == "reference" and d["n_gpus"] == 2 and d["value"] > 0
+    assert d["metric"] == bench.METRIC and d["config"]["workload"] == bench.WORKLOAD
