@@ -250,8 +250,10 @@ MS_API ms_status ms_kv_create_typed(ms_ctx *ctx, const ms_model *model, int n_se
  * its positions, together with every page below it, so short and long
  * sequences share the pool in proportion to their lengths.  Sliding layers
  * keep a ring of slide_cap slots per slot (they never grow past it).
- * MS_ERR_CAPACITY when the pool runs out (before any launch).  Every other
- * call works on it as on an ms_kv_create cache. */
+ * MS_ERR_CAPACITY when the pool runs out, before any launch; the refused
+ * call then holds no pages (every page it took is given back; ms_prefill:
+ * its chunks of max_rows rows that ran keep theirs).  Every other call works
+ * on it as on an ms_kv_create cache. */
 MS_API ms_status ms_kv_create_pooled(ms_ctx *ctx, const ms_model *model, int n_seq, int max_pos,
                                      int slide_cap, int dtype, int pool_pages, ms_kv **out);
 /* Slot `seq` is free for a new request: its pages go back to the pool (pages

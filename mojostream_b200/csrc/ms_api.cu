@@ -31,6 +31,7 @@
 #include "../../include/mojostream_cuda.h"
 #include "ms_internal.h"
 #include "ms_kernels.h"
+#include "ms_pages.h"
 
 using namespace ms;
 
@@ -173,12 +174,10 @@ struct ms_kv {
   size_t bytes = 0;
   // pooled mode (ms_kv_create_pooled): the full-attention layers draw pages
   // from one pool of pool_pages pages (a page id indexes every full layer's
-  // pool), assigned on first use and shared by reference (prefixes); the
-  // host mirror of bt_full, the free list and per-page reference counts
+  // pool), assigned on first use and shared by reference (prefixes); `pool`
+  // is the host side of bt_full with the free list and reference counts
   int pooled = 0, pool_pages = 0;
-  std::vector<int> bt_host;
-  std::vector<int> free_pages;
-  std::vector<int> refs;
+  PagePool pool;
 };
 
 struct ms_q4_weight {
@@ -1262,8 +1261,7 @@ static ms_status kv_create(ms_ctx* c, const ms_model* m, int n_seq, int max_pos,
   if (pool_pages > 0) {
     kv->pooled = 1;
     kv->pool_pages = pool_pages;
-    kv->refs.assign((size_t)pool_pages, 0);
-    for (int p = pool_pages - 1; p >= 0; --p) kv->free_pages.push_back(p);  // pop_back: 0, 1, ...
+    kv->pool.init(n_seq, kv->pages_full, pool_pages, kv->page);
   }
   // block tables: sequence s owns pages [s * P, (s + 1) * P) of every pool,
   // except the full-attention pages of a pooled cache (unassigned: -1)
@@ -1273,7 +1271,6 @@ static ms_status kv_create(ms_ctx* c, const ms_model* m, int n_seq, int max_pos,
     if (P == 0) continue;
     for (int s = 0; s < n_seq; ++s)
       for (int j = 0; j < P; ++j) bt[(size_t)s * P + j] = (pass == 0 && kv->pooled) ? -1 : s * P + j;
-    if (pass == 0 && kv->pooled) kv->bt_host.assign(bt.begin(), bt.begin() + (size_t)n_seq * P);
     int** dst = pass == 0 ? &kv->bt_full : &kv->bt_slide;
     if (dev_alloc(c, (void**)dst, (size_t)n_seq * P * sizeof(int)) != MS_OK) return cleanup(MS_ERR_OOM);
     cudaMemcpy(*dst, bt.data(), (size_t)n_seq * P * sizeof(int), cudaMemcpyHostToDevice);
@@ -1342,11 +1339,9 @@ extern "C" ms_status ms_kv_reset(ms_ctx* c, ms_kv* kv) {
   }
   MS_CUDA(c, cudaMemsetAsync(kv->tok, 0xFF, (size_t)kv->n_seq * kv->max_pos * sizeof(int), c->stream));
   if (kv->pooled) {
-    std::fill(kv->bt_host.begin(), kv->bt_host.end(), -1);
-    std::fill(kv->refs.begin(), kv->refs.end(), 0);
-    kv->free_pages.clear();
-    for (int p = kv->pool_pages - 1; p >= 0; --p) kv->free_pages.push_back(p);
-    MS_CUDA(c, cudaMemcpyAsync(kv->bt_full, kv->bt_host.data(), kv->bt_host.size() * sizeof(int),
+    kv->pool.reset();
+    const std::vector<int>& t = kv->pool.table();
+    MS_CUDA(c, cudaMemcpyAsync(kv->bt_full, t.data(), t.size() * sizeof(int),
                                cudaMemcpyHostToDevice, c->stream));
   }
   return MS_OK;
@@ -1373,41 +1368,39 @@ static ms_status kv_copy_page(ms_ctx* c, ms_kv* kv, int from, int to, cudaStream
   return MS_OK;
 }
 
-// Pooled cache: give sequence seq pages for every position up to pos_hi (all
-// pages below it too, so no position a kernel may read maps to no page), and
-// a private copy of any page shared with another sequence that positions
-// lo_write .. pos_hi fall in (copy on write).  dirty: the sequence's table
-// row changed.
-static ms_status kv_assign(ms_ctx* c, ms_kv* kv, int seq, int lo_write, int pos_hi, bool* dirty,
-                           cudaStream_t s) {
-  const int P = kv->pages_full;
-  int* row = kv->bt_host.data() + (size_t)seq * P;
-  const int j_hi = pos_hi / kv->page;
-  for (int j = 0; j <= j_hi; ++j) {
-    const bool written = j >= lo_write / kv->page;
-    if (row[j] >= 0 && !(written && kv->refs[row[j]] > 1)) continue;
-    if (kv->free_pages.empty())
-      return fail(c, MS_ERR_CAPACITY,
-                  "kv: the page pool (%d pages of %d positions) is exhausted (sequence %d, "
-                  "position %d); release finished sequences", kv->pool_pages, kv->page, seq,
-                  j * kv->page);
-    const int fresh = kv->free_pages.back();
-    kv->free_pages.pop_back();
-    if (row[j] >= 0) {  // shared page about to be written: private copy
-      MS_TRY(kv_copy_page(c, kv, row[j], fresh, s));
-      --kv->refs[row[j]];
-    }
-    kv->refs[fresh] = 1;
-    row[j] = fresh;
-    *dirty = true;
-  }
+static ms_status kv_upload_row(ms_ctx* c, ms_kv* kv, int seq, cudaStream_t s) {
+  const size_t P = (size_t)kv->pages_full;
+  MS_CUDA(c, cudaMemcpyAsync(kv->bt_full + seq * P, kv->pool.row(seq), P * sizeof(int),
+                             cudaMemcpyHostToDevice, s));
   return MS_OK;
 }
 
-static ms_status kv_upload_row(ms_ctx* c, ms_kv* kv, int seq, cudaStream_t s) {
-  const size_t P = (size_t)kv->pages_full;
-  MS_CUDA(c, cudaMemcpyAsync(kv->bt_full + seq * P, kv->bt_host.data() + seq * P, P * sizeof(int),
-                             cudaMemcpyHostToDevice, s));
+// Pooled cache, before a call that writes positions lo[q] .. hi[q] of each
+// sequence q with hi[q] >= 0: assign the pages they need (PagePool::assign),
+// then copy the shared pages being replaced and upload the changed rows.
+// All or nothing: when the pool runs out, every change of the call is undone
+// and nothing is issued on the device.
+static ms_status kv_assign_all(ms_ctx* c, ms_kv* kv, const std::vector<int>& lo,
+                               const std::vector<int>& hi, cudaStream_t s) {
+  PagePool& pool = kv->pool;
+  pool.begin();
+  std::vector<int> dirty_seqs;
+  for (int q = 0; q < (int)hi.size(); ++q) {
+    if (hi[q] < 0) continue;
+    bool dirty = false;
+    const int short_at = pool.assign(q, lo[q], hi[q], &dirty);
+    if (short_at >= 0) {
+      pool.rollback();
+      return fail(c, MS_ERR_CAPACITY,
+                  "kv: the page pool (%d pages of %d positions) is exhausted (sequence %d, "
+                  "position %d); release finished sequences", kv->pool_pages, kv->page, q,
+                  short_at);
+    }
+    if (dirty) dirty_seqs.push_back(q);
+  }
+  for (const PagePool::Copy& cp : pool.copies()) MS_TRY(kv_copy_page(c, kv, cp.from, cp.to, s));
+  for (int q : dirty_seqs) MS_TRY(kv_upload_row(c, kv, q, s));
+  pool.begin();
   return MS_OK;
 }
 
@@ -1421,16 +1414,11 @@ static ms_status kv_prepare(ms_ctx* c, ms_kv* kv, const int* seq, const int* pos
     lo[seq[r]] = std::min(lo[seq[r]], pos[r]);
     hi[seq[r]] = std::max(hi[seq[r]], pos[r] + extra);
   }
-  for (int q = 0; q < kv->n_seq; ++q) {
-    if (hi[q] < 0) continue;
+  for (int q = 0; q < kv->n_seq; ++q)
     if (hi[q] >= kv->max_pos)
       return fail(c, MS_ERR_CAPACITY, "sequence %d: position %d outside the cache (max_pos %d)", q,
                   hi[q], kv->max_pos);
-    bool dirty = false;
-    MS_TRY(kv_assign(c, kv, q, lo[q], hi[q], &dirty, s));
-    if (dirty) MS_TRY(kv_upload_row(c, kv, q, s));
-  }
-  return MS_OK;
+  return kv_assign_all(c, kv, lo, hi, s);
 }
 
 extern "C" ms_status ms_kv_release(ms_ctx* c, ms_kv* kv, int seq) {
@@ -1441,12 +1429,7 @@ extern "C" ms_status ms_kv_release(ms_ctx* c, ms_kv* kv, int seq) {
   cudaStream_t s = c->stream;
   MS_CUDA(c, cudaMemsetAsync(kv->tok + (size_t)seq * kv->max_pos, 0xFF, kv->max_pos * sizeof(int), s));
   if (!kv->pooled) return MS_OK;
-  int* row = kv->bt_host.data() + (size_t)seq * kv->pages_full;
-  for (int j = 0; j < kv->pages_full; ++j) {
-    if (row[j] < 0) continue;
-    if (--kv->refs[row[j]] == 0) kv->free_pages.push_back(row[j]);
-    row[j] = -1;
-  }
+  kv->pool.release(seq);
   return kv_upload_row(c, kv, seq, s);
 }
 
@@ -1460,29 +1443,20 @@ extern "C" ms_status ms_kv_share_prefix(ms_ctx* c, ms_kv* kv, int src, int dst, 
   cudaStream_t s = c->stream;
   const size_t P = (size_t)kv->pages_full;
   if (kv->pooled) {
-    int* rs = kv->bt_host.data() + src * P;
-    int* rd = kv->bt_host.data() + dst * P;
-    for (size_t j = 0; j < P; ++j)
-      if (rd[j] >= 0)
+    // whole pages shared by reference, the page the prefix ends in copied
+    PagePool::Copy cp{};
+    bool has_copy = false;
+    switch (kv->pool.share_prefix(src, dst, n_pos, &cp, &has_copy)) {
+      case 0: break;
+      case 1:
         return fail(c, MS_ERR_STATE, "ms_kv_share_prefix: sequence %d holds pages (release it)", dst);
-    const int full = n_pos / kv->page, part = n_pos % kv->page;
-    for (int j = 0; j < full + (part ? 1 : 0); ++j)
-      if (rs[j] < 0)
-        return fail(c, MS_ERR_STATE, "ms_kv_share_prefix: sequence %d has no page at position %d",
-                    src, j * kv->page);
-    if (part && kv->free_pages.empty())
-      return fail(c, MS_ERR_CAPACITY, "ms_kv_share_prefix: the page pool is exhausted");
-    for (int j = 0; j < full; ++j) {  // whole pages: shared by reference
-      rd[j] = rs[j];
-      ++kv->refs[rs[j]];
+      case 2:
+        return fail(c, MS_ERR_STATE, "ms_kv_share_prefix: sequence %d lacks a page below position %d",
+                    src, n_pos);
+      default:
+        return fail(c, MS_ERR_CAPACITY, "ms_kv_share_prefix: the page pool is exhausted");
     }
-    if (part) {  // the page the prefix ends in: a private copy
-      const int fresh = kv->free_pages.back();
-      kv->free_pages.pop_back();
-      MS_TRY(kv_copy_page(c, kv, rs[full], fresh, s));
-      kv->refs[fresh] = 1;
-      rd[full] = fresh;
-    }
+    if (has_copy) MS_TRY(kv_copy_page(c, kv, cp.from, cp.to, s));
     MS_TRY(kv_upload_row(c, kv, dst, s));
   } else {
     // fixed pages: copy the prefix rows of every full-attention layer
@@ -1524,7 +1498,7 @@ extern "C" ms_status ms_kv_allow_window_overwrite(ms_ctx* c, ms_kv* kv, int allo
 extern "C" ms_status ms_kv_pages(const ms_kv* kv, int* used, int* total) {
   if (!kv) return MS_ERR_INVALID_ARG;
   const int tot = kv->pooled ? kv->pool_pages : kv->n_seq * kv->pages_full;
-  const int fr = kv->pooled ? (int)kv->free_pages.size() : 0;
+  const int fr = kv->pooled ? kv->pool.free_count() : 0;
   if (used) *used = tot - fr;
   if (total) *total = tot;
   return MS_OK;
@@ -1562,9 +1536,10 @@ extern "C" ms_status ms_kv_write(ms_ctx* c, ms_kv* kv, int layer, int seq, int p
   if (!c || !kv) return MS_ERR_INVALID_ARG;
   MS_TRY(kv_rows_check(c, kv, layer, seq, pos0, n, k, v, "ms_kv_write"));
   if (kv->pooled && kv->model->layers[layer].d.window == 0) {
-    bool dirty = false;
-    MS_TRY(kv_assign(c, kv, seq, pos0, pos0 + n - 1, &dirty, pick(c, stream)));
-    if (dirty) MS_TRY(kv_upload_row(c, kv, seq, pick(c, stream)));
+    std::vector<int> lo(kv->n_seq, 1 << 30), hi(kv->n_seq, -1);
+    lo[seq] = pos0;
+    hi[seq] = pos0 + n - 1;
+    MS_TRY(kv_assign_all(c, kv, lo, hi, pick(c, stream)));
   }
   MS_CUDA(c, launch_kv_copy(kv_view(kv, layer), seq, pos0, n, const_cast<float*>(k),
                             const_cast<float*>(v), 0, pick(c, stream)));
@@ -1577,7 +1552,7 @@ extern "C" ms_status ms_kv_read(ms_ctx* c, const ms_kv* kv, int layer, int seq, 
   MS_TRY(kv_rows_check(c, kv, layer, seq, pos0, n, k, v, "ms_kv_read"));
   if (kv->pooled && kv->model->layers[layer].d.window == 0)
     for (int j = pos0 / kv->page; j <= (pos0 + n - 1) / kv->page; ++j)
-      if (kv->bt_host[(size_t)seq * kv->pages_full + j] < 0)
+      if (kv->pool.row(seq)[j] < 0)
         return fail(c, MS_ERR_STATE, "ms_kv_read: sequence %d has no page at position %d", seq,
                     j * kv->page);
   MS_CUDA(c, launch_kv_copy(kv_view(kv, layer), seq, pos0, n, k, v, 1, pick(c, stream)));
