@@ -621,6 +621,11 @@ static ms_status ensure_tc_scratch(ms_ctx* c, int M, int K) {
 
 constexpr int kMaxDecodeCluster = 8;  // k-segments that merge inside one cluster
 
+// The streaming decode kernel holds a k-segment's activations in registers:
+// at most 2560 / mg values per row, i.e. 40 (mg 1) or 20 (mg 2) chunks
+// (launch_gemv_stream refuses longer segments).
+constexpr int decode_seg_max(int mg) { return mg == 1 ? 40 : 20; }
+
 static GemvPlan plan_gemv(const ms_ctx* c, int M, int K, int n_tiles, bool allow_tc = true,
                           bool allow_sk = true) {
   GemvPlan pl{};
@@ -661,7 +666,7 @@ static GemvPlan plan_gemv(const ms_ctx* c, int M, int K, int n_tiles, bool allow
     pl.mg = M <= 4 ? 1 : 2;
     const int mb = 4 * pl.mg;
     const int groups = padded_tiles(n_tiles) / kGroupTiles;
-    const int seg_max = pl.mg == 1 ? 40 : 20;
+    const int seg_max = decode_seg_max(pl.mg);
     // at least one CTA per SM (rounded up; at most a cluster of 8 k-segments)
     int ksplit = std::max(1, std::min(kMaxDecodeCluster, (c->sm_count + groups - 1) / groups));
     ksplit = std::max(ksplit, (chunks + seg_max - 1) / seg_max);
@@ -738,6 +743,11 @@ extern "C" ms_status ms_q4_gemm(ms_ctx* c, const ms_q4_weight* w, float* C, cons
     return fail(c, MS_ERR_ALIGN, "ms_q4_gemm: A must be 16-byte and C 8-byte aligned");
   const int n_tiles = w->N / kTileN;
   GemvPlan pl = plan_gemv(c, M, w->K, n_tiles);
+  if (pl.dec && pl.kseg > decode_seg_max(pl.mg) * kChunkK)
+    return fail(c, MS_ERR_CAPACITY,
+                "ms_q4_gemm: M=%d K=%d N=%d: the k-split the decode kernel needs for this K "
+                "would exceed the context's partial-sum scratch (%zu floats)",
+                M, w->K, w->N, c->part_floats);
   if (pl.tc) MS_TRY(ensure_tc_scratch(c, M, w->K));
   GemvParams p = gemv_base(c, w->w, n_tiles, w->K, M, pl);
   p.x = A;
@@ -813,7 +823,7 @@ static bool noalloc_fit(GemvPlan& pl, int M, int K, int n_tiles) {
     GemvPlan q = pl;
     if (q.dec) {
       const int seg = (chunks + ks - 1) / ks;
-      if (seg > (q.mg == 1 ? 40 : 20)) break;
+      if (seg > decode_seg_max(q.mg)) break;
       q.kseg = seg * kChunkK;
       q.ksplit = (chunks + seg - 1) / seg;
     } else {
