@@ -220,7 +220,8 @@ bool read_and_check(const char* path, FileView& f) {
       return f.fail(MS_ERR_SHAPE, "[TensorGuard] Tensor[%llu] Layer %d %s: offset=%llu not 4096-aligned",
                     (unsigned long long)i, layer, nm, (unsigned long long)e.offset);
     const uint64_t bytes = (uint64_t)e.rows * (e.cols / 2);
-    if (e.offset < I.data_start || e.offset + bytes > I.file_size)
+    // (written so that no sum can wrap: offsets are 64-bit values from the file)
+    if (e.offset < I.data_start || e.offset > I.file_size || bytes > I.file_size - e.offset)
       return f.fail(MS_ERR_SHAPE,
                     "[TensorGuard] Tensor[%llu] Layer %d %s: offset=%llu + size=%llu outside the data "
                     "region [%llu, %llu)",

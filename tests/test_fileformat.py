@@ -129,6 +129,7 @@ ENTRY = lambda i: 128 + 32 * i  # noqa: E731
     (ENTRY(5) + 24, "<Q", 4096 * 3 + 8, "not 4096-aligned"),
     (ENTRY(23) + 24, "<Q", 4096 * 1000, "outside the data region"),
     (ENTRY(1) + 24, "<Q", 0, "outside the data region"),
+    (ENTRY(5) + 24, "<Q", 2**64 - 4096, "outside the data region"),  # offset + size wraps
     (ENTRY(17) + 12, "<I", 96, "head_dim 24 gives kv_dim 48"),
     (12, "<I", 7, "format tag 7"),
 ])
