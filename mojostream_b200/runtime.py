@@ -18,6 +18,21 @@ def _ptr(t):
     return ctypes.c_void_p(t.ctypes.data)
 
 
+def _check_f32(t, what, min_numel=0):
+    """A tensor handed to the C-ABI as a bare pointer: the library reads or
+    writes min_numel dense fp32 values there, so it must be a contiguous
+    float32 CUDA tensor holding at least that many (the library cannot see a
+    tensor's size; alignment and device residency it checks itself)."""
+    if not getattr(t, "is_cuda", False):
+        raise ValueError(f"{what}: a CUDA tensor is needed")
+    if str(t.dtype) != "torch.float32":
+        raise ValueError(f"{what}: float32 needed, got {t.dtype}")
+    if not t.is_contiguous():
+        raise ValueError(f"{what}: a contiguous tensor is needed")
+    if t.numel() < min_numel:
+        raise ValueError(f"{what}: {t.numel()} values, the call uses {min_numel}")
+
+
 _CUDA_STREAM_LEGACY = 1  # cudaStreamLegacy: the legacy default stream handle
 
 
@@ -68,6 +83,7 @@ class Context:
         device."""
         import torch
         M, V = logits.shape
+        _check_f32(logits, "logits", M * V)
         hist = [int(t) for g in generated for t in g]
         off = np.zeros(M + 1, np.int32)
         off[1:] = np.cumsum([len(g) for g in generated])
@@ -116,6 +132,8 @@ class Q4Weight:
 
     def gemm(self, A, C, accumulate=False):
         M = A.shape[0]
+        _check_f32(A, "A", M * self.K)
+        _check_f32(C, "C", M * self.N)
         self.ctx.check(lib().ms_q4_gemm(self.ctx.h, self.h, _ptr(C), _ptr(A), M,
                                         1 if accumulate else 0, _stream()))
         return C
@@ -213,12 +231,14 @@ class Model:
     def layer_forward(self, layer, x, kv, seq, pos):
         """x: CUDA float32 tensor [M][hidden], updated in place."""
         M = x.shape[0]
+        _check_f32(x, "x", M * self.spec.hidden)
         self.ctx.check(lib().ms_layer_forward(self.ctx.h, self.h, layer, _ptr(x), kv.h,
                                               int_array(seq), int_array(pos), M, _stream()))
         return x
 
     def forward(self, x, kv, seq, pos):
         M = x.shape[0]
+        _check_f32(x, "x", M * self.spec.hidden)
         self.ctx.check(lib().ms_forward(self.ctx.h, self.h, _ptr(x), kv.h, int_array(seq),
                                         int_array(pos), M, _stream()))
         return x
@@ -233,6 +253,7 @@ class Model:
     def lm_head(self, x, logits=True):
         import torch
         M = x.shape[0]
+        _check_f32(x, "x", M * self.spec.hidden)
         lg = torch.empty((M, self.spec.vocab), dtype=torch.float32, device="cuda") if logits else None
         am = torch.empty(M, dtype=torch.int32, device="cuda")
         self.ctx.check(lib().ms_lm_head(self.ctx.h, self.h, _ptr(x), M,
@@ -291,6 +312,15 @@ class KVCache:
                                                ctypes.byref(h)))
         self.h = h
 
+    def _kv_dim(self, layer):
+        """Values per cached row of `layer` on this rank (its share of the KV
+        heads under tensor parallelism); 0 for a layer the model lacks (the
+        library reports that)."""
+        layers = self.model.spec.layers
+        if not 0 <= layer < len(layers):
+            return 0
+        return layers[layer].kv_dim // max(1, self.ctx.tp_world)
+
     def release(self, seq):
         """ms_kv_release: slot seq is free for a new request."""
         self.ctx.check(lib().ms_kv_release(self.ctx.h, self.h, seq))
@@ -321,6 +351,9 @@ class KVCache:
     def write(self, layer, seq, pos0, k, v):
         """ms_kv_write: rows k, v (fp32 device tensors [n][kv_dim]) become the
         cached K / V of positions pos0 .. pos0 + n - 1 of sequence seq."""
+        n = k.shape[0]
+        _check_f32(k, "k", n * self._kv_dim(layer))
+        _check_f32(v, "v", n * self._kv_dim(layer))
         self.ctx.check(lib().ms_kv_write(self.ctx.h, self.h, layer, seq, pos0, k.shape[0],
                                          _ptr(k), _ptr(v), _stream()))
 
@@ -328,6 +361,8 @@ class KVCache:
         """ms_kv_read: the cached K / V rows of positions pos0 .. pos0 + n - 1
         as two fp32 device tensors [n][kv_dim]."""
         import torch
+        if 0 < self._kv_dim(layer) != kv_dim:
+            raise ValueError(f"kv_dim {kv_dim}: layer {layer} caches rows of {self._kv_dim(layer)}")
         k = torch.empty((n, kv_dim), dtype=torch.float32, device="cuda")
         v = torch.empty((n, kv_dim), dtype=torch.float32, device="cuda")
         self.ctx.check(lib().ms_kv_read(self.ctx.h, self.h, layer, seq, pos0, n, _ptr(k),

@@ -1,0 +1,36 @@
+"""The Python wrappers hand tensors to the C-ABI as bare pointers, so they
+check what the library cannot see (device, dtype, layout, size) before the
+call; checked here without a GPU through a stand-in tensor."""
+import pytest
+import torch
+
+from mojostream_b200.runtime import _check_f32
+
+
+class FakeCuda:
+    """What _check_f32 reads of a CUDA tensor."""
+
+    def __init__(self, n, dtype=torch.float32, contiguous=True):
+        self.is_cuda, self.dtype, self._c, self._n = True, dtype, contiguous, n
+
+    def is_contiguous(self):
+        return self._c
+
+    def numel(self):
+        return self._n
+
+
+def test_accepts_a_dense_f32_cuda_tensor_of_enough_values():
+    _check_f32(FakeCuda(12), "x", 12)
+    _check_f32(FakeCuda(13), "x", 12)
+
+
+@pytest.mark.parametrize("t,needle", [
+    (torch.zeros(12), "CUDA tensor"),
+    (FakeCuda(12, dtype=torch.bfloat16), "float32 needed"),
+    (FakeCuda(12, contiguous=False), "contiguous"),
+    (FakeCuda(11), "11 values, the call uses 12"),
+])
+def test_rejects_what_the_library_would_misread(t, needle):
+    with pytest.raises(ValueError, match=needle):
+        _check_f32(t, "x", 12)
