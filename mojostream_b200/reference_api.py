@@ -23,6 +23,8 @@ argument (the reference reads perf_counter_ns, which stays the default).
 import time
 from dataclasses import dataclass
 
+import numpy as np
+
 from . import runtime
 from ._lib import MsError  # noqa: F401  (re-exported for callers)
 
@@ -57,11 +59,24 @@ class KVCache:
 def matmul_q4_bpack_raw(C, A, bq_ptr, packed_cols, scale, workers=0, ctx=None):
     """C[M, N] += A[M, K] . dequant(bq); bq is [K][packed_cols] uint8 (host or
     device), N = 2 * packed_cols.  C and A are CUDA float32 tensors.  ``workers``
-    is accepted for signature parity (the GPU decides its own parallelism)."""
+    is accepted for signature parity (the GPU decides its own parallelism).
+
+    Given raw bytes, each call uploads and repacks the weight (and, without
+    ``ctx``, makes a context) and waits for the result: right for a one-off
+    call.  A host loop makes a ``runtime.Q4Weight`` once and passes it as
+    ``bq_ptr``: the call then only launches the projection on torch's current
+    stream (its scale must equal ``scale``)."""
     K = A.shape[1]
     N = 2 * packed_cols
     if C.shape[1] != N or C.shape[0] != A.shape[0]:
         raise ValueError(f"C is {tuple(C.shape)}, expected ({A.shape[0]}, {N})")
+    if isinstance(bq_ptr, runtime.Q4Weight):
+        if (bq_ptr.K, bq_ptr.N) != (K, N):
+            raise ValueError(f"weight is {bq_ptr.K} x {bq_ptr.N}, expected {K} x {N}")
+        if np.float32(scale) != np.float32(bq_ptr.scale):
+            raise ValueError(f"scale {scale} differs from the weight's {bq_ptr.scale}")
+        bq_ptr.gemm(A, C, accumulate=True)
+        return C
     if tuple(bq_ptr.shape) != (K, packed_cols):
         raise ValueError(f"weights are {tuple(bq_ptr.shape)}, expected ({K}, {packed_cols})")
     own = ctx is None
@@ -69,7 +84,8 @@ def matmul_q4_bpack_raw(C, A, bq_ptr, packed_cols, scale, workers=0, ctx=None):
     w = runtime.Q4Weight(ctx, bq_ptr, K, N, scale)
     try:
         w.gemm(A, C, accumulate=True)
-        ctx.sync() if own else None
+        if own:
+            ctx.sync(current=True)
     finally:
         w.close()
         if own:

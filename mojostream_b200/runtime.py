@@ -67,8 +67,11 @@ class Context:
     def check(self, status):
         check(status, self.h)
 
-    def sync(self):
-        self.check(lib().ms_sync(self.h, None))
+    def sync(self, current=False):
+        """ms_sync: wait for the context's stream (current=True: torch's
+        current stream, where the wrappers launch) and raise any error the
+        kernels recorded."""
+        self.check(lib().ms_sync(self.h, _stream() if current else None))
 
     @property
     def stream_ptr(self):
@@ -124,7 +127,7 @@ class Q4Weight:
     """ms_q4_weight: one Q4 matrix repacked for the tensor-core projection."""
 
     def __init__(self, ctx, w_rx, K, N, scale):
-        self.ctx, self.K, self.N = ctx, K, N
+        self.ctx, self.K, self.N, self.scale = ctx, K, N, float(scale)
         h = ctypes.c_void_p()
         ctx.check(lib().ms_q4_weight_create(ctx.h, _ptr(w_rx), K, N, float(scale),
                                             ctypes.byref(h)))

@@ -34,3 +34,19 @@ def test_accepts_a_dense_f32_cuda_tensor_of_enough_values():
 def test_rejects_what_the_library_would_misread(t, needle):
     with pytest.raises(ValueError, match=needle):
         _check_f32(t, "x", 12)
+
+
+def test_reference_matmul_refuses_a_mismatched_prebuilt_weight():
+    """reference_api.matmul_q4_bpack_raw with a Q4Weight made once: a weight
+    of another shape or scale is refused before any launch."""
+    from mojostream_b200 import reference_api as ra
+    from mojostream_b200.runtime import Q4Weight
+    w = object.__new__(Q4Weight)  # the fields the call checks; no device weight
+    w.K, w.N, w.scale, w.h = 64, 32, 0.01, None
+    A, C = torch.zeros((2, 64)), torch.zeros((2, 32))
+    with pytest.raises(ValueError, match="scale"):
+        ra.matmul_q4_bpack_raw(C, A, w, 16, 0.02)
+    with pytest.raises(ValueError, match="weight is 64 x 32"):
+        ra.matmul_q4_bpack_raw(torch.zeros((2, 64)), A, w, 32, 0.01)
+    with pytest.raises(ValueError, match="C is"):
+        ra.matmul_q4_bpack_raw(torch.zeros((3, 32)), A, w, 16, 0.01)
