@@ -62,12 +62,18 @@ typedef struct ms_q4_weight ms_q4_weight;
 
 /* ---------------------------------------------------------------- context */
 
+/* MS_ABI_VERSION of the built library: a binding compares it with the
+ * header it was written against.  No counterpart in the reference. */
 MS_API int ms_abi_version(void);
+/* A short description of a status code ("capacity exceeded", ...); static
+ * storage. */
 MS_API const char *ms_status_string(ms_status s);
 
 /* Bind to CUDA device `device` and create a context with its own stream. */
 MS_API ms_status ms_init(int device, ms_ctx **out);
 MS_API ms_status ms_destroy(ms_ctx *ctx);
+/* The message of the context's last failed call; the text stays valid until
+ * a later call on the context fails. */
 MS_API const char *ms_last_error(const ms_ctx *ctx);
 /* Wait for all work on `stream` (NULL = the context stream). */
 MS_API ms_status ms_sync(ms_ctx *ctx, void *stream);
@@ -299,7 +305,11 @@ MS_API ms_status ms_kv_write(ms_ctx *ctx, ms_kv *kv, int layer, int seq, int pos
                              const float *k, const float *v, void *stream);
 MS_API ms_status ms_kv_read(ms_ctx *ctx, const ms_kv *kv, int layer, int seq, int pos0, int n,
                             float *k, float *v, void *stream);
+/* Every slot empty again, as KVCache.reset (src/main.mojo:295-297) sets
+ * cur_len to 0: K / V zeroed, token histories cleared, a pooled cache's
+ * pages all free.  Stream-ordered on the context stream. */
 MS_API ms_status ms_kv_reset(ms_ctx *ctx, ms_kv *kv);
+/* Device bytes the cache holds (K / V pools of every layer). */
 MS_API size_t ms_kv_bytes(const ms_kv *kv);
 
 /* ---------------------------------------------------------------- forward */
