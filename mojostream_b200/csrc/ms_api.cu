@@ -2298,8 +2298,10 @@ extern "C" ms_status ms_prefill(ms_ctx* c, const ms_model* mc, ms_kv* kv, const 
       }
   }
   if (st == MS_OK && first_ids && n_keep) {
-    MS_CUDA(c, launch_rowstats(m->S[1], keep, m->hidden, n_keep, m->hidden, s, false));
-    if (m->sampling()) {  // each sequence's last row: its sequence and position
+    // (errors go through st from here on, so `keep` is always freed below)
+    const cudaError_t e = launch_rowstats(m->S[1], keep, m->hidden, n_keep, m->hidden, s, false);
+    if (e != cudaSuccess) st = fail(c, MS_ERR_CUDA, "prefill row statistics: %s", cudaGetErrorString(e));
+    if (st == MS_OK && m->sampling()) {  // each sequence's last row: its sequence and position
       std::vector<int> ks(kept_seq), kp(n_keep);
       for (int i = 0; i < n_keep; ++i) kp[i] = pos[last_row[kept_seq[i]]];
       st = ensure_sampler(c, m, n_keep);
@@ -2309,7 +2311,7 @@ extern "C" ms_status ms_prefill(ms_ctx* c, const ms_model* mc, ms_kv* kv, const 
         st = lm_head_launch(c, m, keep, m->S[1], n_keep, m->d_logits, nullptr, s, true);
       }
       if (st == MS_OK) st = sample_rows(c, m, kv, n_keep, m->d_seq, m->d_pos, m->d_next, s);
-    } else {
+    } else if (st == MS_OK) {
       st = lm_head_launch(c, m, keep, m->S[1], n_keep, nullptr, m->d_next, s, true);
     }
     std::vector<int> nxt(n_keep);
