@@ -155,6 +155,18 @@ class ClockSampler:
 
 
 # --------------------------------------------------------------- helpers --
+def decode_launches(n_layers, batch, kv="f32", sampling=False):
+    """Kernels one decode step launches: the embedding; per layer QKV,
+    attention, O, gate|up and down, plus the int8 cache's K / V quantiser and,
+    from 9 rows up, the activation quantiser before each of the 4 tensor-core
+    projections; the lm_head (one ring launch up to 8 rows, else row
+    statistics + a tensor-core pass per 64 rows); the sampler when sampling;
+    the token feedback."""
+    per_layer = 5 + (1 if kv == "i8" else 0) + (4 if batch > 8 else 0)
+    lm = 1 if batch <= 8 else 2 * ((batch + 63) // 64)
+    return 1 + per_layer * n_layers + lm + (1 if sampling else 0) + 1
+
+
 def measured_peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -325,9 +337,8 @@ def run_ours(args, ws, rank, local):
     tokens = BATCH * args.steps * ws
     value = tokens / (r["dev_ms"] / 1000.0)
     e2e_val = tokens / (r["e2e_ms"] / 1000.0)
-    launches_per_step = 1 + (6 if args.kv == "i8" else 5) * spec.n_layers + (BATCH + 3) // 4 + 1
-    if args.temperature > 0.01 or args.penalty > 1.0:
-        launches_per_step += 1  # the sampler after the lm_head
+    launches_per_step = decode_launches(spec.n_layers, BATCH, args.kv,
+                                        args.temperature > 0.01 or args.penalty > 1.0)
     cfg = main_config(spec, ws)
     cfg["kv_dtype"] = args.kv
     if args.temperature > 0.01 or args.penalty > 1.0:

@@ -65,3 +65,13 @@ def test_reference_arm_under_torchrun_prints_one_line():
     d = json.loads(lines[0])
     assert d["impl"] == "reference" and d["n_gpus"] == 2 and d["value"] > 0
     assert d["metric"] == bench.METRIC and d["config"]["workload"] == bench.WORKLOAD
+
+
+def test_launch_count_matches_the_committed_launch_lists():
+    """gpu_launches is counted, not measured: the rule must reproduce the
+    per-step counts of the launch lists in profiles/ (two graph replays of 426
+    launches at batch 4; 382 launches in one step at batch 64)."""
+    assert bench.decode_launches(42, 4) == 426 // 2
+    assert bench.decode_launches(42, 64) == 382
+    assert bench.decode_launches(42, 4, "i8") == 213 + 42
+    assert bench.decode_launches(42, 4, sampling=True) == 214
