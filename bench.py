@@ -11,7 +11,8 @@ are far larger than L2 (126 MB), so no L2 flush is needed between steps.
 value : decode tokens/s, device-resident loop (CUDA-graph replays on the
         library stream, CUDA events), max over ranks
 e2e   : the same through ms_decode_step with host buffers (per step: ids / seq /
-        pos host->device from pinned memory, next ids device->host)
+        pos host->device from pinned memory, next ids and the context's error
+        word device->host)
 --gpus N (torchrun): every rank runs the E4B loop as an independent replica
         (the sequences are independent; no collective on the data path), weak
         scaling; then the 14B-class model runs tensor parallel over the N ranks
@@ -363,7 +364,7 @@ def run_ours(args, ws, rank, local):
         "config": cfg,
         "ttft_ms": round(r["ttft_ms"], 3) if r["ttft_ms"] is not None else None,
         "e2e": {"value": round(e2e_val, 2), "unit": "tokens/s",
-                "h2d_bytes_per_step": 3 * 4 * BATCH, "d2h_bytes_per_step": 4 * BATCH,
+                "h2d_bytes_per_step": 3 * 4 * BATCH, "d2h_bytes_per_step": 4 * BATCH + 4,
                 "wall_s": round(r["wall"], 4)},
         "gpu_launches": launches_per_step * args.steps,
         "roofline": {
@@ -466,7 +467,7 @@ def run_long(args, ctx, model, lib_stream, hbm, B=64, P=4096, steps=32, warmup=4
         "ms_per_step": round(step_ms, 4), "steps": steps, "warmup": warmup,
         "ttft_ms": round(r["ttft_ms"], 2),
         "e2e": {"value": round(B * steps / (r["e2e_ms"] / 1e3), 2), "unit": "tokens/s",
-                "h2d_bytes_per_step": 12 * B, "d2h_bytes_per_step": 4 * B},
+                "h2d_bytes_per_step": 12 * B, "d2h_bytes_per_step": 4 * B + 4},
         "step_roofline": {"bytes_per_step": step_bytes, "peak": hbm,
                           "frac": round(step_bytes / (step_ms / 1e3) / 1e9 / hbm, 4),
                           "note": "Q4 + fp32 lm_head + fp32 KV read per step"},
@@ -625,7 +626,7 @@ def run_tp_block(args, ws, rank, local, D, B=64, P=1024, steps=24, warmup=4):
         "n_gpus": ws, "scaling": "strong", "ms_per_step": round(step_ms, 4),
         "steps": steps, "warmup": warmup, "ttft_ms": round(r["ttft_ms"], 2),
         "e2e": {"value": round(B * steps / (r["e2e_ms"] / 1e3), 2), "unit": "tokens/s",
-                "h2d_bytes_per_step": 12 * B, "d2h_bytes_per_step": 4 * B},
+                "h2d_bytes_per_step": 12 * B, "d2h_bytes_per_step": 4 * B + 4},
         "step_roofline": {"bytes_per_step_per_gpu": int(step_bytes), "peak": hbm,
                           "peak_source": kind,
                           "frac": round(step_bytes / (step_ms / 1e3) / 1e9 / hbm, 4)},
