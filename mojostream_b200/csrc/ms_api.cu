@@ -32,6 +32,7 @@
 #include "ms_internal.h"
 #include "ms_kernels.h"
 #include "ms_pages.h"
+#include "ms_plan.h"
 
 using namespace ms;
 
@@ -580,15 +581,6 @@ static bool splitk_global_forced() {
   return on;
 }
 
-// Launch plan of one projection: decode kernel (M <= 8) or the tiled kernel,
-// m-group size, chunks per round, k-segment and the number of k-segments.
-struct GemvPlan {
-  bool dec, tc, sk;  // sk: the decode-batch tensor-core kernel (tc is set too)
-  int mg, ch, kseg, ksplit;
-};
-
-// Rows above which projections run on the tensor cores (tcgen05 GEMM).
-constexpr int kTcMinRows = 9;
 // Tensor parallel: up to this many rows the O / down all-reduce runs inside
 // the tensor-core epilogue over peer memory (measured faster at batch 64 on 2
 // GPUs); larger calls use one NCCL all-reduce (faster for 2048-row prefills).
@@ -619,93 +611,11 @@ static ms_status ensure_tc_scratch(ms_ctx* c, int M, int K) {
   return MS_OK;
 }
 
-constexpr int kMaxDecodeCluster = 8;  // k-segments that merge inside one cluster
-
-// The streaming decode kernel holds a k-segment's activations in registers:
-// at most 2560 / mg values per row, i.e. 40 (mg 1) or 20 (mg 2) chunks
-// (launch_gemv_stream refuses longer segments).
-constexpr int decode_seg_max(int mg) { return mg == 1 ? 40 : 20; }
-
+// The projection planner (ms_plan.h) over this context's limits.
 static GemvPlan plan_gemv(const ms_ctx* c, int M, int K, int n_tiles, bool allow_tc = true,
                           bool allow_sk = true) {
-  GemvPlan pl{};
-  const int chunks = K / kChunkK;
-  if (allow_tc && allow_sk && M >= kTcMinRows && M <= sk_rows_max()) {
-    // decode batches: weights on the MMA's 128-row side, about one CTA per SM
-    // (tile groups x k-slices), the slices of a group one cluster (<= 8)
-    pl.tc = pl.sk = true;
-    const int groups = padded_tiles(n_tiles) / kGroupTiles;
-    int ks = std::max(1, (c->sm_count + groups / 2) / groups);
-    ks = std::min(std::min(ks, 8), chunks);
-    const int seg = (chunks + ks - 1) / ks;
-    pl.kseg = seg * kChunkK;
-    pl.ksplit = (chunks + seg - 1) / seg;
-    return pl;
-  }
-  if (allow_tc && M >= kTcMinRows) {
-    // one CTA per (tile group, 128-row tile), all of K -- or k slices when
-    // that grid cannot fill the GPU (small batches of narrow projections);
-    // the slices' fp32 tiles are summed in k order by the last one
-    pl.tc = true;
-    const long tiles = (long)(padded_tiles(n_tiles) / kGroupTiles) * ((M + 127) / 128);
-    int ks = 1;
-    if (tiles < c->sm_count) ks = (int)std::min<long>((c->sm_count + tiles - 1) / tiles, 16);
-    ks = std::max(1, std::min(ks, chunks / 4));
-    while (ks > 1 && ((size_t)tiles * ks * 128 * 128 > c->part_floats || (size_t)tiles > c->n_counters))
-      --ks;
-    const int seg = (chunks + ks - 1) / ks;
-    pl.kseg = seg * kChunkK;
-    pl.ksplit = (chunks + seg - 1) / seg;
-    return pl;
-  }
-  if (M <= 8) {
-    // streaming kernel: one CTA per (tile group, k-segment); about one CTA per
-    // SM, a k-segment of at most 40 chunks (mg 1) / 20 (mg 2) so stages +
-    // fragments stay near 100 KB and the next kernel's CTAs co-reside
-    pl.dec = true;
-    pl.mg = M <= 4 ? 1 : 2;
-    const int mb = 4 * pl.mg;
-    const int groups = padded_tiles(n_tiles) / kGroupTiles;
-    const int seg_max = decode_seg_max(pl.mg);
-    // at least one CTA per SM (rounded up; at most a cluster of 8 k-segments)
-    int ksplit = std::max(1, std::min(kMaxDecodeCluster, (c->sm_count + groups - 1) / groups));
-    ksplit = std::max(ksplit, (chunks + seg_max - 1) / seg_max);
-    ksplit = std::min(ksplit, chunks);
-    // a group whose whole K is at most 32 chunks (128 KB of weights, twice
-    // what the stage ring holds before the dependency release) runs as one
-    // CTA: the cluster merge of a split costs more than the longer stream
-    // (measured on the E4B O projection, K 2048: 2.906 -> 2.82 ms per step;
-    // the QKV projection, 40 chunks, is faster split)
-    if (chunks <= std::min(32, seg_max)) ksplit = 1;
-    auto fits = [&](int ks) {
-      return ks == 1 || ((size_t)padded_tiles(n_tiles) * ks * kTileN * mb <= c->part_floats &&
-                         (size_t)groups <= c->n_counters);
-    };
-    while (ksplit > 1 && !fits(ksplit)) --ksplit;
-    const int seg = (chunks + ksplit - 1) / ksplit;
-    pl.kseg = seg * kChunkK;
-    pl.ksplit = (chunks + seg - 1) / seg;
-    pl.ch = 0;
-    return pl;
-  }
-  int mg = 1;
-  while (mg < 16 && 4 * mg < M) mg *= 2;
-  pl.mg = mg;
-  const int mb = 4 * mg;
-  const int mblocks = (M + mb - 1) / mb;
-  const int nct = (n_tiles + 3) / 4;
-  const long base = (long)mblocks * nct;
-  const long target = 3L * c->sm_count;  // CTAs wanted in flight
-  pl.ch = mg <= 2 ? 8 : (mg == 4 ? 4 : (mg == 8 ? 4 : 2));
-  if (mg <= 2 && base * ((chunks + 7) / 8) < target) pl.ch = 4;  // small matrix: finer split
-  const int rounds = (chunks + pl.ch - 1) / pl.ch;  // rounds if one CTA covered all of K
-  int ksplit = (int)std::min<long>(rounds, std::max<long>(1, (target + base - 1) / base));
-  auto need = [&](int ks) { return ks > 1 ? (size_t)base * ks * 4 * kTileN * mb : (size_t)0; };
-  while (ksplit > 1 && (need(ksplit) > c->part_floats || (size_t)base > c->n_counters)) --ksplit;
-  const int rounds_per = (rounds + ksplit - 1) / ksplit;
-  pl.kseg = rounds_per * pl.ch * kChunkK;
-  pl.ksplit = (K + pl.kseg - 1) / pl.kseg;
-  return pl;
+  const PlanLimits lim{c->sm_count, c->part_floats, c->n_counters, sk_rows_max()};
+  return ms::plan_gemv(&lim, M, K, n_tiles, allow_tc, allow_sk);
 }
 
 static cudaError_t launch_proj(const GemvParams& p, const GemvPlan& pl, cudaStream_t s, bool pdl) {
@@ -789,23 +699,6 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kNaBytes];
 // and the address is published through an atomic.
 static std::atomic<unsigned char*> g_noalloc_addr[kNaMaxDevices];
 static std::mutex g_noalloc_mu;
-
-// Partial-sum floats and tickets a projection plan uses (0 without a k-split).
-static void plan_scratch(const GemvPlan& pl, int M, int n_tiles, size_t* floats,
-                         size_t* tickets) {
-  *floats = 0;
-  *tickets = 0;
-  if (pl.ksplit <= 1) return;
-  const int mb = 4 * pl.mg;
-  if (pl.dec) {
-    *floats = (size_t)padded_tiles(n_tiles) * pl.ksplit * kTileN * mb;
-    *tickets = (size_t)padded_tiles(n_tiles) / kGroupTiles;
-  } else {
-    const size_t base = (size_t)((M + mb - 1) / mb) * ((n_tiles + 3) / 4);
-    *floats = base * pl.ksplit * 4 * kTileN * mb;
-    *tickets = base;
-  }
-}
 
 // The largest k-split that fits the static scratch, starting from the
 // context's plan and going down to the kernel's smallest split (the decode
