@@ -95,10 +95,13 @@ __device__ __forceinline__ float* kv_dst(const KvView& kv, int dst, int m, int s
 // int8 cache quantisation of one head row with absolute maximum amax:
 // scale = amax / 127, q = rint(v * (127 / amax)) clamped to [-127, 127]
 // (every step one IEEE-rounded operation, so a CPU restatement reproduces
-// it bit for bit); an all-zero row has scale 0 and q 0.
+// it bit for bit).  A row whose amax is below 2^-120 (zero rows included;
+// 127 / amax would overflow below about 2^-121) is stored as scale 0, q 0.
+constexpr float kI8MinAmax = 0x1p-120f;
 __device__ __forceinline__ void i8_scale(float amax, float& scale, float& inv) {
-  scale = __fdiv_rn(amax, 127.0f);
-  inv = amax > 0.f ? __fdiv_rn(127.0f, amax) : 0.f;
+  const bool live = amax >= kI8MinAmax;
+  scale = live ? __fdiv_rn(amax, 127.0f) : 0.f;
+  inv = live ? __fdiv_rn(127.0f, amax) : 0.f;
 }
 __device__ __forceinline__ int i8_quant(float v, float inv) {
   const float r = rintf(__fmul_rn(v, inv));

@@ -49,12 +49,13 @@ void orc_quant_i8(const float *x, int n, signed char *q, float *scale)
         const float a = fabsf(x[i]);
         if (a > amax) amax = a;
     }
-    const float s = amax / 127.0f;
-    const float inv = amax > 0.0f ? 127.0f / amax : 0.0f;
+    /* rows below 2^-120 (127 / amax would overflow) are stored as zero rows;
+     * the clamp is fminf(fmaxf()) as on the GPU, which also maps a NaN to -127 */
+    const int live = amax >= 0x1p-120f;
+    const float s = live ? amax / 127.0f : 0.0f;
+    const float inv = live ? 127.0f / amax : 0.0f;
     for (int i = 0; i < n; ++i) {
-        float r = rintf(x[i] * inv);
-        if (r > 127.0f) r = 127.0f;
-        if (r < -127.0f) r = -127.0f;
+        const float r = fminf(fmaxf(rintf(x[i] * inv), -127.0f), 127.0f);
         q[i] = (signed char)r;
     }
     *scale = s;

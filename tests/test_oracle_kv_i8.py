@@ -1,8 +1,9 @@
 """The int8 KV cache's quantiser in the oracle (oracle/ms_oracle.c
 orc_quant_i8), pinned against an independent NumPy restatement of the rule
 the GPU cache applies per (position, KV head) row: scale = max|v| / 127,
-q = rint(v * (127 / max|v|)) clamped to [-127, 127], read back as q * scale,
-every step one IEEE float32 operation.  The reference has no int8 cache (it is
+q = rint(v * (127 / max|v|)) clamped to [-127, 127] (fminf(fmaxf()), as on the
+GPU), read back as q * scale, every step one IEEE float32 operation; a row
+whose max|v| is below 2^-120 (127 / max|v| would overflow) is a zero row.  The reference has no int8 cache (it is
 on its roadmap, README.md:487-489), so the rule itself is the specification.
 """
 import numpy as np
@@ -10,14 +11,18 @@ import numpy as np
 from oracle import oracle
 
 
+MIN_AMAX = np.float32(2.0 ** -120)
+
+
 def numpy_quant(x):
     x = np.asarray(x, np.float32)
     amax = np.abs(x).max(axis=1)
-    scale = amax / np.float32(127)
-    with np.errstate(divide="ignore"):
-        inv = np.where(amax > 0, np.float32(127) / amax, np.float32(0)).astype(np.float32)
-    q = np.clip(np.rint(x * inv[:, None]), -127, 127).astype(np.int8)
-    return q, scale.astype(np.float32)
+    live = amax >= MIN_AMAX
+    scale = np.where(live, amax / np.float32(127), np.float32(0)).astype(np.float32)
+    with np.errstate(divide="ignore", over="ignore"):
+        inv = np.where(live, np.float32(127) / amax, np.float32(0)).astype(np.float32)
+    r = np.fmin(np.fmax(np.rint(x * inv[:, None]), np.float32(-127)), np.float32(127))
+    return r.astype(np.int8), scale
 
 
 def rows(seed):
@@ -29,6 +34,14 @@ def rows(seed):
     x[7, :] = 0.0
     x[7, 9] = np.float32(1e-30)                    # one tiny value
     x[8] = np.arange(256, dtype=np.float32) - 128  # integer ramp: ties at .5 steps
+    x[9] = 0.0
+    x[9, 3] = np.float32(1e-38)                    # 127 / amax overflows: a zero row
+    x[10] = rng.standard_normal(256).astype(np.float32) * np.float32(2.0 ** -140)  # subnormal
+    x[11] = 0.0
+    x[11, 0] = MIN_AMAX                            # the smallest row still quantised
+    x[11, 1] = -MIN_AMAX / np.float32(2)
+    x[12] = 0.0
+    x[12, 0] = MIN_AMAX / np.float32(2)            # just below it: a zero row
     return x
 
 
@@ -44,13 +57,15 @@ def test_quant_properties():
     x = rows(9)
     q, s = oracle.quant_i8(x)
     back = q.astype(np.float32) * s[:, None]
-    nz = np.abs(x).max(axis=1) > 0
-    # the largest magnitude of a row maps to +-127; zero rows to scale 0
+    nz = np.abs(x).max(axis=1) >= MIN_AMAX
+    # the largest magnitude of a row maps to +-127; zero and tiny rows to scale 0
     assert (np.abs(q[nz]).max(axis=1) == 127).all()
     assert (s[~nz] == 0).all() and (q[~nz] == 0).all()
-    # error at most half a step (plus float rounding)
+    assert (np.abs(x[~nz]) < MIN_AMAX).all()
+    # error at most half a step (plus float rounding); a tiny row's error is
+    # its own magnitude, below 2^-120
     err = np.abs(back - x)
-    assert (err <= s[:, None] * np.float32(0.5 + 1e-5) + 1e-38).all()
+    assert (err[nz] <= s[nz, None] * np.float32(0.5 + 1e-5) + 1e-38).all()
     # idempotent: quantising what the cache reads back gives the same bytes
     q2, s2 = oracle.quant_i8(back)
     assert np.array_equal(q2, q)
