@@ -243,8 +243,9 @@ enum { MS_KV_F32 = 0, MS_KV_BF16 = 1, MS_KV_I8 = 2 };
  * kv_dim % 8 == 0) or MS_KV_I8 (about a quarter of the bytes, the int8 KV
  * cache of the reference's roadmap, README.md:487-489: each K or V head row
  * of a position is stored as int8 q with one fp32 scale = max|v| / 127,
- * q = rint(v * 127 / max|v|); a value reads back as q * scale; needs every
- * head_dim % 16 == 0).  Attention, softmax and accumulation stay fp32. */
+ * q = rint(v * 127 / max|v|); a value reads back as q * scale; a row whose
+ * max|v| is below 2^-120 is stored as zeros; needs every head_dim % 16 ==
+ * 0).  Attention, softmax and accumulation stay fp32. */
 MS_API ms_status ms_kv_create_typed(ms_ctx *ctx, const ms_model *model, int n_seq, int max_pos,
                                     int slide_cap, int dtype, ms_kv **out);
 /* A cache for serving requests that come and go (the reference's roadmap:
