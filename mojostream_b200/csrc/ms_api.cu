@@ -1596,36 +1596,18 @@ static ms_status run_layer(ms_ctx* c, ms_model* m, const ms_kv* kv, int li, int 
     a.window = L.d.window;
     a.M = M;
     a.scale = 1.0f / sqrtf((float)L.d.head_dim);
-    // splits: about one CTA per SM at the longest span the cache can hold;
-    // the kernel sizes each row's ranges itself (short rows leave splits
-    // idle), so one launch shape -- and one captured graph -- serves every
-    // position
+    // position splits and their merge (ms_plan.h) at the longest span the
+    // cache can hold, so one launch shape serves every position
     const int span = L.d.window > 0 ? std::min(L.d.window, kv->max_pos) : kv->max_pos;
-    const long ctas_per_split = (long)M * L.d.n_kv_heads;
-    const int min_per = 8;  // positions per split at least
-    int splits = (int)std::max<long>(1, (c->sm_count + ctas_per_split - 1) / ctas_per_split);
-    // long spans: at most ~256 positions per split, so a large batch at long
-    // context still has enough CTAs to keep every SM streaming
-    splits = std::max(splits, (span + 255) / 256);
-    splits = std::min(splits, std::max(1, (span + min_per - 1) / min_per));
-    splits = std::min(splits, attention_max_splits());
-    // merge inside a thread-block cluster when the splits fit one (up to 16;
-    // a fill-rule count a little above that is trimmed to it), unless
-    // MS_SPLITK_GLOBAL=1 asks for the global-memory merge
-    const int max_cl = attention_max_cluster();
-    const bool try_cl = max_cl > 0 && !splitk_global_forced();
-    if (try_cl && splits > max_cl && splits <= max_cl + max_cl / 2 &&
-        (span + 255) / 256 <= max_cl)
-      splits = max_cl;
     const int G = L.d.n_heads / L.d.n_kv_heads;
-    while (splits > 1 &&
-           (size_t)M * L.d.n_kv_heads * splits * G * (L.d.head_dim + 4) > c->part_floats)
-      splits = (splits + 1) / 2;
-    a.cluster = try_cl && splits > 1 && splits <= max_cl;
+    const AttnLimits al{c->sm_count, c->part_floats, attention_max_splits(),
+                        attention_max_cluster(), splitk_global_forced()};
+    const AttnPlan ap = plan_attention(&al, M, L.d.n_kv_heads, G, L.d.head_dim, span);
+    a.cluster = ap.cluster;
     if ((size_t)M * L.d.n_kv_heads > c->n_counters)
       return fail(c, MS_ERR_CAPACITY, "attention: too many rows for the ticket counters");
-    a.chunk = min_per;
-    a.n_splits = splits;
+    a.chunk = kAttnMinPerSplit;
+    a.n_splits = ap.splits;
     a.part = c->part;
     a.counters = c->counters;
     a.err = c->d_err;

@@ -135,4 +135,48 @@ inline void plan_scratch(const GemvPlan& pl, int M, int n_tiles, size_t* floats,
   }
 }
 
+// Flash-decode attention of one layer: position splits per (row, KV head)
+// and whether they merge inside a thread-block cluster.  Limits: SMs, the
+// context's partial-sum floats, the kernel's largest split count and
+// cluster (0: clusters unavailable), and whether the global-memory merge is
+// forced (MS_SPLITK_GLOBAL=1).
+struct AttnLimits {
+  int sm_count;
+  size_t part_floats;
+  int max_splits, max_cluster;
+  bool global_forced;
+};
+struct AttnPlan {
+  int splits;
+  bool cluster;
+};
+constexpr int kAttnMinPerSplit = 8;  // positions per split at least
+
+// span: the longest run of positions a row of this layer can attend (the
+// window, or the cache's max_pos); the kernel sizes each row's ranges itself
+// (short rows leave splits idle), so one launch shape -- and one captured
+// graph -- serves every position.
+inline AttnPlan plan_attention(const AttnLimits* c, int M, int n_kv, int G, int hd, int span) {
+  // about one CTA per SM
+  const long ctas_per_split = (long)M * n_kv;
+  const int min_per = kAttnMinPerSplit;
+  int splits = (int)std::max<long>(1, (c->sm_count + ctas_per_split - 1) / ctas_per_split);
+  // long spans: at most ~256 positions per split, so a large batch at long
+  // context still has enough CTAs to keep every SM streaming
+  splits = std::max(splits, (span + 255) / 256);
+  splits = std::min(splits, std::max(1, (span + min_per - 1) / min_per));
+  splits = std::min(splits, c->max_splits);
+  // merge inside a thread-block cluster when the splits fit one (up to 16;
+  // a fill-rule count a little above that is trimmed to it), unless the
+  // global-memory merge is forced
+  const int max_cl = c->max_cluster;
+  const bool try_cl = max_cl > 0 && !c->global_forced;
+  if (try_cl && splits > max_cl && splits <= max_cl + max_cl / 2 &&
+      (span + 255) / 256 <= max_cl)
+    splits = max_cl;
+  while (splits > 1 && (size_t)M * n_kv * splits * G * (hd + 4) > c->part_floats)
+    splits = (splits + 1) / 2;
+  return AttnPlan{splits, try_cl && splits > 1 && splits <= max_cl};
+}
+
 }  // namespace ms

@@ -12,6 +12,11 @@
 //     registers, unless even the split that would allow that exceeds the
 //     scratch (ms_q4_gemm then refuses the shape with MS_ERR_CAPACITY);
 //   * merge decode-batch k-slices inside one cluster (at most 8).
+// And every decode attention plan (position splits per row and KV head) must
+// stay within the kernel's split count, give no split less than 8
+// positions of the span, keep its partial sums inside the scratch, and merge
+// inside a cluster only where clusters exist, are not overridden and hold
+// all the splits.
 #include <cstdio>
 #include <cstdlib>
 
@@ -79,6 +84,19 @@ static void check(const PlanLimits& L, int M, int K, int nt, bool at, bool as) {
   }
 }
 
+static void check_attn(const AttnLimits& L, int M, int n_kv, int G, int hd, int span) {
+  const AttnPlan a = plan_attention(&L, M, n_kv, G, hd, span);
+  CHECK(a.splits >= 1 && a.splits <= L.max_splits, "attn M%d span%d: %d splits", M, span, a.splits);
+  CHECK(a.splits <= std::max(1, (span + kAttnMinPerSplit - 1) / kAttnMinPerSplit),
+        "attn M%d span%d: %d splits of fewer than %d positions", M, span, a.splits,
+        kAttnMinPerSplit);
+  CHECK(a.splits == 1 || (size_t)M * n_kv * a.splits * G * (hd + 4) <= L.part_floats,
+        "attn M%d kv%d G%d hd%d: %d splits over the scratch", M, n_kv, G, hd, a.splits);
+  CHECK(!a.cluster || (L.max_cluster > 0 && !L.global_forced && a.splits > 1 &&
+                       a.splits <= L.max_cluster),
+        "attn M%d span%d: cluster merge of %d splits", M, span, a.splits);
+}
+
 int main() {
   // the library's context (ms_init) on a 148-SM B200, and one with 1/128 of
   // its partial-sum scratch so that the fallbacks are reached
@@ -92,10 +110,22 @@ int main() {
         for (int nt : tiles)
           for (int at = 0; at < 2; ++at)
             for (int as = 0; as < 2; ++as, ++n) check(L, M, K, nt, at, as);
+  long na = 0;
+  for (size_t pf : {(size_t)8 << 20, (size_t)1 << 14})
+    for (int mcl : {16, 0})
+      for (int forced = 0; forced < 2; ++forced) {
+        const AttnLimits L{148, pf, 64, mcl, forced != 0};
+        for (int M = 1; M <= 2048; M = M < 16 ? M + 1 : M * 2)
+          for (int n_kv : {1, 2, 8})
+            for (int G : {1, 4, 8})
+              for (int hd : {64, 256, 512})
+                for (int span = 1; span <= 131072; span = span < 64 ? span + 1 : span * 2 - 1, ++na)
+                  check_attn(L, M, n_kv, G, hd, span);
+      }
   if (g_fail) {
     std::printf("FAILED %ld checks of %ld plans\n", g_fail, n);
     return 1;
   }
-  std::printf("ok: %ld plans\n", n);
+  std::printf("ok: %ld projection plans, %ld attention plans\n", n, na);
   return 0;
 }

@@ -1,9 +1,11 @@
-"""The Q4 projection planner (mojostream_b200/csrc/ms_plan.h) on the host:
+"""The launch planners (mojostream_b200/csrc/ms_plan.h) on the host:
 tests/plan_check.cu walks a broad grid of shapes under the library's
-context limits and checks every plan's invariants (K covered exactly, the
-kernel the row count calls for, split-K scratch within the context's
-buffers, decode segments within the streaming kernel's registers, cluster
-merges of at most 8).  Built with nvcc because the planner's header shares
+context limits and checks every plan's invariants.  Q4 projections: K
+covered exactly, the kernel the row count calls for, split-K scratch within
+the context's buffers, decode segments within the streaming kernel's
+registers, cluster merges of at most 8.  Decode attention: split counts
+within the kernel's, splits of at least 8 positions, partial sums within the
+scratch, cluster merges only where they can hold every split.  Built with nvcc because the planner's header shares
 the kernels' definitions; nothing runs on a GPU."""
 import os
 import shutil
