@@ -75,36 +75,6 @@ def test_q4_gemm_accumulates_like_the_reference(ctx, torch_cuda, oracle_lib):
     assert rel_rmse(C.cpu().numpy(), ref) < 2e-5
 
 
-def test_reference_named_q4_matmul_both_forms(ctx, torch_cuda, oracle_lib):
-    """reference_api.matmul_q4_bpack_raw (kernels.mojo:201-267: C += A . W)
-    given raw bytes (a one-off call: its own context, upload and repack) and
-    given a Q4Weight made once (a host loop's form, called twice), both
-    against the oracle; a scale other than the weight's is refused."""
-    from mojostream_b200 import reference_api as ra
-    from mojostream_b200.runtime import Q4Weight
-    torch = torch_cuda
-    rng = np.random.default_rng(3)
-    K, N, M = 1024, 512, 4
-    W = rng.integers(0, 256, size=(K, N // 2), dtype=np.uint8)
-    A = rng.standard_normal((M, K)).astype(np.float32)
-    C0 = rng.standard_normal((M, N)).astype(np.float32)
-    once = oracle_lib.q4_matmul(A, W, N, 0.01, C=C0)
-    C = to_dev(torch, C0)
-    ra.matmul_q4_bpack_raw(C, to_dev(torch, A), W, N // 2, 0.01)
-    torch.cuda.synchronize()
-    assert rel_rmse(C.cpu().numpy(), once) < 2e-5
-    w = Q4Weight(ctx, W, K, N, 0.01)
-    C = to_dev(torch, C0)
-    for _ in range(2):
-        ra.matmul_q4_bpack_raw(C, to_dev(torch, A), w, N // 2, 0.01)
-    torch.cuda.synchronize()
-    twice = oracle_lib.q4_matmul(A, W, N, 0.01, C=once)
-    assert rel_rmse(C.cpu().numpy(), twice) < 2e-5
-    with pytest.raises(ValueError, match="scale"):
-        ra.matmul_q4_bpack_raw(C, to_dev(torch, A), w, N // 2, 0.02)
-    w.close()
-
-
 def test_q4_dequant_bit_exact(ctx, torch_cuda, oracle_lib):
     """One-hot rows read the dequantised weights back: (nibble - 8) * scale
     must be bit-identical to the reference's dequant_vec."""
