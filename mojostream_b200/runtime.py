@@ -33,6 +33,14 @@ def _check_f32(t, what, min_numel=0):
         raise ValueError(f"{what}: {t.numel()} values, the call uses {min_numel}")
 
 
+def _check_rows(M, **lists):
+    """Per-row lists handed to the C-ABI as bare arrays of M ints: each must
+    have exactly M entries (the library reads M of each)."""
+    for name, v in lists.items():
+        if len(v) != M:
+            raise ValueError(f"{name}: {len(v)} entries for {M} rows")
+
+
 _CUDA_STREAM_LEGACY = 1  # cudaStreamLegacy: the legacy default stream handle
 
 
@@ -235,6 +243,7 @@ class Model:
         """x: CUDA float32 tensor [M][hidden], updated in place."""
         M = x.shape[0]
         _check_f32(x, "x", M * self.spec.hidden)
+        _check_rows(M, seq=seq, pos=pos)
         self.ctx.check(lib().ms_layer_forward(self.ctx.h, self.h, layer, _ptr(x), kv.h,
                                               int_array(seq), int_array(pos), M, _stream()))
         return x
@@ -242,6 +251,7 @@ class Model:
     def forward(self, x, kv, seq, pos):
         M = x.shape[0]
         _check_f32(x, "x", M * self.spec.hidden)
+        _check_rows(M, seq=seq, pos=pos)
         self.ctx.check(lib().ms_forward(self.ctx.h, self.h, _ptr(x), kv.h, int_array(seq),
                                         int_array(pos), M, _stream()))
         return x
@@ -271,6 +281,7 @@ class Model:
 
     def decode_step(self, kv, ids, seq, pos):
         M = len(ids)
+        _check_rows(M, seq=seq, pos=pos)
         out = (ctypes.c_int * M)()
         self.ctx.check(lib().ms_decode_step(self.ctx.h, self.h, kv.h, int_array(ids),
                                             int_array(seq), int_array(pos), M, out))
@@ -280,6 +291,7 @@ class Model:
         """Tokens [steps][M] (greedy unless set_sampling chose otherwise); with
         timing=True also the device ms of the loop."""
         M = len(ids)
+        _check_rows(M, seq=seq, pos=pos)
         out = (ctypes.c_int * (M * steps))()
         ms = ctypes.c_float(0.0)
         self.ctx.check(lib().ms_generate(self.ctx.h, self.h, kv.h, int_array(ids),
@@ -289,6 +301,7 @@ class Model:
         return (ids_out, float(ms.value)) if timing else ids_out
 
     def prefill(self, kv, ids, seq, pos):
+        _check_rows(len(ids), seq=seq, pos=pos)
         first = (ctypes.c_int * kv.n_seq)(*([-1] * kv.n_seq))
         self.ctx.check(lib().ms_prefill(self.ctx.h, self.h, kv.h, int_array(ids),
                                         int_array(seq), int_array(pos), len(ids), first))

@@ -50,3 +50,10 @@ def test_reference_matmul_refuses_a_mismatched_prebuilt_weight():
         ra.matmul_q4_bpack_raw(torch.zeros((2, 64)), A, w, 32, 0.01)
     with pytest.raises(ValueError, match="C is"):
         ra.matmul_q4_bpack_raw(torch.zeros((3, 32)), A, w, 16, 0.01)
+
+
+def test_row_lists_must_match_the_row_count():
+    from mojostream_b200.runtime import _check_rows
+    _check_rows(3, seq=[0, 0, 1], pos=[4, 5, 0])
+    with pytest.raises(ValueError, match="pos: 2 entries for 3 rows"):
+        _check_rows(3, seq=[0, 0, 1], pos=[4, 5])
