@@ -1,5 +1,6 @@
-"""The Mojo binding stubs in INTEGRATION.md cannot be compiled here (no Mojo
-toolchain), so this keeps them exact by reading them as text: every
+"""The Mojo binding stubs of the repository's integration guide cannot be
+compiled here (no Mojo toolchain), so this keeps them exact by reading them
+as text: every
 `get_function[fn (...) -> R]("ms_...")` names a function the header
 declares, with the same number of arguments and the same kind of value in
 each place (pointer, 32-bit integer, 32-bit float, 64-bit integer), and the
