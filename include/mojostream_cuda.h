@@ -18,7 +18,10 @@
  *     are borrowed for the duration of the call only.
  *   - One context per host thread (thread-compatible, not thread-safe).
  *     Calls are asynchronous on the given stream unless stated otherwise;
- *     ms_sync() waits.
+ *     ms_sync() waits.  A context's split-K and attention partial sums are
+ *     one buffer shared by all its calls and models: calls given different
+ *     streams must not overlap in time (run them on one stream, or give each
+ *     concurrent stream its own context).
  *   - Activations are fp32 row-major, Q4 weights are the reference's layout
  *     [K][N/2] (low nibble = even column, value (nibble - 8) * scale,
  *     src/linalg/kernels.mojo:64-70), fp32 lm_head is [D][V].
