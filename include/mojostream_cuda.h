@@ -102,9 +102,10 @@ MS_API ms_status ms_q4_weight_destroy(ms_ctx *ctx, ms_q4_weight *w);
  * C[M,N] += A[M,K] . deq(W)  (accumulate = 1, the reference's semantics,
  * matmul_q4_bpack_raw, src/linalg/kernels.mojo:201-267)
  * A, C: device pointers, row-major, A 16-byte and C 8-byte aligned.
- * MS_ERR_CAPACITY (before launch) when a decode call (M 5..8) would need a
+ * MS_ERR_CAPACITY (before launch) when a decode call (M <= 8) would need a
  * k-split whose partial sums exceed the context's 32 MiB scratch: only for
- * very wide and long weights (e.g. N 262144 with K 10240). */
+ * very wide and long weights (N 262144 with K above 5120 at M 8, above
+ * 20480 at M 4). */
 MS_API ms_status ms_q4_gemm(ms_ctx *ctx, const ms_q4_weight *w, float *C, const float *A, int M,
                      int accumulate, void *stream);
 /* No counterpart in the reference.  The same projection as ms_q4_gemm
