@@ -57,3 +57,42 @@ def test_row_lists_must_match_the_row_count():
     _check_rows(3, seq=[0, 0, 1], pos=[4, 5, 0])
     with pytest.raises(ValueError, match="pos: 2 entries for 3 rows"):
         _check_rows(3, seq=[0, 0, 1], pos=[4, 5])
+
+
+def test_reference_matmul_raw_form_call_sequence(monkeypatch):
+    """matmul_q4_bpack_raw given raw bytes: it makes its own context, uploads
+    the weight, launches with accumulation, waits on the launching stream and
+    closes both, in that order (stand-ins for the library objects)."""
+    import numpy as np
+
+    from mojostream_b200 import reference_api as ra
+    calls = []
+
+    class Ctx:
+        def __init__(self, device=0):
+            calls.append(("ctx", device))
+
+        def sync(self, current=False):
+            calls.append(("sync", current))
+
+        def close(self):
+            calls.append(("ctx.close",))
+
+    class W:
+        def __init__(self, ctx, w, K, N, scale):
+            calls.append(("weight", w.shape, K, N, scale))
+
+        def gemm(self, A, C, accumulate=False):
+            calls.append(("gemm", tuple(A.shape), tuple(C.shape), accumulate))
+
+        def close(self):
+            calls.append(("weight.close",))
+
+    monkeypatch.setattr(ra.runtime, "Context", Ctx)
+    monkeypatch.setattr(ra.runtime, "Q4Weight", W)
+    A, C = torch.zeros((4, 64)), torch.zeros((4, 32))
+    bq = np.zeros((64, 16), np.uint8)
+    assert ra.matmul_q4_bpack_raw(C, A, bq, 16, 0.01) is C
+    assert calls == [("ctx", 0), ("weight", (64, 16), 64, 32, 0.01),
+                     ("gemm", (4, 64), (4, 32), True), ("sync", True), ("weight.close",),
+                     ("ctx.close",)]
